@@ -1,0 +1,245 @@
+"""NVFP4 oracle: e2m1/e4m3 codecs, the reference dequantiser, fixture
+quantisers and the dequantise-then-matmul linear.  Test infrastructure only.
+
+Reference anchors (paths inside the reference project):
+  * e2m1 lookup table          adallm/infra/nvfp4.py:7-18 (same table at
+                               adallm/ops/nvfp4_gemm.py:7-18)
+  * dequant_nvfp4              adallm/infra/nvfp4.py:36-77
+  * nvfp4_linear semantics     adallm/ops/nvfp4_gemm.py:460-564 (kernel :58-136)
+  * weight / scale layout      adallm/ops/linear.py:31-43 (uint8 [N, K/2],
+                               fp16 [N, K/16] holding e4m3 values, fp32 [])
+
+The reference ships no quantiser (checkpoints come from NVIDIA ModelOpt), so
+``quantize_weight`` follows the synthetic-config text: one e4m3 scale per 16
+contiguous K elements (block amax / 6) relative to one fp32 per-tensor global
+scale (amax / (6 * 448)), nearest-e2m1 codes, two codes per byte with the even
+K index in the low nibble.
+
+``quantize_act_terms`` is the bit-exact specification of the activation
+quantiser that feeds the tcgen05 ``kind::mxf4nvf4`` GEMM of adallm_b200 (it
+has no reference counterpart): the bf16 activation row is written as a sum of
+T NVFP4 terms that share one fp32 per-row global scale, each term quantising
+the residual left by the previous ones.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+E4M3_MAX = 448.0
+E2M1_MAX = 6.0
+GLOBAL_DIV = 6.0 * 448.0  # 2688
+
+
+def _e2m1_magnitudes() -> np.ndarray:
+    # code bits: s e1 e0 m  (adallm/infra/nvfp4.py:7-18)
+    out = []
+    for code in range(8):
+        exp = (code >> 1) & 0x3
+        mant = code & 0x1
+        if exp == 0:
+            out.append(0.5 * mant)
+        else:
+            out.append((1.0 + 0.5 * mant) * 2.0 ** (exp - 1))
+    return np.asarray(out, dtype=np.float64)
+
+
+def _e4m3_magnitudes() -> np.ndarray:
+    # e4m3fn: bias 7, no inf, 0x7f / 0xff are NaN; codes 0..126 are finite
+    out = []
+    for code in range(127):
+        e = (code >> 3) & 0xF
+        m = code & 0x7
+        if e == 0:
+            out.append(m / 8.0 * 2.0 ** -6)
+        else:
+            out.append((1.0 + m / 8.0) * 2.0 ** (e - 7))
+    return np.asarray(out, dtype=np.float64)
+
+
+E2M1_MAG = _e2m1_magnitudes()
+E4M3_MAG = _e4m3_magnitudes()
+E2M1_LUT = np.concatenate([E2M1_MAG, -E2M1_MAG]).astype(np.float32)  # 16 entries
+
+
+def _round_to_table(mag: np.ndarray, table: np.ndarray) -> np.ndarray:
+    """Round non-negative float magnitudes to the nearest entry of a sorted
+    table, ties to the even code, saturating at the last entry.  Returns codes."""
+    x = np.asarray(mag, dtype=np.float64)
+    n = table.shape[0]
+    hi = np.searchsorted(table, x, side="left")
+    hi = np.clip(hi, 1, n - 1)
+    lo = hi - 1
+    d_lo = x - table[lo]
+    d_hi = table[hi] - x
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & ((hi & 1) == 0))
+    code = np.where(pick_hi, hi, lo)
+    code = np.where(x >= table[-1], n - 1, code)
+    code = np.where(x <= 0, 0, code)
+    return code.astype(np.uint8)
+
+
+def e2m1_encode(v: np.ndarray) -> np.ndarray:
+    """fp32 -> e2m1 code (round-to-nearest-even, saturate to +-6)."""
+    v = np.asarray(v, dtype=np.float32)
+    code = _round_to_table(np.abs(v), E2M1_MAG)
+    return (code | (np.signbit(v).astype(np.uint8) << 3)).astype(np.uint8)
+
+
+def e2m1_decode(code: np.ndarray) -> np.ndarray:
+    return E2M1_LUT[np.asarray(code, dtype=np.int64) & 0xF]
+
+
+def e4m3_encode(v: np.ndarray) -> np.ndarray:
+    """fp32 -> e4m3fn bits, round-to-nearest-even, saturating to +-448 (the
+    ``cvt.rn.satfinite`` behaviour; the reference's Triton store at
+    adallm/ops/attention.py:11-31 casts the same way)."""
+    v = np.asarray(v, dtype=np.float32)
+    code = _round_to_table(np.abs(v), E4M3_MAG)
+    code = code | (np.signbit(v).astype(np.uint8) << 7)
+    code = np.where(np.isnan(v), np.uint8(0x7F), code)
+    return code.astype(np.uint8)
+
+
+def e4m3_decode(bits: np.ndarray) -> np.ndarray:
+    b = np.asarray(bits, dtype=np.uint8)
+    mag = E4M3_MAG[np.minimum(b & 0x7F, 126)].astype(np.float32)
+    mag = np.where((b & 0x7F) == 0x7F, np.float32(np.nan), mag)
+    return np.where(b & 0x80, -mag, mag).astype(np.float32)
+
+
+def pack_codes(codes: np.ndarray) -> np.ndarray:
+    """[..., K] e2m1 codes -> [..., K/2] bytes, even K in the low nibble
+    (adallm/infra/nvfp4.py:54-61)."""
+    c = np.asarray(codes, dtype=np.uint8)
+    return (c[..., 0::2] & 0xF) | ((c[..., 1::2] & 0xF) << 4)
+
+
+def unpack_codes(packed: np.ndarray) -> np.ndarray:
+    p = np.asarray(packed, dtype=np.uint8)
+    out = np.empty(p.shape[:-1] + (p.shape[-1] * 2,), dtype=np.uint8)
+    out[..., 0::2] = p & 0xF
+    out[..., 1::2] = p >> 4
+    return out
+
+
+def dequant_nvfp4(packed: np.ndarray, scale: np.ndarray, scale_2, group_size: int = 16) -> np.ndarray:
+    """Restates adallm/infra/nvfp4.py:36-77: W = lut[nibble] * scale[n, k//g] * scale_2 in fp32."""
+    packed = np.asarray(packed)
+    if packed.dtype != np.uint8:
+        raise ValueError("packed_weight must be uint8 for NVFP4 dequantization")
+    if packed.ndim != 2:
+        raise ValueError("packed_weight must be 2D [out, in/2]")
+    n, khalf = packed.shape
+    k = khalf * 2
+    if k % group_size != 0:
+        raise ValueError("in_features must be divisible by group_size")
+    vals = e2m1_decode(unpack_codes(packed))  # [n, k] fp32
+    s = np.asarray(scale, dtype=np.float32)
+    if scale_2 is not None:
+        s = s * np.float32(np.asarray(scale_2, dtype=np.float32))
+    if s.ndim == 1:
+        s = s.reshape(n, 1)
+    groups = k // group_size
+    if s.shape[1] not in (1, groups):
+        raise ValueError("weight_scale shape does not match packed_weight")
+    v = vals.reshape(n, groups, group_size)
+    if s.shape[1] == 1:
+        v = v * s.reshape(n, 1, 1)
+    else:
+        v = v * s.reshape(n, groups, 1)
+    return v.reshape(n, k).astype(np.float32)
+
+
+def quantize_weight(w: np.ndarray, group_size: int = 16):
+    """Fixture quantiser for synthetic NVFP4 weights (no reference counterpart).
+
+    Returns (packed uint8 [N, K/2], scale_bits uint8 [N, K/16] (e4m3),
+    scale_2 float32 scalar)."""
+    w = np.asarray(w, dtype=np.float32)
+    n, k = w.shape
+    amax = np.float32(np.max(np.abs(w))) if w.size else np.float32(0)
+    g = np.float32(amax / np.float32(GLOBAL_DIV)) if amax > 0 else np.float32(1.0)
+    blocks = w.reshape(n, k // group_size, group_size)
+    bamax = np.max(np.abs(blocks), axis=-1)
+    g6 = np.float32(g * np.float32(6.0))
+    s_bits = e4m3_encode((bamax / g6).astype(np.float32))
+    s_val = e4m3_decode(s_bits)
+    denom = (s_val * g).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        rcp = np.where(denom > 0, np.float32(1.0) / denom, np.float32(0)).astype(np.float32)
+    v = (blocks * rcp[..., None]).astype(np.float32)
+    codes = e2m1_encode(v)
+    codes = np.where((s_val > 0)[..., None], codes, np.uint8(0)).reshape(n, k)
+    return pack_codes(codes), s_bits, g
+
+
+def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16):
+    """Bit-exact specification of adallm_b200's activation quantiser.
+
+    x: [M, K] (bf16 values given as fp32).  For each row:
+      g = rowamax / 2688 (1.0 for an all-zero row), r = x
+      for t in range(terms):
+        per 16-block: s = e4m3(blockamax(r) / (g*6)); denom = s*g
+        code = e2m1(r * (1/denom))   (0 when s == 0)
+        r = r - lut[code]*denom
+    Every operation is one IEEE fp32 rounding (no fused multiply-add).
+    Returns codes uint8 [T, M, K], scale bits uint8 [T, M, K/16], g fp32 [M].
+    """
+    x = np.asarray(x, dtype=np.float32)
+    m, k = x.shape
+    groups = k // group_size
+    amax = np.max(np.abs(x), axis=1).astype(np.float32) if k else np.zeros(m, np.float32)
+    g = np.where(amax > 0, (amax / np.float32(GLOBAL_DIV)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+    g6 = (g * np.float32(6.0)).astype(np.float32)
+    r = x.reshape(m, groups, group_size).copy()
+    codes = np.zeros((terms, m, groups, group_size), np.uint8)
+    sbits = np.zeros((terms, m, groups), np.uint8)
+    for t in range(terms):
+        bamax = np.max(np.abs(r), axis=-1).astype(np.float32)
+        sb = e4m3_encode((bamax / g6[:, None]).astype(np.float32))
+        sv = e4m3_decode(sb)
+        denom = (sv * g[:, None]).astype(np.float32)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            rcp = np.where(denom > 0, np.float32(1.0) / denom, np.float32(0)).astype(np.float32)
+        v = (r * rcp[..., None]).astype(np.float32)
+        c = e2m1_encode(v)
+        c = np.where((sv > 0)[..., None], c, np.uint8(0))
+        deq = (e2m1_decode(c) * denom[..., None]).astype(np.float32)
+        r = (r - deq).astype(np.float32)
+        codes[t] = c
+        sbits[t] = sb
+    return codes.reshape(terms, m, k), sbits, g
+
+
+def dequant_act_terms(codes: np.ndarray, sbits: np.ndarray, g: np.ndarray, group_size: int = 16) -> np.ndarray:
+    """Sum of the T dequantised activation terms -> fp32 [M, K]."""
+    t, m, k = codes.shape
+    vals = e2m1_decode(codes).reshape(t, m, k // group_size, group_size)
+    s = e4m3_decode(sbits)[..., None] * np.asarray(g, np.float32)[None, :, None, None]
+    return (vals * s).sum(axis=0).reshape(m, k).astype(np.float32)
+
+
+def linear_ref(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, scale_2, bias=None) -> np.ndarray:
+    """Dequantise-then-matmul oracle of nvfp4_linear (adallm/ops/nvfp4_gemm.py:460-564,
+    run as the reference's "dequant" mode does: adallm/infra/loader.py:92-102 then
+    adallm/ops/linear.py:74).  fp32 result [M, N]."""
+    w = dequant_nvfp4(packed, scale, scale_2)
+    y = np.asarray(x, dtype=np.float32) @ w.T
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float32)
+    return y.astype(np.float32)
+
+
+def linear_terms_ref(codes, sbits, g, packed, scale, scale_2) -> np.ndarray:
+    """Dequantise-both oracle for the mxf4nvf4 GEMM: the exact math the tensor
+    cores perform (fp32 [M, N])."""
+    xq = dequant_act_terms(codes, sbits, g)
+    w = dequant_nvfp4(packed, scale, scale_2)
+    return (xq.astype(np.float64) @ w.T.astype(np.float64)).astype(np.float32)
+
+
+def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    den = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))
