@@ -1,0 +1,100 @@
+"""ctypes binding of the adallm_b200 C ABI (include/adallm_b200.h).
+
+The CUDA library is built in-tree (``python -m adallm_b200.build``) and loaded
+from ``adallm_b200/_lib``.  There is no CPU or PyTorch fallback: if the library
+is missing, every op raises.  Status codes map to the reference's exception
+types: shape / argument problems raise ValueError (as adallm/ops/nvfp4_gemm.py:477-478
+does), launch and device failures raise RuntimeError with "no fallback" wording
+(as adallm/ops/nvfp4_gemm.py:532-535 and adallm/ops/attention.py:409-414 do).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libadallm_b200.so")
+HEADER = os.path.join(os.path.dirname(_HERE), "include", "adallm_b200.h")
+
+ADA_OK = 0
+ADA_ERR_INVALID_ARG = 1
+ADA_ERR_UNSUPPORTED = 2
+ADA_ERR_ALIGNMENT = 3
+ADA_ERR_WORKSPACE = 4
+ADA_ERR_LAUNCH = 5
+ADA_ERR_TIMEOUT = 6
+ADA_ERR_CUDA = 7
+
+DT = {torch.bfloat16: 0, torch.float16: 1}
+
+P, I32, I64, F32, INT, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_int, C.c_size_t
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "ada_status_string": (C.c_char_p, [INT]),
+    "ada_abi_version": (INT, []),
+    "ada_fp8_paged_decode_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
+    "ada_fp8_paged_decode": (INT, [P, INT, I64, I64, P, P, I64, I64, I64, I64, P, I64, I32, P, I32, I32, I32, I32, I32,
+                                   F32, F32, F32, I32, P, INT, P, SZ, P]),
+    "ada_store_kvcache_fp8": (INT, [P, P, INT, I64, I32, I32, I64, I64, P, P, P, I64, F32, F32, P]),
+    "ada_rmsnorm": (INT, [P, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, P]),
+    "ada_rope": (INT, [P, P, I64, P, I64, P, P, I64, I32, I32, I32, P, I64, INT, P]),
+    "ada_gated_act": (INT, [P, I64, P, I64, I64, I32, INT, INT, P]),
+    "ada_embedding": (INT, [P, I64, P, I64, I64, I32, P, INT, P]),
+    "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P]),
+}
+
+_lib = None
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise NativeLibraryMissing(
+                f"adallm_b200 CUDA library not found at {LIB_PATH}; build it with "
+                "`python -m adallm_b200.build`. There is no CPU/PyTorch fallback.")
+        h = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def declared_symbols() -> list[str]:
+    """Entry points declared in include/adallm_b200.h."""
+    with open(HEADER, "r", encoding="utf-8") as f:
+        text = f.read()
+    return sorted(set(re.findall(r"^ADA_API\s+(?:const\s+)?\w+\*?\s+\**(ada_\w+)\s*\(", text, flags=re.M)))
+
+
+def check(status: int, what: str) -> None:
+    if status == ADA_OK:
+        return
+    msg = lib().ada_status_string(status).decode()
+    if status in (ADA_ERR_INVALID_ARG, ADA_ERR_UNSUPPORTED, ADA_ERR_ALIGNMENT, ADA_ERR_WORKSPACE):
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what} failed ({msg}); no fallback is allowed in this runtime.")
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(*tensors: torch.Tensor, what: str) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{what} requires CUDA tensors")

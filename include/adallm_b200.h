@@ -1,0 +1,148 @@
+/*
+ * adallm_b200 -- C ABI of the B200 (sm_100a) kernels that replace the decode
+ * hot path of the AdaLLM NVFP4 runtime (package `adallm`).
+ *
+ * Conventions
+ *   - Every entry point returns an int status (ADA_OK == 0).  Nothing aborts
+ *     or exits; bad arguments are reported before any launch.
+ *   - Pointers are device pointers unless stated; sizes and strides are in
+ *     elements of the pointed-to type.  `stream` is a cudaStream_t passed as
+ *     void* so this header needs no CUDA include.
+ *   - dtype codes: ADA_DT_BF16 = 0, ADA_DT_F16 = 1.
+ *   - No entry point allocates or frees memory: outputs and workspaces are
+ *     owned by the caller (the reference's ops allocate with torch.empty,
+ *     adallm/ops/nvfp4_gemm.py:479, adallm/ops/attention.py:367; the Python
+ *     layer of this package does the same with the torch caching allocator).
+ *   - All launches go to `stream` and are CUDA-graph capturable.
+ *
+ * The reference interface each entry point replaces is cited beside it as
+ * path:line inside the reference project.
+ */
+#ifndef ADALLM_B200_H_
+#define ADALLM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ADA_API __attribute__((visibility("default")))
+#else
+#define ADA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ADA_OK = 0,
+  ADA_ERR_INVALID_ARG = 1,  /* null pointer, negative or inconsistent size  */
+  ADA_ERR_UNSUPPORTED = 2,  /* shape this build does not implement          */
+  ADA_ERR_ALIGNMENT = 3,    /* pointer / stride alignment rule violated      */
+  ADA_ERR_WORKSPACE = 4,    /* workspace smaller than *_workspace_size()     */
+  ADA_ERR_LAUNCH = 5,       /* CUDA reported an error at launch              */
+  ADA_ERR_TIMEOUT = 6,      /* a bounded device-side wait gave up            */
+  ADA_ERR_CUDA = 7          /* other CUDA runtime / driver failure           */
+};
+
+enum { ADA_DT_BF16 = 0, ADA_DT_F16 = 1 };
+
+/* Human-readable text for a status code (static storage). */
+ADA_API const char* ada_status_string(int status);
+/* ABI version of this library (bumped on any signature change). */
+ADA_API int ada_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * FP8 paged split-K decode attention
+ * Replaces fp8_kv_decode_group_kernel + its launch in Attention.forward
+ * (adallm/ops/attention.py:126-233, :359-414).
+ *
+ * q        [batch, num_heads, head_dim] (q_dtype), strides q_stride_b/q_stride_h, unit stride in D
+ * k_cache, v_cache  e4m3fn bytes; element (page, row, kv_head, d) at
+ *          page*kv_stride_page + row*kv_stride_tok + kv_head*kv_stride_head + d
+ *          (the reference layout [num_pages, page, Hkv, D], adallm/runtime/model_runner.py:137-169);
+ *          block ids outside [0, num_pages) are masked like the reference's -1 padding
+ * block_tables int32 [batch, >= max_pages] with row stride bt_stride, -1 padded
+ * context_lens int32 [batch]  (includes the current token; tokens past max_pages*page_size are ignored)
+ * window   0 = full attention; W > 0 attends to tokens [max(ctx - W, 0), ctx)
+ * k_scale, v_scale  per-tensor dequant scales of the cache (1.0 = reference)
+ * out      [batch, num_heads, head_dim] (out_dtype), contiguous
+ * Implemented: head_dim 128, num_heads/num_kv_heads in 1..8, page_size % 16 == 0.
+ * A zero-length sequence produces zeros.
+ * ---------------------------------------------------------------------- */
+ADA_API size_t ada_fp8_paged_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t max_pages,
+                                           int32_t page_size, int32_t head_dim);
+ADA_API int ada_fp8_paged_decode(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                         const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
+                         int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
+                         const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                         const int32_t* context_lens, int32_t batch, int32_t num_heads,
+                         int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float scale,
+                         float k_scale, float v_scale, int32_t window, void* out, int out_dtype,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * FP8 KV-cache store
+ * Replaces store_kvcache / store_kvcache_kernel (adallm/ops/attention.py:11-31, :236-251).
+ * key/value [num_tokens, num_kv_heads, head_dim] (in_dtype), row strides key_stride/value_stride,
+ * heads contiguous (stride head_dim).  Row slot_mapping[i] of the cache viewed as
+ * [-1, num_kv_heads*head_dim] receives e4m3(key[i] / k_scale) (round-to-nearest-even,
+ * saturating); slot -1 is skipped.  cache_row_stride = elements between slots.
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_store_kvcache_fp8(const void* key, const void* value, int in_dtype, int64_t num_tokens,
+                          int32_t num_kv_heads, int32_t head_dim, int64_t key_stride,
+                          int64_t value_stride, const int32_t* slot_mapping, uint8_t* k_cache,
+                          uint8_t* v_cache, int64_t cache_row_stride, float k_scale, float v_scale,
+                          void* stream);
+
+/* ------------------------------------------------------------------------
+ * RMSNorm family
+ * Replaces RMSNorm.rms_forward / add_rms_forward (adallm/ops/layernorm.py:16-40) and
+ * GemmaRMSNorm.rms_forward / add_rms_forward (adallm/ops/layernorm.py:64-92).
+ * x [rows, hidden] (row stride ldx); weight [hidden]; y [rows, hidden] (row stride ldy).
+ * residual == NULL: plain norm.  Otherwise sum = x + residual (row stride ld_res) is
+ * written back to residual_out (row stride ld_res_out; may alias residual) and normalised.
+ * gemma = 0: y = bf16(bf16(x*rsqrt) * w)   gemma = 1: y = bf16(x*rsqrt*(1+w))
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ld_res,
+                void* residual_out, int64_t ld_res_out, const void* weight, void* y, int64_t ldy,
+                int64_t rows, int32_t hidden, float eps, int gemma, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Rotary embedding (NeoX rotate-half) from the reference's fp32 cos/sin cache
+ * Replaces RotaryEmbedding.forward (adallm/ops/rotary_embedding.py:45-56).
+ * positions int64 [num_tokens]; cos_sin [max_position, head_dim] fp32 = [cos | sin];
+ * positions outside [0, max_position) are clamped into it (never read out of bounds).
+ * q [num_tokens, num_q_heads, head_dim] row stride q_stride (heads contiguous), k likewise;
+ * results go to q_out/k_out (contiguous [num_tokens, heads, head_dim]); may alias the inputs.
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_rope(const int64_t* positions, const void* q, int64_t q_stride, const void* k,
+             int64_t k_stride, void* q_out, void* k_out, int64_t num_tokens, int32_t num_q_heads,
+             int32_t num_kv_heads, int32_t head_dim, const float* cos_sin, int64_t max_position,
+             int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Gated activation: y[t, i] = act(x[t, i]) * x[t, I + i]
+ * Replaces SiluAndMul / GeluAndMul (adallm/ops/activation.py:6-26).  act 0 = SiLU, 1 = GELU(tanh).
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_gated_act(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows,
+                  int32_t inter, int act, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Token embedding gather: y[t] = table[ids[t]] (bf16/f16 rows of width hidden).
+ * Replaces the lookup of VocabParallelEmbedding.forward (adallm/ops/embed_head.py:28-42)
+ * at tensor-parallel size 1, and the per-rank masked lookup when vocab_start/vocab_end
+ * delimit this rank's shard (rows outside it are written as zeros).
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_embedding(const int64_t* ids, int64_t num_tokens, const void* table, int64_t vocab_start,
+                  int64_t vocab_end, int32_t hidden, void* y, int dtype, void* stream);
+
+/* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum), logits bf16/f16. */
+ADA_API int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
+               int64_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ADALLM_B200_H_ */
