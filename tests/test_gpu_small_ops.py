@@ -58,8 +58,11 @@ def test_rmsnorm(hidden, gemma, with_res):
     else:
         y = rms_norm(x.to(d), w.to(d), 1e-6, gemma=gemma)
         y_ref = (ol.gemma_rms_norm if gemma else ol.rms_norm)(x, w, 1e-6)
+    # a 1-ulp difference of the normalised value (rsqrt / reduction order) can become
+    # 2 ulps after the bf16 weight multiply of the Qwen variant
     frac, mx = bf16_ulp_mismatch(y.cpu(), y_ref)
-    assert mx <= 1 and frac < 0.02, (frac, mx)
+    assert mx <= 2 and frac < 0.01, (frac, mx)
+    assert rel_l2(y.float().cpu(), y_ref.float()) < 1e-3
 
 
 def test_norm_modules_per_head():
@@ -69,7 +72,7 @@ def test_norm_modules_per_head():
     y = m(x)
     assert y.shape == x.shape
     frac, mx = bf16_ulp_mismatch(y.cpu(), ol.rms_norm(x.cpu(), m.weight.cpu(), 1e-6))
-    assert mx <= 1 and frac < 0.02
+    assert mx <= 2 and frac < 0.01
     gm = GemmaRMSNorm(256).to(d).to(torch.bfloat16)
     x2 = torch.randn(3, 256, device=d, dtype=torch.bfloat16)
     y2, r2 = gm(x2, x2)
