@@ -137,6 +137,52 @@ ADA_API int ada_gated_act(const void* x, int64_t ldx, void* y, int64_t ldy, int6
 ADA_API int ada_embedding(const int64_t* ids, int64_t num_tokens, const void* table, int64_t vocab_start,
                   int64_t vocab_end, int32_t hidden, void* y, int dtype, void* stream);
 
+/* ------------------------------------------------------------------------
+ * NVFP4 linear: y[m, n] = sum_k x[m, k] * W[n, k] (+ bias[n])
+ * Replaces nvfp4_linear / nvfp4_gemm_kernel (adallm/ops/nvfp4_gemm.py:58-136, :460-564);
+ * W uses the reference's parameter layout (adallm/ops/linear.py:31-43):
+ *   w_packed  uint8 [N, K/2] (row stride ldw bytes), e2m1 codes, even k in the low nibble
+ *   scales    [N, K/16] e4m3 values (stored as fp16 by the reference loader, or raw bytes)
+ *   w_scale_2 fp32 per-tensor scale (device pointer to one float)
+ * The scales are first re-laid out once per weight with ada_nvfp4_prepack_scales into
+ * ada_nvfp4_sf_bytes(N, K) bytes (the layout the block-scaled tensor-core MMA reads;
+ * this is the post-load hook next to adallm/infra/loader.py:129-162).
+ * x [M, K] bf16/f16 (row stride ldx) is quantised on the device into `terms` NVFP4
+ * terms (1 = W4A4, 3 = within ~1e-3 of the fp32 dequantise-then-matmul result) and
+ * multiplied with tcgen05 kind::mxf4nvf4 MMAs.  y [M, N] bf16/f16, row stride ldy.
+ * Implemented: N % 128 == 0, K % 256 == 0, terms in 1..3.
+ * workspace: ada_nvfp4_linear_workspace_size(M, N, K, terms) bytes, 256-byte aligned,
+ * ZERO-FILLED before its first use; every call leaves it ready for the next call.  Calls
+ * that share a workspace must be ordered (same stream).
+ * ---------------------------------------------------------------------- */
+ADA_API size_t ada_nvfp4_sf_bytes(int64_t n, int64_t k);
+ADA_API int ada_nvfp4_prepack_scales(const void* scale, int scale_is_fp16, int64_t ld_scale, int64_t n,
+                                     int64_t k, uint8_t* sf_out, void* stream);
+ADA_API size_t ada_nvfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int terms);
+ADA_API int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                             const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                             const float* w_scale_2, int64_t n, const void* bias, void* y, int y_dtype,
+                             int64_t ldy, int terms, void* workspace, size_t workspace_bytes, void* stream);
+/* Same as ada_nvfp4_linear with an explicit split-K factor (0 = library choice; tests and tuning). */
+ADA_API int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                const float* w_scale_2, int64_t n, const void* bias, void* y, int y_dtype,
+                                int64_t ldy, int terms, int force_ksplit, void* workspace,
+                                size_t workspace_bytes, void* stream);
+/* The activation quantiser on its own (the first half of ada_nvfp4_linear; no reference
+ * counterpart -- the reference never quantises activations to e2m1).  Row m of x becomes
+ * `terms` NVFP4 terms sharing the fp32 row scale gx[m] = amax(row) / 2688:
+ *   xq  [terms][m_pad][k/2]               packed e2m1, even k in the low nibble
+ *   sfx [terms][m_pad/block_n][k/64][512] ue4m3 scales, MMA scale-factor layout
+ *   gx  [m_pad]                           (1.0 for the zero padding rows)
+ * with m_pad = ceil(m / block_n) * block_n and block_n in {16, 32, 64, 128}. */
+ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
+                                int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
+/* Reads the device error word of an NVFP4 workspace (0 = ok; bit 1/2/4 = a bounded
+ * pipeline wait timed out).  Synchronises `stream`.  Not capturable. */
+ADA_API int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,
+                                       unsigned int* status_out, void* stream);
+
 /* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum), logits bf16/f16. */
 ADA_API int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
                int64_t* out, void* stream);
