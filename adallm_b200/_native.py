@@ -43,6 +43,8 @@ _SIGS = {
     "ada_rmsnorm": (INT, [P, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, P]),
     "ada_rope": (INT, [P, P, I64, P, I64, P, P, I64, I32, I32, I32, P, I64, INT, P]),
     "ada_gated_act": (INT, [P, I64, P, I64, I64, I32, INT, INT, P]),
+    "ada_qk_norm_rope_store": (INT, [P, I64, I64, I32, I32, I32, P, P, F32, P, P, I64, P, P, P, F32, F32, P, P,
+                                     INT, P]),
     "ada_embedding": (INT, [P, I64, P, I64, I64, I32, P, INT, P]),
     "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P]),
     "ada_nvfp4_sf_bytes": (SZ, [I64, I64]),
@@ -52,6 +54,9 @@ _SIGS = {
     "ada_nvfp4_linear_ex": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I64, P, P, INT, I64, INT, INT, P, SZ, P]),
     "ada_nvfp4_workspace_status": (INT, [P, I64, I64, I64, INT, P, P]),
     "ada_nvfp4_act_quant": (INT, [P, INT, I64, I64, I64, INT, INT, P, P, P, P]),
+    "ada_nvfp4_block_n": (INT, [I64]),
+    "ada_nvfp4_gemm_workspace_size": (SZ, [I64, I64, I64, INT]),
+    "ada_nvfp4_gemm": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, P, INT, I64, INT, P, SZ, P]),
 }
 
 _lib = None

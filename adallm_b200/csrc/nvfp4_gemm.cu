@@ -485,10 +485,51 @@ static int dispatch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const G
   return ADA_ERR_UNSUPPORTED;
 }
 
+static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const float* gx, int m, int n, int k,
+                    const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w, const float* w_scale_2,
+                    const void* bias, void* y, int y_dtype, int64_t ldy, uint8_t* ctl, uint8_t* part,
+                    cudaStream_t st) {
+  CUtensorMap tmw, tmx;
+  if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, BM)) return ADA_ERR_CUDA;
+  if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2), (uint32_t)P.bn))
+    return ADA_ERR_CUDA;
+  GemmParams gp;
+  gp.sfw = sf_w;
+  gp.sfx = sfx;
+  gp.gx = gx;
+  gp.gw = w_scale_2;
+  gp.bias = bias;
+  gp.y = y;
+  gp.partial = reinterpret_cast<float*>(part);
+  gp.counters = reinterpret_cast<int*>(ctl);
+  gp.err = reinterpret_cast<unsigned int*>(ctl + (size_t)P.n_tiles * P.m_tiles * 4);
+  gp.M = m;
+  gp.N = n;
+  gp.K = k;
+  gp.ldy = (int)ldy;
+  gp.m_pad = P.m_pad;
+  gp.n_tiles = P.n_tiles;
+  gp.m_tiles = P.m_tiles;
+  gp.ksplit = P.ksplit;
+  gp.stages = P.stages;
+  gp.tmem_cols = P.tmem_cols;
+  gp.out_dtype = y_dtype;
+  return dispatch_gemm(tmw, tmx, gp, P, st);
+}
+
+// Workspace of the pre-quantised GEMM: control words + split-K partials only.
+static size_t gemm_ws_bytes(const Plan& P, int64_t n) {
+  size_t off = al256((size_t)P.n_tiles * P.m_tiles * 4 + 16);
+  if (P.ksplit > 1) off = al256(off + (size_t)P.ksplit * P.m_pad * (size_t)n * 4);
+  return off;
+}
+
 }  // namespace fp4
 }  // namespace ada
 
 using namespace ada;
+
+static inline size_t al256_pub(size_t x) { return (x + 255) & ~size_t(255); }
 
 extern "C" size_t ada_nvfp4_sf_bytes(int64_t n, int64_t k) {
   if (n <= 0 || k <= 0 || k % 64) return 0;
@@ -545,32 +586,8 @@ extern "C" int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int6
                                                            terms, P.bn, P.m_tiles, P.m_pad, xq, sfx, gx);
   ADA_CHECK_LAUNCH();
 
-  CUtensorMap tmw, tmx;
-  if (!fp4::make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, fp4::BM)) return ADA_ERR_CUDA;
-  if (!fp4::make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)terms * P.m_pad, (uint64_t)(k / 2), (uint32_t)P.bn))
-    return ADA_ERR_CUDA;
-  fp4::GemmParams gp;
-  gp.sfw = sf_w;
-  gp.sfx = sfx;
-  gp.gx = gx;
-  gp.gw = w_scale_2;
-  gp.bias = bias;
-  gp.y = y;
-  gp.partial = reinterpret_cast<float*>(ws + P.off_part);
-  gp.counters = reinterpret_cast<int*>(ws + P.off_ctl);
-  gp.err = reinterpret_cast<unsigned int*>(ws + P.off_ctl + (size_t)P.n_tiles * P.m_tiles * 4);
-  gp.M = (int)m;
-  gp.N = (int)n;
-  gp.K = (int)k;
-  gp.ldy = (int)ldy;
-  gp.m_pad = P.m_pad;
-  gp.n_tiles = P.n_tiles;
-  gp.m_tiles = P.m_tiles;
-  gp.ksplit = P.ksplit;
-  gp.stages = P.stages;
-  gp.tmem_cols = P.tmem_cols;
-  gp.out_dtype = y_dtype;
-  return fp4::dispatch_gemm(tmw, tmx, gp, P, st);
+  return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y, y_dtype,
+                       ldy, ws + P.off_ctl, ws + P.off_part, st);
 }
 
 extern "C" int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
@@ -612,4 +629,37 @@ extern "C" int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int6
   if (cudaMemcpyAsync(status_out, errp, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return ADA_ERR_CUDA;
   if (cudaStreamSynchronize(st) != cudaSuccess) return ADA_ERR_CUDA;
   return ADA_OK;
+}
+
+extern "C" int ada_nvfp4_block_n(int64_t m) {
+  if (m <= 0) return 0;
+  return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+}
+
+extern "C" size_t ada_nvfp4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int terms) {
+  fp4::Plan P;
+  if (fp4::make_plan(m, n, k, terms, 0, P) != ADA_OK) return 0;
+  return fp4::gemm_ws_bytes(P, n);
+}
+
+extern "C" int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
+                              int block_n, const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                              const float* w_scale_2, int64_t n, int64_t k, const void* bias, void* y, int y_dtype,
+                              int64_t ldy, int force_ksplit, void* workspace, size_t workspace_bytes, void* stream) {
+  if (m == 0) return ADA_OK;
+  if (!xq || !sfx || !gx || !w_packed || !sf_w || !w_scale_2 || !y || !workspace) return ADA_ERR_INVALID_ARG;
+  if (y_dtype != ADA_DT_BF16 && y_dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  if (ldy < n || ldw < k / 2) return ADA_ERR_INVALID_ARG;
+  fp4::Plan P;
+  int rc = fp4::make_plan(m, n, k, terms, force_ksplit, P);
+  if (rc != ADA_OK) return rc;
+  if (block_n != P.bn) return ADA_ERR_INVALID_ARG;
+  if (workspace_bytes < fp4::gemm_ws_bytes(P, n)) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)xq & 15) || ((uintptr_t)sfx & 15) || ((uintptr_t)w_packed & 15) || (ldw & 15) ||
+      ((uintptr_t)sf_w & 15) || ((uintptr_t)workspace & 255))
+    return ADA_ERR_ALIGNMENT;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const size_t part_off = al256_pub((size_t)P.n_tiles * P.m_tiles * 4 + 16);
+  return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y, y_dtype, ldy,
+                       ws, ws + part_off, reinterpret_cast<cudaStream_t>(stream));
 }

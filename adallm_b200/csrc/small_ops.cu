@@ -163,6 +163,96 @@ __global__ void __launch_bounds__(128) rope_kernel(const int64_t* __restrict__ p
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Fused decode prologue of the attention block (Qwen3Attention.forward,
+// adallm/architectures/qwen3.py:476-486): per token, per head of the fused qkv row
+//   q, k : RMSNorm over head_dim with q_norm / k_norm (skipped when the weight is null),
+//          then NeoX RoPE at positions[t]  (rotary_embedding.py:6-14)
+//   k, v : e4m3 store into the paged cache at slot_mapping[t] (attention.py:11-31)
+//   q    : written to q_out [T, hq, D]; k (normed + roped, bf16) optionally to k_out.
+// One CTA per token, one warp per head; a lane owns 4 consecutive elements and the
+// rotate-half partner lives 16 lanes away.  Implemented for head_dim == 128.
+template <typename T>
+__global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
+    const T* __restrict__ qkv, int64_t ld, int hq, int hkv, const T* __restrict__ qw, const T* __restrict__ kw,
+    float eps, const int64_t* __restrict__ pos, const float* __restrict__ cs, int64_t max_pos,
+    const int32_t* __restrict__ slots, uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, float k_scale,
+    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out) {
+  constexpr int D = 128;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nheads = hq + 2 * hkv;
+  const int64_t p = min(max(__ldg(pos + t), (int64_t)0), max_pos - 1);
+  const float* c = cs + p * D;
+  const int slot = __ldg(slots + t);
+  const int i0 = (lane & 15) * 4;  // rotation-pair index of this lane's first element
+  for (int h = warp; h < nheads; h += blockDim.x >> 5) {
+    const T* src = qkv + (int64_t)t * ld + (int64_t)h * D + lane * 4;
+    float x[4];
+    {
+      const uint2 u = *reinterpret_cast<const uint2*>(src);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] = to_f32(e[j]);
+    }
+    const bool is_q = h < hq, is_k = !is_q && h < hq + hkv;
+    if (is_q || is_k) {
+      const T* w = is_q ? qw : kw;
+      if (w) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss = fmaf(x[j], x[j], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rs = rsqrtf(ss / (float)D + eps);
+        const uint2 wu = *reinterpret_cast<const uint2*>(w + lane * 4);
+        const T* we = reinterpret_cast<const T*>(&wu);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)  // layernorm.py:24-25: cast, then weight multiply, cast again
+          x[j] = to_f32(from_f32<T>(__fmul_rn(to_f32(from_f32<T>(__fmul_rn(x[j], rs))), to_f32(we[j]))));
+      }
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float partner = __shfl_xor_sync(0xffffffffu, x[j], 16);
+        const float co = __ldg(c + i0 + j), si = __ldg(c + D / 2 + i0 + j);
+        y[j] = lane < 16 ? __fsub_rn(__fmul_rn(x[j], co), __fmul_rn(partner, si))
+                         : __fadd_rn(__fmul_rn(x[j], co), __fmul_rn(partner, si));
+        y[j] = to_f32(from_f32<T>(y[j]));
+      }
+      if (is_q) {
+        uint2 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) oe[j] = from_f32<T>(y[j]);
+        *reinterpret_cast<uint2*>(q_out + ((int64_t)t * hq + h) * D + lane * 4) = o;
+      } else {
+        if (k_out) {
+          uint2 o;
+          T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) oe[j] = from_f32<T>(y[j]);
+          *reinterpret_cast<uint2*>(k_out + ((int64_t)t * hkv + (h - hq)) * D + lane * 4) = o;
+        }
+        if (slot >= 0) {
+          float s[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) s[j] = k_scale != 1.f ? __fdiv_rn(y[j], k_scale) : y[j];
+          const uint32_t b = (uint32_t)f32x2_to_e4m3x2(s[0], s[1]) | ((uint32_t)f32x2_to_e4m3x2(s[2], s[3]) << 16);
+          *reinterpret_cast<uint32_t*>(kc + ((int64_t)slot * hkv + (h - hq)) * D + lane * 4) = b;
+        }
+      }
+    } else if (slot >= 0) {  // v head: straight e4m3 store
+      float s[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[j] = v_scale != 1.f ? __fdiv_rn(x[j], v_scale) : x[j];
+      const uint32_t b = (uint32_t)f32x2_to_e4m3x2(s[0], s[1]) | ((uint32_t)f32x2_to_e4m3x2(s[2], s[3]) << 16);
+      *reinterpret_cast<uint32_t*>(vc + ((int64_t)slot * hkv + (h - hq - hkv)) * D + lane * 4) = b;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.f, expf(-x))); }
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -327,6 +417,35 @@ extern "C" int ada_rope(const int64_t* positions, const void* q, int64_t q_strid
                                                                      (const __half*)k, k_stride, (__half*)q_out,
                                                                      (__half*)k_out, num_q_heads, num_kv_heads,
                                                                      head_dim, cos_sin, max_position);
+  ADA_CHECK_LAUNCH();
+  return ADA_OK;
+}
+
+extern "C" int ada_qk_norm_rope_store(const void* qkv, int64_t ld, int64_t num_tokens, int32_t num_q_heads,
+                                      int32_t num_kv_heads, int32_t head_dim, const void* q_norm_w,
+                                      const void* k_norm_w, float eps, const int64_t* positions, const float* cos_sin,
+                                      int64_t max_position, const int32_t* slot_mapping, uint8_t* k_cache,
+                                      uint8_t* v_cache, float k_scale, float v_scale, void* q_out, void* k_out,
+                                      int dtype, void* stream) {
+  if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return ADA_ERR_INVALID_ARG;
+  if (num_tokens == 0) return ADA_OK;
+  if (!qkv || !positions || !cos_sin || !slot_mapping || !k_cache || !v_cache || !q_out || max_position <= 0)
+    return ADA_ERR_INVALID_ARG;
+  if (!(k_scale > 0.f) || !(v_scale > 0.f)) return ADA_ERR_INVALID_ARG;
+  if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  if (head_dim != 128) return ADA_ERR_UNSUPPORTED;
+  if (ld < (int64_t)(num_q_heads + 2 * num_kv_heads) * head_dim) return ADA_ERR_INVALID_ARG;
+  if (((uintptr_t)qkv & 7) || (ld & 3) || ((uintptr_t)q_out & 7) || ((uintptr_t)k_out & 7) ||
+      ((uintptr_t)q_norm_w & 7) || ((uintptr_t)k_norm_w & 7) || ((uintptr_t)k_cache & 3) || ((uintptr_t)v_cache & 3))
+    return ADA_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define ADA_QK(T)                                                                                               \
+  small::qk_norm_rope_store_kernel<T><<<(unsigned)num_tokens, 256, 0, st>>>(                                     \
+      (const T*)qkv, ld, num_q_heads, num_kv_heads, (const T*)q_norm_w, (const T*)k_norm_w, eps, positions,       \
+      cos_sin, max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out)
+  if (dtype == ADA_DT_BF16) ADA_QK(__nv_bfloat16);
+  else ADA_QK(__half);
+#undef ADA_QK
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }

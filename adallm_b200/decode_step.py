@@ -1,0 +1,413 @@
+"""Qwen3-shape decode step built from the adallm_b200 kernels.
+
+This is the hot loop of the reference runtime -- ``ModelRunner.run_model`` replaying
+one CUDA graph of ``Qwen3DecoderLayer.forward`` x L (adallm/runtime/model_runner.py:307-323,
+adallm/architectures/qwen3.py:1358-1371, :471-487, :512-516) -- restated over this
+package's ops so it can be timed and checked on its own:
+
+    residual-add + RMSNorm            (adallm/ops/layernorm.py:28-40)
+    qkv_proj  NVFP4 (column-parallel)  (adallm/ops/linear.py:158-191)
+    q/k per-head RMSNorm, RoPE         (adallm/architectures/qwen3.py:481-484)
+    FP8 KV store + paged decode attn   (adallm/ops/attention.py:307-428)
+    o_proj    NVFP4 (row-parallel, all-reduce)   (adallm/ops/linear.py:193-215)
+    residual-add + RMSNorm, gate_up NVFP4, SiLU*up, down NVFP4 (+ all-reduce)
+    final RMSNorm, lm_head (bf16, vocab-parallel) and greedy argmax
+
+Tensor parallelism follows the reference's sharding exactly: column-parallel shards
+of q / k / v and gate / up rows, row-parallel shards of the K dimension of o_proj and
+down_proj with an NCCL all-reduce after them, head-sharded KV cache, vocab-sharded
+embedding / lm_head (adallm/ops/embed_head.py:9-66).
+
+Weights are random-init NVFP4 (random e2m1 codes, e4m3 block scales and a per-matrix
+fp32 scale_2, sized so every projection has roughly unit gain).  They are generated on
+the device from seeded generators per full (unsharded) matrix, so every tensor-parallel
+rank holds exactly its slice of the same model.
+"""
+from __future__ import annotations
+
+import math
+import zlib
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+from .nvfp4_gemm import prepack_scales, sf_bytes, workspace_bytes
+
+
+@dataclass
+class DecodeConfig:
+    num_layers: int = 36
+    hidden: int = 4096
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 12288
+    vocab: int = 151936
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    max_position: int = 40960
+    page_size: int = 16
+    terms: int = 3
+    tp_size: int = 1
+    tp_rank: int = 0
+
+    @property
+    def hq(self):
+        return self.num_heads // self.tp_size
+
+    @property
+    def hkv(self):
+        return self.num_kv_heads // self.tp_size
+
+    @property
+    def inter(self):
+        return self.intermediate // self.tp_size
+
+    @property
+    def vocab_shard(self):
+        return self.vocab // self.tp_size
+
+
+QWEN3_8B = DecodeConfig()
+
+
+@dataclass
+class NVFP4Weight:
+    packed: torch.Tensor      # uint8 [N, K/2]
+    scale: torch.Tensor       # fp16 [N, K/16]  (reference parameter layout)
+    scale_2: torch.Tensor     # fp32 []
+    sf: torch.Tensor = field(default=None)  # prepacked scale factors
+
+    @property
+    def n(self):
+        return self.packed.shape[0]
+
+    @property
+    def k(self):
+        return self.packed.shape[1] * 2
+
+
+def stable_seed(*parts) -> int:
+    """Process-independent seed (Python's str hash is salted per process)."""
+    return zlib.crc32(repr(parts).encode()) & 0x7FFFFFFF
+
+
+def _gen(seed: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def random_nvfp4(n: int, k: int, seed: int, device) -> tuple[torch.Tensor, torch.Tensor, float]:
+    """Full [n, k] random NVFP4 matrix: uniform e2m1 codes, e4m3 block scales in
+    [0.5, 2], scale_2 chosen for unit gain (E[code^2] = 8.5625 for uniform codes)."""
+    g = _gen(seed, device)
+    packed = torch.randint(0, 256, (n, k // 2), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    sbits = torch.randint(0x30, 0x41, (n, k // 16), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    scale = sbits.view(torch.float8_e4m3fn).to(torch.float16)
+    scale_2 = 1.0 / (math.sqrt(k) * math.sqrt(8.5625) * 1.1)
+    return packed, scale, scale_2
+
+
+class Qwen3DecodeEngine:
+    """Static-shape decode engine for batch ``max_batch`` (graph-capturable)."""
+
+    def __init__(self, cfg: DecodeConfig, device, max_batch: int, max_ctx: int, seed: int = 0,
+                 group=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.B = max_batch
+        self.max_pages_per_seq = -(-max_ctx // cfg.page_size)
+        self.group = group
+        self.seed = seed
+        self._init_weights()
+        self._alloc_state()
+
+    # ------------------------------------------------------------------ weights
+    def _sharded(self, kind: str, layer: int, parts: list[tuple[str, int]], k_full: int, split_k: bool) -> NVFP4Weight:
+        """Build this rank's shard of a (possibly fused) NVFP4 linear.
+
+        parts: [(name, full_rows)], concatenated per rank like QKVParallelLinear /
+        MergedColumnParallelLinear (adallm/ops/linear.py:138-191); split_k shards the
+        K dimension like RowParallelLinear (adallm/ops/linear.py:193-209)."""
+        c = self.cfg
+        d = self.device
+        packs, scales = [], []
+        scale_2 = None
+        for pi, (name, rows) in enumerate(parts):
+            seed = stable_seed(self.seed, kind, layer, name)
+            packed, scale, s2 = random_nvfp4(rows, k_full, seed, d)
+            scale_2 = s2 if scale_2 is None else scale_2  # one global scale per fused linear
+            if split_k:
+                kk = k_full // c.tp_size
+                packed = packed[:, c.tp_rank * kk // 2:(c.tp_rank + 1) * kk // 2]
+                scale = scale[:, c.tp_rank * kk // 16:(c.tp_rank + 1) * kk // 16]
+            else:
+                r = rows // c.tp_size
+                packed = packed[c.tp_rank * r:(c.tp_rank + 1) * r]
+                scale = scale[c.tp_rank * r:(c.tp_rank + 1) * r]
+            packs.append(packed.contiguous())
+            scales.append(scale.contiguous())
+        w = NVFP4Weight(torch.cat(packs).contiguous(), torch.cat(scales).contiguous(),
+                        torch.tensor(scale_2, dtype=torch.float32, device=d))
+        w.sf = prepack_scales(w.scale, w.n, w.k)
+        return w
+
+    def _init_weights(self):
+        c = self.cfg
+        d = self.device
+        D = c.head_dim
+        self.layers = []
+        for li in range(c.num_layers):
+            L = {}
+            L["qkv"] = self._sharded("qkv", li, [("q", c.num_heads * D), ("k", c.num_kv_heads * D),
+                                                 ("v", c.num_kv_heads * D)], c.hidden, False)
+            L["o"] = self._sharded("o", li, [("o", c.hidden)], c.num_heads * D, True)
+            L["gate_up"] = self._sharded("gu", li, [("gate", c.intermediate), ("up", c.intermediate)], c.hidden,
+                                         False)
+            L["down"] = self._sharded("down", li, [("down", c.hidden)], c.intermediate, True)
+            L["in_norm"] = torch.ones(c.hidden, dtype=torch.bfloat16, device=d)
+            L["post_norm"] = torch.ones(c.hidden, dtype=torch.bfloat16, device=d)
+            L["q_norm"] = torch.ones(D, dtype=torch.bfloat16, device=d)
+            L["k_norm"] = torch.ones(D, dtype=torch.bfloat16, device=d)
+            self.layers.append(L)
+        self.final_norm = torch.ones(c.hidden, dtype=torch.bfloat16, device=d)
+        v0 = c.tp_rank * c.vocab_shard
+        emb = torch.empty((c.vocab_shard, c.hidden), dtype=torch.bfloat16, device=d)
+        # generated in fixed chunks so every rank's shard equals the same rows of the full table
+        self._fill_rows(emb, "embed", v0)
+        self.embed = emb
+        lm = torch.empty((c.vocab_shard, c.hidden), dtype=torch.bfloat16, device=d)
+        self._fill_rows(lm, "lm_head", v0)
+        self.lm_head = lm
+        from .rotary_embedding import build_cos_sin_cache
+        self.cos_sin = build_cos_sin_cache(D, c.max_position, c.rope_theta, None, d).contiguous()
+
+    def _fill_rows(self, out: torch.Tensor, name: str, row0: int, chunk: int = 4096):
+        rows = out.shape[0]
+        first = row0 // chunk
+        last = (row0 + rows - 1) // chunk
+        for ci in range(first, last + 1):
+            g = _gen(stable_seed(self.seed, name, ci), self.device)
+            blk = (torch.randn((chunk, out.shape[1]), generator=g, device=self.device) * 0.02).to(torch.bfloat16)
+            lo = max(row0, ci * chunk)
+            hi = min(row0 + rows, (ci + 1) * chunk)
+            out[lo - row0:hi - row0] = blk[lo - ci * chunk:hi - ci * chunk]
+
+    # ------------------------------------------------------------------ state
+    def _alloc_state(self):
+        c = self.cfg
+        d = self.device
+        B, D = self.B, c.head_dim
+        bf = torch.bfloat16
+        self.num_pages = B * self.max_pages_per_seq
+        # [2, L, pages, page, Hkv, D] like ModelRunner.allocate_kv_cache (model_runner.py:137-169)
+        self.kv_cache = torch.zeros((2, c.num_layers, self.num_pages, c.page_size, c.hkv, D),
+                                    dtype=torch.float8_e4m3fn, device=d)
+        # per-step inputs (static for graph capture)
+        self.input_ids = torch.zeros(B, dtype=torch.int64, device=d)
+        self.positions = torch.zeros(B, dtype=torch.int64, device=d)
+        self.slot_mapping = torch.zeros(B, dtype=torch.int32, device=d)
+        self.context_lens = torch.zeros(B, dtype=torch.int32, device=d)
+        self.block_tables = torch.full((B, self.max_pages_per_seq), -1, dtype=torch.int32, device=d)
+        self.next_tokens = torch.zeros(B, dtype=torch.int64, device=d)
+        # activations
+        H, qkv_n = c.hidden, (c.hq + 2 * c.hkv) * D
+        self.hidden = torch.zeros((B, H), dtype=bf, device=d)
+        self.residual = torch.zeros((B, H), dtype=bf, device=d)
+        self.xnorm = torch.zeros((B, H), dtype=bf, device=d)
+        self.qkv = torch.zeros((B, qkv_n), dtype=bf, device=d)
+        self.q_rot = torch.zeros((B, c.hq, D), dtype=bf, device=d)
+        self.attn = torch.zeros((B, c.hq, D), dtype=bf, device=d)
+        self.gate_up = torch.zeros((B, 2 * c.inter), dtype=bf, device=d)
+        self.act = torch.zeros((B, c.inter), dtype=bf, device=d)
+        self.logits = torch.zeros((B, c.vocab_shard), dtype=bf, device=d)
+        # workspaces (zeroed once; the kernels leave them ready for reuse)
+        shapes = [(B, w.n, w.k) for w in self.layers[0].values() if isinstance(w, NVFP4Weight)]
+        self.gemm_ws = torch.zeros(max(workspace_bytes(*s, c.terms) for s in shapes), dtype=torch.uint8, device=d)
+        self.attn_ws_bytes = int(N.lib().ada_fp8_paged_decode_workspace_size(B, c.hq, self.max_pages_per_seq,
+                                                                             c.page_size, D))
+        self.attn_ws = torch.zeros(max(self.attn_ws_bytes, 256), dtype=torch.uint8, device=d)
+
+    # ------------------------------------------------------------------ ops
+    def _linear(self, x: torch.Tensor, w: NVFP4Weight, y: torch.Tensor, stream: int):
+        c = self.cfg
+        st = N.lib().ada_nvfp4_linear(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
+                                      w.packed.stride(0), w.sf.data_ptr(), w.scale_2.data_ptr(), w.n, None,
+                                      y.data_ptr(), 0, y.stride(0), c.terms, self.gemm_ws.data_ptr(),
+                                      self.gemm_ws.numel(), stream)
+        N.check(st, "NVFP4 kernel")
+
+    def _rms(self, x, w, y, stream, residual=None, rows=None, hidden=None):
+        c = self.cfg
+        hidden = hidden or x.shape[-1]
+        rows = rows or x.numel() // hidden
+        if residual is None:
+            st = N.lib().ada_rmsnorm(x.data_ptr(), hidden, None, 0, None, 0, w.data_ptr(), y.data_ptr(), hidden,
+                                     rows, hidden, c.rms_eps, 0, 0, stream)
+        else:
+            st = N.lib().ada_rmsnorm(x.data_ptr(), hidden, residual.data_ptr(), hidden, residual.data_ptr(), hidden,
+                                     w.data_ptr(), y.data_ptr(), hidden, rows, hidden, c.rms_eps, 0, 0, stream)
+        N.check(st, "rms_norm")
+
+    def _all_reduce(self, t: torch.Tensor):
+        if self.cfg.tp_size > 1:
+            dist.all_reduce(t, group=self.group)
+
+    def forward(self):
+        """One decode step for the static batch: reads input_ids / positions / slot_mapping /
+        context_lens / block_tables, writes next_tokens (greedy) and the KV cache."""
+        c = self.cfg
+        B, D = self.B, c.head_dim
+        lib = N.lib()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        v0 = c.tp_rank * c.vocab_shard
+        N.check(lib.ada_embedding(self.input_ids.data_ptr(), B, self.embed.data_ptr(), v0, v0 + c.vocab_shard,
+                                  c.hidden, self.hidden.data_ptr(), 0, stream), "embedding")
+        self._all_reduce(self.hidden)
+        qn, kn = c.hq * D, c.hkv * D
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                self.residual.copy_(self.hidden)
+                self._rms(self.hidden, L["in_norm"], self.xnorm, stream)
+            else:
+                self._rms(self.hidden, L["in_norm"], self.xnorm, stream, residual=self.residual)
+            self._linear(self.xnorm, L["qkv"], self.qkv, stream)
+            kc, vc = self.kv_cache[0, li], self.kv_cache[1, li]
+            # q/k RMSNorm + RoPE + FP8 KV store in one kernel (qwen3.py:481-486, attention.py:311-312)
+            N.check(lib.ada_qk_norm_rope_store(self.qkv.data_ptr(), self.qkv.stride(0), B, c.hq, c.hkv, D,
+                                               L["q_norm"].data_ptr(), L["k_norm"].data_ptr(), c.rms_eps,
+                                               self.positions.data_ptr(), self.cos_sin.data_ptr(),
+                                               self.cos_sin.shape[0], self.slot_mapping.data_ptr(), kc.data_ptr(),
+                                               vc.data_ptr(), 1.0, 1.0, self.q_rot.data_ptr(), None, 0, stream),
+                    "qk_norm_rope_store")
+            N.check(lib.ada_fp8_paged_decode(self.q_rot.data_ptr(), 0, qn, D, kc.data_ptr(), vc.data_ptr(),
+                                             kc.stride(0), kc.stride(1), kc.stride(2), self.num_pages,
+                                             self.block_tables.data_ptr(), self.block_tables.stride(0),
+                                             self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv,
+                                             D, c.page_size, D ** -0.5, 1.0, 1.0, 0, self.attn.data_ptr(), 0,
+                                             self.attn_ws.data_ptr(), self.attn_ws_bytes, stream), "attention")
+            self._linear(self.attn.view(B, qn), L["o"], self.hidden, stream)
+            self._all_reduce(self.hidden)
+            self._rms(self.hidden, L["post_norm"], self.xnorm, stream, residual=self.residual)
+            self._linear(self.xnorm, L["gate_up"], self.gate_up, stream)
+            N.check(lib.ada_gated_act(self.gate_up.data_ptr(), 2 * c.inter, self.act.data_ptr(), c.inter, B, c.inter,
+                                      0, 0, stream), "silu_and_mul")
+            self._linear(self.act, L["down"], self.hidden, stream)
+            self._all_reduce(self.hidden)
+        self._rms(self.hidden, self.final_norm, self.xnorm, stream, residual=self.residual)
+        torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
+        self._argmax(stream)
+
+    def _argmax(self, stream):
+        c = self.cfg
+        N.check(N.lib().ada_argmax(self.logits.data_ptr(), c.vocab_shard, self.B, c.vocab_shard, 0,
+                                   self.next_tokens.data_ptr(), stream), "argmax")
+        if c.tp_size > 1:
+            # vocab-parallel greedy pick: gather (max, index) per rank, take the first global maximum
+            loc = self.logits.float().gather(1, self.next_tokens.view(-1, 1)).view(-1)
+            pair = torch.stack([loc, (self.next_tokens + c.tp_rank * c.vocab_shard).float()], 1)
+            allp = [torch.empty_like(pair) for _ in range(c.tp_size)]
+            dist.all_gather(allp, pair, group=self.group)
+            vals = torch.stack([p[:, 0] for p in allp], 1)
+            idx = torch.stack([p[:, 1] for p in allp], 1)
+            best = vals.argmax(dim=1, keepdim=True)
+            self.next_tokens.copy_(idx.gather(1, best).view(-1).to(torch.int64))
+
+    # ------------------------------------------------------------------ graphs
+    def advance(self):
+        """Device-side bookkeeping of one generated token (the next step's inputs), the
+        on-device counterpart of ModelRunner.prepare_decode (model_runner.py:278-298)."""
+        page = self.cfg.page_size
+        self.input_ids.copy_(self.next_tokens)
+        self.positions.add_(1)
+        self.context_lens.add_(1)
+        pg = torch.div(self.positions, page, rounding_mode="floor").unsqueeze(1)
+        blk = self.block_tables.gather(1, pg).squeeze(1).to(torch.int64)
+        self.slot_mapping.copy_((blk * page + self.positions % page).to(torch.int32))
+
+    def capture(self, with_advance: bool = False) -> torch.cuda.CUDAGraph:
+        """Capture forward() (and optionally advance()) into one CUDA graph, the way the
+        reference captures its decode step (model_runner.py:333-368)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):  # warm-up outside capture (sets kernel attributes, NCCL comms)
+            self.forward()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.forward()
+            if with_advance:
+                self.advance()
+        return g
+
+    def kernels_per_step(self) -> int:
+        """adallm_b200 kernels launched by one forward(): embedding, per layer (norm, act-quant+GEMM x4,
+        qk-norm/rope/store, attention split + reduce, norm, SiLU*up), final norm, argmax."""
+        return 1 + self.cfg.num_layers * 14 + 2
+
+    def export_cpu_weights(self) -> dict:
+        """CPU copies in the reference parameter layout (tensor-parallel size 1 only)."""
+        assert self.cfg.tp_size == 1
+        layers = []
+        for L in self.layers:
+            d = {}
+            for name in ("qkv", "o", "gate_up", "down"):
+                w = L[name]
+                d[name] = (w.packed.cpu(), w.scale.cpu(), float(w.scale_2.item()))
+            for name in ("in_norm", "post_norm", "q_norm", "k_norm"):
+                d[name] = L[name].cpu()
+            layers.append(d)
+        return dict(layers=layers, embed=self.embed.cpu(), lm_head=self.lm_head.cpu(),
+                    final_norm=self.final_norm.cpu(), cos_sin=self.cos_sin.cpu())
+
+
+class DecodeSession:
+    """Host-side sequence bookkeeping for a static batch, mirroring ModelRunner.prepare_decode
+    (adallm/runtime/model_runner.py:278-298): every sequence owns a seeded random set of pages
+    of the pool (as a block manager would hand out), and each step uploads token ids,
+    positions, slot_mapping and context_lens from pinned host memory."""
+
+    def __init__(self, engine: Qwen3DecodeEngine, seed: int = 0):
+        self.e = engine
+        B, P = engine.B, engine.max_pages_per_seq
+        g = torch.Generator().manual_seed(seed)
+        perm = torch.randperm(engine.num_pages, generator=g).to(torch.int32)
+        self.block_tables = perm.view(B, P).contiguous()
+        engine.block_tables.copy_(self.block_tables)
+        self.lens = torch.zeros(B, dtype=torch.int64)
+        pin = torch.cuda.is_available()
+        self.h_ids = torch.zeros(B, dtype=torch.int64).pin_memory() if pin else torch.zeros(B, dtype=torch.int64)
+        self.h_pos = torch.zeros(B, dtype=torch.int64).pin_memory() if pin else torch.zeros(B, dtype=torch.int64)
+        self.h_slot = torch.zeros(B, dtype=torch.int32).pin_memory() if pin else torch.zeros(B, dtype=torch.int32)
+        self.h_ctx = torch.zeros(B, dtype=torch.int32).pin_memory() if pin else torch.zeros(B, dtype=torch.int32)
+        self.h_out = torch.zeros(B, dtype=torch.int64).pin_memory() if pin else torch.zeros(B, dtype=torch.int64)
+
+    H2D_BYTES_PER_STEP = property(lambda self: self.e.B * (8 + 8 + 4 + 4))
+    D2H_BYTES_PER_STEP = property(lambda self: self.e.B * 8)
+
+    def prepare(self, tokens: torch.Tensor):
+        page = self.e.cfg.page_size
+        pos = self.lens
+        self.h_ids.copy_(tokens)
+        self.h_pos.copy_(pos)
+        blk = self.block_tables.gather(1, (pos // page).unsqueeze(1)).squeeze(1).to(torch.int64)
+        self.h_slot.copy_((blk * page + pos % page).to(torch.int32))
+        self.h_ctx.copy_((pos + 1).to(torch.int32))
+
+    def upload(self):
+        e = self.e
+        e.input_ids.copy_(self.h_ids, non_blocking=True)
+        e.positions.copy_(self.h_pos, non_blocking=True)
+        e.slot_mapping.copy_(self.h_slot, non_blocking=True)
+        e.context_lens.copy_(self.h_ctx, non_blocking=True)
+
+    def download(self) -> torch.Tensor:
+        self.h_out.copy_(self.e.next_tokens, non_blocking=True)
+        torch.cuda.current_stream(self.e.device).synchronize()
+        return self.h_out.clone()
+
+    def commit(self):
+        self.lens += 1

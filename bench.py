@@ -1,0 +1,358 @@
+#!/usr/bin/env python
+"""Decode throughput of the adallm_b200 hot path on B200.
+
+Metric: decode tok/s of a Qwen3-8B-shape model at batch 16 -- 36 layers,
+hidden 4096, 32 query / 8 KV heads of 128, SwiGLU 12288, vocab 151936, random-init NVFP4
+weights, FP8 paged KV (page 16), greedy decode after a 16-token random prompt.
+
+One "step" = one full decode step for the 16 sequences (all layers, lm_head, greedy pick),
+replayed from a CUDA graph.  The weights (~5.2 GB per step at TP=1) are far larger than the
+126 MB L2, so every step streams them from HBM; no L2 flush is needed.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+N > 1 runs tensor parallelism over N ranks (launched with torch.distributed.run, NCCL
+all-reduce after the row-parallel projections), so `scaling` is "strong": the batch of 16
+is fixed and split by heads / columns across the GPUs.
+
+`--impl reference` times the reference's own CPU path (dequantise-then-compute, restated
+in oracle/) on the host cores; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (Qwen3-8B shape, bs16)"
+WORKLOAD = ("Qwen3-8B-shape decode step: 36 layers, hidden 4096, 32q/8kv heads x128, SwiGLU 12288, "
+            "vocab 151936, random-init NVFP4 weights, FP8 paged KV page 16, batch 16, 16-token prompt, greedy")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=36, help="decoder layers (36 = the Qwen3-8B shape)")
+    ap.add_argument("--prompt", type=int, default=16)
+    ap.add_argument("--terms", type=int, default=3, help="NVFP4 activation terms (1 = W4A4)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-reps", type=int, default=5)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    """dram bytes per launch of the GEMM kernel from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "nvfp4_gemm_decode_bs16.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in names.items():
+                    if mask & bit:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_baseline(args, ctx):
+    from oracle.baseline import CpuDecodeSample
+    t0 = time.perf_counter()
+    s = CpuDecodeSample(args.layers, 4096, 32, 8, 128, 12288, 151936, args.batch, ctx)
+    setup = time.perf_counter() - t0
+    step, one, head = s.estimate_step_seconds(args.cpu_reps)
+    return {"value": args.batch / step, "unit": "tok/s", "cores": s.threads, "kind": "port",
+            "sample": (f"1 of {args.layers} decoder layers (full size, weights dequantised to bf16 as the "
+                       f"reference's dequant mode) + full lm_head at ctx {ctx}, median of {args.cpu_reps} steps "
+                       f"({one * 1e3:.1f} ms/layer-step, lm_head {head * 1e3:.1f} ms), scaled to "
+                       f"{args.layers} layers; setup {setup:.0f} s untimed")}
+
+
+def run_reference(args, rank):
+    """The reference's CPU path (oracle restatement) on the host cores: rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    from oracle.baseline import CpuDecodeSample
+    ctx = args.prompt + args.warmup + args.steps // 2
+    s = CpuDecodeSample(args.layers, 4096, 32, 8, 128, 12288, 151936, args.batch, ctx)
+    for _ in range(max(1, args.warmup // 4)):
+        s.one_step()
+    # each step: one sampled layer-step; the metric scales the median to all layers
+    steps = max(3, min(args.steps, 16))
+    ones = sorted(s.one_step() for _ in range(steps))
+    heads = sorted(s.lm_head_time() for _ in range(3))
+    t1, th = ones[len(ones) // 2], heads[len(heads) // 2]
+    step_s = th + args.layers * max(t1 - th, 0.0)
+    value = args.batch / step_s
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 (dequantised NVFP4 weights)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": args.batch, "seq_len": ctx,
+                       "parallelism": "cpu", "layers": args.layers},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": s.threads, "kind": "port",
+                             "sample": f"median of {steps} one-layer decode steps + lm_head, scaled to "
+                                       f"{args.layers} layers (reference dequant mode on the host cores)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    del torch
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from adallm_b200 import _native as N
+    from adallm_b200.decode_step import DecodeConfig, Qwen3DecodeEngine, DecodeSession
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = dist.group.WORLD if world > 1 else None
+    cfg = DecodeConfig(num_layers=args.layers, terms=args.terms, tp_size=world, tp_rank=rank)
+    B = args.batch
+    total_steps = args.prompt + 2 * (args.warmup + args.steps) + 8
+    engine = Qwen3DecodeEngine(cfg, dev, B, max_ctx=total_steps + 16, seed=0, group=group)
+    sess = DecodeSession(engine, seed=0)
+    g_plain = engine.capture(with_advance=False)
+    g_adv = engine.capture(with_advance=True)
+
+    # prompt (16 random ids per sequence) fed through the decode step token by token
+    gen = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (B, args.prompt), generator=gen)
+    toks = None
+    for i in range(args.prompt):
+        sess.prepare(prompt[:, i])
+        sess.upload()
+        g_plain.replay()
+        toks = sess.download()
+        sess.commit()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(ms: float) -> float:
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+    # ---------------- value: device-resident step loop (graph = forward + on-device advance)
+    sess.prepare(toks)
+    sess.upload()
+    for _ in range(args.warmup):
+        g_adv.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            g_adv.replay()
+        e1.record(stream)
+        e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = B * args.steps / (ms / 1e3)
+    # sync host bookkeeping with the device-side advance (warmup + steps tokens were generated)
+    sess.lens += args.warmup + args.steps
+    toks = engine.input_ids.cpu()
+
+    # ---------------- e2e: host-fed steps through the session (H2D inputs, D2H tokens every step)
+    for _ in range(args.warmup):
+        sess.prepare(toks)
+        sess.upload()
+        g_plain.replay()
+        toks = sess.download()
+        sess.commit()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        sess.prepare(toks)
+        sess.upload()
+        g_plain.replay()
+        toks = sess.download()
+        sess.commit()
+    f1.record(stream)
+    f1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    e2e = B * args.steps / (e2e_ms / 1e3)
+
+    # ---------------- roofline of the dominant kernel: the NVFP4 tensor-core GEMM, timed alone over
+    # every projection of every layer (cold weights: 36 layers x 108 MB >> L2)
+    m = B
+    bn = N.lib().ada_nvfp4_block_n(m)
+    lin = [(L[name]) for L in engine.layers for name in ("qkv", "o", "gate_up", "down")]
+    kmax = max(w.k for w in lin)
+    xq = torch.zeros(cfg.terms * bn * kmax // 2, dtype=torch.uint8, device=dev)
+    sfx = torch.zeros(cfg.terms * (kmax // 64) * 512, dtype=torch.uint8, device=dev)
+    gx = torch.zeros(bn, dtype=torch.float32, device=dev)
+    xin = torch.randn((m, kmax), device=dev, dtype=torch.bfloat16)
+    ys = {w.n: torch.empty((m, w.n), device=dev, dtype=torch.bfloat16) for w in lin}
+    wsb = max(int(N.lib().ada_nvfp4_gemm_workspace_size(m, w.n, w.k, cfg.terms)) for w in lin)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    sp = stream.cuda_stream
+    quant = {}
+    for kk in sorted({w.k for w in lin}):
+        N.check(N.lib().ada_nvfp4_act_quant(xin.data_ptr(), 0, kmax, m, kk, cfg.terms, bn, xq.data_ptr(),
+                                            sfx.data_ptr(), gx.data_ptr(), sp), "act_quant")
+        quant[kk] = (xq.clone(), sfx.clone(), gx.clone())
+
+    def gemm_pass():
+        for w in lin:
+            a, b, c_ = quant[w.k]
+            N.check(N.lib().ada_nvfp4_gemm(a.data_ptr(), b.data_ptr(), c_.data_ptr(), m, cfg.terms, bn,
+                                           w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                           w.scale_2.data_ptr(), w.n, w.k, None, ys[w.n].data_ptr(), 0, w.n, 0,
+                                           ws.data_ptr(), ws.numel(), sp), "gemm")
+
+    for _ in range(3):
+        gemm_pass()
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    r0.record(stream)
+    for _ in range(reps):
+        gemm_pass()
+    r1.record(stream)
+    r1.synchronize()
+    launches = reps * len(lin)
+    gemm_ms = r0.elapsed_time(r1) / launches
+    alg_bytes = sum(w.n * w.k // 2 + w.n * w.k // 16 + m * w.k * 2 + m * w.n * 2 for w in lin) / len(lin)
+    peak, peak_kind = measured_peaks()
+    achieved = alg_bytes / (gemm_ms / 1e3) / 1e9
+    traffic = traffic_from_profile()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                "kernel": "adallm_b200 nvfp4 gemm_kernel (tcgen05 mxf4nvf4)",
+                "alg_bytes_per_launch": int(alg_bytes), "us_per_launch": round(gemm_ms * 1e3, 3),
+                "launch_mix": "qkv/o/gate_up/down of all layers, batch 16"}
+
+    ctx_end = int(sess.lens.max().item())
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, ctx=args.prompt + args.warmup + args.steps // 2)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": ctx_end,
+                           "parallelism": f"tp{world}", "layers": cfg.num_layers, "nvfp4_act_terms": cfg.terms,
+                           "l2": "inputs larger than L2 (every step streams ~5.2 GB of weights at tp1)"},
+                "roofline": roofline,
+                "cpu_baseline": cpu,
+                "e2e": {"value": round(e2e, 2), "unit": "tok/s",
+                        "h2d_bytes_per_step": sess.H2D_BYTES_PER_STEP, "d2h_bytes_per_step": sess.D2H_BYTES_PER_STEP,
+                        "ms_per_step": round(e2e_ms / args.steps, 4)},
+                "gpu_launches": engine.kernels_per_step() * args.steps,
+                "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    del g_plain, g_adv  # graphs holding NCCL work go before the process group
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world != 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch.distributed as dist
+    if world > 1:
+        import torch
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

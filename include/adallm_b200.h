@@ -122,6 +122,22 @@ ADA_API int ada_rope(const int64_t* positions, const void* q, int64_t q_stride, 
              int dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Fused attention-block prologue for decode: per token of the fused qkv row
+ * [q heads | k heads | v heads] (row stride ld): q/k RMSNorm over head_dim with
+ * q_norm_w / k_norm_w (adallm/architectures/qwen3.py:481-483; NULL weight = no norm),
+ * RoPE from the fp32 cos/sin cache (adallm/ops/rotary_embedding.py:45-56), e4m3 store
+ * of k and v at slot_mapping[t] into caches laid out [slots, num_kv_heads, head_dim]
+ * (adallm/ops/attention.py:236-251), q written to q_out [T, num_q_heads, head_dim];
+ * k_out (optional, may be NULL) receives the normalised, rotated k.  head_dim 128.
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_qk_norm_rope_store(const void* qkv, int64_t ld, int64_t num_tokens, int32_t num_q_heads,
+                                   int32_t num_kv_heads, int32_t head_dim, const void* q_norm_w,
+                                   const void* k_norm_w, float eps, const int64_t* positions,
+                                   const float* cos_sin, int64_t max_position, const int32_t* slot_mapping,
+                                   uint8_t* k_cache, uint8_t* v_cache, float k_scale, float v_scale,
+                                   void* q_out, void* k_out, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * Gated activation: y[t, i] = act(x[t, i]) * x[t, I + i]
  * Replaces SiluAndMul / GeluAndMul (adallm/ops/activation.py:6-26).  act 0 = SiLU, 1 = GELU(tanh).
  * ---------------------------------------------------------------------- */
@@ -178,6 +194,17 @@ ADA_API int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int64_t
  * with m_pad = ceil(m / block_n) * block_n and block_n in {16, 32, 64, 128}. */
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
+/* The tensor-core GEMM on its own, for activations already quantised by
+ * ada_nvfp4_act_quant (or by a fused producer writing the same layout) with
+ * block_n == ada_nvfp4_block_n(m).  workspace: ada_nvfp4_gemm_workspace_size(m, n, k, terms)
+ * bytes, 256-byte aligned, zero-filled before first use (left ready for the next call). */
+ADA_API int ada_nvfp4_block_n(int64_t m);
+ADA_API size_t ada_nvfp4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int terms);
+ADA_API int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
+                           int block_n, const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                           const float* w_scale_2, int64_t n, int64_t k, const void* bias, void* y,
+                           int y_dtype, int64_t ldy, int force_ksplit, void* workspace,
+                           size_t workspace_bytes, void* stream);
 /* Reads the device error word of an NVFP4 workspace (0 = ok; bit 1/2/4 = a bounded
  * pipeline wait timed out).  Synchronises `stream`.  Not capturable. */
 ADA_API int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,

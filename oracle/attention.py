@@ -77,6 +77,7 @@ def paged_decode(q, k_cache_bits, v_cache_bits, block_tables, context_lens, scal
     group = hq // hkv
     out = torch.zeros((b, hq, d), dtype=torch.float64)
     bt = np.asarray(block_tables)
+    head_map = torch.arange(hq) // group
     for i in range(b):
         ctx = int(context_lens[i])
         if ctx == 0:
@@ -88,13 +89,13 @@ def paged_decode(q, k_cache_bits, v_cache_bits, block_tables, context_lens, scal
         toks, pages = toks[valid], pages[valid]
         if toks.size == 0:
             continue
-        kk = kf[torch.from_numpy(pages.astype(np.int64)), torch.from_numpy(toks % page)]  # [n, Hkv, D]
-        vv = vf[torch.from_numpy(pages.astype(np.int64)), torch.from_numpy(toks % page)]
-        for h in range(hq):
-            kh = h // group
-            s = (kk[:, kh, :] @ q[i, h]) * float(scale)
-            p = torch.softmax(s, dim=0)
-            out[i, h] = p @ vv[:, kh, :]
+        pi = torch.from_numpy(pages.astype(np.int64))
+        ti = torch.from_numpy(toks % page)
+        kk = kf[pi, ti][:, head_map]  # [n, Hq, D] (GQA repeat)
+        vv = vf[pi, ti][:, head_map]
+        s = torch.einsum("nhd,hd->nh", kk, q[i]) * float(scale)
+        p = torch.softmax(s, dim=0)
+        out[i] = torch.einsum("nh,nhd->hd", p, vv)
     return out.to(torch.float32).numpy()
 
 

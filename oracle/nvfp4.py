@@ -150,6 +150,23 @@ def dequant_nvfp4(packed: np.ndarray, scale: np.ndarray, scale_2, group_size: in
     return v.reshape(n, k).astype(np.float32)
 
 
+def dequant_nvfp4_torch(packed, scale, scale_2, group_size: int = 16, dtype=None):
+    """Same arithmetic as dequant_nvfp4 (adallm/infra/nvfp4.py:36-77) in multi-threaded CPU
+    torch, for the large one-time dequantisation of the timed CPU baseline."""
+    import torch
+    p = torch.as_tensor(packed)
+    n, khalf = p.shape
+    lut = torch.from_numpy(E2M1_LUT)
+    vals = torch.empty((n, khalf * 2), dtype=torch.float32)
+    vals[:, 0::2] = lut[(p & 0x0F).long()]
+    vals[:, 1::2] = lut[(p >> 4).long()]
+    s = torch.as_tensor(scale).float()
+    if scale_2 is not None:
+        s = s * float(scale_2)
+    out = (vals.view(n, -1, group_size) * s.view(n, -1, 1)).view(n, khalf * 2)
+    return out if dtype is None else out.to(dtype)
+
+
 def quantize_weight(w: np.ndarray, group_size: int = 16):
     """Fixture quantiser for synthetic NVFP4 weights (no reference counterpart).
 

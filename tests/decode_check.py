@@ -1,0 +1,56 @@
+"""Greedy-token agreement between the B200 decode engine and the CPU oracle decoder
+(teacher-forced: both consume the oracle's token each step, so one disagreement does
+not cascade).  Used by tests/test_gpu_decode.py and __graft_entry__.smoke()."""
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+from oracle.decode import OracleDecoder
+from adallm_b200.decode_step import DecodeConfig, Qwen3DecodeEngine, DecodeSession
+
+
+def small_config(layers: int) -> DecodeConfig:
+    return DecodeConfig(num_layers=layers, hidden=1024, num_heads=8, num_kv_heads=2, head_dim=128,
+                        intermediate=3072, vocab=4096, max_position=4096, page_size=16)
+
+
+def run_agreement(layers=2, steps=8, batch=4, prompt=4, graph=True, return_logits=False):
+    d = torch.device("cuda:0")
+    cfg = small_config(layers)
+    eng = Qwen3DecodeEngine(cfg, d, batch, max_ctx=prompt + steps + 8, seed=1)
+    sess = DecodeSession(eng, seed=1)
+    w = eng.export_cpu_weights()
+    ocfg = SimpleNamespace(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
+                           num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, intermediate=cfg.intermediate,
+                           rms_eps=cfg.rms_eps, page_size=cfg.page_size)
+    oracle = OracleDecoder(ocfg, w, exact=True)
+    kc = [np.zeros((eng.num_pages, cfg.page_size, cfg.num_kv_heads, cfg.head_dim), np.uint8) for _ in range(layers)]
+    vc = [np.zeros_like(kc[0]) for _ in range(layers)]
+    g = eng.capture() if graph else None
+    gen = torch.Generator().manual_seed(3)
+    tokens = torch.randint(0, cfg.vocab, (batch, prompt), generator=gen)
+    agree, total = 0, 0
+    logit_err = []
+    cur = tokens[:, 0]
+    for i in range(prompt + steps):
+        sess.prepare(cur)
+        sess.upload()
+        if g is not None:
+            g.replay()
+        else:
+            eng.forward()
+        ours = sess.download()
+        logits = oracle.step(sess.h_ids.clone(), sess.h_pos.clone(), sess.h_slot.numpy().copy(),
+                             sess.h_ctx.numpy().copy(), sess.block_tables.numpy(), kc, vc)
+        theirs = logits.argmax(dim=1)
+        sess.commit()
+        if i >= prompt - 1:
+            agree += int((ours == theirs).sum())
+            total += batch
+        cur = tokens[:, i + 1] if i + 1 < prompt else theirs
+        logit_err.append(float((eng.logits.float().cpu() - logits).norm() / logits.norm()))
+    frac = agree / max(total, 1)
+    return (frac, logit_err) if return_logits else frac

@@ -138,3 +138,11 @@ def test_store_kvcache_oracle_skips_minus_one():
     oa.store_kvcache(key, val, kc, vc, np.array([5, -1, 0]))
     assert (nv.e4m3_decode(kc.reshape(-1, 16)[5]) == 1).all() and (nv.e4m3_decode(vc.reshape(-1, 16)[0]) == -1).all()
     assert (kc.reshape(-1, 16)[[1, 2, 3, 4, 6]] == 0).all()
+
+
+def test_torch_dequant_matches_numpy(golden_dir):
+    g = _load(golden_dir, "golden_nvfp4.npz")
+    a = nv.dequant_nvfp4(g["packed"], g["scale_fp16"].astype(np.float32), g["scale_2"])
+    b = nv.dequant_nvfp4_torch(torch.from_numpy(g["packed"]), torch.from_numpy(g["scale_fp16"]).float(),
+                               float(g["scale_2"]))
+    np.testing.assert_array_equal(a, b.numpy())
