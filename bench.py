@@ -298,6 +298,24 @@ def run_ours(args, rank, world, local_rank):
     r1.synchronize()
     launches = reps * len(lin)
     gemm_ms = r0.elapsed_time(r1) / launches
+    per_shape = {}
+    for name in ("qkv", "o", "gate_up", "down"):
+        ws_ = [L[name] for L in engine.layers]
+        w0 = ws_[0]
+        a, b, c_ = quant[w0.k]
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(reps):
+            for w in ws_:
+                N.check(N.lib().ada_nvfp4_gemm(a.data_ptr(), b.data_ptr(), c_.data_ptr(), m, cfg.terms, bn,
+                                               w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                               w.scale_2.data_ptr(), w.n, w.k, None, ys[w.n].data_ptr(), 0, w.n,
+                                               0, ws.data_ptr(), ws.numel(), sp), "gemm")
+        s1.record(stream)
+        s1.synchronize()
+        us = s0.elapsed_time(s1) / (reps * len(ws_)) * 1e3
+        nb = w0.n * w0.k // 2 + w0.n * w0.k // 16 + m * w0.k * 2 + m * w0.n * 2
+        per_shape[name] = {"n": w0.n, "k": w0.k, "us": round(us, 2), "gbs": round(nb / us / 1e3, 1)}
     alg_bytes = sum(w.n * w.k // 2 + w.n * w.k // 16 + m * w.k * 2 + m * w.n * 2 for w in lin) / len(lin)
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (gemm_ms / 1e3) / 1e9
@@ -306,7 +324,7 @@ def run_ours(args, rank, world, local_rank):
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
                 "kernel": "adallm_b200 nvfp4 gemm_kernel (tcgen05 mxf4nvf4)",
                 "alg_bytes_per_launch": int(alg_bytes), "us_per_launch": round(gemm_ms * 1e3, 3),
-                "launch_mix": "qkv/o/gate_up/down of all layers, batch 16"}
+                "launch_mix": "qkv/o/gate_up/down of all layers, batch 16", "per_shape": per_shape}
 
     ctx_end = int(sess.lens.max().item())
     cpu = None

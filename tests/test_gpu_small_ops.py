@@ -111,8 +111,9 @@ def test_gated_act(act):
     x = (torch.randn(17, 2 * 1536) * 3).to(torch.bfloat16)
     y = gated_act(x.to(d), act)
     y_ref = (ol.silu_and_mul if act == 0 else ol.gelu_and_mul)(x)
-    frac, mx = bf16_ulp_mismatch(y.cpu(), y_ref)
-    assert mx <= 2 and frac < 0.02
+    # transcendental implementations differ by ~1 ulp; GELU's far tail is ~1e-30 either side of zero
+    assert torch.allclose(y.float().cpu(), y_ref.float(), rtol=2 ** -7, atol=1e-6)
+    assert rel_l2(y.float().cpu(), y_ref.float()) < 2e-3
 
 
 def test_embedding_and_argmax():
