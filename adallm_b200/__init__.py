@@ -8,5 +8,6 @@ Build the CUDA library with ``python -m adallm_b200.build``.  No CPU or
 PyTorch fallback exists: ops raise if the library is missing.
 """
 from . import _native  # noqa: F401
+from .install import install  # noqa: F401
 
-__all__ = ["_native"]
+__all__ = ["_native", "install"]

@@ -46,7 +46,8 @@ _SIGS = {
     "ada_qk_norm_rope_store": (INT, [P, I64, I64, I32, I32, I32, P, P, F32, P, P, I64, P, P, P, F32, F32, P, P,
                                      INT, P]),
     "ada_embedding": (INT, [P, I64, P, I64, I64, I32, P, INT, P]),
-    "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P]),
+    "ada_argmax_workspace_size": (SZ, [I64, I64]),
+    "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P, SZ, P]),
     "ada_nvfp4_sf_bytes": (SZ, [I64, I64]),
     "ada_nvfp4_prepack_scales": (INT, [P, INT, I64, I64, I64, P, P]),
     "ada_nvfp4_linear_workspace_size": (SZ, [I64, I64, I64, INT]),
@@ -54,7 +55,7 @@ _SIGS = {
     "ada_nvfp4_linear_ex": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I64, P, P, INT, I64, INT, INT, P, SZ, P]),
     "ada_nvfp4_workspace_status": (INT, [P, I64, I64, I64, INT, P, P]),
     "ada_nvfp4_act_quant": (INT, [P, INT, I64, I64, I64, INT, INT, P, P, P, P]),
-    "ada_nvfp4_block_n": (INT, [I64]),
+    "ada_nvfp4_block_n": (INT, [I64, INT]),
     "ada_nvfp4_gemm_workspace_size": (SZ, [I64, I64, I64, INT]),
     "ada_nvfp4_gemm": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, P, INT, I64, INT, P, SZ, P]),
 }

@@ -49,17 +49,22 @@ struct GemmParams {
   int M, N, K, ldy, m_pad, n_tiles, m_tiles, ksplit, stages, tmem_cols, out_dtype;
 };
 
+// The T activation terms of a token tile are stacked along the MMA N dimension:
+// B operand rows [t*BN, (t+1)*BN) hold term t, so one MMA per 64-wide K block covers
+// every term (NB = T*BN <= 128 rows, one scale-factor block).
 template <int BN, int T>
 struct Cfg {
+  static constexpr int NB = BN * T;
+  static_assert(NB % 16 == 0 && NB <= 128, "stacked terms must fit one 128-row scale block");
   static constexpr uint32_t A_BYTES = BM * KT_BYTES;      // 16 KiB
-  static constexpr uint32_t B_BYTES = BN * KT_BYTES;      // per term
+  static constexpr uint32_t B_BYTES = NB * KT_BYTES;      // all terms
   static constexpr uint32_t SFA_BYTES = 4 * SF_BLOCK;     // 2 KiB
-  static constexpr uint32_t SFB_BYTES = 4 * SF_BLOCK;     // per term
-  static constexpr uint32_t STAGE = A_BYTES + T * B_BYTES + SFA_BYTES + T * SFB_BYTES;
-  static constexpr uint32_t SF_COLS = 16 + 16 * T;        // TMEM columns of scales per stage
+  static constexpr uint32_t SFB_BYTES = 4 * SF_BLOCK;     // 2 KiB
+  static constexpr uint32_t STAGE = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr uint32_t SF_COLS = 32;                 // TMEM columns of scales per stage
   static constexpr uint32_t CTRL = 256;
   static size_t smem_bytes(int stages) { return 1024 + (size_t)stages * STAGE + CTRL; }
-  static uint32_t tmem_need(int stages) { return BN + stages * SF_COLS; }
+  static uint32_t tmem_need(int stages) { return NB + stages * SF_COLS; }
 };
 
 __device__ __forceinline__ void store_out(void* y, int dtype, int64_t idx, float v) {
@@ -129,23 +134,18 @@ __global__ void __launch_bounds__(128, 1)
         const int kt = kt0 + i;
         mbar_arrive_expect_tx(&full[s], C::STAGE);
         tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, n_tile * BM);
-#pragma unroll
-        for (int t = 0; t < T; ++t)
-          tma_load_2d(st + C::A_BYTES + t * C::B_BYTES, &tmx, &full[s], kt * KT_BYTES, t * p.m_pad + m_tile * BN);
-        uint8_t* sf = st + C::A_BYTES + T * C::B_BYTES;
+        tma_load_2d(st + C::A_BYTES, &tmx, &full[s], kt * KT_BYTES, m_tile * C::NB);
+        uint8_t* sf = st + C::A_BYTES + C::B_BYTES;
         bulk_load(sf, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFA_BYTES, &full[s]);
-#pragma unroll
-        for (int t = 0; t < T; ++t)
-          bulk_load(sf + C::SFA_BYTES + t * C::SFB_BYTES,
-                    p.sfx + (((size_t)t * p.m_tiles + m_tile) * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES,
-                    &full[s]);
+        bulk_load(sf + C::SFA_BYTES, p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES,
+                  &full[s]);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = idesc_mxf4nvf4(BN);
+      constexpr uint32_t idesc = idesc_mxf4nvf4(C::NB);
       for (int i = 0; i < nk; ++i) {
         const int s = i % stages;
         if (!mbar_wait_bounded(&full[s], (i / stages) & 1, abort_v, p.err, 2u)) break;
@@ -153,24 +153,18 @@ __global__ void __launch_bounds__(128, 1)
         uint8_t* st = smem + (size_t)s * C::STAGE;
         const uint32_t a_addr = smem_u32(st);
         const uint32_t b_addr = a_addr + C::A_BYTES;
-        const uint32_t sfa_addr = b_addr + T * C::B_BYTES;
+        const uint32_t sfa_addr = b_addr + C::B_BYTES;
         const uint32_t sfb_addr = sfa_addr + C::SFA_BYTES;
-        const uint32_t sf_col = tmem + BN + s * C::SF_COLS;
-#pragma unroll
-        for (int kb = 0; kb < 4; ++kb) tmem_cp_32x128b_x4(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
-#pragma unroll
-        for (int t = 0; t < T; ++t)
-#pragma unroll
-          for (int kb = 0; kb < 4; ++kb)
-            tmem_cp_32x128b_x4(sf_col + 16 + 16 * t + 4 * kb, desc_sf(sfb_addr + t * C::SFB_BYTES + kb * SF_BLOCK));
+        const uint32_t sf_col = tmem + C::NB + s * C::SF_COLS;
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb) {
-#pragma unroll
-          for (int t = 0; t < T; ++t) {
-            mma_mxf4nvf4(tmem, desc_kmajor_sw128(a_addr + kb * 32), desc_kmajor_sw128(b_addr + t * C::B_BYTES + kb * 32),
-                         idesc, (i | kb | t) != 0, sf_col + 4 * kb, sf_col + 16 + 16 * t + 4 * kb);
-          }
+          tmem_cp_32x128b_x4(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
+          tmem_cp_32x128b_x4(sf_col + 16 + 4 * kb, desc_sf(sfb_addr + kb * SF_BLOCK));
         }
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+          mma_mxf4nvf4(tmem, desc_kmajor_sw128(a_addr + kb * 32), desc_kmajor_sw128(b_addr + kb * 32), idesc,
+                       (i | kb) != 0, sf_col + 4 * kb, sf_col + 16 + 4 * kb);
         tc_commit(&empty[s]);  // stage reusable once these MMAs have read it
       }
       tc_commit(accf);  // accumulator complete (also issued after an abort, to drain)
@@ -185,32 +179,33 @@ __global__ void __launch_bounds__(128, 1)
   const int n = n_tile * BM + warp * 32 + lane;  // accumulator lane -> output column
   const float gw = __ldg(p.gw);
   const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  // accumulator column t*BN + j holds term t of token m_tile*BN + j: sum the terms in order
+  float out[BN];
+#pragma unroll
+  for (int j = 0; j < BN; ++j) out[j] = 0.f;
+#pragma unroll
+  for (int c = 0; c < C::NB; c += 16) {
+    float v[16];
+    tmem_ld16(lane_addr + c, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[(c % BN) + i] += v[i];
+  }
   if (p.ksplit == 1) {
+    if (ok) {
+      const float b = load_bias(p.bias, p.out_dtype, n);
 #pragma unroll
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      tmem_ld16(lane_addr + c, v);
-      if (ok) {
-        const float b = load_bias(p.bias, p.out_dtype, n);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m_tile * BN + c + j;
-          if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, v[j] * (gw * __ldg(p.gx + m)) + b);
-        }
+      for (int j = 0; j < BN; ++j) {
+        const int m = m_tile * BN + j;
+        if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, out[j] * (gw * __ldg(p.gx + m)) + b);
       }
     }
   } else {
     float* part = p.partial + (size_t)split * p.m_pad * p.N;
+    if (ok) {
 #pragma unroll
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      tmem_ld16(lane_addr + c, v);
-      if (ok) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m_tile * BN + c + j;
-          part[(size_t)m * p.N + n] = v[j] * (gw * __ldg(p.gx + m));
-        }
+      for (int j = 0; j < BN; ++j) {
+        const int m = m_tile * BN + j;
+        part[(size_t)m * p.N + n] = out[j] * (gw * __ldg(p.gx + m));
       }
     }
     __threadfence();
@@ -220,12 +215,23 @@ __global__ void __launch_bounds__(128, 1)
     if (*last_flag) {
       __threadfence();
       const float b = load_bias(p.bias, p.out_dtype, n);
-      for (int j = 0; j < BN; ++j) {
-        const int m = m_tile * BN + j;
-        if (m >= p.M) break;
-        float acc = 0.f;
-        for (int s = 0; s < p.ksplit; ++s) acc += __ldcg(p.partial + ((size_t)s * p.m_pad + m) * p.N + n);
-        store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, acc + b);
+      // splits summed in order (deterministic); each pass issues 16 independent L2 loads
+#pragma unroll
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+        const float* col = p.partial + (size_t)(m_tile * BN + j0) * p.N + n;
+        for (int s = 0; s < p.ksplit; ++s) {
+          const float* ps = col + (size_t)s * p.m_pad * p.N;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] += __ldcg(ps + (size_t)j * p.N);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m_tile * BN + j0 + j;
+          if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, acc[j] + b);
+        }
       }
       if (threadIdx.x == 0) p.counters[tile] = 0;  // leave the workspace ready for the next call
     }
@@ -237,9 +243,10 @@ __global__ void __launch_bounds__(128, 1)
 
 // ---------------------------------------------------------------------------
 // Activation quantiser (bit-exact spec: oracle/nvfp4.py quantize_act_terms).
-// One CTA per (padded) row.  Layouts written:
-//   xq  [T][m_pad][K/2]           packed e2m1, even K in the low nibble
-//   sfx [T][m_tiles][K/64][512]   ue4m3 scales in the MMA scale-factor layout
+// One CTA per (padded) row.  Token m = mt*bn + j, term t is operand row r = t*bn + j
+// of token tile mt (terms stacked along the MMA N dimension).  Layouts written:
+//   xq  [m_tiles][T*bn][K/2]      packed e2m1, even K in the low nibble
+//   sfx [m_tiles][K/64][512]      ue4m3 scales in the MMA scale-factor layout
 //   gx  [m_pad]                   per-row fp32 scale (1.0 for padding rows)
 __device__ __forceinline__ float e2m1_value(uint32_t c) {
   const uint32_t mag = c & 7u;
@@ -261,13 +268,16 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const TI* __restrict__ x
   const int kb64 = K >> 6;
   const int mt = m / bn, row = m - mt * bn;
   const size_t khalf = (size_t)K >> 1;
+  const int nb = terms * bn;
   auto sf_off = [&](int t, int blk) {
-    return (((size_t)t * m_tiles + mt) * kb64 + (blk >> 2)) * 512 + (row & 31) * 16 + (row >> 5) * 4 + (blk & 3);
+    const int r = t * bn + row;
+    return ((size_t)mt * kb64 + (blk >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (blk & 3);
   };
+  auto xq_row = [&](int t) { return xq + ((size_t)mt * nb + (size_t)t * bn + row) * khalf; };
   if (m >= M) {  // padding row: zero codes and scales
     for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x)
       for (int t = 0; t < terms; ++t) {
-        *reinterpret_cast<uint2*>(xq + ((size_t)t * m_pad + m) * khalf + (size_t)blk * 8) = make_uint2(0, 0);
+        *reinterpret_cast<uint2*>(xq_row(t) + (size_t)blk * 8) = make_uint2(0, 0);
         sfx[sf_off(t, blk)] = 0;
       }
     if (threadIdx.x == 0) gx[m] = 1.f;
@@ -317,7 +327,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const TI* __restrict__ x
           r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(c), denom));
         }
       }
-      *reinterpret_cast<uint2*>(xq + ((size_t)t * m_pad + m) * khalf + (size_t)blk * 8) = codes;
+      *reinterpret_cast<uint2*>(xq_row(t) + (size_t)blk * 8) = codes;
       sfx[sf_off(t, blk)] = sb;
     }
   }
@@ -381,6 +391,13 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, u
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Token tile: the smallest of 16/32/64/128 covering m, capped so terms*bn <= 128.
+static inline int block_n_for(int64_t m, int terms) {
+  const int cap = terms == 1 ? 128 : terms == 2 ? 64 : 32;
+  int bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+  return bn < cap ? bn : cap;
+}
+
 struct Plan {
   int terms, bn, m_tiles, m_pad, n_tiles, nkt, ksplit, stages, tmem_cols;
   size_t smem;
@@ -413,7 +430,7 @@ static void stages_for(int& stages, uint32_t& cols, size_t& smem) {
 static void stages_dispatch(int bn, int t, int& stages, uint32_t& cols, size_t& smem) {
 #define ADA_SD(B, TT) if (bn == B && t == TT) { stages_for<B, TT>(stages, cols, smem); return; }
   ADA_SD(16, 1) ADA_SD(16, 2) ADA_SD(16, 3) ADA_SD(32, 1) ADA_SD(32, 2) ADA_SD(32, 3)
-  ADA_SD(64, 1) ADA_SD(64, 2) ADA_SD(64, 3) ADA_SD(128, 1) ADA_SD(128, 2) ADA_SD(128, 3)
+  ADA_SD(64, 1) ADA_SD(64, 2) ADA_SD(128, 1)
 #undef ADA_SD
   stages = 0;
 }
@@ -424,7 +441,7 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_kspli
   if (n % BM || k % KT) return ADA_ERR_UNSUPPORTED;
   if (m > (1 << 24) || n > (1 << 24) || k > (1 << 24)) return ADA_ERR_UNSUPPORTED;
   P.terms = terms;
-  P.bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+  P.bn = block_n_for(m, terms);
   P.m_tiles = (int)cdiv(m, P.bn);
   P.m_pad = P.m_tiles * P.bn;
   P.n_tiles = (int)(n / BM);
@@ -451,7 +468,7 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_kspli
   P.off_xq = off;
   off = al256(off + (size_t)terms * P.m_pad * (size_t)(k / 2));
   P.off_sfx = off;
-  off = al256(off + (size_t)terms * P.m_tiles * (size_t)(k / 64) * 512);
+  off = al256(off + (size_t)P.m_tiles * (size_t)(k / 64) * 512);
   P.off_gx = off;
   off = al256(off + (size_t)P.m_pad * 4);
   P.off_part = off;
@@ -480,7 +497,7 @@ static int dispatch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const G
                          cudaStream_t st) {
 #define ADA_G(B, TT) if (P.bn == B && P.terms == TT) return launch_gemm<B, TT>(tmw, tmx, gp, P, st);
   ADA_G(16, 1) ADA_G(16, 2) ADA_G(16, 3) ADA_G(32, 1) ADA_G(32, 2) ADA_G(32, 3)
-  ADA_G(64, 1) ADA_G(64, 2) ADA_G(64, 3) ADA_G(128, 1) ADA_G(128, 2) ADA_G(128, 3)
+  ADA_G(64, 1) ADA_G(64, 2) ADA_G(128, 1)
 #undef ADA_G
   return ADA_ERR_UNSUPPORTED;
 }
@@ -491,7 +508,8 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
                     cudaStream_t st) {
   CUtensorMap tmw, tmx;
   if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, BM)) return ADA_ERR_CUDA;
-  if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2), (uint32_t)P.bn))
+  if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2),
+                (uint32_t)(P.terms * P.bn)))
     return ADA_ERR_CUDA;
   GemmParams gp;
   gp.sfw = sf_w;
@@ -603,6 +621,7 @@ extern "C" int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int6
   if (m <= 0 || k <= 0 || !x || !xq || !sfx || !gx) return ADA_ERR_INVALID_ARG;
   if (terms < 1 || terms > 3 || (x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16)) return ADA_ERR_INVALID_ARG;
   if (block_n != 16 && block_n != 32 && block_n != 64 && block_n != 128) return ADA_ERR_INVALID_ARG;
+  if (terms * block_n > 128) return ADA_ERR_INVALID_ARG;
   if (k % 256 || ldx < k) return ADA_ERR_UNSUPPORTED;
   if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)xq & 15)) return ADA_ERR_ALIGNMENT;
   const int m_tiles = (int)cdiv(m, block_n), m_pad = m_tiles * block_n;
@@ -631,9 +650,9 @@ extern "C" int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int6
   return ADA_OK;
 }
 
-extern "C" int ada_nvfp4_block_n(int64_t m) {
-  if (m <= 0) return 0;
-  return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+extern "C" int ada_nvfp4_block_n(int64_t m, int terms) {
+  if (m <= 0 || terms < 1 || terms > 3) return 0;
+  return fp4::block_n_for(m, terms);
 }
 
 extern "C" size_t ada_nvfp4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int terms) {

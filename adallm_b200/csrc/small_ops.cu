@@ -171,23 +171,26 @@ __global__ void __launch_bounds__(128) rope_kernel(const int64_t* __restrict__ p
 //          then NeoX RoPE at positions[t]  (rotary_embedding.py:6-14)
 //   k, v : e4m3 store into the paged cache at slot_mapping[t] (attention.py:11-31)
 //   q    : written to q_out [T, hq, D]; k (normed + roped, bf16) optionally to k_out.
-// One CTA per token, one warp per head; a lane owns 4 consecutive elements and the
-// rotate-half partner lives 16 lanes away.  Implemented for head_dim == 128.
+// One warp per (token, head) item, 4 warps per CTA; a lane owns 4 consecutive elements
+// and the rotate-half partner lives 16 lanes away.  Implemented for head_dim == 128.
 template <typename T>
-__global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
+__global__ void __launch_bounds__(128) qk_norm_rope_store_kernel(
     const T* __restrict__ qkv, int64_t ld, int hq, int hkv, const T* __restrict__ qw, const T* __restrict__ kw,
     float eps, const int64_t* __restrict__ pos, const float* __restrict__ cs, int64_t max_pos,
     const int32_t* __restrict__ slots, uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, float k_scale,
-    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out) {
+    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out, int64_t num_tokens) {
   constexpr int D = 128;
-  const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int nheads = hq + 2 * hkv;
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (item >= num_tokens * nheads) return;
+  const int64_t t = item / nheads;
+  const int h = (int)(item - t * nheads);
   const int64_t p = min(max(__ldg(pos + t), (int64_t)0), max_pos - 1);
   const float* c = cs + p * D;
   const int slot = __ldg(slots + t);
   const int i0 = (lane & 15) * 4;  // rotation-pair index of this lane's first element
-  for (int h = warp; h < nheads; h += blockDim.x >> 5) {
+  {
     const T* src = qkv + (int64_t)t * ld + (int64_t)h * D + lane * 4;
     float x[4];
     {
@@ -291,39 +294,75 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const uint4* _
     y[(int64_t)t * nvec + i] = in ? table[(id - v0) * nvec + i] : make_uint4(0, 0, 0, 0);
 }
 
+// Greedy argmax in two stages: stage 1 splits every row into chunks of 8-aligned
+// columns (16-byte loads) and writes one (max, index) pair per chunk; stage 2 picks
+// the first maximum of each row.  Ties resolve to the lowest index (torch.argmax).
+__device__ __forceinline__ void better(float& bv, int64_t& bi, float v, int64_t i) {
+  if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
 template <typename T>
-__global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, int64_t ld, int64_t cols,
-                                                      int64_t* __restrict__ out) {
-  __shared__ float sv[32];
-  __shared__ int64_t si[32];
-  const int64_t r = blockIdx.x;
-  float best = -INFINITY;
+__global__ void __launch_bounds__(256) argmax_stage1(const T* __restrict__ x, int64_t ld, int64_t cols,
+                                                     int64_t chunk, float* __restrict__ pv,
+                                                     int64_t* __restrict__ pi) {
+  __shared__ float sv[8];
+  __shared__ int64_t si[8];
+  const int64_t r = blockIdx.y;
+  const int64_t c0 = (int64_t)blockIdx.x * chunk;
+  const int64_t c1 = min(cols, c0 + chunk);
+  float bv = -INFINITY;
   int64_t bi = 0x7fffffffffffffffLL;
-  for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) {
-    const float v = to_f32(x[r * ld + j]);
-    if (v > best || (v == best && j < bi)) { best = v; bi = j; }
+  const T* row = x + r * ld;
+  const bool vec = ((ld & 7) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  if (vec) {
+    for (int64_t j = c0 + threadIdx.x * 8; j < c1; j += blockDim.x * 8) {
+      if (j + 8 <= c1) {
+        float f[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(row + j), f);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) better(bv, bi, f[q], j + q);
+      } else {
+        for (int64_t q = j; q < c1; ++q) better(bv, bi, to_f32(row[q]), q);
+      }
+    }
+  } else {
+    for (int64_t j = c0 + threadIdx.x; j < c1; j += blockDim.x) better(bv, bi, to_f32(row[j]), j);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    better(bv, bi, ov, oi);
   }
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) { sv[w] = best; si[w] = bi; }
+  if (l == 0) { sv[w] = bv; si[w] = bi; }
   __syncthreads();
-  if (w == 0) {
-    const int nw = blockDim.x >> 5;
-    best = l < nw ? sv[l] : -INFINITY;
-    bi = l < nw ? si[l] : 0x7fffffffffffffffLL;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-    }
-    if (l == 0) out[r] = bi == 0x7fffffffffffffffLL ? 0 : bi;
+  if (threadIdx.x == 0) {
+    for (int q = 1; q < (int)(blockDim.x >> 5); ++q) better(bv, bi, sv[q], si[q]);
+    pv[r * gridDim.x + blockIdx.x] = bv;
+    pi[r * gridDim.x + blockIdx.x] = bi;
   }
+}
+
+__global__ void __launch_bounds__(32) argmax_stage2(const float* __restrict__ pv, const int64_t* __restrict__ pi,
+                                                    int chunks, int64_t* __restrict__ out) {
+  const int64_t r = blockIdx.x;
+  float bv = -INFINITY;
+  int64_t bi = 0x7fffffffffffffffLL;
+  for (int c = threadIdx.x; c < chunks; c += 32) better(bv, bi, pv[r * chunks + c], pi[r * chunks + c]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, ov, oi);
+  }
+  if (threadIdx.x == 0) out[r] = bi == 0x7fffffffffffffffLL ? 0 : bi;
+}
+
+static inline int argmax_chunks(int64_t cols) {
+  int64_t c = (cols + 2047) / 2048;  // ~2048 columns per CTA
+  if (c > 256) c = 256;
+  return (int)(c < 1 ? 1 : c);
 }
 
 }  // namespace small
@@ -439,10 +478,12 @@ extern "C" int ada_qk_norm_rope_store(const void* qkv, int64_t ld, int64_t num_t
       ((uintptr_t)q_norm_w & 7) || ((uintptr_t)k_norm_w & 7) || ((uintptr_t)k_cache & 3) || ((uintptr_t)v_cache & 3))
     return ADA_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t items = num_tokens * (num_q_heads + 2 * num_kv_heads);
+  const unsigned blocks = (unsigned)((items + 3) / 4);
 #define ADA_QK(T)                                                                                               \
-  small::qk_norm_rope_store_kernel<T><<<(unsigned)num_tokens, 256, 0, st>>>(                                     \
+  small::qk_norm_rope_store_kernel<T><<<blocks, 128, 0, st>>>(                                                   \
       (const T*)qkv, ld, num_q_heads, num_kv_heads, (const T*)q_norm_w, (const T*)k_norm_w, eps, positions,       \
-      cos_sin, max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out)
+      cos_sin, max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out, num_tokens)
   if (dtype == ADA_DT_BF16) ADA_QK(__nv_bfloat16);
   else ADA_QK(__half);
 #undef ADA_QK
@@ -484,18 +525,33 @@ extern "C" int ada_embedding(const int64_t* ids, int64_t num_tokens, const void*
   return ADA_OK;
 }
 
+extern "C" size_t ada_argmax_workspace_size(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return (size_t)rows * small::argmax_chunks(cols) * (sizeof(float) + sizeof(int64_t)) + 16;
+}
+
 extern "C" int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype, int64_t* out,
-                          void* stream) {
+                          void* workspace, size_t workspace_bytes, void* stream) {
   if (rows < 0 || cols <= 0 || ld < cols) return ADA_ERR_INVALID_ARG;
   if (rows == 0) return ADA_OK;
-  if (!logits || !out) return ADA_ERR_INVALID_ARG;
+  if (!logits || !out || !workspace) return ADA_ERR_INVALID_ARG;
+  if (rows > 65535) return ADA_ERR_UNSUPPORTED;
+  if (workspace_bytes < ada_argmax_workspace_size(rows, cols)) return ADA_ERR_WORKSPACE;
+  if ((uintptr_t)workspace & 7) return ADA_ERR_ALIGNMENT;
+  const int chunks = small::argmax_chunks(cols);
+  const int64_t chunk = ((cols + chunks - 1) / chunks + 7) & ~int64_t(7);
+  int64_t* pi = reinterpret_cast<int64_t*>(workspace);
+  float* pv = reinterpret_cast<float*>(pi + rows * chunks);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 g1(chunks, (unsigned)rows);
   if (dtype == ADA_DT_BF16)
-    small::argmax_kernel<__nv_bfloat16><<<(unsigned)rows, 1024, 0, st>>>((const __nv_bfloat16*)logits, ld, cols, out);
+    small::argmax_stage1<__nv_bfloat16><<<g1, 256, 0, st>>>((const __nv_bfloat16*)logits, ld, cols, chunk, pv, pi);
   else if (dtype == ADA_DT_F16)
-    small::argmax_kernel<__half><<<(unsigned)rows, 1024, 0, st>>>((const __half*)logits, ld, cols, out);
+    small::argmax_stage1<__half><<<g1, 256, 0, st>>>((const __half*)logits, ld, cols, chunk, pv, pi);
   else
     return ADA_ERR_INVALID_ARG;
+  ADA_CHECK_LAUNCH();
+  small::argmax_stage2<<<(unsigned)rows, 32, 0, st>>>(pv, pi, chunks, out);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }

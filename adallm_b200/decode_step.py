@@ -224,6 +224,8 @@ class Qwen3DecodeEngine:
         self.gate_up = torch.zeros((B, 2 * c.inter), dtype=bf, device=d)
         self.act = torch.zeros((B, c.inter), dtype=bf, device=d)
         self.logits = torch.zeros((B, c.vocab_shard), dtype=bf, device=d)
+        self.argmax_ws = torch.zeros(int(N.lib().ada_argmax_workspace_size(B, c.vocab_shard)), dtype=torch.uint8,
+                                     device=d)
         # workspaces (zeroed once; the kernels leave them ready for reuse)
         shapes = [(B, w.n, w.k) for w in self.layers[0].values() if isinstance(w, NVFP4Weight)]
         self.gemm_ws = torch.zeros(max(workspace_bytes(*s, c.terms) for s in shapes), dtype=torch.uint8, device=d)
@@ -304,7 +306,8 @@ class Qwen3DecodeEngine:
     def _argmax(self, stream):
         c = self.cfg
         N.check(N.lib().ada_argmax(self.logits.data_ptr(), c.vocab_shard, self.B, c.vocab_shard, 0,
-                                   self.next_tokens.data_ptr(), stream), "argmax")
+                                   self.next_tokens.data_ptr(), self.argmax_ws.data_ptr(), self.argmax_ws.numel(),
+                                   stream), "argmax")
         if c.tp_size > 1:
             # vocab-parallel greedy pick: gather (max, index) per rank, take the first global maximum
             loc = self.logits.float().gather(1, self.next_tokens.view(-1, 1)).view(-1)
@@ -346,7 +349,7 @@ class Qwen3DecodeEngine:
     def kernels_per_step(self) -> int:
         """adallm_b200 kernels launched by one forward(): embedding, per layer (norm, act-quant+GEMM x4,
         qk-norm/rope/store, attention split + reduce, norm, SiLU*up), final norm, argmax."""
-        return 1 + self.cfg.num_layers * 14 + 2
+        return 1 + self.cfg.num_layers * 14 + 3
 
     def export_cpu_weights(self) -> dict:
         """CPU copies in the reference parameter layout (tensor-parallel size 1 only)."""

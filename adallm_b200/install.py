@@ -1,0 +1,115 @@
+"""Install the B200 kernels into the reference runtime (package ``adallm``).
+
+    import adallm_b200
+    adallm_b200.install()          # before adallm.LLMEngine(...) builds the model
+
+Replaces, by the same names and signatures:
+  adallm.ops.nvfp4_gemm.nvfp4_linear / nvfp4_linear_dual / nvfp4_linear_gather   (nvfp4_gemm.py:460, :567, :657)
+  adallm.ops.linear.nvfp4_linear (the name LinearBase._linear calls, linear.py:6, :61-74)
+  adallm.ops.attention.store_kvcache                                            (attention.py:236)
+  adallm.ops.attention.Attention.forward -- decode branch only; prefill (flash-attn varlen,
+      attention.py:335-358) keeps the reference implementation
+  adallm.ops.layernorm.RMSNorm.forward / GemmaRMSNorm.forward                    (layernorm.py:42-50, :94-102)
+  adallm.ops.rotary_embedding.RotaryEmbedding.forward                            (rotary_embedding.py:45-56)
+  adallm.ops.activation.SiluAndMul.forward / GeluAndMul.forward                   (activation.py:11-26)
+  adallm.runtime.model_runner.ModelRunner.fp8_decode_selftest (model_runner.py:171-232 imports the
+      Triton kernel by name; the replacement runs the same zero-input smoke on this kernel)
+and points this package's forward context at adallm.infra.context.get_context.
+
+Weight layout, loader and engine are untouched: NVFP4 parameters keep their
+uint8 [N, K/2] / fp16 [N, K/16] / fp32 [] layout (linear.py:31-43); the tensor-core
+scale layout is derived from weight_scale on first use and cached on the tensor.
+"""
+from __future__ import annotations
+
+import torch
+
+_INSTALLED = False
+
+
+def install(terms: int | None = None) -> None:
+    global _INSTALLED
+    import adallm.infra.context as ref_ctx
+    import adallm.ops.activation as ref_act
+    import adallm.ops.attention as ref_attn
+    import adallm.ops.layernorm as ref_ln
+    import adallm.ops.linear as ref_linear
+    import adallm.ops.nvfp4_gemm as ref_gemm
+    import adallm.ops.rotary_embedding as ref_rope
+
+    from . import activation, attention, context, layernorm, nvfp4_gemm, rotary_embedding
+    from . import _native as N
+
+    N.lib()  # fail loudly now if the CUDA library is missing: there is no fallback
+    if terms is not None:
+        nvfp4_gemm.DEFAULT_TERMS = int(terms)
+
+    ref_gemm.nvfp4_linear = nvfp4_gemm.nvfp4_linear
+    ref_gemm.nvfp4_linear_dual = nvfp4_gemm.nvfp4_linear_dual
+    ref_gemm.nvfp4_linear_gather = nvfp4_gemm.nvfp4_linear_gather
+    ref_linear.nvfp4_linear = nvfp4_gemm.nvfp4_linear
+    try:  # the MoE blocks import the functional ops by name
+        import adallm.architectures.qwen3 as ref_qwen3
+        for name in ("nvfp4_linear", "nvfp4_linear_dual", "nvfp4_linear_gather"):
+            if hasattr(ref_qwen3, name):
+                setattr(ref_qwen3, name, getattr(nvfp4_gemm, name))
+    except Exception:
+        pass
+
+    def store_kvcache(key, value, k_cache, v_cache, slot_mapping):
+        attention.store_kvcache(key, value, k_cache, v_cache, slot_mapping)
+
+    ref_attn.store_kvcache = store_kvcache
+
+    orig_forward = getattr(ref_attn.Attention, "_adallm_ref_forward", ref_attn.Attention.forward)
+    ref_attn.Attention._adallm_ref_forward = orig_forward
+
+    def attn_forward(self, q, k, v):
+        ctx = ref_ctx.get_context()
+        if ctx.is_prefill or self.k_cache.dtype != torch.float8_e4m3fn:
+            return orig_forward(self, q, k, v)
+        orig_dtype = q.dtype
+        if self.k_cache.numel() and self.v_cache.numel():
+            attention.store_kvcache(k, v, self.k_cache, self.v_cache, ctx.slot_mapping)
+        window = self.sliding_window if (self.sliding_window is not None and self.sliding_window > 0) else 0
+        try:
+            o = attention.paged_decode(q.view(-1, self.num_heads, self.head_dim), self.k_cache, self.v_cache,
+                                       ctx.block_tables, ctx.context_lens, self.scale, window)
+        except Exception as exc:
+            if torch.cuda.is_current_stream_capturing() or isinstance(exc, ValueError):
+                raise
+            raise RuntimeError("FP8 KV decode kernel failed; no fallback is allowed in this runtime.") from exc
+        return o if o.dtype == orig_dtype else o.to(orig_dtype)
+
+    ref_attn.Attention.forward = attn_forward
+
+    ref_ln.RMSNorm.forward = lambda self, x, residual=None: layernorm.rms_norm(x, self.weight, self.eps, residual)
+    ref_ln.GemmaRMSNorm.forward = lambda self, x, residual=None: layernorm.rms_norm(x, self.weight, self.eps,
+                                                                                   residual, gemma=True)
+    ref_rope.RotaryEmbedding.forward = lambda self, positions, query, key: rotary_embedding.apply_rope(
+        positions, query, key, self.cos_sin_cache)
+    ref_act.SiluAndMul.forward = lambda self, x: activation.gated_act(x, 0)
+    ref_act.GeluAndMul.forward = lambda self, x: activation.gated_act(x, 1)
+
+    try:
+        import adallm.runtime.model_runner as ref_runner
+
+        def selftest(self):
+            # zero-input compile/run check of the replacement decode kernel (model_runner.py:171-232)
+            dev = torch.device("cuda", torch.cuda.current_device())
+            q = torch.zeros((1, 8, 128), dtype=torch.bfloat16, device=dev)
+            kc = torch.zeros((1, 16, 8, 128), dtype=torch.float8_e4m3fn, device=dev)
+            attention.paged_decode(q, kc, kc, torch.zeros((1, 1), dtype=torch.int32, device=dev),
+                                   torch.ones(1, dtype=torch.int32, device=dev), 1.0)
+            torch.cuda.synchronize()
+
+        ref_runner.ModelRunner.fp8_decode_selftest = selftest
+    except Exception:
+        pass
+
+    context.use_context_provider(ref_ctx.get_context)
+    _INSTALLED = True
+
+
+def installed() -> bool:
+    return _INSTALLED

@@ -187,18 +187,20 @@ ADA_API int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int64_t
                                 size_t workspace_bytes, void* stream);
 /* The activation quantiser on its own (the first half of ada_nvfp4_linear; no reference
  * counterpart -- the reference never quantises activations to e2m1).  Row m of x becomes
- * `terms` NVFP4 terms sharing the fp32 row scale gx[m] = amax(row) / 2688:
- *   xq  [terms][m_pad][k/2]               packed e2m1, even k in the low nibble
- *   sfx [terms][m_pad/block_n][k/64][512] ue4m3 scales, MMA scale-factor layout
- *   gx  [m_pad]                           (1.0 for the zero padding rows)
- * with m_pad = ceil(m / block_n) * block_n and block_n in {16, 32, 64, 128}. */
+ * `terms` NVFP4 terms sharing the fp32 row scale gx[m] = amax(row) / 2688.  Token
+ * m = mt*block_n + j, term t is operand row t*block_n + j of token tile mt:
+ *   xq  [m_pad/block_n][terms*block_n][k/2]   packed e2m1, even k in the low nibble
+ *   sfx [m_pad/block_n][k/64][512]            ue4m3 scales, MMA scale-factor layout
+ *   gx  [m_pad]                               (1.0 for the zero padding rows)
+ * with m_pad = ceil(m / block_n) * block_n, block_n in {16, 32, 64, 128} and
+ * terms * block_n <= 128 (ada_nvfp4_block_n(m, terms) gives the GEMM's choice). */
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by
  * ada_nvfp4_act_quant (or by a fused producer writing the same layout) with
- * block_n == ada_nvfp4_block_n(m).  workspace: ada_nvfp4_gemm_workspace_size(m, n, k, terms)
+ * block_n == ada_nvfp4_block_n(m, terms).  workspace: ada_nvfp4_gemm_workspace_size(m, n, k, terms)
  * bytes, 256-byte aligned, zero-filled before first use (left ready for the next call). */
-ADA_API int ada_nvfp4_block_n(int64_t m);
+ADA_API int ada_nvfp4_block_n(int64_t m, int terms);
 ADA_API size_t ada_nvfp4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int terms);
 ADA_API int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
                            int block_n, const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
@@ -210,9 +212,11 @@ ADA_API int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* g
 ADA_API int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,
                                        unsigned int* status_out, void* stream);
 
-/* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum), logits bf16/f16. */
+/* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum, like torch.argmax),
+ * logits bf16/f16.  workspace: ada_argmax_workspace_size(rows, cols) bytes, 8-byte aligned. */
+ADA_API size_t ada_argmax_workspace_size(int64_t rows, int64_t cols);
 ADA_API int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
-               int64_t* out, void* stream);
+                       int64_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -20,10 +20,18 @@ pytestmark = pytest.mark.gpu
 
 
 def unpack_sf(sfx: np.ndarray, terms: int, m_tiles: int, bn: int, k: int) -> np.ndarray:
+    """[m_tiles][k/64][512] scale-factor blocks (operand row r = t*bn + j) -> [terms, m_pad, k/16]."""
     kb = k // 64
-    a = sfx[: terms * m_tiles * kb * 512].reshape(terms, m_tiles, kb, 32, 4, 4)
-    a = a.transpose(0, 1, 4, 3, 2, 5).reshape(terms, m_tiles, 128, kb * 4)
-    return a[:, :, :bn, :].reshape(terms, m_tiles * bn, kb * 4)
+    a = sfx[: m_tiles * kb * 512].reshape(m_tiles, kb, 32, 4, 4)        # [mt, kb, r0, r1, j]
+    a = a.transpose(0, 3, 2, 1, 4).reshape(m_tiles, 128, kb * 4)        # [mt, r1*32 + r0, kb*4 + j]
+    a = a[:, : terms * bn].reshape(m_tiles, terms, bn, kb * 4)
+    return a.transpose(1, 0, 2, 3).reshape(terms, m_tiles * bn, kb * 4)
+
+
+def unpack_xq(xq: np.ndarray, terms: int, m_tiles: int, bn: int, k: int) -> np.ndarray:
+    """[m_tiles][terms*bn][k/2] packed codes -> [terms, m_pad, k] codes."""
+    a = xq[: m_tiles * terms * bn * k // 2].reshape(m_tiles, terms, bn, k // 2).transpose(1, 0, 2, 3)
+    return nv.unpack_codes(a.reshape(terms, m_tiles * bn, k // 2))
 
 
 def random_weight(n, k, seed, realistic=True):
@@ -49,7 +57,8 @@ def run_linear(x_bf16: torch.Tensor, packed, scale16, s2, terms=3, ksplit=0, bia
     return y.float().cpu()
 
 
-@pytest.mark.parametrize("m,k,terms,bn", [(20, 1024, 3, 16), (5, 256, 1, 16), (70, 512, 2, 64), (130, 768, 3, 128)])
+@pytest.mark.parametrize("m,k,terms,bn", [(20, 1024, 3, 16), (5, 256, 1, 16), (70, 512, 2, 64), (130, 768, 3, 32),
+                                          (200, 512, 1, 128)])
 def test_act_quant_bit_exact(m, k, terms, bn):
     d = dev()
     g = torch.Generator().manual_seed(m)
@@ -61,7 +70,7 @@ def test_act_quant_bit_exact(m, k, terms, bn):
     m_tiles = -(-m // bn)
     m_pad = m_tiles * bn
     xq = torch.zeros(terms * m_pad * k // 2, dtype=torch.uint8, device=d)
-    sfx = torch.zeros(terms * m_tiles * (k // 64) * 512, dtype=torch.uint8, device=d)
+    sfx = torch.zeros(m_tiles * (k // 64) * 512, dtype=torch.uint8, device=d)
     gx = torch.zeros(m_pad, dtype=torch.float32, device=d)
     xd = xb.to(d)
     st = N.lib().ada_nvfp4_act_quant(xd.data_ptr(), 0, k, m, k, terms, bn, xq.data_ptr(), sfx.data_ptr(),
@@ -69,7 +78,7 @@ def test_act_quant_bit_exact(m, k, terms, bn):
     N.check(st, "act_quant")
     torch.cuda.synchronize()
     codes, sbits, g_ref = nv.quantize_act_terms(xb.float().numpy(), terms)
-    got_codes = nv.unpack_codes(xq.cpu().numpy().reshape(terms, m_pad, k // 2))
+    got_codes = unpack_xq(xq.cpu().numpy(), terms, m_tiles, bn, k)
     got_sf = unpack_sf(sfx.cpu().numpy(), terms, m_tiles, bn, k)
     norm = lambda c: np.where((c & 7) == 0, 0, c)  # +0 / -0 codes decode identically
     np.testing.assert_array_equal(norm(got_codes[:, :m]), norm(codes))

@@ -132,7 +132,14 @@ def test_embedding_and_argmax():
     logits[2, 17] = 100.0
     logits[2, 99] = 100.0  # first maximum wins
     out = torch.empty(6, device=d, dtype=torch.long)
-    N.check(N.lib().ada_argmax(logits.data_ptr(), 151936, 6, 151936, 0, out.data_ptr(), s), "argmax")
+    ws = torch.empty(N.lib().ada_argmax_workspace_size(6, 151936), dtype=torch.uint8, device=d)
+    N.check(N.lib().ada_argmax(logits.data_ptr(), 151936, 6, 151936, 0, out.data_ptr(), ws.data_ptr(), ws.numel(), s),
+            "argmax")
     ref = logits.float().argmax(dim=1)
     assert out[2].item() == 17
     assert torch.equal(out.cpu(), ref.cpu())
+    # odd widths / strides take the scalar path
+    odd = torch.randn(3, 1001, device=d, dtype=torch.float16)[:, :999]
+    N.check(N.lib().ada_argmax(odd.data_ptr(), 1001, 3, 999, 1, out.data_ptr(), ws.data_ptr(), ws.numel(), s),
+            "argmax")
+    assert torch.equal(out[:3].cpu(), odd.float().argmax(dim=1).cpu())

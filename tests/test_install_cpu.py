@@ -1,0 +1,70 @@
+"""The drop-in shim against the real reference package (CPU: import and patch only;
+no kernel runs).  Skipped where the reference checkout is absent (the GPU box)."""
+import inspect
+import os
+import sys
+
+import pytest
+
+REF = os.environ.get("ADALLM_REF", "/root/reference")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.isdir(os.path.join(REF, "adallm")):
+        pytest.skip("reference checkout not available")
+    os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
+    sys.path.insert(0, REF)
+    try:
+        import adallm.ops.nvfp4_gemm as g  # noqa: F401
+    except Exception as exc:  # pragma: no cover
+        pytest.skip(f"reference not importable here: {exc}")
+    import adallm
+    return adallm
+
+
+def test_signatures_match_reference(ref):
+    import adallm.ops.nvfp4_gemm as rg
+    import adallm.ops.attention as ra
+    from adallm_b200 import nvfp4_gemm, attention
+    for name in ("nvfp4_linear", "nvfp4_linear_dual", "nvfp4_linear_gather"):
+        rp = list(inspect.signature(getattr(rg, name)).parameters)
+        op = list(inspect.signature(getattr(nvfp4_gemm, name)).parameters)
+        assert op[:len(rp)] == rp, (name, rp, op)
+    rp = list(inspect.signature(ra.store_kvcache).parameters)
+    op = list(inspect.signature(attention.store_kvcache).parameters)
+    assert op[:len(rp)] == rp
+
+
+def test_install_patches_reference_ops(ref):
+    import adallm.ops.nvfp4_gemm as rg
+    import adallm.ops.linear as rl
+    import adallm.ops.attention as ra
+    import adallm.ops.layernorm as rln
+    import adallm.ops.rotary_embedding as rr
+    import adallm_b200
+    from adallm_b200 import nvfp4_gemm, context
+    ref_fwd = ra.Attention.forward
+    adallm_b200.install()
+    assert rg.nvfp4_linear is nvfp4_gemm.nvfp4_linear
+    assert rl.nvfp4_linear is nvfp4_gemm.nvfp4_linear
+    assert ra.Attention._adallm_ref_forward is ref_fwd or ra.Attention._adallm_ref_forward.__name__ == "forward"
+    assert ra.Attention.forward.__name__ == "attn_forward"
+    assert "rms_norm" in rln.RMSNorm.forward.__code__.co_names
+    assert "apply_rope" in rr.RotaryEmbedding.forward.__code__.co_names
+    # our context now reads the reference's
+    import adallm.infra.context as rc
+    rc.set_context(False, slot_mapping="s")
+    assert context.get_context().slot_mapping == "s"
+    rc.reset_context()
+    context.use_context_provider(None)
+    assert adallm_b200.install is not None
+
+
+def test_ops_raise_without_cuda(ref):
+    import torch
+    from adallm_b200.nvfp4_gemm import nvfp4_linear
+    x = torch.zeros(2, 256, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        nvfp4_linear(x, torch.zeros(128, 128, dtype=torch.uint8), torch.zeros(128, 16, dtype=torch.float16),
+                     torch.tensor(1.0), None, None, 16)
