@@ -36,9 +36,14 @@ P, I32, I64, F32, INT, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_int
 _SIGS = {
     "ada_status_string": (C.c_char_p, [INT]),
     "ada_abi_version": (INT, []),
+    "ada_set_pdl": (INT, [INT]),
     "ada_fp8_paged_decode_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "ada_fp8_paged_decode": (INT, [P, INT, I64, I64, P, P, I64, I64, I64, I64, P, I64, I32, P, I32, I32, I32, I32, I32,
                                    F32, F32, F32, I32, P, INT, P, SZ, P]),
+    "ada_fp8_paged_decode_quant": (INT, [P, INT, I64, I64, P, P, I64, I64, I64, I64, P, I64, I32, P, I32, I32, I32,
+                                         I32, I32, F32, F32, F32, I32, P, INT, INT, INT, P, P, P, P, SZ, P]),
+    "ada_rmsnorm_quant": (INT, [P, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT, P, P, P, P]),
+    "ada_gated_act_quant": (INT, [P, I64, P, I64, I64, I32, INT, INT, INT, INT, P, P, P, P]),
     "ada_store_kvcache_fp8": (INT, [P, P, INT, I64, I32, I32, I64, I64, P, P, P, I64, F32, F32, P]),
     "ada_rmsnorm": (INT, [P, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, P]),
     "ada_rope": (INT, [P, P, I64, P, I64, P, P, I64, I32, I32, I32, P, I64, INT, P]),
@@ -79,6 +84,8 @@ def lib():
             fn = getattr(h, name)
             fn.restype = res
             fn.argtypes = args
+        if os.environ.get("ADALLM_B200_PDL", "1") == "0":
+            h.ada_set_pdl(0)
         _lib = h
     return _lib
 

@@ -20,7 +20,7 @@
 // g+8 (the permutation is applied to Q identically); for the V operand the
 // output dimension is permuted so thread (g, c) needs bytes [16g, 16g+16) of
 // tokens 2c, 2c+1, 2c+8, 2c+9.  A warp therefore reads whole 128-byte rows.
-#include "common.cuh"
+#include "quant.cuh"
 
 namespace ada {
 namespace attn {
@@ -97,6 +97,9 @@ __device__ __forceinline__ void load_tile(const Params& P, int b, int kvh, int t
 
 template <typename TQ>
 __global__ void __launch_bounds__(THREADS, 3) decode_split_kernel(Params P) {
+  pdl_wait();
+  pdl_trigger();
+
   const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
@@ -280,6 +283,9 @@ __global__ void __launch_bounds__(THREADS, 3) decode_split_kernel(Params P) {
 
 template <typename TO>
 __global__ void __launch_bounds__(D) decode_reduce_kernel(Params P, TO* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
@@ -299,6 +305,77 @@ __global__ void __launch_bounds__(D) decode_reduce_kernel(Params P, TO* __restri
   out[((int64_t)b * P.num_heads + h) * D + d] = from_f32<TO>(r);
 }
 
+
+// Split-K merge fused with the NVFP4 activation quantiser (quant.cuh): one CTA per
+// token, thread i owns 16-element blocks of the token's [num_heads * 128] attention
+// row; the merged row (rounded to the output dtype, as the unfused kernel writes it)
+// is quantised as the operand of o_proj.  `out` may be null.
+template <typename TO, int MAXU>
+__global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* __restrict__ out, int batch,
+                                                                  q::QuantDst dst) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  const int row_len = P.num_heads * D;
+  const int nblk = row_len >> 4;
+  if (b >= batch) {
+    for (int k = threadIdx.x; k < nblk; k += blockDim.x) q::zero_block16(dst, b, k);
+    if (threadIdx.x == 0) dst.gx[b] = 1.f;
+    return;
+  }
+  const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
+  int start, start16, nsplit;
+  seq_range(P, ctx, start, start16, nsplit);
+  float v[MAXU][16];
+  float amax = 0.f;
+#pragma unroll
+  for (int u = 0; u < MAXU; ++u) {
+    const int k = threadIdx.x + u * blockDim.x;
+    if (k >= nblk) continue;
+    const int h = (k * 16) / D, d0 = (k * 16) % D;
+    const int64_t row0 = ((int64_t)b * P.num_heads + h) * P.max_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, P.ml_part[(row0 + s) * 2]);
+    float L = 0.f, O[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) O[i] = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < nsplit; ++s) {
+        const float w = fast_exp2(P.ml_part[(row0 + s) * 2] - M);
+        L += P.ml_part[(row0 + s) * 2 + 1] * w;
+        const float4* op = reinterpret_cast<const float4*>(P.o_part + (row0 + s) * D + d0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 f = op[i];
+          O[4 * i + 0] += f.x * w;
+          O[4 * i + 1] += f.y * w;
+          O[4 * i + 2] += f.z * w;
+          O[4 * i + 3] += f.w * w;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[u][i] = to_f32(from_f32<TO>(L > 0.f ? O[i] / L : 0.f));
+      amax = fmaxf(amax, fabsf(v[u][i]));
+    }
+    if (out) {
+      TO* op = out + (int64_t)b * row_len + k * 16;
+      *reinterpret_cast<uint4*>(op) = pack8<TO>(v[u]);
+      *reinterpret_cast<uint4*>(op + 8) = pack8<TO>(v[u] + 8);
+    }
+  }
+  const float g = q::row_scale(q::block_max(amax, red));
+  const float g6 = __fmul_rn(g, 6.f);
+  if (threadIdx.x == 0) dst.gx[b] = g;
+#pragma unroll
+  for (int u = 0; u < MAXU; ++u) {
+    const int k = threadIdx.x + u * blockDim.x;
+    if (k < nblk) q::quant_block16(dst, b, k, v[u], g, g6);
+  }
+}
+
 inline int max_splits_for(int32_t max_pages, int32_t page) {
   const int64_t toks = (int64_t)max_pages * page;
   return (int)cdiv(toks + 15, CHUNK);  // +15: the tile-aligned window start can add one tile
@@ -316,18 +393,63 @@ extern "C" size_t ada_fp8_paged_decode_workspace_size(int32_t batch, int32_t num
   return (size_t)batch * num_heads * S * (head_dim + 2) * sizeof(float);
 }
 
+static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                             const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
+                             int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
+                             const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                             const int32_t* context_lens, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                             int32_t head_dim, int32_t page_size, float scale, float k_scale, float v_scale,
+                             int32_t window, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                             void* stream, const q::QuantDst* qd);
+
 extern "C" int ada_fp8_paged_decode(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                                     const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
                                     int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
-                                    const int32_t* block_tables,
-                                    int64_t bt_stride, int32_t max_pages, const int32_t* context_lens,
-                                    int32_t batch, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
-                                    int32_t page_size, float scale, float k_scale, float v_scale, int32_t window,
-                                    void* out, int out_dtype, void* workspace, size_t workspace_bytes,
-                                    void* stream) {
+                                    const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                                    const int32_t* context_lens, int32_t batch, int32_t num_heads,
+                                    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float scale,
+                                    float k_scale, float v_scale, int32_t window, void* out, int out_dtype,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!out) return ADA_ERR_INVALID_ARG;
+  return paged_decode_impl(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_tok,
+                           kv_stride_head, num_pages, block_tables, bt_stride, max_pages, context_lens, batch,
+                           num_heads, num_kv_heads, head_dim, page_size, scale, k_scale, v_scale, window, out,
+                           out_dtype, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                          const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
+                                          int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
+                                          const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                                          const int32_t* context_lens, int32_t batch, int32_t num_heads,
+                                          int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float scale,
+                                          float k_scale, float v_scale, int32_t window, void* out, int out_dtype,
+                                          int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  const int row = num_heads * head_dim;
+  if (terms < 1 || terms > 3 || (block_n != 16 && block_n != 32 && block_n != 64 && block_n != 128) ||
+      terms * block_n > 128 || !xq || !sfx || !gx)
+    return ADA_ERR_INVALID_ARG;
+  if (row % 256) return ADA_ERR_UNSUPPORTED;
+  if ((uintptr_t)xq & 15) return ADA_ERR_ALIGNMENT;
+  const q::QuantDst qd{xq, sfx, gx, terms, block_n, row};
+  return paged_decode_impl(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_tok,
+                           kv_stride_head, num_pages, block_tables, bt_stride, max_pages, context_lens, batch,
+                           num_heads, num_kv_heads, head_dim, page_size, scale, k_scale, v_scale, window, out,
+                           out_dtype, workspace, workspace_bytes, stream, &qd);
+}
+
+static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                             const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
+                             int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
+                             const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                             const int32_t* context_lens, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                             int32_t head_dim, int32_t page_size, float scale, float k_scale, float v_scale,
+                             int32_t window, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                             void* stream, const q::QuantDst* qd) {
   if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_pages <= 0 || page_size <= 0) return ADA_ERR_INVALID_ARG;
   if (batch == 0) return ADA_OK;
-  if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out || !workspace) return ADA_ERR_INVALID_ARG;
+  if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !workspace) return ADA_ERR_INVALID_ARG;
   if ((q_dtype != ADA_DT_BF16 && q_dtype != ADA_DT_F16) || (out_dtype != ADA_DT_BF16 && out_dtype != ADA_DT_F16))
     return ADA_ERR_INVALID_ARG;
   if (head_dim != attn::D) return ADA_ERR_UNSUPPORTED;
@@ -370,15 +492,32 @@ extern "C" int ada_fp8_paged_decode(const void* q, int q_dtype, int64_t q_stride
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(P.max_splits, num_kv_heads, batch);
   if (q_dtype == ADA_DT_BF16)
-    attn::decode_split_kernel<__nv_bfloat16><<<grid, attn::THREADS, 0, st>>>(P);
+    (void)ada::launch_k(attn::decode_split_kernel<__nv_bfloat16>, dim3(grid), dim3(attn::THREADS), 0, st, P);
   else
-    attn::decode_split_kernel<__half><<<grid, attn::THREADS, 0, st>>>(P);
+    (void)ada::launch_k(attn::decode_split_kernel<__half>, dim3(grid), dim3(attn::THREADS), 0, st, P);
   ADA_CHECK_LAUNCH();
+  if (qd) {
+    const int m_pad = (int)cdiv(batch, qd->bn) * qd->bn;
+    const int nblk = num_heads * head_dim / 16;
+    const int maxu = (nblk + 255) / 256;
+    if (maxu > 4) return ADA_ERR_UNSUPPORTED;
+#define ADA_RQ(TO, MU)                                                                                              \
+    (void)ada::launch_k(attn::decode_reduce_quant_kernel<TO, MU>, dim3(m_pad), dim3(256), 0, st, P,                   \
+                        reinterpret_cast<TO*>(out), batch, *qd)
+    if (out_dtype == ADA_DT_BF16) {
+      if (maxu == 1) ADA_RQ(__nv_bfloat16, 1); else if (maxu == 2) ADA_RQ(__nv_bfloat16, 2); else ADA_RQ(__nv_bfloat16, 4);
+    } else {
+      if (maxu == 1) ADA_RQ(__half, 1); else if (maxu == 2) ADA_RQ(__half, 2); else ADA_RQ(__half, 4);
+    }
+#undef ADA_RQ
+    ADA_CHECK_LAUNCH();
+    return ADA_OK;
+  }
   dim3 rgrid(num_heads, batch);
   if (out_dtype == ADA_DT_BF16)
-    attn::decode_reduce_kernel<__nv_bfloat16><<<rgrid, attn::D, 0, st>>>(P, reinterpret_cast<__nv_bfloat16*>(out));
+    (void)ada::launch_k(attn::decode_reduce_kernel<__nv_bfloat16>, dim3(rgrid), dim3(attn::D), 0, st, P, reinterpret_cast<__nv_bfloat16*>(out));
   else
-    attn::decode_reduce_kernel<__half><<<rgrid, attn::D, 0, st>>>(P, reinterpret_cast<__half*>(out));
+    (void)ada::launch_k(attn::decode_reduce_kernel<__half>, dim3(rgrid), dim3(attn::D), 0, st, P, reinterpret_cast<__half*>(out));
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }

@@ -23,6 +23,7 @@
 // allocation, and all four warps run the epilogue (warp w reads TMEM lanes
 // 32w..32w+31).  Every mbarrier wait is bounded (2 s); a timeout sets an error
 // bit in the workspace and the CTA drains and exits.
+#include "quant.cuh"
 #include "sm100.cuh"
 
 namespace ada {
@@ -82,6 +83,8 @@ __device__ __forceinline__ float load_bias(const void* b, int dtype, int n) {
 template <int BN, int T>
 __global__ void __launch_bounds__(128, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
+  // dependency wait placed inside (weights are prefetched before it)
+
   using C = Cfg<BN, T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -127,18 +130,34 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer: TMA tiles + bulk scale copies ----------------
+      // The weights and their scales never depend on the previous kernel: the first
+      // `stages` weight tiles are requested before the programmatic-launch dependency
+      // wait, so they stream in while the producer of the activations finishes.
+      const int pre = nk < stages ? nk : stages;
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* st = smem + (size_t)i * C::STAGE;
+        const int kt = kt0 + i;
+        mbar_expect_tx(&full[i], C::A_BYTES + C::SFA_BYTES);
+        tma_load_2d(st, &tmw, &full[i], kt * KT_BYTES, n_tile * BM);
+        bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
+                  C::SFA_BYTES, &full[i]);
+      }
+      pdl_wait();
       for (int i = 0; i < nk; ++i) {
         const int s = i % stages;
-        if (i >= stages && !mbar_wait_bounded(&empty[s], ((i / stages) & 1) ^ 1, abort_v, p.err, 1u)) break;
         uint8_t* st = smem + (size_t)s * C::STAGE;
         const int kt = kt0 + i;
-        mbar_arrive_expect_tx(&full[s], C::STAGE);
-        tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, n_tile * BM);
+        if (i >= stages) {
+          if (!mbar_wait_bounded(&empty[s], ((i / stages) & 1) ^ 1, abort_v, p.err, 1u)) break;
+          mbar_expect_tx(&full[s], C::A_BYTES + C::SFA_BYTES);
+          tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, n_tile * BM);
+          bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
+                    C::SFA_BYTES, &full[s]);
+        }
+        mbar_arrive_expect_tx(&full[s], C::B_BYTES + C::SFB_BYTES);
         tma_load_2d(st + C::A_BYTES, &tmx, &full[s], kt * KT_BYTES, m_tile * C::NB);
-        uint8_t* sf = st + C::A_BYTES + C::B_BYTES;
-        bulk_load(sf, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFA_BYTES, &full[s]);
-        bulk_load(sf + C::SFA_BYTES, p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES,
-                  &full[s]);
+        bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
+                  p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES, &full[s]);
       }
     }
     __syncwarp();
@@ -173,6 +192,8 @@ __global__ void __launch_bounds__(128, 1)
   }
 
   // ---------------- epilogue: all 4 warps ----------------
+  pdl_wait();     // activations / scales / workspace of earlier kernels are visible from here on
+  pdl_trigger();  // the next kernel may get resident while this one drains
   const bool ok = mbar_wait_bounded(accf, 0, abort_v, p.err, 4u) && !*abort_v;
   tc_fence_after();
   __syncwarp();
@@ -242,44 +263,19 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Activation quantiser (bit-exact spec: oracle/nvfp4.py quantize_act_terms).
-// One CTA per (padded) row.  Token m = mt*bn + j, term t is operand row r = t*bn + j
-// of token tile mt (terms stacked along the MMA N dimension).  Layouts written:
-//   xq  [m_tiles][T*bn][K/2]      packed e2m1, even K in the low nibble
-//   sfx [m_tiles][K/64][512]      ue4m3 scales in the MMA scale-factor layout
-//   gx  [m_pad]                   per-row fp32 scale (1.0 for padding rows)
-__device__ __forceinline__ float e2m1_value(uint32_t c) {
-  const uint32_t mag = c & 7u;
-  float v = mag < 2u ? 0.5f * (float)mag : (float)(2u + (mag & 1u)) * __int_as_float((int)(((mag >> 1) + 125u) << 23));
-  return (c & 8u) ? -v : v;
-}
-__device__ __forceinline__ float e4m3_value(uint8_t b) {
-  const uint32_t h = e4m3x2_to_f16x2((uint16_t)b);
-  return __half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)));
-}
-
+// Activation quantiser (layout and arithmetic: quant.cuh).  One CTA per (padded) row.
 template <typename TI>
 __global__ void __launch_bounds__(256) act_quant_kernel(const TI* __restrict__ x, int64_t ldx, int M, int K, int terms,
                                                         int bn, int m_tiles, int m_pad, uint8_t* __restrict__ xq,
                                                         uint8_t* __restrict__ sfx, float* __restrict__ gx) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8];
   const int m = blockIdx.x;
   const int nblk = K >> 4;
-  const int kb64 = K >> 6;
-  const int mt = m / bn, row = m - mt * bn;
-  const size_t khalf = (size_t)K >> 1;
-  const int nb = terms * bn;
-  auto sf_off = [&](int t, int blk) {
-    const int r = t * bn + row;
-    return ((size_t)mt * kb64 + (blk >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (blk & 3);
-  };
-  auto xq_row = [&](int t) { return xq + ((size_t)mt * nb + (size_t)t * bn + row) * khalf; };
-  if (m >= M) {  // padding row: zero codes and scales
-    for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x)
-      for (int t = 0; t < terms; ++t) {
-        *reinterpret_cast<uint2*>(xq_row(t) + (size_t)blk * 8) = make_uint2(0, 0);
-        sfx[sf_off(t, blk)] = 0;
-      }
+  const q::QuantDst dst{xq, sfx, gx, terms, bn, K};
+  if (m >= M) {
+    for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x) q::zero_block16(dst, m, blk);
     if (threadIdx.x == 0) gx[m] = 1.f;
     return;
   }
@@ -292,44 +288,15 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const TI* __restrict__ x
 #pragma unroll
     for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-  __syncthreads();
-  amax = 0.f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
-  const float g = amax > 0.f ? __fdiv_rn(amax, 2688.f) : 1.f;
+  amax = q::block_max(amax, red);
+  const float g = q::row_scale(amax);
   const float g6 = __fmul_rn(g, 6.f);
   if (threadIdx.x == 0) gx[m] = g;
-
   for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x) {
     float r[16];
     unpack8<TI>(*reinterpret_cast<const uint4*>(xr + blk * 16), r);
     unpack8<TI>(*reinterpret_cast<const uint4*>(xr + blk * 16 + 8), r + 8);
-    for (int t = 0; t < terms; ++t) {
-      float bamax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(r[i]));
-      const uint8_t sb = (uint8_t)(f32x2_to_e4m3x2(__fdiv_rn(bamax, g6), 0.f) & 0xFFu);
-      const float sv = e4m3_value(sb);
-      uint2 codes = make_uint2(0, 0);
-      if (sv > 0.f) {
-        const float denom = __fmul_rn(sv, g);
-        const float rcp = __fdiv_rn(1.f, denom);
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(r[i], rcp);
-        codes.x = f32x8_to_e2m1x8(v);
-        codes.y = f32x8_to_e2m1x8(v + 8);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t c = ((i < 8 ? codes.x : codes.y) >> (4 * (i & 7))) & 0xFu;
-          r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(c), denom));
-        }
-      }
-      *reinterpret_cast<uint2*>(xq_row(t) + (size_t)blk * 8) = codes;
-      sfx[sf_off(t, blk)] = sb;
-    }
+    q::quant_block16(dst, m, blk, r, g, g6);
   }
 }
 
@@ -337,6 +304,9 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const TI* __restrict__ x
 // [N/128][K/64][512] bytes in the MMA scale-factor layout.
 __global__ void __launch_bounds__(128) prepack_kernel(const void* __restrict__ scale, int is_fp16, int64_t ld, int N,
                                                       int K, uint8_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+
   const int kb64 = K >> 6;
   const int nb = blockIdx.x / kb64, kb = blockIdx.x - nb * kb64;
   const int r = threadIdx.x;
@@ -488,7 +458,7 @@ static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const Gem
     configured = P.smem;
   }
   dim3 grid(P.n_tiles * P.m_tiles, P.ksplit);
-  kern<<<grid, 128, P.smem, st>>>(tmw, tmx, gp);
+  (void)ada::launch_k(kern, dim3(grid), dim3(128), P.smem, st, tmw, tmx, gp);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }
@@ -561,7 +531,7 @@ extern "C" int ada_nvfp4_prepack_scales(const void* scale, int scale_is_fp16, in
   if ((uintptr_t)sf_out & 15) return ADA_ERR_ALIGNMENT;
   const int64_t blocks = cdiv(n, 128) * (k / 64);
   if (blocks > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
-  fp4::prepack_kernel<<<(unsigned)blocks, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  (void)ada::launch_k(fp4::prepack_kernel, dim3((unsigned)blocks), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream), 
       scale, scale_is_fp16, ld_scale, (int)n, (int)k, sf_out);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
@@ -596,11 +566,11 @@ extern "C" int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int6
   uint8_t* sfx = ws + P.off_sfx;
   float* gx = reinterpret_cast<float*>(ws + P.off_gx);
   if (x_dtype == ADA_DT_BF16)
-    fp4::act_quant_kernel<__nv_bfloat16><<<P.m_pad, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+    (void)ada::launch_k(fp4::act_quant_kernel<__nv_bfloat16>, dim3(P.m_pad), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                                                   (int)m, (int)k, terms, P.bn, P.m_tiles, P.m_pad, xq,
                                                                   sfx, gx);
   else
-    fp4::act_quant_kernel<__half><<<P.m_pad, 256, 0, st>>>(reinterpret_cast<const __half*>(x), ldx, (int)m, (int)k,
+    (void)ada::launch_k(fp4::act_quant_kernel<__half>, dim3(P.m_pad), dim3(256), 0, st, reinterpret_cast<const __half*>(x), ldx, (int)m, (int)k,
                                                            terms, P.bn, P.m_tiles, P.m_pad, xq, sfx, gx);
   ADA_CHECK_LAUNCH();
 
@@ -627,11 +597,11 @@ extern "C" int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int6
   const int m_tiles = (int)cdiv(m, block_n), m_pad = m_tiles * block_n;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (x_dtype == ADA_DT_BF16)
-    fp4::act_quant_kernel<__nv_bfloat16><<<m_pad, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+    (void)ada::launch_k(fp4::act_quant_kernel<__nv_bfloat16>, dim3(m_pad), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                                                 (int)m, (int)k, terms, block_n, m_tiles, m_pad, xq,
                                                                 sfx, gx);
   else
-    fp4::act_quant_kernel<__half><<<m_pad, 256, 0, st>>>(reinterpret_cast<const __half*>(x), ldx, (int)m, (int)k,
+    (void)ada::launch_k(fp4::act_quant_kernel<__half>, dim3(m_pad), dim3(256), 0, st, reinterpret_cast<const __half*>(x), ldx, (int)m, (int)k,
                                                          terms, block_n, m_tiles, m_pad, xq, sfx, gx);
   ADA_CHECK_LAUNCH();
   return ADA_OK;

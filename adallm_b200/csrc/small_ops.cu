@@ -21,6 +21,9 @@ __global__ void __launch_bounds__(128) store_kv_kernel(const T* __restrict__ key
                                                        int64_t ks, int64_t vs, const int32_t* __restrict__ slots,
                                                        uint8_t* __restrict__ kc, uint8_t* __restrict__ vc,
                                                        int64_t crs, int hd, float k_scale, float v_scale) {
+  pdl_wait();
+  pdl_trigger();
+
   const int t = blockIdx.x;
   const int slot = __ldg(slots + t);
   if (slot < 0) return;  // -1 marks a padded token (attention.py:21)
@@ -76,6 +79,9 @@ template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, int64_t ldx, const T* res, int64_t ldr,
                                                       T* res_out, int64_t ldro, const T* __restrict__ w, T* y,
                                                       int64_t ldy, int hidden, float eps, int gemma) {
+  pdl_wait();
+  pdl_trigger();
+
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nvec = hidden >> 3;
@@ -132,6 +138,9 @@ template <typename T>
 __global__ void __launch_bounds__(128) rope_kernel(const int64_t* __restrict__ pos, const T* q, int64_t qs,
                                                    const T* k, int64_t ks, T* qo, T* ko, int hq, int hk, int d,
                                                    const float* __restrict__ cs, int64_t max_pos) {
+  pdl_wait();
+  pdl_trigger();
+
   const int t = blockIdx.x;
   const int half = d >> 1;
   const int per_head = half >> 3;
@@ -179,6 +188,9 @@ __global__ void __launch_bounds__(128) qk_norm_rope_store_kernel(
     float eps, const int64_t* __restrict__ pos, const float* __restrict__ cs, int64_t max_pos,
     const int32_t* __restrict__ slots, uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, float k_scale,
     float v_scale, T* __restrict__ q_out, T* __restrict__ k_out, int64_t num_tokens) {
+  pdl_wait();
+  pdl_trigger();
+
   constexpr int D = 128;
   const int lane = threadIdx.x & 31;
   const int nheads = hq + 2 * hkv;
@@ -267,6 +279,9 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 template <typename T>
 __global__ void gated_act_kernel(const T* __restrict__ x, int64_t ldx, T* __restrict__ y, int64_t ldy, int64_t rows,
                                  int inter, int act) {
+  pdl_wait();
+  pdl_trigger();
+
   const int nvec = inter >> 3;
   const int64_t total = rows * nvec;
   for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < total; it += (int64_t)gridDim.x * blockDim.x) {
@@ -287,6 +302,9 @@ __global__ void gated_act_kernel(const T* __restrict__ x, int64_t ldx, T* __rest
 // ---------------------------------------------------------------------------
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const uint4* __restrict__ table, int64_t v0,
                                  int64_t v1, int nvec, uint4* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+
   const int t = blockIdx.x;
   const int64_t id = __ldg(ids + t);
   const bool in = id >= v0 && id < v1;
@@ -305,6 +323,9 @@ template <typename T>
 __global__ void __launch_bounds__(256) argmax_stage1(const T* __restrict__ x, int64_t ld, int64_t cols,
                                                      int64_t chunk, float* __restrict__ pv,
                                                      int64_t* __restrict__ pi) {
+  pdl_wait();
+  pdl_trigger();
+
   __shared__ float sv[8];
   __shared__ int64_t si[8];
   const int64_t r = blockIdx.y;
@@ -346,6 +367,9 @@ __global__ void __launch_bounds__(256) argmax_stage1(const T* __restrict__ x, in
 
 __global__ void __launch_bounds__(32) argmax_stage2(const float* __restrict__ pv, const int64_t* __restrict__ pi,
                                                     int chunks, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+
   const int64_t r = blockIdx.x;
   float bv = -INFINITY;
   int64_t bi = 0x7fffffffffffffffLL;
@@ -387,11 +411,11 @@ extern "C" int ada_store_kvcache_fp8(const void* key, const void* value, int in_
   if (((uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)cache_row_stride) & 7) return ADA_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (in_dtype == ADA_DT_BF16)
-    small::store_kv_kernel<__nv_bfloat16><<<(unsigned)num_tokens, 128, 0, st>>>(
+    (void)ada::launch_k(small::store_kv_kernel<__nv_bfloat16>, dim3((unsigned)num_tokens), dim3(128), 0, st, 
         (const __nv_bfloat16*)key, (const __nv_bfloat16*)value, key_stride, value_stride, slot_mapping, k_cache,
         v_cache, cache_row_stride, hd, k_scale, v_scale);
   else
-    small::store_kv_kernel<__half><<<(unsigned)num_tokens, 128, 0, st>>>(
+    (void)ada::launch_k(small::store_kv_kernel<__half>, dim3((unsigned)num_tokens), dim3(128), 0, st, 
         (const __half*)key, (const __half*)value, key_stride, value_stride, slot_mapping, k_cache, v_cache,
         cache_row_stride, hd, k_scale, v_scale);
   ADA_CHECK_LAUNCH();
@@ -406,7 +430,7 @@ static int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t l
   int threads = nvec >= 256 ? 256 : ((nvec + 31) / 32) * 32;
   const int per = (nvec + threads - 1) / threads;
 #define ADA_RMS(MV)                                                                                         \
-  small::rmsnorm_kernel<T, MV><<<(unsigned)rows, threads, 0, st>>>((const T*)x, ldx, (const T*)res, ldr,    \
+  (void)ada::launch_k(small::rmsnorm_kernel<T, MV>, dim3((unsigned)rows), dim3(threads), 0, st, (const T*)x, ldx, (const T*)res, ldr,    \
                                                                    (T*)ro, ldro, (const T*)w, (T*)y, ldy,   \
                                                                    hidden, eps, gemma)
   if (per <= 1) ADA_RMS(1);
@@ -448,11 +472,11 @@ extern "C" int ada_rope(const int64_t* positions, const void* q, int64_t q_strid
   if (!a16(q) || !a16(k) || !a16(q_out) || !a16(k_out) || (q_stride & 7) || (k_stride & 7)) return ADA_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == ADA_DT_BF16)
-    small::rope_kernel<__nv_bfloat16><<<(unsigned)num_tokens, 128, 0, st>>>(
+    (void)ada::launch_k(small::rope_kernel<__nv_bfloat16>, dim3((unsigned)num_tokens), dim3(128), 0, st, 
         positions, (const __nv_bfloat16*)q, q_stride, (const __nv_bfloat16*)k, k_stride, (__nv_bfloat16*)q_out,
         (__nv_bfloat16*)k_out, num_q_heads, num_kv_heads, head_dim, cos_sin, max_position);
   else
-    small::rope_kernel<__half><<<(unsigned)num_tokens, 128, 0, st>>>(positions, (const __half*)q, q_stride,
+    (void)ada::launch_k(small::rope_kernel<__half>, dim3((unsigned)num_tokens), dim3(128), 0, st, positions, (const __half*)q, q_stride,
                                                                      (const __half*)k, k_stride, (__half*)q_out,
                                                                      (__half*)k_out, num_q_heads, num_kv_heads,
                                                                      head_dim, cos_sin, max_position);
@@ -481,7 +505,7 @@ extern "C" int ada_qk_norm_rope_store(const void* qkv, int64_t ld, int64_t num_t
   const int64_t items = num_tokens * (num_q_heads + 2 * num_kv_heads);
   const unsigned blocks = (unsigned)((items + 3) / 4);
 #define ADA_QK(T)                                                                                               \
-  small::qk_norm_rope_store_kernel<T><<<blocks, 128, 0, st>>>(                                                   \
+  (void)ada::launch_k(small::qk_norm_rope_store_kernel<T>, dim3(blocks), dim3(128), 0, st,                                                    \
       (const T*)qkv, ld, num_q_heads, num_kv_heads, (const T*)q_norm_w, (const T*)k_norm_w, eps, positions,       \
       cos_sin, max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out, num_tokens)
   if (dtype == ADA_DT_BF16) ADA_QK(__nv_bfloat16);
@@ -503,10 +527,10 @@ extern "C" int ada_gated_act(const void* x, int64_t ldx, void* y, int64_t ldy, i
   const int64_t total = rows * (inter / 8);
   const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8);
   if (dtype == ADA_DT_BF16)
-    small::gated_act_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x, ldx, (__nv_bfloat16*)y,
+    (void)ada::launch_k(small::gated_act_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, (const __nv_bfloat16*)x, ldx, (__nv_bfloat16*)y,
                                                                    ldy, rows, inter, act);
   else
-    small::gated_act_kernel<__half><<<blocks, 256, 0, st>>>((const __half*)x, ldx, (__half*)y, ldy, rows, inter, act);
+    (void)ada::launch_k(small::gated_act_kernel<__half>, dim3(blocks), dim3(256), 0, st, (const __half*)x, ldx, (__half*)y, ldy, rows, inter, act);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }
@@ -519,7 +543,7 @@ extern "C" int ada_embedding(const int64_t* ids, int64_t num_tokens, const void*
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
   if (hidden % 8) return ADA_ERR_UNSUPPORTED;
   if (!a16(table) || !a16(y)) return ADA_ERR_ALIGNMENT;
-  small::embedding_kernel<<<(unsigned)num_tokens, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  (void)ada::launch_k(small::embedding_kernel, dim3((unsigned)num_tokens), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream), 
       ids, (const uint4*)table, vocab_start, vocab_end, hidden / 8, (uint4*)y);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
@@ -545,13 +569,13 @@ extern "C" int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 g1(chunks, (unsigned)rows);
   if (dtype == ADA_DT_BF16)
-    small::argmax_stage1<__nv_bfloat16><<<g1, 256, 0, st>>>((const __nv_bfloat16*)logits, ld, cols, chunk, pv, pi);
+    (void)ada::launch_k(small::argmax_stage1<__nv_bfloat16>, dim3(g1), dim3(256), 0, st, (const __nv_bfloat16*)logits, ld, cols, chunk, pv, pi);
   else if (dtype == ADA_DT_F16)
-    small::argmax_stage1<__half><<<g1, 256, 0, st>>>((const __half*)logits, ld, cols, chunk, pv, pi);
+    (void)ada::launch_k(small::argmax_stage1<__half>, dim3(g1), dim3(256), 0, st, (const __half*)logits, ld, cols, chunk, pv, pi);
   else
     return ADA_ERR_INVALID_ARG;
   ADA_CHECK_LAUNCH();
-  small::argmax_stage2<<<(unsigned)rows, 32, 0, st>>>(pv, pi, chunks, out);
+  (void)ada::launch_k(small::argmax_stage2, dim3((unsigned)rows), dim3(32), 0, st, pv, pi, chunks, out);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }
@@ -571,3 +595,9 @@ extern "C" const char* ada_status_string(int status) {
 }
 
 extern "C" int ada_abi_version(void) { return 1; }
+
+extern "C" int ada_set_pdl(int enable) {
+  const int prev = ada::g_pdl_enabled ? 1 : 0;
+  ada::g_pdl_enabled = enable != 0;
+  return prev;
+}

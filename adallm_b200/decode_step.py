@@ -115,8 +115,9 @@ class Qwen3DecodeEngine:
     """Static-shape decode engine for batch ``max_batch`` (graph-capturable)."""
 
     def __init__(self, cfg: DecodeConfig, device, max_batch: int, max_ctx: int, seed: int = 0,
-                 group=None):
+                 group=None, fused: bool = True):
         self.cfg = cfg
+        self.fused = fused
         self.device = torch.device(device)
         self.B = max_batch
         self.max_pages_per_seq = -(-max_ctx // cfg.page_size)
@@ -231,6 +232,19 @@ class Qwen3DecodeEngine:
         self.gemm_ws = torch.zeros(max(workspace_bytes(*s, c.terms) for s in shapes), dtype=torch.uint8, device=d)
         self.attn_ws_bytes = int(N.lib().ada_fp8_paged_decode_workspace_size(B, c.hq, self.max_pages_per_seq,
                                                                              c.page_size, D))
+        # quantised GEMM operands written by the fused producers (ada_nvfp4_act_quant layout)
+        self.bn = int(N.lib().ada_nvfp4_block_n(B, c.terms))
+        self.m_pad = -(-B // self.bn) * self.bn
+
+        def qbuf(k):
+            return (torch.zeros(self.m_pad * c.terms * k // 2, dtype=torch.uint8, device=d),
+                    torch.zeros((self.m_pad // self.bn) * (k // 64) * 512, dtype=torch.uint8, device=d),
+                    torch.ones(self.m_pad, dtype=torch.float32, device=d))
+        self.q_hidden = qbuf(H)
+        self.q_attn = qbuf(c.hq * D)
+        self.q_inter = qbuf(c.inter)
+        self.gemm_only_ws = torch.zeros(max(int(N.lib().ada_nvfp4_gemm_workspace_size(*s_, c.terms))
+                                            for s_ in shapes), dtype=torch.uint8, device=d)
         self.attn_ws = torch.zeros(max(self.attn_ws_bytes, 256), dtype=torch.uint8, device=d)
 
     # ------------------------------------------------------------------ ops
@@ -241,6 +255,24 @@ class Qwen3DecodeEngine:
                                       y.data_ptr(), 0, y.stride(0), c.terms, self.gemm_ws.data_ptr(),
                                       self.gemm_ws.numel(), stream)
         N.check(st, "NVFP4 kernel")
+
+    def _gemm(self, qb, w: NVFP4Weight, y: torch.Tensor, stream: int):
+        c = self.cfg
+        xq, sfx, gx = qb
+        st = N.lib().ada_nvfp4_gemm(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), self.B, c.terms, self.bn,
+                                    w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(), w.scale_2.data_ptr(),
+                                    w.n, w.k, None, y.data_ptr(), 0, y.stride(0), 0, self.gemm_only_ws.data_ptr(),
+                                    self.gemm_only_ws.numel(), stream)
+        N.check(st, "NVFP4 kernel")
+
+    def _rms_quant(self, x, w, qb, stream, residual=None):
+        c = self.cfg
+        H = x.shape[-1]
+        xq, sfx, gx = qb
+        rp = residual.data_ptr() if residual is not None else None
+        st = N.lib().ada_rmsnorm_quant(x.data_ptr(), H, rp, H, rp, H, w.data_ptr(), None, 0, self.B, H, c.rms_eps, 0, 0,
+                                       c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), stream)
+        N.check(st, "rms_norm+quant")
 
     def _rms(self, x, w, y, stream, residual=None, rows=None, hidden=None):
         c = self.cfg
@@ -269,6 +301,49 @@ class Qwen3DecodeEngine:
         N.check(lib.ada_embedding(self.input_ids.data_ptr(), B, self.embed.data_ptr(), v0, v0 + c.vocab_shard,
                                   c.hidden, self.hidden.data_ptr(), 0, stream), "embedding")
         self._all_reduce(self.hidden)
+        qn, kn = c.hq * D, c.hkv * D
+        if not self.fused:
+            self._layers_unfused(lib, stream)
+        else:
+            for li, L in enumerate(self.layers):
+                if li == 0:
+                    self.residual.copy_(self.hidden)
+                    self._rms_quant(self.hidden, L["in_norm"], self.q_hidden, stream)
+                else:
+                    self._rms_quant(self.hidden, L["in_norm"], self.q_hidden, stream, residual=self.residual)
+                self._gemm(self.q_hidden, L["qkv"], self.qkv, stream)
+                kc, vc = self.kv_cache[0, li], self.kv_cache[1, li]
+                N.check(lib.ada_qk_norm_rope_store(self.qkv.data_ptr(), self.qkv.stride(0), B, c.hq, c.hkv, D,
+                                                   L["q_norm"].data_ptr(), L["k_norm"].data_ptr(), c.rms_eps,
+                                                   self.positions.data_ptr(), self.cos_sin.data_ptr(),
+                                                   self.cos_sin.shape[0], self.slot_mapping.data_ptr(),
+                                                   kc.data_ptr(), vc.data_ptr(), 1.0, 1.0, self.q_rot.data_ptr(),
+                                                   None, 0, stream), "qk_norm_rope_store")
+                xq, sfx, gx = self.q_attn
+                N.check(lib.ada_fp8_paged_decode_quant(
+                    self.q_rot.data_ptr(), 0, qn, D, kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1),
+                    kc.stride(2), self.num_pages, self.block_tables.data_ptr(), self.block_tables.stride(0),
+                    self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv, D, c.page_size,
+                    D ** -0.5, 1.0, 1.0, 0, None, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
+                    gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, stream), "attention")
+                self._gemm(self.q_attn, L["o"], self.hidden, stream)
+                self._all_reduce(self.hidden)
+                self._rms_quant(self.hidden, L["post_norm"], self.q_hidden, stream, residual=self.residual)
+                self._gemm(self.q_hidden, L["gate_up"], self.gate_up, stream)
+                xq, sfx, gx = self.q_inter
+                N.check(lib.ada_gated_act_quant(self.gate_up.data_ptr(), 2 * c.inter, None, 0, B, c.inter, 0, 0,
+                                                c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(),
+                                                stream), "silu_and_mul+quant")
+                self._gemm(self.q_inter, L["down"], self.hidden, stream)
+                self._all_reduce(self.hidden)
+        self._rms(self.hidden, self.final_norm, self.xnorm, stream, residual=self.residual)
+        torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
+        self._argmax(stream)
+
+    def _layers_unfused(self, lib, stream):
+        """Reference-shaped sequence: every op a separate kernel (act-quant separate from the GEMM)."""
+        c = self.cfg
+        B, D = self.B, c.head_dim
         qn, kn = c.hq * D, c.hkv * D
         for li, L in enumerate(self.layers):
             if li == 0:
@@ -299,9 +374,6 @@ class Qwen3DecodeEngine:
                                       0, 0, stream), "silu_and_mul")
             self._linear(self.act, L["down"], self.hidden, stream)
             self._all_reduce(self.hidden)
-        self._rms(self.hidden, self.final_norm, self.xnorm, stream, residual=self.residual)
-        torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
-        self._argmax(stream)
 
     def _argmax(self, stream):
         c = self.cfg
@@ -347,9 +419,11 @@ class Qwen3DecodeEngine:
         return g
 
     def kernels_per_step(self) -> int:
-        """adallm_b200 kernels launched by one forward(): embedding, per layer (norm, act-quant+GEMM x4,
-        qk-norm/rope/store, attention split + reduce, norm, SiLU*up), final norm, argmax."""
-        return 1 + self.cfg.num_layers * 14 + 3
+        """adallm_b200 kernels launched by one forward(): embedding; per layer fused: norm+quant x2,
+        GEMM x4, qk-norm/rope/store, attention split + merge+quant, SiLU*up+quant (unfused: norm x2,
+        act-quant + GEMM x4, qk-norm/rope/store, attention split + merge, SiLU*up); final norm; argmax x2."""
+        per_layer = 10 if self.fused else 14
+        return 1 + self.cfg.num_layers * per_layer + 3
 
     def export_cpu_weights(self) -> dict:
         """CPU copies in the reference parameter layout (tensor-parallel size 1 only)."""

@@ -51,6 +51,11 @@ enum { ADA_DT_BF16 = 0, ADA_DT_F16 = 1 };
 ADA_API const char* ada_status_string(int status);
 /* ABI version of this library (bumped on any signature change). */
 ADA_API int ada_abi_version(void);
+/* Programmatic dependent launch (on by default): every kernel may start while the previous
+ * kernel on its stream drains, and waits on the device (griddepcontrol.wait) before reading
+ * anything that kernel wrote.  ada_set_pdl(0) launches kernels with plain stream ordering.
+ * Returns the previous setting.  Process-wide; set it before capturing graphs. */
+ADA_API int ada_set_pdl(int enable);
 
 /* ------------------------------------------------------------------------
  * FP8 paged split-K decode attention
@@ -81,6 +86,22 @@ ADA_API int ada_fp8_paged_decode(const void* q, int q_dtype, int64_t q_stride_b,
                          float k_scale, float v_scale, int32_t window, void* out, int out_dtype,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same, with the split-K merge fused with the NVFP4 activation quantiser: the merged
+ * attention row of every sequence ([num_heads * head_dim], rounded to out_dtype) is written
+ * as the operand of o_proj in the ada_nvfp4_act_quant layout (xq / sfx / gx, `terms`,
+ * block_n); `out` may be NULL.  num_heads * head_dim must be a multiple of 256. */
+ADA_API int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                       const uint8_t* k_cache, const uint8_t* v_cache,
+                                       int64_t kv_stride_page, int64_t kv_stride_tok,
+                                       int64_t kv_stride_head, int64_t num_pages,
+                                       const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                                       const int32_t* context_lens, int32_t batch, int32_t num_heads,
+                                       int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                       float scale, float k_scale, float v_scale, int32_t window,
+                                       void* out, int out_dtype, int terms, int block_n, uint8_t* xq,
+                                       uint8_t* sfx, float* gx, void* workspace, size_t workspace_bytes,
+                                       void* stream);
+
 /* ------------------------------------------------------------------------
  * FP8 KV-cache store
  * Replaces store_kvcache / store_kvcache_kernel (adallm/ops/attention.py:11-31, :236-251).
@@ -107,6 +128,15 @@ ADA_API int ada_store_kvcache_fp8(const void* key, const void* value, int in_dty
 ADA_API int ada_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ld_res,
                 void* residual_out, int64_t ld_res_out, const void* weight, void* y, int64_t ldy,
                 int64_t rows, int32_t hidden, float eps, int gemma, int dtype, void* stream);
+
+/* RMSNorm fused with the NVFP4 activation quantiser: the normalised row (exactly what
+ * ada_rmsnorm returns) is written as the GEMM operand in the ada_nvfp4_act_quant layout
+ * (xq / sfx / gx for `terms` and block_n; rows up to ceil(rows/block_n)*block_n, padding
+ * rows zero).  y may be NULL (no bf16 copy).  hidden must be a multiple of 256. */
+ADA_API int ada_rmsnorm_quant(const void* x, int64_t ldx, const void* residual, int64_t ld_res,
+                              void* residual_out, int64_t ld_res_out, const void* weight, void* y,
+                              int64_t ldy, int64_t rows, int32_t hidden, float eps, int gemma, int dtype,
+                              int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 
 /* ------------------------------------------------------------------------
  * Rotary embedding (NeoX rotate-half) from the reference's fp32 cos/sin cache
@@ -143,6 +173,12 @@ ADA_API int ada_qk_norm_rope_store(const void* qkv, int64_t ld, int64_t num_toke
  * ---------------------------------------------------------------------- */
 ADA_API int ada_gated_act(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows,
                   int32_t inter, int act, int dtype, void* stream);
+
+/* Gated activation fused with the NVFP4 activation quantiser (operand of down_proj);
+ * y may be NULL.  inter must be a multiple of 256. */
+ADA_API int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows,
+                                int32_t inter, int act, int dtype, int terms, int block_n, uint8_t* xq,
+                                uint8_t* sfx, float* gx, void* stream);
 
 /* ------------------------------------------------------------------------
  * Token embedding gather: y[t] = table[ids[t]] (bf16/f16 rows of width hidden).

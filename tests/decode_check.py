@@ -3,7 +3,7 @@
 not cascade).  Used by tests/test_gpu_decode.py and __graft_entry__.smoke().
 
 Two figures are returned: raw agreement, and agreement over *decisive* steps where the
-oracle's top-1 / top-2 logit gap exceeds 1% of the logit RMS.  Random-init models have
+oracle's top-1 / top-2 logit gap exceeds 10% of the logit RMS.  Random-init models have
 near-tied logits, and the e4m3 KV cache turns last-bit bf16 differences into ~6% jumps
 of single K/V elements, so any implementation whose k/v are not bit-identical to the
 oracle's flips some near-ties (an emulation of the reference's own fp16 numerics agrees
@@ -57,9 +57,10 @@ def run_agreement(layers=2, steps=8, batch=4, prompt=4, graph=True, return_logit
         if i >= prompt - 1:
             agree += int((ours == theirs).sum())
             total += batch
-            # decisive steps: the oracle's top-1 / top-2 gap exceeds 1% of the logit RMS
+            # decisive steps: the oracle's top-1 / top-2 gap exceeds 10% of the logit RMS (about three
+            # standard deviations of the top-2 difference under the ~2% logit deviation measured here)
             top2 = logits.topk(2, dim=1).values
-            decisive = (top2[:, 0] - top2[:, 1]) > 0.01 * logits.pow(2).mean(dim=1).sqrt()
+            decisive = (top2[:, 0] - top2[:, 1]) > 0.1 * logits.pow(2).mean(dim=1).sqrt()
             dec_agree += int(((ours == theirs) & decisive).sum())
             dec_total += int(decisive.sum())
         cur = tokens[:, i + 1] if i + 1 < prompt else theirs

@@ -10,7 +10,7 @@ pytestmark = pytest.mark.gpu
 
 
 def test_decode_step_agreement_graph():
-    raw, decisive, errs = run_agreement(layers=4, steps=32, batch=4, prompt=8, graph=True, return_logits=True)
+    raw, decisive, errs = run_agreement(layers=4, steps=64, batch=4, prompt=8, graph=True, return_logits=True)
     assert decisive >= 0.99, (raw, decisive)
     assert raw >= 0.90, (raw, decisive)
     assert max(errs) < 5e-2, errs
