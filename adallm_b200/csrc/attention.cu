@@ -20,6 +20,7 @@
 // g+8 (the permutation is applied to Q identically); for the V operand the
 // output dimension is permuted so thread (g, c) needs bytes [16g, 16g+16) of
 // tokens 2c, 2c+1, 2c+8, 2c+9.  A warp therefore reads whole 128-byte rows.
+#include "cluster.cuh"
 #include "quant.cuh"
 
 namespace ada {
@@ -306,22 +307,27 @@ __global__ void __launch_bounds__(D) decode_reduce_kernel(Params P, TO* __restri
 }
 
 
-// Split-K merge fused with the NVFP4 activation quantiser (quant.cuh): one CTA per
-// token, thread i owns 16-element blocks of the token's [num_heads * 128] attention
-// row; the merged row (rounded to the output dtype, as the unfused kernel writes it)
-// is quantised as the operand of o_proj.  `out` may be null.
+// Split-K merge fused with the NVFP4 activation quantiser (quant.cuh): the token's
+// [num_heads * 128] attention row is spread over a cluster of CTAs (grid (ctas, m_pad),
+// cluster.cuh), each merging a contiguous slice of 16-element units; the merged row
+// (rounded to the output dtype, as the unfused kernel writes it) is quantised as the
+// operand of o_proj once the cluster has combined the row amax.  `out` may be null.
 template <typename TO, int MAXU>
 __global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* __restrict__ out, int batch,
                                                                   q::QuantDst dst) {
+  cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
   __shared__ float red[8];
-  const int b = blockIdx.x;
+  __shared__ float slots[cl::MAX_CLUSTER];
+  const int b = blockIdx.y;
   const int row_len = P.num_heads * D;
   const int nblk = row_len >> 4;
+  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
   if (b >= batch) {
-    for (int k = threadIdx.x; k < nblk; k += blockDim.x) q::zero_block16(dst, b, k);
-    if (threadIdx.x == 0) dst.gx[b] = 1.f;
+    for (int k = u0 + threadIdx.x; k < u1; k += blockDim.x) q::zero_unit(dst, b, k);
+    if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[b] = 1.f;
+    cl::cluster_wait();
     return;
   }
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
@@ -331,8 +337,8 @@ __global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* 
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int k = threadIdx.x + u * blockDim.x;
-    if (k >= nblk) continue;
+    const int k = u0 + threadIdx.x + u * blockDim.x;
+    if (k >= u1) continue;
     const int h = (k * 16) / D, d0 = (k * 16) % D;
     const int64_t row0 = ((int64_t)b * P.num_heads + h) * P.max_splits;
     float M = -INFINITY;
@@ -366,13 +372,13 @@ __global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* 
       *reinterpret_cast<uint4*>(op + 8) = pack8<TO>(v[u] + 8);
     }
   }
-  const float g = q::row_scale(q::block_max(amax, red));
-  const float g6 = __fmul_rn(g, 6.f);
-  if (threadIdx.x == 0) dst.gx[b] = g;
+  cl::cluster_wait();
+  const q::RowQ rq = q::make_rowq(cl::cluster_allreduce<cl::OpMax>(amax, red, slots), dst.terms);
+  if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[b] = rq.g[0];
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int k = threadIdx.x + u * blockDim.x;
-    if (k < nblk) q::quant_block16(dst, b, k, v[u], g, g6);
+    const int k = u0 + threadIdx.x + u * blockDim.x;
+    if (k < u1) q::quant_unit(dst, b, k, v[u], rq);
   }
 }
 
@@ -427,11 +433,9 @@ extern "C" int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_
                                           int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
                                           void* workspace, size_t workspace_bytes, void* stream) {
   const int row = num_heads * head_dim;
-  if (terms < 1 || terms > 3 || (block_n != 16 && block_n != 32 && block_n != 64 && block_n != 128) ||
-      terms * block_n > 128 || !xq || !sfx || !gx)
-    return ADA_ERR_INVALID_ARG;
   if (row % 256) return ADA_ERR_UNSUPPORTED;
-  if ((uintptr_t)xq & 15) return ADA_ERR_ALIGNMENT;
+  if (!q::dst_ok(terms, block_n, row) || !xq || !gx || (terms == 1 && !sfx)) return ADA_ERR_INVALID_ARG;
+  if (((uintptr_t)xq & 15) || ((uintptr_t)gx & 3)) return ADA_ERR_ALIGNMENT;
   const q::QuantDst qd{xq, sfx, gx, terms, block_n, row};
   return paged_decode_impl(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_tok,
                            kv_stride_head, num_pages, block_tables, bt_stride, max_pages, context_lens, batch,
@@ -498,16 +502,16 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
   ADA_CHECK_LAUNCH();
   if (qd) {
     const int m_pad = (int)cdiv(batch, qd->bn) * qd->bn;
-    const int nblk = num_heads * head_dim / 16;
-    const int maxu = (nblk + 255) / 256;
-    if (maxu > 4) return ADA_ERR_UNSUPPORTED;
-#define ADA_RQ(TO, MU)                                                                                              \
-    (void)ada::launch_k(attn::decode_reduce_quant_kernel<TO, MU>, dim3(m_pad), dim3(256), 0, st, P,                   \
-                        reinterpret_cast<TO*>(out), batch, *qd)
+    const cl::RowSplit sp = cl::row_split(num_heads * head_dim / 16);
+    if (!sp.maxu || sp.maxu > 4 || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
+    const dim3 rg((unsigned)sp.ctas, (unsigned)m_pad), rb((unsigned)sp.threads);
+#define ADA_RQ(TO, MU)                                                                                         \
+    (void)ada::launch_kc(attn::decode_reduce_quant_kernel<TO, MU>, rg, rb, 0, st, sp.ctas, P,                  \
+                         reinterpret_cast<TO*>(out), batch, *qd)
     if (out_dtype == ADA_DT_BF16) {
-      if (maxu == 1) ADA_RQ(__nv_bfloat16, 1); else if (maxu == 2) ADA_RQ(__nv_bfloat16, 2); else ADA_RQ(__nv_bfloat16, 4);
+      if (sp.maxu == 1) ADA_RQ(__nv_bfloat16, 1); else if (sp.maxu == 2) ADA_RQ(__nv_bfloat16, 2); else ADA_RQ(__nv_bfloat16, 4);
     } else {
-      if (maxu == 1) ADA_RQ(__half, 1); else if (maxu == 2) ADA_RQ(__half, 2); else ADA_RQ(__half, 4);
+      if (sp.maxu == 1) ADA_RQ(__half, 1); else if (sp.maxu == 2) ADA_RQ(__half, 2); else ADA_RQ(__half, 4);
     }
 #undef ADA_RQ
     ADA_CHECK_LAUNCH();

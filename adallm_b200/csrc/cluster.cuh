@@ -1,0 +1,117 @@
+// Thread-block-cluster helpers (sm_90+ PTX, used here on sm_100a): a row that is
+// too short to keep one CTA busy for long is split over the CTAs of one cluster,
+// which combine their partial reductions through distributed shared memory.
+//
+// Protocol of a cluster row kernel (every thread of every CTA runs all of it; no
+// thread returns early, so every hardware cluster barrier completes):
+//   cluster_arrive_relaxed()            right after start
+//   ... load the slice, local partial ...
+//   cluster_wait()                      every CTA of the cluster is running: DSMEM is live
+//   v = cluster_allreduce<Op>(v, slots) one per reduction, each with its own slot array
+// A CTA writes the remote shared memory of its peers only between the first wait and
+// its last reduction barrier, so no CTA exits while a peer still writes into it.
+#pragma once
+
+#include "common.cuh"
+
+namespace ada {
+namespace cl {
+
+constexpr int MAX_CLUSTER = 8;
+
+__device__ __forceinline__ uint32_t ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync() {
+  cluster_arrive();
+  cluster_wait();
+}
+
+// Shared-memory address of `p` (a __shared__ object of this CTA) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p)), r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+struct OpMax {
+  __device__ static float apply(float a, float b) { return fmaxf(a, b); }
+  static constexpr float identity = 0.f;  // reductions of magnitudes
+};
+struct OpSum {
+  __device__ static float apply(float a, float b) { return __fadd_rn(a, b); }
+  static constexpr float identity = 0.f;
+};
+
+// CTA-wide reduction (any blockDim.x multiple of 32, <= 1024), warps combined in order.
+template <typename Op>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = Op::apply(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) r = Op::apply(r, red[i]);
+  return r;
+}
+
+// Cluster-wide reduction: CTA partials combined in rank order (deterministic for sums).
+// `slots` is a __shared__ float[MAX_CLUSTER] used by this reduction only.
+template <typename Op>
+__device__ __forceinline__ float cluster_allreduce(float v, float* red, float* slots) {
+  v = block_reduce<Op>(v, red);
+  const uint32_t n = nctarank();
+  if (n == 1) return v;
+  const uint32_t me = ctarank();
+  if (threadIdx.x < n) st_cluster_f32(mapa(&slots[me], threadIdx.x), v);
+  cluster_sync();
+  float r = slots[0];
+  for (uint32_t i = 1; i < n; ++i) r = Op::apply(r, slots[i]);
+  return r;
+}
+
+// How a row of `units` 16-element units is spread over a cluster: `ctas` CTAs of `threads`
+// threads, each thread owning up to `maxu` units of its CTA's contiguous slice.  Depends on
+// the row length only, so every kernel that reduces rows of one length rounds the same way.
+struct RowSplit {
+  int ctas, threads, maxu;
+};
+inline RowSplit row_split(int units) {
+  RowSplit s;
+  s.ctas = units / 32;
+  s.ctas = s.ctas < 1 ? 1 : s.ctas > MAX_CLUSTER ? MAX_CLUSTER : s.ctas;
+  const int per = (units + s.ctas - 1) / s.ctas;
+  s.threads = ((per + 31) / 32) * 32;
+  if (s.threads > 256) s.threads = 256;
+  const int mu = (per + s.threads - 1) / s.threads;
+  s.maxu = mu <= 1 ? 1 : mu <= 2 ? 2 : mu <= 4 ? 4 : mu <= 8 ? 8 : 0;  // 0: row too long
+  return s;
+}
+// Units [u0, u1) of CTA `rank` out of `ctas`.
+__host__ __device__ __forceinline__ int slice_begin(int units, int rank, int ctas) {
+  return (int)(((int64_t)units * rank) / ctas);
+}
+
+}  // namespace cl
+}  // namespace ada

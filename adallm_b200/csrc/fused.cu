@@ -5,16 +5,21 @@
 //     (reference adallm/ops/layernorm.py:16-40, :64-92)
 //   * SiLU(gate) * up / GELU(tanh)(gate) * up -> quantised operand of down_proj
 //     (reference adallm/ops/activation.py:6-26)
+//   * plain quantisation of a bf16/fp16 matrix (the prologue of ada_nvfp4_linear)
 // The bf16 value each kernel quantises is exactly the value the unfused op would
 // have returned (same rounding order), so fused and unfused paths agree bit for bit.
+//
+// Decode rows are short (16 tokens x 4096..21504 values), so each row is spread over
+// a thread-block cluster of up to 8 CTAs (cluster.cuh): grid (ctas, rows), every CTA
+// owns a contiguous slice of the row, and the row reductions (sum of squares, amax)
+// are combined across the cluster through distributed shared memory.
 #include <type_traits>
 
+#include "cluster.cuh"
 #include "quant.cuh"
 
 namespace ada {
 namespace fused {
-
-constexpr int THREADS = 256;
 
 template <typename T>
 __device__ __forceinline__ void load16(const T* p, float* f) {
@@ -31,40 +36,56 @@ __device__ __forceinline__ float round_to(float v) {
   return to_f32(from_f32<T>(v));
 }
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r += red[i];
-  return r;
+// Unit `u` of this thread (u < MAXU) in the CTA's slice [u0, u1), or -1.
+__device__ __forceinline__ int my_unit(int u, int u0, int u1) {
+  const int b = u0 + (int)threadIdx.x + u * (int)blockDim.x;
+  return b < u1 ? b : -1;
 }
 
-// One CTA per (padded) token row; thread i owns 16-element blocks i, i + 256, ...
+// Quantise the slice held in v once the row amax is known; rank 0 records the row scale.
+template <int MAXU>
+__device__ __forceinline__ void quant_slice(const q::QuantDst& dst, int m, float (&v)[MAXU][16], int u0, int u1,
+                                            float amax) {
+  const q::RowQ rq = q::make_rowq(amax, dst.terms);
+  if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[m] = rq.g[0];
+#pragma unroll
+  for (int u = 0; u < MAXU; ++u) {
+    const int b = my_unit(u, u0, u1);
+    if (b >= 0) q::quant_unit(dst, m, b, v[u], rq);
+  }
+}
+// Padding token of the last token tile: zero codes, unit scale.
+__device__ __forceinline__ void zero_slice(const q::QuantDst& dst, int m, int u0, int u1) {
+  for (int b = u0 + (int)threadIdx.x; b < u1; b += blockDim.x) q::zero_unit(dst, m, b);
+  if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[m] = 1.f;
+}
+
+// grid (ctas, m_pad), cluster (ctas, 1, 1).  dst.xq == null: plain RMSNorm (ada_rmsnorm).
 template <typename T, int MAXU>
-__global__ void __launch_bounds__(THREADS) rmsnorm_quant_kernel(const T* __restrict__ x, int64_t ldx, const T* res,
-                                                                int64_t ldr, T* res_out, int64_t ldro,
-                                                                const T* __restrict__ w, T* y, int64_t ldy, int rows,
-                                                                int hidden, float eps, int gemma, q::QuantDst dst) {
+__global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const T* __restrict__ x, int64_t ldx, const T* res,
+                                                            int64_t ldr, T* res_out, int64_t ldro,
+                                                            const T* __restrict__ w, T* y, int64_t ldy, int rows,
+                                                            int hidden, float eps, int gemma, q::QuantDst dst) {
+  cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[THREADS / 32];
-  const int m = blockIdx.x;
+  __shared__ float red[8];
+  __shared__ float slots[2][cl::MAX_CLUSTER];
+  const int m = blockIdx.y;
   const int nblk = hidden >> 4;
+  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
+  const bool quant = dst.xq != nullptr;
   if (m >= rows) {
-    for (int b = threadIdx.x; b < nblk; b += THREADS) q::zero_block16(dst, m, b);
-    if (threadIdx.x == 0) dst.gx[m] = 1.f;
+    if (quant) zero_slice(dst, m, u0, u1);
+    cl::cluster_wait();
     return;
   }
   float v[MAXU][16];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = threadIdx.x + u * THREADS;
-    if (b < nblk) {
+    const int b = my_unit(u, u0, u1);
+    if (b >= 0) {
       load16<T>(x + (int64_t)m * ldx + b * 16, v[u]);
       if (res) {
         float r[16];
@@ -80,12 +101,13 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_quant_kernel(const T* __restr
       for (int i = 0; i < 16; ++i) ss = fmaf(v[u][i], v[u][i], ss);
     }
   }
-  const float rs = rsqrtf(block_sum(ss, red) / (float)hidden + eps);
+  cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
+  const float rs = rsqrtf(cl::cluster_allreduce<cl::OpSum>(ss, red, slots[0]) / (float)hidden + eps);
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = threadIdx.x + u * THREADS;
-    if (b < nblk) {
+    const int b = my_unit(u, u0, u1);
+    if (b >= 0) {
       float wf[16];
       load16<T>(w + b * 16, wf);
 #pragma unroll
@@ -98,14 +120,8 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_quant_kernel(const T* __restr
       if (y) store16<T>(y + (int64_t)m * ldy + b * 16, v[u]);
     }
   }
-  const float g = q::row_scale(q::block_max(amax, red));
-  const float g6 = __fmul_rn(g, 6.f);
-  if (threadIdx.x == 0) dst.gx[m] = g;
-#pragma unroll
-  for (int u = 0; u < MAXU; ++u) {
-    const int b = threadIdx.x + u * THREADS;
-    if (b < nblk) q::quant_block16(dst, m, b, v[u], g, g6);
-  }
+  if (!quant) return;
+  quant_slice<MAXU>(dst, m, v, u0, u1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots[1]));
 }
 
 __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.f, expf(-x))); }
@@ -115,26 +131,29 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   return 0.5f * x * (1.f + tanhf(inner));
 }
 
+// grid (ctas, m_pad), cluster (ctas, 1, 1).
 template <typename T, int MAXU>
-__global__ void __launch_bounds__(THREADS) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y,
-                                                                  int64_t ldy, int rows, int inter, int act,
-                                                                  q::QuantDst dst) {
+__global__ void __launch_bounds__(256) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y, int64_t ldy,
+                                                              int rows, int inter, int act, q::QuantDst dst) {
+  cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[THREADS / 32];
-  const int m = blockIdx.x;
+  __shared__ float red[8];
+  __shared__ float slots[cl::MAX_CLUSTER];
+  const int m = blockIdx.y;
   const int nblk = inter >> 4;
+  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
   if (m >= rows) {
-    for (int b = threadIdx.x; b < nblk; b += THREADS) q::zero_block16(dst, m, b);
-    if (threadIdx.x == 0) dst.gx[m] = 1.f;
+    zero_slice(dst, m, u0, u1);
+    cl::cluster_wait();
     return;
   }
   float v[MAXU][16];
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = threadIdx.x + u * THREADS;
-    if (b < nblk) {
+    const int b = my_unit(u, u0, u1);
+    if (b >= 0) {
       float gt[16], up[16];
       load16<T>(x + (int64_t)m * ldx + b * 16, gt);
       load16<T>(x + (int64_t)m * ldx + inter + b * 16, up);
@@ -147,14 +166,107 @@ __global__ void __launch_bounds__(THREADS) gated_act_quant_kernel(const T* __res
       if (y) store16<T>(y + (int64_t)m * ldy + b * 16, v[u]);
     }
   }
-  const float g = q::row_scale(q::block_max(amax, red));
-  const float g6 = __fmul_rn(g, 6.f);
-  if (threadIdx.x == 0) dst.gx[m] = g;
+  cl::cluster_wait();
+  quant_slice<MAXU>(dst, m, v, u0, u1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
+}
+
+// grid (ctas, m_pad), cluster (ctas, 1, 1).
+template <typename T, int MAXU>
+__global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x, int64_t ldx, int rows, int k,
+                                                        q::QuantDst dst) {
+  cl::cluster_arrive_relaxed();
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[8];
+  __shared__ float slots[cl::MAX_CLUSTER];
+  const int m = blockIdx.y;
+  const int nblk = k >> 4;
+  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
+  if (m >= rows) {
+    zero_slice(dst, m, u0, u1);
+    cl::cluster_wait();
+    return;
+  }
+  float v[MAXU][16];
+  float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = threadIdx.x + u * THREADS;
-    if (b < nblk) q::quant_block16(dst, m, b, v[u], g, g6);
+    const int b = my_unit(u, u0, u1);
+    if (b >= 0) {
+      load16<T>(x + (int64_t)m * ldx + b * 16, v[u]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
+    }
   }
+  cl::cluster_wait();
+  quant_slice<MAXU>(dst, m, v, u0, u1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
+}
+
+static inline bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+bool quant_args_ok(const q::QuantDst& d) {
+  if (!q::dst_ok(d.terms, d.bn, d.k)) return false;
+  if (!d.xq || !d.gx || (d.terms == 1 && !d.sfx)) return false;
+  return a16(d.xq) && ((uintptr_t)d.gx & 3) == 0;
+}
+
+// Row kernels dispatch on the dtype and on the per-thread unit count of the row split.
+#define ADA_ROW_DISPATCH(KERNEL, T_, SPLIT, ...)                                                       \
+  do {                                                                                                 \
+    const dim3 blk_((unsigned)(SPLIT).threads);                                                        \
+    switch ((SPLIT).maxu) {                                                                            \
+      case 1: err_ = launch_kc(KERNEL<T_, 1>, grid_, blk_, 0, st, (SPLIT).ctas, __VA_ARGS__); break;   \
+      case 2: err_ = launch_kc(KERNEL<T_, 2>, grid_, blk_, 0, st, (SPLIT).ctas, __VA_ARGS__); break;   \
+      case 4: err_ = launch_kc(KERNEL<T_, 4>, grid_, blk_, 0, st, (SPLIT).ctas, __VA_ARGS__); break;   \
+      default: err_ = launch_kc(KERNEL<T_, 8>, grid_, blk_, 0, st, (SPLIT).ctas, __VA_ARGS__); break;  \
+    }                                                                                                  \
+  } while (0)
+
+// RMSNorm (quantised or not) of `launch_rows` rows (rows beyond `rows` are padding).
+int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro, const void* w,
+                   void* y, int64_t ldy, int64_t rows, int64_t launch_rows, int hidden, float eps, int gemma,
+                   int dtype, const q::QuantDst& dst, cudaStream_t st) {
+  if (hidden % 16) return ADA_ERR_UNSUPPORTED;
+  const cl::RowSplit sp = cl::row_split(hidden / 16);
+  if (!sp.maxu || launch_rows > 65535) return ADA_ERR_UNSUPPORTED;
+  const dim3 grid_((unsigned)sp.ctas, (unsigned)launch_rows);
+  cudaError_t err_;
+  if (dtype == ADA_DT_BF16) {
+    using TT = __nv_bfloat16;
+    ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
+                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst);
+  } else {
+    using TT = __half;
+    ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
+                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst);
+  }
+  return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+// Plain RMSNorm through the same kernel (ada_rmsnorm for hidden % 16 == 0), so fused and
+// unfused paths round identically.
+int launch_rmsnorm16(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro,
+                     const void* w, void* y, int64_t ldy, int64_t rows, int hidden, float eps, int gemma, int dtype,
+                     cudaStream_t st) {
+  const q::QuantDst none{nullptr, nullptr, nullptr, 1, 16, hidden};
+  return launch_rmsnorm(x, ldx, res, ldr, ro, ldro, w, y, ldy, rows, rows, hidden, eps, gemma, dtype, none, st);
+}
+
+// Quantise x [m, k] into the GEMM operand (prologue of ada_nvfp4_linear).
+int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
+                     cudaStream_t st) {
+  const cl::RowSplit sp = cl::row_split(dst.k / 16);
+  if (!sp.maxu || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
+  const dim3 grid_((unsigned)sp.ctas, (unsigned)m_pad);
+  cudaError_t err_;
+  if (x_dtype == ADA_DT_BF16) {
+    using TT = __nv_bfloat16;
+    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst);
+  } else {
+    using TT = __half;
+    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst);
+  }
+  return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
 
 }  // namespace fused
@@ -162,46 +274,21 @@ __global__ void __launch_bounds__(THREADS) gated_act_quant_kernel(const T* __res
 
 using namespace ada;
 
-static bool quant_args_ok(int terms, int block_n, int k, const void* xq, const void* sfx, const void* gx) {
-  if (terms < 1 || terms > 3) return false;
-  if (block_n != 16 && block_n != 32 && block_n != 64 && block_n != 128) return false;
-  if (terms * block_n > 128 || k % 256) return false;
-  return xq && sfx && gx && (((uintptr_t)xq & 15) == 0);
-}
-
 extern "C" int ada_rmsnorm_quant(const void* x, int64_t ldx, const void* residual, int64_t ld_res, void* residual_out,
                                  int64_t ld_res_out, const void* weight, void* y, int64_t ldy, int64_t rows,
                                  int32_t hidden, float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
                                  uint8_t* sfx, float* gx, void* stream) {
   if (rows <= 0 || hidden <= 0 || !x || !weight || (residual && !residual_out)) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
-  if (!quant_args_ok(terms, block_n, hidden, xq, sfx, gx)) return ADA_ERR_INVALID_ARG;
-  const int nblk = hidden / 16;
-  const int maxu = (nblk + fused::THREADS - 1) / fused::THREADS;
-  if (maxu > 4) return ADA_ERR_UNSUPPORTED;
-  auto a16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  if (!a16(x) || !a16(weight) || (ldx & 7) || (y && (!a16(y) || (ldy & 7)))) return ADA_ERR_ALIGNMENT;
-  if (residual && (!a16(residual) || !a16(residual_out) || (ld_res & 7) || (ld_res_out & 7))) return ADA_ERR_ALIGNMENT;
-  const int64_t m_pad = cdiv(rows, block_n) * block_n;
   const q::QuantDst dst{xq, sfx, gx, terms, block_n, hidden};
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define ADA_RQ(T, MU)                                                                                               \
-  (void)launch_k(fused::rmsnorm_quant_kernel<T, MU>, dim3((unsigned)m_pad), dim3(fused::THREADS), 0, st,            \
-                 (const T*)x, ldx, (const T*)residual, ld_res, (T*)residual_out, ld_res_out, (const T*)weight, (T*)y, \
-                 ldy, (int)rows, (int)hidden, eps, gemma, dst)
-#define ADA_RQT(T)                    \
-  if (maxu == 1) ADA_RQ(T, 1);        \
-  else if (maxu == 2) ADA_RQ(T, 2);   \
-  else ADA_RQ(T, 4);
-  if (dtype == ADA_DT_BF16) {
-    ADA_RQT(__nv_bfloat16)
-  } else {
-    ADA_RQT(__half)
-  }
-#undef ADA_RQT
-#undef ADA_RQ
-  ADA_CHECK_LAUNCH();
-  return ADA_OK;
+  if (!fused::quant_args_ok(dst)) return ADA_ERR_INVALID_ARG;
+  if (!fused::a16(x) || !fused::a16(weight) || (ldx & 7) || (y && (!fused::a16(y) || (ldy & 7))))
+    return ADA_ERR_ALIGNMENT;
+  if (residual && (!fused::a16(residual) || !fused::a16(residual_out) || (ld_res & 7) || (ld_res_out & 7)))
+    return ADA_ERR_ALIGNMENT;
+  const int64_t m_pad = cdiv(rows, block_n) * block_n;
+  return fused::launch_rmsnorm(x, ldx, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows, m_pad,
+                               hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter,
@@ -209,29 +296,23 @@ extern "C" int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t 
                                    void* stream) {
   if (rows <= 0 || inter <= 0 || !x || (act != 0 && act != 1)) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
-  if (!quant_args_ok(terms, block_n, inter, xq, sfx, gx)) return ADA_ERR_INVALID_ARG;
-  const int nblk = inter / 16;
-  const int maxu = (nblk + fused::THREADS - 1) / fused::THREADS;
-  if (maxu > 8) return ADA_ERR_UNSUPPORTED;
-  if (((uintptr_t)x & 15) || (ldx & 7) || (y && (((uintptr_t)y & 15) || (ldy & 7)))) return ADA_ERR_ALIGNMENT;
-  const int64_t m_pad = cdiv(rows, block_n) * block_n;
   const q::QuantDst dst{xq, sfx, gx, terms, block_n, inter};
+  if (!fused::quant_args_ok(dst)) return ADA_ERR_INVALID_ARG;
+  if (!fused::a16(x) || (ldx & 7) || (y && (!fused::a16(y) || (ldy & 7)))) return ADA_ERR_ALIGNMENT;
+  const cl::RowSplit sp = cl::row_split(inter / 16);
+  const int64_t m_pad = cdiv(rows, block_n) * block_n;
+  if (!sp.maxu || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define ADA_GQ(T, MU)                                                                                     \
-  (void)launch_k(fused::gated_act_quant_kernel<T, MU>, dim3((unsigned)m_pad), dim3(fused::THREADS), 0, st, \
-                 (const T*)x, ldx, (T*)y, ldy, (int)rows, (int)inter, act, dst)
-#define ADA_GQT(T)                    \
-  if (maxu == 1) ADA_GQ(T, 1);        \
-  else if (maxu == 2) ADA_GQ(T, 2);   \
-  else if (maxu <= 4) ADA_GQ(T, 4);   \
-  else ADA_GQ(T, 8);
+  const dim3 grid_((unsigned)sp.ctas, (unsigned)m_pad);
+  cudaError_t err_;
   if (dtype == ADA_DT_BF16) {
-    ADA_GQT(__nv_bfloat16)
+    using TT = __nv_bfloat16;
+    ADA_ROW_DISPATCH(fused::gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows,
+                     (int)inter, act, dst);
   } else {
-    ADA_GQT(__half)
+    using TT = __half;
+    ADA_ROW_DISPATCH(fused::gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows,
+                     (int)inter, act, dst);
   }
-#undef ADA_GQT
-#undef ADA_GQ
-  ADA_CHECK_LAUNCH();
-  return ADA_OK;
+  return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }

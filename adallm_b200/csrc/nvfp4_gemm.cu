@@ -7,22 +7,25 @@
 //   * W [N, K/2] e2m1 bytes (even K in the low nibble) is TMA-loaded as-is into
 //     128-byte-swizzled shared memory; its e4m3 per-16 scales are re-laid out
 //     once at load ("prepack") into the block-scaled MMA scale-factor layout.
-//   * The bf16 activation row is quantised by a prologue kernel into T NVFP4
-//     terms that share one fp32 per-row scale: term t quantises the residual
-//     left by terms < t (T = 3 keeps the result within ~1e-3 of the fp32
-//     dequantise-then-matmul oracle; T = 1 is plain W4A4).
-//   * tcgen05.mma.kind::mxf4nvf4.block_scale.block16 with M = 128 weight rows
-//     ("swap AB": tokens are the MMA N dimension), fp32 accumulation in TMEM;
-//     the T terms are T MMAs into the same accumulator.
-//   * Split-K over CTAs with a deterministic reduction: every split writes its
-//     scaled fp32 partial, the last CTA of a tile sums the splits in order,
-//     adds the bias and writes bf16/fp16.
+//   * The bf16 activation row is quantised by the producing kernel (quant.cuh) into
+//     `terms` e2m1 terms: terms == 1 is NVFP4 with per-16 block scales (W4A4); terms >= 2
+//     are row-scaled terms (unit block scales, one fp32 scale per row and term) whose sum
+//     is within ~1e-3 (4 terms) of the bf16 activation.
+//   * tcgen05.mma.kind::mxf4nvf4.block_scale.block16 with M = 128 weight rows ("swap AB":
+//     tokens are the MMA N dimension); the terms are stacked along N (N = terms x tokens),
+//     so one MMA per 64-wide K block covers every term.  fp32 accumulation in TMEM.  For
+//     row-scaled terms the activation block scales are the constant 1.0, copied to TMEM once.
+//   * The epilogue scales each term's accumulator column by its row scale, sums the terms,
+//     and writes bf16/fp16.  Split-K: the CTAs sharing one output tile form a thread-block
+//     cluster; each sends its scaled fp32 partial rows to the CTA owning them through
+//     distributed shared memory, and the owner sums the partials in CTA-rank order
+//     (deterministic, no global partials, no atomics).
 //
-// Warp roles (128 threads): warp 0 lane 0 issues TMA / bulk copies, warp 1
-// lane 0 issues tcgen05.cp (scales -> TMEM) and MMAs, warp 1 owns the TMEM
-// allocation, and all four warps run the epilogue (warp w reads TMEM lanes
-// 32w..32w+31).  Every mbarrier wait is bounded (2 s); a timeout sets an error
-// bit in the workspace and the CTA drains and exits.
+// Warp roles (192 threads): warp 0 lane 0 issues TMA / bulk copies, warp 1 owns the TMEM
+// allocation and lane 0 issues tcgen05.cp (scales -> TMEM) and the MMAs, warps 2..5 run the
+// epilogue (warp w reads TMEM lanes 32*(w%4)..+31).  Every mbarrier wait is bounded (2 s);
+// a timeout sets an error bit in the workspace and the CTA drains and exits.
+#include "cluster.cuh"
 #include "quant.cuh"
 #include "sm100.cuh"
 
@@ -36,36 +39,38 @@ constexpr int KT = 256;            // K elements per pipeline stage (4 MMA k-blo
 constexpr int KT_BYTES = KT / 2;   // 128 bytes of packed e2m1 per row and stage
 constexpr int SF_BLOCK = 512;      // scale bytes per 128 rows x 64 K
 constexpr int MAX_STAGES = 8;
+constexpr int MAX_KS = cl::MAX_CLUSTER;
+constexpr uint32_t UNIT_SCALE4 = 0x38383838u;  // four ue4m3 1.0
 
 struct GemmParams {
   const uint8_t* sfw;  // [N/128][K/64][512]
-  const uint8_t* sfx;  // [T][m_tiles][K/64][512]
-  const float* gx;     // [m_pad] per-row activation scale
+  const uint8_t* sfx;  // [m_tiles][K/64][512] (terms == 1)
+  const float* gx;     // [m_pad] row scale (g or g_0)
   const float* gw;     // weight_scale_2 (device scalar)
   const void* bias;    // [N] (out dtype) or null
   void* y;             // [M, ldy] out dtype
-  float* partial;      // [ksplit][m_pad][N] fp32 (ksplit > 1)
-  int* counters;       // [n_tiles * m_tiles]
   unsigned int* err;
-  int M, N, K, ldy, m_pad, n_tiles, m_tiles, ksplit, stages, tmem_cols, out_dtype;
+  int M, N, K, ldy, n_tiles, nkt, stages, tmem_cols, out_dtype, ks, rows_max;
 };
 
-// The T activation terms of a token tile are stacked along the MMA N dimension:
-// B operand rows [t*BN, (t+1)*BN) hold term t, so one MMA per 64-wide K block covers
-// every term (NB = T*BN <= 128 rows, one scale-factor block).
 template <int BN, int T>
 struct Cfg {
   static constexpr int NB = BN * T;
   static_assert(NB % 16 == 0 && NB <= 128, "stacked terms must fit one 128-row scale block");
+  static constexpr bool BLOCK_SF = T == 1;                // activation block scales per stage
   static constexpr uint32_t A_BYTES = BM * KT_BYTES;      // 16 KiB
   static constexpr uint32_t B_BYTES = NB * KT_BYTES;      // all terms
   static constexpr uint32_t SFA_BYTES = 4 * SF_BLOCK;     // 2 KiB
-  static constexpr uint32_t SFB_BYTES = 4 * SF_BLOCK;     // 2 KiB
-  static constexpr uint32_t STAGE = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-  static constexpr uint32_t SF_COLS = 32;                 // TMEM columns of scales per stage
-  static constexpr uint32_t CTRL = 256;
-  static size_t smem_bytes(int stages) { return 1024 + (size_t)stages * STAGE + CTRL; }
-  static uint32_t tmem_need(int stages) { return NB + stages * SF_COLS; }
+  static constexpr uint32_t SFB_BYTES = BLOCK_SF ? 4 * SF_BLOCK : 0;
+  static constexpr uint32_t STAGE = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // multiple of 1024
+  static constexpr uint32_t SF_COLS = BLOCK_SF ? 32 : 16;  // TMEM scale columns per stage
+  static constexpr uint32_t CONST_SF = BLOCK_SF ? 0 : SF_BLOCK;
+  static constexpr uint32_t CTRL = 1024;
+  __host__ __device__ static size_t recv_bytes(int ks, int rows_max) { return ks > 1 ? (size_t)ks * rows_max * BN * 4 : 0; }
+  static size_t smem_bytes(int stages, size_t recv) {
+    return 1024 + (size_t)stages * STAGE + CONST_SF + recv + CTRL;
+  }
+  static uint32_t tmem_need(int stages) { return NB + stages * SF_COLS + (BLOCK_SF ? 0 : 4); }
 };
 
 __device__ __forceinline__ void store_out(void* y, int dtype, int64_t idx, float v) {
@@ -79,34 +84,42 @@ __device__ __forceinline__ float load_bias(const void* b, int dtype, int n) {
   return dtype == ADA_DT_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(b)[n])
                               : __half2float(reinterpret_cast<const __half*>(b)[n]);
 }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
+// Split-K ownership of the 128 rows of a tile: row r belongs to CTA (r * ks) / 128.
+__host__ __device__ __forceinline__ int owner_begin(int o, int ks) { return (o * BM + ks - 1) / ks; }
+
+// grid (ks, tiles), cluster (ks, 1, 1) when ks > 1.  CTA `rank` of a cluster accumulates
+// K steps [rank*nkt/ks, (rank+1)*nkt/ks) of tile blockIdx.y.
 template <int BN, int T>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(192, 2)
     gemm_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
-  // dependency wait placed inside (weights are prefetched before it)
-
   using C = Cfg<BN, T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int stages = p.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)stages * C::STAGE);
+  const int stages = p.stages, ks = p.ks;
+  uint8_t* const_sf = smem + (size_t)stages * C::STAGE;
+  float* recv = reinterpret_cast<float*>(const_sf + C::CONST_SF);  // [ks][rows_max][BN]
+  uint8_t* ctrl = reinterpret_cast<uint8_t*>(recv) + C::recv_bytes(ks, p.rows_max);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
   uint64_t* empty = full + MAX_STAGES;
   uint64_t* accf = empty + MAX_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  int* last_flag = abort_flag + 1;
+  float* gsc = reinterpret_cast<float*>(ctrl + 256);  // [T][BN] gw * term scale per token
   volatile int* abort_v = abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
+  const int rank = blockIdx.x, tile = blockIdx.y;
   const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
-  const int split = blockIdx.y;
+  const int kt0 = (int)((int64_t)rank * p.nkt / ks), kt1 = (int)((int64_t)(rank + 1) * p.nkt / ks);
+  const int nunits = kt1 - kt0;
   const int kb64 = p.K / 64;
-  const int nkt = p.K / KT;
-  const int kt0 = (int)((int64_t)split * nkt / p.ksplit);
-  const int kt1 = (int)((int64_t)(split + 1) * nkt / p.ksplit);
-  const int nk = kt1 - kt0;
 
+  if (ks > 1) cl::cluster_arrive_relaxed();
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -114,8 +127,11 @@ __global__ void __launch_bounds__(128, 1)
     }
     mbar_init(accf, 1);
     *abort_flag = 0;
-    *last_flag = 0;
     fence_mbar_init();
+  }
+  if (!C::BLOCK_SF && threadIdx.x < C::CONST_SF / 4) {
+    reinterpret_cast<uint32_t*>(const_sf)[threadIdx.x] = UNIT_SCALE4;
+    fence_proxy_async_smem();  // visible to tcgen05.cp
   }
   if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
   if (warp == 0 && lane == 0) {
@@ -129,24 +145,23 @@ __global__ void __launch_bounds__(128, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: TMA tiles + bulk scale copies ----------------
-      // The weights and their scales never depend on the previous kernel: the first
-      // `stages` weight tiles are requested before the programmatic-launch dependency
-      // wait, so they stream in while the producer of the activations finishes.
-      const int pre = nk < stages ? nk : stages;
+      // ---------------- producer ----------------
+      // The weights never depend on the previous kernel: the first `stages` weight tiles
+      // are requested before the programmatic-launch dependency wait.
+      const int pre = nunits < stages ? nunits : stages;
       for (int i = 0; i < pre; ++i) {
-        uint8_t* st = smem + (size_t)i * C::STAGE;
         const int kt = kt0 + i;
+        uint8_t* st = smem + (size_t)i * C::STAGE;
         mbar_expect_tx(&full[i], C::A_BYTES + C::SFA_BYTES);
         tma_load_2d(st, &tmw, &full[i], kt * KT_BYTES, n_tile * BM);
         bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
                   C::SFA_BYTES, &full[i]);
       }
       pdl_wait();
-      for (int i = 0; i < nk; ++i) {
+      for (int i = 0; i < nunits; ++i) {
         const int s = i % stages;
-        uint8_t* st = smem + (size_t)s * C::STAGE;
         const int kt = kt0 + i;
+        uint8_t* st = smem + (size_t)s * C::STAGE;
         if (i >= stages) {
           if (!mbar_wait_bounded(&empty[s], ((i / stages) & 1) ^ 1, abort_v, p.err, 1u)) break;
           mbar_expect_tx(&full[s], C::A_BYTES + C::SFA_BYTES);
@@ -156,8 +171,9 @@ __global__ void __launch_bounds__(128, 1)
         }
         mbar_arrive_expect_tx(&full[s], C::B_BYTES + C::SFB_BYTES);
         tma_load_2d(st + C::A_BYTES, &tmx, &full[s], kt * KT_BYTES, m_tile * C::NB);
-        bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
-                  p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES, &full[s]);
+        if (C::BLOCK_SF)
+          bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
+                    p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES, &full[s]);
       }
     }
     __syncwarp();
@@ -165,7 +181,10 @@ __global__ void __launch_bounds__(128, 1)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_mxf4nvf4(C::NB);
-      for (int i = 0; i < nk; ++i) {
+      const uint32_t sf_base = tmem + C::NB;
+      const uint32_t sfb_unit = sf_base + stages * C::SF_COLS;  // constant 1.0 activation scales
+      if (!C::BLOCK_SF) tmem_cp_32x128b_x4(sfb_unit, desc_sf(smem_u32(const_sf)));
+      for (int i = 0; i < nunits; ++i) {
         const int s = i % stages;
         if (!mbar_wait_bounded(&full[s], (i / stages) & 1, abort_v, p.err, 2u)) break;
         tc_fence_after();
@@ -173,131 +192,87 @@ __global__ void __launch_bounds__(128, 1)
         const uint32_t a_addr = smem_u32(st);
         const uint32_t b_addr = a_addr + C::A_BYTES;
         const uint32_t sfa_addr = b_addr + C::B_BYTES;
-        const uint32_t sfb_addr = sfa_addr + C::SFA_BYTES;
-        const uint32_t sf_col = tmem + C::NB + s * C::SF_COLS;
+        const uint32_t sf_col = sf_base + s * C::SF_COLS;
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb) {
           tmem_cp_32x128b_x4(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
-          tmem_cp_32x128b_x4(sf_col + 16 + 4 * kb, desc_sf(sfb_addr + kb * SF_BLOCK));
+          if (C::BLOCK_SF) tmem_cp_32x128b_x4(sf_col + 16 + 4 * kb, desc_sf(sfa_addr + C::SFA_BYTES + kb * SF_BLOCK));
         }
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
           mma_mxf4nvf4(tmem, desc_kmajor_sw128(a_addr + kb * 32), desc_kmajor_sw128(b_addr + kb * 32), idesc,
-                       (i | kb) != 0, sf_col + 4 * kb, sf_col + 16 + 4 * kb);
+                       (i | kb) != 0, sf_col + 4 * kb, C::BLOCK_SF ? sf_col + 16 + 4 * kb : sfb_unit);
         tc_commit(&empty[s]);  // stage reusable once these MMAs have read it
       }
-      tc_commit(accf);  // accumulator complete (also issued after an abort, to drain)
+      tc_commit(accf);  // accumulator complete (also after an abort: drains issued MMAs)
     }
     __syncwarp();
-  }
-
-  // ---------------- epilogue: all 4 warps ----------------
-  pdl_wait();     // activations / scales / workspace of earlier kernels are visible from here on
-  pdl_trigger();  // the next kernel may get resident while this one drains
-  const bool ok = mbar_wait_bounded(accf, 0, abort_v, p.err, 4u) && !*abort_v;
-  tc_fence_after();
-  __syncwarp();
-  const int n = n_tile * BM + warp * 32 + lane;  // accumulator lane -> output column
-  const float gw = __ldg(p.gw);
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-  // accumulator column t*BN + j holds term t of token m_tile*BN + j: sum the terms in order
-  float out[BN];
-#pragma unroll
-  for (int j = 0; j < BN; ++j) out[j] = 0.f;
-#pragma unroll
-  for (int c = 0; c < C::NB; c += 16) {
-    float v[16];
-    tmem_ld16(lane_addr + c, v);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) out[(c % BN) + i] += v[i];
-  }
-  if (p.ksplit == 1) {
-    if (ok) {
-      const float b = load_bias(p.bias, p.out_dtype, n);
-#pragma unroll
-      for (int j = 0; j < BN; ++j) {
-        const int m = m_tile * BN + j;
-        if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, out[j] * (gw * __ldg(p.gx + m)) + b);
-      }
-    }
   } else {
-    float* part = p.partial + (size_t)split * p.m_pad * p.N;
-    if (ok) {
+    // ---------------- epilogue (warps 2..5: TMEM lane quarter = warp % 4) ----------------
+    pdl_wait();     // row scales written by the producing kernel are visible from here on
+    pdl_trigger();  // let the next kernel get resident while this one streams
+    const int q = warp & 3;
+    const int et = threadIdx.x - 64;  // 0..127 within the epilogue group
+    if (et < BN) {
+      const float gw = __ldg(p.gw);
+      float g = __ldg(p.gx + m_tile * BN + et);
 #pragma unroll
-      for (int j = 0; j < BN; ++j) {
-        const int m = m_tile * BN + j;
-        part[(size_t)m * p.N + n] = out[j] * (gw * __ldg(p.gx + m));
+      for (int t = 0; t < T; ++t) {
+        gsc[t * BN + et] = __fmul_rn(gw, g);
+        g = q::next_term_scale(g);
       }
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0 && !*abort_v) *last_flag = (atomicAdd(&p.counters[tile], 1) == p.ksplit - 1);
-    __syncthreads();
-    if (*last_flag) {
-      __threadfence();
-      const float b = load_bias(p.bias, p.out_dtype, n);
-      // splits summed in order (deterministic); each pass issues 16 independent L2 loads
+    epi_bar();
+    const bool ok = mbar_wait_bounded(accf, 0, abort_v, p.err, 4u) && !*abort_v;
+    tc_fence_after();
+    __syncwarp();
+    float out[BN];
 #pragma unroll
-      for (int j0 = 0; j0 < BN; j0 += 16) {
-        float acc[16];
+    for (int j = 0; j < BN; ++j) out[j] = 0.f;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-        const float* col = p.partial + (size_t)(m_tile * BN + j0) * p.N + n;
-        for (int s = 0; s < p.ksplit; ++s) {
-          const float* ps = col + (size_t)s * p.m_pad * p.N;
+    for (int c = 0; c < C::NB; c += 16) {
+      float v[16];
+      tmem_ld16(lane_addr + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] += __ldcg(ps + (size_t)j * p.N);
-        }
+      for (int k = 0; k < 16; ++k) out[(c % BN) + k] = fmaf(v[k], gsc[c + k], out[(c % BN) + k]);  // terms in order
+    }
+    const int r = q * 32 + lane;
+    if (ks == 1) {
+      if (ok) {
+        const int n = n_tile * BM + r;
+        const float b = load_bias(p.bias, p.out_dtype, n);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m_tile * BN + j0 + j;
-          if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, acc[j] + b);
+        for (int j = 0; j < BN; ++j) {
+          const int m = m_tile * BN + j;
+          if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, out[j] + b);
         }
       }
-      if (threadIdx.x == 0) p.counters[tile] = 0;  // leave the workspace ready for the next call
+    } else {
+      const int owner = (r * ks) / BM;
+      const int rl = r - owner_begin(owner, ks);
+      cl::cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
+      const uint32_t dst = cl::mapa(recv + ((size_t)rank * p.rows_max + rl) * BN, (uint32_t)owner);
+#pragma unroll
+      for (int j = 0; j < BN; j += 4) cl::st_cluster_v4(dst + j * 4, out[j], out[j + 1], out[j + 2], out[j + 3]);
+      cl::cluster_sync();  // all partial rows delivered
+      const int r0 = owner_begin(rank, ks), rows = owner_begin(rank + 1, ks) - r0;
+      for (int e = et; e < rows * BN; e += 128) {
+        const int rr = e % rows, j = e / rows;
+        float acc = 0.f;
+        for (int src = 0; src < ks; ++src) acc += recv[((size_t)src * p.rows_max + rr) * BN + j];  // rank order
+        const int n = n_tile * BM + r0 + rr, m = m_tile * BN + j;
+        if (ok && m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, acc + load_bias(p.bias, p.out_dtype, n));
+      }
     }
+  }
+  if (ks > 1 && warp < 2) {  // the producer and MMA warps take part in both cluster barriers
+    cl::cluster_wait();
+    cl::cluster_sync();
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, p.tmem_cols);
-}
-
-// ---------------------------------------------------------------------------
-// Activation quantiser (layout and arithmetic: quant.cuh).  One CTA per (padded) row.
-template <typename TI>
-__global__ void __launch_bounds__(256) act_quant_kernel(const TI* __restrict__ x, int64_t ldx, int M, int K, int terms,
-                                                        int bn, int m_tiles, int m_pad, uint8_t* __restrict__ xq,
-                                                        uint8_t* __restrict__ sfx, float* __restrict__ gx) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float red[8];
-  const int m = blockIdx.x;
-  const int nblk = K >> 4;
-  const q::QuantDst dst{xq, sfx, gx, terms, bn, K};
-  if (m >= M) {
-    for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x) q::zero_block16(dst, m, blk);
-    if (threadIdx.x == 0) gx[m] = 1.f;
-    return;
-  }
-  const TI* xr = x + (int64_t)m * ldx;
-  float amax = 0.f;
-  for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x) {
-    float f[16];
-    unpack8<TI>(*reinterpret_cast<const uint4*>(xr + blk * 16), f);
-    unpack8<TI>(*reinterpret_cast<const uint4*>(xr + blk * 16 + 8), f + 8);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
-  }
-  amax = q::block_max(amax, red);
-  const float g = q::row_scale(amax);
-  const float g6 = __fmul_rn(g, 6.f);
-  if (threadIdx.x == 0) gx[m] = g;
-  for (int blk = threadIdx.x; blk < nblk; blk += blockDim.x) {
-    float r[16];
-    unpack8<TI>(*reinterpret_cast<const uint4*>(xr + blk * 16), r);
-    unpack8<TI>(*reinterpret_cast<const uint4*>(xr + blk * 16 + 8), r + 8);
-    q::quant_block16(dst, m, blk, r, g, g6);
-  }
 }
 
 // Scale prepack: [N, K/16] (fp16 holding e4m3 values, or raw e4m3 bytes) ->
@@ -306,7 +281,6 @@ __global__ void __launch_bounds__(128) prepack_kernel(const void* __restrict__ s
                                                       int K, uint8_t* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
-
   const int kb64 = K >> 6;
   const int nb = blockIdx.x / kb64, kb = blockIdx.x - nb * kb64;
   const int r = threadIdx.x;
@@ -338,11 +312,11 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 static EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
   }
   return fn;
 }
@@ -363,16 +337,19 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, u
 
 // Token tile: the smallest of 16/32/64/128 covering m, capped so terms*bn <= 128.
 static inline int block_n_for(int64_t m, int terms) {
-  const int cap = terms == 1 ? 128 : terms == 2 ? 64 : 32;
+  int cap = 128;
+  while (cap > 16 && cap * terms > 128) cap >>= 1;
   int bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
   return bn < cap ? bn : cap;
 }
 
+constexpr size_t ERR_BYTES = 256;  // error word at offset 0 of every GEMM workspace
+
 struct Plan {
-  int terms, bn, m_tiles, m_pad, n_tiles, nkt, ksplit, stages, tmem_cols;
+  int terms, bn, m_tiles, m_pad, n_tiles, nkt, ks, rows_max, stages, tmem_cols;
   size_t smem;
-  // workspace layout (bytes, 256-aligned)
-  size_t off_ctl, off_xq, off_sfx, off_gx, off_part, total;
+  // workspace of ada_nvfp4_linear (bytes, 256-aligned): [err][xq][sfx][gx]
+  size_t off_xq, off_sfx, off_gx, total;
 };
 
 static inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -382,32 +359,49 @@ static inline uint32_t pow2_cols(uint32_t c) {
   return r;
 }
 
+// Two co-resident CTAs per SM when shared memory and TMEM allow (each CTA's MMA thread
+// issues its own tcgen05 stream); else one CTA per SM with a deeper pipeline.
 template <int BN, int T>
-static void stages_for(int& stages, uint32_t& cols, size_t& smem) {
+static void stages_for(int ks, int rows_max, int& stages, uint32_t& cols, size_t& smem) {
   using C = Cfg<BN, T>;
-  // two CTAs per SM: <= 112 KiB shared memory and <= 256 TMEM columns each
+  const size_t recv = C::recv_bytes(ks, rows_max);
   int s = 0;
-  for (int k = MAX_STAGES; k >= 2; --k)
-    if (C::smem_bytes(k) <= 112 * 1024 && C::tmem_need(k) <= 256) { s = k; break; }
-  if (s == 0)  // one CTA per SM
+  for (int k = MAX_STAGES; k >= 3; --k)
+    if (C::smem_bytes(k, recv) <= 113 * 1024 && C::tmem_need(k) <= 256) { s = k; break; }
+  if (s == 0)
     for (int k = MAX_STAGES; k >= 2; --k)
-      if (C::smem_bytes(k) <= 220 * 1024 && C::tmem_need(k) <= 512) { s = k; break; }
+      if (C::smem_bytes(k, recv) <= 226 * 1024 && C::tmem_need(k) <= 512) { s = k; break; }
   stages = s;
-  cols = pow2_cols(C::tmem_need(s));
-  smem = C::smem_bytes(s);
+  cols = s ? pow2_cols(C::tmem_need(s)) : 0;
+  smem = C::smem_bytes(s, recv);
 }
 
-static void stages_dispatch(int bn, int t, int& stages, uint32_t& cols, size_t& smem) {
-#define ADA_SD(B, TT) if (bn == B && t == TT) { stages_for<B, TT>(stages, cols, smem); return; }
-  ADA_SD(16, 1) ADA_SD(16, 2) ADA_SD(16, 3) ADA_SD(32, 1) ADA_SD(32, 2) ADA_SD(32, 3)
-  ADA_SD(64, 1) ADA_SD(64, 2) ADA_SD(128, 1)
+#define ADA_FP4_CONFIGS(X) \
+  X(16, 1) X(16, 2) X(16, 3) X(16, 4) X(16, 5) X(16, 6) X(16, 7) X(16, 8) \
+  X(32, 1) X(32, 2) X(32, 3) X(32, 4) X(64, 1) X(64, 2) X(128, 1)
+
+static void stages_dispatch(int bn, int t, int ks, int rows_max, int& stages, uint32_t& cols, size_t& smem) {
+#define ADA_SD(B, TT) if (bn == B && t == TT) { stages_for<B, TT>(ks, rows_max, stages, cols, smem); return; }
+  ADA_FP4_CONFIGS(ADA_SD)
 #undef ADA_SD
   stages = 0;
 }
 
-static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ksplit, Plan& P) {
+static int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int v = 0;
+    cache[dev] = (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) ? v : 148;
+  }
+  return cache[dev];
+}
+
+// force_ks > 0 overrides the split-K factor (tests of the cluster reduction).
+static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, Plan& P) {
   if (m <= 0 || n <= 0 || k <= 0) return ADA_ERR_INVALID_ARG;
-  if (terms < 1 || terms > 3) return ADA_ERR_INVALID_ARG;
+  if (terms < 1 || terms > q::MAX_TERMS) return ADA_ERR_INVALID_ARG;
   if (n % BM || k % KT) return ADA_ERR_UNSUPPORTED;
   if (m > (1 << 24) || n > (1 << 24) || k > (1 << 24)) return ADA_ERR_UNSUPPORTED;
   P.terms = terms;
@@ -416,33 +410,25 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_kspli
   P.m_pad = P.m_tiles * P.bn;
   P.n_tiles = (int)(n / BM);
   P.nkt = (int)(k / KT);
-  const int tiles = P.n_tiles * P.m_tiles;
-  int ks = 1;
-  if (force_ksplit > 0) {
-    ks = force_ksplit;
-  } else if (tiles < 148) {
-    ks = 296 / tiles;
-    ks = ks < P.nkt / 2 ? ks : P.nkt / 2;
-    if (ks < 1) ks = 1;
-  }
+  const int64_t tiles = (int64_t)P.n_tiles * P.m_tiles;
+  if (tiles > 65535) return ADA_ERR_UNSUPPORTED;
+  int64_t ks = force_ks > 0 ? force_ks : (2 * (int64_t)num_sms()) / tiles;
+  if (ks > MAX_KS) ks = MAX_KS;
   if (ks > P.nkt) ks = P.nkt;
-  if (ks > 64) ks = 64;
-  P.ksplit = ks;
+  if (ks < 1) ks = 1;
+  P.ks = (int)ks;
+  P.rows_max = (int)cdiv(BM, ks);
   uint32_t cols = 0;
-  stages_dispatch(P.bn, terms, P.stages, cols, P.smem);
+  stages_dispatch(P.bn, terms, P.ks, P.rows_max, P.stages, cols, P.smem);
   if (P.stages < 2) return ADA_ERR_UNSUPPORTED;
   P.tmem_cols = (int)cols;
-  size_t off = 0;
-  P.off_ctl = off;
-  off = al256(off + (size_t)tiles * 4 + 16);
+  size_t off = ERR_BYTES;
   P.off_xq = off;
   off = al256(off + (size_t)terms * P.m_pad * (size_t)(k / 2));
   P.off_sfx = off;
-  off = al256(off + (size_t)P.m_tiles * (size_t)(k / 64) * 512);
+  if (terms == 1) off = al256(off + (size_t)P.m_tiles * (size_t)(k / 64) * 512);
   P.off_gx = off;
   off = al256(off + (size_t)P.m_pad * 4);
-  P.off_part = off;
-  if (P.ksplit > 1) off = al256(off + (size_t)P.ksplit * P.m_pad * (size_t)n * 4);
   P.total = off;
   return ADA_OK;
 }
@@ -457,8 +443,11 @@ static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const Gem
       return ADA_ERR_CUDA;
     configured = P.smem;
   }
-  dim3 grid(P.n_tiles * P.m_tiles, P.ksplit);
-  (void)ada::launch_k(kern, dim3(grid), dim3(128), P.smem, st, tmw, tmx, gp);
+  const dim3 grid((unsigned)P.ks, (unsigned)(P.n_tiles * P.m_tiles));
+  if (P.ks > 1)
+    (void)ada::launch_kc(kern, grid, dim3(192), P.smem, st, P.ks, tmw, tmx, gp);
+  else
+    (void)ada::launch_k(kern, grid, dim3(192), P.smem, st, tmw, tmx, gp);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }
@@ -466,16 +455,14 @@ static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const Gem
 static int dispatch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmParams& gp, const Plan& P,
                          cudaStream_t st) {
 #define ADA_G(B, TT) if (P.bn == B && P.terms == TT) return launch_gemm<B, TT>(tmw, tmx, gp, P, st);
-  ADA_G(16, 1) ADA_G(16, 2) ADA_G(16, 3) ADA_G(32, 1) ADA_G(32, 2) ADA_G(32, 3)
-  ADA_G(64, 1) ADA_G(64, 2) ADA_G(128, 1)
+  ADA_FP4_CONFIGS(ADA_G)
 #undef ADA_G
   return ADA_ERR_UNSUPPORTED;
 }
 
 static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const float* gx, int m, int n, int k,
                     const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w, const float* w_scale_2,
-                    const void* bias, void* y, int y_dtype, int64_t ldy, uint8_t* ctl, uint8_t* part,
-                    cudaStream_t st) {
+                    const void* bias, void* y, int y_dtype, int64_t ldy, unsigned int* err, cudaStream_t st) {
   CUtensorMap tmw, tmx;
   if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, BM)) return ADA_ERR_CUDA;
   if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2),
@@ -488,36 +475,30 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
   gp.gw = w_scale_2;
   gp.bias = bias;
   gp.y = y;
-  gp.partial = reinterpret_cast<float*>(part);
-  gp.counters = reinterpret_cast<int*>(ctl);
-  gp.err = reinterpret_cast<unsigned int*>(ctl + (size_t)P.n_tiles * P.m_tiles * 4);
+  gp.err = err;
   gp.M = m;
   gp.N = n;
   gp.K = k;
   gp.ldy = (int)ldy;
-  gp.m_pad = P.m_pad;
   gp.n_tiles = P.n_tiles;
-  gp.m_tiles = P.m_tiles;
-  gp.ksplit = P.ksplit;
+  gp.nkt = P.nkt;
   gp.stages = P.stages;
   gp.tmem_cols = P.tmem_cols;
   gp.out_dtype = y_dtype;
+  gp.ks = P.ks;
+  gp.rows_max = P.rows_max;
   return dispatch_gemm(tmw, tmx, gp, P, st);
 }
 
-// Workspace of the pre-quantised GEMM: control words + split-K partials only.
-static size_t gemm_ws_bytes(const Plan& P, int64_t n) {
-  size_t off = al256((size_t)P.n_tiles * P.m_tiles * 4 + 16);
-  if (P.ksplit > 1) off = al256(off + (size_t)P.ksplit * P.m_pad * (size_t)n * 4);
-  return off;
-}
-
 }  // namespace fp4
+
+namespace fused {
+int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
+                     cudaStream_t st);
+}
 }  // namespace ada
 
 using namespace ada;
-
-static inline size_t al256_pub(size_t x) { return (x + 255) & ~size_t(255); }
 
 extern "C" size_t ada_nvfp4_sf_bytes(int64_t n, int64_t k) {
   if (n <= 0 || k <= 0 || k % 64) return 0;
@@ -531,8 +512,8 @@ extern "C" int ada_nvfp4_prepack_scales(const void* scale, int scale_is_fp16, in
   if ((uintptr_t)sf_out & 15) return ADA_ERR_ALIGNMENT;
   const int64_t blocks = cdiv(n, 128) * (k / 64);
   if (blocks > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
-  (void)ada::launch_k(fp4::prepack_kernel, dim3((unsigned)blocks), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream), 
-      scale, scale_is_fp16, ld_scale, (int)n, (int)k, sf_out);
+  (void)ada::launch_k(fp4::prepack_kernel, dim3((unsigned)blocks), dim3(128), 0,
+                      reinterpret_cast<cudaStream_t>(stream), scale, scale_is_fp16, ld_scale, (int)n, (int)k, sf_out);
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }
@@ -551,7 +532,7 @@ extern "C" int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int6
   if (!x || !w_packed || !sf_w || !w_scale_2 || !y || !workspace) return ADA_ERR_INVALID_ARG;
   if ((x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16) || (y_dtype != ADA_DT_BF16 && y_dtype != ADA_DT_F16))
     return ADA_ERR_INVALID_ARG;
-  if (ldx < k || ldy < n || ldw < k / 2) return ADA_ERR_INVALID_ARG;
+  if (ldx < k || ldy < n || ldw < k / 2 || force_ksplit < 0) return ADA_ERR_INVALID_ARG;
   fp4::Plan P;
   int rc = fp4::make_plan(m, n, k, terms, force_ksplit, P);
   if (rc != ADA_OK) return rc;
@@ -561,21 +542,11 @@ extern "C" int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int6
     return ADA_ERR_ALIGNMENT;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-
-  uint8_t* xq = ws + P.off_xq;
-  uint8_t* sfx = ws + P.off_sfx;
-  float* gx = reinterpret_cast<float*>(ws + P.off_gx);
-  if (x_dtype == ADA_DT_BF16)
-    (void)ada::launch_k(fp4::act_quant_kernel<__nv_bfloat16>, dim3(P.m_pad), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                                                  (int)m, (int)k, terms, P.bn, P.m_tiles, P.m_pad, xq,
-                                                                  sfx, gx);
-  else
-    (void)ada::launch_k(fp4::act_quant_kernel<__half>, dim3(P.m_pad), dim3(256), 0, st, reinterpret_cast<const __half*>(x), ldx, (int)m, (int)k,
-                                                           terms, P.bn, P.m_tiles, P.m_pad, xq, sfx, gx);
-  ADA_CHECK_LAUNCH();
-
-  return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y, y_dtype,
-                       ldy, ws + P.off_ctl, ws + P.off_part, st);
+  const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st);
+  if (rc != ADA_OK) return rc;
+  return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y,
+                       y_dtype, ldy, reinterpret_cast<unsigned int*>(ws), st);
 }
 
 extern "C" int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
@@ -588,47 +559,39 @@ extern "C" int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t
 
 extern "C" int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                    int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream) {
-  if (m <= 0 || k <= 0 || !x || !xq || !sfx || !gx) return ADA_ERR_INVALID_ARG;
-  if (terms < 1 || terms > 3 || (x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16)) return ADA_ERR_INVALID_ARG;
-  if (block_n != 16 && block_n != 32 && block_n != 64 && block_n != 128) return ADA_ERR_INVALID_ARG;
-  if (terms * block_n > 128) return ADA_ERR_INVALID_ARG;
-  if (k % 256 || ldx < k) return ADA_ERR_UNSUPPORTED;
-  if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)xq & 15)) return ADA_ERR_ALIGNMENT;
-  const int m_tiles = (int)cdiv(m, block_n), m_pad = m_tiles * block_n;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (x_dtype == ADA_DT_BF16)
-    (void)ada::launch_k(fp4::act_quant_kernel<__nv_bfloat16>, dim3(m_pad), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                                                (int)m, (int)k, terms, block_n, m_tiles, m_pad, xq,
-                                                                sfx, gx);
-  else
-    (void)ada::launch_k(fp4::act_quant_kernel<__half>, dim3(m_pad), dim3(256), 0, st, reinterpret_cast<const __half*>(x), ldx, (int)m, (int)k,
-                                                         terms, block_n, m_tiles, m_pad, xq, sfx, gx);
-  ADA_CHECK_LAUNCH();
-  return ADA_OK;
+  if (m <= 0 || k <= 0 || !x || !xq || !gx) return ADA_ERR_INVALID_ARG;
+  if (x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  if (ldx < k) return ADA_ERR_INVALID_ARG;
+  if (k % 256) return ADA_ERR_UNSUPPORTED;
+  if (!q::dst_ok(terms, block_n, (int)k) || (terms == 1 && !sfx)) return ADA_ERR_INVALID_ARG;
+  if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)xq & 15) || ((uintptr_t)gx & 3)) return ADA_ERR_ALIGNMENT;
+  const int64_t m_pad = cdiv(m, block_n) * block_n;
+  const q::QuantDst dst{xq, sfx, gx, terms, block_n, (int)k};
+  return fused::launch_act_quant(x, x_dtype, ldx, m, m_pad, dst, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,
                                           unsigned int* status_out, void* stream) {
+  (void)m;
+  (void)n;
+  (void)k;
+  (void)terms;
   if (!workspace || !status_out) return ADA_ERR_INVALID_ARG;
-  fp4::Plan P;
-  int rc = fp4::make_plan(m, n, k, terms, 0, P);
-  if (rc != ADA_OK) return rc;
-  const uint8_t* errp = reinterpret_cast<const uint8_t*>(workspace) + P.off_ctl + (size_t)P.n_tiles * P.m_tiles * 4;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(status_out, errp, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return ADA_ERR_CUDA;
+  if (cudaMemcpyAsync(status_out, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return ADA_ERR_CUDA;
   if (cudaStreamSynchronize(st) != cudaSuccess) return ADA_ERR_CUDA;
   return ADA_OK;
 }
 
 extern "C" int ada_nvfp4_block_n(int64_t m, int terms) {
-  if (m <= 0 || terms < 1 || terms > 3) return 0;
+  if (m <= 0 || terms < 1 || terms > q::MAX_TERMS) return 0;
   return fp4::block_n_for(m, terms);
 }
 
 extern "C" size_t ada_nvfp4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int terms) {
   fp4::Plan P;
   if (fp4::make_plan(m, n, k, terms, 0, P) != ADA_OK) return 0;
-  return fp4::gemm_ws_bytes(P, n);
+  return fp4::ERR_BYTES;
 }
 
 extern "C" int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
@@ -636,19 +599,18 @@ extern "C" int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float
                               const float* w_scale_2, int64_t n, int64_t k, const void* bias, void* y, int y_dtype,
                               int64_t ldy, int force_ksplit, void* workspace, size_t workspace_bytes, void* stream) {
   if (m == 0) return ADA_OK;
-  if (!xq || !sfx || !gx || !w_packed || !sf_w || !w_scale_2 || !y || !workspace) return ADA_ERR_INVALID_ARG;
+  if (!xq || !gx || !w_packed || !sf_w || !w_scale_2 || !y || !workspace) return ADA_ERR_INVALID_ARG;
+  if (terms == 1 && !sfx) return ADA_ERR_INVALID_ARG;
   if (y_dtype != ADA_DT_BF16 && y_dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
-  if (ldy < n || ldw < k / 2) return ADA_ERR_INVALID_ARG;
+  if (ldy < n || ldw < k / 2 || force_ksplit < 0) return ADA_ERR_INVALID_ARG;
   fp4::Plan P;
   int rc = fp4::make_plan(m, n, k, terms, force_ksplit, P);
   if (rc != ADA_OK) return rc;
   if (block_n != P.bn) return ADA_ERR_INVALID_ARG;
-  if (workspace_bytes < fp4::gemm_ws_bytes(P, n)) return ADA_ERR_WORKSPACE;
-  if (((uintptr_t)xq & 15) || ((uintptr_t)sfx & 15) || ((uintptr_t)w_packed & 15) || (ldw & 15) ||
+  if (workspace_bytes < fp4::ERR_BYTES) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)xq & 15) || (sfx && ((uintptr_t)sfx & 15)) || ((uintptr_t)w_packed & 15) || (ldw & 15) ||
       ((uintptr_t)sf_w & 15) || ((uintptr_t)workspace & 255))
     return ADA_ERR_ALIGNMENT;
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  const size_t part_off = al256_pub((size_t)P.n_tiles * P.m_tiles * 4 + 16);
   return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y, y_dtype, ldy,
-                       ws, ws + part_off, reinterpret_cast<cudaStream_t>(stream));
+                       reinterpret_cast<unsigned int*>(workspace), reinterpret_cast<cudaStream_t>(stream));
 }

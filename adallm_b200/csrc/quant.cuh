@@ -1,16 +1,23 @@
-// Multi-term NVFP4 activation quantiser shared by every kernel that produces an
-// input of the tensor-core NVFP4 GEMM (bit-exact spec: oracle/nvfp4.py
-// quantize_act_terms).  A row of K values is written as `terms` NVFP4 terms that
-// share the fp32 row scale g = amax(row) / 2688; term t quantises, per 16-element
-// block, the residual left by terms < t: s = e4m3(blockamax / (6g)), code =
-// e2m1(r / (s*g)), r -= lut[code] * s * g.  Every operation is one IEEE fp32
-// rounding (explicit _rn intrinsics: no fused multiply-add).
+// Activation quantiser shared by every kernel that produces an operand of the
+// tensor-core NVFP4 GEMM (bit-exact spec: oracle/nvfp4.py quantize_act_terms).
+//
+// Two operand modes, selected by `terms`:
+//   terms == 1   NVFP4 activations (W4A4): g = amax(row) / 2688, per 16-element block
+//                s = e4m3(blockamax / (6g)), code = e2m1(x * (1 / (s*g))) (0 when s == 0).
+//   terms 2..8   the row is a sum of `terms` e2m1 terms with unit block scales and one fp32
+//                scale per (row, term): g_0 = amax(row) / 6, g_t = g_{t-1} / 6,
+//                code_t = e2m1(r_t * (1 / g_t)), r_0 = x, r_{t+1} = r_t - e2m1val(code_t) * g_t.
+//                The residual of a term is at most g_t in magnitude, so term t + 1 never
+//                saturates; 4 terms are within ~1e-3 relative L2 of the input, 6 within ~1e-4.
+// Only the row amax couples the elements of a row, so a row may be quantised by many CTAs
+// once that one reduction is done.  A row whose amax is below 2^-64 quantises to zero
+// (g = 1).  Every operation is one IEEE fp32 rounding (explicit _rn: no fused multiply-add).
 //
 // Operand layout for token m = mt*bn + j (tile mt of bn tokens), term t -> row t*bn + j:
 //   xq  [m_tiles][terms*bn][K/2]   packed e2m1, even K in the low nibble
-//   sfx [m_tiles][K/64][512]       ue4m3 scales in the block-scaled MMA layout
-//                                  (row r of a 128-row block at (r%32)*16 + (r/32)*4)
-//   gx  [m_pad]                    g per token (1.0 for zero padding rows)
+//   sfx [m_tiles][K/64][512]       (terms == 1 only) ue4m3 scales in the block-scaled MMA
+//                                  layout: row r of a 128-row block at (r%32)*16 + (r/32)*4
+//   gx  [m_pad]                    g (terms == 1) or g_0 (terms >= 2); 1.0 for padding rows
 #pragma once
 
 #include "common.cuh"
@@ -18,9 +25,12 @@
 namespace ada {
 namespace q {
 
+constexpr int MAX_TERMS = 8;
+constexpr float MIN_AMAX = 5.421010862427522e-20f;  // 2^-64
+
 struct QuantDst {
   uint8_t* xq;
-  uint8_t* sfx;
+  uint8_t* sfx;  // terms == 1 only
   float* gx;
   int terms, bn, k;
 };
@@ -35,63 +45,98 @@ __device__ __forceinline__ float e4m3_value(uint8_t b) {
   return __half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)));
 }
 
-__device__ __forceinline__ float row_scale(float amax) { return amax > 0.f ? __fdiv_rn(amax, 2688.f) : 1.f; }
+// Scale of term t of a row with scale g_0 (terms >= 2); the GEMM epilogue derives the
+// term scales from gx with the same recurrence.
+__device__ __forceinline__ float next_term_scale(float g) { return __fdiv_rn(g, 6.f); }
 
-// Quantise one 16-element block `blk` of token m (values r[], consumed in place).
-__device__ __forceinline__ void quant_block16(const QuantDst& d, int m, int blk, float* r, float g, float g6) {
+// Per-row constants, derived from the row amax.
+struct RowQ {
+  float g[MAX_TERMS];    // terms >= 2: g_t; terms == 1: g[0] = g, g[1] = 6g
+  float rcp[MAX_TERMS];  // terms >= 2: 1 / g_t
+  int terms;
+};
+__device__ __forceinline__ RowQ make_rowq(float amax, int terms) {
+  RowQ q;
+  q.terms = terms;
+  const bool live = amax >= MIN_AMAX;
+  if (terms == 1) {
+    q.g[0] = live ? __fdiv_rn(amax, 2688.f) : 1.f;
+    q.g[1] = __fmul_rn(q.g[0], 6.f);
+    return q;
+  }
+  float g = live ? __fdiv_rn(amax, 6.f) : 1.f;
+#pragma unroll
+  for (int t = 0; t < MAX_TERMS; ++t) {
+    q.g[t] = g;
+    q.rcp[t] = __fdiv_rn(1.f, g);
+    g = next_term_scale(g);
+  }
+  return q;
+}
+
+__device__ __forceinline__ uint8_t* xq_row(const QuantDst& d, int m, int t) {
   const int mt = m / d.bn, j = m - mt * d.bn;
-  const int kb64 = d.k >> 6;
-  const size_t khalf = (size_t)d.k >> 1;
-  for (int t = 0; t < d.terms; ++t) {
+  return d.xq + ((size_t)mt * d.terms * d.bn + (size_t)t * d.bn + j) * ((size_t)d.k >> 1);
+}
+__device__ __forceinline__ uint8_t* sf_byte(const QuantDst& d, int m, int blk) {
+  const int mt = m / d.bn, j = m - mt * d.bn;
+  return d.sfx + ((size_t)mt * (d.k >> 6) + (blk >> 2)) * 512 + (j & 31) * 16 + (j >> 5) * 4 + (blk & 3);
+}
+
+// Quantise the 16-element block `blk` of token m (r is clobbered for terms >= 2).
+__device__ __forceinline__ void quant_unit(const QuantDst& d, int m, int blk, float* r, const RowQ& q) {
+  if (q.terms == 1) {
     float bamax = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(r[i]));
-    const uint8_t sb = (uint8_t)(f32x2_to_e4m3x2(__fdiv_rn(bamax, g6), 0.f) & 0xFFu);
+    const uint8_t sb = (uint8_t)(f32x2_to_e4m3x2(__fdiv_rn(bamax, q.g[1]), 0.f) & 0xFFu);
     const float sv = e4m3_value(sb);
     uint2 codes = make_uint2(0, 0);
     if (sv > 0.f) {
-      const float denom = __fmul_rn(sv, g);
-      const float rcp = __fdiv_rn(1.f, denom);
+      const float rcp = __fdiv_rn(1.f, __fmul_rn(sv, q.g[0]));
       float v[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(r[i], rcp);
       codes.x = f32x8_to_e2m1x8(v);
       codes.y = f32x8_to_e2m1x8(v + 8);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t c = ((i < 8 ? codes.x : codes.y) >> (4 * (i & 7))) & 0xFu;
-        r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(c), denom));
-      }
     }
-    const int row = t * d.bn + j;
-    *reinterpret_cast<uint2*>(d.xq + ((size_t)mt * d.terms * d.bn + row) * khalf + (size_t)blk * 8) = codes;
-    d.sfx[((size_t)mt * kb64 + (blk >> 2)) * 512 + (row & 31) * 16 + (row >> 5) * 4 + (blk & 3)] = sb;
+    *reinterpret_cast<uint2*>(xq_row(d, m, 0) + (size_t)blk * 8) = codes;
+    *sf_byte(d, m, blk) = sb;
+    return;
   }
-}
-
-// Zero codes / scales of a padding token (m in [M, m_pad)): one block per call.
-__device__ __forceinline__ void zero_block16(const QuantDst& d, int m, int blk) {
-  const int mt = m / d.bn, j = m - mt * d.bn;
-  const int kb64 = d.k >> 6;
-  const size_t khalf = (size_t)d.k >> 1;
-  for (int t = 0; t < d.terms; ++t) {
-    const int row = t * d.bn + j;
-    *reinterpret_cast<uint2*>(d.xq + ((size_t)mt * d.terms * d.bn + row) * khalf + (size_t)blk * 8) = make_uint2(0, 0);
-    d.sfx[((size_t)mt * kb64 + (blk >> 2)) * 512 + (row & 31) * 16 + (row >> 5) * 4 + (blk & 3)] = 0;
-  }
-}
-
-// Block-wide max of non-negative values (blockDim.x multiple of 32, <= 1024).
-__device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
-  return r;
+  for (int t = 0; t < MAX_TERMS; ++t) {
+    if (t < q.terms) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(r[i], q.rcp[t]);
+      uint2 codes;
+      codes.x = f32x8_to_e2m1x8(v);
+      codes.y = f32x8_to_e2m1x8(v + 8);
+      if (t + 1 < q.terms) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t c = ((i < 8 ? codes.x : codes.y) >> (4 * (i & 7))) & 0xFu;
+          r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(c), q.g[t]));
+        }
+      }
+      *reinterpret_cast<uint2*>(xq_row(d, m, t) + (size_t)blk * 8) = codes;
+    }
+  }
+}
+
+// Codes (and block scales) of a padding token m in [M, m_pad): zero.
+__device__ __forceinline__ void zero_unit(const QuantDst& d, int m, int blk) {
+  for (int t = 0; t < d.terms; ++t) *reinterpret_cast<uint2*>(xq_row(d, m, t) + (size_t)blk * 8) = make_uint2(0, 0);
+  if (d.terms == 1) *sf_byte(d, m, blk) = 0;
+}
+
+// Valid operand configuration: terms 1..8, token tile 16/32/64/128 with terms*bn <= 128,
+// K a multiple of 256 (one GEMM pipeline stage), block scales present iff terms == 1.
+__host__ __device__ inline bool dst_ok(int terms, int bn, int k) {
+  if (terms < 1 || terms > MAX_TERMS) return false;
+  if (bn != 16 && bn != 32 && bn != 64 && bn != 128) return false;
+  return terms * bn <= 128 && k > 0 && k % 256 == 0;
 }
 
 }  // namespace q

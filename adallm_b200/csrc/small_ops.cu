@@ -12,6 +12,11 @@
 #include "common.cuh"
 
 namespace ada {
+namespace fused {
+int launch_rmsnorm16(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro,
+                     const void* w, void* y, int64_t ldy, int64_t rows, int hidden, float eps, int gemma, int dtype,
+                     cudaStream_t st);
+}
 namespace small {
 
 // ---------------------------------------------------------------------------
@@ -454,6 +459,9 @@ extern "C" int ada_rmsnorm(const void* x, int64_t ldx, const void* residual, int
   if (!a16(x) || !a16(weight) || !a16(y) || (ldx & 7) || (ldy & 7)) return ADA_ERR_ALIGNMENT;
   if (residual && (!a16(residual) || !a16(residual_out) || (ld_res & 7) || (ld_res_out & 7))) return ADA_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (hidden % 16 == 0 && hidden / 16 <= 4 * 256)
+    return ada::fused::launch_rmsnorm16(x, ldx, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
+                                        hidden, eps, gemma, dtype, st);
   if (dtype == ADA_DT_BF16)
     return launch_rmsnorm<__nv_bfloat16>(x, ldx, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
                                          hidden, eps, gemma, st);

@@ -49,7 +49,7 @@ class DecodeConfig:
     rope_theta: float = 1e6
     max_position: int = 40960
     page_size: int = 16
-    terms: int = 3
+    terms: int = 4
     tp_size: int = 1
     tp_rank: int = 0
 
@@ -237,8 +237,9 @@ class Qwen3DecodeEngine:
         self.m_pad = -(-B // self.bn) * self.bn
 
         def qbuf(k):
+            sf_len = (self.m_pad // self.bn) * (k // 64) * 512 if c.terms == 1 else 16  # block scales: terms == 1
             return (torch.zeros(self.m_pad * c.terms * k // 2, dtype=torch.uint8, device=d),
-                    torch.zeros((self.m_pad // self.bn) * (k // 64) * 512, dtype=torch.uint8, device=d),
+                    torch.zeros(sf_len, dtype=torch.uint8, device=d),
                     torch.ones(self.m_pad, dtype=torch.float32, device=d))
         self.q_hidden = qbuf(H)
         self.q_attn = qbuf(c.hq * D)

@@ -9,9 +9,11 @@ Weights keep the reference parameter layout (adallm/ops/linear.py:31-43).  The f
 scale tensor is re-laid out once into the tensor-core scale-factor layout
 (``prepack_scales``) and cached on the scale tensor.
 
-Activation precision: ``terms`` NVFP4 terms per activation row (default 3, within
-~1e-3 of the fp32 dequantise-then-matmul oracle; 1 = W4A4).  Set with the
-environment variable ADALLM_B200_NVFP4_TERMS or per call.
+Activation precision: ``terms`` e2m1 terms per activation row.  1 = NVFP4 activations
+with per-16 block scales (W4A4, ~0.1 relative deviation from the reference); 2..8 =
+row-scaled terms whose sum approximates the bf16 activation (4 terms, the default:
+~5e-4 relative L2 for Gaussian rows; 6 terms: ~1e-5).  Set with the environment
+variable ADALLM_B200_NVFP4_TERMS or per call.
 """
 from __future__ import annotations
 
@@ -21,7 +23,7 @@ import torch
 
 from . import _native as N
 
-DEFAULT_TERMS = int(os.environ.get("ADALLM_B200_NVFP4_TERMS", "3"))
+DEFAULT_TERMS = int(os.environ.get("ADALLM_B200_NVFP4_TERMS", "4"))
 
 
 def sf_bytes(n: int, k: int) -> int:

@@ -46,7 +46,7 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--layers", type=int, default=36, help="decoder layers (36 = the Qwen3-8B shape)")
     ap.add_argument("--prompt", type=int, default=16)
-    ap.add_argument("--terms", type=int, default=3, help="NVFP4 activation terms (1 = W4A4)")
+    ap.add_argument("--terms", type=int, default=4, help="activation e2m1 terms (1 = W4A4 NVFP4, 2..8 row-scaled)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-reps", type=int, default=5)
     return ap.parse_args()

@@ -199,13 +199,14 @@ ADA_API int ada_embedding(const int64_t* ids, int64_t num_tokens, const void* ta
  * The scales are first re-laid out once per weight with ada_nvfp4_prepack_scales into
  * ada_nvfp4_sf_bytes(N, K) bytes (the layout the block-scaled tensor-core MMA reads;
  * this is the post-load hook next to adallm/infra/loader.py:129-162).
- * x [M, K] bf16/f16 (row stride ldx) is quantised on the device into `terms` NVFP4
- * terms (1 = W4A4, 3 = within ~1e-3 of the fp32 dequantise-then-matmul result) and
- * multiplied with tcgen05 kind::mxf4nvf4 MMAs.  y [M, N] bf16/f16, row stride ldy.
- * Implemented: N % 128 == 0, K % 256 == 0, terms in 1..3.
- * workspace: ada_nvfp4_linear_workspace_size(M, N, K, terms) bytes, 256-byte aligned,
- * ZERO-FILLED before its first use; every call leaves it ready for the next call.  Calls
- * that share a workspace must be ordered (same stream).
+ * x [M, K] bf16/f16 (row stride ldx) is quantised on the device into `terms` e2m1 terms
+ * (see ada_nvfp4_act_quant; 4 terms keep the result within ~1e-3 of the fp32
+ * dequantise-then-matmul result, 1 = W4A4) and multiplied with tcgen05 kind::mxf4nvf4
+ * MMAs.  y [M, N] bf16/f16, row stride ldy.
+ * Implemented: N % 128 == 0, K % 256 == 0, terms in 1..8.
+ * workspace: ada_nvfp4_linear_workspace_size(M, N, K, terms) bytes, 256-byte aligned; its
+ * first 4 bytes are the error word (ada_nvfp4_workspace_status), which must be zero before
+ * the first use.  Calls that share a workspace must be ordered (same stream).
  * ---------------------------------------------------------------------- */
 ADA_API size_t ada_nvfp4_sf_bytes(int64_t n, int64_t k);
 ADA_API int ada_nvfp4_prepack_scales(const void* scale, int scale_is_fp16, int64_t ld_scale, int64_t n,
@@ -215,18 +216,23 @@ ADA_API int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m,
                              const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
                              const float* w_scale_2, int64_t n, const void* bias, void* y, int y_dtype,
                              int64_t ldy, int terms, void* workspace, size_t workspace_bytes, void* stream);
-/* Same as ada_nvfp4_linear with an explicit split-K factor (0 = library choice; tests and tuning). */
+/* Same as ada_nvfp4_linear with an explicit split-K factor (0 = library choice, else 1..8
+ * CTAs per output tile; tests and tuning). */
 ADA_API int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
                                 const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
                                 const float* w_scale_2, int64_t n, const void* bias, void* y, int y_dtype,
                                 int64_t ldy, int terms, int force_ksplit, void* workspace,
                                 size_t workspace_bytes, void* stream);
 /* The activation quantiser on its own (the first half of ada_nvfp4_linear; no reference
- * counterpart -- the reference never quantises activations to e2m1).  Row m of x becomes
- * `terms` NVFP4 terms sharing the fp32 row scale gx[m] = amax(row) / 2688.  Token
- * m = mt*block_n + j, term t is operand row t*block_n + j of token tile mt:
+ * counterpart -- the reference never quantises activations to e2m1).  Row m of x becomes:
+ *   terms == 1   NVFP4: gx[m] = g = amax(row) / 2688, per 16-block ue4m3 scale
+ *                s = e4m3(blockamax / (6g)) in sfx, codes e2m1(x / (s*g));
+ *   terms 2..8   `terms` row-scaled e2m1 terms with unit block scales: gx[m] = g_0 =
+ *                amax(row) / 6, term t has scale g_t = g_{t-1} / 6 and quantises the
+ *                residual left by the terms before it (sfx unused, may be NULL).
+ * Token m = mt*block_n + j, term t is operand row t*block_n + j of token tile mt:
  *   xq  [m_pad/block_n][terms*block_n][k/2]   packed e2m1, even k in the low nibble
- *   sfx [m_pad/block_n][k/64][512]            ue4m3 scales, MMA scale-factor layout
+ *   sfx [m_pad/block_n][k/64][512]            (terms == 1) ue4m3 scales, MMA scale-factor layout
  *   gx  [m_pad]                               (1.0 for the zero padding rows)
  * with m_pad = ceil(m / block_n) * block_n, block_n in {16, 32, 64, 128} and
  * terms * block_n <= 128 (ada_nvfp4_block_n(m, terms) gives the GEMM's choice). */
@@ -234,8 +240,10 @@ ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by
  * ada_nvfp4_act_quant (or by a fused producer writing the same layout) with
- * block_n == ada_nvfp4_block_n(m, terms).  workspace: ada_nvfp4_gemm_workspace_size(m, n, k, terms)
- * bytes, 256-byte aligned, zero-filled before first use (left ready for the next call). */
+ * block_n == ada_nvfp4_block_n(m, terms) (sfx only read for terms == 1).  workspace:
+ * ada_nvfp4_gemm_workspace_size(m, n, k, terms) bytes (the error word), 256-byte aligned,
+ * zero before first use.  force_ksplit: 0 = library choice, else the number of CTAs (1..8,
+ * one thread-block cluster) that split each output tile's K range. */
 ADA_API int ada_nvfp4_block_n(int64_t m, int terms);
 ADA_API size_t ada_nvfp4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int terms);
 ADA_API int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,

@@ -190,50 +190,76 @@ def quantize_weight(w: np.ndarray, group_size: int = 16):
     return pack_codes(codes), s_bits, g
 
 
-def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16):
-    """Bit-exact specification of adallm_b200's activation quantiser.
+MIN_AMAX = np.float32(2.0 ** -64)
+MAX_TERMS = 8
 
-    x: [M, K] (bf16 values given as fp32).  For each row:
-      g = rowamax / 2688 (1.0 for an all-zero row), r = x
-      for t in range(terms):
-        per 16-block: s = e4m3(blockamax(r) / (g*6)); denom = s*g
-        code = e2m1(r * (1/denom))   (0 when s == 0)
-        r = r - lut[code]*denom
+
+def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16):
+    """Bit-exact specification of adallm_b200's activation quantiser (csrc/quant.cuh).
+
+    x: [M, K] (bf16 values given as fp32).  Per row, with amax = max|x| (a row whose amax
+    is below 2^-64 quantises to zero with scale 1.0):
+      terms == 1 (NVFP4, block scales): g = amax / 2688; per 16-block
+          s = e4m3(blockamax / (g*6)), code = e2m1(x * (1 / (s*g)))   (0 when s == 0)
+      terms >= 2 (row-scaled terms, unit block scales): g_0 = amax / 6, g_t = g_{t-1} / 6,
+          r_0 = x, code_t = e2m1(r_t * (1 / g_t)), r_{t+1} = r_t - e2m1val(code_t) * g_t
     Every operation is one IEEE fp32 rounding (no fused multiply-add).
-    Returns codes uint8 [T, M, K], scale bits uint8 [T, M, K/16], g fp32 [M].
+    Returns codes uint8 [T, M, K], block-scale bits uint8 [M, K/16] (terms == 1; None
+    otherwise) and the row scale fp32 [M] (g, or g_0).
     """
     x = np.asarray(x, dtype=np.float32)
+    if not 1 <= terms <= MAX_TERMS:
+        raise ValueError("terms must be in 1..8")
     m, k = x.shape
     groups = k // group_size
     amax = np.max(np.abs(x), axis=1).astype(np.float32) if k else np.zeros(m, np.float32)
-    g = np.where(amax > 0, (amax / np.float32(GLOBAL_DIV)).astype(np.float32), np.float32(1.0)).astype(np.float32)
-    g6 = (g * np.float32(6.0)).astype(np.float32)
-    r = x.reshape(m, groups, group_size).copy()
-    codes = np.zeros((terms, m, groups, group_size), np.uint8)
-    sbits = np.zeros((terms, m, groups), np.uint8)
-    for t in range(terms):
+    live = amax >= MIN_AMAX
+    if terms == 1:
+        g = np.where(live, (amax / np.float32(GLOBAL_DIV)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+        g6 = (g * np.float32(6.0)).astype(np.float32)
+        r = x.reshape(m, groups, group_size)
         bamax = np.max(np.abs(r), axis=-1).astype(np.float32)
         sb = e4m3_encode((bamax / g6[:, None]).astype(np.float32))
         sv = e4m3_decode(sb)
         denom = (sv * g[:, None]).astype(np.float32)
         with np.errstate(divide="ignore", invalid="ignore"):
             rcp = np.where(denom > 0, np.float32(1.0) / denom, np.float32(0)).astype(np.float32)
-        v = (r * rcp[..., None]).astype(np.float32)
-        c = e2m1_encode(v)
+        c = e2m1_encode((r * rcp[..., None]).astype(np.float32))
         c = np.where((sv > 0)[..., None], c, np.uint8(0))
-        deq = (e2m1_decode(c) * denom[..., None]).astype(np.float32)
+        return c.reshape(1, m, k), sb, g
+    g0 = np.where(live, (amax / np.float32(6.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+    g = g0.copy()
+    r = x.copy()
+    codes = np.zeros((terms, m, k), np.uint8)
+    for t in range(terms):
+        rcp = (np.float32(1.0) / g).astype(np.float32)
+        c = e2m1_encode((r * rcp[:, None]).astype(np.float32))
+        deq = (e2m1_decode(c) * g[:, None]).astype(np.float32)
         r = (r - deq).astype(np.float32)
         codes[t] = c
-        sbits[t] = sb
-    return codes.reshape(terms, m, k), sbits, g
+        g = (g / np.float32(6.0)).astype(np.float32)
+    return codes, None, g0
 
 
-def dequant_act_terms(codes: np.ndarray, sbits: np.ndarray, g: np.ndarray, group_size: int = 16) -> np.ndarray:
-    """Sum of the T dequantised activation terms -> fp32 [M, K]."""
+def term_scales(g0: np.ndarray, terms: int) -> np.ndarray:
+    """Scale of each row-scaled term: [T, M] with g_t = g_{t-1} / 6 (fp32)."""
+    g = np.asarray(g0, np.float32).copy()
+    out = np.zeros((terms,) + g.shape, np.float32)
+    for t in range(terms):
+        out[t] = g
+        g = (g / np.float32(6.0)).astype(np.float32)
+    return out
+
+
+def dequant_act_terms(codes: np.ndarray, sbits, g: np.ndarray, group_size: int = 16) -> np.ndarray:
+    """Value the GEMM sees for the quantised activations -> fp32 [M, K] (sum of terms in float64)."""
     t, m, k = codes.shape
-    vals = e2m1_decode(codes).reshape(t, m, k // group_size, group_size)
-    s = e4m3_decode(sbits)[..., None] * np.asarray(g, np.float32)[None, :, None, None]
-    return (vals * s).sum(axis=0).reshape(m, k).astype(np.float32)
+    vals = e2m1_decode(codes).astype(np.float64)
+    if t == 1:
+        s = e4m3_decode(sbits).astype(np.float64) * np.asarray(g, np.float64)[:, None]
+        return (vals[0].reshape(m, k // group_size, group_size) * s[..., None]).reshape(m, k).astype(np.float32)
+    gt = term_scales(g, t).astype(np.float64)
+    return (vals * gt[:, :, None]).sum(axis=0).astype(np.float32)
 
 
 def linear_ref(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, scale_2, bias=None) -> np.ndarray:

@@ -38,7 +38,7 @@ def same(a, b):
 
 @pytest.mark.parametrize("hidden,gemma,with_res", [(4096, False, True), (4096, False, False), (5376, True, True),
                                                    (512, False, True)])
-@pytest.mark.parametrize("rows,terms,bn", [(16, 3, 16), (5, 3, 16), (40, 2, 64)])
+@pytest.mark.parametrize("rows,terms,bn", [(16, 4, 16), (5, 1, 16), (40, 2, 64), (16, 8, 16)])
 def test_rmsnorm_quant_matches_unfused(hidden, gemma, with_res, rows, terms, bn):
     d = dev()
     g = torch.Generator(device="cpu").manual_seed(hidden + rows)
@@ -65,15 +65,15 @@ def test_rmsnorm_quant_matches_unfused(hidden, gemma, with_res, rows, terms, bn)
     same(got, ref)
 
 
-@pytest.mark.parametrize("inter,act", [(12288, 0), (1536, 0), (3072, 1)])
-def test_gated_act_quant_matches_unfused(inter, act):
+@pytest.mark.parametrize("inter,act,terms", [(12288, 0, 4), (1536, 0, 1), (3072, 1, 4), (21504, 1, 6)])
+def test_gated_act_quant_matches_unfused(inter, act, terms):
     d = dev()
     x = (torch.randn((16, 2 * inter), device=d) * 2).to(torch.bfloat16)
     y_ref = gated_act(x, act)
-    ref = act_quant(y_ref, 3, 16)
-    got = qbufs(16, inter, 3, 16, d)
+    ref = act_quant(y_ref, terms, 16)
+    got = qbufs(16, inter, terms, 16, d)
     y = torch.empty_like(y_ref)
-    N.check(N.lib().ada_gated_act_quant(x.data_ptr(), 2 * inter, y.data_ptr(), inter, 16, inter, act, 0, 3, 16,
+    N.check(N.lib().ada_gated_act_quant(x.data_ptr(), 2 * inter, y.data_ptr(), inter, 16, inter, act, 0, terms, 16,
                                         got[0].data_ptr(), got[1].data_ptr(), got[2].data_ptr(),
                                         torch.cuda.current_stream().cuda_stream), "gated_act_quant")
     torch.cuda.synchronize()
@@ -81,8 +81,8 @@ def test_gated_act_quant_matches_unfused(inter, act):
     same(got, ref)
 
 
-@pytest.mark.parametrize("batch,hq,hkv", [(16, 32, 8), (7, 16, 2)])
-def test_paged_decode_quant_matches_unfused(batch, hq, hkv):
+@pytest.mark.parametrize("batch,hq,hkv,terms", [(16, 32, 8, 4), (7, 16, 2, 1), (16, 64, 8, 5)])
+def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms):
     d = dev()
     case = oa.make_paged_case(5, batch=batch, hq=hq, hkv=hkv, d=128, page=16, ctx_lo=1, ctx_hi=900)
     q = torch.from_numpy(case["q"]).to(torch.bfloat16).to(d)
@@ -91,15 +91,15 @@ def test_paged_decode_quant_matches_unfused(batch, hq, hkv):
     bt = torch.from_numpy(case["block_tables"]).to(d)
     ctx = torch.from_numpy(case["context_lens"]).to(d)
     out_ref = paged_decode(q, k, v, bt, ctx, case["scale"])
-    ref = act_quant(out_ref.view(batch, hq * 128), 3, 16)
-    got = qbufs(batch, hq * 128, 3, 16, d)
+    ref = act_quant(out_ref.view(batch, hq * 128), terms, 16)
+    got = qbufs(batch, hq * 128, terms, 16, d)
     out = torch.empty_like(out_ref)
     wsb = int(N.lib().ada_fp8_paged_decode_workspace_size(batch, hq, bt.shape[1], 16, 128))
     ws = torch.empty(wsb, dtype=torch.uint8, device=d)
     N.check(N.lib().ada_fp8_paged_decode_quant(
         q.data_ptr(), 0, q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
         k.shape[0], bt.data_ptr(), bt.stride(0), bt.shape[1], ctx.data_ptr(), batch, hq, hkv, 128, 16,
-        case["scale"], 1.0, 1.0, 0, out.data_ptr(), 0, 3, 16, got[0].data_ptr(), got[1].data_ptr(),
+        case["scale"], 1.0, 1.0, 0, out.data_ptr(), 0, terms, 16, got[0].data_ptr(), got[1].data_ptr(),
         got[2].data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream), "decode_quant")
     torch.cuda.synchronize()
     assert torch.equal(out, out_ref)

@@ -111,8 +111,9 @@ def test_gated_act(act):
     x = (torch.randn(17, 2 * 1536) * 3).to(torch.bfloat16)
     y = gated_act(x.to(d), act)
     y_ref = (ol.silu_and_mul if act == 0 else ol.gelu_and_mul)(x)
-    # transcendental implementations differ by ~1 ulp; GELU's far tail is ~1e-30 either side of zero
-    assert torch.allclose(y.float().cpu(), y_ref.float(), rtol=2 ** -7, atol=1e-6)
+    # the activation's transcendental differs by ~1 fp32 ulp, which can move the bf16 activation by
+    # one ulp before the product rounds again (<= 2 bf16 ulps); GELU's far tail is ~0 either side of zero
+    assert torch.allclose(y.float().cpu(), y_ref.float(), rtol=2 ** -6, atol=1e-5)
     assert rel_l2(y.float().cpu(), y_ref.float()) < 2e-3
 
 

@@ -122,12 +122,28 @@ def test_paged_decode_oracle_matches_gather_softmax():
 def test_act_terms_reconstruct():
     rng = np.random.default_rng(0)
     x = torch.from_numpy(rng.standard_normal((4, 512)).astype(np.float32)).to(torch.bfloat16).float().numpy()
-    errs = []
-    for t in (1, 2, 3):
+    errs = {}
+    for t in (1, 2, 3, 4, 6, 8):
         c, s, g = nv.quantize_act_terms(x, t)
-        errs.append(nv.rel_l2(nv.dequant_act_terms(c, s, g), x))
-    assert errs[0] < 0.12 and errs[1] < 0.015 and errs[2] < 0.002
-    assert errs[0] > errs[1] > errs[2]
+        errs[t] = nv.rel_l2(nv.dequant_act_terms(c, s, g), x)
+    assert errs[1] < 0.12 and errs[2] < 0.03 and errs[4] < 1e-3 and errs[6] < 5e-5 and errs[8] < 2e-6
+    assert errs[2] > errs[3] > errs[4] > errs[6] > errs[8]
+
+
+def test_act_terms_known_answer():
+    # row amax 6 -> g_0 = 1: term 0 holds the e2m1-representable values exactly, term 1
+    # (g_1 = 1/6) the remainder of 5 = 4 + 1, term 2 what 1 * 6 = 6 leaves (nothing)
+    x = np.zeros((2, 256), np.float32)
+    x[0, :4] = [6.0, -3.0, 0.5, 5.0]
+    x[1, :] = 2.0 ** -70  # below 2^-64: quantises to zero with scale 1
+    c, s, g = nv.quantize_act_terms(x, 3)
+    assert s is None and g[0] == 1.0 and g[1] == 1.0
+    vals = nv.e2m1_decode(c)
+    assert list(vals[0, 0, :4]) == [6.0, -3.0, 0.5, 4.0]
+    assert list(vals[1, 0, :4]) == [0.0, 0.0, 0.0, 6.0]
+    assert np.all(vals[2, 0] == 0) and np.all(vals[:, 1] == 0)
+    np.testing.assert_array_equal(nv.dequant_act_terms(c, s, g)[0, :4], x[0, :4])
+    np.testing.assert_array_equal(nv.term_scales(np.float32([6.0]), 3)[:, 0], np.float32([6.0, 1.0, 1.0 / 6.0]))
 
 
 def test_store_kvcache_oracle_skips_minus_one():
