@@ -313,19 +313,19 @@ __global__ void __launch_bounds__(D) decode_reduce_kernel(Params P, TO* __restri
 // (rounded to the output dtype, as the unfused kernel writes it) is quantised as the
 // operand of o_proj once the cluster has combined the row amax.  `out` may be null.
 template <typename TO, int MAXU>
-__global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* __restrict__ out, int batch,
+__global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* __restrict__ out, int batch,
                                                                   q::QuantDst dst) {
   cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[8];
+  __shared__ float red[cl::MAX_WARPS];
   __shared__ float slots[cl::MAX_CLUSTER];
   const int b = blockIdx.y;
   const int row_len = P.num_heads * D;
-  const int nblk = row_len >> 4;
-  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
+  const int o0 = cl::slice_octet(row_len >> 4, blockIdx.x, gridDim.x);
+  const int o1 = cl::slice_octet(row_len >> 4, blockIdx.x + 1, gridDim.x);
   if (b >= batch) {
-    for (int k = u0 + threadIdx.x; k < u1; k += blockDim.x) q::zero_unit(dst, b, k);
+    for (int o = o0 + threadIdx.x; o < o1; o += blockDim.x) q::zero_oct(dst, b, o);
     if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[b] = 1.f;
     cl::cluster_wait();
     return;
@@ -333,26 +333,28 @@ __global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* 
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
   seq_range(P, ctx, start, start16, nsplit);
-  float v[MAXU][16];
+  float v[MAXU][8];
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int k = u0 + threadIdx.x + u * blockDim.x;
-    if (k >= u1) continue;
-    const int h = (k * 16) / D, d0 = (k * 16) % D;
+    const int o = o0 + threadIdx.x + u * blockDim.x;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+    if (o >= o1) continue;
+    const int h = (o * 8) / D, d0 = (o * 8) % D;
     const int64_t row0 = ((int64_t)b * P.num_heads + h) * P.max_splits;
     float M = -INFINITY;
     for (int s = 0; s < nsplit; ++s) M = fmaxf(M, P.ml_part[(row0 + s) * 2]);
-    float L = 0.f, O[16];
+    float L = 0.f, O[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) O[i] = 0.f;
+    for (int i = 0; i < 8; ++i) O[i] = 0.f;
     if (M != -INFINITY) {
       for (int s = 0; s < nsplit; ++s) {
         const float w = fast_exp2(P.ml_part[(row0 + s) * 2] - M);
         L += P.ml_part[(row0 + s) * 2 + 1] * w;
         const float4* op = reinterpret_cast<const float4*>(P.o_part + (row0 + s) * D + d0);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
           const float4 f = op[i];
           O[4 * i + 0] += f.x * w;
           O[4 * i + 1] += f.y * w;
@@ -362,23 +364,19 @@ __global__ void __launch_bounds__(256) decode_reduce_quant_kernel(Params P, TO* 
       }
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       v[u][i] = to_f32(from_f32<TO>(L > 0.f ? O[i] / L : 0.f));
       amax = fmaxf(amax, fabsf(v[u][i]));
     }
-    if (out) {
-      TO* op = out + (int64_t)b * row_len + k * 16;
-      *reinterpret_cast<uint4*>(op) = pack8<TO>(v[u]);
-      *reinterpret_cast<uint4*>(op + 8) = pack8<TO>(v[u] + 8);
-    }
+    if (out) *reinterpret_cast<uint4*>(out + (int64_t)b * row_len + o * 8) = pack8<TO>(v[u]);
   }
   cl::cluster_wait();
   const q::RowQ rq = q::make_rowq(cl::cluster_allreduce<cl::OpMax>(amax, red, slots), dst.terms);
   if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[b] = rq.g[0];
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int k = u0 + threadIdx.x + u * blockDim.x;
-    if (k < u1) q::quant_unit(dst, b, k, v[u], rq);
+    const int o = o0 + threadIdx.x + u * blockDim.x;
+    q::quant_oct(dst, b, o < o1 ? o : 0, v[u], rq, o < o1);
   }
 }
 

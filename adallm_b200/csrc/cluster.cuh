@@ -55,14 +55,15 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
 
 struct OpMax {
   __device__ static float apply(float a, float b) { return fmaxf(a, b); }
-  static constexpr float identity = 0.f;  // reductions of magnitudes
 };
 struct OpSum {
   __device__ static float apply(float a, float b) { return __fadd_rn(a, b); }
-  static constexpr float identity = 0.f;
 };
 
-// CTA-wide reduction (any blockDim.x multiple of 32, <= 1024), warps combined in order.
+constexpr int MAX_WARPS = 16;  // row kernels run <= 512 threads
+
+// CTA-wide reduction (blockDim.x a multiple of 32, <= 32 * MAX_WARPS; `red` holds MAX_WARPS
+// floats), warps combined in order.
 template <typename Op>
 __device__ __forceinline__ float block_reduce(float v, float* red) {
 #pragma unroll
@@ -91,9 +92,10 @@ __device__ __forceinline__ float cluster_allreduce(float v, float* red, float* s
   return r;
 }
 
-// How a row of `units` 16-element units is spread over a cluster: `ctas` CTAs of `threads`
-// threads, each thread owning up to `maxu` units of its CTA's contiguous slice.  Depends on
-// the row length only, so every kernel that reduces rows of one length rounds the same way.
+// How a row of `units` 16-element blocks is spread over a cluster: `ctas` CTAs, each
+// owning a contiguous slice of blocks, of `threads` threads that each own up to `maxu`
+// octets (8 consecutive elements; the two octets of a block sit in adjacent lanes).
+// Depends on the row length only, so every kernel reducing rows of one length rounds alike.
 struct RowSplit {
   int ctas, threads, maxu;
 };
@@ -101,16 +103,16 @@ inline RowSplit row_split(int units) {
   RowSplit s;
   s.ctas = units / 32;
   s.ctas = s.ctas < 1 ? 1 : s.ctas > MAX_CLUSTER ? MAX_CLUSTER : s.ctas;
-  const int per = (units + s.ctas - 1) / s.ctas;
-  s.threads = ((per + 31) / 32) * 32;
-  if (s.threads > 256) s.threads = 256;
-  const int mu = (per + s.threads - 1) / s.threads;
+  const int octets = 2 * ((units + s.ctas - 1) / s.ctas);
+  s.threads = ((octets + 31) / 32) * 32;
+  if (s.threads > 512) s.threads = 512;
+  const int mu = (octets + s.threads - 1) / s.threads;
   s.maxu = mu <= 1 ? 1 : mu <= 2 ? 2 : mu <= 4 ? 4 : mu <= 8 ? 8 : 0;  // 0: row too long
   return s;
 }
-// Units [u0, u1) of CTA `rank` out of `ctas`.
-__host__ __device__ __forceinline__ int slice_begin(int units, int rank, int ctas) {
-  return (int)(((int64_t)units * rank) / ctas);
+// First octet of CTA `rank`'s slice (slices are whole 16-element blocks).
+__host__ __device__ __forceinline__ int slice_octet(int units, int rank, int ctas) {
+  return 2 * (int)(((int64_t)units * rank) / ctas);
 }
 
 }  // namespace cl

@@ -135,6 +135,23 @@ __device__ __forceinline__ uint32_t f32x8_to_e2m1x8(const float* v) {
   return r;
 }
 
+// Eight e2m1 nibbles (element 0 in the low nibble) -> their exact values as four f16x2
+// (low half = even element).  Integer-only: one byte permute per pair picks the f16 high
+// byte of each magnitude {0, .5, 1, 1.5, 2, 3, 4, 6} = {00, 38, 3C, 3E, 40, 42, 44, 46}
+// (low bytes are zero, and table entry 0 supplies the zero low bytes), then the sign bits
+// are moved into place.
+__device__ __forceinline__ void e2m1x8_to_f16x8(uint32_t codes, uint32_t* h) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t c = codes >> (8 * p);
+    const uint32_t sel = ((c & 0x7u) << 4) | ((c & 0x70u) << 8);
+    const uint32_t sign = ((c & 0x8u) << 12) | ((c & 0x80u) << 24);
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(0x3E3C3800u), "r"(0x46444240u), "r"(sel));
+    h[p] = r | sign;
+  }
+}
+
 // 2^x via the SFU (ex2.approx); -inf -> 0.
 __device__ __forceinline__ float fast_exp2(float x) {
   float r;

@@ -22,83 +22,96 @@ namespace ada {
 namespace fused {
 
 template <typename T>
-__device__ __forceinline__ void load16(const T* p, float* f) {
-  unpack8<T>(*reinterpret_cast<const uint4*>(p), f);
-  unpack8<T>(*reinterpret_cast<const uint4*>(p + 8), f + 8);
-}
-template <typename T>
-__device__ __forceinline__ void store16(T* p, const float* f) {
-  *reinterpret_cast<uint4*>(p) = pack8<T>(f);
-  *reinterpret_cast<uint4*>(p + 8) = pack8<T>(f + 8);
-}
-template <typename T>
 __device__ __forceinline__ float round_to(float v) {
   return to_f32(from_f32<T>(v));
 }
 
-// Unit `u` of this thread (u < MAXU) in the CTA's slice [u0, u1), or -1.
-__device__ __forceinline__ int my_unit(int u, int u0, int u1) {
-  const int b = u0 + (int)threadIdx.x + u * (int)blockDim.x;
-  return b < u1 ? b : -1;
+// Octet `u` of this thread (u < MAXU) in the CTA's slice [o0, o1), or -1.
+__device__ __forceinline__ int my_oct(int u, int o0, int o1) {
+  const int o = o0 + (int)threadIdx.x + u * (int)blockDim.x;
+  return o < o1 ? o : -1;
+}
+__device__ __forceinline__ void slice_of(int k, int& o0, int& o1) {
+  o0 = cl::slice_octet(k >> 4, blockIdx.x, gridDim.x);
+  o1 = cl::slice_octet(k >> 4, blockIdx.x + 1, gridDim.x);
 }
 
-// Quantise the slice held in v once the row amax is known; rank 0 records the row scale.
+// Quantise the slice held in v once the row amax is known; CTA 0 records the row scale.
+// Every thread calls it (terms == 1 pairs lanes of a warp).
 template <int MAXU>
-__device__ __forceinline__ void quant_slice(const q::QuantDst& dst, int m, float (&v)[MAXU][16], int u0, int u1,
+__device__ __forceinline__ void quant_slice(const q::QuantDst& dst, int m, float (&v)[MAXU][8], int o0, int o1,
                                             float amax) {
   const q::RowQ rq = q::make_rowq(amax, dst.terms);
   if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[m] = rq.g[0];
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = my_unit(u, u0, u1);
-    if (b >= 0) q::quant_unit(dst, m, b, v[u], rq);
+    const int o = my_oct(u, o0, o1);
+    q::quant_oct(dst, m, o < 0 ? 0 : o, v[u], rq, o >= 0);
   }
 }
 // Padding token of the last token tile: zero codes, unit scale.
-__device__ __forceinline__ void zero_slice(const q::QuantDst& dst, int m, int u0, int u1) {
-  for (int b = u0 + (int)threadIdx.x; b < u1; b += blockDim.x) q::zero_unit(dst, m, b);
+__device__ __forceinline__ void zero_slice(const q::QuantDst& dst, int m, int o0, int o1) {
+  for (int o = o0 + (int)threadIdx.x; o < o1; o += blockDim.x) q::zero_oct(dst, m, o);
   if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[m] = 1.f;
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* f) {
+  unpack8<T>(*reinterpret_cast<const uint4*>(p), f);
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* f) {
+  *reinterpret_cast<uint4*>(p) = pack8<T>(f);
 }
 
 // grid (ctas, m_pad), cluster (ctas, 1, 1).  dst.xq == null: plain RMSNorm (ada_rmsnorm).
 template <typename T, int MAXU>
-__global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const T* __restrict__ x, int64_t ldx, const T* res,
+__global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict__ x, int64_t ldx, const T* res,
                                                             int64_t ldr, T* res_out, int64_t ldro,
                                                             const T* __restrict__ w, T* y, int64_t ldy, int rows,
                                                             int hidden, float eps, int gemma, q::QuantDst dst) {
   cl::cluster_arrive_relaxed();
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float red[8];
+  __shared__ float red[cl::MAX_WARPS];
   __shared__ float slots[2][cl::MAX_CLUSTER];
   const int m = blockIdx.y;
-  const int nblk = hidden >> 4;
-  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
+  int o0, o1;
+  slice_of(hidden, o0, o1);
   const bool quant = dst.xq != nullptr;
+  float wf[MAXU][8];  // the norm weight never depends on the previous kernel: load it first
+#pragma unroll
+  for (int u = 0; u < MAXU; ++u) {
+    const int o = my_oct(u, o0, o1);
+    if (o >= 0 && m < rows) load8<T>(w + o * 8, wf[u]);
+  }
+  pdl_wait();
+  pdl_trigger();
   if (m >= rows) {
-    if (quant) zero_slice(dst, m, u0, u1);
+    if (quant) zero_slice(dst, m, o0, o1);
     cl::cluster_wait();
     return;
   }
-  float v[MAXU][16];
+  float v[MAXU][8];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = my_unit(u, u0, u1);
-    if (b >= 0) {
-      load16<T>(x + (int64_t)m * ldx + b * 16, v[u]);
+    const int o = my_oct(u, o0, o1);
+    if (o >= 0) {
+      load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
       if (res) {
-        float r[16];
-        load16<T>(res + (int64_t)m * ldr + b * 16, r);
+        float r[8];
+        load8<T>(res + (int64_t)m * ldr + o * 8, r);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 8; ++i) {
           v[u][i] = __fadd_rn(v[u][i], r[i]);
           if (gemma && std::is_same<T, __nv_bfloat16>::value) v[u][i] = round_to<T>(v[u][i]);
         }
-        store16<T>(res_out + (int64_t)m * ldro + b * 16, v[u]);
+        store8<T>(res_out + (int64_t)m * ldro + o * 8, v[u]);
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) ss = fmaf(v[u][i], v[u][i], ss);
+      for (int i = 0; i < 8; ++i) ss = fmaf(v[u][i], v[u][i], ss);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     }
   }
   cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
@@ -106,25 +119,24 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const T* __restrict_
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = my_unit(u, u0, u1);
-    if (b >= 0) {
-      float wf[16];
-      load16<T>(w + b * 16, wf);
+    const int o = my_oct(u, o0, o1);
+    if (o >= 0) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const float xn = __fmul_rn(v[u][i], rs);
-        v[u][i] = gemma ? round_to<T>(__fmul_rn(xn, __fadd_rn(1.f, wf[i])))
-                        : round_to<T>(__fmul_rn(round_to<T>(xn), wf[i]));
+        v[u][i] = gemma ? round_to<T>(__fmul_rn(xn, __fadd_rn(1.f, wf[u][i])))
+                        : round_to<T>(__fmul_rn(round_to<T>(xn), wf[u][i]));
         amax = fmaxf(amax, fabsf(v[u][i]));
       }
-      if (y) store16<T>(y + (int64_t)m * ldy + b * 16, v[u]);
+      if (y) store8<T>(y + (int64_t)m * ldy + o * 8, v[u]);
     }
   }
   if (!quant) return;
-  quant_slice<MAXU>(dst, m, v, u0, u1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots[1]));
+  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots[1]));
 }
 
-__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.f, expf(-x))); }
+// SiLU with the hardware exponential (within 2 ulp of fp32 before the bf16 rounding).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
   const float inner = k0 * (x + k1 * x * x * x);
@@ -133,73 +145,79 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 
 // grid (ctas, m_pad), cluster (ctas, 1, 1).
 template <typename T, int MAXU>
-__global__ void __launch_bounds__(256) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y, int64_t ldy,
+__global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y, int64_t ldy,
                                                               int rows, int inter, int act, q::QuantDst dst) {
   cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[8];
+  __shared__ float red[cl::MAX_WARPS];
   __shared__ float slots[cl::MAX_CLUSTER];
   const int m = blockIdx.y;
-  const int nblk = inter >> 4;
-  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
+  int o0, o1;
+  slice_of(inter, o0, o1);
   if (m >= rows) {
-    zero_slice(dst, m, u0, u1);
+    zero_slice(dst, m, o0, o1);
     cl::cluster_wait();
     return;
   }
-  float v[MAXU][16];
+  float v[MAXU][8];
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = my_unit(u, u0, u1);
-    if (b >= 0) {
-      float gt[16], up[16];
-      load16<T>(x + (int64_t)m * ldx + b * 16, gt);
-      load16<T>(x + (int64_t)m * ldx + inter + b * 16, up);
+    const int o = my_oct(u, o0, o1);
+    if (o >= 0) {
+      float gt[8], up[8];
+      load8<T>(x + (int64_t)m * ldx + o * 8, gt);
+      load8<T>(x + (int64_t)m * ldx + inter + o * 8, up);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const float a = act == 0 ? silu_f(gt[i]) : gelu_tanh_f(gt[i]);
         v[u][i] = round_to<T>(__fmul_rn(round_to<T>(a), up[i]));
         amax = fmaxf(amax, fabsf(v[u][i]));
       }
-      if (y) store16<T>(y + (int64_t)m * ldy + b * 16, v[u]);
+      if (y) store8<T>(y + (int64_t)m * ldy + o * 8, v[u]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     }
   }
   cl::cluster_wait();
-  quant_slice<MAXU>(dst, m, v, u0, u1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
+  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
 }
 
 // grid (ctas, m_pad), cluster (ctas, 1, 1).
 template <typename T, int MAXU>
-__global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x, int64_t ldx, int rows, int k,
+__global__ void __launch_bounds__(512) act_quant_kernel(const T* __restrict__ x, int64_t ldx, int rows, int k,
                                                         q::QuantDst dst) {
   cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[8];
+  __shared__ float red[cl::MAX_WARPS];
   __shared__ float slots[cl::MAX_CLUSTER];
   const int m = blockIdx.y;
-  const int nblk = k >> 4;
-  const int u0 = cl::slice_begin(nblk, blockIdx.x, gridDim.x), u1 = cl::slice_begin(nblk, blockIdx.x + 1, gridDim.x);
+  int o0, o1;
+  slice_of(k, o0, o1);
   if (m >= rows) {
-    zero_slice(dst, m, u0, u1);
+    zero_slice(dst, m, o0, o1);
     cl::cluster_wait();
     return;
   }
-  float v[MAXU][16];
+  float v[MAXU][8];
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
-    const int b = my_unit(u, u0, u1);
-    if (b >= 0) {
-      load16<T>(x + (int64_t)m * ldx + b * 16, v[u]);
+    const int o = my_oct(u, o0, o1);
+    if (o >= 0) {
+      load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     }
   }
   cl::cluster_wait();
-  quant_slice<MAXU>(dst, m, v, u0, u1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
+  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
 }
 
 static inline bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }

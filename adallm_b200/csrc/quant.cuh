@@ -35,11 +35,6 @@ struct QuantDst {
   int terms, bn, k;
 };
 
-__device__ __forceinline__ float e2m1_value(uint32_t c) {
-  const uint32_t mag = c & 7u;
-  float v = mag < 2u ? 0.5f * (float)mag : (float)(2u + (mag & 1u)) * __int_as_float((int)(((mag >> 1) + 125u) << 23));
-  return (c & 8u) ? -v : v;
-}
 __device__ __forceinline__ float e4m3_value(uint8_t b) {
   const uint32_t h = e4m3x2_to_f16x2((uint16_t)b);
   return __half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)));
@@ -83,52 +78,57 @@ __device__ __forceinline__ uint8_t* sf_byte(const QuantDst& d, int m, int blk) {
   return d.sfx + ((size_t)mt * (d.k >> 6) + (blk >> 2)) * 512 + (j & 31) * 16 + (j >> 5) * 4 + (blk & 3);
 }
 
-// Quantise the 16-element block `blk` of token m (r is clobbered for terms >= 2).
-__device__ __forceinline__ void quant_unit(const QuantDst& d, int m, int blk, float* r, const RowQ& q) {
+// Quantise the 8 elements r[0..8) of octet `oc` (elements 8*oc .. 8*oc+7) of token m
+// (r is clobbered for terms >= 2).  For terms == 1 the two octets of a 16-element block
+// are held by lanes l and l^1 of one warp, which share the block amax: every lane of the
+// warp calls this together; lanes with valid == false contribute zeros and store nothing.
+__device__ __forceinline__ void quant_oct(const QuantDst& d, int m, int oc, float* r, const RowQ& q, bool valid) {
   if (q.terms == 1) {
     float bamax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(r[i]));
+    for (int i = 0; i < 8; ++i) bamax = fmaxf(bamax, valid ? fabsf(r[i]) : 0.f);
+    bamax = fmaxf(bamax, __shfl_xor_sync(0xffffffffu, bamax, 1));
     const uint8_t sb = (uint8_t)(f32x2_to_e4m3x2(__fdiv_rn(bamax, q.g[1]), 0.f) & 0xFFu);
     const float sv = e4m3_value(sb);
-    uint2 codes = make_uint2(0, 0);
+    uint32_t codes = 0;
     if (sv > 0.f) {
       const float rcp = __fdiv_rn(1.f, __fmul_rn(sv, q.g[0]));
-      float v[16];
+      float v[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(r[i], rcp);
-      codes.x = f32x8_to_e2m1x8(v);
-      codes.y = f32x8_to_e2m1x8(v + 8);
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(r[i], rcp);
+      codes = f32x8_to_e2m1x8(v);
     }
-    *reinterpret_cast<uint2*>(xq_row(d, m, 0) + (size_t)blk * 8) = codes;
-    *sf_byte(d, m, blk) = sb;
+    if (valid) {
+      *reinterpret_cast<uint32_t*>(xq_row(d, m, 0) + (size_t)oc * 4) = codes;
+      if (!(oc & 1)) *sf_byte(d, m, oc >> 1) = sb;
+    }
     return;
   }
 #pragma unroll
   for (int t = 0; t < MAX_TERMS; ++t) {
     if (t < q.terms) {
-      float v[16];
+      float v[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(r[i], q.rcp[t]);
-      uint2 codes;
-      codes.x = f32x8_to_e2m1x8(v);
-      codes.y = f32x8_to_e2m1x8(v + 8);
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(r[i], q.rcp[t]);
+      const uint32_t codes = f32x8_to_e2m1x8(v);
       if (t + 1 < q.terms) {
+        uint32_t h[4];
+        e2m1x8_to_f16x8(codes, h);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t c = ((i < 8 ? codes.x : codes.y) >> (4 * (i & 7))) & 0xFu;
-          r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(c), q.g[t]));
+        for (int i = 0; i < 8; ++i) {
+          const uint16_t hb = (uint16_t)(h[i >> 1] >> (16 * (i & 1)));
+          r[i] = __fsub_rn(r[i], __fmul_rn(__half2float(__ushort_as_half(hb)), q.g[t]));
         }
       }
-      *reinterpret_cast<uint2*>(xq_row(d, m, t) + (size_t)blk * 8) = codes;
+      if (valid) *reinterpret_cast<uint32_t*>(xq_row(d, m, t) + (size_t)oc * 4) = codes;
     }
   }
 }
 
 // Codes (and block scales) of a padding token m in [M, m_pad): zero.
-__device__ __forceinline__ void zero_unit(const QuantDst& d, int m, int blk) {
-  for (int t = 0; t < d.terms; ++t) *reinterpret_cast<uint2*>(xq_row(d, m, t) + (size_t)blk * 8) = make_uint2(0, 0);
-  if (d.terms == 1) *sf_byte(d, m, blk) = 0;
+__device__ __forceinline__ void zero_oct(const QuantDst& d, int m, int oc) {
+  for (int t = 0; t < d.terms; ++t) *reinterpret_cast<uint32_t*>(xq_row(d, m, t) + (size_t)oc * 4) = 0u;
+  if (d.terms == 1 && !(oc & 1)) *sf_byte(d, m, oc >> 1) = 0;
 }
 
 // Valid operand configuration: terms 1..8, token tile 16/32/64/128 with terms*bn <= 128,
