@@ -387,6 +387,73 @@ static void stages_dispatch(int bn, int t, int ks, int rows_max, int& stages, ui
   stages = 0;
 }
 
+// Raise the kernel's dynamic shared memory limit to `smem` (never lowers it) and prefer the
+// maximum shared-memory carveout.
+template <int BN, int T>
+static bool ensure_smem(size_t smem) {
+  static size_t configured[64] = {0};  // per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (smem <= configured[dev]) return true;
+  if (cudaFuncSetAttribute(gemm_kernel<BN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return false;
+  // The whole unified L1/shared array as shared memory, so two ~100 KB CTAs fit on one SM
+  // (the default carveout leaves room for one).
+  if (cudaFuncSetAttribute(gemm_kernel<BN, T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return false;
+  configured[dev] = smem;
+  return true;
+}
+
+// Stand-in for gemm_kernel in occupancy queries: same block size, register cap and dynamic
+// shared memory, but no TMEM allocation.  The occupancy calculator assumes one CTA per SM for
+// kernels that allocate TMEM, while the hardware co-schedules two of these CTAs per SM
+// (measured), so cluster capacity is queried on this twin instead.
+__global__ void __launch_bounds__(192, 2) occupancy_twin() {}
+
+// Clusters of `ks` CTAs (with the shared memory the plan gives them) that fit on the GPU at
+// once; 0 if unknown.  A split whose clusters do not all fit runs in two waves.
+template <int BN, int T>
+static int active_clusters(int ks) {
+  static int cache[64][MAX_KS + 1] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || ks < 1 || ks > MAX_KS) return 0;
+  if (cache[dev][ks]) return cache[dev][ks] > 0 ? cache[dev][ks] : 0;
+  int stages = 0;
+  uint32_t cols = 0;
+  size_t smem = 0;
+  stages_for<BN, T>(ks, (int)cdiv(BM, ks), stages, cols, smem);
+  int n = 0;
+  if (stages >= 2 &&
+      cudaFuncSetAttribute(occupancy_twin, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
+      cudaFuncSetAttribute(occupancy_twin, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ks, 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, occupancy_twin, &cfg) != cudaSuccess) n = 0;
+  }
+  (void)cudaGetLastError();
+  cache[dev][ks] = n > 0 ? n : -1;
+  return n;
+}
+
+static int active_clusters_dispatch(int bn, int t, int ks) {
+#define ADA_AC(B, TT) if (bn == B && t == TT) return active_clusters<B, TT>(ks);
+  ADA_FP4_CONFIGS(ADA_AC)
+#undef ADA_AC
+  return 0;
+}
+
 static int num_sms() {
   static int cache[64] = {0};
   int dev = 0;
@@ -412,10 +479,22 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   P.nkt = (int)(k / KT);
   const int64_t tiles = (int64_t)P.n_tiles * P.m_tiles;
   if (tiles > 65535) return ADA_ERR_UNSUPPORTED;
-  int64_t ks = force_ks > 0 ? force_ks : (2 * (int64_t)num_sms()) / tiles;
-  if (ks > MAX_KS) ks = MAX_KS;
-  if (ks > P.nkt) ks = P.nkt;
-  if (ks < 1) ks = 1;
+  // Split-K factor: the largest ks <= 8 that divides the K steps evenly, leaves every CTA at
+  // least 4 of them (shorter splits cost more in the cluster reduction than they gain), and
+  // whose clusters (one per tile) all fit on the GPU in one wave, at most two CTAs per SM.
+  int64_t ks = 1;
+  const int64_t ks_cap = P.nkt < MAX_KS ? P.nkt : MAX_KS;
+  if (force_ks > 0) {
+    ks = force_ks < ks_cap ? force_ks : ks_cap;
+  } else {
+    for (int64_t c = (P.nkt / 4 < ks_cap ? P.nkt / 4 : ks_cap); c >= 2; --c) {
+      if (P.nkt % c || tiles * c > 2 * (int64_t)num_sms()) continue;
+      if (tiles <= active_clusters_dispatch(P.bn, terms, (int)c)) {
+        ks = c;
+        break;
+      }
+    }
+  }
   P.ks = (int)ks;
   P.rows_max = (int)cdiv(BM, ks);
   uint32_t cols = 0;
@@ -437,12 +516,7 @@ template <int BN, int T>
 static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmParams& gp, const Plan& P,
                        cudaStream_t st) {
   auto kern = gemm_kernel<BN, T>;
-  static size_t configured = 0;  // per instantiation
-  if (P.smem > configured) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem) != cudaSuccess)
-      return ADA_ERR_CUDA;
-    configured = P.smem;
-  }
+  if (!ensure_smem<BN, T>(P.smem)) return ADA_ERR_CUDA;
   const dim3 grid((unsigned)P.ks, (unsigned)(P.n_tiles * P.m_tiles));
   if (P.ks > 1)
     (void)ada::launch_kc(kern, grid, dim3(192), P.smem, st, P.ks, tmw, tmx, gp);
