@@ -111,6 +111,59 @@ def random_nvfp4(n: int, k: int, seed: int, device) -> tuple[torch.Tensor, torch
     return packed, scale, scale_2
 
 
+def sharded_nvfp4(seed: int, kind: str, layer: int, parts: list[tuple[str, int]], k_full: int, split_k: bool,
+                  tp_size: int, tp_rank: int, device) -> tuple[torch.Tensor, torch.Tensor, float]:
+    """This rank's shard of a (possibly fused) random NVFP4 linear, in the reference layout.
+
+    parts: [(name, full_rows)], each generated whole from its own seed and sharded per rank,
+    then concatenated like QKVParallelLinear / MergedColumnParallelLinear
+    (adallm/ops/linear.py:138-191); split_k shards K like RowParallelLinear
+    (adallm/ops/linear.py:193-209).  One fp32 global scale per fused linear (the loader keeps
+    the last shard's, adallm/infra/loader.py:103-115; here all parts share it)."""
+    packs, scales = [], []
+    scale_2 = None
+    for name, rows in parts:
+        packed, scale, s2 = random_nvfp4(rows, k_full, stable_seed(seed, kind, layer, name), device)
+        scale_2 = s2 if scale_2 is None else scale_2
+        if split_k:
+            kk = k_full // tp_size
+            packed = packed[:, tp_rank * kk // 2:(tp_rank + 1) * kk // 2]
+            scale = scale[:, tp_rank * kk // 16:(tp_rank + 1) * kk // 16]
+        else:
+            r = rows // tp_size
+            packed = packed[tp_rank * r:(tp_rank + 1) * r]
+            scale = scale[tp_rank * r:(tp_rank + 1) * r]
+        packs.append(packed.contiguous())
+        scales.append(scale.contiguous())
+    return torch.cat(packs).contiguous(), torch.cat(scales).contiguous(), scale_2
+
+
+def fill_rows(out: torch.Tensor, seed: int, name: str, row0: int, chunk: int = 4096) -> None:
+    """Rows [row0, row0 + len(out)) of a random bf16 table N(0, 0.02), generated in fixed chunks so
+    that a vocab shard equals the same rows of the full table on every rank."""
+    rows = out.shape[0]
+    for ci in range(row0 // chunk, (row0 + rows - 1) // chunk + 1):
+        g = _gen(stable_seed(seed, name, ci), out.device)
+        blk = (torch.randn((chunk, out.shape[1]), generator=g, device=out.device) * 0.02).to(torch.bfloat16)
+        lo = max(row0, ci * chunk)
+        hi = min(row0 + rows, (ci + 1) * chunk)
+        out[lo - row0:hi - row0] = blk[lo - ci * chunk:hi - ci * chunk]
+
+
+def vocab_parallel_pick(local_max: torch.Tensor, local_idx: torch.Tensor, tp_rank: int, vocab_shard: int,
+                        tp_size: int, group=None) -> torch.Tensor:
+    """Greedy token over a vocab-parallel lm_head (adallm/ops/embed_head.py:56-66 gathers the
+    logits instead): all-gather each rank's (max logit, global index) and take the first global
+    maximum, i.e. torch.argmax over the full vocabulary.  Returns int64 [B]."""
+    pair = torch.stack([local_max.float(), (local_idx + tp_rank * vocab_shard).float()], 1)
+    allp = [torch.empty_like(pair) for _ in range(tp_size)]
+    dist.all_gather(allp, pair, group=group)
+    vals = torch.stack([p[:, 0] for p in allp], 1)
+    idx = torch.stack([p[:, 1] for p in allp], 1)
+    best = vals.argmax(dim=1, keepdim=True)  # ties: the lower rank, i.e. the lower index
+    return idx.gather(1, best).view(-1).to(torch.int64)
+
+
 class Qwen3DecodeEngine:
     """Static-shape decode engine for batch ``max_batch`` (graph-capturable)."""
 
@@ -128,31 +181,10 @@ class Qwen3DecodeEngine:
 
     # ------------------------------------------------------------------ weights
     def _sharded(self, kind: str, layer: int, parts: list[tuple[str, int]], k_full: int, split_k: bool) -> NVFP4Weight:
-        """Build this rank's shard of a (possibly fused) NVFP4 linear.
-
-        parts: [(name, full_rows)], concatenated per rank like QKVParallelLinear /
-        MergedColumnParallelLinear (adallm/ops/linear.py:138-191); split_k shards the
-        K dimension like RowParallelLinear (adallm/ops/linear.py:193-209)."""
         c = self.cfg
-        d = self.device
-        packs, scales = [], []
-        scale_2 = None
-        for pi, (name, rows) in enumerate(parts):
-            seed = stable_seed(self.seed, kind, layer, name)
-            packed, scale, s2 = random_nvfp4(rows, k_full, seed, d)
-            scale_2 = s2 if scale_2 is None else scale_2  # one global scale per fused linear
-            if split_k:
-                kk = k_full // c.tp_size
-                packed = packed[:, c.tp_rank * kk // 2:(c.tp_rank + 1) * kk // 2]
-                scale = scale[:, c.tp_rank * kk // 16:(c.tp_rank + 1) * kk // 16]
-            else:
-                r = rows // c.tp_size
-                packed = packed[c.tp_rank * r:(c.tp_rank + 1) * r]
-                scale = scale[c.tp_rank * r:(c.tp_rank + 1) * r]
-            packs.append(packed.contiguous())
-            scales.append(scale.contiguous())
-        w = NVFP4Weight(torch.cat(packs).contiguous(), torch.cat(scales).contiguous(),
-                        torch.tensor(scale_2, dtype=torch.float32, device=d))
+        packed, scale, scale_2 = sharded_nvfp4(self.seed, kind, layer, parts, k_full, split_k, c.tp_size, c.tp_rank,
+                                               self.device)
+        w = NVFP4Weight(packed, scale, torch.tensor(scale_2, dtype=torch.float32, device=self.device))
         w.sf = prepack_scales(w.scale, w.n, w.k)
         return w
 
@@ -186,16 +218,8 @@ class Qwen3DecodeEngine:
         from .rotary_embedding import build_cos_sin_cache
         self.cos_sin = build_cos_sin_cache(D, c.max_position, c.rope_theta, None, d).contiguous()
 
-    def _fill_rows(self, out: torch.Tensor, name: str, row0: int, chunk: int = 4096):
-        rows = out.shape[0]
-        first = row0 // chunk
-        last = (row0 + rows - 1) // chunk
-        for ci in range(first, last + 1):
-            g = _gen(stable_seed(self.seed, name, ci), self.device)
-            blk = (torch.randn((chunk, out.shape[1]), generator=g, device=self.device) * 0.02).to(torch.bfloat16)
-            lo = max(row0, ci * chunk)
-            hi = min(row0 + rows, (ci + 1) * chunk)
-            out[lo - row0:hi - row0] = blk[lo - ci * chunk:hi - ci * chunk]
+    def _fill_rows(self, out: torch.Tensor, name: str, row0: int):
+        fill_rows(out, self.seed, name, row0)
 
     # ------------------------------------------------------------------ state
     def _alloc_state(self):
@@ -382,15 +406,9 @@ class Qwen3DecodeEngine:
                                    self.next_tokens.data_ptr(), self.argmax_ws.data_ptr(), self.argmax_ws.numel(),
                                    stream), "argmax")
         if c.tp_size > 1:
-            # vocab-parallel greedy pick: gather (max, index) per rank, take the first global maximum
             loc = self.logits.float().gather(1, self.next_tokens.view(-1, 1)).view(-1)
-            pair = torch.stack([loc, (self.next_tokens + c.tp_rank * c.vocab_shard).float()], 1)
-            allp = [torch.empty_like(pair) for _ in range(c.tp_size)]
-            dist.all_gather(allp, pair, group=self.group)
-            vals = torch.stack([p[:, 0] for p in allp], 1)
-            idx = torch.stack([p[:, 1] for p in allp], 1)
-            best = vals.argmax(dim=1, keepdim=True)
-            self.next_tokens.copy_(idx.gather(1, best).view(-1).to(torch.int64))
+            self.next_tokens.copy_(vocab_parallel_pick(loc, self.next_tokens, c.tp_rank, c.vocab_shard, c.tp_size,
+                                                       self.group))
 
     # ------------------------------------------------------------------ graphs
     def advance(self):

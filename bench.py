@@ -144,6 +144,80 @@ def cpu_baseline(args, ctx):
                        f"{args.layers} layers; setup {setup:.0f} s untimed")}
 
 
+def kernel_benches(dev, peak):
+    """The two kernels BASELINE's metric quotes besides the decode step, each on its own,
+    cold-cache (a 256 MiB buffer is written between timed launches; only the launch is
+    timed), CUDA events on the launching stream:
+      * config 0: NVFP4 linear x bf16 [16, 4096] . W [12288, 4096] (act-quant + GEMM, the
+        drop-in nvfp4_linear) -- algorithmic bytes W 25,165,824 + e4m3 scales 3,145,728 +
+        x 131,072 + y 393,216 + 4;
+      * config 1: FP8 paged decode attention B16 Hq32 Hkv8 D128, ctx ~ U[512, 8192], page 16,
+        seeded random page permutation (split + merge kernels) -- algorithmic bytes
+        2*sum(ctx)*Hkv*D (e4m3 K and V) + q + out + 4*sum(pages) + 4*B."""
+    import torch
+    from adallm_b200.attention import paged_decode, paged_decode_workspace_bytes
+    from adallm_b200.decode_step import random_nvfp4
+    from adallm_b200.nvfp4_gemm import nvfp4_linear, prepack_scales, workspace_bytes
+
+    st = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts) * 1e3  # us
+
+    out = {}
+    m, n, k = 16, 12288, 4096
+    packed, scale, s2 = random_nvfp4(n, k, 4242, dev)
+    sf = prepack_scales(scale, n, k)
+    g2 = torch.tensor(s2, dtype=torch.float32, device=dev)
+    x = torch.randn((m, k), device=dev, dtype=torch.bfloat16)
+    y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+    ws = torch.zeros(workspace_bytes(m, n, k, 4), dtype=torch.uint8, device=dev)
+    us = timed(lambda: nvfp4_linear(x, packed, scale, g2, None, None, 16, terms=4, sf=sf, out=y, workspace=ws))
+    nb = n * k // 2 + n * k // 16 + m * k * 2 + m * n * 2 + 4
+    out["gemm_config0"] = {"us": round(us, 2), "alg_bytes": nb, "gbs": round(nb / us / 1e3, 1),
+                           "frac": round(nb / us / 1e3 / peak, 4), "launches": 2,
+                           "tflops": round(2 * m * n * k / us / 1e6, 2)}
+    del packed, scale, sf, x, y, ws
+
+    g = torch.Generator().manual_seed(0)
+    B, hq, hkv, D, page = 16, 32, 8, 128, 16
+    ctx = torch.randint(512, 8193, (B,), generator=g, dtype=torch.int32)
+    pages = [(int(c) + page - 1) // page for c in ctx]
+    pool = sum(pages)
+    perm = torch.randperm(pool, generator=g).to(torch.int32)
+    bt = torch.full((B, max(pages)), -1, dtype=torch.int32)
+    o = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[o:o + pages[b]]
+        o += pages[b]
+    kc = torch.randn((pool, page, hkv, D), device=dev, dtype=torch.bfloat16).to(torch.float8_e4m3fn)
+    vc = torch.randn((pool, page, hkv, D), device=dev, dtype=torch.bfloat16).to(torch.float8_e4m3fn)
+    q = torch.randn((B, hq, D), device=dev, dtype=torch.bfloat16)
+    bt_d, ctx_d = bt.to(dev), ctx.to(dev)
+    o_buf = torch.empty_like(q)
+    aws = torch.empty(paged_decode_workspace_bytes(B, hq, bt.shape[1], page, D), dtype=torch.uint8, device=dev)
+    us = timed(lambda: paged_decode(q, kc, vc, bt_d, ctx_d, D ** -0.5, out=o_buf, workspace=aws))
+    sctx = int(ctx.sum())
+    nb = 2 * sctx * hkv * D + 2 * q.numel() * 2 + 4 * pool + 4 * B
+    out["attention_config1"] = {"us": round(us, 2), "alg_bytes": nb, "gbs": round(nb / us / 1e3, 1),
+                                "frac": round(nb / us / 1e3 / peak, 4), "launches": 2, "sum_ctx": sctx}
+    del kc, vc, flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args, rank):
     """The reference's CPU path (oracle restatement) on the host cores: rank 0 only."""
     if rank != 0:
@@ -333,6 +407,8 @@ def run_ours(args, rank, world, local_rank):
                 "alg_bytes_per_launch": int(alg_bytes), "us_per_launch": round(gemm_ms * 1e3, 3),
                 "launch_mix": "qkv/o/gate_up/down of all layers, batch 16", "per_shape": per_shape}
 
+    kernels = kernel_benches(dev, peak) if rank == 0 and world == 1 else None
+
     ctx_end = int(sess.lens.max().item())
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -346,6 +422,7 @@ def run_ours(args, rank, world, local_rank):
                            "parallelism": f"tp{world}", "layers": cfg.num_layers, "nvfp4_act_terms": cfg.terms,
                            "l2": "inputs larger than L2 (every step streams ~5.2 GB of weights at tp1)"},
                 "roofline": roofline,
+                "kernels": kernels,
                 "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s",
                         "h2d_bytes_per_step": sess.H2D_BYTES_PER_STEP, "d2h_bytes_per_step": sess.D2H_BYTES_PER_STEP,
