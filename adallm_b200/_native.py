@@ -53,6 +53,7 @@ _SIGS = {
     "ada_embedding": (INT, [P, I64, P, I64, I64, I32, P, INT, P]),
     "ada_argmax_workspace_size": (SZ, [I64, I64]),
     "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P, SZ, P]),
+    "ada_argmax_noalloc": (INT, [P, I64, I64, I64, INT, P, P]),
     "ada_nvfp4_sf_bytes": (SZ, [I64, I64]),
     "ada_nvfp4_prepack_scales": (INT, [P, INT, I64, I64, I64, P, P]),
     "ada_nvfp4_linear_workspace_size": (SZ, [I64, I64, I64, INT]),

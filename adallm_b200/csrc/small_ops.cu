@@ -588,6 +588,65 @@ extern "C" int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t 
   return ADA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Greedy argmax without a caller workspace.  For callers that cannot allocate device
+// memory where they sample: a host runtime that binds this C ABI directly (no caching
+// allocator) and launches into work it is recording, where cudaMalloc is not allowed.
+// The two stages exchange their per-chunk partials through this file-scope scratch instead.
+// Limit: rows * chunks(cols) * 12 + 16 <= ADA_ARGMAX_SCRATCH_BYTES (256 KiB; the Qwen3 vocab
+// of 151936 splits into 75 chunks, so up to 291 rows).  Nothing in it needs to start at zero:
+// stage 1 writes every (row, chunk) slot before stage 2 reads it.  One scratch per device:
+// calls that overlap in time on one device (different streams, or host threads) race.
+#define ADA_ARGMAX_SCRATCH_BYTES (256u * 1024u)
+static __device__ __align__(256) unsigned char g_argmax_scratch[ADA_ARGMAX_SCRATCH_BYTES];
+
+// Device address of g_argmax_scratch for the current device, looked up once per device (the
+// first call on each device; make it before capturing launches into a graph).
+static int argmax_scratch(void** ptr) {
+  static void* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || !p) {
+      (void)cudaGetLastError();
+      return ADA_ERR_CUDA;
+    }
+    cache[dev] = p;
+  }
+  *ptr = cache[dev];
+  return ADA_OK;
+}
+
+extern "C" int ada_argmax_noalloc(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
+                                  int64_t* out, void* stream) {
+  if (rows < 0 || cols <= 0 || ld < cols) return ADA_ERR_INVALID_ARG;
+  if (rows == 0) return ADA_OK;
+  if (!logits || !out) return ADA_ERR_INVALID_ARG;
+  if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  if (rows > 65535) return ADA_ERR_UNSUPPORTED;
+  if (ada_argmax_workspace_size(rows, cols) > ADA_ARGMAX_SCRATCH_BYTES) return ADA_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int rc = argmax_scratch(&scratch);
+  if (rc != ADA_OK) return rc;
+  const int chunks = small::argmax_chunks(cols);
+  const int64_t chunk = ((cols + chunks - 1) / chunks + 7) & ~int64_t(7);
+  int64_t* pi = reinterpret_cast<int64_t*>(scratch);
+  float* pv = reinterpret_cast<float*>(pi + rows * chunks);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 g1(chunks, (unsigned)rows);
+  if (dtype == ADA_DT_BF16)
+    (void)ada::launch_k(small::argmax_stage1<__nv_bfloat16>, g1, dim3(256), 0, st, (const __nv_bfloat16*)logits, ld,
+                        cols, chunk, pv, pi);
+  else
+    (void)ada::launch_k(small::argmax_stage1<__half>, g1, dim3(256), 0, st, (const __half*)logits, ld, cols, chunk, pv,
+                        pi);
+  ADA_CHECK_LAUNCH();
+  (void)ada::launch_k(small::argmax_stage2, dim3((unsigned)rows), dim3(32), 0, st, pv, pi, chunks, out);
+  ADA_CHECK_LAUNCH();
+  return ADA_OK;
+}
+
 extern "C" const char* ada_status_string(int status) {
   switch (status) {
     case ADA_OK: return "ok";

@@ -261,6 +261,16 @@ ADA_API int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t
 ADA_API size_t ada_argmax_workspace_size(int64_t rows, int64_t cols);
 ADA_API int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
                        int64_t* out, void* workspace, size_t workspace_bytes, void* stream);
+/* ada_argmax without a caller workspace: no counterpart in the reference (its sampler runs
+ * torch.argmax).  For callers that cannot allocate device memory where they sample (a host
+ * runtime binding this ABI directly, launching into work it records, where cudaMalloc is not
+ * allowed).  Partials go through a 256 KiB scratch array inside the library:
+ * rows * chunks(cols) * 12 + 16 must be <= 256 KiB (ada_argmax_workspace_size(rows, cols);
+ * e.g. up to 291 rows of a 151936-entry vocabulary), else ADA_ERR_WORKSPACE.  The first call on
+ * each device looks up the scratch address (make it before recording launches).  Nothing needs
+ * to start at zero.  One scratch per device: calls overlapping in time on a device race. */
+ADA_API int ada_argmax_noalloc(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
+                               int64_t* out, void* stream);
 
 #ifdef __cplusplus
 }
