@@ -12,24 +12,27 @@
 //     (the reference reads past a page for pages < 64);
 //   * optional per-tensor k_scale / v_scale (1.0 reproduces the reference).
 //
-// Tile = 16 tokens of one page.  One warp computes S^T = K_tile . Q^T with
-// mma.m16n8k16 (tokens on M, heads on N), an online softmax per head, and
-// O^T += V_tile^T . P^T.  Every thread gathers its K and V bytes straight
-// from HBM with 16-byte loads: for the K operand the head dimension is
-// permuted so that thread (g, c) needs bytes [32c, 32c+32) of tokens g and
-// g+8 (the permutation is applied to Q identically); for the V operand the
-// output dimension is permuted so thread (g, c) needs bytes [16g, 16g+16) of
-// tokens 2c, 2c+1, 2c+8, 2c+9.  A warp therefore reads whole 128-byte rows.
+// Tile = 16 tokens of one page.  At start one thread issues a TMA load (4-D tensor map
+// over [pages][page][Hkv][D] bytes, 128-byte swizzle, one mbarrier per tile) of the K and
+// V rows of every tile of the CTA's 256-token chunk: the whole 64 KB chunk is in flight
+// at once, gathered page by page through the block table.  Warps take tiles round-robin
+// as they land.  One warp computes S^T = K_tile . Q^T with mma.m16n8k16 (tokens on M,
+// heads on N), an online softmax per head, and O^T += V_tile^T . P^T.  For the K operand
+// the head dimension is permuted so that thread (g, c) needs bytes [32c, 32c+32) of tokens
+// g and g+8 (the permutation is applied to Q identically); for the V operand the output
+// dimension is permuted so thread (g, c) needs bytes [16g, 16g+16) of tokens 2c, 2c+1,
+// 2c+8, 2c+9: 16-byte shared-memory reads, conflict-free through the swizzle.
 #include "cluster.cuh"
 #include "quant.cuh"
+#include "sm100.cuh"
 
 namespace ada {
 namespace attn {
 
 constexpr int D = 128;
-constexpr int WARPS = 4;
-constexpr int THREADS = WARPS * 32;
 constexpr int CHUNK = 256;  // tokens per split (CTA)
+constexpr int TILE = 16;
+constexpr int TILE_BYTES = TILE * D;  // one K (or V) tile: 16 rows x 128 bytes
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Params {
@@ -61,251 +64,349 @@ __device__ __forceinline__ void seq_range(const Params& P, int ctx, int& start, 
   nsplit = ctx > 0 ? min((ctx - start16 + CHUNK - 1) / CHUNK, P.max_splits) : 0;
 }
 
-struct TileRegs {
-  uint4 k0[2];  // token g,   bytes [32c, 32c+32)
-  uint4 k8[2];  // token g+8
-  uint4 v[4];   // tokens 2c, 2c+1, 2c+8, 2c+9, bytes [16g, 16g+16)
-  int block;
-};
-
-__device__ __forceinline__ void load_tile(const Params& P, int b, int kvh, int tile_t0, int ctx, int g, int c,
-                                          TileRegs& r) {
-  const int page_idx = tile_t0 / P.page;
-  const int row0 = tile_t0 - page_idx * P.page;
-  r.block = __ldg(P.bt + (int64_t)b * P.bt_stride + page_idx);
-  if (r.block >= P.num_pages) r.block = -1;
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  if (r.block < 0) {
-    r.k0[0] = r.k0[1] = r.k8[0] = r.k8[1] = z;
-    r.v[0] = r.v[1] = r.v[2] = r.v[3] = z;
-    return;
-  }
-  const int64_t base = (int64_t)r.block * P.s_page + (int64_t)row0 * P.s_tok + (int64_t)kvh * P.s_head;
-  const uint8_t* kp = P.k + base + 32 * c;
-  r.k0[0] = ldg_stream16(kp + (int64_t)g * P.s_tok);
-  r.k0[1] = ldg_stream16(kp + (int64_t)g * P.s_tok + 16);
-  r.k8[0] = ldg_stream16(kp + (int64_t)(g + 8) * P.s_tok);
-  r.k8[1] = ldg_stream16(kp + (int64_t)(g + 8) * P.s_tok + 16);
-  const uint8_t* vp = P.v + base + 16 * g;
-  const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    // Rows at or past ctx may hold uninitialised bytes (NaN in e4m3); they get
-    // probability 0, so their V must be finite: zero them.
-    r.v[i] = (tile_t0 + toks[i] < ctx) ? ldg_stream16(vp + (int64_t)toks[i] * P.s_tok) : z;
-  }
+// 16 bytes at (row, 16-byte chunk) of a 128-byte-swizzled tile (chunk index XOR row % 8).
+__device__ __forceinline__ uint4 tile_ld16(const uint8_t* tile, int row, int chunk) {
+  return *reinterpret_cast<const uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// One warp = one work item (sequence b, KV head, 256-token split) at a time: items are dealt
+// to the grid's warps round-robin.  Each warp streams its item's tiles through its own ring of
+// RING tile slots (K and V, 4 KB per tile): lane i looks up tile i's page, lane 0 issues the
+// TMA loads RING tiles ahead of the tile being computed, and the warp writes the item's
+// unnormalised partial (per head: O, max, sum) straight from its registers.
+constexpr int RING = 4;
+constexpr int SPLIT_WARPS = 4;
+constexpr int SPLIT_SMEM_V3 = 1024 + SPLIT_WARPS * RING * 2 * TILE_BYTES + SPLIT_WARPS * RING * 8 + 64;
+
 template <typename TQ>
-__global__ void __launch_bounds__(THREADS, 3) decode_split_kernel(Params P) {
-  pdl_wait();
-  pdl_trigger();
-
-  const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
-  int start, start16, nsplit;
-  seq_range(P, ctx, start, start16, nsplit);
-  if (s >= nsplit) return;
-  const int t0 = start16 + s * CHUNK;
-  const int t1 = min(ctx, t0 + CHUNK);
-  const int ntiles = (t1 - t0 + 15) >> 4;
-  const int lo = max(start, t0);
-
+__global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
+    decode_split_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Params P,
+                        int num_kv_heads, int batch) {
+  using namespace sm100;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int group = P.group;
 
-  __shared__ __align__(16) __half p_s[WARPS][8][16];
-  __shared__ float sm_m[WARPS][8], sm_l[WARPS][8];
-  __shared__ __align__(16) float sm_o[WARPS][8][D];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = ring_base + warp * RING * 2 * TILE_BYTES;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ring_base + SPLIT_WARPS * RING * 2 * TILE_BYTES) + warp * RING;
+  int* abort_flag = reinterpret_cast<int*>(reinterpret_cast<uint64_t*>(ring_base + SPLIT_WARPS * RING * 2 * TILE_BYTES) +
+                                           SPLIT_WARPS * RING);
+  __shared__ __align__(16) __half p_s[SPLIT_WARPS][8][16];
 
-  // Q operand (B of the score MMA): head g of the group, d in [32c, 32c+32),
-  // fp16 as the reference (attention.py:314-324).  qf[2s], qf[2s+1] = k-step s.
-  uint32_t qf[16];
-  if (g < group) {
-    const TQ* qp = reinterpret_cast<const TQ*>(P.q) + (int64_t)b * P.q_sb + (int64_t)(kvh * group + g) * P.q_sh + 32 * c;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float f[8];
-      unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * i), f);
-      qf[4 * i + 0] = pack_half2(f[0], f[1]);
-      qf[4 * i + 1] = pack_half2(f[2], f[3]);
-      qf[4 * i + 2] = pack_half2(f[4], f[5]);
-      qf[4 * i + 3] = pack_half2(f[6], f[7]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) qf[i] = 0u;
-  }
-
-  float acc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-  TileRegs cur, nxt;
-  int tile = warp;
-  if (tile < ntiles) load_tile(P, b, kvh, t0 + 16 * tile, ctx, g, c, cur);
-  for (; tile < ntiles; tile += WARPS) {
-    const int tt = t0 + 16 * tile;
-    const bool has_next = tile + WARPS < ntiles;
-    if (has_next) load_tile(P, b, kvh, tt + 16 * WARPS, ctx, g, c, nxt);
-
-    // ---- scores S^T[token][head] -------------------------------------------
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t* kg = reinterpret_cast<const uint32_t*>(cur.k0);
-    const uint32_t* kg8 = reinterpret_cast<const uint32_t*>(cur.k8);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t a[4];
-      a[0] = e4m3x2_to_f16x2((uint16_t)(kg[ks] & 0xFFFFu));
-      a[1] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] & 0xFFFFu));
-      a[2] = e4m3x2_to_f16x2((uint16_t)(kg[ks] >> 16));
-      a[3] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] >> 16));
-      mma_16816_f16(sc, a, &qf[2 * ks]);
-    }
-    const bool blk_ok = cur.block >= 0;
-    const int tg = tt + g, tg8 = tt + g + 8;
-    const bool vg = blk_ok && tg >= lo && tg < t1;
-    const bool vg8 = blk_ok && tg8 >= lo && tg8 < t1;
-    const float x0 = vg ? sc[0] * P.scale_log2 : -INFINITY;   // token g,   head 2c
-    const float x1 = vg ? sc[1] * P.scale_log2 : -INFINITY;   // token g,   head 2c+1
-    const float x2 = vg8 ? sc[2] * P.scale_log2 : -INFINITY;  // token g+8, head 2c
-    const float x3 = vg8 ? sc[3] * P.scale_log2 : -INFINITY;  // token g+8, head 2c+1
-    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    float al0 = 1.f, al1 = 1.f, p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-    if (mn0 != -INFINITY) {
-      al0 = fast_exp2(m0 - mn0);
-      p0 = fast_exp2(x0 - mn0);
-      p2 = fast_exp2(x2 - mn0);
-    }
-    if (mn1 != -INFINITY) {
-      al1 = fast_exp2(m1 - mn1);
-      p1 = fast_exp2(x1 - mn1);
-      p3 = fast_exp2(x3 - mn1);
-    }
-    m0 = mn0;
-    m1 = mn1;
-    // fp32 probabilities feed the row sum, fp16 ones feed P.V (attention.py:219-223)
-    const __half hp0 = __float2half_rn(p0), hp1 = __float2half_rn(p1);
-    const __half hp2 = __float2half_rn(p2), hp3 = __float2half_rn(p3);
-    l0 = l0 * al0 + (p0 + p2);
-    l1 = l1 * al1 + (p1 + p3);
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      acc[mt][0] *= al0;
-      acc[mt][1] *= al1;
-      acc[mt][2] *= al0;
-      acc[mt][3] *= al1;
-    }
-    // ---- transpose P through shared memory: P^T operand wants (token pairs, head g)
-    p_s[warp][2 * c][g] = hp0;
-    p_s[warp][2 * c + 1][g] = hp1;
-    p_s[warp][2 * c][g + 8] = hp2;
-    p_s[warp][2 * c + 1][g + 8] = hp3;
-    __syncwarp();
-    uint32_t bp[2];
-    bp[0] = *reinterpret_cast<const uint32_t*>(&p_s[warp][g][2 * c]);
-    bp[1] = *reinterpret_cast<const uint32_t*>(&p_s[warp][g][2 * c + 8]);
-    __syncwarp();
-
-    // ---- O^T[d][head] += V^T . P^T ----------------------------------------
-    const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&cur.v[0]);
-    const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&cur.v[1]);
-    const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&cur.v[2]);
-    const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&cur.v[3]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const uint32_t sel = half ? 0x7362u : 0x5140u;
-        const uint32_t lo01 = prmt(v0[j], v1[j], sel);
-        const uint32_t lo89 = prmt(v8[j], v9[j], sel);
-        uint32_t a[4];
-        a[0] = e4m3x2_to_f16x2((uint16_t)(lo01 & 0xFFFFu));
-        a[1] = e4m3x2_to_f16x2((uint16_t)(lo01 >> 16));
-        a[2] = e4m3x2_to_f16x2((uint16_t)(lo89 & 0xFFFFu));
-        a[3] = e4m3x2_to_f16x2((uint16_t)(lo89 >> 16));
-        mma_16816_f16(acc[2 * j + half], a, bp);
-      }
-    }
-    if (has_next) cur = nxt;
-  }
-
-  // ---- merge the warps' partial states ------------------------------------
-#pragma unroll
-  for (int o = 4; o < 32; o <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-  }
-  if (g == 0) {
-    sm_m[warp][2 * c] = m0;
-    sm_m[warp][2 * c + 1] = m1;
-    sm_l[warp][2 * c] = l0;
-    sm_l[warp][2 * c + 1] = l1;
-  }
-#pragma unroll
-  for (int mt = 0; mt < 8; ++mt) {
-    const int d = 16 * g + 2 * mt;
-    sm_o[warp][2 * c][d] = acc[mt][0];
-    sm_o[warp][2 * c + 1][d] = acc[mt][1];
-    sm_o[warp][2 * c][d + 1] = acc[mt][2];
-    sm_o[warp][2 * c + 1][d + 1] = acc[mt][3];
-  }
+  if (threadIdx.x == 0) *abort_flag = 0;
+  if (lane < RING) mbar_init(&bar[lane], 1);
+  fence_mbar_init();
   __syncthreads();
-  const int d = threadIdx.x;  // THREADS == D
-  for (int h = 0; h < group; ++h) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, sm_m[w][h]);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < WARPS; ++w) {
-        const float sw = fast_exp2(sm_m[w][h] - M);
-        L += sm_l[w][h] * sw;
-        O += sm_o[w][h][d] * sw;
-      }
-    }
-    const int64_t row = ((int64_t)b * P.num_heads + kvh * group + h) * P.max_splits + s;
-    P.o_part[row * D + d] = O * P.v_scale;
-    if (d == 0) {
-      P.ml_part[row * 2 + 0] = M;
-      P.ml_part[row * 2 + 1] = L;
-    }
-  }
-}
-
-template <typename TO>
-__global__ void __launch_bounds__(D) decode_reduce_kernel(Params P, TO* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
 
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  uint32_t uses = 0;  // tiles this warp has put through its ring (slot = uses % RING, parity = (uses / RING) & 1)
+  const int items = batch * num_kv_heads * P.max_splits;
+  for (int item = blockIdx.x * SPLIT_WARPS + warp; item < items; item += gridDim.x * SPLIT_WARPS) {
+    // KV head fastest: neighbouring warps (and CTAs) read the rows of the same pages together
+    const int kvh = item % num_kv_heads;
+    const int s = (item / num_kv_heads) % P.max_splits;
+    const int b = item / (P.max_splits * num_kv_heads);
+    const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
+    int start, start16, nsplit;
+    seq_range(P, ctx, start, start16, nsplit);
+    if (s >= nsplit) continue;  // warp-uniform
+    const int t0 = start16 + s * CHUNK;
+    const int t1 = min(ctx, t0 + CHUNK);
+    const int ntiles = (t1 - t0 + 15) >> 4;
+    const int lo = max(start, t0);
+
+    // lane i: page of tile i (lanes >= ntiles: unused)
+    int my_block = -1, my_row0 = 0;
+    if (lane < ntiles) {
+      const int tt = t0 + TILE * lane;
+      const int page_idx = tt / P.page;
+      my_row0 = tt - page_idx * P.page;
+      my_block = __ldg(P.bt + (int64_t)b * P.bt_stride + page_idx);
+      if (my_block >= P.num_pages) my_block = -1;
+    }
+    auto issue = [&](int k, uint32_t use) {  // lane 0 only
+      const int blk = __shfl_sync(0xffffffffu, my_block, k);
+      const int row0 = __shfl_sync(0xffffffffu, my_row0, k);
+      if (lane == 0) {
+        const int slot = use % RING;
+        uint64_t* bb = &bar[slot];
+        if (blk >= 0) {
+          mbar_arrive_expect_tx(bb, 2 * TILE_BYTES);
+          tma_load_4d(ring + slot * 2 * TILE_BYTES, &tmk, bb, 0, kvh, row0, blk);
+          tma_load_4d(ring + slot * 2 * TILE_BYTES + TILE_BYTES, &tmv, bb, 0, kvh, row0, blk);
+        } else {
+          mbar_arrive_plain(bb);  // a hole in the block table: nothing to load
+        }
+      }
+    };
+    for (int k = 0; k < RING && k < ntiles; ++k) issue(k, uses + k);
+
+    // Q operand (B of the score MMA): head g of the group, d in [32c, 32c+32),
+    // fp16 as the reference (attention.py:314-324).  qf[2s], qf[2s+1] = k-step s.
+    uint32_t qf[16];
+    if (g < group) {
+      const TQ* qp =
+          reinterpret_cast<const TQ*>(P.q) + (int64_t)b * P.q_sb + (int64_t)(kvh * group + g) * P.q_sh + 32 * c;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float f[8];
+        unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * i), f);
+        qf[4 * i + 0] = pack_half2(f[0], f[1]);
+        qf[4 * i + 1] = pack_half2(f[2], f[3]);
+        qf[4 * i + 2] = pack_half2(f[4], f[5]);
+        qf[4 * i + 3] = pack_half2(f[6], f[7]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qf[i] = 0u;
+    }
+
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    bool failed = false;
+
+    for (int k = 0; k < ntiles; ++k) {
+      const uint32_t use = uses + k;
+      const int slot = use % RING;
+      if (!mbar_wait_bounded(&bar[slot], (use / RING) & 1, abort_flag, nullptr, 0u)) {
+        failed = true;
+        break;
+      }
+      const int tt = t0 + TILE * k;
+      const uint8_t* kt = ring + slot * 2 * TILE_BYTES;
+      const uint8_t* vt = kt + TILE_BYTES;
+      const bool blk_ok = __shfl_sync(0xffffffffu, my_block, k) >= 0;
+      uint4 k0[2], k8[2], vv[4];
+      k0[0] = tile_ld16(kt, g, 2 * c);
+      k0[1] = tile_ld16(kt, g, 2 * c + 1);
+      k8[0] = tile_ld16(kt, g + 8, 2 * c);
+      k8[1] = tile_ld16(kt, g + 8, 2 * c + 1);
+      const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        // Rows at or past ctx (and holes) may hold stale or uninitialised bytes (NaN in
+        // e4m3); they get probability 0, so their V must be finite: zero them.
+        vv[i] = (blk_ok && tt + toks[i] < ctx) ? tile_ld16(vt, toks[i], g) : z;
+      }
+
+      // ---- scores S^T[token][head] -----------------------------------------
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t* kg = reinterpret_cast<const uint32_t*>(k0);
+      const uint32_t* kg8 = reinterpret_cast<const uint32_t*>(k8);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[4];
+        a[0] = e4m3x2_to_f16x2((uint16_t)(kg[ks] & 0xFFFFu));
+        a[1] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] & 0xFFFFu));
+        a[2] = e4m3x2_to_f16x2((uint16_t)(kg[ks] >> 16));
+        a[3] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] >> 16));
+        mma_16816_f16(sc, a, &qf[2 * ks]);
+      }
+      const int tg = tt + g, tg8 = tt + g + 8;
+      const bool vg = blk_ok && tg >= lo && tg < t1;
+      const bool vg8 = blk_ok && tg8 >= lo && tg8 < t1;
+      const float x0 = vg ? sc[0] * P.scale_log2 : -INFINITY;   // token g,   head 2c
+      const float x1 = vg ? sc[1] * P.scale_log2 : -INFINITY;   // token g,   head 2c+1
+      const float x2 = vg8 ? sc[2] * P.scale_log2 : -INFINITY;  // token g+8, head 2c
+      const float x3 = vg8 ? sc[3] * P.scale_log2 : -INFINITY;  // token g+8, head 2c+1
+      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      float al0 = 1.f, al1 = 1.f, p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+      if (mn0 != -INFINITY) {
+        al0 = fast_exp2(m0 - mn0);
+        p0 = fast_exp2(x0 - mn0);
+        p2 = fast_exp2(x2 - mn0);
+      }
+      if (mn1 != -INFINITY) {
+        al1 = fast_exp2(m1 - mn1);
+        p1 = fast_exp2(x1 - mn1);
+        p3 = fast_exp2(x3 - mn1);
+      }
+      m0 = mn0;
+      m1 = mn1;
+      // fp32 probabilities feed the row sum, fp16 ones feed P.V (attention.py:219-223)
+      const __half hp0 = __float2half_rn(p0), hp1 = __float2half_rn(p1);
+      const __half hp2 = __float2half_rn(p2), hp3 = __float2half_rn(p3);
+      l0 = l0 * al0 + (p0 + p2);
+      l1 = l1 * al1 + (p1 + p3);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        acc[mt][0] *= al0;
+        acc[mt][1] *= al1;
+        acc[mt][2] *= al0;
+        acc[mt][3] *= al1;
+      }
+      // ---- transpose P through shared memory: P^T operand wants (token pairs, head g)
+      p_s[warp][2 * c][g] = hp0;
+      p_s[warp][2 * c + 1][g] = hp1;
+      p_s[warp][2 * c][g + 8] = hp2;
+      p_s[warp][2 * c + 1][g + 8] = hp3;
+      __syncwarp();
+      uint32_t bp[2];
+      bp[0] = *reinterpret_cast<const uint32_t*>(&p_s[warp][g][2 * c]);
+      bp[1] = *reinterpret_cast<const uint32_t*>(&p_s[warp][g][2 * c + 8]);
+      __syncwarp();
+
+      // ---- O^T[d][head] += V^T . P^T --------------------------------------
+      const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0]);
+      const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1]);
+      const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&vv[2]);
+      const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&vv[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t sel = half ? 0x7362u : 0x5140u;
+          const uint32_t lo01 = prmt(v0[j], v1[j], sel);
+          const uint32_t lo89 = prmt(v8[j], v9[j], sel);
+          uint32_t a[4];
+          a[0] = e4m3x2_to_f16x2((uint16_t)(lo01 & 0xFFFFu));
+          a[1] = e4m3x2_to_f16x2((uint16_t)(lo01 >> 16));
+          a[2] = e4m3x2_to_f16x2((uint16_t)(lo89 & 0xFFFFu));
+          a[3] = e4m3x2_to_f16x2((uint16_t)(lo89 >> 16));
+          mma_16816_f16(acc[2 * j + half], a, bp);
+        }
+      }
+      // every byte of the slot has been consumed by the MMAs above: refill it with tile k + RING
+      __syncwarp();
+      if (k + RING < ntiles) {
+        if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(k + RING, use + RING);
+      }
+    }
+    uses += ntiles;
+    if (failed) {  // a tile never arrived: poison this split's result and stop using the ring
+      m0 = m1 = l0 = l1 = __int_as_float(0x7fc00000);
+    }
+
+    // ---- this item's partial, straight from the fragments ------------------------
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    const int64_t row0 = ((int64_t)b * P.num_heads + kvh * group + 2 * c) * P.max_splits + s;  // head 2c
+    const int64_t row1 = row0 + P.max_splits;                                                  // head 2c+1
+    if (2 * c < group) {
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d = 16 * g + 2 * mt;
+        *reinterpret_cast<float2*>(P.o_part + row0 * D + d) =
+            make_float2(acc[mt][0] * P.v_scale, acc[mt][2] * P.v_scale);
+      }
+      if (g == 0) *reinterpret_cast<float2*>(P.ml_part + row0 * 2) = make_float2(m0, l0);
+    }
+    if (2 * c + 1 < group) {
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d = 16 * g + 2 * mt;
+        *reinterpret_cast<float2*>(P.o_part + row1 * D + d) =
+            make_float2(acc[mt][1] * P.v_scale, acc[mt][3] * P.v_scale);
+      }
+      if (g == 0) *reinterpret_cast<float2*>(P.ml_part + row1 * 2) = make_float2(m1, l1);
+    }
+    if (failed) break;
+  }
+}
+
+// ---- split merge ------------------------------------------------------------------
+// The (max, sum) statistics of the splits of heads [h0, h0 + nh) of sequence b are staged in
+// shared memory: sw[hl * nsplit + s] = 2^(m_s - M) (the weight of split s), sl[hl] = the
+// merged sum L.  One warp per head: lane-strided max and sum plus a fixed xor-shuffle tree,
+// so every kernel that merges a head rounds identically.  All threads of the CTA call it.
+__device__ __forceinline__ void merge_weights(const Params& P, int b, int h0, int nh, int nsplit, float* sw,
+                                              float* sl) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int hl = warp; hl < nh; hl += nw) {
+    const float* ml = P.ml_part + ((int64_t)b * P.num_heads + h0 + hl) * P.max_splits * 2;
+    float M = -INFINITY;
+    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, ml[2 * s]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    for (int s = lane; s < nsplit; s += 32) {
+      const float w = M != -INFINITY ? fast_exp2(ml[2 * s] - M) : 0.f;
+      sw[hl * nsplit + s] = w;
+      L += ml[2 * s + 1] * w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) sl[hl] = L;
+  }
+  __syncthreads();
+}
+
+// Split-merge order shared by every merge kernel: A_j = sum over splits s = j, j+4, j+8, ...
+// (ascending) of fmaf(o_part[s][d], w_s, .), O = ((A_0 + A_1) + A_2) + A_3, then O / L.
+template <int N>
+__device__ __forceinline__ void merge_partial(const Params& P, int b, int h, int d0, int nsplit, const float* w, int j,
+                                              float* A) {
+  const float* op = P.o_part + ((int64_t)b * P.num_heads + h) * P.max_splits * D + d0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) A[i] = 0.f;
+#pragma unroll 2
+  for (int s = j; s < nsplit; s += 4) {
+    const float ws = w[s];
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 f = *reinterpret_cast<const float4*>(op + (int64_t)s * D + i);
+      A[i + 0] = fmaf(f.x, ws, A[i + 0]);
+      A[i + 1] = fmaf(f.y, ws, A[i + 1]);
+      A[i + 2] = fmaf(f.z, ws, A[i + 2]);
+      A[i + 3] = fmaf(f.w, ws, A[i + 3]);
+    }
+  }
+}
+__device__ __forceinline__ float merge_finish(float a0, float a1, float a2, float a3, float L) {
+  const float O = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+  return L > 0.f ? __fdiv_rn(O, L) : 0.f;
+}
+
+// All four interleaved partials in one thread (the fused merge+quant kernel).
+template <int N>
+__device__ __forceinline__ void merge_out(const Params& P, int b, int h, int d0, int nsplit, const float* w, float L,
+                                          float* out) {
+  float A[4][N];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) merge_partial<N>(P, b, h, d0, nsplit, w, j, A[j]);
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = merge_finish(A[0][i], A[1][i], A[2][i], A[3][i], L);
+}
+
+// One CTA per (head, sequence): warp j accumulates the splits s = j (mod 4) for all 128 dims
+// (4 per lane); thread t combines dim t.  Dynamic shared memory: nsplit floats.
+template <typename TO>
+__global__ void __launch_bounds__(128) decode_reduce_kernel(Params P, TO* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float merge_smem[];
+  __shared__ float sl[1];
+  __shared__ __align__(16) float part[4][D];
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
   seq_range(P, ctx, start, start16, nsplit);
-  const int64_t row0 = ((int64_t)b * P.num_heads + h) * P.max_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, P.ml_part[(row0 + s) * 2]);
-  float L = 0.f, O = 0.f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = fast_exp2(P.ml_part[(row0 + s) * 2] - M);
-      L += P.ml_part[(row0 + s) * 2 + 1] * w;
-      O += P.o_part[(row0 + s) * D + d] * w;
-    }
-  }
-  const float r = L > 0.f ? O / L : 0.f;
-  out[((int64_t)b * P.num_heads + h) * D + d] = from_f32<TO>(r);
+  merge_weights(P, b, h, 1, nsplit, merge_smem, sl);
+  float A[4];
+  merge_partial<4>(P, b, h, 4 * lane, nsplit, merge_smem, warp, A);
+  *reinterpret_cast<float4*>(&part[warp][4 * lane]) = make_float4(A[0], A[1], A[2], A[3]);
+  __syncthreads();
+  const int d = threadIdx.x;
+  out[((int64_t)b * P.num_heads + h) * D + d] =
+      from_f32<TO>(merge_finish(part[0][d], part[1][d], part[2][d], part[3][d], sl[0]));
 }
-
 
 // Split-K merge fused with the NVFP4 activation quantiser (quant.cuh): the token's
 // [num_heads * 128] attention row is spread over a cluster of CTAs (grid (ctas, m_pad),
@@ -333,6 +434,10 @@ __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* 
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
   seq_range(P, ctx, start, start16, nsplit);
+  extern __shared__ float merge_smem[];  // [heads of this slice][nsplit] weights, then [heads] sums
+  const int h0 = (o0 * 8) / D, nh = ((o1 * 8 - 1) / D) - h0 + 1;
+  float* sl = merge_smem + nh * nsplit;
+  merge_weights(P, b, h0, nh, nsplit, merge_smem, sl);
   float v[MAXU][8];
   float amax = 0.f;
 #pragma unroll
@@ -342,30 +447,11 @@ __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* 
     for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     if (o >= o1) continue;
     const int h = (o * 8) / D, d0 = (o * 8) % D;
-    const int64_t row0 = ((int64_t)b * P.num_heads + h) * P.max_splits;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, P.ml_part[(row0 + s) * 2]);
-    float L = 0.f, O[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) O[i] = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < nsplit; ++s) {
-        const float w = fast_exp2(P.ml_part[(row0 + s) * 2] - M);
-        L += P.ml_part[(row0 + s) * 2 + 1] * w;
-        const float4* op = reinterpret_cast<const float4*>(P.o_part + (row0 + s) * D + d0);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const float4 f = op[i];
-          O[4 * i + 0] += f.x * w;
-          O[4 * i + 1] += f.y * w;
-          O[4 * i + 2] += f.z * w;
-          O[4 * i + 3] += f.w * w;
-        }
-      }
-    }
+    float r[8];
+    merge_out<8>(P, b, h, d0, nsplit, merge_smem + (h - h0) * nsplit, sl[h - h0], r);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      v[u][i] = to_f32(from_f32<TO>(L > 0.f ? O[i] / L : 0.f));
+      v[u][i] = to_f32(from_f32<TO>(r[i]));
       amax = fmaxf(amax, fabsf(v[u][i]));
     }
     if (out) *reinterpret_cast<uint4*>(out + (int64_t)b * row_len + o * 8) = pack8<TO>(v[u]);
@@ -378,6 +464,23 @@ __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* 
     const int o = o0 + threadIdx.x + u * blockDim.x;
     q::quant_oct(dst, b, o < o1 ? o : 0, v[u], rq, o < o1);
   }
+}
+
+// Dynamic shared memory above 48 KB and the maximum shared carveout (three CTAs per SM),
+// set once per device.
+template <typename TQ>
+inline bool split_smem_ready() {
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return true;
+  if (cudaFuncSetAttribute(decode_split_kernel<TQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, SPLIT_SMEM_V3) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(decode_split_kernel<TQ>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return false;
+  done[dev] = true;
+  return true;
 }
 
 inline int max_splits_for(int32_t max_pages, int32_t page) {
@@ -491,20 +594,49 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
   P.o_part = reinterpret_cast<float*>(workspace);
   P.ml_part = P.o_part + (size_t)batch * num_heads * P.max_splits * attn::D;
 
+  // K / V caches as 4-D byte tensors [num_pages][page][Hkv][D] -> TMA box of 16 rows x 128 B
+  CUtensorMap tmk, tmv;
+  const cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_kv_heads, (cuuint64_t)page_size,
+                              (cuuint64_t)num_pages};
+  const cuuint64_t strides[3] = {(cuuint64_t)kv_stride_head, (cuuint64_t)kv_stride_tok, (cuuint64_t)kv_stride_page};
+  const cuuint32_t box[4] = {(cuuint32_t)head_dim, 1, (cuuint32_t)attn::TILE, 1};
+  if (!sm100::encode_bytes(&tmk, k_cache, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !sm100::encode_bytes(&tmv, v_cache, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    return ADA_ERR_CUDA;
+
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  dim3 grid(P.max_splits, num_kv_heads, batch);
-  if (q_dtype == ADA_DT_BF16)
-    (void)ada::launch_k(attn::decode_split_kernel<__nv_bfloat16>, dim3(grid), dim3(attn::THREADS), 0, st, P);
-  else
-    (void)ada::launch_k(attn::decode_split_kernel<__half>, dim3(grid), dim3(attn::THREADS), 0, st, P);
+  // persistent-style grid: every warp takes work items (sequence, KV head, split) round-robin
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
+  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return ADA_ERR_CUDA;
+  const int64_t items = (int64_t)batch * num_kv_heads * P.max_splits;
+  if (items > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
+  const int64_t want = (items + attn::SPLIT_WARPS - 1) / attn::SPLIT_WARPS;
+  const unsigned grid = (unsigned)(want < 3 * (int64_t)sms[dev] ? want : 3 * (int64_t)sms[dev]);
+  if (q_dtype == ADA_DT_BF16) {
+    if (!attn::split_smem_ready<__nv_bfloat16>()) return ADA_ERR_CUDA;
+    (void)ada::launch_k(attn::decode_split_kernel<__nv_bfloat16>, dim3(grid), dim3(attn::SPLIT_WARPS * 32),
+                        attn::SPLIT_SMEM_V3, st, tmk, tmv, P, (int)num_kv_heads, (int)batch);
+  } else {
+    if (!attn::split_smem_ready<__half>()) return ADA_ERR_CUDA;
+    (void)ada::launch_k(attn::decode_split_kernel<__half>, dim3(grid), dim3(attn::SPLIT_WARPS * 32),
+                        attn::SPLIT_SMEM_V3, st, tmk, tmv, P, (int)num_kv_heads, (int)batch);
+  }
   ADA_CHECK_LAUNCH();
   if (qd) {
     const int m_pad = (int)cdiv(batch, qd->bn) * qd->bn;
     const cl::RowSplit sp = cl::row_split(num_heads * head_dim / 16);
     if (!sp.maxu || sp.maxu > 4 || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
     const dim3 rg((unsigned)sp.ctas, (unsigned)m_pad), rb((unsigned)sp.threads);
+    // staged merge weights: the heads one CTA's slice touches x the splits, plus their sums
+    const int units = num_heads * head_dim / 16;
+    const int nh_max = (2 * ((units + sp.ctas - 1) / sp.ctas) * 8 + attn::D - 1) / attn::D + 1;
+    const size_t msmem = (size_t)nh_max * (P.max_splits + 1) * sizeof(float);
+    if (msmem > 48 * 1024) return ADA_ERR_UNSUPPORTED;
 #define ADA_RQ(TO, MU)                                                                                         \
-    (void)ada::launch_kc(attn::decode_reduce_quant_kernel<TO, MU>, rg, rb, 0, st, sp.ctas, P,                  \
+    (void)ada::launch_kc(attn::decode_reduce_quant_kernel<TO, MU>, rg, rb, msmem, st, sp.ctas, P,              \
                          reinterpret_cast<TO*>(out), batch, *qd)
     if (out_dtype == ADA_DT_BF16) {
       if (sp.maxu == 1) ADA_RQ(__nv_bfloat16, 1); else if (sp.maxu == 2) ADA_RQ(__nv_bfloat16, 2); else ADA_RQ(__nv_bfloat16, 4);
@@ -516,10 +648,14 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
     return ADA_OK;
   }
   dim3 rgrid(num_heads, batch);
+  const size_t rsmem = (size_t)P.max_splits * sizeof(float);
+  if (rsmem > 48 * 1024) return ADA_ERR_UNSUPPORTED;
   if (out_dtype == ADA_DT_BF16)
-    (void)ada::launch_k(attn::decode_reduce_kernel<__nv_bfloat16>, dim3(rgrid), dim3(attn::D), 0, st, P, reinterpret_cast<__nv_bfloat16*>(out));
+    (void)ada::launch_k(attn::decode_reduce_kernel<__nv_bfloat16>, rgrid, dim3(128), rsmem, st, P,
+                        reinterpret_cast<__nv_bfloat16*>(out));
   else
-    (void)ada::launch_k(attn::decode_reduce_kernel<__half>, dim3(rgrid), dim3(attn::D), 0, st, P, reinterpret_cast<__half*>(out));
+    (void)ada::launch_k(attn::decode_reduce_kernel<__half>, rgrid, dim3(128), rsmem, st, P,
+                        reinterpret_cast<__half*>(out));
   ADA_CHECK_LAUNCH();
   return ADA_OK;
 }

@@ -305,34 +305,13 @@ __global__ void __launch_bounds__(128) prepack_kernel(const void* __restrict__ s
 
 // ---------------------------------------------------------------------------
 // Host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult qr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) == cudaSuccess &&
-        qr == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
 // 2-D byte matrix [rows, inner_bytes] with row stride `stride` bytes; box = 128 bytes x box_rows, 128B swizzle.
 static bool make_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t stride,
                      uint32_t box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {inner_bytes, rows};
-  cuuint64_t strides[1] = {stride};
-  cuuint32_t box[2] = {128, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const cuuint64_t dims[2] = {inner_bytes, rows};
+  const cuuint64_t strides[1] = {stride};
+  const cuuint32_t box[2] = {128, box_rows};
+  return encode_bytes(map, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Token tile: the smallest of 16/32/64/128 covering m, capped so terms*bn <= 128.
