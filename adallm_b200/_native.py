@@ -64,6 +64,13 @@ _SIGS = {
     "ada_nvfp4_block_n": (INT, [I64, INT]),
     "ada_nvfp4_gemm_workspace_size": (SZ, [I64, I64, I64, INT]),
     "ada_nvfp4_gemm": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, P, INT, I64, INT, P, SZ, P]),
+    "ada_nvfp4_gemm_splits": (INT, [I64, I64, I64, INT]),
+    "ada_nvfp4_gemm_partials": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, I64, I64, INT, P, SZ, P]),
+    "ada_rmsnorm_quant_parts": (INT, [P, I32, I64, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT,
+                                      P, P, P, P]),
+    "ada_gated_act_quant_parts": (INT, [P, I32, I64, I64, P, I64, I64, I32, INT, INT, INT, INT, P, P, P, P]),
+    "ada_qk_norm_rope_store_parts": (INT, [P, I32, I64, I64, I64, I32, I32, I32, P, P, F32, P, P, I64, P, P, P, F32,
+                                           F32, P, P, INT, P]),
 }
 
 _lib = None

@@ -16,6 +16,7 @@
 #include <type_traits>
 
 #include "cluster.cuh"
+#include "parts.cuh"
 #include "quant.cuh"
 
 namespace ada {
@@ -69,7 +70,8 @@ template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict__ x, int64_t ldx, const T* res,
                                                             int64_t ldr, T* res_out, int64_t ldro,
                                                             const T* __restrict__ w, T* y, int64_t ldy, int rows,
-                                                            int hidden, float eps, int gemma, q::QuantDst dst) {
+                                                            int hidden, float eps, int gemma, q::QuantDst dst,
+                                                            PartIn pin) {
   cl::cluster_arrive_relaxed();
   __shared__ float red[cl::MAX_WARPS];
   __shared__ float slots[2][cl::MAX_CLUSTER];
@@ -96,7 +98,10 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
   for (int u = 0; u < MAXU; ++u) {
     const int o = my_oct(u, o0, o1);
     if (o >= 0) {
-      load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
+      if (pin.n)
+        load_parts<T, 8>(pin, m, o * 8, v[u]);  // the producing GEMM's split-K planes
+      else
+        load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
       if (res) {
         float r[8];
         load8<T>(res + (int64_t)m * ldr + o * 8, r);
@@ -146,7 +151,8 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 // grid (ctas, m_pad), cluster (ctas, 1, 1).
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y, int64_t ldy,
-                                                              int rows, int inter, int act, q::QuantDst dst) {
+                                                              int rows, int inter, int act, q::QuantDst dst,
+                                                              PartIn pin) {
   cl::cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
@@ -167,8 +173,13 @@ __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restric
     const int o = my_oct(u, o0, o1);
     if (o >= 0) {
       float gt[8], up[8];
-      load8<T>(x + (int64_t)m * ldx + o * 8, gt);
-      load8<T>(x + (int64_t)m * ldx + inter + o * 8, up);
+      if (pin.n) {
+        load_parts<T, 8>(pin, m, o * 8, gt);
+        load_parts<T, 8>(pin, m, inter + o * 8, up);
+      } else {
+        load8<T>(x + (int64_t)m * ldx + o * 8, gt);
+        load8<T>(x + (int64_t)m * ldx + inter + o * 8, up);
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float a = act == 0 ? silu_f(gt[i]) : gelu_tanh_f(gt[i]);
@@ -243,7 +254,7 @@ bool quant_args_ok(const q::QuantDst& d) {
 // RMSNorm (quantised or not) of `launch_rows` rows (rows beyond `rows` are padding).
 int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro, const void* w,
                    void* y, int64_t ldy, int64_t rows, int64_t launch_rows, int hidden, float eps, int gemma,
-                   int dtype, const q::QuantDst& dst, cudaStream_t st) {
+                   int dtype, const q::QuantDst& dst, cudaStream_t st, const PartIn& pin = PartIn{nullptr, 0, 0, 0}) {
   if (hidden % 16) return ADA_ERR_UNSUPPORTED;
   const cl::RowSplit sp = cl::row_split(hidden / 16);
   if (!sp.maxu || launch_rows > 65535) return ADA_ERR_UNSUPPORTED;
@@ -252,11 +263,11 @@ int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, voi
   if (dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst);
+                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin);
   } else {
     using TT = __half;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst);
+                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
@@ -309,14 +320,21 @@ extern "C" int ada_rmsnorm_quant(const void* x, int64_t ldx, const void* residua
                                hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter,
-                                   int act, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
-                                   void* stream) {
-  if (rows <= 0 || inter <= 0 || !x || (act != 0 && act != 1)) return ADA_ERR_INVALID_ARG;
+static int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter, int act,
+                                int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream,
+                                const PartIn& pin) {
+  if (rows <= 0 || inter <= 0 || (act != 0 && act != 1)) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
   const q::QuantDst dst{xq, sfx, gx, terms, block_n, inter};
   if (!fused::quant_args_ok(dst)) return ADA_ERR_INVALID_ARG;
-  if (!fused::a16(x) || (ldx & 7) || (y && (!fused::a16(y) || (ldy & 7)))) return ADA_ERR_ALIGNMENT;
+  if (pin.n) {
+    if (!parts_ok(pin, rows, 2 * (int64_t)inter)) return ADA_ERR_INVALID_ARG;
+  } else if (!x) {
+    return ADA_ERR_INVALID_ARG;
+  } else if (!fused::a16(x) || (ldx & 7)) {
+    return ADA_ERR_ALIGNMENT;
+  }
+  if (y && (!fused::a16(y) || (ldy & 7))) return ADA_ERR_ALIGNMENT;
   const cl::RowSplit sp = cl::row_split(inter / 16);
   const int64_t m_pad = cdiv(rows, block_n) * block_n;
   if (!sp.maxu || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
@@ -326,11 +344,46 @@ extern "C" int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t 
   if (dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
     ADA_ROW_DISPATCH(fused::gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows,
-                     (int)inter, act, dst);
+                     (int)inter, act, dst, pin);
   } else {
     using TT = __half;
     ADA_ROW_DISPATCH(fused::gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows,
-                     (int)inter, act, dst);
+                     (int)inter, act, dst, pin);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+extern "C" int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter,
+                                   int act, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
+                                   void* stream) {
+  return gated_act_quant_impl(x, ldx, y, ldy, rows, inter, act, dtype, terms, block_n, xq, sfx, gx, stream,
+                              PartIn{nullptr, 0, 0, 0});
+}
+
+extern "C" int ada_gated_act_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp, void* y,
+                                         int64_t ldy, int64_t rows, int32_t inter, int act, int dtype, int terms,
+                                         int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream) {
+  if (nparts < 1) return ADA_ERR_INVALID_ARG;
+  return gated_act_quant_impl(nullptr, 0, y, ldy, rows, inter, act, dtype, terms, block_n, xq, sfx, gx, stream,
+                              PartIn{parts, nparts, plane, ldp});
+}
+
+extern "C" int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                       const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                       const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
+                                       float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
+                                       uint8_t* sfx, float* gx, void* stream) {
+  if (rows <= 0 || hidden <= 0 || !weight || (residual && !residual_out) || nparts < 1) return ADA_ERR_INVALID_ARG;
+  if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  const PartIn pin{parts, nparts, plane, ldp};
+  if (!parts_ok(pin, rows, hidden)) return ADA_ERR_INVALID_ARG;
+  const bool quant = xq != nullptr;  // without a quantised output this is a plain RMSNorm into y
+  const q::QuantDst dst{xq, sfx, gx, quant ? terms : 1, quant ? block_n : 16, hidden};
+  if (quant ? !fused::quant_args_ok(dst) : !y) return ADA_ERR_INVALID_ARG;
+  if (!fused::a16(weight) || (y && (!fused::a16(y) || (ldy & 7)))) return ADA_ERR_ALIGNMENT;
+  if (residual && (!fused::a16(residual) || !fused::a16(residual_out) || (ld_res & 7) || (ld_res_out & 7)))
+    return ADA_ERR_ALIGNMENT;
+  const int64_t launch_rows = quant ? cdiv(rows, block_n) * block_n : rows;
+  return fused::launch_rmsnorm(nullptr, 0, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
+                               launch_rows, hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream), pin);
 }

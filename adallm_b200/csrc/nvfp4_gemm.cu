@@ -50,6 +50,9 @@ struct GemmParams {
   const void* bias;    // [N] (out dtype) or null
   void* y;             // [M, ldy] out dtype
   unsigned int* err;
+  float* part;          // non-null: write scaled fp32 partial planes instead of reducing (no cluster)
+  int64_t part_plane;   // floats between planes (one plane per K split)
+  int part_ld;          // floats between rows of a plane
   int M, N, K, ldy, n_tiles, nkt, stages, tmem_cols, out_dtype, ks, rows_max;
 };
 
@@ -101,9 +104,10 @@ __global__ void __launch_bounds__(192, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = p.stages, ks = p.ks;
+  const bool cluster = ks > 1 && p.part == nullptr;  // split-K reduced through the cluster
   uint8_t* const_sf = smem + (size_t)stages * C::STAGE;
   float* recv = reinterpret_cast<float*>(const_sf + C::CONST_SF);  // [ks][rows_max][BN]
-  uint8_t* ctrl = reinterpret_cast<uint8_t*>(recv) + C::recv_bytes(ks, p.rows_max);
+  uint8_t* ctrl = reinterpret_cast<uint8_t*>(recv) + C::recv_bytes(cluster ? ks : 1, p.rows_max);
   uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
   uint64_t* empty = full + MAX_STAGES;
   uint64_t* accf = empty + MAX_STAGES;
@@ -119,7 +123,7 @@ __global__ void __launch_bounds__(192, 2)
   const int nunits = kt1 - kt0;
   const int kb64 = p.K / 64;
 
-  if (ks > 1) cl::cluster_arrive_relaxed();
+  if (cluster) cl::cluster_arrive_relaxed();
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -238,7 +242,17 @@ __global__ void __launch_bounds__(192, 2)
       for (int k = 0; k < 16; ++k) out[(c % BN) + k] = fmaf(v[k], gsc[c + k], out[(c % BN) + k]);  // terms in order
     }
     const int r = q * 32 + lane;
-    if (ks == 1) {
+    if (p.part) {
+      // fp32 partial of this K split; the consumer sums the planes in split order
+      if (ok) {
+        float* pp = p.part + (int64_t)rank * p.part_plane + n_tile * BM + r;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int m = m_tile * BN + j;
+          if (m < p.M) pp[(int64_t)m * p.part_ld] = out[j];
+        }
+      }
+    } else if (ks == 1) {
       if (ok) {
         const int n = n_tile * BM + r;
         const float b = load_bias(p.bias, p.out_dtype, n);
@@ -266,7 +280,7 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
   }
-  if (ks > 1 && warp < 2) {  // the producer and MMA warps take part in both cluster barriers
+  if (cluster && warp < 2) {  // the producer and MMA warps take part in both cluster barriers
     cl::cluster_wait();
     cl::cluster_sync();
   }
@@ -445,7 +459,8 @@ static int num_sms() {
 }
 
 // force_ks > 0 overrides the split-K factor (tests of the cluster reduction).
-static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, Plan& P) {
+// parts: split-K partial planes are written out (no cluster reduction, any split works).
+static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, Plan& P, bool parts = false) {
   if (m <= 0 || n <= 0 || k <= 0) return ADA_ERR_INVALID_ARG;
   if (terms < 1 || terms > q::MAX_TERMS) return ADA_ERR_INVALID_ARG;
   if (n % BM || k % KT) return ADA_ERR_UNSUPPORTED;
@@ -465,6 +480,10 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   const int64_t ks_cap = P.nkt < MAX_KS ? P.nkt : MAX_KS;
   if (force_ks > 0) {
     ks = force_ks < ks_cap ? force_ks : ks_cap;
+  } else if (parts) {
+    // as many splits as keep every CTA resident in one wave (two per SM)
+    ks = (2 * (int64_t)num_sms()) / tiles;
+    ks = ks < 1 ? 1 : ks > ks_cap ? ks_cap : ks;
   } else {
     for (int64_t c = (P.nkt / 4 < ks_cap ? P.nkt / 4 : ks_cap); c >= 2; --c) {
       if (P.nkt % c || tiles * c > 2 * (int64_t)num_sms()) continue;
@@ -477,7 +496,7 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   P.ks = (int)ks;
   P.rows_max = (int)cdiv(BM, ks);
   uint32_t cols = 0;
-  stages_dispatch(P.bn, terms, P.ks, P.rows_max, P.stages, cols, P.smem);
+  stages_dispatch(P.bn, terms, parts ? 1 : P.ks, P.rows_max, P.stages, cols, P.smem);
   if (P.stages < 2) return ADA_ERR_UNSUPPORTED;
   P.tmem_cols = (int)cols;
   size_t off = ERR_BYTES;
@@ -497,7 +516,7 @@ static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const Gem
   auto kern = gemm_kernel<BN, T>;
   if (!ensure_smem<BN, T>(P.smem)) return ADA_ERR_CUDA;
   const dim3 grid((unsigned)P.ks, (unsigned)(P.n_tiles * P.m_tiles));
-  if (P.ks > 1)
+  if (P.ks > 1 && !gp.part)
     (void)ada::launch_kc(kern, grid, dim3(192), P.smem, st, P.ks, tmw, tmx, gp);
   else
     (void)ada::launch_k(kern, grid, dim3(192), P.smem, st, tmw, tmx, gp);
@@ -515,7 +534,8 @@ static int dispatch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const G
 
 static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const float* gx, int m, int n, int k,
                     const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w, const float* w_scale_2,
-                    const void* bias, void* y, int y_dtype, int64_t ldy, unsigned int* err, cudaStream_t st) {
+                    const void* bias, void* y, int y_dtype, int64_t ldy, unsigned int* err, cudaStream_t st,
+                    float* part = nullptr, int64_t part_plane = 0, int64_t part_ld = 0) {
   CUtensorMap tmw, tmx;
   if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, BM)) return ADA_ERR_CUDA;
   if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2),
@@ -529,6 +549,9 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
   gp.bias = bias;
   gp.y = y;
   gp.err = err;
+  gp.part = part;
+  gp.part_plane = part_plane;
+  gp.part_ld = (int)part_ld;
   gp.M = m;
   gp.N = n;
   gp.K = k;
@@ -666,4 +689,33 @@ extern "C" int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float
     return ADA_ERR_ALIGNMENT;
   return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y, y_dtype, ldy,
                        reinterpret_cast<unsigned int*>(workspace), reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ada_nvfp4_gemm_splits(int64_t m, int64_t n, int64_t k, int terms) {
+  fp4::Plan P;
+  if (fp4::make_plan(m, n, k, terms, 0, P, true) != ADA_OK) return 0;
+  return P.ks;
+}
+
+extern "C" int ada_nvfp4_gemm_partials(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
+                                       int block_n, const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                       const float* w_scale_2, int64_t n, int64_t k, float* parts, int64_t part_ld,
+                                       int64_t part_plane, int nplanes, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  if (m == 0) return ADA_OK;
+  if (!xq || !gx || !w_packed || !sf_w || !w_scale_2 || !parts || !workspace) return ADA_ERR_INVALID_ARG;
+  if (terms == 1 && !sfx) return ADA_ERR_INVALID_ARG;
+  if (ldw < k / 2 || part_ld < n || part_plane < m * part_ld || nplanes < 1) return ADA_ERR_INVALID_ARG;
+  if (part_ld > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
+  fp4::Plan P;
+  int rc = fp4::make_plan(m, n, k, terms, nplanes, P, true);
+  if (rc != ADA_OK) return rc;
+  if (block_n != P.bn || P.ks != nplanes) return ADA_ERR_INVALID_ARG;
+  if (workspace_bytes < fp4::ERR_BYTES) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)xq & 15) || (sfx && ((uintptr_t)sfx & 15)) || ((uintptr_t)w_packed & 15) || (ldw & 15) ||
+      ((uintptr_t)sf_w & 15) || ((uintptr_t)workspace & 255) || ((uintptr_t)parts & 3))
+    return ADA_ERR_ALIGNMENT;
+  return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, nullptr,
+                       ADA_DT_BF16, n, reinterpret_cast<unsigned int*>(workspace), reinterpret_cast<cudaStream_t>(stream),
+                       parts, part_plane, part_ld);
 }

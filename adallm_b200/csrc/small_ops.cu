@@ -10,6 +10,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "parts.cuh"
 
 namespace ada {
 namespace fused {
@@ -192,7 +193,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_store_kernel(
     const T* __restrict__ qkv, int64_t ld, int hq, int hkv, const T* __restrict__ qw, const T* __restrict__ kw,
     float eps, const int64_t* __restrict__ pos, const float* __restrict__ cs, int64_t max_pos,
     const int32_t* __restrict__ slots, uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, float k_scale,
-    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out, int64_t num_tokens) {
+    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out, int64_t num_tokens, PartIn pin) {
   pdl_wait();
   pdl_trigger();
 
@@ -208,9 +209,11 @@ __global__ void __launch_bounds__(128) qk_norm_rope_store_kernel(
   const int slot = __ldg(slots + t);
   const int i0 = (lane & 15) * 4;  // rotation-pair index of this lane's first element
   {
-    const T* src = qkv + (int64_t)t * ld + (int64_t)h * D + lane * 4;
     float x[4];
-    {
+    if (pin.n) {  // the qkv GEMM's split-K planes
+      load_parts<T, 4>(pin, t, (int64_t)h * D + lane * 4, x);
+    } else {
+      const T* src = qkv + (int64_t)t * ld + (int64_t)h * D + lane * 4;
       const uint2 u = *reinterpret_cast<const uint2*>(src);
       const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
@@ -492,35 +495,66 @@ extern "C" int ada_rope(const int64_t* positions, const void* q, int64_t q_strid
   return ADA_OK;
 }
 
+static int qk_norm_rope_store_impl(const void* qkv, int64_t ld, const PartIn& pin, int64_t num_tokens,
+                                   int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const void* q_norm_w,
+                                   const void* k_norm_w, float eps, const int64_t* positions, const float* cos_sin,
+                                   int64_t max_position, const int32_t* slot_mapping, uint8_t* k_cache,
+                                   uint8_t* v_cache, float k_scale, float v_scale, void* q_out, void* k_out, int dtype,
+                                   void* stream) {
+  if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return ADA_ERR_INVALID_ARG;
+  if (num_tokens == 0) return ADA_OK;
+  if (!positions || !cos_sin || !slot_mapping || !k_cache || !v_cache || !q_out || max_position <= 0)
+    return ADA_ERR_INVALID_ARG;
+  if (!(k_scale > 0.f) || !(v_scale > 0.f)) return ADA_ERR_INVALID_ARG;
+  if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  if (head_dim != 128) return ADA_ERR_UNSUPPORTED;
+  const int64_t width = (int64_t)(num_q_heads + 2 * num_kv_heads) * head_dim;
+  if (pin.n) {
+    if (!parts_ok(pin, num_tokens, width)) return ADA_ERR_INVALID_ARG;
+  } else {
+    if (!qkv || ld < width) return ADA_ERR_INVALID_ARG;
+    if (((uintptr_t)qkv & 7) || (ld & 3)) return ADA_ERR_ALIGNMENT;
+  }
+  if (((uintptr_t)q_out & 7) || ((uintptr_t)k_out & 7) || ((uintptr_t)q_norm_w & 7) || ((uintptr_t)k_norm_w & 7) ||
+      ((uintptr_t)k_cache & 3) || ((uintptr_t)v_cache & 3))
+    return ADA_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t items = num_tokens * (num_q_heads + 2 * num_kv_heads);
+  const unsigned blocks = (unsigned)((items + 3) / 4);
+#define ADA_QK(T)                                                                                                \
+  (void)ada::launch_k(small::qk_norm_rope_store_kernel<T>, dim3(blocks), dim3(128), 0, st, (const T*)qkv, ld,      \
+                      num_q_heads, num_kv_heads, (const T*)q_norm_w, (const T*)k_norm_w, eps, positions, cos_sin, \
+                      max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out,       \
+                      num_tokens, pin)
+  if (dtype == ADA_DT_BF16) ADA_QK(__nv_bfloat16);
+  else ADA_QK(__half);
+#undef ADA_QK
+  ADA_CHECK_LAUNCH();
+  return ADA_OK;
+}
+
 extern "C" int ada_qk_norm_rope_store(const void* qkv, int64_t ld, int64_t num_tokens, int32_t num_q_heads,
                                       int32_t num_kv_heads, int32_t head_dim, const void* q_norm_w,
                                       const void* k_norm_w, float eps, const int64_t* positions, const float* cos_sin,
                                       int64_t max_position, const int32_t* slot_mapping, uint8_t* k_cache,
                                       uint8_t* v_cache, float k_scale, float v_scale, void* q_out, void* k_out,
                                       int dtype, void* stream) {
-  if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return ADA_ERR_INVALID_ARG;
-  if (num_tokens == 0) return ADA_OK;
-  if (!qkv || !positions || !cos_sin || !slot_mapping || !k_cache || !v_cache || !q_out || max_position <= 0)
-    return ADA_ERR_INVALID_ARG;
-  if (!(k_scale > 0.f) || !(v_scale > 0.f)) return ADA_ERR_INVALID_ARG;
-  if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
-  if (head_dim != 128) return ADA_ERR_UNSUPPORTED;
-  if (ld < (int64_t)(num_q_heads + 2 * num_kv_heads) * head_dim) return ADA_ERR_INVALID_ARG;
-  if (((uintptr_t)qkv & 7) || (ld & 3) || ((uintptr_t)q_out & 7) || ((uintptr_t)k_out & 7) ||
-      ((uintptr_t)q_norm_w & 7) || ((uintptr_t)k_norm_w & 7) || ((uintptr_t)k_cache & 3) || ((uintptr_t)v_cache & 3))
-    return ADA_ERR_ALIGNMENT;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t items = num_tokens * (num_q_heads + 2 * num_kv_heads);
-  const unsigned blocks = (unsigned)((items + 3) / 4);
-#define ADA_QK(T)                                                                                               \
-  (void)ada::launch_k(small::qk_norm_rope_store_kernel<T>, dim3(blocks), dim3(128), 0, st,                                                    \
-      (const T*)qkv, ld, num_q_heads, num_kv_heads, (const T*)q_norm_w, (const T*)k_norm_w, eps, positions,       \
-      cos_sin, max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out, num_tokens)
-  if (dtype == ADA_DT_BF16) ADA_QK(__nv_bfloat16);
-  else ADA_QK(__half);
-#undef ADA_QK
-  ADA_CHECK_LAUNCH();
-  return ADA_OK;
+  return qk_norm_rope_store_impl(qkv, ld, PartIn{nullptr, 0, 0, 0}, num_tokens, num_q_heads, num_kv_heads, head_dim,
+                                 q_norm_w, k_norm_w, eps, positions, cos_sin, max_position, slot_mapping, k_cache,
+                                 v_cache, k_scale, v_scale, q_out, k_out, dtype, stream);
+}
+
+extern "C" int ada_qk_norm_rope_store_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                            int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                            int32_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                                            const int64_t* positions, const float* cos_sin, int64_t max_position,
+                                            const int32_t* slot_mapping, uint8_t* k_cache, uint8_t* v_cache,
+                                            float k_scale, float v_scale, void* q_out, void* k_out, int dtype,
+                                            void* stream) {
+  if (nparts < 1) return ADA_ERR_INVALID_ARG;
+  return qk_norm_rope_store_impl(nullptr, 0, PartIn{parts, nparts, plane, ldp}, num_tokens, num_q_heads,
+                                 num_kv_heads, head_dim, q_norm_w, k_norm_w, eps, positions, cos_sin, max_position,
+                                 slot_mapping, k_cache, v_cache, k_scale, v_scale, q_out, k_out, dtype, stream);
 }
 
 extern "C" int ada_gated_act(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter, int act,

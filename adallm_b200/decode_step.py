@@ -271,14 +271,26 @@ class Qwen3DecodeEngine:
         self.gemm_only_ws = torch.zeros(max(int(N.lib().ada_nvfp4_gemm_workspace_size(*s_, c.terms))
                                             for s_ in shapes), dtype=torch.uint8, device=d)
         self.attn_ws = torch.zeros(max(self.attn_ws_bytes, 256), dtype=torch.uint8, device=d)
+        # split-K partial planes (TP1 fused path): each projection leaves nplanes fp32 planes
+        # [nplanes][B][n] that its consumer sums; one buffer serves all four (each is consumed
+        # by the very next kernel, which completes before the next projection writes)
+        self.splits = {name: int(N.lib().ada_nvfp4_gemm_splits(B, w.n, w.k, c.terms))
+                       for name, w in self.layers[0].items() if isinstance(w, NVFP4Weight)}
+        self.use_parts = self.fused and c.tp_size == 1 and all(v > 0 for v in self.splits.values())
+        plane_max = max(self.splits[name] * B * w.n for name, w in self.layers[0].items()
+                        if isinstance(w, NVFP4Weight))
+        self.parts = torch.zeros(plane_max if self.use_parts else 4, dtype=torch.float32, device=d)
 
     # ------------------------------------------------------------------ ops
-    def _linear(self, x: torch.Tensor, w: NVFP4Weight, y: torch.Tensor, stream: int):
+    def _linear(self, x: torch.Tensor, w: NVFP4Weight, y: torch.Tensor, stream: int, name: str | None = None):
+        """act-quant + GEMM; with the split count of the partial-plane path, so both paths sum
+        the same K splits in the same order (bit-identical results)."""
         c = self.cfg
-        st = N.lib().ada_nvfp4_linear(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
-                                      w.packed.stride(0), w.sf.data_ptr(), w.scale_2.data_ptr(), w.n, None,
-                                      y.data_ptr(), 0, y.stride(0), c.terms, self.gemm_ws.data_ptr(),
-                                      self.gemm_ws.numel(), stream)
+        ks = self.splits.get(name, 0) if name else 0
+        st = N.lib().ada_nvfp4_linear_ex(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
+                                         w.packed.stride(0), w.sf.data_ptr(), w.scale_2.data_ptr(), w.n, None,
+                                         y.data_ptr(), 0, y.stride(0), c.terms, ks, self.gemm_ws.data_ptr(),
+                                         self.gemm_ws.numel(), stream)
         N.check(st, "NVFP4 kernel")
 
     def _gemm(self, qb, w: NVFP4Weight, y: torch.Tensor, stream: int):
@@ -289,6 +301,30 @@ class Qwen3DecodeEngine:
                                     w.n, w.k, None, y.data_ptr(), 0, y.stride(0), 0, self.gemm_only_ws.data_ptr(),
                                     self.gemm_only_ws.numel(), stream)
         N.check(st, "NVFP4 kernel")
+
+    def _gemm_parts(self, qb, w: NVFP4Weight, name: str, stream: int):
+        c = self.cfg
+        xq, sfx, gx = qb
+        ns = self.splits[name]
+        st = N.lib().ada_nvfp4_gemm_partials(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), self.B, c.terms, self.bn,
+                                             w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                             w.scale_2.data_ptr(), w.n, w.k, self.parts.data_ptr(), w.n,
+                                             self.B * w.n, ns, self.gemm_only_ws.data_ptr(),
+                                             self.gemm_only_ws.numel(), stream)
+        N.check(st, "NVFP4 kernel")
+        return ns, w.n  # planes, row stride
+
+    def _rms_quant_parts(self, planes, w, qb, stream, y=None):
+        """residual += sum(planes); normed = RMSNorm(residual); quantised into qb (or into y when qb is None)."""
+        c = self.cfg
+        ns, ld = planes
+        H = c.hidden
+        rp = self.residual.data_ptr()
+        xq, sfx, gx = qb if qb is not None else (None, None, None)
+        st = N.lib().ada_rmsnorm_quant_parts(self.parts.data_ptr(), ns, self.B * ld, ld, rp, H, rp, H, w.data_ptr(),
+                                             N.ptr(y), H, self.B, H, c.rms_eps, 0, 0, c.terms, self.bn,
+                                             N.ptr(xq), N.ptr(sfx), N.ptr(gx), stream)
+        N.check(st, "rms_norm+quant")
 
     def _rms_quant(self, x, w, qb, stream, residual=None):
         c = self.cfg
@@ -329,6 +365,11 @@ class Qwen3DecodeEngine:
         qn, kn = c.hq * D, c.hkv * D
         if not self.fused:
             self._layers_unfused(lib, stream)
+        elif self.use_parts:
+            self._layers_parts(lib, stream)
+            torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
+            self._argmax(stream)
+            return
         else:
             for li, L in enumerate(self.layers):
                 if li == 0:
@@ -365,6 +406,44 @@ class Qwen3DecodeEngine:
         torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
         self._argmax(stream)
 
+    def _layers_parts(self, lib, stream):
+        """TP1 fused step where every projection leaves split-K partial planes and the next
+        kernel sums them while loading (no split-K reduction inside the GEMMs)."""
+        c = self.cfg
+        B, D = self.B, c.head_dim
+        qn = c.hq * D
+        planes = None
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                self.residual.copy_(self.hidden)
+                self._rms_quant(self.hidden, L["in_norm"], self.q_hidden, stream)
+            else:
+                self._rms_quant_parts(planes, L["in_norm"], self.q_hidden, stream)
+            ns, ld = self._gemm_parts(self.q_hidden, L["qkv"], "qkv", stream)
+            kc, vc = self.kv_cache[0, li], self.kv_cache[1, li]
+            N.check(lib.ada_qk_norm_rope_store_parts(self.parts.data_ptr(), ns, B * ld, ld, B, c.hq, c.hkv, D,
+                                                     L["q_norm"].data_ptr(), L["k_norm"].data_ptr(), c.rms_eps,
+                                                     self.positions.data_ptr(), self.cos_sin.data_ptr(),
+                                                     self.cos_sin.shape[0], self.slot_mapping.data_ptr(),
+                                                     kc.data_ptr(), vc.data_ptr(), 1.0, 1.0, self.q_rot.data_ptr(),
+                                                     None, 0, stream), "qk_norm_rope_store")
+            xq, sfx, gx = self.q_attn
+            N.check(lib.ada_fp8_paged_decode_quant(
+                self.q_rot.data_ptr(), 0, qn, D, kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1),
+                kc.stride(2), self.num_pages, self.block_tables.data_ptr(), self.block_tables.stride(0),
+                self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv, D, c.page_size,
+                D ** -0.5, 1.0, 1.0, 0, None, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
+                gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, stream), "attention")
+            planes = self._gemm_parts(self.q_attn, L["o"], "o", stream)
+            self._rms_quant_parts(planes, L["post_norm"], self.q_hidden, stream)
+            ns, ld = self._gemm_parts(self.q_hidden, L["gate_up"], "gate_up", stream)
+            xq, sfx, gx = self.q_inter
+            N.check(lib.ada_gated_act_quant_parts(self.parts.data_ptr(), ns, B * ld, ld, None, 0, B, c.inter, 0, 0,
+                                                  c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(),
+                                                  stream), "silu_and_mul+quant")
+            planes = self._gemm_parts(self.q_inter, L["down"], "down", stream)
+        self._rms_quant_parts(planes, self.final_norm, None, stream, y=self.xnorm)
+
     def _layers_unfused(self, lib, stream):
         """Reference-shaped sequence: every op a separate kernel (act-quant separate from the GEMM)."""
         c = self.cfg
@@ -376,7 +455,7 @@ class Qwen3DecodeEngine:
                 self._rms(self.hidden, L["in_norm"], self.xnorm, stream)
             else:
                 self._rms(self.hidden, L["in_norm"], self.xnorm, stream, residual=self.residual)
-            self._linear(self.xnorm, L["qkv"], self.qkv, stream)
+            self._linear(self.xnorm, L["qkv"], self.qkv, stream, "qkv")
             kc, vc = self.kv_cache[0, li], self.kv_cache[1, li]
             # q/k RMSNorm + RoPE + FP8 KV store in one kernel (qwen3.py:481-486, attention.py:311-312)
             N.check(lib.ada_qk_norm_rope_store(self.qkv.data_ptr(), self.qkv.stride(0), B, c.hq, c.hkv, D,
@@ -391,13 +470,13 @@ class Qwen3DecodeEngine:
                                              self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv,
                                              D, c.page_size, D ** -0.5, 1.0, 1.0, 0, self.attn.data_ptr(), 0,
                                              self.attn_ws.data_ptr(), self.attn_ws_bytes, stream), "attention")
-            self._linear(self.attn.view(B, qn), L["o"], self.hidden, stream)
+            self._linear(self.attn.view(B, qn), L["o"], self.hidden, stream, "o")
             self._all_reduce(self.hidden)
             self._rms(self.hidden, L["post_norm"], self.xnorm, stream, residual=self.residual)
-            self._linear(self.xnorm, L["gate_up"], self.gate_up, stream)
+            self._linear(self.xnorm, L["gate_up"], self.gate_up, stream, "gate_up")
             N.check(lib.ada_gated_act(self.gate_up.data_ptr(), 2 * c.inter, self.act.data_ptr(), c.inter, B, c.inter,
                                       0, 0, stream), "silu_and_mul")
-            self._linear(self.act, L["down"], self.hidden, stream)
+            self._linear(self.act, L["down"], self.hidden, stream, "down")
             self._all_reduce(self.hidden)
 
     def _argmax(self, stream):

@@ -256,6 +256,40 @@ ADA_API int ada_nvfp4_gemm(const uint8_t* xq, const uint8_t* sfx, const float* g
 ADA_API int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,
                                        unsigned int* status_out, void* stream);
 
+/* Split-K partial mode of the GEMM (no reference counterpart; used by the decode engine):
+ * instead of reducing its K splits, the GEMM writes each split's scaled fp32 partial
+ * y_s[m, n] to parts + s * part_plane + m * part_ld + n (s < nplanes, m < M), and the
+ * kernel that consumes the output sums the planes in order (the *_parts entry points
+ * below), which gives bit for bit what ada_nvfp4_gemm with the same split count stores.
+ * nplanes: 1..8 (ada_nvfp4_gemm_splits gives the library's choice: as many splits as
+ * keep every CTA resident); no bias.  workspace as ada_nvfp4_gemm. */
+ADA_API int ada_nvfp4_gemm_splits(int64_t m, int64_t n, int64_t k, int terms);
+ADA_API int ada_nvfp4_gemm_partials(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
+                                    int block_n, const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                    const float* w_scale_2, int64_t n, int64_t k, float* parts, int64_t part_ld,
+                                    int64_t part_plane, int nplanes, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
+/* Consumers of partial planes (parts: nparts fp32 planes, plane / ldp = floats between planes /
+ * rows, 16-byte aligned): the input element is the plane sum rounded to dtype, then exactly
+ * ada_rmsnorm_quant (xq == NULL: plain RMSNorm into y), ada_gated_act_quant and
+ * ada_qk_norm_rope_store. */
+ADA_API int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                    const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                    const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden, float eps,
+                                    int gemma, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx,
+                                    float* gx, void* stream);
+ADA_API int ada_gated_act_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp, void* y,
+                                      int64_t ldy, int64_t rows, int32_t inter, int act, int dtype, int terms,
+                                      int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
+ADA_API int ada_qk_norm_rope_store_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                         int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                         int32_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                                         const int64_t* positions, const float* cos_sin, int64_t max_position,
+                                         const int32_t* slot_mapping, uint8_t* k_cache, uint8_t* v_cache,
+                                         float k_scale, float v_scale, void* q_out, void* k_out, int dtype,
+                                         void* stream);
+
 /* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum, like torch.argmax),
  * logits bf16/f16.  workspace: ada_argmax_workspace_size(rows, cols) bytes, 8-byte aligned. */
 ADA_API size_t ada_argmax_workspace_size(int64_t rows, int64_t cols);

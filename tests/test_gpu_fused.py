@@ -147,3 +147,128 @@ def test_pdl_toggle_gives_identical_results():
         finally:
             N.lib().ada_set_pdl(prev)
     assert torch.equal(res[0], res[1])
+
+
+# ---- split-K partial planes: GEMM leaves fp32 planes, the next kernel sums them ------------------
+def _rand_weight(n, k, d, seed):
+    from adallm_b200.decode_step import random_nvfp4
+    from adallm_b200.nvfp4_gemm import prepack_scales
+    packed, scale, s2 = random_nvfp4(n, k, seed, d)
+    return packed, prepack_scales(scale, n, k), torch.tensor(s2, dtype=torch.float32, device=d)
+
+
+def _gemm_partials(xq, sfx, gx, m, terms, bn, w, n, k, d):
+    ns = int(N.lib().ada_nvfp4_gemm_splits(m, n, k, terms))
+    assert 1 <= ns <= 8
+    parts = torch.full((ns, m, n), float("nan"), dtype=torch.float32, device=d)
+    ws = torch.zeros(256, dtype=torch.uint8, device=d)
+    N.check(N.lib().ada_nvfp4_gemm_partials(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), m, terms, bn,
+                                            w[0].data_ptr(), w[0].stride(0), w[1].data_ptr(), w[2].data_ptr(), n, k,
+                                            parts.data_ptr(), n, m * n, ns, ws.data_ptr(), 256,
+                                            torch.cuda.current_stream().cuda_stream), "gemm_partials")
+    return parts, ns
+
+
+def _gemm_reduced(xq, sfx, gx, m, terms, bn, w, n, k, ns, d):
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=d)
+    ws = torch.zeros(256, dtype=torch.uint8, device=d)
+    N.check(N.lib().ada_nvfp4_gemm(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), m, terms, bn, w[0].data_ptr(),
+                                   w[0].stride(0), w[1].data_ptr(), w[2].data_ptr(), n, k, None, y.data_ptr(), 0, n,
+                                   ns, ws.data_ptr(), 256, torch.cuda.current_stream().cuda_stream), "gemm")
+    return y
+
+
+def _plane_sum(parts):
+    acc = parts[0].clone()
+    for p in parts[1:]:
+        acc = acc + p  # fp32, plane order
+    return acc.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 6144, 4096), (16, 4096, 12288), (16, 24576, 4096), (5, 512, 1024)])
+def test_gemm_partials_sum_to_reduced_gemm(m, n, k):
+    d = dev()
+    terms, bn = 4, int(N.lib().ada_nvfp4_block_n(m, 4))
+    x = torch.randn((m, k), device=d, dtype=torch.bfloat16)
+    xq, sfx, gx = act_quant(x, terms, bn)
+    w = _rand_weight(n, k, d, n + k)
+    parts, ns = _gemm_partials(xq, sfx, gx, m, terms, bn, w, n, k, d)
+    torch.cuda.synchronize()
+    assert not torch.isnan(parts).any()
+    y = _gemm_reduced(xq, sfx, gx, m, terms, bn, w, n, k, ns, d)
+    assert torch.equal(_plane_sum(parts), y)
+
+
+def test_parts_consumers_match_plain_ops():
+    d = dev()
+    s = torch.cuda.current_stream().cuda_stream
+    m, H, I, terms, bn = 16, 4096, 12288, 4, 16
+    g = torch.Generator(device="cpu").manual_seed(11)
+    # RMSNorm + residual from planes
+    parts = (torch.randn((3, m, H), generator=g) * 2).to(d)
+    x = _plane_sum(parts)
+    res = torch.randn((m, H), generator=g).to(torch.bfloat16).to(d)
+    w = (torch.randn(H, generator=g) * 0.1 + 1).to(torch.bfloat16).to(d)
+    r1, r2 = res.clone(), res.clone()
+    ref = qbufs(m, H, terms, bn, d)
+    got = qbufs(m, H, terms, bn, d)
+    N.check(N.lib().ada_rmsnorm_quant(x.data_ptr(), H, r1.data_ptr(), H, r1.data_ptr(), H, w.data_ptr(), None, 0, m,
+                                      H, 1e-6, 0, 0, terms, bn, ref[0].data_ptr(), ref[1].data_ptr(),
+                                      ref[2].data_ptr(), s), "rmsq")
+    N.check(N.lib().ada_rmsnorm_quant_parts(parts.data_ptr(), 3, m * H, H, r2.data_ptr(), H, r2.data_ptr(), H,
+                                            w.data_ptr(), None, 0, m, H, 1e-6, 0, 0, terms, bn, got[0].data_ptr(),
+                                            got[1].data_ptr(), got[2].data_ptr(), s), "rmsq_parts")
+    y1, y2 = torch.empty_like(x), torch.empty_like(x)
+    r3, r4 = res.clone(), res.clone()
+    N.check(N.lib().ada_rmsnorm(x.data_ptr(), H, r3.data_ptr(), H, r3.data_ptr(), H, w.data_ptr(), y1.data_ptr(), H,
+                                m, H, 1e-6, 0, 0, s), "rms")
+    N.check(N.lib().ada_rmsnorm_quant_parts(parts.data_ptr(), 3, m * H, H, r4.data_ptr(), H, r4.data_ptr(), H,
+                                            w.data_ptr(), y2.data_ptr(), H, m, H, 1e-6, 0, 0, terms, bn, None, None,
+                                            None, s), "rms_parts_plain")
+    torch.cuda.synchronize()
+    same(got, ref)
+    assert torch.equal(r1, r2) and torch.equal(y1, y2) and torch.equal(r3, r4)
+    # SiLU * up from planes
+    parts = (torch.randn((1, m, 2 * I), generator=g) * 2).to(d)
+    x = _plane_sum(parts)
+    ref = act_quant(gated_act(x, 0), terms, bn)
+    got = qbufs(m, I, terms, bn, d)
+    N.check(N.lib().ada_gated_act_quant_parts(parts.data_ptr(), 1, m * 2 * I, 2 * I, None, 0, m, I, 0, 0, terms, bn,
+                                              got[0].data_ptr(), got[1].data_ptr(), got[2].data_ptr(), s), "act_parts")
+    torch.cuda.synchronize()
+    same(got, ref)
+
+
+def test_qk_norm_rope_store_from_planes():
+    from adallm_b200.rotary_embedding import build_cos_sin_cache
+    d = dev()
+    s = torch.cuda.current_stream().cuda_stream
+    T, hq, hkv, D = 7, 32, 8, 128
+    width = (hq + 2 * hkv) * D
+    g = torch.Generator(device="cpu").manual_seed(5)
+    parts = torch.randn((4, T, width), generator=g).to(d)
+    qkv = _plane_sum(parts)
+    qw = (torch.randn(D, generator=g) * 0.1 + 1).to(torch.bfloat16).to(d)
+    kw = (torch.randn(D, generator=g) * 0.1 + 1).to(torch.bfloat16).to(d)
+    pos = torch.randint(0, 100, (T,), generator=g).to(d)
+    cs = build_cos_sin_cache(D, 128, 1e6, None, d).contiguous()
+    slots = torch.arange(T, dtype=torch.int32, device=d) * 3
+    out = []
+    for use_parts in (False, True):
+        kc = torch.zeros((64, 1, hkv, D), dtype=torch.uint8, device=d)
+        vc = torch.zeros_like(kc)
+        q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=d)
+        if use_parts:
+            st = N.lib().ada_qk_norm_rope_store_parts(parts.data_ptr(), 4, T * width, width, T, hq, hkv, D,
+                                                      qw.data_ptr(), kw.data_ptr(), 1e-6, pos.data_ptr(),
+                                                      cs.data_ptr(), cs.shape[0], slots.data_ptr(), kc.data_ptr(),
+                                                      vc.data_ptr(), 1.0, 1.0, q.data_ptr(), None, 0, s)
+        else:
+            st = N.lib().ada_qk_norm_rope_store(qkv.data_ptr(), width, T, hq, hkv, D, qw.data_ptr(), kw.data_ptr(),
+                                                1e-6, pos.data_ptr(), cs.data_ptr(), cs.shape[0], slots.data_ptr(),
+                                                kc.data_ptr(), vc.data_ptr(), 1.0, 1.0, q.data_ptr(), None, 0, s)
+        N.check(st, "qk")
+        out.append((q, kc, vc))
+    torch.cuda.synchronize()
+    for a, b in zip(out[0], out[1]):
+        assert torch.equal(a, b)
