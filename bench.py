@@ -352,13 +352,24 @@ def run_ours(args, rank, world, local_rank):
                                             sfx.data_ptr(), gx.data_ptr(), sp), "act_quant")
         quant[kk] = (xq.clone(), sfx.clone(), gx.clone())
 
+    # the GEMM exactly as the decode step runs it: split-K partial planes when the engine uses
+    # them (TP1), else the reduced bf16 output
+    part_buf = torch.empty(max(8 * m * w.n for w in lin), dtype=torch.float32, device=dev)
+
     def gemm_launch(w):
         a, b, c_ = quant[w.k]
-        N.check(N.lib().ada_nvfp4_gemm(a.data_ptr(), b.data_ptr(), c_.data_ptr(), m, cfg.terms, bn,
-                                       w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
-                                       w.scale_2.data_ptr(), w.n, w.k, None, ys[w.n].data_ptr(), 0, w.n, 0,
-                                       ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream),
-                "gemm")
+        st = torch.cuda.current_stream(dev).cuda_stream
+        if engine.use_parts:
+            ns = int(N.lib().ada_nvfp4_gemm_splits(m, w.n, w.k, cfg.terms))
+            N.check(N.lib().ada_nvfp4_gemm_partials(a.data_ptr(), b.data_ptr(), c_.data_ptr(), m, cfg.terms, bn,
+                                                    w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                                    w.scale_2.data_ptr(), w.n, w.k, part_buf.data_ptr(), w.n,
+                                                    m * w.n, ns, ws.data_ptr(), ws.numel(), st), "gemm")
+        else:
+            N.check(N.lib().ada_nvfp4_gemm(a.data_ptr(), b.data_ptr(), c_.data_ptr(), m, cfg.terms, bn,
+                                           w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                           w.scale_2.data_ptr(), w.n, w.k, None, ys[w.n].data_ptr(), 0, w.n, 0,
+                                           ws.data_ptr(), ws.numel(), st), "gemm")
 
     def graph_of(ws_list):
         """GEMM launches captured once, so the timing has no host launch overhead."""
@@ -403,7 +414,8 @@ def run_ours(args, rank, world, local_rank):
     traffic = traffic_from_profile()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
-                "kernel": "adallm_b200 nvfp4 gemm_kernel (tcgen05 mxf4nvf4)",
+                "kernel": "adallm_b200 nvfp4 gemm_kernel (tcgen05 mxf4nvf4)" +
+                          (", split-K partial planes as in the step" if engine.use_parts else ""),
                 "alg_bytes_per_launch": int(alg_bytes), "us_per_launch": round(gemm_ms * 1e3, 3),
                 "launch_mix": "qkv/o/gate_up/down of all layers, batch 16", "per_shape": per_shape}
 
