@@ -69,6 +69,146 @@ __device__ __forceinline__ uint4 tile_ld16(const uint8_t* tile, int row, int chu
   return *reinterpret_cast<const uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// Q operand (B of the score MMA) of the GQA group of KV head kvh: head g of the group,
+// d in [32c, 32c+32), fp16 as the reference (attention.py:314-324).  qf[2s], qf[2s+1] = k-step s.
+template <typename TQ>
+__device__ __forceinline__ void load_q_frag(const Params& P, int b, int kvh, int g, int c, uint32_t* qf) {
+  if (g < P.group) {
+    const TQ* qp =
+        reinterpret_cast<const TQ*>(P.q) + (int64_t)b * P.q_sb + (int64_t)(kvh * P.group + g) * P.q_sh + 32 * c;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float f[8];
+      unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * i), f);
+      qf[4 * i + 0] = pack_half2(f[0], f[1]);
+      qf[4 * i + 1] = pack_half2(f[2], f[3]);
+      qf[4 * i + 2] = pack_half2(f[4], f[5]);
+      qf[4 * i + 3] = pack_half2(f[6], f[7]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qf[i] = 0u;
+  }
+}
+
+// Online-softmax state of one warp over the tiles it has seen: O^T fragments (d = 16g + 2mt
+// (+1), heads 2c / 2c+1) and per head pair the running max (log2 units) and sum.
+struct WarpState {
+  float acc[8][4];
+  float m0, m1, l0, l1;
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  }
+};
+
+// Fold one 16-token tile (K at kt, V at kt + TILE_BYTES, 128-byte swizzled) into the warp's
+// state.  Tokens outside [lo, t1) or of a hole in the block table get probability 0.
+__device__ __forceinline__ void attn_tile(const Params& P, const uint8_t* kt, bool blk_ok, int tt, int ctx, int lo,
+                                          int t1, const uint32_t* qf, WarpState& st, __half (*p_s)[16], int g,
+                                          int c) {
+  const uint8_t* vt = kt + TILE_BYTES;
+  uint4 k0[2], k8[2], vv[4];
+  k0[0] = tile_ld16(kt, g, 2 * c);
+  k0[1] = tile_ld16(kt, g, 2 * c + 1);
+  k8[0] = tile_ld16(kt, g + 8, 2 * c);
+  k8[1] = tile_ld16(kt, g + 8, 2 * c + 1);
+  const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+  const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // Rows at or past ctx (and holes) may hold stale or uninitialised bytes (NaN in
+    // e4m3); they get probability 0, so their V must be finite: zero them.
+    vv[i] = (blk_ok && tt + toks[i] < ctx) ? tile_ld16(vt, toks[i], g) : z;
+  }
+
+  // ---- scores S^T[token][head] -------------------------------------------
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t* kg = reinterpret_cast<const uint32_t*>(k0);
+  const uint32_t* kg8 = reinterpret_cast<const uint32_t*>(k8);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t a[4];
+    a[0] = e4m3x2_to_f16x2((uint16_t)(kg[ks] & 0xFFFFu));
+    a[1] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] & 0xFFFFu));
+    a[2] = e4m3x2_to_f16x2((uint16_t)(kg[ks] >> 16));
+    a[3] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] >> 16));
+    mma_16816_f16(sc, a, &qf[2 * ks]);
+  }
+  const int tg = tt + g, tg8 = tt + g + 8;
+  const bool vg = blk_ok && tg >= lo && tg < t1;
+  const bool vg8 = blk_ok && tg8 >= lo && tg8 < t1;
+  const float x0 = vg ? sc[0] * P.scale_log2 : -INFINITY;   // token g,   head 2c
+  const float x1 = vg ? sc[1] * P.scale_log2 : -INFINITY;   // token g,   head 2c+1
+  const float x2 = vg8 ? sc[2] * P.scale_log2 : -INFINITY;  // token g+8, head 2c
+  const float x3 = vg8 ? sc[3] * P.scale_log2 : -INFINITY;  // token g+8, head 2c+1
+  float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+  }
+  const float mn0 = fmaxf(st.m0, mx0), mn1 = fmaxf(st.m1, mx1);
+  float al0 = 1.f, al1 = 1.f, p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+  if (mn0 != -INFINITY) {
+    al0 = fast_exp2(st.m0 - mn0);
+    p0 = fast_exp2(x0 - mn0);
+    p2 = fast_exp2(x2 - mn0);
+  }
+  if (mn1 != -INFINITY) {
+    al1 = fast_exp2(st.m1 - mn1);
+    p1 = fast_exp2(x1 - mn1);
+    p3 = fast_exp2(x3 - mn1);
+  }
+  st.m0 = mn0;
+  st.m1 = mn1;
+  // fp32 probabilities feed the row sum, fp16 ones feed P.V (attention.py:219-223)
+  const __half hp0 = __float2half_rn(p0), hp1 = __float2half_rn(p1);
+  const __half hp2 = __float2half_rn(p2), hp3 = __float2half_rn(p3);
+  st.l0 = st.l0 * al0 + (p0 + p2);
+  st.l1 = st.l1 * al1 + (p1 + p3);
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    st.acc[mt][0] *= al0;
+    st.acc[mt][1] *= al1;
+    st.acc[mt][2] *= al0;
+    st.acc[mt][3] *= al1;
+  }
+  // ---- transpose P through shared memory: P^T operand wants (token pairs, head g)
+  p_s[2 * c][g] = hp0;
+  p_s[2 * c + 1][g] = hp1;
+  p_s[2 * c][g + 8] = hp2;
+  p_s[2 * c + 1][g + 8] = hp3;
+  __syncwarp();
+  uint32_t bp[2];
+  bp[0] = *reinterpret_cast<const uint32_t*>(&p_s[g][2 * c]);
+  bp[1] = *reinterpret_cast<const uint32_t*>(&p_s[g][2 * c + 8]);
+  __syncwarp();
+
+  // ---- O^T[d][head] += V^T . P^T ----------------------------------------
+  const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0]);
+  const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1]);
+  const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&vv[2]);
+  const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&vv[3]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t sel = half ? 0x7362u : 0x5140u;
+      const uint32_t lo01 = prmt(v0[j], v1[j], sel);
+      const uint32_t lo89 = prmt(v8[j], v9[j], sel);
+      uint32_t a[4];
+      a[0] = e4m3x2_to_f16x2((uint16_t)(lo01 & 0xFFFFu));
+      a[1] = e4m3x2_to_f16x2((uint16_t)(lo01 >> 16));
+      a[2] = e4m3x2_to_f16x2((uint16_t)(lo89 & 0xFFFFu));
+      a[3] = e4m3x2_to_f16x2((uint16_t)(lo89 >> 16));
+      mma_16816_f16(st.acc[2 * j + half], a, bp);
+    }
+  }
+}
+
 // One warp = one work item (sequence b, KV head, 256-token split) at a time: items are dealt
 // to the grid's warps round-robin.  Each warp streams its item's tiles through its own ring of
 // RING tile slots (K and V, 4 KB per tile): lane i looks up tile i's page, lane 0 issues the
@@ -144,30 +284,10 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
     };
     for (int k = 0; k < RING && k < ntiles; ++k) issue(k, uses + k);
 
-    // Q operand (B of the score MMA): head g of the group, d in [32c, 32c+32),
-    // fp16 as the reference (attention.py:314-324).  qf[2s], qf[2s+1] = k-step s.
     uint32_t qf[16];
-    if (g < group) {
-      const TQ* qp =
-          reinterpret_cast<const TQ*>(P.q) + (int64_t)b * P.q_sb + (int64_t)(kvh * group + g) * P.q_sh + 32 * c;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float f[8];
-        unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * i), f);
-        qf[4 * i + 0] = pack_half2(f[0], f[1]);
-        qf[4 * i + 1] = pack_half2(f[2], f[3]);
-        qf[4 * i + 2] = pack_half2(f[4], f[5]);
-        qf[4 * i + 3] = pack_half2(f[6], f[7]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) qf[i] = 0u;
-    }
-
-    float acc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    load_q_frag<TQ>(P, b, kvh, g, c, qf);
+    WarpState ws;
+    ws.init();
     bool failed = false;
 
     for (int k = 0; k < ntiles; ++k) {
@@ -177,107 +297,8 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
         failed = true;
         break;
       }
-      const int tt = t0 + TILE * k;
-      const uint8_t* kt = ring + slot * 2 * TILE_BYTES;
-      const uint8_t* vt = kt + TILE_BYTES;
       const bool blk_ok = __shfl_sync(0xffffffffu, my_block, k) >= 0;
-      uint4 k0[2], k8[2], vv[4];
-      k0[0] = tile_ld16(kt, g, 2 * c);
-      k0[1] = tile_ld16(kt, g, 2 * c + 1);
-      k8[0] = tile_ld16(kt, g + 8, 2 * c);
-      k8[1] = tile_ld16(kt, g + 8, 2 * c + 1);
-      const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-      const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        // Rows at or past ctx (and holes) may hold stale or uninitialised bytes (NaN in
-        // e4m3); they get probability 0, so their V must be finite: zero them.
-        vv[i] = (blk_ok && tt + toks[i] < ctx) ? tile_ld16(vt, toks[i], g) : z;
-      }
-
-      // ---- scores S^T[token][head] -----------------------------------------
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t* kg = reinterpret_cast<const uint32_t*>(k0);
-      const uint32_t* kg8 = reinterpret_cast<const uint32_t*>(k8);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a[4];
-        a[0] = e4m3x2_to_f16x2((uint16_t)(kg[ks] & 0xFFFFu));
-        a[1] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] & 0xFFFFu));
-        a[2] = e4m3x2_to_f16x2((uint16_t)(kg[ks] >> 16));
-        a[3] = e4m3x2_to_f16x2((uint16_t)(kg8[ks] >> 16));
-        mma_16816_f16(sc, a, &qf[2 * ks]);
-      }
-      const int tg = tt + g, tg8 = tt + g + 8;
-      const bool vg = blk_ok && tg >= lo && tg < t1;
-      const bool vg8 = blk_ok && tg8 >= lo && tg8 < t1;
-      const float x0 = vg ? sc[0] * P.scale_log2 : -INFINITY;   // token g,   head 2c
-      const float x1 = vg ? sc[1] * P.scale_log2 : -INFINITY;   // token g,   head 2c+1
-      const float x2 = vg8 ? sc[2] * P.scale_log2 : -INFINITY;  // token g+8, head 2c
-      const float x3 = vg8 ? sc[3] * P.scale_log2 : -INFINITY;  // token g+8, head 2c+1
-      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-      }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      float al0 = 1.f, al1 = 1.f, p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-      if (mn0 != -INFINITY) {
-        al0 = fast_exp2(m0 - mn0);
-        p0 = fast_exp2(x0 - mn0);
-        p2 = fast_exp2(x2 - mn0);
-      }
-      if (mn1 != -INFINITY) {
-        al1 = fast_exp2(m1 - mn1);
-        p1 = fast_exp2(x1 - mn1);
-        p3 = fast_exp2(x3 - mn1);
-      }
-      m0 = mn0;
-      m1 = mn1;
-      // fp32 probabilities feed the row sum, fp16 ones feed P.V (attention.py:219-223)
-      const __half hp0 = __float2half_rn(p0), hp1 = __float2half_rn(p1);
-      const __half hp2 = __float2half_rn(p2), hp3 = __float2half_rn(p3);
-      l0 = l0 * al0 + (p0 + p2);
-      l1 = l1 * al1 + (p1 + p3);
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        acc[mt][0] *= al0;
-        acc[mt][1] *= al1;
-        acc[mt][2] *= al0;
-        acc[mt][3] *= al1;
-      }
-      // ---- transpose P through shared memory: P^T operand wants (token pairs, head g)
-      p_s[warp][2 * c][g] = hp0;
-      p_s[warp][2 * c + 1][g] = hp1;
-      p_s[warp][2 * c][g + 8] = hp2;
-      p_s[warp][2 * c + 1][g + 8] = hp3;
-      __syncwarp();
-      uint32_t bp[2];
-      bp[0] = *reinterpret_cast<const uint32_t*>(&p_s[warp][g][2 * c]);
-      bp[1] = *reinterpret_cast<const uint32_t*>(&p_s[warp][g][2 * c + 8]);
-      __syncwarp();
-
-      // ---- O^T[d][head] += V^T . P^T --------------------------------------
-      const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0]);
-      const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1]);
-      const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&vv[2]);
-      const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&vv[3]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t sel = half ? 0x7362u : 0x5140u;
-          const uint32_t lo01 = prmt(v0[j], v1[j], sel);
-          const uint32_t lo89 = prmt(v8[j], v9[j], sel);
-          uint32_t a[4];
-          a[0] = e4m3x2_to_f16x2((uint16_t)(lo01 & 0xFFFFu));
-          a[1] = e4m3x2_to_f16x2((uint16_t)(lo01 >> 16));
-          a[2] = e4m3x2_to_f16x2((uint16_t)(lo89 & 0xFFFFu));
-          a[3] = e4m3x2_to_f16x2((uint16_t)(lo89 >> 16));
-          mma_16816_f16(acc[2 * j + half], a, bp);
-        }
-      }
+      attn_tile(P, ring + slot * 2 * TILE_BYTES, blk_ok, t0 + TILE * k, ctx, lo, t1, qf, ws, p_s[warp], g, c);
       // every byte of the slot has been consumed by the MMAs above: refill it with tile k + RING
       __syncwarp();
       if (k + RING < ntiles) {
@@ -286,6 +307,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
       }
     }
     uses += ntiles;
+    float m0 = ws.m0, m1 = ws.m1, l0 = ws.l0, l1 = ws.l1;
     if (failed) {  // a tile never arrived: poison this split's result and stop using the ring
       m0 = m1 = l0 = l1 = __int_as_float(0x7fc00000);
     }
@@ -303,7 +325,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
       for (int mt = 0; mt < 8; ++mt) {
         const int d = 16 * g + 2 * mt;
         *reinterpret_cast<float2*>(P.o_part + row0 * D + d) =
-            make_float2(acc[mt][0] * P.v_scale, acc[mt][2] * P.v_scale);
+            make_float2(ws.acc[mt][0] * P.v_scale, ws.acc[mt][2] * P.v_scale);
       }
       if (g == 0) *reinterpret_cast<float2*>(P.ml_part + row0 * 2) = make_float2(m0, l0);
     }
@@ -312,12 +334,191 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
       for (int mt = 0; mt < 8; ++mt) {
         const int d = 16 * g + 2 * mt;
         *reinterpret_cast<float2*>(P.o_part + row1 * D + d) =
-            make_float2(acc[mt][1] * P.v_scale, acc[mt][3] * P.v_scale);
+            make_float2(ws.acc[mt][1] * P.v_scale, ws.acc[mt][3] * P.v_scale);
       }
       if (g == 0) *reinterpret_cast<float2*>(P.ml_part + row1 * 2) = make_float2(m1, l1);
     }
     if (failed) break;
   }
+}
+
+// ---- short caches: the whole decode attention of a token in one cluster ----------------
+// When the cache holds at most FUSED_MAX_TOKENS tokens per sequence, the split/merge pair is
+// replaced by one kernel: grid (Hkv, rows), cluster (Hkv, 1, 1) = one CTA per KV head of a
+// token.  The 4 warps of a CTA take the token's tiles round-robin (each through its own TMA
+// ring), merge their softmax states in shared memory and write the normalised heads of the
+// group.  With a quantised output the cluster combines the token row's amax through DSMEM and
+// every CTA quantises its heads' slice of the o_proj operand (quant.cuh).
+constexpr int FUSED_MAX_TOKENS = 1024;
+constexpr int FUSED_SMEM = 1024 + SPLIT_WARPS * RING * 2 * TILE_BYTES + SPLIT_WARPS * RING * 8 + 64;
+
+template <typename TQ, typename TO>
+__global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
+    decode_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Params P,
+                        TO* __restrict__ out, int batch, q::QuantDst dst, int quant) {
+  using namespace sm100;
+  cl::cluster_arrive_relaxed();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int group = P.group;
+  const int kvh = blockIdx.x, b = blockIdx.y;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = ring_base + warp * RING * 2 * TILE_BYTES;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ring_base + SPLIT_WARPS * RING * 2 * TILE_BYTES) + warp * RING;
+  int* abort_flag = reinterpret_cast<int*>(reinterpret_cast<uint64_t*>(ring_base + SPLIT_WARPS * RING * 2 * TILE_BYTES) +
+                                           SPLIT_WARPS * RING);
+  __shared__ __align__(16) __half p_s[SPLIT_WARPS][8][16];
+  __shared__ float sm_m[SPLIT_WARPS][8], sm_l[SPLIT_WARPS][8];
+  __shared__ float red[cl::MAX_WARPS];
+  __shared__ float slots[cl::MAX_CLUSTER];
+
+  if (threadIdx.x == 0) *abort_flag = 0;
+  if (lane < RING) mbar_init(&bar[lane], 1);
+  fence_mbar_init();
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+
+  const int o_begin = kvh * group * (D / 8), o_count = group * (D / 8);  // this CTA's octets of the row
+  if (b >= batch) {  // padding row of the last token tile: zero operand, unit scale
+    if (quant) {
+      for (int o = threadIdx.x; o < o_count; o += blockDim.x) q::zero_oct(dst, b, o_begin + o);
+      if (kvh == 0 && threadIdx.x == 0) dst.gx[b] = 1.f;
+    }
+    cl::cluster_wait();
+    return;
+  }
+  const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
+  int start, start16, nsplit;
+  seq_range(P, ctx, start, start16, nsplit);
+  const int t0 = start16, t1 = ctx;
+  const int ntiles = ctx > t0 ? (t1 - t0 + 15) >> 4 : 0;
+  const int nk = ntiles > warp ? (ntiles - warp + SPLIT_WARPS - 1) / SPLIT_WARPS : 0;  // this warp's tiles
+  // lane j: page of this warp's j-th tile (tile warp + 4j)
+  int my_block = -1, my_row0 = 0;
+  if (lane < nk) {
+    const int tt = t0 + TILE * (warp + SPLIT_WARPS * lane);
+    const int page_idx = tt / P.page;
+    my_row0 = tt - page_idx * P.page;
+    my_block = __ldg(P.bt + (int64_t)b * P.bt_stride + page_idx);
+    if (my_block >= P.num_pages) my_block = -1;
+  }
+  auto issue = [&](int k) {
+    const int blk = __shfl_sync(0xffffffffu, my_block, k);
+    const int row0 = __shfl_sync(0xffffffffu, my_row0, k);
+    if (lane == 0) {
+      const int slot = k % RING;
+      uint64_t* bb = &bar[slot];
+      if (blk >= 0) {
+        mbar_arrive_expect_tx(bb, 2 * TILE_BYTES);
+        tma_load_4d(ring + slot * 2 * TILE_BYTES, &tmk, bb, 0, kvh, row0, blk);
+        tma_load_4d(ring + slot * 2 * TILE_BYTES + TILE_BYTES, &tmv, bb, 0, kvh, row0, blk);
+      } else {
+        mbar_arrive_plain(bb);
+      }
+    }
+  };
+  for (int k = 0; k < RING && k < nk; ++k) issue(k);
+  uint32_t qf[16];
+  load_q_frag<TQ>(P, b, kvh, g, c, qf);
+  WarpState ws;
+  ws.init();
+  bool failed = false;
+  for (int k = 0; k < nk; ++k) {
+    const int slot = k % RING;
+    if (!mbar_wait_bounded(&bar[slot], (k / RING) & 1, abort_flag, nullptr, 0u)) {
+      failed = true;
+      break;
+    }
+    const bool blk_ok = __shfl_sync(0xffffffffu, my_block, k) >= 0;
+    attn_tile(P, ring + slot * 2 * TILE_BYTES, blk_ok, t0 + TILE * (warp + SPLIT_WARPS * k), ctx, start, t1, qf, ws,
+              p_s[warp], g, c);
+    __syncwarp();
+    if (k + RING < nk) {
+      if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(k + RING);
+    }
+  }
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    ws.l0 += __shfl_xor_sync(0xffffffffu, ws.l0, o);
+    ws.l1 += __shfl_xor_sync(0xffffffffu, ws.l1, o);
+  }
+  if (failed) *abort_flag = 1;
+  __syncthreads();  // every warp is done with its ring: the ring memory is reused below
+  float(*sm_o)[8][D] = reinterpret_cast<float(*)[8][D]>(ring_base);  // [warp][head][d]
+  float* vals = reinterpret_cast<float*>(ring_base + SPLIT_WARPS * 8 * D * sizeof(float));  // [head][d]
+  if (g == 0) {
+    sm_m[warp][2 * c] = ws.m0;
+    sm_m[warp][2 * c + 1] = ws.m1;
+    sm_l[warp][2 * c] = ws.l0;
+    sm_l[warp][2 * c + 1] = ws.l1;
+  }
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int d = 16 * g + 2 * mt;
+    sm_o[warp][2 * c][d] = ws.acc[mt][0];
+    sm_o[warp][2 * c + 1][d] = ws.acc[mt][1];
+    sm_o[warp][2 * c][d + 1] = ws.acc[mt][2];
+    sm_o[warp][2 * c + 1][d + 1] = ws.acc[mt][3];
+  }
+  __syncthreads();
+  const bool bad = *abort_flag != 0;  // a tile never arrived: poison the token's output
+  const int d = threadIdx.x;          // 128 threads == D
+  float amax = 0.f;
+  for (int h = 0; h < group; ++h) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < SPLIT_WARPS; ++w) M = fmaxf(M, sm_m[w][h]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < SPLIT_WARPS; ++w) {
+        const float sw = fast_exp2(sm_m[w][h] - M);
+        L += sm_l[w][h] * sw;
+        O += sm_o[w][h][d] * sw;
+      }
+    }
+    float v = L > 0.f ? (O * P.v_scale) / L : 0.f;
+    if (bad) v = __int_as_float(0x7fc00000);
+    v = to_f32(from_f32<TO>(v));
+    if (out) out[((int64_t)b * P.num_heads + kvh * group + h) * D + d] = from_f32<TO>(v);
+    vals[h * D + d] = v;
+    amax = fmaxf(amax, fabsf(v));
+  }
+  cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
+  if (!quant) return;
+  const q::RowQ rq = q::make_rowq(cl::cluster_allreduce<cl::OpMax>(amax, red, slots), dst.terms);
+  if (kvh == 0 && threadIdx.x == 0) dst.gx[b] = rq.g[0];
+  for (int o0 = 0; o0 < o_count; o0 += blockDim.x) {  // every lane calls quant_oct (terms == 1 pairs lanes)
+    const int o = o0 + (int)threadIdx.x;
+    float r[8];
+    if (o < o_count) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = vals[o * 8 + i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = 0.f;
+    }
+    q::quant_oct(dst, b, o_begin + (o < o_count ? o : 0), r, rq, o < o_count);
+  }
+}
+
+template <typename TQ, typename TO>
+inline bool fused_smem_ready() {
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return true;
+  if (cudaFuncSetAttribute(decode_fused_kernel<TQ, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, FUSED_SMEM) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(decode_fused_kernel<TQ, TO>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return false;
+  done[dev] = true;
+  return true;
 }
 
 // ---- split merge ------------------------------------------------------------------
@@ -605,6 +806,28 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
     return ADA_ERR_CUDA;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if ((int64_t)max_pages * page_size <= attn::FUSED_MAX_TOKENS && num_kv_heads <= cl::MAX_CLUSTER) {
+    // short cache: split, merge and (optionally) quantisation in one cluster per token
+    const int rows = qd ? (int)cdiv(batch, qd->bn) * qd->bn : batch;
+    if (rows > 65535) return ADA_ERR_UNSUPPORTED;
+    const q::QuantDst none{nullptr, nullptr, nullptr, 1, 16, num_heads * head_dim};
+    const q::QuantDst& dq = qd ? *qd : none;
+    const dim3 fg((unsigned)num_kv_heads, (unsigned)rows);
+#define ADA_FUSED(TQ, TO)                                                                                       \
+    do {                                                                                                        \
+      if (!attn::fused_smem_ready<TQ, TO>()) return ADA_ERR_CUDA;                                               \
+      (void)ada::launch_kc(attn::decode_fused_kernel<TQ, TO>, fg, dim3(attn::SPLIT_WARPS * 32), attn::FUSED_SMEM, \
+                           st, num_kv_heads, tmk, tmv, P, reinterpret_cast<TO*>(out), (int)batch, dq, qd ? 1 : 0); \
+    } while (0)
+    if (q_dtype == ADA_DT_BF16) {
+      if (out_dtype == ADA_DT_BF16) ADA_FUSED(__nv_bfloat16, __nv_bfloat16); else ADA_FUSED(__nv_bfloat16, __half);
+    } else {
+      if (out_dtype == ADA_DT_BF16) ADA_FUSED(__half, __nv_bfloat16); else ADA_FUSED(__half, __half);
+    }
+#undef ADA_FUSED
+    ADA_CHECK_LAUNCH();
+    return ADA_OK;
+  }
   // persistent-style grid: every warp takes work items (sequence, KV head, split) round-robin
   static int sms[64] = {0};
   int dev = 0;

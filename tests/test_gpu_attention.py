@@ -45,8 +45,9 @@ def test_pages_and_groups(page, hq, hkv):
 
 
 @pytest.mark.parametrize("window", [1, 17, 1024])
-def test_sliding_window(window):
-    case = oa.make_paged_case(11, batch=6, hq=32, hkv=16, d=128, page=16, ctx_lo=1, ctx_hi=3000)
+@pytest.mark.parametrize("hkv,ctx_hi", [(16, 3000), (8, 1000)])  # split-K path / short-cache one-cluster path
+def test_sliding_window(window, hkv, ctx_hi):
+    case = oa.make_paged_case(11, batch=6, hq=32, hkv=hkv, d=128, page=16, ctx_lo=1, ctx_hi=ctx_hi)
     out, ref = _run(case, window=window)
     assert rel_l2(out, ref) < TOL
 
