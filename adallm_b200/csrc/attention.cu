@@ -357,7 +357,8 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
     decode_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Params P,
                         TO* __restrict__ out, int batch, q::QuantDst dst, int quant) {
   using namespace sm100;
-  cl::cluster_arrive_relaxed();
+  __shared__ cl::Exchange xch;
+  cl::cluster_start(&xch, 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int group = P.group;
@@ -372,7 +373,6 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   __shared__ __align__(16) __half p_s[SPLIT_WARPS][8][16];
   __shared__ float sm_m[SPLIT_WARPS][8], sm_l[SPLIT_WARPS][8];
   __shared__ float red[cl::MAX_WARPS];
-  __shared__ float slots[cl::MAX_CLUSTER];
 
   if (threadIdx.x == 0) *abort_flag = 0;
   if (lane < RING) mbar_init(&bar[lane], 1);
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   }
   cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
   if (!quant) return;
-  const q::RowQ rq = q::make_rowq(cl::cluster_allreduce<cl::OpMax>(amax, red, slots), dst.terms);
+  const q::RowQ rq = q::make_rowq(cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch), dst.terms);
   if (kvh == 0 && threadIdx.x == 0) dst.gx[b] = rq.g[0];
   for (int o0 = 0; o0 < o_count; o0 += blockDim.x) {  // every lane calls quant_oct (terms == 1 pairs lanes)
     const int o = o0 + (int)threadIdx.x;
@@ -617,11 +617,11 @@ __global__ void __launch_bounds__(128) decode_reduce_kernel(Params P, TO* __rest
 template <typename TO, int MAXU>
 __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* __restrict__ out, int batch,
                                                                   q::QuantDst dst) {
-  cl::cluster_arrive_relaxed();
+  __shared__ float red[cl::MAX_WARPS];
+  __shared__ cl::Exchange xch;
+  cl::cluster_start(&xch, 1);
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[cl::MAX_WARPS];
-  __shared__ float slots[cl::MAX_CLUSTER];
   const int b = blockIdx.y;
   const int row_len = P.num_heads * D;
   const int o0 = cl::slice_octet(row_len >> 4, blockIdx.x, gridDim.x);
@@ -658,7 +658,7 @@ __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* 
     if (out) *reinterpret_cast<uint4*>(out + (int64_t)b * row_len + o * 8) = pack8<TO>(v[u]);
   }
   cl::cluster_wait();
-  const q::RowQ rq = q::make_rowq(cl::cluster_allreduce<cl::OpMax>(amax, red, slots), dst.terms);
+  const q::RowQ rq = q::make_rowq(cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch), dst.terms);
   if (blockIdx.x == 0 && threadIdx.x == 0) dst.gx[b] = rq.g[0];
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {

@@ -2,14 +2,14 @@
 // too short to keep one CTA busy for long is split over the CTAs of one cluster,
 // which combine their partial reductions through distributed shared memory.
 //
-// Protocol of a cluster row kernel (every thread of every CTA runs all of it; no
-// thread returns early, so every hardware cluster barrier completes):
-//   cluster_arrive_relaxed()            right after start
+// Protocol of a cluster row kernel (every thread of every CTA runs all of it up to its
+// last reduction; a padding CTA returns only after cluster_wait()):
+//   cluster_start(xch, n)                  right after start: n exchanges, one per reduction
 //   ... load the slice, local partial ...
-//   cluster_wait()                      every CTA of the cluster is running: DSMEM is live
-//   v = cluster_allreduce<Op>(v, slots) one per reduction, each with its own slot array
-// A CTA writes the remote shared memory of its peers only between the first wait and
-// its last reduction barrier, so no CTA exits while a peer still writes into it.
+//   cluster_wait()                         every CTA of the cluster is running: DSMEM is live
+//   v = cluster_allreduce_x<Op>(v, red, &xch[i])   one per reduction
+// A CTA is written by its peers only before its own wait on that exchange completes, so no
+// CTA exits while a peer still writes into it.
 #pragma once
 
 #include "common.cuh"
@@ -77,18 +77,75 @@ __device__ __forceinline__ float block_reduce(float v, float* red) {
   return r;
 }
 
-// Cluster-wide reduction: CTA partials combined in rank order (deterministic for sums).
-// `slots` is a __shared__ float[MAX_CLUSTER] used by this reduction only.
+// ---- cross-CTA reduction: DSMEM stores + mbarrier arrivals ----------------------------
+// Thread r of each CTA writes the CTA's partial into its slot of CTA r and arrives on CTA r's
+// mbarrier (release at cluster scope, which orders the store before the arrival); every thread
+// then waits on its own CTA's barrier for the n arrivals (acquire at cluster scope).  Unlike
+// barrier.cluster it waits for the partials only, not for every thread of every CTA.
+// Each exchange's barrier is initialised (count = cluster size) before the cluster's start
+// barrier and completes exactly one phase, so every exchange serves one reduction.
+struct Exchange {
+  float slots[MAX_CLUSTER];
+  unsigned long long bar;
+};
+__device__ __forceinline__ void exchange_init(Exchange* x) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(&x->bar)),
+               "r"(nctarank())
+               : "memory");
+}
+__device__ __forceinline__ void fence_exchange_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Bounded wait (about 2 s) for phase 0 of the exchange's barrier; false when it gave up.
+__device__ __forceinline__ bool exchange_wait(Exchange* x) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(&x->bar);
+  uint64_t t0 = 0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a)
+        : "memory");
+    if (ok) return true;
+    if ((it & 63u) == 63u) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 2000000000ull || it > (1u << 30)) return false;
+    }
+  }
+}
+
+// Start of a cluster row kernel: initialise its `count` exchanges, then arrive on the
+// cluster's start barrier (the matching cluster_wait() makes the initialisation visible).
+__device__ __forceinline__ void cluster_start(Exchange* xs, int count) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < count; ++i) exchange_init(&xs[i]);
+    fence_exchange_init();
+  }
+  cluster_arrive_relaxed();
+}
+
+// Cluster-wide reduction through an Exchange: CTA partials combined in rank order
+// (deterministic for sums).
 template <typename Op>
-__device__ __forceinline__ float cluster_allreduce(float v, float* red, float* slots) {
+__device__ __forceinline__ float cluster_allreduce_x(float v, float* red, Exchange* x) {
   v = block_reduce<Op>(v, red);
   const uint32_t n = nctarank();
   if (n == 1) return v;
-  const uint32_t me = ctarank();
-  if (threadIdx.x < n) st_cluster_f32(mapa(&slots[me], threadIdx.x), v);
-  cluster_sync();
-  float r = slots[0];
-  for (uint32_t i = 1; i < n; ++i) r = Op::apply(r, slots[i]);
+  if (threadIdx.x < n) {
+    st_cluster_f32(mapa(&x->slots[ctarank()], threadIdx.x), v);
+    mbar_arrive_remote(mapa(&x->bar, threadIdx.x));
+  }
+  exchange_wait(x);
+  float r = x->slots[0];
+  for (uint32_t i = 1; i < n; ++i) r = Op::apply(r, x->slots[i]);
   return r;
 }
 

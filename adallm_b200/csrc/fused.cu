@@ -72,9 +72,9 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
                                                             const T* __restrict__ w, T* y, int64_t ldy, int rows,
                                                             int hidden, float eps, int gemma, q::QuantDst dst,
                                                             PartIn pin) {
-  cl::cluster_arrive_relaxed();
   __shared__ float red[cl::MAX_WARPS];
-  __shared__ float slots[2][cl::MAX_CLUSTER];
+  __shared__ cl::Exchange xch[2];
+  cl::cluster_start(xch, 2);
   const int m = blockIdx.y;
   int o0, o1;
   slice_of(hidden, o0, o1);
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
     }
   }
   cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
-  const float rs = rsqrtf(cl::cluster_allreduce<cl::OpSum>(ss, red, slots[0]) / (float)hidden + eps);
+  const float rs = rsqrtf(cl::cluster_allreduce_x<cl::OpSum>(ss, red, &xch[0]) / (float)hidden + eps);
   float amax = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
     }
   }
   if (!quant) return;
-  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots[1]));
+  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch[1]));
 }
 
 // SiLU with the hardware exponential (within 2 ulp of fp32 before the bf16 rounding).
@@ -153,11 +153,11 @@ template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y, int64_t ldy,
                                                               int rows, int inter, int act, q::QuantDst dst,
                                                               PartIn pin) {
-  cl::cluster_arrive_relaxed();
+  __shared__ float red[cl::MAX_WARPS];
+  __shared__ cl::Exchange xch;
+  cl::cluster_start(&xch, 1);
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[cl::MAX_WARPS];
-  __shared__ float slots[cl::MAX_CLUSTER];
   const int m = blockIdx.y;
   int o0, o1;
   slice_of(inter, o0, o1);
@@ -193,18 +193,18 @@ __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restric
     }
   }
   cl::cluster_wait();
-  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
+  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch));
 }
 
 // grid (ctas, m_pad), cluster (ctas, 1, 1).
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) act_quant_kernel(const T* __restrict__ x, int64_t ldx, int rows, int k,
                                                         q::QuantDst dst) {
-  cl::cluster_arrive_relaxed();
+  __shared__ float red[cl::MAX_WARPS];
+  __shared__ cl::Exchange xch;
+  cl::cluster_start(&xch, 1);
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[cl::MAX_WARPS];
-  __shared__ float slots[cl::MAX_CLUSTER];
   const int m = blockIdx.y;
   int o0, o1;
   slice_of(k, o0, o1);
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(512) act_quant_kernel(const T* __restrict__ x,
     }
   }
   cl::cluster_wait();
-  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce<cl::OpMax>(amax, red, slots));
+  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch));
 }
 
 static inline bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
