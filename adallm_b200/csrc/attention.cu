@@ -50,6 +50,11 @@ struct Params {
   float v_scale;
   float* o_part;   // [B][Hq][max_splits][D]
   float* ml_part;  // [B][Hq][max_splits][2]   (max in log2 units, sum)
+  // 1: context_lens, block_tables and every cached K/V row except each sequence's newest
+  // position (ctx - 1) were written at least two kernels earlier on the stream, so the
+  // short-cache kernel may read them (and start the TMA loads of those tiles) before its
+  // programmatic-launch wait; q and the newest row are read after it.
+  int early;
 };
 
 // Tokens beyond the block table's reach (ctx > max_pages * page) cannot be addressed and are
@@ -378,11 +383,17 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   if (lane < RING) mbar_init(&bar[lane], 1);
   fence_mbar_init();
   __syncthreads();
-  pdl_wait();
-  pdl_trigger();
+  if (!P.early) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   const int o_begin = kvh * group * (D / 8), o_count = group * (D / 8);  // this CTA's octets of the row
   if (b >= batch) {  // padding row of the last token tile: zero operand, unit scale
+    if (P.early) {
+      pdl_wait();
+      pdl_trigger();
+    }
     if (quant) {
       for (int o = threadIdx.x; o < o_count; o += blockDim.x) q::zero_oct(dst, b, o_begin + o);
       if (kvh == 0 && threadIdx.x == 0) dst.gx[b] = 1.f;
@@ -420,7 +431,16 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
       }
     }
   };
-  for (int k = 0; k < RING && k < nk; ++k) issue(k);
+  // early mode: the tile holding position ctx - 1 (this warp's tile `held`) waits for the
+  // programmatic-launch dependency; the others are requested before it.
+  const int held = (P.early && ntiles > 0 && (ntiles - 1) % SPLIT_WARPS == warp) ? (ntiles - 1) / SPLIT_WARPS : -1;
+  for (int k = 0; k < RING && k < nk; ++k)
+    if (k != held) issue(k);
+  if (P.early) {
+    pdl_wait();
+    pdl_trigger();
+    if (held >= 0 && held < RING) issue(held);
+  }
   uint32_t qf[16];
   load_q_frag<TQ>(P, b, kvh, g, c, qf);
   WarpState ws;
@@ -708,7 +728,7 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
                              const int32_t* context_lens, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
                              int32_t head_dim, int32_t page_size, float scale, float k_scale, float v_scale,
                              int32_t window, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
-                             void* stream, const q::QuantDst* qd);
+                             void* stream, const q::QuantDst* qd, int32_t flags);
 
 extern "C" int ada_fp8_paged_decode(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                                     const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
@@ -722,7 +742,28 @@ extern "C" int ada_fp8_paged_decode(const void* q, int q_dtype, int64_t q_stride
   return paged_decode_impl(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_tok,
                            kv_stride_head, num_pages, block_tables, bt_stride, max_pages, context_lens, batch,
                            num_heads, num_kv_heads, head_dim, page_size, scale, k_scale, v_scale, window, out,
-                           out_dtype, workspace, workspace_bytes, stream, nullptr);
+                           out_dtype, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+extern "C" int ada_fp8_paged_decode_quant_ex(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                             const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
+                                             int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
+                                             const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                                             const int32_t* context_lens, int32_t batch, int32_t num_heads,
+                                             int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float scale,
+                                             float k_scale, float v_scale, int32_t window, void* out, int out_dtype,
+                                             int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
+                                             void* workspace, size_t workspace_bytes, int32_t flags, void* stream) {
+  if (flags & ~ADA_ATTN_META_EARLY) return ADA_ERR_INVALID_ARG;
+  const int row = num_heads * head_dim;
+  if (row % 256) return ADA_ERR_UNSUPPORTED;
+  if (!q::dst_ok(terms, block_n, row) || !xq || !gx || (terms == 1 && !sfx)) return ADA_ERR_INVALID_ARG;
+  if (((uintptr_t)xq & 15) || ((uintptr_t)gx & 3)) return ADA_ERR_ALIGNMENT;
+  const q::QuantDst qd{xq, sfx, gx, terms, block_n, row};
+  return paged_decode_impl(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_tok,
+                           kv_stride_head, num_pages, block_tables, bt_stride, max_pages, context_lens, batch,
+                           num_heads, num_kv_heads, head_dim, page_size, scale, k_scale, v_scale, window, out,
+                           out_dtype, workspace, workspace_bytes, stream, &qd, flags);
 }
 
 extern "C" int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
@@ -734,15 +775,11 @@ extern "C" int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_
                                           float k_scale, float v_scale, int32_t window, void* out, int out_dtype,
                                           int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
                                           void* workspace, size_t workspace_bytes, void* stream) {
-  const int row = num_heads * head_dim;
-  if (row % 256) return ADA_ERR_UNSUPPORTED;
-  if (!q::dst_ok(terms, block_n, row) || !xq || !gx || (terms == 1 && !sfx)) return ADA_ERR_INVALID_ARG;
-  if (((uintptr_t)xq & 15) || ((uintptr_t)gx & 3)) return ADA_ERR_ALIGNMENT;
-  const q::QuantDst qd{xq, sfx, gx, terms, block_n, row};
-  return paged_decode_impl(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page, kv_stride_tok,
-                           kv_stride_head, num_pages, block_tables, bt_stride, max_pages, context_lens, batch,
-                           num_heads, num_kv_heads, head_dim, page_size, scale, k_scale, v_scale, window, out,
-                           out_dtype, workspace, workspace_bytes, stream, &qd);
+  return ada_fp8_paged_decode_quant_ex(q, q_dtype, q_stride_b, q_stride_h, k_cache, v_cache, kv_stride_page,
+                                       kv_stride_tok, kv_stride_head, num_pages, block_tables, bt_stride, max_pages,
+                                       context_lens, batch, num_heads, num_kv_heads, head_dim, page_size, scale,
+                                       k_scale, v_scale, window, out, out_dtype, terms, block_n, xq, sfx, gx,
+                                       workspace, workspace_bytes, 0, stream);
 }
 
 static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
@@ -752,7 +789,7 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
                              const int32_t* context_lens, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
                              int32_t head_dim, int32_t page_size, float scale, float k_scale, float v_scale,
                              int32_t window, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
-                             void* stream, const q::QuantDst* qd) {
+                             void* stream, const q::QuantDst* qd, int32_t flags) {
   if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_pages <= 0 || page_size <= 0) return ADA_ERR_INVALID_ARG;
   if (batch == 0) return ADA_OK;
   if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !workspace) return ADA_ERR_INVALID_ARG;
@@ -794,6 +831,7 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
   P.v_scale = v_scale;
   P.o_part = reinterpret_cast<float*>(workspace);
   P.ml_part = P.o_part + (size_t)batch * num_heads * P.max_splits * attn::D;
+  P.early = (flags & ADA_ATTN_META_EARLY) ? 1 : 0;
 
   // K / V caches as 4-D byte tensors [num_pages][page][Hkv][D] -> TMA box of 16 rows x 128 B
   CUtensorMap tmk, tmv;

@@ -77,27 +77,30 @@ __device__ __forceinline__ float block_reduce(float v, float* red) {
   return r;
 }
 
-// ---- cross-CTA reduction: DSMEM stores + mbarrier arrivals ----------------------------
-// Thread r of each CTA writes the CTA's partial into its slot of CTA r and arrives on CTA r's
-// mbarrier (release at cluster scope, which orders the store before the arrival); every thread
-// then waits on its own CTA's barrier for the n arrivals (acquire at cluster scope).  Unlike
-// barrier.cluster it waits for the partials only, not for every thread of every CTA.
-// Each exchange's barrier is initialised (count = cluster size) before the cluster's start
-// barrier and completes exactly one phase, so every exchange serves one reduction.
+// ---- cross-CTA reduction: asynchronous DSMEM stores counted by mbarriers -----------------
+// Thread r of each CTA sends the CTA's partial into its slot of CTA r with st.async, which
+// completes 4 bytes of transaction on CTA r's mbarrier; every thread then waits on its own
+// CTA's barrier until all n partials have landed (acquire at cluster scope).  Each barrier is
+// initialised with one arrival that is made at once with the expected n * 4 bytes, before the
+// cluster's start barrier, and completes exactly one phase: every exchange serves one
+// reduction.  Unlike barrier.cluster it waits for the partials only, not for every thread of
+// every CTA, and each partial is one one-way transaction.
 struct Exchange {
   float slots[MAX_CLUSTER];
   unsigned long long bar;
 };
 __device__ __forceinline__ void exchange_init(Exchange* x) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(&x->bar)),
-               "r"(nctarank())
-               : "memory");
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(&x->bar);
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(a) : "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(nctarank() * 4u) : "memory");
 }
 __device__ __forceinline__ void fence_exchange_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+__device__ __forceinline__ void st_async_f32(uint32_t cluster_addr, float v, uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(cluster_addr), "f"(v),
+               "r"(cluster_bar)
+               : "memory");
 }
 // Bounded wait (about 2 s) for phase 0 of the exchange's barrier; false when it gave up.
 __device__ __forceinline__ bool exchange_wait(Exchange* x) {
@@ -139,10 +142,7 @@ __device__ __forceinline__ float cluster_allreduce_x(float v, float* red, Exchan
   v = block_reduce<Op>(v, red);
   const uint32_t n = nctarank();
   if (n == 1) return v;
-  if (threadIdx.x < n) {
-    st_cluster_f32(mapa(&x->slots[ctarank()], threadIdx.x), v);
-    mbar_arrive_remote(mapa(&x->bar, threadIdx.x));
-  }
+  if (threadIdx.x < n) st_async_f32(mapa(&x->slots[ctarank()], threadIdx.x), v, mapa(&x->bar, threadIdx.x));
   exchange_wait(x);
   float r = x->slots[0];
   for (uint32_t i = 1; i < n; ++i) r = Op::apply(r, x->slots[i]);

@@ -161,6 +161,12 @@ __global__ void __launch_bounds__(192, 2)
         bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
                   C::SFA_BYTES, &full[i]);
       }
+      // The rest of this CTA's weight slice is pulled into L2 while the previous kernel runs.
+      for (int i = pre; i < nunits; ++i) {
+        const int kt = kt0 + i;
+        tma_prefetch_l2_2d(&tmw, kt * KT_BYTES, n_tile * BM);
+        bulk_prefetch_l2(p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFA_BYTES);
+      }
       pdl_wait();
       for (int i = 0; i < nunits; ++i) {
         const int s = i % stages;

@@ -20,23 +20,31 @@ template <typename T, int N>
 __device__ __forceinline__ void load_parts(const PartIn& pi, int64_t row, int64_t col, float* f) {
   static_assert(N % 4 == 0, "whole float4s");
   const float* base = pi.p + row * pi.ld + col;
+  for (int k = 0; k < pi.n; k += 4) {  // four planes' loads in flight together, summed in plane order
+    float4 a[4][N / 4];
 #pragma unroll
-  for (int i = 0; i < N; i += 4) {
-    const float4 a = *reinterpret_cast<const float4*>(base + i);
-    f[i] = a.x;
-    f[i + 1] = a.y;
-    f[i + 2] = a.z;
-    f[i + 3] = a.w;
-  }
-  for (int k = 1; k < pi.n; ++k) {
-    const float* b = base + (int64_t)k * pi.plane;
+    for (int j = 0; j < 4; ++j)
+      if (k + j < pi.n)
 #pragma unroll
-    for (int i = 0; i < N; i += 4) {
-      const float4 a = *reinterpret_cast<const float4*>(b + i);
-      f[i] = __fadd_rn(f[i], a.x);
-      f[i + 1] = __fadd_rn(f[i + 1], a.y);
-      f[i + 2] = __fadd_rn(f[i + 2], a.z);
-      f[i + 3] = __fadd_rn(f[i + 3], a.w);
+        for (int i = 0; i < N / 4; ++i)
+          a[j][i] = *reinterpret_cast<const float4*>(base + (int64_t)(k + j) * pi.plane + 4 * i);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (k + j >= pi.n) break;
+#pragma unroll
+      for (int i = 0; i < N / 4; ++i) {
+        if (k + j == 0) {
+          f[4 * i] = a[j][i].x;
+          f[4 * i + 1] = a[j][i].y;
+          f[4 * i + 2] = a[j][i].z;
+          f[4 * i + 3] = a[j][i].w;
+        } else {
+          f[4 * i] = __fadd_rn(f[4 * i], a[j][i].x);
+          f[4 * i + 1] = __fadd_rn(f[4 * i + 1], a[j][i].y);
+          f[4 * i + 2] = __fadd_rn(f[4 * i + 2], a[j][i].z);
+          f[4 * i + 3] = __fadd_rn(f[4 * i + 3], a[j][i].w);
+        }
+      }
     }
   }
 #pragma unroll

@@ -62,9 +62,11 @@ __device__ __forceinline__ RowQ make_rowq(float amax, int terms) {
   float g = live ? __fdiv_rn(amax, 6.f) : 1.f;
 #pragma unroll
   for (int t = 0; t < MAX_TERMS; ++t) {
-    q.g[t] = g;
-    q.rcp[t] = __fdiv_rn(1.f, g);
-    g = next_term_scale(g);
+    if (t < terms) {  // only the scales in use: the recurrence is a chain of divisions
+      q.g[t] = g;
+      q.rcp[t] = __frcp_rn(g);  // correctly rounded 1 / g (g is normal: >= 2^-64 / 6^8)
+      g = next_term_scale(g);
+    }
   }
   return q;
 }

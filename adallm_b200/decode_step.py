@@ -35,6 +35,12 @@ import torch.distributed as dist
 from . import _native as N
 from .nvfp4_gemm import prepack_scales, sf_bytes, workspace_bytes
 
+# In the decode step the kernel right before attention is qk_norm_rope_store, which appends each
+# sequence's new K/V row at position context_lens - 1 (slot_mapping is that position) and writes
+# q; context_lens and block_tables come from the host upload or advance(), both long before.  So
+# attention may read its metadata and start the older cache tiles' loads before waiting.
+ATTN_META_EARLY = 1
+
 
 @dataclass
 class DecodeConfig:
@@ -386,12 +392,12 @@ class Qwen3DecodeEngine:
                                                    kc.data_ptr(), vc.data_ptr(), 1.0, 1.0, self.q_rot.data_ptr(),
                                                    None, 0, stream), "qk_norm_rope_store")
                 xq, sfx, gx = self.q_attn
-                N.check(lib.ada_fp8_paged_decode_quant(
+                N.check(lib.ada_fp8_paged_decode_quant_ex(
                     self.q_rot.data_ptr(), 0, qn, D, kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1),
                     kc.stride(2), self.num_pages, self.block_tables.data_ptr(), self.block_tables.stride(0),
                     self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv, D, c.page_size,
                     D ** -0.5, 1.0, 1.0, 0, None, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
-                    gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, stream), "attention")
+                    gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, ATTN_META_EARLY, stream), "attention")
                 self._gemm(self.q_attn, L["o"], self.hidden, stream)
                 self._all_reduce(self.hidden)
                 self._rms_quant(self.hidden, L["post_norm"], self.q_hidden, stream, residual=self.residual)
@@ -428,12 +434,12 @@ class Qwen3DecodeEngine:
                                                      kc.data_ptr(), vc.data_ptr(), 1.0, 1.0, self.q_rot.data_ptr(),
                                                      None, 0, stream), "qk_norm_rope_store")
             xq, sfx, gx = self.q_attn
-            N.check(lib.ada_fp8_paged_decode_quant(
+            N.check(lib.ada_fp8_paged_decode_quant_ex(
                 self.q_rot.data_ptr(), 0, qn, D, kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1),
                 kc.stride(2), self.num_pages, self.block_tables.data_ptr(), self.block_tables.stride(0),
                 self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv, D, c.page_size,
                 D ** -0.5, 1.0, 1.0, 0, None, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
-                gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, stream), "attention")
+                gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, ATTN_META_EARLY, stream), "attention")
             planes = self._gemm_parts(self.q_attn, L["o"], "o", stream)
             self._rms_quant_parts(planes, L["post_norm"], self.q_hidden, stream)
             ns, ld = self._gemm_parts(self.q_hidden, L["gate_up"], "gate_up", stream)

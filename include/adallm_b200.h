@@ -101,6 +101,23 @@ ADA_API int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_str
                                        void* out, int out_dtype, int terms, int block_n, uint8_t* xq,
                                        uint8_t* sfx, float* gx, void* workspace, size_t workspace_bytes,
                                        void* stream);
+/* As ada_fp8_paged_decode_quant, with launch flags (no counterpart in the reference).
+ * ADA_ATTN_META_EARLY: context_lens, block_tables and every cached K/V row except each sequence's
+ * newest position (context_lens[b] - 1) were written at least two kernels earlier on `stream`
+ * (e.g. the kernel just before is the one appending the new token's K/V): the short-cache kernel
+ * then reads the metadata and starts its cache loads before waiting for that kernel. */
+#define ADA_ATTN_META_EARLY 1
+ADA_API int ada_fp8_paged_decode_quant_ex(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                          const uint8_t* k_cache, const uint8_t* v_cache,
+                                          int64_t kv_stride_page, int64_t kv_stride_tok,
+                                          int64_t kv_stride_head, int64_t num_pages,
+                                          const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                                          const int32_t* context_lens, int32_t batch, int32_t num_heads,
+                                          int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                          float scale, float k_scale, float v_scale, int32_t window,
+                                          void* out, int out_dtype, int terms, int block_n, uint8_t* xq,
+                                          uint8_t* sfx, float* gx, void* workspace, size_t workspace_bytes,
+                                          int32_t flags, void* stream);
 
 /* ------------------------------------------------------------------------
  * FP8 KV-cache store

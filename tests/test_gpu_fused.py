@@ -81,8 +81,9 @@ def test_gated_act_quant_matches_unfused(inter, act, terms):
     same(got, ref)
 
 
+@pytest.mark.parametrize("flags", [0, 1])
 @pytest.mark.parametrize("batch,hq,hkv,terms", [(16, 32, 8, 4), (7, 16, 2, 1), (16, 64, 8, 5)])
-def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms):
+def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms, flags):
     d = dev()
     case = oa.make_paged_case(5, batch=batch, hq=hq, hkv=hkv, d=128, page=16, ctx_lo=1, ctx_hi=900)
     q = torch.from_numpy(case["q"]).to(torch.bfloat16).to(d)
@@ -96,11 +97,12 @@ def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms):
     out = torch.empty_like(out_ref)
     wsb = int(N.lib().ada_fp8_paged_decode_workspace_size(batch, hq, bt.shape[1], 16, 128))
     ws = torch.empty(wsb, dtype=torch.uint8, device=d)
-    N.check(N.lib().ada_fp8_paged_decode_quant(
+    # flags 1 (ADA_ATTN_META_EARLY): metadata read before the programmatic-launch wait, same result
+    N.check(N.lib().ada_fp8_paged_decode_quant_ex(
         q.data_ptr(), 0, q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
         k.shape[0], bt.data_ptr(), bt.stride(0), bt.shape[1], ctx.data_ptr(), batch, hq, hkv, 128, 16,
         case["scale"], 1.0, 1.0, 0, out.data_ptr(), 0, terms, 16, got[0].data_ptr(), got[1].data_ptr(),
-        got[2].data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream), "decode_quant")
+        got[2].data_ptr(), ws.data_ptr(), wsb, flags, torch.cuda.current_stream().cuda_stream), "decode_quant")
     torch.cuda.synchronize()
     assert torch.equal(out, out_ref)
     same(got, ref)

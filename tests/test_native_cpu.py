@@ -45,6 +45,10 @@ def test_argument_errors_are_reported_before_any_launch(built):
     assert st == N.ADA_ERR_UNSUPPORTED
     st = lib.ada_rmsnorm(None, 0, None, 0, None, 0, None, None, 0, 4, 128, 1e-6, 0, 0, None)
     assert st == N.ADA_ERR_INVALID_ARG
+    # unknown attention launch flags are rejected
+    st = lib.ada_fp8_paged_decode_quant_ex(16, 0, 0, 0, 16, 16, 0, 0, 0, 4, 16, 4, 4, 16, 1, 32, 8, 128, 16, 1.0,
+                                           1.0, 1.0, 0, None, 0, 4, 16, 16, None, 16, 16, 1 << 20, 2, None)
+    assert st == N.ADA_ERR_INVALID_ARG
     with pytest.raises(ValueError):
         N.check(N.ADA_ERR_ALIGNMENT, "x")
     with pytest.raises(RuntimeError, match="no fallback"):
