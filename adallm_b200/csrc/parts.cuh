@@ -19,17 +19,18 @@ struct PartIn {
 template <typename T, int N>
 __device__ __forceinline__ void load_parts(const PartIn& pi, int64_t row, int64_t col, float* f) {
   static_assert(N % 4 == 0, "whole float4s");
+  constexpr int G = 8;
   const float* base = pi.p + row * pi.ld + col;
-  for (int k = 0; k < pi.n; k += 4) {  // four planes' loads in flight together, summed in plane order
-    float4 a[4][N / 4];
+  for (int k = 0; k < pi.n; k += G) {  // G planes' loads in flight together, summed in plane order
+    float4 a[G][N / 4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < G; ++j)
       if (k + j < pi.n)
 #pragma unroll
         for (int i = 0; i < N / 4; ++i)
           a[j][i] = *reinterpret_cast<const float4*>(base + (int64_t)(k + j) * pi.plane + 4 * i);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < G; ++j) {
       if (k + j >= pi.n) break;
 #pragma unroll
       for (int i = 0; i < N / 4; ++i) {

@@ -46,8 +46,8 @@ __device__ __forceinline__ float next_term_scale(float g) { return __fdiv_rn(g, 
 
 // Per-row constants, derived from the row amax.
 struct RowQ {
-  float g[MAX_TERMS];    // terms >= 2: g_t; terms == 1: g[0] = g, g[1] = 6g
-  float rcp[MAX_TERMS];  // terms >= 2: 1 / g_t
+  float g[2];  // terms >= 2: g[0] = g_0 (the term scales follow by next_term_scale);
+               // terms == 1: g[0] = g, g[1] = 6g
   int terms;
 };
 __device__ __forceinline__ RowQ make_rowq(float amax, int terms) {
@@ -59,15 +59,8 @@ __device__ __forceinline__ RowQ make_rowq(float amax, int terms) {
     q.g[1] = __fmul_rn(q.g[0], 6.f);
     return q;
   }
-  float g = live ? __fdiv_rn(amax, 6.f) : 1.f;
-#pragma unroll
-  for (int t = 0; t < MAX_TERMS; ++t) {
-    if (t < terms) {  // only the scales in use: the recurrence is a chain of divisions
-      q.g[t] = g;
-      q.rcp[t] = __frcp_rn(g);  // correctly rounded 1 / g (g is normal: >= 2^-64 / 6^8)
-      g = next_term_scale(g);
-    }
-  }
+  q.g[0] = live ? __fdiv_rn(amax, 6.f) : 1.f;
+  q.g[1] = 0.f;
   return q;
 }
 
@@ -106,24 +99,28 @@ __device__ __forceinline__ void quant_oct(const QuantDst& d, int m, int oc, floa
     }
     return;
   }
+  // one term per iteration (kept rolled: short code for a path every producer kernel runs once)
+  float g = q.g[0];
+  uint8_t* row = xq_row(d, m, 0) + (size_t)oc * 4;
+  const size_t term_stride = (size_t)d.bn * ((size_t)d.k >> 1);
+#pragma unroll 1
+  for (int t = 0; t < q.terms; ++t) {
+    const float rcp = __frcp_rn(g);  // correctly rounded 1 / g_t (g_t is normal: >= 2^-64 / 6^8)
+    float v[8];
 #pragma unroll
-  for (int t = 0; t < MAX_TERMS; ++t) {
-    if (t < q.terms) {
-      float v[8];
+    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(r[i], rcp);
+    const uint32_t codes = f32x8_to_e2m1x8(v);
+    if (t + 1 < q.terms) {
+      uint32_t h[4];
+      e2m1x8_to_f16x8(codes, h);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(r[i], q.rcp[t]);
-      const uint32_t codes = f32x8_to_e2m1x8(v);
-      if (t + 1 < q.terms) {
-        uint32_t h[4];
-        e2m1x8_to_f16x8(codes, h);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint16_t hb = (uint16_t)(h[i >> 1] >> (16 * (i & 1)));
-          r[i] = __fsub_rn(r[i], __fmul_rn(__half2float(__ushort_as_half(hb)), q.g[t]));
-        }
+      for (int i = 0; i < 8; ++i) {
+        const uint16_t hb = (uint16_t)(h[i >> 1] >> (16 * (i & 1)));
+        r[i] = __fsub_rn(r[i], __fmul_rn(__half2float(__ushort_as_half(hb)), g));
       }
-      if (valid) *reinterpret_cast<uint32_t*>(xq_row(d, m, t) + (size_t)oc * 4) = codes;
     }
+    if (valid) *reinterpret_cast<uint32_t*>(row + (size_t)t * term_stride) = codes;
+    g = next_term_scale(g);
   }
 }
 
