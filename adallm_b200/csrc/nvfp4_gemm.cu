@@ -97,8 +97,11 @@ __host__ __device__ __forceinline__ int owner_begin(int o, int ks) { return (o *
 
 // grid (ks, tiles), cluster (ks, 1, 1) when ks > 1.  CTA `rank` of a cluster accumulates
 // K steps [rank*nkt/ks, (rank+1)*nkt/ks) of tile blockIdx.y.
+// Register budget: tiles of at most 96 MMA columns are held to 3 CTAs' worth (96 registers a
+// thread), so two GEMM CTAs leave room on the SM for the CTAs of the kernels around them;
+// wider tiles (which would spill) keep the 2-CTA budget.
 template <int BN, int T>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
     gemm_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
   using C = Cfg<BN, T>;
   extern __shared__ uint8_t smem_raw[];
@@ -360,15 +363,18 @@ static inline uint32_t pow2_cols(uint32_t c) {
 
 // Two co-resident CTAs per SM when shared memory and TMEM allow (each CTA's MMA thread
 // issues its own tcgen05 stream); else one CTA per SM with a deeper pipeline.
+// No more stages than the K steps of the longest split (`max_units`): a pipeline deeper than the
+// work only holds shared memory that the next kernel's CTAs could use.
 template <int BN, int T>
-static void stages_for(int ks, int rows_max, int& stages, uint32_t& cols, size_t& smem) {
+static void stages_for(int ks, int rows_max, int max_units, int& stages, uint32_t& cols, size_t& smem) {
   using C = Cfg<BN, T>;
   const size_t recv = C::recv_bytes(ks, rows_max);
+  const int top = max_units < 2 ? 2 : max_units < MAX_STAGES ? max_units : MAX_STAGES;
   int s = 0;
-  for (int k = MAX_STAGES; k >= 3; --k)
+  for (int k = top; k >= (top < 3 ? top : 3); --k)
     if (C::smem_bytes(k, recv) <= 113 * 1024 && C::tmem_need(k) <= 256) { s = k; break; }
   if (s == 0)
-    for (int k = MAX_STAGES; k >= 2; --k)
+    for (int k = top; k >= 2; --k)
       if (C::smem_bytes(k, recv) <= 226 * 1024 && C::tmem_need(k) <= 512) { s = k; break; }
   stages = s;
   cols = s ? pow2_cols(C::tmem_need(s)) : 0;
@@ -379,8 +385,9 @@ static void stages_for(int ks, int rows_max, int& stages, uint32_t& cols, size_t
   X(16, 1) X(16, 2) X(16, 3) X(16, 4) X(16, 5) X(16, 6) X(16, 7) X(16, 8) \
   X(32, 1) X(32, 2) X(32, 3) X(32, 4) X(64, 1) X(64, 2) X(128, 1)
 
-static void stages_dispatch(int bn, int t, int ks, int rows_max, int& stages, uint32_t& cols, size_t& smem) {
-#define ADA_SD(B, TT) if (bn == B && t == TT) { stages_for<B, TT>(ks, rows_max, stages, cols, smem); return; }
+static void stages_dispatch(int bn, int t, int ks, int rows_max, int max_units, int& stages, uint32_t& cols,
+                            size_t& smem) {
+#define ADA_SD(B, TT) if (bn == B && t == TT) { stages_for<B, TT>(ks, rows_max, max_units, stages, cols, smem); return; }
   ADA_FP4_CONFIGS(ADA_SD)
 #undef ADA_SD
   stages = 0;
@@ -422,7 +429,7 @@ static int active_clusters(int ks) {
   int stages = 0;
   uint32_t cols = 0;
   size_t smem = 0;
-  stages_for<BN, T>(ks, (int)cdiv(BM, ks), stages, cols, smem);
+  stages_for<BN, T>(ks, (int)cdiv(BM, ks), MAX_STAGES, stages, cols, smem);  // deepest pipeline: a lower bound
   int n = 0;
   if (stages >= 2 &&
       cudaFuncSetAttribute(occupancy_twin, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
@@ -502,7 +509,7 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   P.ks = (int)ks;
   P.rows_max = (int)cdiv(BM, ks);
   uint32_t cols = 0;
-  stages_dispatch(P.bn, terms, parts ? 1 : P.ks, P.rows_max, P.stages, cols, P.smem);
+  stages_dispatch(P.bn, terms, parts ? 1 : P.ks, P.rows_max, (int)cdiv(P.nkt, ks), P.stages, cols, P.smem);
   if (P.stages < 2) return ADA_ERR_UNSUPPORTED;
   P.tmem_cols = (int)cols;
   size_t off = ERR_BYTES;
