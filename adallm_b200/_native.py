@@ -31,6 +31,7 @@ ADA_ERR_CUDA = 7
 DT = {torch.bfloat16: 0, torch.float16: 1}
 
 P, I32, I64, F32, INT, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_int, C.c_size_t
+PP, U32 = C.POINTER(C.c_void_p), C.c_uint32
 
 # name -> (restype, argtypes)
 _SIGS = {
@@ -70,6 +71,16 @@ _SIGS = {
     "ada_nvfp4_gemm_partials": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, I64, I64, INT, P, SZ, P]),
     "ada_rmsnorm_quant_parts": (INT, [P, I32, I64, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT,
                                       P, P, P, P]),
+    "ada_peer_alloc": (INT, [SZ, PP, P]),
+    "ada_peer_open": (INT, [P, PP]),
+    "ada_peer_close": (INT, [P]),
+    "ada_peer_free": (INT, [P]),
+    "ada_tp_epoch_advance": (INT, [P, P]),
+    "ada_nvfp4_gemm_ctas": (INT, [I64, I64, I64, INT, INT]),
+    "ada_nvfp4_gemm_partials_peer": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, I64, I64, INT, I32, I32, P,
+                                           P, U32, U32, P, SZ, P]),
+    "ada_rmsnorm_quant_peer": (INT, [P, I32, I64, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT,
+                                     P, P, P, P, U32, U32, P, P]),
     "ada_gated_act_quant_parts": (INT, [P, I32, I64, I64, P, I64, I64, I32, INT, INT, INT, INT, P, P, P, P]),
     "ada_qk_norm_rope_store_parts": (INT, [P, I32, I64, I64, I64, I32, I32, I32, P, P, F32, P, P, I64, P, P, P, F32,
                                            F32, P, P, INT, P]),
@@ -122,6 +133,11 @@ def stream_ptr(device: torch.device | None = None) -> int:
 
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+def ptr_array(addrs: list[int]) -> C.Array:
+    """A host array of device pointers (for the entry points that take `T* const*`)."""
+    return (C.c_void_p * len(addrs))(*addrs)
 
 
 def require_cuda(*tensors: torch.Tensor, what: str) -> None:

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
                                                             int64_t ldr, T* res_out, int64_t ldro,
                                                             const T* __restrict__ w, T* y, int64_t ldy, int rows,
                                                             int hidden, float eps, int gemma, q::QuantDst dst,
-                                                            PartIn pin) {
+                                                            PartIn pin, PeerWait pw) {
   __shared__ float red[cl::MAX_WARPS];
   __shared__ cl::Exchange xch[2];
   cl::cluster_start(xch, 2);
@@ -92,13 +92,16 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
     cl::cluster_wait();
     return;
   }
+  const unsigned int tag = pw.epoch ? peer_tag(pw) : 0u;
   float v[MAXU][8];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
     const int o = my_oct(u, o0, o1);
     if (o >= 0) {
-      if (pin.n)
+      if (pw.epoch)  // tensor parallelism: every rank's planes, polled until this step's tag
+        load_parts_tagged<T, 8>(pin, m, o * 8, pw, tag, v[u]);
+      else if (pin.n)
         load_parts<T, 8>(pin, m, o * 8, v[u]);  // the producing GEMM's split-K planes
       else
         load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
@@ -254,7 +257,8 @@ bool quant_args_ok(const q::QuantDst& d) {
 // RMSNorm (quantised or not) of `launch_rows` rows (rows beyond `rows` are padding).
 int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro, const void* w,
                    void* y, int64_t ldy, int64_t rows, int64_t launch_rows, int hidden, float eps, int gemma,
-                   int dtype, const q::QuantDst& dst, cudaStream_t st, const PartIn& pin = PartIn{nullptr, 0, 0, 0}) {
+                   int dtype, const q::QuantDst& dst, cudaStream_t st, const PartIn& pin = PartIn{nullptr, 0, 0, 0},
+                   const PeerWait& pw = PeerWait{nullptr, 0, 0, nullptr}) {
   if (hidden % 16) return ADA_ERR_UNSUPPORTED;
   const cl::RowSplit sp = cl::row_split(hidden / 16);
   if (!sp.maxu || launch_rows > 65535) return ADA_ERR_UNSUPPORTED;
@@ -263,11 +267,11 @@ int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, voi
   if (dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin);
+                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
   } else {
     using TT = __half;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin);
+                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
@@ -368,11 +372,11 @@ extern "C" int ada_gated_act_quant_parts(const float* parts, int32_t nparts, int
                               PartIn{parts, nparts, plane, ldp});
 }
 
-extern "C" int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
-                                       const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
-                                       const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
-                                       float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
-                                       uint8_t* sfx, float* gx, void* stream) {
+static int rmsnorm_quant_parts_impl(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                    const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                    const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden, float eps,
+                                    int gemma, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
+                                    void* stream, const PeerWait& pw) {
   if (rows <= 0 || hidden <= 0 || !weight || (residual && !residual_out) || nparts < 1) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
   const PartIn pin{parts, nparts, plane, ldp};
@@ -385,5 +389,30 @@ extern "C" int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64
     return ADA_ERR_ALIGNMENT;
   const int64_t launch_rows = quant ? cdiv(rows, block_n) * block_n : rows;
   return fused::launch_rmsnorm(nullptr, 0, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
-                               launch_rows, hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream), pin);
+                               launch_rows, hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream), pin,
+                               pw);
+}
+
+extern "C" int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                       const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                       const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
+                                       float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
+                                       uint8_t* sfx, float* gx, void* stream) {
+  return rmsnorm_quant_parts_impl(parts, nparts, plane, ldp, residual, ld_res, residual_out, ld_res_out, weight, y,
+                                  ldy, rows, hidden, eps, gemma, dtype, terms, block_n, xq, sfx, gx, stream,
+                                  PeerWait{nullptr, 0, 0, nullptr});
+}
+
+extern "C" int ada_rmsnorm_quant_peer(const void* inbox, int32_t nparts, int64_t plane, int64_t ldp,
+                                      const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                      const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
+                                      float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
+                                      uint8_t* sfx, float* gx, const uint32_t* epoch, uint32_t tag_mul,
+                                      uint32_t tag_add, uint32_t* err, void* stream) {
+  if (!epoch || !inbox) return ADA_ERR_INVALID_ARG;
+  if (((uintptr_t)epoch & 3) || ((uintptr_t)err & 3) || ((uintptr_t)inbox & 15) || (plane & 1) || (ldp & 1))
+    return ADA_ERR_ALIGNMENT;
+  return rmsnorm_quant_parts_impl(reinterpret_cast<const float*>(inbox), nparts, plane, ldp, residual, ld_res,
+                                  residual_out, ld_res_out, weight, y, ldy, rows, hidden, eps, gemma, dtype, terms,
+                                  block_n, xq, sfx, gx, stream, PeerWait{epoch, tag_mul, tag_add, err});
 }

@@ -39,6 +39,7 @@ constexpr int KT = 256;            // K elements per pipeline stage (4 MMA k-blo
 constexpr int KT_BYTES = KT / 2;   // 128 bytes of packed e2m1 per row and stage
 constexpr int SF_BLOCK = 512;      // scale bytes per 128 rows x 64 K
 constexpr int MAX_STAGES = 8;
+constexpr int MAX_PEERS = 8;
 constexpr int MAX_KS = cl::MAX_CLUSTER;
 constexpr uint32_t UNIT_SCALE4 = 0x38383838u;  // four ue4m3 1.0
 
@@ -54,6 +55,13 @@ struct GemmParams {
   int64_t part_plane;   // floats between planes (one plane per K split)
   int part_ld;          // floats between rows of a plane
   int M, N, K, ldy, n_tiles, nkt, stages, tmem_cols, out_dtype, ks, rows_max;
+  // tensor parallelism over peer memory (world > 1): the partial of K split s of this rank
+  // goes to plane tp_rank * ks + s of every rank's inbox as tagged 8-byte words (value bits |
+  // tag << 32, tag = *epoch * tag_mul + tag_add), which the consumer polls: no fence, no counter
+  int world, tp_rank;
+  unsigned long long* inbox[MAX_PEERS];
+  const unsigned int* epoch;
+  unsigned int tag_mul, tag_add;
 };
 
 template <int BN, int T>
@@ -251,7 +259,21 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
       for (int k = 0; k < 16; ++k) out[(c % BN) + k] = fmaf(v[k], gsc[c + k], out[(c % BN) + k]);  // terms in order
     }
     const int r = q * 32 + lane;
-    if (p.part) {
+    if (p.part && p.world > 1) {
+      // every rank's inbox gets this rank's partial of K split `rank` (peer stores over NVLink),
+      // each value with this step's tag in the same 8-byte store (stale words are visible as such)
+      const unsigned long long tag = (unsigned long long)(*p.epoch * p.tag_mul + p.tag_add) << 32;
+      const int64_t off = (int64_t)(p.tp_rank * ks + rank) * p.part_plane + n_tile * BM + r;
+      for (int d = 0; d < p.world; ++d) {
+        unsigned long long* pp = p.inbox[d] + off;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int m = m_tile * BN + j;
+          const float v = ok ? out[j] : __int_as_float(0x7fc00000);  // an aborted tile delivers NaN
+          if (m < p.M) pp[(int64_t)m * p.part_ld] = tag | __float_as_uint(v);
+        }
+      }
+    } else if (p.part) {
       // fp32 partial of this K split; the consumer sums the planes in split order
       if (ok) {
         float* pp = p.part + (int64_t)rank * p.part_plane + n_tile * BM + r;
@@ -548,7 +570,9 @@ static int dispatch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const G
 static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const float* gx, int m, int n, int k,
                     const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w, const float* w_scale_2,
                     const void* bias, void* y, int y_dtype, int64_t ldy, unsigned int* err, cudaStream_t st,
-                    float* part = nullptr, int64_t part_plane = 0, int64_t part_ld = 0) {
+                    float* part = nullptr, int64_t part_plane = 0, int64_t part_ld = 0, int world = 1, int tp_rank = 0,
+                    unsigned long long* const* inboxes = nullptr, const unsigned int* epoch = nullptr,
+                    unsigned int tag_mul = 0, unsigned int tag_add = 0) {
   CUtensorMap tmw, tmx;
   if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, BM)) return ADA_ERR_CUDA;
   if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2),
@@ -576,6 +600,12 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
   gp.out_dtype = y_dtype;
   gp.ks = P.ks;
   gp.rows_max = P.rows_max;
+  gp.world = world;
+  gp.tp_rank = tp_rank;
+  for (int d = 0; d < MAX_PEERS; ++d) gp.inbox[d] = d < world && inboxes ? inboxes[d] : nullptr;
+  gp.epoch = epoch;
+  gp.tag_mul = tag_mul;
+  gp.tag_add = tag_add;
   return dispatch_gemm(tmw, tmx, gp, P, st);
 }
 
@@ -731,4 +761,43 @@ extern "C" int ada_nvfp4_gemm_partials(const uint8_t* xq, const uint8_t* sfx, co
   return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, nullptr,
                        ADA_DT_BF16, n, reinterpret_cast<unsigned int*>(workspace), reinterpret_cast<cudaStream_t>(stream),
                        parts, part_plane, part_ld);
+}
+
+extern "C" int ada_nvfp4_gemm_partials_peer(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m,
+                                            int terms, int block_n, const uint8_t* w_packed, int64_t ldw,
+                                            const uint8_t* sf_w, const float* w_scale_2, int64_t n, int64_t k,
+                                            int64_t part_ld, int64_t part_plane, int nplanes, int32_t world,
+                                            int32_t tp_rank, void* const* inboxes, const uint32_t* epoch,
+                                            uint32_t tag_mul, uint32_t tag_add, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  if (m == 0) return ADA_OK;
+  if (world < 2 || world > fp4::MAX_PEERS || tp_rank < 0 || tp_rank >= world || !inboxes || !epoch)
+    return ADA_ERR_INVALID_ARG;
+  for (int d = 0; d < world; ++d)
+    if (!inboxes[d] || ((uintptr_t)inboxes[d] & 15)) return ADA_ERR_INVALID_ARG;
+  if (((uintptr_t)epoch & 3)) return ADA_ERR_ALIGNMENT;
+  if (!xq || !gx || !w_packed || !sf_w || !w_scale_2 || !workspace) return ADA_ERR_INVALID_ARG;
+  if (terms == 1 && !sfx) return ADA_ERR_INVALID_ARG;
+  if (ldw < k / 2 || part_ld < n || part_plane < m * part_ld || nplanes < 1) return ADA_ERR_INVALID_ARG;
+  if (part_ld > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
+  fp4::Plan P;
+  int rc = fp4::make_plan(m, n, k, terms, nplanes, P, true);
+  if (rc != ADA_OK) return rc;
+  if (block_n != P.bn || P.ks != nplanes) return ADA_ERR_INVALID_ARG;
+  if (workspace_bytes < fp4::ERR_BYTES) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)xq & 15) || (sfx && ((uintptr_t)sfx & 15)) || ((uintptr_t)w_packed & 15) || (ldw & 15) ||
+      ((uintptr_t)sf_w & 15) || ((uintptr_t)workspace & 255))
+    return ADA_ERR_ALIGNMENT;
+  unsigned long long* boxes[fp4::MAX_PEERS];
+  for (int d = 0; d < world; ++d) boxes[d] = reinterpret_cast<unsigned long long*>(inboxes[d]);
+  return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, nullptr,
+                       ADA_DT_BF16, n, reinterpret_cast<unsigned int*>(workspace), reinterpret_cast<cudaStream_t>(stream),
+                       reinterpret_cast<float*>(boxes[tp_rank]), part_plane, part_ld, world, tp_rank, boxes, epoch,
+                       tag_mul, tag_add);
+}
+
+extern "C" int ada_nvfp4_gemm_ctas(int64_t m, int64_t n, int64_t k, int terms, int nplanes) {
+  fp4::Plan P;
+  if (fp4::make_plan(m, n, k, terms, nplanes, P, true) != ADA_OK) return -1;
+  return P.ks * P.n_tiles * P.m_tiles;
 }

@@ -25,6 +25,7 @@ rank holds exactly its slice of the same model.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 import zlib
 from dataclasses import dataclass, field
@@ -184,6 +185,8 @@ class Qwen3DecodeEngine:
         self.seed = seed
         self._init_weights()
         self._alloc_state()
+        if self.tp_peer:
+            self._setup_peers()
 
     # ------------------------------------------------------------------ weights
     def _sharded(self, kind: str, layer: int, parts: list[tuple[str, int]], k_full: int, split_k: bool) -> NVFP4Weight:
@@ -282,10 +285,78 @@ class Qwen3DecodeEngine:
         # by the very next kernel, which completes before the next projection writes)
         self.splits = {name: int(N.lib().ada_nvfp4_gemm_splits(B, w.n, w.k, c.terms))
                        for name, w in self.layers[0].items() if isinstance(w, NVFP4Weight)}
-        self.use_parts = self.fused and c.tp_size == 1 and all(v > 0 for v in self.splits.values())
+        self.use_parts = self.fused and all(v > 0 for v in self.splits.values())
+        # TP > 1: the row-parallel projections (o, down) reduce across ranks through NVLink peer
+        # memory inside the GEMM epilogue + the consuming RMSNorm instead of an NCCL all-reduce
+        self.tp_peer = self.use_parts and c.tp_size > 1
         plane_max = max(self.splits[name] * B * w.n for name, w in self.layers[0].items()
                         if isinstance(w, NVFP4Weight))
         self.parts = torch.zeros(plane_max if self.use_parts else 4, dtype=torch.float32, device=d)
+
+    # ------------------------------------------------------------------ TP peer memory
+    def _setup_peers(self):
+        """Each rank: one peer buffer [epoch][o inbox][down inbox], mapped by every other rank
+        through CUDA IPC.  Inbox of a projection kind: the partial planes of all ranks as tagged
+        8-byte words [world * splits][B][hidden]; at most 8 planes in all (the consumer reads
+        every one of them)."""
+        c, B, W = self.cfg, self.B, self.cfg.tp_size
+        lib = N.lib()
+        H = c.hidden
+
+        def al(x):
+            return -(-x // 256) * 256
+        self.peer_ks = {name: max(1, min(self.splits[name], 8 // W)) for name in ("o", "down")}
+        self.off_inbox = {"o": 256}
+        self.off_inbox["down"] = self.off_inbox["o"] + al(W * self.peer_ks["o"] * B * H * 8)
+        total = self.off_inbox["down"] + al(W * self.peer_ks["down"] * B * H * 8)
+        base, handle = C.c_void_p(), (C.c_char * 64)()
+        N.check(lib.ada_peer_alloc(total, C.byref(base), handle), "peer alloc")
+        self._peer_own = base.value
+        handles = [None] * W
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        self.peer_base = []
+        for r in range(W):
+            if r == c.tp_rank:
+                self.peer_base.append(self._peer_own)
+                continue
+            ptr_ = C.c_void_p()
+            N.check(lib.ada_peer_open(handles[r], C.byref(ptr_)), "peer open")
+            self.peer_base.append(ptr_.value)
+        self.epoch_ptr = self._peer_own  # steps completed on this rank (uint32)
+        self.tag_mul = 2 * c.num_layers  # tag of (layer, kind) in a step: epoch * tag_mul + 2 * layer + kind + 1
+        dist.barrier(group=self.group)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (all ranks call it, then synchronise)."""
+        if getattr(self, "_peer_own", None) is None:
+            return
+        lib = N.lib()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for r, b in enumerate(self.peer_base):
+            if r != self.cfg.tp_rank:
+                lib.ada_peer_close(b)
+        dist.barrier(group=self.group)
+        lib.ada_peer_free(self._peer_own)
+        self._peer_own = None
+
+    def _gemm_rowpar(self, qb, w: NVFP4Weight, name: str, li: int, stream: int):
+        """Row-parallel projection (o / down): TP1 -> local partial planes; TP > 1 -> this rank's
+        partials, tagged for (step, layer, kind), into every rank's inbox of that kind."""
+        if not self.tp_peer:
+            return ("local",) + self._gemm_parts(qb, w, name, stream)
+        c, B, W = self.cfg, self.B, self.cfg.tp_size
+        xq, sfx, gx = qb
+        ks, kind = self.peer_ks[name], (0 if name == "o" else 1)
+        inboxes = N.ptr_array([b + self.off_inbox[name] for b in self.peer_base])
+        st = N.lib().ada_nvfp4_gemm_partials_peer(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), B, c.terms, self.bn,
+                                                  w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                                  w.scale_2.data_ptr(), w.n, w.k, w.n, B * w.n, ks, W, c.tp_rank,
+                                                  C.cast(inboxes, C.c_void_p), self.epoch_ptr, self.tag_mul,
+                                                  2 * li + kind + 1, self.gemm_only_ws.data_ptr(),
+                                                  self.gemm_only_ws.numel(), stream)
+        N.check(st, "NVFP4 kernel (peer partials)")
+        return ("peer", name, li, ks, w.n)
 
     # ------------------------------------------------------------------ ops
     def _linear(self, x: torch.Tensor, w: NVFP4Weight, y: torch.Tensor, stream: int, name: str | None = None):
@@ -321,15 +392,25 @@ class Qwen3DecodeEngine:
         return ns, w.n  # planes, row stride
 
     def _rms_quant_parts(self, planes, w, qb, stream, y=None):
-        """residual += sum(planes); normed = RMSNorm(residual); quantised into qb (or into y when qb is None)."""
+        """residual += sum(planes); normed = RMSNorm(residual); quantised into qb (or into y when
+        qb is None).  planes: ("local", n, ld) in self.parts, or ("peer", kind, layer, splits, ld):
+        all ranks' planes in this rank's inbox of that kind, once their count has arrived."""
         c = self.cfg
-        ns, ld = planes
         H = c.hidden
         rp = self.residual.data_ptr()
         xq, sfx, gx = qb if qb is not None else (None, None, None)
-        st = N.lib().ada_rmsnorm_quant_parts(self.parts.data_ptr(), ns, self.B * ld, ld, rp, H, rp, H, w.data_ptr(),
-                                             N.ptr(y), H, self.B, H, c.rms_eps, 0, 0, c.terms, self.bn,
-                                             N.ptr(xq), N.ptr(sfx), N.ptr(gx), stream)
+        if planes[0] == "local":
+            _, ns, ld = planes
+            st = N.lib().ada_rmsnorm_quant_parts(self.parts.data_ptr(), ns, self.B * ld, ld, rp, H, rp, H,
+                                                 w.data_ptr(), N.ptr(y), H, self.B, H, c.rms_eps, 0, 0, c.terms,
+                                                 self.bn, N.ptr(xq), N.ptr(sfx), N.ptr(gx), stream)
+        else:
+            _, name, li, ks, ld = planes
+            W, kind = c.tp_size, (0 if name == "o" else 1)
+            st = N.lib().ada_rmsnorm_quant_peer(self._peer_own + self.off_inbox[name], W * ks, self.B * ld, ld, rp, H,
+                                                rp, H, w.data_ptr(), N.ptr(y), H, self.B, H, c.rms_eps, 0, 0, c.terms,
+                                                self.bn, N.ptr(xq), N.ptr(sfx), N.ptr(gx), self.epoch_ptr,
+                                                self.tag_mul, 2 * li + kind + 1, self.gemm_only_ws.data_ptr(), stream)
         N.check(st, "rms_norm+quant")
 
     def _rms_quant(self, x, w, qb, stream, residual=None):
@@ -413,8 +494,9 @@ class Qwen3DecodeEngine:
         self._argmax(stream)
 
     def _layers_parts(self, lib, stream):
-        """TP1 fused step where every projection leaves split-K partial planes and the next
-        kernel sums them while loading (no split-K reduction inside the GEMMs)."""
+        """Fused step where every projection leaves split-K partial planes and the next kernel
+        sums them while loading (no split-K reduction inside the GEMMs); at TP > 1 the
+        row-parallel projections' planes of all ranks meet in each rank's inbox (peer memory)."""
         c = self.cfg
         B, D = self.B, c.head_dim
         qn = c.hq * D
@@ -440,15 +522,17 @@ class Qwen3DecodeEngine:
                 self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv, D, c.page_size,
                 D ** -0.5, 1.0, 1.0, 0, None, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
                 gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, ATTN_META_EARLY, stream), "attention")
-            planes = self._gemm_parts(self.q_attn, L["o"], "o", stream)
+            planes = self._gemm_rowpar(self.q_attn, L["o"], "o", li, stream)
             self._rms_quant_parts(planes, L["post_norm"], self.q_hidden, stream)
             ns, ld = self._gemm_parts(self.q_hidden, L["gate_up"], "gate_up", stream)
             xq, sfx, gx = self.q_inter
             N.check(lib.ada_gated_act_quant_parts(self.parts.data_ptr(), ns, B * ld, ld, None, 0, B, c.inter, 0, 0,
                                                   c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(),
                                                   stream), "silu_and_mul+quant")
-            planes = self._gemm_parts(self.q_inter, L["down"], "down", stream)
+            planes = self._gemm_rowpar(self.q_inter, L["down"], "down", li, stream)
         self._rms_quant_parts(planes, self.final_norm, None, stream, y=self.xnorm)
+        if self.tp_peer:  # every counter of this step has been consumed
+            N.check(lib.ada_tp_epoch_advance(self.epoch_ptr, stream), "tp epoch")
 
     def _layers_unfused(self, lib, stream):
         """Reference-shaped sequence: every op a separate kernel (act-quant separate from the GEMM)."""
@@ -524,10 +608,13 @@ class Qwen3DecodeEngine:
 
     def kernels_per_step(self) -> int:
         """adallm_b200 kernels launched by one forward(): embedding; per layer fused: norm+quant x2,
-        GEMM x4, qk-norm/rope/store, attention split + merge+quant, SiLU*up+quant (unfused: norm x2,
-        act-quant + GEMM x4, qk-norm/rope/store, attention split + merge, SiLU*up); final norm; argmax x2."""
-        per_layer = 10 if self.fused else 14
-        return 1 + self.cfg.num_layers * per_layer + 3
+        GEMM x4, qk-norm/rope/store, attention (one kernel for short caches, else split +
+        merge+quant), SiLU*up+quant (unfused: norm x2, act-quant + GEMM x4, qk-norm/rope/store,
+        attention split + merge (or one kernel), SiLU*up); final norm; argmax x2; TP peer path:
+        the epoch advance."""
+        attn = 1 if self.max_pages_per_seq * self.cfg.page_size <= 1024 and self.cfg.hkv <= 8 else 2
+        per_layer = (8 if self.fused else 12) + attn
+        return 1 + self.cfg.num_layers * per_layer + 3 + (1 if getattr(self, "tp_peer", False) else 0)
 
     def export_cpu_weights(self) -> dict:
         """CPU copies in the reference parameter layout (tensor-parallel size 1 only)."""

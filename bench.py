@@ -484,6 +484,7 @@ def run_ours(args, rank, world, local_rank):
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     del g_plain, g_adv  # graphs holding NCCL work go before the process group
+    engine.close()  # peer mappings (TP) are released by every rank before the group goes
 
 
 def main():

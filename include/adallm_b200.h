@@ -287,6 +287,47 @@ ADA_API int ada_nvfp4_gemm_partials(const uint8_t* xq, const uint8_t* sfx, const
                                     int64_t part_plane, int nplanes, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/* ------------------------------------------------------------------------
+ * Tensor parallelism over NVLink peer memory (no counterpart in the reference, whose row-parallel
+ * linears all-reduce their outputs with NCCL, adallm/ops/linear.py:193-215).  One process per GPU;
+ * every rank allocates an inbox with ada_peer_alloc, the ranks exchange the 64-byte handles
+ * (e.g. with torch.distributed) and map the peers' inboxes with ada_peer_open.  Plain peer stores
+ * and loads; no multicast object.
+ *
+ * ada_nvfp4_gemm_partials_peer: the partial-plane GEMM of a row-parallel projection (this rank's
+ * K shard) writes its fp32 partial of K split s into plane tp_rank * nplanes + s of EVERY rank's
+ * inbox (inboxes[d] = rank d's inbox as mapped here, 16-byte aligned; planes of 8-byte words
+ * [world * nplanes][m][part_ld]).  Each word is the value's bits | tag << 32 with
+ * tag = *epoch * tag_mul + tag_add, written by one 8-byte store, so no fence or counter is needed.
+ * ada_rmsnorm_quant_peer: ada_rmsnorm_quant_parts over this rank's inbox (nparts = world * nplanes,
+ * summed in plane order, so every rank computes the same rows), polling each word until its tag is
+ * this step's (bounded, ~2 s; then *err = 0x50 and the stale words are used).
+ * *epoch counts the steps completed on this rank; ada_tp_epoch_advance(epoch) ends a step (after
+ * its last consumer); give each projection of each layer its own tag_add in [1, tag_mul].  An inbox
+ * may be rewritten by the peers only after this rank's consumer finished reading it: use one inbox
+ * per projection kind (o_proj, down_proj), whose next writes depend, through the other kind's
+ * words, on this rank having moved on. */
+#define ADA_PEER_HANDLE_BYTES 64
+ADA_API int ada_peer_alloc(size_t bytes, void** ptr, void* handle);
+ADA_API int ada_peer_open(const void* handle, void** ptr);
+ADA_API int ada_peer_close(void* ptr);
+ADA_API int ada_peer_free(void* ptr);
+ADA_API int ada_tp_epoch_advance(uint32_t* epoch, void* stream);
+ADA_API int ada_nvfp4_gemm_ctas(int64_t m, int64_t n, int64_t k, int terms, int nplanes);
+ADA_API int ada_nvfp4_gemm_partials_peer(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m,
+                                         int terms, int block_n, const uint8_t* w_packed, int64_t ldw,
+                                         const uint8_t* sf_w, const float* w_scale_2, int64_t n, int64_t k,
+                                         int64_t part_ld, int64_t part_plane, int nplanes, int32_t world,
+                                         int32_t tp_rank, void* const* inboxes, const uint32_t* epoch,
+                                         uint32_t tag_mul, uint32_t tag_add, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+ADA_API int ada_rmsnorm_quant_peer(const void* inbox, int32_t nparts, int64_t plane, int64_t ldp,
+                                   const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                   const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
+                                   float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
+                                   uint8_t* sfx, float* gx, const uint32_t* epoch, uint32_t tag_mul,
+                                   uint32_t tag_add, uint32_t* err, void* stream);
+
 /* Consumers of partial planes (parts: nparts fp32 planes, plane / ldp = floats between planes /
  * rows, 16-byte aligned): the input element is the plane sum rounded to dtype, then exactly
  * ada_rmsnorm_quant (xq == NULL: plain RMSNorm into y), ada_gated_act_quant and
