@@ -387,12 +387,23 @@ static inline uint32_t pow2_cols(uint32_t c) {
 // issues its own tcgen05 stream); else one CTA per SM with a deeper pipeline.
 // No more stages than the K steps of the longest split (`max_units`): a pipeline deeper than the
 // work only holds shared memory that the next kernel's CTAs could use.
+// per_sm = 3: the plan needs three co-resident CTAs per SM (shared memory <= 74 KB, TMEM <= 128
+// columns; only tiles compiled to the 96-register budget); -1 stages if that does not fit.
 template <int BN, int T>
-static void stages_for(int ks, int rows_max, int max_units, int& stages, uint32_t& cols, size_t& smem) {
+static void stages_for(int ks, int rows_max, int max_units, int& stages, uint32_t& cols, size_t& smem,
+                       int per_sm = 2) {
   using C = Cfg<BN, T>;
   const size_t recv = C::recv_bytes(ks, rows_max);
   const int top = max_units < 2 ? 2 : max_units < MAX_STAGES ? max_units : MAX_STAGES;
   int s = 0;
+  if (per_sm == 3) {
+    for (int k = top; k >= 2 && BN * T <= 96; --k)
+      if (C::smem_bytes(k, recv) <= 74 * 1024 && C::tmem_need(k) <= 128) { s = k; break; }
+    stages = s ? s : -1;
+    cols = s ? pow2_cols(C::tmem_need(s)) : 0;
+    smem = C::smem_bytes(s, recv);
+    return;
+  }
   for (int k = top; k >= (top < 3 ? top : 3); --k)
     if (C::smem_bytes(k, recv) <= 113 * 1024 && C::tmem_need(k) <= 256) { s = k; break; }
   if (s == 0)
@@ -408,8 +419,9 @@ static void stages_for(int ks, int rows_max, int max_units, int& stages, uint32_
   X(32, 1) X(32, 2) X(32, 3) X(32, 4) X(64, 1) X(64, 2) X(128, 1)
 
 static void stages_dispatch(int bn, int t, int ks, int rows_max, int max_units, int& stages, uint32_t& cols,
-                            size_t& smem) {
-#define ADA_SD(B, TT) if (bn == B && t == TT) { stages_for<B, TT>(ks, rows_max, max_units, stages, cols, smem); return; }
+                            size_t& smem, int per_sm = 2) {
+#define ADA_SD(B, TT) \
+  if (bn == B && t == TT) { stages_for<B, TT>(ks, rows_max, max_units, stages, cols, smem, per_sm); return; }
   ADA_FP4_CONFIGS(ADA_SD)
 #undef ADA_SD
   stages = 0;
@@ -493,6 +505,15 @@ static int num_sms() {
   return cache[dev];
 }
 
+// A partial-plane plan of ks splits whose pipeline fits three CTAs to an SM.
+static bool fits_three(int bn, int terms, int64_t ks, int nkt) {
+  int st = 0;
+  uint32_t c = 0;
+  size_t sm = 0;
+  stages_dispatch(bn, terms, 1, (int)cdiv(BM, ks), (int)cdiv(nkt, ks), st, c, sm, 3);
+  return st >= 2;
+}
+
 // force_ks > 0 overrides the split-K factor (tests of the cluster reduction).
 // parts: split-K partial planes are written out (no cluster reduction, any split works).
 static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, Plan& P, bool parts = false) {
@@ -512,13 +533,19 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   // least 4 of them (shorter splits cost more in the cluster reduction than they gain), and
   // whose clusters (one per tile) all fit on the GPU in one wave, at most two CTAs per SM.
   int64_t ks = 1;
+  bool three_per_sm = false;
   const int64_t ks_cap = P.nkt < MAX_KS ? P.nkt : MAX_KS;
   if (force_ks > 0) {
     ks = force_ks < ks_cap ? force_ks : ks_cap;
   } else if (parts) {
-    // as many splits as keep every CTA resident in one wave (two per SM)
-    ks = (2 * (int64_t)num_sms()) / tiles;
+    // as many splits as keep every CTA resident in one wave: three per SM when the pipeline
+    // fits three to an SM (spreads a projection with few tiles over more SMs), else two
+    ks = (3 * (int64_t)num_sms()) / tiles;
     ks = ks < 1 ? 1 : ks > ks_cap ? ks_cap : ks;
+    if (tiles * ks > 2 * (int64_t)num_sms() && !fits_three(P.bn, terms, ks, P.nkt)) {
+      ks = (2 * (int64_t)num_sms()) / tiles;
+      ks = ks < 1 ? 1 : ks > ks_cap ? ks_cap : ks;
+    }
   } else {
     for (int64_t c = (P.nkt / 4 < ks_cap ? P.nkt / 4 : ks_cap); c >= 2; --c) {
       if (P.nkt % c || tiles * c > 2 * (int64_t)num_sms()) continue;
@@ -530,8 +557,10 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   }
   P.ks = (int)ks;
   P.rows_max = (int)cdiv(BM, ks);
+  three_per_sm = parts && tiles * ks > 2 * (int64_t)num_sms() && fits_three(P.bn, terms, ks, P.nkt);
   uint32_t cols = 0;
-  stages_dispatch(P.bn, terms, parts ? 1 : P.ks, P.rows_max, (int)cdiv(P.nkt, ks), P.stages, cols, P.smem);
+  stages_dispatch(P.bn, terms, parts ? 1 : P.ks, P.rows_max, (int)cdiv(P.nkt, ks), P.stages, cols, P.smem,
+                  three_per_sm ? 3 : 2);
   if (P.stages < 2) return ADA_ERR_UNSUPPORTED;
   P.tmem_cols = (int)cols;
   size_t off = ERR_BYTES;
