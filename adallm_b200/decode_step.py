@@ -30,6 +30,7 @@ import math
 import zlib
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -657,13 +658,14 @@ class DecodeSession:
     D2H_BYTES_PER_STEP = property(lambda self: self.e.B * 8)
 
     def prepare(self, tokens: torch.Tensor):
+        """Fill the pinned input buffers for the next step (numpy views: a few microseconds)."""
         page = self.e.cfg.page_size
-        pos = self.lens
-        self.h_ids.copy_(tokens)
-        self.h_pos.copy_(pos)
-        blk = self.block_tables.gather(1, (pos // page).unsqueeze(1)).squeeze(1).to(torch.int64)
-        self.h_slot.copy_((blk * page + pos % page).to(torch.int32))
-        self.h_ctx.copy_((pos + 1).to(torch.int32))
+        pos = self.lens.numpy()
+        self.h_ids.numpy()[:] = tokens.numpy() if isinstance(tokens, torch.Tensor) else tokens
+        self.h_pos.numpy()[:] = pos
+        blk = self.block_tables.numpy()[np.arange(pos.shape[0]), pos // page].astype(np.int64)
+        self.h_slot.numpy()[:] = blk * page + pos % page
+        self.h_ctx.numpy()[:] = pos + 1
 
     def upload(self):
         e = self.e
@@ -674,6 +676,32 @@ class DecodeSession:
 
     def download(self) -> torch.Tensor:
         self.h_out.copy_(self.e.next_tokens, non_blocking=True)
+        torch.cuda.current_stream(self.e.device).synchronize()
+        return self.h_out.clone()
+
+    def capture_step(self) -> torch.cuda.CUDAGraph:
+        """One CUDA graph for a host-fed step: H2D of the pinned inputs, forward(), D2H of the
+        greedy tokens into pinned memory.  step() replays it."""
+        e = self.e
+        s = torch.cuda.Stream(e.device)
+        s.wait_stream(torch.cuda.current_stream(e.device))
+        with torch.cuda.stream(s):  # warm-up outside capture
+            self.upload()
+            e.forward()
+        torch.cuda.current_stream(e.device).wait_stream(s)
+        torch.cuda.synchronize(e.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.upload()
+            e.forward()
+            self.h_out.copy_(e.next_tokens, non_blocking=True)
+        self._step_graph = g
+        return g
+
+    def step(self, tokens) -> torch.Tensor:
+        """prepare + replay of the captured step + wait for the tokens (capture_step() first)."""
+        self.prepare(tokens)
+        self._step_graph.replay()
         torch.cuda.current_stream(self.e.device).synchronize()
         return self.h_out.clone()
 

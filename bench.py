@@ -351,21 +351,18 @@ def run_ours(args, rank, world, local_rank):
     sess.lens += args.warmup + args.steps
     toks = engine.input_ids.cpu()
 
-    # ---------------- e2e: host-fed steps through the session (H2D inputs, D2H tokens every step)
+    # ---------------- e2e: host-fed steps through the session: every step fills the pinned
+    # inputs on the host, replays one graph (H2D copies of the inputs, forward, D2H copy of the
+    # tokens) and waits for the tokens
+    g_step = sess.capture_step()
     for _ in range(args.warmup):
-        sess.prepare(toks)
-        sess.upload()
-        g_plain.replay()
-        toks = sess.download()
+        toks = sess.step(toks)
         sess.commit()
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(args.steps):
-        sess.prepare(toks)
-        sess.upload()
-        g_plain.replay()
-        toks = sess.download()
+        toks = sess.step(toks)
         sess.commit()
     f1.record(stream)
     f1.synchronize()
@@ -483,7 +480,8 @@ def run_ours(args, rank, world, local_rank):
                 "gpu_launches": engine.kernels_per_step() * args.steps,
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
-    del g_plain, g_adv  # graphs holding NCCL work go before the process group
+    del g_plain, g_adv, g_step  # graphs holding NCCL work go before the process group
+    sess._step_graph = None
     engine.close()  # peer mappings (TP) are released by every rank before the group goes
 
 
