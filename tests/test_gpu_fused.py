@@ -65,6 +65,40 @@ def test_rmsnorm_quant_matches_unfused(hidden, gemma, with_res, rows, terms, bn)
     same(got, ref)
 
 
+@pytest.mark.parametrize("gemma", [False, True])
+def test_rmsnorm_quant_amax_edge_rows(gemma):
+    """The normalised row amax travels with the sum of squares as candidates; rows where that
+    cannot work take the second exchange.  Both give exactly the unfused amax: a constant row
+    (every element a candidate), ties of the maximum across CTAs, an all-zero row, rows near the
+    bottom and the top of the range, one huge outlier, and ordinary rows."""
+    d = dev()
+    H, rows, terms, bn = 4096, 16, 4, 16
+    g = torch.Generator(device="cpu").manual_seed(21)
+    x = torch.randn((rows, H), generator=g)
+    x[0] = 1.5
+    x[1] = 0.0
+    x[2, ::512] = 9.0  # the same maximum in every CTA's slice
+    x[3] *= 1e-30
+    x[4] *= 1e30
+    x[5, 1234] = 3.0e4
+    x[6] = torch.where(torch.arange(H) % 2 == 0, 2.0, -2.0)
+    x = x.to(torch.bfloat16).to(d)
+    w = (torch.randn(H, generator=g) * 0.1 + (0 if gemma else 1)).to(torch.bfloat16)
+    w[:8] = 0.0
+    w = w.to(d)
+    s = torch.cuda.current_stream().cuda_stream
+    y_ref = rms_norm(x, w, 1e-6, gemma=gemma)
+    ref = act_quant(y_ref, terms, bn)
+    got = qbufs(rows, H, terms, bn, d)
+    y = torch.empty_like(x)
+    N.check(N.lib().ada_rmsnorm_quant(x.data_ptr(), H, None, H, None, H, w.data_ptr(), y.data_ptr(), H, rows, H,
+                                      1e-6, int(gemma), 0, terms, bn, got[0].data_ptr(), got[1].data_ptr(),
+                                      got[2].data_ptr(), s), "rmsnorm_quant")
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    same(got, ref)
+
+
 @pytest.mark.parametrize("inter,act,terms", [(12288, 0, 4), (1536, 0, 1), (3072, 1, 4), (21504, 1, 6)])
 def test_gated_act_quant_matches_unfused(inter, act, terms):
     d = dev()
