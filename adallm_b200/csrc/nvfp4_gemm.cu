@@ -59,6 +59,11 @@ struct GemmParams {
   // goes to plane tp_rank * ks + s of every rank's inbox as tagged 8-byte words (value bits |
   // tag << 32, tag = *epoch * tag_mul + tag_add), which the consumer polls: no fence, no counter
   int world, tp_rank;
+  // grouped (MoE) GEMM: m-tile t of the operand belongs to expert tile_expert[t] (< 0: unused
+  // tile, the CTA exits), whose weights are rows [e * N, (e + 1) * N) of the stacked matrix;
+  // operand row r is output row row_map[r] (< 0: padding, not stored).  Null: dense.
+  const int* tile_expert;
+  const int* row_map;
   unsigned long long* inbox[MAX_PEERS];
   const unsigned int* epoch;
   unsigned int tag_mul, tag_add;
@@ -130,6 +135,13 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = blockIdx.x, tile = blockIdx.y;
   const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+  int expert = 0;
+  if (p.tile_expert) {  // the routing written by the previous kernel decides whether this tile runs
+    pdl_wait();
+    expert = p.tile_expert[m_tile];
+    if (expert < 0) return;  // before any barrier or TMEM: nothing to release
+  }
+  const int w_tile = expert * p.n_tiles + n_tile;  // 128-row block of the (stacked) weight matrix
   const int kt0 = (int)((int64_t)rank * p.nkt / ks), kt1 = (int)((int64_t)(rank + 1) * p.nkt / ks);
   const int nunits = kt1 - kt0;
   const int kb64 = p.K / 64;
@@ -168,15 +180,15 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
         const int kt = kt0 + i;
         uint8_t* st = smem + (size_t)i * C::STAGE;
         mbar_expect_tx(&full[i], C::A_BYTES + C::SFA_BYTES);
-        tma_load_2d(st, &tmw, &full[i], kt * KT_BYTES, n_tile * BM);
-        bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
+        tma_load_2d(st, &tmw, &full[i], kt * KT_BYTES, w_tile * BM);
+        bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)w_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
                   C::SFA_BYTES, &full[i]);
       }
       // The rest of this CTA's weight slice is pulled into L2 while the previous kernel runs.
       for (int i = pre; i < nunits; ++i) {
         const int kt = kt0 + i;
-        tma_prefetch_l2_2d(&tmw, kt * KT_BYTES, n_tile * BM);
-        bulk_prefetch_l2(p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFA_BYTES);
+        tma_prefetch_l2_2d(&tmw, kt * KT_BYTES, w_tile * BM);
+        bulk_prefetch_l2(p.sfw + ((size_t)w_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFA_BYTES);
       }
       pdl_wait();
       for (int i = 0; i < nunits; ++i) {
@@ -186,8 +198,8 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
         if (i >= stages) {
           if (!mbar_wait_bounded(&empty[s], ((i / stages) & 1) ^ 1, abort_v, p.err, 1u)) break;
           mbar_expect_tx(&full[s], C::A_BYTES + C::SFA_BYTES);
-          tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, n_tile * BM);
-          bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
+          tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, w_tile * BM);
+          bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)w_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
                     C::SFA_BYTES, &full[s]);
         }
         mbar_arrive_expect_tx(&full[s], C::B_BYTES + C::SFB_BYTES);
@@ -235,7 +247,7 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
     const int q = warp & 3;
     const int et = threadIdx.x - 64;  // 0..127 within the epilogue group
     if (et < BN) {
-      const float gw = __ldg(p.gw);
+      const float gw = __ldg(p.gw + expert);
       float g = __ldg(p.gx + m_tile * BN + et);
 #pragma unroll
       for (int t = 0; t < T; ++t) {
@@ -289,8 +301,8 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
         const float b = load_bias(p.bias, p.out_dtype, n);
 #pragma unroll
         for (int j = 0; j < BN; ++j) {
-          const int m = m_tile * BN + j;
-          if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, out[j] + b);
+          const int m = p.row_map ? p.row_map[m_tile * BN + j] : m_tile * BN + j;
+          if (m >= 0 && m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, out[j] + b);
         }
       }
     } else {
@@ -516,13 +528,14 @@ static bool fits_three(int bn, int terms, int64_t ks, int nkt) {
 
 // force_ks > 0 overrides the split-K factor (tests of the cluster reduction).
 // parts: split-K partial planes are written out (no cluster reduction, any split works).
-static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, Plan& P, bool parts = false) {
+static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, Plan& P, bool parts = false,
+                     int force_bn = 0) {
   if (m <= 0 || n <= 0 || k <= 0) return ADA_ERR_INVALID_ARG;
   if (terms < 1 || terms > q::MAX_TERMS) return ADA_ERR_INVALID_ARG;
   if (n % BM || k % KT) return ADA_ERR_UNSUPPORTED;
   if (m > (1 << 24) || n > (1 << 24) || k > (1 << 24)) return ADA_ERR_UNSUPPORTED;
   P.terms = terms;
-  P.bn = block_n_for(m, terms);
+  P.bn = force_bn ? force_bn : block_n_for(m, terms);
   P.m_tiles = (int)cdiv(m, P.bn);
   P.m_pad = P.m_tiles * P.bn;
   P.n_tiles = (int)(n / BM);
@@ -601,9 +614,11 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
                     const void* bias, void* y, int y_dtype, int64_t ldy, unsigned int* err, cudaStream_t st,
                     float* part = nullptr, int64_t part_plane = 0, int64_t part_ld = 0, int world = 1, int tp_rank = 0,
                     unsigned long long* const* inboxes = nullptr, const unsigned int* epoch = nullptr,
-                    unsigned int tag_mul = 0, unsigned int tag_add = 0) {
+                    unsigned int tag_mul = 0, unsigned int tag_add = 0, const int* tile_expert = nullptr,
+                    const int* row_map = nullptr, int64_t w_rows = 0) {
   CUtensorMap tmw, tmx;
-  if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)n, (uint64_t)ldw, BM)) return ADA_ERR_CUDA;
+  if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)(w_rows ? w_rows : n), (uint64_t)ldw, BM))
+    return ADA_ERR_CUDA;
   if (!make_map(&tmx, xq, (uint64_t)(k / 2), (uint64_t)P.terms * P.m_pad, (uint64_t)(k / 2),
                 (uint32_t)(P.terms * P.bn)))
     return ADA_ERR_CUDA;
@@ -635,14 +650,65 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
   gp.epoch = epoch;
   gp.tag_mul = tag_mul;
   gp.tag_add = tag_add;
+  gp.tile_expert = tile_expert;
+  gp.row_map = row_map;
   return dispatch_gemm(tmw, tmx, gp, P, st);
 }
+
+// ---- grouped (MoE) GEMM routing ------------------------------------------------------
+// One CTA: rows are counted per expert, every expert gets whole 16-row operand tiles (a prefix
+// sum over experts), tile_expert[t] names the expert of tile t (-1: unused), row_map[s] the
+// input row of operand row s (-1: padding).  Rows keep no particular order inside an expert:
+// each output row depends on its own input row only.  An expert id outside [0, experts) sets
+// the workspace error word (its row is not computed).
+constexpr int GROUP_BN = 16;
+constexpr unsigned int ERR_EXPERT_ID = 0x60;
+
+__global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__ ids, int m, int experts, int t_max,
+                                                     int* tile_expert, int* row_map, unsigned int* err) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int route_smem[];
+  int* cnt = route_smem;        // rows per expert
+  int* base = cnt + experts;    // first tile of the expert
+  int* fill = base + experts;   // rows placed so far
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) cnt[e] = fill[e] = 0;
+  for (int t = threadIdx.x; t < t_max; t += blockDim.x) tile_expert[t] = -1;
+  for (int r = threadIdx.x; r < t_max * GROUP_BN; r += blockDim.x) row_map[r] = -1;
+  __syncthreads();
+  for (int r = threadIdx.x; r < m; r += blockDim.x) {
+    const int e = __ldg(ids + r);
+    if (e >= 0 && e < experts)
+      atomicAdd(&cnt[e], 1);
+    else
+      atomicExch(err, ERR_EXPERT_ID);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // tiles per expert, prefix sum (experts is at most a few thousand)
+    int run = 0;
+    for (int e = 0; e < experts; ++e) {
+      base[e] = run;
+      run += (cnt[e] + GROUP_BN - 1) / GROUP_BN;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < experts; e += blockDim.x)
+    for (int t = 0; t < (cnt[e] + GROUP_BN - 1) / GROUP_BN; ++t) tile_expert[base[e] + t] = e;
+  for (int r = threadIdx.x; r < m; r += blockDim.x) {
+    const int e = __ldg(ids + r);
+    if (e < 0 || e >= experts) continue;
+    row_map[base[e] * GROUP_BN + atomicAdd(&fill[e], 1)] = r;
+  }
+}
+
+// Operand tiles a grouped call can need: every expert's partial tile plus the full ones.
+inline int64_t group_tiles(int64_t m, int64_t experts) { return cdiv(m, GROUP_BN) + (experts < m ? experts : m); }
 
 }  // namespace fp4
 
 namespace fused {
 int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
-                     cudaStream_t st);
+                     cudaStream_t st, const int* row_map);
 }
 }  // namespace ada
 
@@ -691,10 +757,71 @@ extern "C" int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int6
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
-  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st);
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, nullptr);
   if (rc != ADA_OK) return rc;
   return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y,
                        y_dtype, ldy, reinterpret_cast<unsigned int*>(ws), st);
+}
+
+// Grouped plan: 16-row operand tiles, one per (expert, 16 rows), no K split.
+static int grouped_plan(int64_t m, int64_t n, int64_t k, int terms, int64_t experts, fp4::Plan& P, size_t& off_route,
+                        size_t& total) {
+  if (m <= 0 || experts <= 0 || experts > 4096) return ADA_ERR_INVALID_ARG;
+  if (terms * fp4::GROUP_BN > 128) return ADA_ERR_UNSUPPORTED;
+  const int64_t t_max = fp4::group_tiles(m, experts);
+  const int rc = fp4::make_plan(t_max * fp4::GROUP_BN, n, k, terms, 1, P, false, fp4::GROUP_BN);
+  if (rc != ADA_OK) return rc;
+  off_route = (P.total + 255) & ~(size_t)255;
+  total = off_route + (size_t)(1 + t_max + t_max * fp4::GROUP_BN) * sizeof(int);
+  return ADA_OK;
+}
+
+extern "C" size_t ada_nvfp4_linear_grouped_workspace_size(int64_t m, int64_t n, int64_t k, int terms,
+                                                          int32_t num_experts) {
+  fp4::Plan P;
+  size_t off = 0, total = 0;
+  return grouped_plan(m, n, k, terms, num_experts, P, off, total) == ADA_OK ? total : 0;
+}
+
+extern "C" int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                        const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                        const float* w_scale_2, int32_t num_experts, int64_t n,
+                                        const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy, int terms,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (m == 0) return ADA_OK;
+  if (!x || !w_packed || !sf_w || !w_scale_2 || !expert_ids || !y || !workspace) return ADA_ERR_INVALID_ARG;
+  if ((x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16) || (y_dtype != ADA_DT_BF16 && y_dtype != ADA_DT_F16))
+    return ADA_ERR_INVALID_ARG;
+  if (ldx < k || ldy < n || ldw < k / 2) return ADA_ERR_INVALID_ARG;
+  if ((int64_t)num_experts * n > (1 << 24)) return ADA_ERR_UNSUPPORTED;
+  fp4::Plan P;
+  size_t off_route = 0, total = 0;
+  int rc = grouped_plan(m, n, k, terms, num_experts, P, off_route, total);
+  if (rc != ADA_OK) return rc;
+  if (workspace_bytes < total) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)w_packed & 15) || (ldw & 15) || ((uintptr_t)sf_w & 15) ||
+      ((uintptr_t)workspace & 255) || ((uintptr_t)expert_ids & 3))
+    return ADA_ERR_ALIGNMENT;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int t_max = P.m_tiles;
+  int* tile_expert = reinterpret_cast<int*>(ws + off_route) + 1;
+  int* row_map = tile_expert + t_max;
+  unsigned int* err = reinterpret_cast<unsigned int*>(ws);
+  const size_t rsmem = (size_t)3 * num_experts * sizeof(int);
+  if (rsmem > 48 * 1024 &&
+      cudaFuncSetAttribute(fp4::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem) != cudaSuccess)
+    return ADA_ERR_CUDA;
+  (void)launch_k(fp4::route_kernel, dim3(1), dim3(1024), rsmem, st, expert_ids, (int)m, (int)num_experts, t_max,
+                 tile_expert, row_map, err);
+  ADA_CHECK_LAUNCH();
+  const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, row_map);
+  if (rc != ADA_OK) return rc;
+  // the stacked weight matrix [num_experts * n, k / 2]: expert e's tile j is 128-row block e * (n / 128) + j
+  return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, y,
+                       y_dtype, ldy, err, st, nullptr, 0, 0, 1, 0, nullptr, nullptr, 0, 0, tile_expert, row_map,
+                       (int64_t)num_experts * n);
 }
 
 extern "C" int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
@@ -715,7 +842,7 @@ extern "C" int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int6
   if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)xq & 15) || ((uintptr_t)gx & 3)) return ADA_ERR_ALIGNMENT;
   const int64_t m_pad = cdiv(m, block_n) * block_n;
   const q::QuantDst dst{xq, sfx, gx, terms, block_n, (int)k};
-  return fused::launch_act_quant(x, x_dtype, ldx, m, m_pad, dst, reinterpret_cast<cudaStream_t>(stream));
+  return fused::launch_act_quant(x, x_dtype, ldx, m, m_pad, dst, reinterpret_cast<cudaStream_t>(stream), nullptr);
 }
 
 extern "C" int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,

@@ -54,14 +54,16 @@ def prepack_scales(w_scale: torch.Tensor, n: int, k: int, out: torch.Tensor | No
     return out
 
 
-def _cached_sf(w_scale: torch.Tensor, n: int, k: int) -> torch.Tensor:
-    key = (w_scale.data_ptr(), w_scale._version, n, k)
-    cached = getattr(w_scale, "_ada_sf", None)
+def _cached_sf(w_scale: torch.Tensor, n: int, k: int, owner: torch.Tensor | None = None) -> torch.Tensor:
+    """Prepacked scales of w_scale ([n, k/16]), cached on `owner` (default: w_scale itself)."""
+    owner = w_scale if owner is None else owner
+    key = (w_scale.data_ptr(), owner._version, n, k)
+    cached = getattr(owner, "_ada_sf", None)
     if cached is not None and cached[0] == key:
         return cached[1]
     sf = prepack_scales(w_scale, n, k)
     try:
-        w_scale._ada_sf = (key, sf)
+        owner._ada_sf = (key, sf)
     except Exception:
         pass
     return sf
@@ -147,10 +149,14 @@ def nvfp4_linear_dual(x, w1_packed, w1_scale, w1_scale_2, w2_packed, w2_scale, w
 
 
 def nvfp4_linear_gather(x, w_packed, w_scale, w_scale_2, expert_ids, group_size, terms: int | None = None):
-    """Row m uses expert expert_ids[m] (adallm/ops/nvfp4_gemm.py:657-714).  Rows are grouped by
-    expert on the host and each group runs the tensor-core linear (not graph-capturable)."""
+    """Row m uses expert expert_ids[m] (adallm/ops/nvfp4_gemm.py:657-714).  One grouped
+    tensor-core GEMM on the device (ada_nvfp4_linear_grouped): a routing kernel gives every
+    expert whole 16-row operand tiles, the quantiser gathers the rows into them and the GEMM
+    streams only the weights of the experts in use.  No host synchronisation: graph-capturable."""
     if not x.is_cuda:
         raise RuntimeError("nvfp4_linear_gather requires CUDA tensors")
+    if group_size != 16:
+        raise ValueError("adallm_b200 implements NVFP4 group size 16")
     x2 = x.reshape(-1, x.shape[-1])
     m, k = x2.shape
     e, n, khalf = w_packed.shape
@@ -161,10 +167,23 @@ def nvfp4_linear_gather(x, w_packed, w_scale, w_scale_2, expert_ids, group_size,
     if w_scale_2 is None:
         w_scale_2 = torch.ones((e,), device=x.device, dtype=torch.float32)
     dt = x2.dtype if x2.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    x2 = x2.to(dt)
+    if x2.stride(-1) != 1 or (x2.stride(0) % 8) or (x2.data_ptr() % 16):
+        x2 = x2.contiguous()
+    wp = w_packed if w_packed.is_contiguous() else w_packed.contiguous()
+    sf = _cached_sf(w_scale.reshape(e * n, k // 16), e * n, k, owner=w_scale)
+    g2 = w_scale_2.detach().to(device=x.device, dtype=torch.float32).reshape(e).contiguous()
+    ids = expert_ids.to(device=x.device, dtype=torch.int32).reshape(m).contiguous()
+    t = DEFAULT_TERMS if terms is None else int(terms)
     y = torch.empty((m, n), dtype=dt, device=x.device)
-    ids = expert_ids.to(torch.int64)
-    for ex in torch.unique(ids).tolist():
-        rows = (ids == ex).nonzero().flatten()
-        y[rows] = nvfp4_linear(x2[rows].to(dt), w_packed[ex], w_scale[ex], w_scale_2[ex], None, None, group_size,
-                               terms)
+    if m == 0:
+        return y.to(x.dtype).view(*x.shape[:-1], n)
+    need = int(N.lib().ada_nvfp4_linear_grouped_workspace_size(m, n, k, t, e))
+    if need == 0:
+        raise ValueError(f"nvfp4_linear_gather: unsupported shape M={m} N={n} K={k} E={e}")
+    ws = _workspace(x.device, need)
+    st = N.lib().ada_nvfp4_linear_grouped(x2.data_ptr(), N.DT[dt], x2.stride(0), m, k, wp.data_ptr(), wp.stride(1),
+                                          sf.data_ptr(), g2.data_ptr(), e, n, ids.data_ptr(), y.data_ptr(), N.DT[dt],
+                                          y.stride(0), t, ws.data_ptr(), ws.numel(), N.stream_ptr(x.device))
+    N.check(st, "NVFP4 grouped kernel")
     return y.to(x.dtype).view(*x.shape[:-1], n)

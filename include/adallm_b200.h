@@ -253,6 +253,20 @@ ADA_API int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int64_t
  *   gx  [m_pad]                               (1.0 for the zero padding rows)
  * with m_pad = ceil(m / block_n) * block_n, block_n in {16, 32, 64, 128} and
  * terms * block_n <= 128 (ada_nvfp4_block_n(m, terms) gives the GEMM's choice). */
+/* Grouped NVFP4 linear: row m of x uses expert expert_ids[m] (int32, in [0, num_experts)).
+ * Replaces nvfp4_linear_gather (adallm/ops/nvfp4_gemm.py:657-714, kernel :363-457).  w_packed is the
+ * contiguous stack [num_experts][n][k/2] (row stride ldw, expert stride n * ldw), sf_w its prepacked
+ * scales (ada_nvfp4_prepack_scales of the [num_experts * n, k/16] scale matrix), w_scale_2 [num_experts].
+ * A routing kernel gives every expert whole 16-row operand tiles, the quantiser gathers the rows into
+ * them and one tensor-core GEMM streams only the weights of the experts in use; no host sync.  An id
+ * outside the range sets the workspace error word (0x60) and leaves its row unwritten. */
+ADA_API size_t ada_nvfp4_linear_grouped_workspace_size(int64_t m, int64_t n, int64_t k, int terms,
+                                                       int32_t num_experts);
+ADA_API int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                     const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                     const float* w_scale_2, int32_t num_experts, int64_t n,
+                                     const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy, int terms,
+                                     void* workspace, size_t workspace_bytes, void* stream);
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by

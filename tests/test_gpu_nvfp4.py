@@ -187,6 +187,67 @@ def test_dual_and_gather():
         assert rel_l2(y[r:r + 1].float().cpu(), ref) < 1e-2
 
 
+def _experts(e, n, k, seed):
+    return [random_weight(n, k, seed=seed + i, realistic=False) for i in range(e)]
+
+
+@pytest.mark.parametrize("e,m,n,k,mode", [(16, 128, 768, 2048, "random"), (8, 48, 256, 768, "one"),
+                                          (64, 40, 256, 512, "distinct"), (4, 5, 128, 256, "random")])
+def test_grouped_gemm_moe_shapes(e, m, n, k, mode):
+    """One routed grouped GEMM (nvfp4_linear_gather -> ada_nvfp4_linear_grouped) against the
+    oracle per row: MoE-like routing (16 tokens x top-8 over 16 experts), every row on one
+    expert, every row on its own expert, and a ragged small case."""
+    d = dev()
+    ws = _experts(e, n, k, 50)
+    g = torch.Generator().manual_seed(e + m)
+    if mode == "random":
+        ids = torch.randint(0, e, (m,), generator=g)
+    elif mode == "one":
+        ids = torch.full((m,), 3)
+    else:
+        ids = torch.randperm(e, generator=g)[:m]
+    x = torch.randn((m, k), generator=g).to(torch.bfloat16).to(d)
+    wp = torch.stack([torch.from_numpy(w[0]) for w in ws]).to(d)
+    sc = torch.stack([torch.from_numpy(w[2]) for w in ws]).to(d)
+    s2 = torch.tensor([w[3] for w in ws], dtype=torch.float32, device=d)
+    y = nvfp4_linear_gather(x, wp, sc, s2, ids.to(d), 16)
+    torch.cuda.synchronize()
+    xr = x.float().cpu().numpy()
+    ref = np.zeros((m, n), np.float32)
+    for ex in ids.unique().tolist():
+        rows = (ids == ex).nonzero().flatten().numpy()
+        w = ws[ex]
+        ref[rows] = nv.linear_ref(xr[rows], w[0], w[2].astype(np.float32), w[3])
+    assert rel_l2(y.float().cpu(), torch.from_numpy(ref)) < 1e-2
+
+
+def test_grouped_gemm_in_cuda_graph():
+    """The grouped path has no host synchronisation: captured once, replayed with new routing."""
+    d = dev()
+    e, m, n, k = 8, 32, 256, 512
+    ws = _experts(e, n, k, 90)
+    wp = torch.stack([torch.from_numpy(w[0]) for w in ws]).to(d)
+    sc = torch.stack([torch.from_numpy(w[2]) for w in ws]).to(d)
+    s2 = torch.tensor([w[3] for w in ws], dtype=torch.float32, device=d)
+    x = torch.randn((m, k), device=d, dtype=torch.bfloat16)
+    ids = torch.zeros(m, dtype=torch.int32, device=d)
+    nvfp4_linear_gather(x, wp, sc, s2, ids, 16)  # warm-up: scale prepack, kernel attributes
+    torch.cuda.synchronize()
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph):
+        y = nvfp4_linear_gather(x, wp, sc, s2, ids, 16)
+    for seed in range(2):
+        new = torch.randint(0, e, (m,), generator=torch.Generator().manual_seed(seed), dtype=torch.int32)
+        ids.copy_(new.to(d))
+        gph.replay()
+        torch.cuda.synchronize()
+        xr = x.float().cpu().numpy()
+        for r in (0, 7, m - 1):
+            w = ws[int(new[r])]
+            ref = nv.linear_ref(xr[r:r + 1], w[0], w[2].astype(np.float32), w[3])
+            assert rel_l2(y[r:r + 1].float().cpu(), ref) < 1e-2
+
+
 def test_workspace_reports_no_timeout():
     d = dev()
     m, n, k = 16, 1024, 1024
