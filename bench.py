@@ -254,7 +254,33 @@ def kernel_benches(dev, peak):
     us = steady([att(pl) for pl in pools] * 2)
     out["attention_config1"] = line(us, nb, {"mode": "steady", "cold_us": round(us_cold, 2), "launches": 2,
                                              "sum_ctx": sctx})
-    del pools, flush
+    del pools
+
+    # config 4 shape (Qwen3-30B-A3B MoE): the experts' gate+up projection [128][1536][2048] for 16
+    # tokens routed top-8 (128 rows) -- the grouped GEMM (routing + gathering quantiser + one GEMM);
+    # algorithmic bytes: the touched experts' weights and scales + x + y + ids
+    from adallm_b200.nvfp4_gemm import nvfp4_linear_gather
+    E, hid, n_e, tokens, topk = 128, 2048, 1536, 16, 8
+    mm = tokens * topk
+    ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(tokens)]).flatten().to(torch.int32)
+    touched = int(ids.unique().numel())
+    ids = ids.to(dev)
+    sets = []
+    for i in range(2):  # 2 x 226 MB of expert weights > L2
+        packed, scale, s2 = random_nvfp4(E * n_e, hid, 777 + i, dev)
+        sets.append((packed.view(E, n_e, hid // 2), scale.view(E, n_e, hid // 16),
+                     torch.full((E,), s2, dtype=torch.float32, device=dev)))
+    xm = torch.randn((mm, hid), device=dev, dtype=torch.bfloat16)
+
+    def moe(sv):
+        return lambda: nvfp4_linear_gather(xm, sv[0], sv[1], sv[2], ids, 16, terms=4)
+
+    nb = touched * (n_e * hid // 2 + n_e * hid // 16) + mm * hid * 2 + mm * n_e * 2 + 4 * mm
+    us_cold = timed(moe(sets[0]))
+    us = steady([moe(sv) for sv in sets] * 2)
+    out["moe_grouped_config4"] = line(us, nb, {"mode": "steady", "cold_us": round(us_cold, 2), "launches": 3,
+                                               "rows": mm, "experts_touched": touched})
+    del sets, flush
     torch.cuda.empty_cache()
     return out
 
