@@ -1,0 +1,150 @@
+// Mixture-of-experts routing around the grouped NVFP4 GEMM (sm_100a), restating
+// Qwen3MoeSparseMoeBlock.forward (adallm/architectures/qwen3.py:1026-1032 and the weighted sum of
+// the expert outputs that follows):
+//   route:   w = softmax(router_logits) in fp32; (w, ids) = top-k of w; w /= sum(w) when
+//            norm_topk_prob; w cast to the activation dtype.  One warp per token; the top-k is
+//            k rounds of a warp argmax (ties: the lower expert index first).
+//   combine: out[t] = sum_j w[t, j] * y[t * k + j] over the token's k expert rows, fp32 in
+//            expert-slot order, rounded once to the activation dtype.
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace ada {
+namespace moe {
+
+constexpr int MAX_EXPERTS = 1024;  // 32 per lane
+constexpr int MAX_TOPK = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(128) route_kernel(const T* __restrict__ logits, int64_t ld, int tokens, int experts,
+                                                    int topk, int norm, int32_t* __restrict__ ids,
+                                                    T* __restrict__ weights) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= tokens) return;
+  constexpr int PER = MAX_EXPERTS / 32;
+  float p[PER];
+  float mx = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = i * 32 + lane;
+    p[i] = e < experts ? to_f32(logits[(int64_t)t * ld + e]) : -FLT_MAX;
+    mx = fmaxf(mx, p[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = i * 32 + lane;
+    p[i] = e < experts ? expf(p[i] - mx) : 0.f;
+    sum += p[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  float sel_w[MAX_TOPK];
+  int sel_e[MAX_TOPK];
+  float wsum = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    float best = -1.f;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = i * 32 + lane;
+      if (e < experts && (p[i] > best || (p[i] == best && e < be))) {
+        best = p[i];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ob > best || (ob == best && oe < be)) {
+        best = ob;
+        be = oe;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (i * 32 + lane == be) p[i] = -2.f;  // taken
+    sel_w[j] = best / sum;
+    sel_e[j] = be;
+    wsum += sel_w[j];
+  }
+  if (lane == 0)
+    for (int j = 0; j < topk; ++j) {
+      ids[(int64_t)t * topk + j] = sel_e[j];
+      weights[(int64_t)t * topk + j] = from_f32<T>(norm ? sel_w[j] / wsum : sel_w[j]);
+    }
+}
+
+// One CTA per token, 8 hidden elements per thread and step.
+template <typename T>
+__global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, int64_t ldy, const T* __restrict__ w,
+                                                      int topk, int hidden, T* __restrict__ out, int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < topk; ++j) {
+      const float wj = to_f32(w[(int64_t)t * topk + j]);
+      float v[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(y + ((int64_t)t * topk + j) * ldy + c), v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(wj, v[i], acc[i]);
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)t * ldo + c) = pack8<T>(acc);
+  }
+}
+
+}  // namespace moe
+}  // namespace ada
+
+using namespace ada;
+
+extern "C" int ada_moe_route_topk(const void* logits, int dtype, int64_t ld, int64_t tokens, int32_t experts,
+                                  int32_t topk, int32_t norm_topk_prob, int32_t* ids, void* weights, void* stream) {
+  if (tokens < 0 || experts <= 0 || topk <= 0 || ld < experts) return ADA_ERR_INVALID_ARG;
+  if (tokens == 0) return ADA_OK;
+  if (!logits || !ids || !weights) return ADA_ERR_INVALID_ARG;
+  if (experts > moe::MAX_EXPERTS || topk > moe::MAX_TOPK || topk > experts) return ADA_ERR_UNSUPPORTED;
+  if (tokens > (int64_t)65535 * 4) return ADA_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)cdiv(tokens, 4));
+  if (dtype == ADA_DT_BF16)
+    (void)launch_k(moe::route_kernel<__nv_bfloat16>, grid, dim3(128), 0, st, (const __nv_bfloat16*)logits, ld,
+                   (int)tokens, (int)experts, (int)topk, (int)norm_topk_prob, ids, (__nv_bfloat16*)weights);
+  else if (dtype == ADA_DT_F16)
+    (void)launch_k(moe::route_kernel<__half>, grid, dim3(128), 0, st, (const __half*)logits, ld, (int)tokens,
+                   (int)experts, (int)topk, (int)norm_topk_prob, ids, (__half*)weights);
+  else
+    return ADA_ERR_INVALID_ARG;
+  ADA_CHECK_LAUNCH();
+  return ADA_OK;
+}
+
+extern "C" int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void* weights, int64_t tokens,
+                               int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream) {
+  if (tokens < 0 || topk <= 0 || hidden <= 0 || ldy < hidden || ldo < hidden) return ADA_ERR_INVALID_ARG;
+  if (tokens == 0) return ADA_OK;
+  if (!y || !weights || !out) return ADA_ERR_INVALID_ARG;
+  if (hidden % 8 || tokens > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
+  if (((uintptr_t)y & 15) || ((uintptr_t)out & 15) || (ldy & 7) || (ldo & 7)) return ADA_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == ADA_DT_BF16)
+    (void)launch_k(moe::combine_kernel<__nv_bfloat16>, dim3((unsigned)tokens), dim3(256), 0, st,
+                   (const __nv_bfloat16*)y, ldy, (const __nv_bfloat16*)weights, (int)topk, (int)hidden,
+                   (__nv_bfloat16*)out, ldo);
+  else if (dtype == ADA_DT_F16)
+    (void)launch_k(moe::combine_kernel<__half>, dim3((unsigned)tokens), dim3(256), 0, st, (const __half*)y, ldy,
+                   (const __half*)weights, (int)topk, (int)hidden, (__half*)out, ldo);
+  else
+    return ADA_ERR_INVALID_ARG;
+  ADA_CHECK_LAUNCH();
+  return ADA_OK;
+}

@@ -267,6 +267,16 @@ ADA_API int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx, in
                                      const float* w_scale_2, int32_t num_experts, int64_t n,
                                      const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy, int terms,
                                      void* workspace, size_t workspace_bytes, void* stream);
+/* MoE routing and combine around ada_nvfp4_linear_grouped (Qwen3MoeSparseMoeBlock.forward,
+ * adallm/architectures/qwen3.py:1026-1032): ada_moe_route_topk takes router logits [tokens, experts]
+ * (row stride ld; experts <= 1024, topk <= 32) to fp32 softmax, top-k (descending; ties: lower expert
+ * first) and, when norm_topk_prob, weights renormalised to sum 1; writes ids int32 [tokens * topk] and
+ * weights [tokens * topk] in dtype.  ada_moe_combine: out[t] = sum_j weights[t*topk+j] * y[t*topk+j]
+ * (fp32, slot order; hidden % 8 == 0). */
+ADA_API int ada_moe_route_topk(const void* logits, int dtype, int64_t ld, int64_t tokens, int32_t experts,
+                               int32_t topk, int32_t norm_topk_prob, int32_t* ids, void* weights, void* stream);
+ADA_API int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void* weights, int64_t tokens,
+                            int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream);
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by

@@ -1,0 +1,71 @@
+"""MoE routing and combine kernels against the reference's torch ops
+(Qwen3MoeSparseMoeBlock.forward, adallm/architectures/qwen3.py:1026-1032), and one MoE expert
+projection end to end: route -> grouped NVFP4 GEMM -> weighted combine, against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nvfp4 as nv
+from adallm_b200.moe import route_topk, combine
+from adallm_b200.nvfp4_gemm import nvfp4_linear_gather
+from tests.gpu_util import dev, rel_l2
+from tests.test_gpu_nvfp4 import random_weight
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch_route(logits, k, norm):
+    w = torch.softmax(logits.float(), dim=1, dtype=torch.float32)
+    w, ids = torch.topk(w, k, dim=-1)
+    if norm:
+        w = w / w.sum(dim=-1, keepdim=True)
+    return ids, w.to(logits.dtype)
+
+
+@pytest.mark.parametrize("t,e,k,norm", [(16, 128, 8, True), (5, 64, 4, False), (33, 1024, 2, True), (1, 8, 8, True)])
+def test_route_topk_matches_torch(t, e, k, norm):
+    d = dev()
+    g = torch.Generator().manual_seed(t + e)
+    # distinct logits (multiples of 1/256, exact in fp16), so the top-k has no ties to order
+    logits = torch.stack([(torch.randperm(e, generator=g) - e // 2).float() / 256 for _ in range(t)])
+    logits = logits.to(torch.float16).to(d)
+    ids, w = route_topk(logits, k, norm)
+    rid, rw = _torch_route(logits, k, norm)
+    torch.cuda.synchronize()
+    assert torch.equal(ids.long(), rid)
+    assert torch.allclose(w.float(), rw.float(), rtol=2 ** -7, atol=1e-6)
+
+
+def test_combine_weighted_sum():
+    d = dev()
+    t, k, h = 7, 8, 2048
+    y = torch.randn((t * k, h), device=d, dtype=torch.bfloat16)
+    w = torch.rand((t, k), device=d, dtype=torch.bfloat16)
+    out = combine(y, w, k)
+    ref = (y.float().view(t, k, h) * w.float().unsqueeze(-1)).sum(1)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 4e-3
+
+
+def test_moe_projection_end_to_end():
+    d = dev()
+    t, e, k, hid, n = 16, 32, 4, 512, 256
+    ws = [random_weight(n, hid, seed=300 + i, realistic=False) for i in range(e)]
+    wp = torch.stack([torch.from_numpy(w[0]) for w in ws]).to(d)
+    sc = torch.stack([torch.from_numpy(w[2]) for w in ws]).to(d)
+    s2 = torch.tensor([w[3] for w in ws], dtype=torch.float32, device=d)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((t, hid), generator=g).to(torch.bfloat16).to(d)
+    logits = torch.randn((t, e), generator=g).to(torch.bfloat16).to(d)
+    ids, w = route_topk(logits, k, True)
+    h = nvfp4_linear_gather(x.repeat_interleave(k, 0), wp, sc, s2, ids.reshape(-1), 16)
+    out = combine(h, w, k)
+    torch.cuda.synchronize()
+    xr = x.float().cpu().numpy()
+    idn, wn = ids.cpu().numpy(), w.float().cpu().numpy()
+    ref = np.zeros((t, n), np.float32)
+    for i in range(t):
+        for j in range(k):
+            wt = ws[idn[i, j]]
+            ref[i] += wn[i, j] * nv.linear_ref(xr[i:i + 1], wt[0], wt[2].astype(np.float32), wt[3])[0]
+    assert rel_l2(out.float().cpu(), torch.from_numpy(ref)) < 1e-2
