@@ -89,11 +89,13 @@ struct Exchange {
   float slots[MAX_CLUSTER];
   unsigned long long bar;
 };
-__device__ __forceinline__ void exchange_init(Exchange* x) {
-  const uint32_t a = (uint32_t)__cvta_generic_to_shared(&x->bar);
+// One arrival (made here) plus `bytes` of transactions complete the barrier's first phase.
+__device__ __forceinline__ void exchange_init_bytes(unsigned long long* bar, uint32_t bytes) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
   asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(a) : "memory");
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(nctarank() * 4u) : "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void exchange_init(Exchange* x) { exchange_init_bytes(&x->bar, nctarank() * 4u); }
 __device__ __forceinline__ void fence_exchange_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -102,9 +104,18 @@ __device__ __forceinline__ void st_async_f32(uint32_t cluster_addr, float v, uin
                "r"(cluster_bar)
                : "memory");
 }
-// Bounded wait (about 2 s) for phase 0 of the exchange's barrier; false when it gave up.
-__device__ __forceinline__ bool exchange_wait(Exchange* x) {
-  const uint32_t a = (uint32_t)__cvta_generic_to_shared(&x->bar);
+// 16 bytes into another CTA's shared memory, completing 16 bytes of transaction on its barrier
+// (both addresses 16-byte aligned).
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float a, float b, float c, float d,
+                                            uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   cluster_addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
+               : "memory");
+}
+// Bounded wait (about 2 s) for phase 0 of an exchange barrier; false when it gave up.
+__device__ __forceinline__ bool exchange_wait(unsigned long long* bar) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
   uint64_t t0 = 0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   for (uint32_t it = 0;; ++it) {
@@ -143,7 +154,7 @@ __device__ __forceinline__ float cluster_allreduce_x(float v, float* red, Exchan
   const uint32_t n = nctarank();
   if (n == 1) return v;
   if (threadIdx.x < n) st_async_f32(mapa(&x->slots[ctarank()], threadIdx.x), v, mapa(&x->bar, threadIdx.x));
-  exchange_wait(x);
+  exchange_wait(&x->bar);
   float r = x->slots[0];
   for (uint32_t i = 1; i < n; ++i) r = Op::apply(r, x->slots[i]);
   return r;

@@ -129,6 +129,8 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
   uint64_t* accf = empty + MAX_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  // cluster split-K: counts the bytes of this CTA's rows arriving from the cluster (st.async)
+  unsigned long long* rbar = reinterpret_cast<unsigned long long*>(ctrl + 144);
   float* gsc = reinterpret_cast<float*>(ctrl + 256);  // [T][BN] gw * term scale per token
   volatile int* abort_v = abort_flag;
 
@@ -146,7 +148,14 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
   const int nunits = kt1 - kt0;
   const int kb64 = p.K / 64;
 
-  if (cluster) cl::cluster_arrive_relaxed();
+  if (cluster) {
+    if (threadIdx.x == 0) {  // before the cluster's start barrier: peers send into it after theirs
+      const int own = owner_begin(rank + 1, ks) - owner_begin(rank, ks);
+      cl::exchange_init_bytes(rbar, (uint32_t)(ks * own * BN * 4));
+      cl::fence_exchange_init();
+    }
+    cl::cluster_arrive_relaxed();
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -310,9 +319,10 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
       const int rl = r - owner_begin(owner, ks);
       cl::cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
       const uint32_t dst = cl::mapa(recv + ((size_t)rank * p.rows_max + rl) * BN, (uint32_t)owner);
+      const uint32_t obar = cl::mapa(rbar, (uint32_t)owner);
 #pragma unroll
-      for (int j = 0; j < BN; j += 4) cl::st_cluster_v4(dst + j * 4, out[j], out[j + 1], out[j + 2], out[j + 3]);
-      cl::cluster_sync();  // all partial rows delivered
+      for (int j = 0; j < BN; j += 4) cl::st_async_v4(dst + j * 4, out[j], out[j + 1], out[j + 2], out[j + 3], obar);
+      cl::exchange_wait(rbar);  // every partial row this CTA owns has arrived (one-way stores)
       const int r0 = owner_begin(rank, ks), rows = owner_begin(rank + 1, ks) - r0;
       for (int e = et; e < rows * BN; e += 128) {
         const int rr = e % rows, j = e / rows;
@@ -323,10 +333,7 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
       }
     }
   }
-  if (cluster && warp < 2) {  // the producer and MMA warps take part in both cluster barriers
-    cl::cluster_wait();
-    cl::cluster_sync();
-  }
+  if (cluster && warp < 2) cl::cluster_wait();  // the producer and MMA warps complete the start barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, p.tmem_cols);
@@ -467,15 +474,17 @@ __global__ void __launch_bounds__(192, 2) occupancy_twin() {}
 // Clusters of `ks` CTAs (with the shared memory the plan gives them) that fit on the GPU at
 // once; 0 if unknown.  A split whose clusters do not all fit runs in two waves.
 template <int BN, int T>
-static int active_clusters(int ks) {
-  static int cache[64][MAX_KS + 1] = {};
+static int active_clusters(int ks, int per_sm = 2) {
+  static int cache[64][2][MAX_KS + 1] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || ks < 1 || ks > MAX_KS) return 0;
-  if (cache[dev][ks]) return cache[dev][ks] > 0 ? cache[dev][ks] : 0;
+  int& slot = cache[dev][per_sm == 3 ? 1 : 0][ks];
+  if (slot) return slot > 0 ? slot : 0;
   int stages = 0;
   uint32_t cols = 0;
   size_t smem = 0;
-  stages_for<BN, T>(ks, (int)cdiv(BM, ks), MAX_STAGES, stages, cols, smem);  // deepest pipeline: a lower bound
+  // deepest pipeline of the budget: a lower bound of the capacity
+  stages_for<BN, T>(ks, (int)cdiv(BM, ks), MAX_STAGES, stages, cols, smem, per_sm);
   int n = 0;
   if (stages >= 2 &&
       cudaFuncSetAttribute(occupancy_twin, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
@@ -495,12 +504,12 @@ static int active_clusters(int ks) {
     if (cudaOccupancyMaxActiveClusters(&n, occupancy_twin, &cfg) != cudaSuccess) n = 0;
   }
   (void)cudaGetLastError();
-  cache[dev][ks] = n > 0 ? n : -1;
+  slot = n > 0 ? n : -1;
   return n;
 }
 
-static int active_clusters_dispatch(int bn, int t, int ks) {
-#define ADA_AC(B, TT) if (bn == B && t == TT) return active_clusters<B, TT>(ks);
+static int active_clusters_dispatch(int bn, int t, int ks, int per_sm = 2) {
+#define ADA_AC(B, TT) if (bn == B && t == TT) return active_clusters<B, TT>(ks, per_sm);
   ADA_FP4_CONFIGS(ADA_AC)
 #undef ADA_AC
   return 0;
@@ -517,12 +526,13 @@ static int num_sms() {
   return cache[dev];
 }
 
-// A partial-plane plan of ks splits whose pipeline fits three CTAs to an SM.
-static bool fits_three(int bn, int terms, int64_t ks, int nkt) {
+// A plan of ks splits whose pipeline (with the cluster reduction buffer when `cluster`) fits
+// three CTAs to an SM.
+static bool fits_three(int bn, int terms, int64_t ks, int nkt, bool cluster = false) {
   int st = 0;
   uint32_t c = 0;
   size_t sm = 0;
-  stages_dispatch(bn, terms, 1, (int)cdiv(BM, ks), (int)cdiv(nkt, ks), st, c, sm, 3);
+  stages_dispatch(bn, terms, cluster ? (int)ks : 1, (int)cdiv(BM, ks), (int)cdiv(nkt, ks), st, c, sm, 3);
   return st >= 2;
 }
 
@@ -560,17 +570,27 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
       ks = ks < 1 ? 1 : ks > ks_cap ? ks_cap : ks;
     }
   } else {
+    // two CTAs per SM, or three (74 KB pipeline) when that lets a larger split stay in one wave
     for (int64_t c = (P.nkt / 4 < ks_cap ? P.nkt / 4 : ks_cap); c >= 2; --c) {
-      if (P.nkt % c || tiles * c > 2 * (int64_t)num_sms()) continue;
-      if (tiles <= active_clusters_dispatch(P.bn, terms, (int)c)) {
+      if (P.nkt % c) continue;
+      if (tiles * c <= 2 * (int64_t)num_sms() && tiles <= active_clusters_dispatch(P.bn, terms, (int)c)) {
         ks = c;
+        break;
+      }
+      if (tiles * c <= 3 * (int64_t)num_sms() && fits_three(P.bn, terms, c, P.nkt, true) &&
+          tiles <= active_clusters_dispatch(P.bn, terms, (int)c, 3)) {
+        ks = c;
+        three_per_sm = true;
         break;
       }
     }
   }
   P.ks = (int)ks;
   P.rows_max = (int)cdiv(BM, ks);
-  three_per_sm = parts && tiles * ks > 2 * (int64_t)num_sms() && fits_three(P.bn, terms, ks, P.nkt);
+  // three CTAs to an SM whenever the grid outgrows two per SM and no cluster reduction buffer is
+  // needed: partial planes, or a single split (the grouped MoE GEMM)
+  if (!three_per_sm)
+    three_per_sm = (parts || ks == 1) && tiles * ks > 2 * (int64_t)num_sms() && fits_three(P.bn, terms, ks, P.nkt);
   uint32_t cols = 0;
   stages_dispatch(P.bn, terms, parts ? 1 : P.ks, P.rows_max, (int)cdiv(P.nkt, ks), P.stages, cols, P.smem,
                   three_per_sm ? 3 : 2);
