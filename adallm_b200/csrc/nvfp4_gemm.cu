@@ -339,6 +339,184 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
   if (warp == 1) tmem_dealloc(tmem, p.tmem_cols);
 }
 
+// ---- persistent form for large dense problems (prefill) ------------------------------
+// One CTA per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m-tile major, so neighbouring
+// CTAs share the activation tile).  The pipeline ring runs on across tiles, and two TMEM
+// accumulators alternate: the epilogue drains tile i from one while the MMA warp fills tile i + 1
+// into the other.  Dense, one K split, no partial planes (the planner picks it for those grids).
+// TMEM columns: [acc 0: NB][acc 1: NB][stage scale factors][unit scales].
+template <int BN, int T>
+__global__ void __launch_bounds__(192, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                           const GemmParams p) {
+  using C = Cfg<BN, T>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = p.stages;
+  uint8_t* const_sf = smem + (size_t)stages * C::STAGE;
+  uint8_t* ctrl = const_sf + C::CONST_SF;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
+  uint64_t* empty = full + MAX_STAGES;
+  uint64_t* accf = empty + MAX_STAGES;  // [2] accumulator b complete
+  uint64_t* acce = accf + 2;            // [2] accumulator b drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* gsc = reinterpret_cast<float*>(ctrl + 256);  // [T][BN]
+  volatile int* abort_v = abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = p.n_tiles * ((p.M + BN - 1) / BN);
+  const int kb64 = p.K / 64;
+  const int nkt = p.nkt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (!C::BLOCK_SF && threadIdx.x < C::CONST_SF / 4) {
+    reinterpret_cast<uint32_t*>(const_sf)[threadIdx.x] = UNIT_SCALE4;
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmw);
+    prefetch_tmap(&tmx);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- producer ----------------
+      pdl_wait();
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_v; t += gridDim.x) {
+        const int n_tile = t % p.n_tiles, m_tile = t / p.n_tiles;
+        for (int kt = 0; kt < nkt; ++kt, ++it) {
+          const int s = (int)(it % (uint32_t)stages);
+          if (it >= (uint32_t)stages &&
+              !mbar_wait_bounded(&empty[s], ((it / stages) & 1) ^ 1, abort_v, p.err, 1u))
+            break;
+          uint8_t* st = smem + (size_t)s * C::STAGE;
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, n_tile * BM);
+          tma_load_2d(st + C::A_BYTES, &tmx, &full[s], kt * KT_BYTES, m_tile * C::NB);
+          bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
+                    C::SFA_BYTES, &full[s]);
+          if (C::BLOCK_SF)
+            bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
+                      p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES, &full[s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_mxf4nvf4(C::NB);
+      const uint32_t sf_base = tmem + 2 * C::NB;
+      const uint32_t sfb_unit = sf_base + stages * C::SF_COLS;
+      if (!C::BLOCK_SF) tmem_cp_32x128b_x4(sfb_unit, desc_sf(smem_u32(const_sf)));
+      uint32_t it = 0, lt = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_v; t += gridDim.x, ++lt) {
+        const uint32_t b = lt & 1, use = lt >> 1;
+        if (use > 0 && !mbar_wait_bounded(&acce[b], (use - 1) & 1, abort_v, p.err, 8u)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * C::NB;
+        bool failed = false;
+        for (int kt = 0; kt < nkt; ++kt, ++it) {
+          const int s = (int)(it % (uint32_t)stages);
+          if (!mbar_wait_bounded(&full[s], (it / stages) & 1, abort_v, p.err, 2u)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* st = smem + (size_t)s * C::STAGE;
+          const uint32_t a_addr = smem_u32(st);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+          const uint32_t sfa_addr = b_addr + C::B_BYTES;
+          const uint32_t sf_col = sf_base + s * C::SF_COLS;
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            tmem_cp_32x128b_x4(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
+            if (C::BLOCK_SF) tmem_cp_32x128b_x4(sf_col + 16 + 4 * kb, desc_sf(sfa_addr + C::SFA_BYTES + kb * SF_BLOCK));
+          }
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb)
+            mma_mxf4nvf4(acc, desc_kmajor_sw128(a_addr + kb * 32), desc_kmajor_sw128(b_addr + kb * 32), idesc,
+                         (kt | kb) != 0, sf_col + 4 * kb, C::BLOCK_SF ? sf_col + 16 + 4 * kb : sfb_unit);
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&accf[b]);  // also after a failure: drains the issued MMAs
+        if (failed) break;
+      }
+    }
+    __syncwarp();
+  } else {  // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();
+    pdl_trigger();
+    const int q = warp & 3;
+    const int et = threadIdx.x - 64;
+    const int r = q * 32 + lane;
+    const float gw = __ldg(p.gw);
+    uint32_t lt = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      const int n_tile = t % p.n_tiles, m_tile = t / p.n_tiles;
+      const uint32_t b = lt & 1, use = lt >> 1;
+      if (et < BN) {
+        float g = p.gx[m_tile * BN + et];
+#pragma unroll
+        for (int tt = 0; tt < T; ++tt) {
+          gsc[tt * BN + et] = __fmul_rn(gw, g);
+          g = q::next_term_scale(g);
+        }
+      }
+      epi_bar();
+      const bool ok = mbar_wait_bounded(&accf[b], use & 1, abort_v, p.err, 4u) && !*abort_v;
+      tc_fence_after();
+      __syncwarp();
+      const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + b * C::NB;
+      const int n = n_tile * BM + r;
+      const float bias = load_bias(p.bias, p.out_dtype, n);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {  // 16 tokens at a time, terms summed in order
+        float o[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) o[k] = 0.f;
+#pragma unroll
+        for (int tt = 0; tt < T; ++tt) {
+          float v[16];
+          tmem_ld16(lane_addr + tt * BN + c, v);
+#pragma unroll
+          for (int k = 0; k < 16; ++k) o[k] = fmaf(v[k], gsc[tt * BN + c + k], o[k]);
+        }
+        if (ok) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int m = m_tile * BN + c + k;
+            if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, o[k] + bias);
+          }
+        }
+      }
+      tc_fence_before();
+      epi_bar();  // every lane has read accumulator b (and gsc may be rewritten)
+      if (et == 0) mbar_arrive_plain(&acce[b]);
+      if (!ok) break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, p.tmem_cols);
+}
+
 // Scale prepack: [N, K/16] (fp16 holding e4m3 values, or raw e4m3 bytes) ->
 // [N/128][K/64][512] bytes in the MMA scale-factor layout.
 __global__ void __launch_bounds__(128) prepack_kernel(const void* __restrict__ scale, int is_fp16, int64_t ld, int N,
@@ -391,6 +569,10 @@ constexpr size_t ERR_BYTES = 256;  // error word at offset 0 of every GEMM works
 struct Plan {
   int terms, bn, m_tiles, m_pad, n_tiles, nkt, ks, rows_max, stages, tmem_cols;
   size_t smem;
+  // persistent form (dense, one split, more tiles than two per SM): pipeline and TMEM of it
+  bool persistent;
+  int p_stages, p_cols;
+  size_t p_smem;
   // workspace of ada_nvfp4_linear (bytes, 256-aligned): [err][xq][sfx][gx]
   size_t off_xq, off_sfx, off_gx, total;
 };
@@ -431,6 +613,20 @@ static void stages_for(int ks, int rows_max, int max_units, int& stages, uint32_
   stages = s;
   cols = s ? pow2_cols(C::tmem_need(s)) : 0;
   smem = C::smem_bytes(s, recv);
+}
+
+// Persistent form: one CTA per SM, two accumulators; the deepest pipeline that fits.
+template <int BN, int T>
+static void persistent_stages_for(int& stages, uint32_t& cols, size_t& smem) {
+  using C = Cfg<BN, T>;
+  int s = 0;
+  for (int k = MAX_STAGES; k >= 2; --k) {
+    const size_t sm = 1024 + (size_t)k * C::STAGE + C::CONST_SF + C::CTRL;
+    if (sm <= 226 * 1024 && 2 * C::NB + k * C::SF_COLS + (C::BLOCK_SF ? 0 : 4) <= 512) { s = k; break; }
+  }
+  stages = s;
+  cols = s ? pow2_cols(2 * C::NB + s * C::SF_COLS + (C::BLOCK_SF ? 0 : 4)) : 0;
+  smem = 1024 + (size_t)s * C::STAGE + C::CONST_SF + C::CTRL;
 }
 
 #define ADA_FP4_CONFIGS(X) \
@@ -596,6 +792,16 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
                   three_per_sm ? 3 : 2);
   if (P.stages < 2) return ADA_ERR_UNSUPPORTED;
   P.tmem_cols = (int)cols;
+  P.persistent = false;
+  P.p_stages = 0;
+  if (!parts && ks == 1 && tiles > 2 * (int64_t)num_sms()) {
+    uint32_t pc = 0;
+#define ADA_PS(B, TT) if (P.bn == B && terms == TT) persistent_stages_for<B, TT>(P.p_stages, pc, P.p_smem);
+    ADA_FP4_CONFIGS(ADA_PS)
+#undef ADA_PS
+    P.p_cols = (int)pc;
+    P.persistent = P.p_stages >= 2;
+  }
   size_t off = ERR_BYTES;
   P.off_xq = off;
   off = al256(off + (size_t)terms * P.m_pad * (size_t)(k / 2));
@@ -610,6 +816,25 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
 template <int BN, int T>
 static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmParams& gp, const Plan& P,
                        cudaStream_t st) {
+  if (P.persistent && !gp.part && !gp.tile_expert) {  // prefill-size dense GEMM
+    static size_t configured[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
+    if (P.p_smem > configured[dev]) {
+      if (cudaFuncSetAttribute(gemm_persistent_kernel<BN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)P.p_smem) != cudaSuccess)
+        return ADA_ERR_CUDA;
+      configured[dev] = P.p_smem;
+    }
+    GemmParams pp = gp;
+    pp.stages = P.p_stages;
+    pp.tmem_cols = P.p_cols;
+    const int64_t tiles = (int64_t)P.n_tiles * P.m_tiles;
+    const unsigned grid = (unsigned)(tiles < num_sms() ? tiles : num_sms());
+    (void)ada::launch_k(gemm_persistent_kernel<BN, T>, dim3(grid), dim3(192), P.p_smem, st, tmw, tmx, pp);
+    ADA_CHECK_LAUNCH();
+    return ADA_OK;
+  }
   auto kern = gemm_kernel<BN, T>;
   if (!ensure_smem<BN, T>(P.smem)) return ADA_ERR_CUDA;
   const dim3 grid((unsigned)P.ks, (unsigned)(P.n_tiles * P.m_tiles));

@@ -62,6 +62,14 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def measured_bf16():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return None
+
+
 def traffic_from_profile():
     """dram bytes per launch of the GEMM kernel from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "nvfp4_gemm_decode_bs16.md")
@@ -280,7 +288,25 @@ def kernel_benches(dev, peak):
     us = steady([moe(sv) for sv in sets] * 2)
     out["moe_grouped_config4"] = line(us, nb, {"mode": "steady", "cold_us": round(us_cold, 2), "launches": 3,
                                                "rows": mm, "experts_touched": touched})
-    del sets, flush
+    del sets, xm
+
+    # prefill-size GEMM (tensor-core bound): M 8192 tokens x gate_up N 24576 K 4096, W4A4 operand
+    # (terms 1); FLOPs 2MNK against spec dense FP4 (9 PFLOP/s) and 4x the measured bf16 burst
+    mp, npf, kpf = 8192, 24576, 4096
+    packed, scale, s2 = random_nvfp4(npf, kpf, 4711, dev)
+    sfp, s2t = prepack_scales(scale, npf, kpf), torch.tensor(s2, dtype=torch.float32, device=dev)
+    xp = torch.randn((mp, kpf), device=dev, dtype=torch.bfloat16)
+    yp = torch.empty((mp, npf), device=dev, dtype=torch.bfloat16)
+    wsp = torch.zeros(workspace_bytes(mp, npf, kpf, 1), dtype=torch.uint8, device=dev)
+    pf = lambda: nvfp4_linear(xp, packed, scale, s2t, None, None, 16, terms=1, sf=sfp, out=yp, workspace=wsp)
+    us = steady([pf] * 4, reps=3)
+    tf = 2 * mp * npf * kpf / us / 1e6
+    bf16_burst = measured_bf16()
+    out["gemm_prefill_w4a4"] = {"us": round(us, 1), "tflops": round(tf, 1), "m": mp, "n": npf, "k": kpf, "terms": 1,
+                                "frac_fp4_spec": round(tf / 9000.0, 4),
+                                "frac_4x_bf16_measured": round(tf / (4 * bf16_burst), 4) if bf16_burst else None,
+                                "mode": "steady", "launches": 2}
+    del xp, yp, wsp, packed, scale, flush
     torch.cuda.empty_cache()
     return out
 

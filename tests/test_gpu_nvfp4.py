@@ -120,6 +120,24 @@ def test_split_k_is_deterministic_and_exact(ksplit, terms):
     assert rel_l2(y1, y_one) < 3e-3
 
 
+@pytest.mark.parametrize("terms,tol", [(1, 0.15), (4, 1e-2)])
+def test_prefill_size(terms, tol):
+    """Prefill-size GEMM (M 2048 tokens, the qkv projection N 6144 K 4096; the persistent
+    two-accumulator kernel): W4A4 (terms 1, the tensor-core rate mode, whose 1-term activations
+    deviate ~0.1 from the reference) and the default 4-term operand, against dequantise-then-matmul
+    in fp32."""
+    d = dev()
+    m, n, k = 2048, 6144, 4096
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=8, realistic=False)
+    x = torch.randn((m, k), generator=torch.Generator().manual_seed(8)).to(torch.bfloat16).to(d)
+    y = nvfp4_linear(x, torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d), torch.tensor(s2, device=d),
+                     None, None, 16, terms=terms)
+    w = nv.dequant_nvfp4_torch(packed, scale16.astype(np.float32), s2).to(d)
+    ref = x.float() @ w.float().t()
+    torch.cuda.synchronize()
+    assert rel_l2(y.float(), ref) < tol
+
+
 def test_config0_full_size():
     # BASELINE config 0: x bf16 [16, 4096] ~N(0,1), W [12288, 4096] NVFP4, output bf16 [16, 12288]
     m, n, k = 16, 12288, 4096
