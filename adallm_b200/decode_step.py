@@ -15,8 +15,10 @@ package's ops so it can be timed and checked on its own:
 
 Tensor parallelism follows the reference's sharding exactly: column-parallel shards
 of q / k / v and gate / up rows, row-parallel shards of the K dimension of o_proj and
-down_proj with an NCCL all-reduce after them, head-sharded KV cache, vocab-sharded
-embedding / lm_head (adallm/ops/embed_head.py:9-66).
+down_proj, head-sharded KV cache, vocab-sharded embedding / lm_head
+(adallm/ops/embed_head.py:9-66).  The reduction after the row-parallel projections (an NCCL
+all-reduce in the reference) runs over NVLink peer memory: each rank's GEMM writes its
+partials into every rank's inbox and the next RMSNorm sums them (``_gemm_rowpar``).
 
 Weights are random-init NVFP4 (random e2m1 codes, e4m3 block scales and a per-matrix
 fp32 scale_2, sized so every projection has roughly unit gain).  They are generated on
