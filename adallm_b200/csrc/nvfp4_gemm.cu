@@ -64,6 +64,7 @@ struct GemmParams {
   // operand row r is output row row_map[r] (< 0: padding, not stored).  Null: dense.
   const int* tile_expert;
   const int* row_map;
+  int m_tiles_max;  // grouped: operand tiles in the plan (the routing uses a prefix of them)
   unsigned long long* inbox[MAX_PEERS];
   const unsigned int* epoch;
   unsigned int tag_mul, tag_add;
@@ -339,11 +340,11 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
   if (warp == 1) tmem_dealloc(tmem, p.tmem_cols);
 }
 
-// ---- persistent form for large dense problems (prefill) ------------------------------
+// ---- persistent form for large problems (prefill; grouped MoE with many routed tiles) ----
 // One CTA per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m-tile major, so neighbouring
 // CTAs share the activation tile).  The pipeline ring runs on across tiles, and two TMEM
 // accumulators alternate: the epilogue drains tile i from one while the MMA warp fills tile i + 1
-// into the other.  Dense, one K split, no partial planes (the planner picks it for those grids).
+// into the other.  One K split, no partial planes (the planner picks it for those grids).
 // TMEM columns: [acc 0: NB][acc 1: NB][stage scale factors][unit scales].
 template <int BN, int T>
 __global__ void __launch_bounds__(192, 1)
@@ -365,7 +366,9 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_v = abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = p.n_tiles * ((p.M + BN - 1) / BN);
+  // grouped (MoE): the m-tiles come from the routing (written by an earlier kernel), the used
+  // ones first; a tile whose expert is < 0 and every later one are skipped by all roles alike
+  const int tiles = p.n_tiles * (p.tile_expert ? p.m_tiles_max : (p.M + BN - 1) / BN);
   const int kb64 = p.K / 64;
   const int nkt = p.nkt;
 
@@ -401,6 +404,9 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t it = 0;
       for (int t = blockIdx.x; t < tiles && !*abort_v; t += gridDim.x) {
         const int n_tile = t % p.n_tiles, m_tile = t / p.n_tiles;
+        const int expert = p.tile_expert ? p.tile_expert[m_tile] : 0;
+        if (expert < 0) break;
+        const int w_tile = expert * p.n_tiles + n_tile;
         for (int kt = 0; kt < nkt; ++kt, ++it) {
           const int s = (int)(it % (uint32_t)stages);
           if (it >= (uint32_t)stages &&
@@ -408,9 +414,9 @@ __global__ void __launch_bounds__(192, 1)
             break;
           uint8_t* st = smem + (size_t)s * C::STAGE;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
-          tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, n_tile * BM);
+          tma_load_2d(st, &tmw, &full[s], kt * KT_BYTES, w_tile * BM);
           tma_load_2d(st + C::A_BYTES, &tmx, &full[s], kt * KT_BYTES, m_tile * C::NB);
-          bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)n_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
+          bulk_load(st + C::A_BYTES + C::B_BYTES, p.sfw + ((size_t)w_tile * kb64 + (size_t)kt * 4) * SF_BLOCK,
                     C::SFA_BYTES, &full[s]);
           if (C::BLOCK_SF)
             bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
@@ -425,8 +431,10 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t sf_base = tmem + 2 * C::NB;
       const uint32_t sfb_unit = sf_base + stages * C::SF_COLS;
       if (!C::BLOCK_SF) tmem_cp_32x128b_x4(sfb_unit, desc_sf(smem_u32(const_sf)));
+      if (p.tile_expert) pdl_wait();  // the routing is read below
       uint32_t it = 0, lt = 0;
       for (int t = blockIdx.x; t < tiles && !*abort_v; t += gridDim.x, ++lt) {
+        if (p.tile_expert && p.tile_expert[t / p.n_tiles] < 0) break;
         const uint32_t b = lt & 1, use = lt >> 1;
         if (use > 0 && !mbar_wait_bounded(&acce[b], (use - 1) & 1, abort_v, p.err, 8u)) break;
         tc_fence_after();
@@ -466,10 +474,12 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;
     const int et = threadIdx.x - 64;
     const int r = q * 32 + lane;
-    const float gw = __ldg(p.gw);
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
       const int n_tile = t % p.n_tiles, m_tile = t / p.n_tiles;
+      const int expert = p.tile_expert ? p.tile_expert[m_tile] : 0;
+      if (expert < 0) break;
+      const float gw = __ldg(p.gw + expert);
       const uint32_t b = lt & 1, use = lt >> 1;
       if (et < BN) {
         float g = p.gx[m_tile * BN + et];
@@ -501,8 +511,8 @@ __global__ void __launch_bounds__(192, 1)
         if (ok) {
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const int m = m_tile * BN + c + k;
-            if (m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, o[k] + bias);
+            const int m = p.row_map ? p.row_map[m_tile * BN + c + k] : m_tile * BN + c + k;
+            if (m >= 0 && m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, o[k] + bias);
           }
         }
       }
@@ -569,7 +579,7 @@ constexpr size_t ERR_BYTES = 256;  // error word at offset 0 of every GEMM works
 struct Plan {
   int terms, bn, m_tiles, m_pad, n_tiles, nkt, ks, rows_max, stages, tmem_cols;
   size_t smem;
-  // persistent form (dense, one split, more tiles than two per SM): pipeline and TMEM of it
+  // persistent form (one split, more tiles than two per SM): pipeline and TMEM of it
   bool persistent;
   int p_stages, p_cols;
   size_t p_smem;
@@ -816,7 +826,7 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
 template <int BN, int T>
 static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmParams& gp, const Plan& P,
                        cudaStream_t st) {
-  if (P.persistent && !gp.part && !gp.tile_expert) {  // prefill-size dense GEMM
+  if (P.persistent && !gp.part) {  // prefill-size dense GEMM, or the grouped MoE GEMM
     static size_t configured[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
@@ -897,6 +907,7 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
   gp.tag_add = tag_add;
   gp.tile_expert = tile_expert;
   gp.row_map = row_map;
+  gp.m_tiles_max = P.m_tiles;
   return dispatch_gemm(tmw, tmx, gp, P, st);
 }
 

@@ -210,11 +210,14 @@ def _experts(e, n, k, seed):
 
 
 @pytest.mark.parametrize("e,m,n,k,mode", [(16, 128, 768, 2048, "random"), (8, 48, 256, 768, "one"),
-                                          (64, 40, 256, 512, "distinct"), (4, 5, 128, 256, "random")])
+                                          (64, 40, 256, 512, "distinct"), (4, 5, 128, 256, "random"),
+                                          (32, 128, 1536, 1024, "random"), (128, 128, 384, 512, "distinct")])
 def test_grouped_gemm_moe_shapes(e, m, n, k, mode):
     """One routed grouped GEMM (nvfp4_linear_gather -> ada_nvfp4_linear_grouped) against the
     oracle per row: MoE-like routing (16 tokens x top-8 over 16 experts), every row on one
-    expert, every row on its own expert, and a ragged small case."""
+    expert, every row on its own expert, and a ragged small case.  The last two have more
+    (expert, n) tiles than two per SM and run the persistent kernel (one CTA per SM walking the
+    routed tiles; the unused tail of the tile list is skipped)."""
     d = dev()
     ws = _experts(e, n, k, 50)
     g = torch.Generator().manual_seed(e + m)
