@@ -45,6 +45,8 @@ _SIGS = {
                                          I32, I32, F32, F32, F32, I32, P, INT, INT, INT, P, P, P, P, SZ, P]),
     "ada_fp8_paged_decode_quant_ex": (INT, [P, INT, I64, I64, P, P, I64, I64, I64, I64, P, I64, I32, P, I32, I32, I32,
                                             I32, I32, F32, F32, F32, I32, P, INT, INT, INT, P, P, P, P, SZ, I32, P]),
+    "ada_fp8_paged_prefill": (INT, [P, INT, I64, I64, P, P, I64, I64, I64, I64, P, I64, I32, P, P, I32, I32, I32,
+                                    I32, I32, I32, F32, F32, F32, I32, P, INT, I64, I64, P, P]),
     "ada_rmsnorm_quant": (INT, [P, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT, P, P, P, P]),
     "ada_gated_act_quant": (INT, [P, I64, P, I64, I64, I32, INT, INT, INT, INT, P, P, P, P]),
     "ada_store_kvcache_fp8": (INT, [P, P, INT, I64, I32, I32, I64, I64, P, P, P, I64, F32, F32, P]),

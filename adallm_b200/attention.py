@@ -4,9 +4,12 @@ Mirrors the reference interface in adallm/ops/attention.py:
   * store_kvcache(key, value, k_cache, v_cache, slot_mapping)   (:236-251)
   * Attention(num_heads, head_dim, scale, num_kv_heads, sliding_window).forward(q, k, v)
     decode branch (:307-428), reading per-step metadata from the forward context
-Prefill attention (flash-attn varlen in the reference, :335-358) is not part of
-this package's hot path; ``Attention.forward`` raises for prefill contexts when
-used standalone, and ``adallm_b200.install`` keeps the reference's prefill branch.
+  * paged_prefill: the prefix-cache prefill branch (:335-358), which the reference runs as
+    _gather_kv_from_blocks (:254-286) + flash_attn_varlen_func(causal=True, window=(W, 0));
+    here one kernel reads the e4m3 pages in place through the block table.
+A prefill without a prefix cache (no block table: the reference attends over the fresh
+bf16 K/V with flash-attn) is not part of this package: ``Attention.forward`` raises for it
+when used standalone, and ``adallm_b200.install`` keeps the reference's branch for it.
 """
 from __future__ import annotations
 
@@ -80,6 +83,51 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     return out
 
 
+def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                  cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor, max_seqlen_q: int, scale: float,
+                  window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0, out: torch.Tensor | None = None,
+                  err: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal prefill attention of the new tokens against the e4m3 paged cache.
+
+    q [total_q, Hq, D] bf16/fp16 (sequence b: rows cu_seqlens_q[b]..cu_seqlens_q[b+1]);
+    k_cache/v_cache [num_pages, page, Hkv, D] e4m3 holding every sequence's cached prefix and
+    new tokens (store_kvcache runs first); block_tables int32 [B, max_pages] (-1 padded);
+    cu_seqlens_q / cu_seqlens_k int32 [B + 1] (the reference's forward-context fields);
+    window W > 0: query i sees keys [i + off - W, i + off], off = len_k - len_q.
+    Returns [total_q, Hq, D] in q.dtype (the reference returns fp16 cast back to q.dtype).
+    err: optional int32 [1] device word; 0x70 is OR-ed in if a tile wait ran out."""
+    N.require_cuda(q, k_cache, v_cache, block_tables, cu_seqlens_q, cu_seqlens_k, what="paged_prefill")
+    total_q, hq, d = q.shape
+    _, page, hkv, _ = k_cache.shape
+    if q.dtype not in N.DT:
+        raise ValueError("q must be bf16 or fp16")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1:
+        raise ValueError("k_cache and v_cache must share a [pages, page, Hkv, D] layout")
+    if k_cache.dtype != torch.float8_e4m3fn or v_cache.dtype != torch.float8_e4m3fn:
+        raise ValueError("the paged prefill reads a float8_e4m3fn cache")
+    for t, name in ((block_tables, "block_tables"), (cu_seqlens_q, "cu_seqlens_q"), (cu_seqlens_k, "cu_seqlens_k")):
+        if t.dtype != torch.int32:
+            raise ValueError(f"{name} must be int32")
+    batch = cu_seqlens_q.numel() - 1
+    if cu_seqlens_k.numel() != batch + 1 or block_tables.shape[0] < batch:
+        raise ValueError("cu_seqlens_q, cu_seqlens_k and block_tables must describe the same sequences")
+    if out is None:
+        out = torch.empty((total_q, hq, d), dtype=q.dtype, device=q.device)
+    if total_q == 0 or batch == 0:
+        return out
+    st = N.lib().ada_fp8_paged_prefill(
+        q.data_ptr(), N.DT[q.dtype], q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), k_cache.shape[0], block_tables.data_ptr(),
+        block_tables.stride(0), block_tables.shape[1], cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch,
+        int(max_seqlen_q), hq, hkv, d, page, float(scale), float(k_scale), float(v_scale), int(window),
+        out.data_ptr(), N.DT[out.dtype], out.stride(0), out.stride(1),
+        err.data_ptr() if err is not None else None, N.stream_ptr(q.device))
+    N.check(st, "FP8 paged prefill attention")
+    return out
+
+
 class Attention(nn.Module):
     """Drop-in for adallm.ops.attention.Attention (decode branch).
 
@@ -99,11 +147,21 @@ class Attention(nn.Module):
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         context = get_context()
-        if context.is_prefill:
-            raise NotImplementedError("adallm_b200 implements the decode branch; prefill stays on the reference path")
+        if context.is_prefill and context.block_tables is None:
+            raise NotImplementedError("adallm_b200 runs the prefix-cache prefill and the decode branch; a prefill "
+                                      "without a block table stays on the reference path")
         if self.k_cache.numel() and self.v_cache.numel():
             store_kvcache(k, v, self.k_cache, self.v_cache, context.slot_mapping, self.k_scale, self.v_scale)
         window = self.sliding_window if (self.sliding_window is not None and self.sliding_window > 0) else 0
+        if context.is_prefill:
+            try:
+                return paged_prefill(q.view(-1, self.num_heads, self.head_dim), self.k_cache, self.v_cache,
+                                     context.block_tables, context.cu_seqlens_q, context.cu_seqlens_k,
+                                     context.max_seqlen_q, self.scale, window, self.k_scale, self.v_scale)
+            except Exception as exc:
+                if torch.cuda.is_current_stream_capturing() or isinstance(exc, ValueError):
+                    raise
+                raise RuntimeError("FP8 paged prefill kernel failed; no fallback is allowed in this runtime.") from exc
         try:
             return paged_decode(q.view(-1, self.num_heads, self.head_dim), self.k_cache, self.v_cache,
                                 context.block_tables, context.context_lens, self.scale, window,

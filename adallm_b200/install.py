@@ -7,8 +7,9 @@ Replaces, by the same names and signatures:
   adallm.ops.nvfp4_gemm.nvfp4_linear / nvfp4_linear_dual / nvfp4_linear_gather   (nvfp4_gemm.py:460, :567, :657)
   adallm.ops.linear.nvfp4_linear (the name LinearBase._linear calls, linear.py:6, :61-74)
   adallm.ops.attention.store_kvcache                                            (attention.py:236)
-  adallm.ops.attention.Attention.forward -- decode branch only; prefill (flash-attn varlen,
-      attention.py:335-358) keeps the reference implementation
+  adallm.ops.attention.Attention.forward -- decode branch, and the prefix-cache prefill branch
+      (attention.py:335-358: gather + flash-attn varlen -> one kernel over the e4m3 pages); a
+      prefill without a block table keeps the reference implementation
   adallm.ops.layernorm.RMSNorm.forward / GemmaRMSNorm.forward                    (layernorm.py:42-50, :94-102)
   adallm.ops.rotary_embedding.RotaryEmbedding.forward                            (rotary_embedding.py:45-56)
   adallm.ops.activation.SiluAndMul.forward / GeluAndMul.forward                   (activation.py:11-26)
@@ -66,12 +67,22 @@ def install(terms: int | None = None) -> None:
 
     def attn_forward(self, q, k, v):
         ctx = ref_ctx.get_context()
-        if ctx.is_prefill or self.k_cache.dtype != torch.float8_e4m3fn:
+        if self.k_cache.dtype != torch.float8_e4m3fn or (ctx.is_prefill and ctx.block_tables is None):
             return orig_forward(self, q, k, v)
         orig_dtype = q.dtype
         if self.k_cache.numel() and self.v_cache.numel():
             attention.store_kvcache(k, v, self.k_cache, self.v_cache, ctx.slot_mapping)
         window = self.sliding_window if (self.sliding_window is not None and self.sliding_window > 0) else 0
+        if ctx.is_prefill:
+            try:
+                o = attention.paged_prefill(q.view(-1, self.num_heads, self.head_dim), self.k_cache, self.v_cache,
+                                            ctx.block_tables, ctx.cu_seqlens_q, ctx.cu_seqlens_k, ctx.max_seqlen_q,
+                                            self.scale, window)
+            except Exception as exc:
+                if torch.cuda.is_current_stream_capturing() or isinstance(exc, ValueError):
+                    raise
+                raise RuntimeError("FP8 paged prefill kernel failed; no fallback is allowed in this runtime.") from exc
+            return o if o.dtype == orig_dtype else o.to(orig_dtype)
         try:
             o = attention.paged_decode(q.view(-1, self.num_heads, self.head_dim), self.k_cache, self.v_cache,
                                        ctx.block_tables, ctx.context_lens, self.scale, window)

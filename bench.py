@@ -308,6 +308,33 @@ def kernel_benches(dev, peak):
                                 "mode": "steady", "launches": 2}
     del xp, yp, wsp, packed, scale, flush
     torch.cuda.empty_cache()
+
+    # prefix-cache prefill attention on the e4m3 pages (Qwen3-8B heads): 4 sequences with 2048
+    # cached tokens and 2048 new ones; FLOPs = 4 * D * (visible keys summed over query rows and
+    # heads), the causal half of the new block included, masked work not counted
+    from adallm_b200.attention import paged_prefill
+    nseq, cached, new = 4, 2048, 2048
+    lk = cached + new
+    npg = lk // page
+    bt_p = torch.arange(nseq * npg, dtype=torch.int32).view(nseq, npg)
+    bt_p = bt_p.flatten()[torch.randperm(nseq * npg, generator=g)].view(nseq, npg).to(dev)
+    kc = torch.randn((nseq * npg, page, hkv, D), device=dev, dtype=torch.bfloat16).to(torch.float8_e4m3fn)
+    vc = torch.randn((nseq * npg, page, hkv, D), device=dev, dtype=torch.bfloat16).to(torch.float8_e4m3fn)
+    qp = torch.randn((nseq * new, hq, D), device=dev, dtype=torch.bfloat16)
+    op = torch.empty_like(qp)
+    cu_q = torch.arange(0, (nseq + 1) * new, new, dtype=torch.int32, device=dev)
+    cu_k = torch.arange(0, (nseq + 1) * lk, lk, dtype=torch.int32, device=dev)
+    pa = lambda: paged_prefill(qp, kc, vc, bt_p, cu_q, cu_k, new, D ** -0.5, out=op)
+    us = steady([pa] * 4, reps=3)
+    vis = nseq * hq * (cached * new + new * (new + 1) // 2)
+    tf = 4 * D * vis / us / 1e6
+    bf16_burst = measured_bf16()
+    out["prefill_attention_fp8"] = {"us": round(us, 1), "tflops": round(tf, 1), "seqs": nseq, "cached": cached,
+                                    "new": new, "heads": [hq, hkv], "page": page,
+                                    "frac_bf16_measured": round(tf / bf16_burst, 4) if bf16_burst else None,
+                                    "mode": "steady", "launches": 1}
+    del kc, vc, qp, op
+    torch.cuda.empty_cache()
     return out
 
 

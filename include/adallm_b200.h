@@ -120,6 +120,35 @@ ADA_API int ada_fp8_paged_decode_quant_ex(const void* q, int q_dtype, int64_t q_
                                           int32_t flags, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Causal prefill attention reading the FP8 paged cache in place
+ * Replaces the prefix-cache prefill branch of Attention.forward (adallm/ops/attention.py:335-358):
+ * _gather_kv_from_blocks (:254-286) + flash_attn_varlen_func(causal=True, window_size=(W, 0)).
+ *
+ * q        [total_q, num_heads, head_dim] (q_dtype), token stride q_stride_t, head stride
+ *          q_stride_h, unit stride in D; sequence b owns rows [cu_seqlens_q[b], cu_seqlens_q[b+1])
+ * cu_seqlens_q, cu_seqlens_k  int32 [batch + 1] (the reference's forward-context fields):
+ *          len_k(b) = cu_seqlens_k[b+1] - cu_seqlens_k[b] keys, cached prefix + the new tokens,
+ *          all already stored in the pages (store_kvcache runs first)
+ * max_seqlen_q  max over b of len_q(b) (sizes the grid; larger is allowed)
+ * k_cache, v_cache, block_tables, num_pages, page_size, k_scale, v_scale: as the decode entry
+ * window   0 = causal only; W > 0: query i (0-based among the new tokens) sees keys
+ *          [i + len_k - len_q - W, i + len_k - len_q] (flash-attn's window_size = (W, 0))
+ * out      [total_q, num_heads, head_dim] (out_dtype), strides out_stride_t / out_stride_h
+ * err      optional uint32 word: 0x70 is OR-ed in if a tile load wait ran out (~2 s)
+ * Implemented: head_dim 128, num_heads / num_kv_heads <= 64, page_size % 16 == 0.  Rows that
+ * see no key are written as zeros.
+ * ---------------------------------------------------------------------- */
+ADA_API int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_stride_t, int64_t q_stride_h,
+                                  const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
+                                  int64_t kv_stride_tok, int64_t kv_stride_head, int64_t num_pages,
+                                  const int32_t* block_tables, int64_t bt_stride, int32_t max_pages,
+                                  const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
+                                  int32_t max_seqlen_q, int32_t num_heads, int32_t num_kv_heads,
+                                  int32_t head_dim, int32_t page_size, float scale, float k_scale,
+                                  float v_scale, int32_t window, void* out, int out_dtype,
+                                  int64_t out_stride_t, int64_t out_stride_h, unsigned int* err, void* stream);
+
+/* ------------------------------------------------------------------------
  * FP8 KV-cache store
  * Replaces store_kvcache / store_kvcache_kernel (adallm/ops/attention.py:11-31, :236-251).
  * key/value [num_tokens, num_kv_heads, head_dim] (in_dtype), row strides key_stride/value_stride,

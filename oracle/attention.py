@@ -1,4 +1,5 @@
-"""FP8 paged decode attention + FP8 KV-cache store oracle.  Test infrastructure only.
+"""FP8 paged decode and prefix-cache prefill attention + FP8 KV-cache store oracle.
+Test infrastructure only.
 
 Reference anchors (paths inside the reference project):
   * store_kvcache_kernel / store_kvcache   adallm/ops/attention.py:11-31, :236-251
@@ -6,6 +7,9 @@ Reference anchors (paths inside the reference project):
   * _gather_kv_from_blocks                 adallm/ops/attention.py:254-286
   * decode launch (q -> fp16, out fp16)    adallm/ops/attention.py:314-324, :359-414
   * slot = page_id * page + offset         adallm/runtime/model_runner.py:262-267, :291
+  * prefix-cache prefill                   adallm/ops/attention.py:335-358 (gather, then
+                                           flash_attn_varlen_func causal, window (W, 0));
+                                           metadata from model_runner.py:240-276
 
 Cache layout (reference): k_cache / v_cache are e4m3fn [num_pages, page, Hkv, D];
 block_tables int32 [B, max_pages] padded with -1; context_lens int32 [B]
@@ -97,6 +101,91 @@ def paged_decode(q, k_cache_bits, v_cache_bits, block_tables, context_lens, scal
         p = torch.softmax(s, dim=0)
         out[i] = torch.einsum("nh,nhd->hd", p, vv)
     return out.to(torch.float32).numpy()
+
+
+def paged_prefill(q, k_cache_bits, v_cache_bits, block_tables, cu_seqlens_q, cu_seqlens_k, scale,
+                  window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0):
+    """Prefix-cache prefill attention (attention.py:335-358).
+
+    The reference gathers each sequence's first len_k = cu_seqlens_k[b+1] - cu_seqlens_k[b]
+    cached tokens to fp16 (_gather_kv_from_blocks, :254-286; e4m3 -> fp16 is exact) and calls
+    flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, causal=True,
+    window_size=(W, 0)).  flash-attn's published masking for varlen causal attention aligns
+    the mask to the bottom right: query i of the len_q new tokens sees key j iff
+    j <= i + len_k - len_q, and with W > 0 also j >= i + len_k - len_q - W.  A row that sees
+    no key is zero.  Keys on a page whose block id is outside [0, num_pages) are masked (the
+    reference would fail on such a table; the kernel treats it like the decode path does).
+
+    q: [total_q, Hq, D] float (bf16 values), rounded to fp16 as the reference does
+    (:319-324).  Returns fp32 [total_q, Hq, D]."""
+    q = torch.as_tensor(np.asarray(q, np.float32)).to(torch.float16).to(torch.float64)
+    kf = torch.from_numpy(e4m3_decode(k_cache_bits)).to(torch.float64) * float(k_scale)
+    vf = torch.from_numpy(e4m3_decode(v_cache_bits)).to(torch.float64) * float(v_scale)
+    num_pages, page, hkv = k_cache_bits.shape[0], k_cache_bits.shape[1], k_cache_bits.shape[2]
+    total_q, hq, d = q.shape
+    group = hq // hkv
+    head_map = torch.arange(hq) // group
+    out = torch.zeros((total_q, hq, d), dtype=torch.float64)
+    bt = np.asarray(block_tables)
+    cu_q = np.asarray(cu_seqlens_q, np.int64)
+    cu_k = np.asarray(cu_seqlens_k, np.int64)
+    for b in range(len(cu_q) - 1):
+        q0, len_q = int(cu_q[b]), int(cu_q[b + 1] - cu_q[b])
+        len_k = int(cu_k[b + 1] - cu_k[b])
+        if len_q <= 0 or len_k <= 0:
+            continue
+        keys = np.arange(len_k)
+        keys = keys[keys < bt.shape[1] * page]
+        pages = bt[b, keys // page].astype(np.int64)
+        ok = (pages >= 0) & (pages < num_pages)
+        pi = torch.from_numpy(np.where(ok, pages, 0))
+        ti = torch.from_numpy(keys % page)
+        kk = kf[pi, ti][:, head_map]  # [n, Hq, D]
+        vv = vf[pi, ti][:, head_map]
+        vv[torch.from_numpy(~ok)] = 0.0
+        off = len_k - len_q
+        i = torch.arange(len_q)[:, None]
+        j = torch.from_numpy(keys)[None, :]
+        vis = (j <= i + off) & torch.from_numpy(ok)[None, :]
+        if window > 0:
+            vis &= j >= i + off - window
+        s = torch.einsum("qhd,khd->hqk", q[q0:q0 + len_q], kk) * float(scale)
+        s = s.masked_fill(~vis[None], float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        p = torch.nan_to_num(p, nan=0.0)  # rows with no visible key
+        out[q0:q0 + len_q] = torch.einsum("hqk,khd->qhd", p, vv)
+    return out.to(torch.float32).numpy()
+
+
+def make_prefill_case(seed: int, cached: list, new: list, hq: int, hkv: int, d: int, page: int,
+                      extra_pages: int = 0, holes: int = 0):
+    """Seeded prefix-cache prefill case: sequence b has cached[b] tokens already in the cache
+    and new[b] new query tokens (all len_k = cached + new tokens stored, as store_kvcache does
+    before attention); pages from a random permutation of a pool with `extra_pages` unused
+    pages; `holes` random table entries inside the used range set to -1.  K, V ~ N(0,1) cast
+    to e4m3, q ~ N(0,1) bf16."""
+    g = torch.Generator().manual_seed(seed)
+    len_k = np.asarray([c + n for c, n in zip(cached, new)], np.int64)
+    npages = (len_k + page - 1) // page
+    pool = int(npages.sum()) + extra_pages
+    perm = torch.randperm(max(pool, 1), generator=g).numpy().astype(np.int32)
+    max_pages = max(int(npages.max()) if len(npages) else 1, 1)
+    bt = -np.ones((len(new), max_pages), np.int32)
+    o = 0
+    for b in range(len(new)):
+        bt[b, :npages[b]] = perm[o:o + npages[b]]
+        o += int(npages[b])
+    for _ in range(holes):
+        b = int(torch.randint(0, len(new), (1,), generator=g))
+        if npages[b]:
+            bt[b, int(torch.randint(0, int(npages[b]), (1,), generator=g))] = -1
+    kbits = e4m3_encode(torch.randn((max(pool, 1), page, hkv, d), generator=g).numpy())
+    vbits = e4m3_encode(torch.randn((max(pool, 1), page, hkv, d), generator=g).numpy())
+    cu_q = np.concatenate([[0], np.cumsum(new)]).astype(np.int32)
+    cu_k = np.concatenate([[0], np.cumsum(len_k)]).astype(np.int32)
+    q = torch.randn((int(cu_q[-1]), hq, d), generator=g).to(torch.bfloat16).to(torch.float32).numpy()
+    return dict(q=q, k=kbits, v=vbits, block_tables=bt, cu_q=cu_q, cu_k=cu_k,
+                max_seqlen_q=int(max(new)) if len(new) else 0, scale=1.0 / np.sqrt(d))
 
 
 def make_paged_case(seed: int, batch: int, hq: int, hkv: int, d: int, page: int,

@@ -68,3 +68,46 @@ def test_ops_raise_without_cuda(ref):
     with pytest.raises(RuntimeError, match="CUDA"):
         nvfp4_linear(x, torch.zeros(128, 128, dtype=torch.uint8), torch.zeros(128, 16, dtype=torch.float16),
                      torch.tensor(1.0), None, None, 16)
+
+
+def test_prefill_routing(ref, monkeypatch):
+    """After install(): a prefill with a block table (prefix cache) and an e4m3 cache goes to
+    the paged prefill kernel with the context's metadata; a prefill without one stays on the
+    reference branch.  The kernels are replaced by recorders (no CUDA here)."""
+    import torch
+    import adallm.ops.attention as ra
+    import adallm.infra.context as rc
+    import adallm_b200
+    from adallm_b200 import attention, context
+    adallm_b200.install()
+    calls = []
+    monkeypatch.setattr(attention, "store_kvcache", lambda *a, **k: calls.append("store"))
+
+    def fake_prefill(q, kc, vc, bt, cu_q, cu_k, max_q, scale, window=0, *a, **k):
+        calls.append(("prefill", bt, cu_q, cu_k, max_q, window))
+        return torch.ones_like(q, dtype=torch.float16)
+
+    monkeypatch.setattr(attention, "paged_prefill", fake_prefill)
+    m = ra.Attention(8, 128, 0.088, 2, sliding_window=64)
+    m.k_cache = torch.zeros((4, 16, 2, 128), dtype=torch.float8_e4m3fn)
+    m.v_cache = torch.zeros((4, 16, 2, 128), dtype=torch.float8_e4m3fn)
+    q = torch.zeros((5, 8 * 128), dtype=torch.bfloat16)
+    kv = torch.zeros((5, 2, 128), dtype=torch.bfloat16)
+    cu_q = torch.tensor([0, 5], dtype=torch.int32)
+    cu_k = torch.tensor([0, 20], dtype=torch.int32)
+    bt = torch.tensor([[2, 0]], dtype=torch.int32)
+    try:
+        rc.set_context(True, cu_q, cu_k, 5, 20, torch.arange(5, dtype=torch.int32), None, bt)
+        o = m.forward(q, kv, kv)
+        assert calls[0] == "store" and calls[1][0] == "prefill"
+        assert calls[1][1] is bt and calls[1][2] is cu_q and calls[1][3] is cu_k
+        assert calls[1][4] == 5 and calls[1][5] == 64
+        assert o.dtype == torch.bfloat16 and o.shape == (5, 8, 128)
+        calls.clear()
+        rc.set_context(True, cu_q, cu_q, 5, 5, torch.arange(5, dtype=torch.int32), None, None)
+        with pytest.raises(Exception):  # the reference branch (flash-attn) cannot run on CPU
+            m.forward(q, kv, kv)
+        assert all(c == "store" for c in calls)
+    finally:
+        rc.reset_context()
+        context.use_context_provider(None)
