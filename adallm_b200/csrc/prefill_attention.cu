@@ -41,7 +41,8 @@ constexpr int D = 128;
 constexpr int TILE = 16;
 constexpr int TILE_BYTES = TILE * D;       // 16 keys x 128 e4m3 bytes
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K tile, V tile
-constexpr int STAGES = 6;
+constexpr int STAGES = 8;
+constexpr int KB = 4;                      // tiles per online-softmax step (64 keys)
 constexpr int ROWS = 64;                   // (token, head) rows per CTA
 constexpr int MMA_WARPS = 4;
 constexpr int THREADS = (MMA_WARPS + 1) * 32;
@@ -209,76 +210,94 @@ __global__ void __launch_bounds__(THREADS, 2)
   float m0 = -INFINITY, m8 = -INFINITY, l0 = 0.f, l8 = 0.f;
   const uint4 z = make_uint4(0, 0, 0, 0);
 
-  for (int i = 0; i < ntiles; ++i) {
-    const int s = i % STAGES;
-    if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_v, P.err, ERR_TILE_WAIT)) break;
-    const bool blk_ok = slot_ok[s] != 0;
-    const uint8_t* kt = ring + s * STAGE_BYTES;
-    const uint8_t* vt = kt + TILE_BYTES;
-    const int key0 = (kt0 + i) * TILE;
-
-    // ---- S = Q . K^T: n-block j covers keys key0 + 8j .. +8 ----
-    uint4 kg[2], kg8[2];
-    kg[0] = tile_ld16(kt, g, 2 * c);
-    kg[1] = tile_ld16(kt, g, 2 * c + 1);
-    kg8[0] = tile_ld16(kt, g + 8, 2 * c);
-    kg8[1] = tile_ld16(kt, g + 8, 2 * c + 1);
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const uint32_t* kw = reinterpret_cast<const uint32_t*>(kg);
-    const uint32_t* kw8 = reinterpret_cast<const uint32_t*>(kg8);
+  bool failed = false;
+  for (int i0 = 0; i0 < ntiles && !failed; i0 += KB) {
+    // ---- S = Q . K^T over KB tiles (64 keys): tile u, n-block j covers keys key0(u) + 8j .. +8
+    float sc[KB][2][4];
+    bool blk_ok[KB];
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t b0[2], b1[2];
-      b0[0] = e4m3x2_to_f16x2((uint16_t)(kw[ks] & 0xFFFFu));
-      b0[1] = e4m3x2_to_f16x2((uint16_t)(kw[ks] >> 16));
-      b1[0] = e4m3x2_to_f16x2((uint16_t)(kw8[ks] & 0xFFFFu));
-      b1[1] = e4m3x2_to_f16x2((uint16_t)(kw8[ks] >> 16));
-      mma_16816_f16(sc[0], &qa[4 * ks], b0);
-      mma_16816_f16(sc[1], &qa[4 * ks], b1);
-    }
-
-    // ---- masks, online softmax (rows g: sc[j][0..1], rows g+8: sc[j][2..3]) ----
-    float x[2][4];
+    for (int u = 0; u < KB; ++u) {
+      sc[u][0][0] = sc[u][0][1] = sc[u][0][2] = sc[u][0][3] = 0.f;
+      sc[u][1][0] = sc[u][1][1] = sc[u][1][2] = sc[u][1][3] = 0.f;
+      blk_ok[u] = false;
+      const int i = i0 + u;
+      if (i >= ntiles) continue;  // warp-uniform
+      const int s = i % STAGES;
+      // a wait that ran out marks the step failed; its (stale) tile is computed and discarded
+      if (!failed && !mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_v, P.err, ERR_TILE_WAIT)) failed = true;
+      blk_ok[u] = slot_ok[s] != 0;
+      const uint8_t* kt = ring + s * STAGE_BYTES;
+      uint4 kg[2], kg8[2];
+      kg[0] = tile_ld16(kt, g, 2 * c);
+      kg[1] = tile_ld16(kt, g, 2 * c + 1);
+      kg8[0] = tile_ld16(kt, g + 8, 2 * c);
+      kg8[1] = tile_ld16(kt, g + 8, 2 * c + 1);
+      const uint32_t* kw = reinterpret_cast<const uint32_t*>(kg);
+      const uint32_t* kw8 = reinterpret_cast<const uint32_t*>(kg8);
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = key0 + 8 * j + 2 * c + e;
-        x[j][e] = (blk_ok && key >= lo0 && key < hi0) ? sc[j][e] * P.scale_log2 : -INFINITY;
-        x[j][2 + e] = (blk_ok && key >= lo8 && key < hi8) ? sc[j][2 + e] * P.scale_log2 : -INFINITY;
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t b0[2], b1[2];
+        b0[0] = e4m3x2_to_f16x2((uint16_t)(kw[ks] & 0xFFFFu));
+        b0[1] = e4m3x2_to_f16x2((uint16_t)(kw[ks] >> 16));
+        b1[0] = e4m3x2_to_f16x2((uint16_t)(kw8[ks] & 0xFFFFu));
+        b1[1] = e4m3x2_to_f16x2((uint16_t)(kw8[ks] >> 16));
+        mma_16816_f16(sc[u][0], &qa[4 * ks], b0);
+        mma_16816_f16(sc[u][1], &qa[4 * ks], b1);
       }
     }
-    float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
-    float mx8 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+    if (failed) break;
+
+    // ---- masks, one online-softmax step for the 64 keys (rows g: [..][0..1], rows g+8: [..][2..3])
+    float mx0 = -INFINITY, mx8 = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = (kt0 + i0 + u) * TILE + 8 * j + 2 * c + e;
+          sc[u][j][e] = (blk_ok[u] && key >= lo0 && key < hi0) ? sc[u][j][e] * P.scale_log2 : -INFINITY;
+          sc[u][j][2 + e] = (blk_ok[u] && key >= lo8 && key < hi8) ? sc[u][j][2 + e] * P.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, sc[u][j][e]);
+          mx8 = fmaxf(mx8, sc[u][j][2 + e]);
+        }
+      }
+    }
 #pragma unroll
     for (int sh = 1; sh < 4; sh <<= 1) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
       mx8 = fmaxf(mx8, __shfl_xor_sync(0xffffffffu, mx8, sh));
     }
     const float mn0 = fmaxf(m0, mx0), mn8 = fmaxf(m8, mx8);
-    float al0 = 1.f, al8 = 1.f;
-    float p[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    if (mn0 != -INFINITY) {
-      al0 = fast_exp2(m0 - mn0);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        p[j][0] = fast_exp2(x[j][0] - mn0);
-        p[j][1] = fast_exp2(x[j][1] - mn0);
-      }
-    }
-    if (mn8 != -INFINITY) {
-      al8 = fast_exp2(m8 - mn8);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        p[j][2] = fast_exp2(x[j][2] - mn8);
-        p[j][3] = fast_exp2(x[j][3] - mn8);
-      }
-    }
+    const float al0 = mn0 != -INFINITY ? fast_exp2(m0 - mn0) : 1.f;
+    const float al8 = mn8 != -INFINITY ? fast_exp2(m8 - mn8) : 1.f;
+    const float sub0 = mn0 != -INFINITY ? mn0 : 0.f;  // exp2(-inf - 0) = 0 for a row with nothing yet
+    const float sub8 = mn8 != -INFINITY ? mn8 : 0.f;
     m0 = mn0;
     m8 = mn8;
-    // fp32 probabilities feed the row sums, fp16 ones feed P.V
-    l0 = l0 * al0 + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);
-    l8 = l8 * al8 + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
+    float ps0 = 0.f, ps8 = 0.f;
+    uint32_t pa[KB][4];
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      float p[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        p[j][0] = fast_exp2(sc[u][j][0] - sub0);
+        p[j][1] = fast_exp2(sc[u][j][1] - sub0);
+        p[j][2] = fast_exp2(sc[u][j][2] - sub8);
+        p[j][3] = fast_exp2(sc[u][j][3] - sub8);
+      }
+      // fp32 probabilities feed the row sums, fp16 ones feed P.V; the S accumulator layout is
+      // the A-operand layout of P . V (keys 2c.. in a0/a1, 2c+8.. in a2/a3)
+      ps0 += (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
+      ps8 += (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
+      pa[u][0] = pack_half2(p[0][0], p[0][1]);
+      pa[u][1] = pack_half2(p[0][2], p[0][3]);
+      pa[u][2] = pack_half2(p[1][0], p[1][1]);
+      pa[u][3] = pack_half2(p[1][2], p[1][3]);
+    }
+    l0 = l0 * al0 + ps0;
+    l8 = l8 * al8 + ps8;
 #pragma unroll
     for (int nb = 0; nb < 16; ++nb) {
       o[nb][0] *= al0;
@@ -286,40 +305,43 @@ __global__ void __launch_bounds__(THREADS, 2)
       o[nb][2] *= al8;
       o[nb][3] *= al8;
     }
-    // the S accumulator layout is the A-operand layout of P . V (keys 2c.. in a0/a1, 2c+8.. in a2/a3)
-    uint32_t pa[4];
-    pa[0] = pack_half2(p[0][0], p[0][1]);
-    pa[1] = pack_half2(p[0][2], p[0][3]);
-    pa[2] = pack_half2(p[1][0], p[1][1]);
-    pa[3] = pack_half2(p[1][2], p[1][3]);
 
-    // ---- O += P . V: keys past len_k and holes may hold stale bytes (NaN in e4m3): zero them
-    uint4 vv[4];
-    const int vk[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+    // ---- O += P . V, tile by tile; keys past len_k and holes may hold stale bytes (NaN in
+    // e4m3): their V rows are zeroed
 #pragma unroll
-    for (int e = 0; e < 4; ++e) vv[e] = (blk_ok && key0 + vk[e] < len_k) ? tile_ld16(vt, vk[e], g) : z;
-    const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0]);
-    const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1]);
-    const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&vv[2]);
-    const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&vv[3]);
+    for (int u = 0; u < KB; ++u) {
+      const int i = i0 + u;
+      if (i >= ntiles) continue;  // warp-uniform
+      const int s = i % STAGES;
+      const uint8_t* vt = ring + s * STAGE_BYTES + TILE_BYTES;
+      const int key0 = (kt0 + i) * TILE;
+      uint4 vv[4];
+      const int vk[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+      for (int e = 0; e < 4; ++e) vv[e] = (blk_ok[u] && key0 + vk[e] < len_k) ? tile_ld16(vt, vk[e], g) : z;
+      const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0]);
+      const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1]);
+      const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&vv[2]);
+      const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&vv[3]);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const uint32_t sel = half ? 0x7362u : 0x5140u;
-        const uint32_t w01 = prmt(v0[j], v1[j], sel);  // dims 16g + 4j + 2half + {0, 1}, keys 2c, 2c+1
-        const uint32_t w89 = prmt(v8[j], v9[j], sel);  // same dims, keys 2c+8, 2c+9
-        uint32_t bv[2];
-        bv[0] = e4m3x2_to_f16x2((uint16_t)(w01 & 0xFFFFu));
-        bv[1] = e4m3x2_to_f16x2((uint16_t)(w89 & 0xFFFFu));
-        mma_16816_f16(o[4 * j + 2 * half], pa, bv);
-        bv[0] = e4m3x2_to_f16x2((uint16_t)(w01 >> 16));
-        bv[1] = e4m3x2_to_f16x2((uint16_t)(w89 >> 16));
-        mma_16816_f16(o[4 * j + 2 * half + 1], pa, bv);
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t sel = half ? 0x7362u : 0x5140u;
+          const uint32_t w01 = prmt(v0[j], v1[j], sel);  // dims 16g + 4j + 2half + {0, 1}, keys 2c, 2c+1
+          const uint32_t w89 = prmt(v8[j], v9[j], sel);  // same dims, keys 2c+8, 2c+9
+          uint32_t bv[2];
+          bv[0] = e4m3x2_to_f16x2((uint16_t)(w01 & 0xFFFFu));
+          bv[1] = e4m3x2_to_f16x2((uint16_t)(w89 & 0xFFFFu));
+          mma_16816_f16(o[4 * j + 2 * half], pa[u], bv);
+          bv[0] = e4m3x2_to_f16x2((uint16_t)(w01 >> 16));
+          bv[1] = e4m3x2_to_f16x2((uint16_t)(w89 >> 16));
+          mma_16816_f16(o[4 * j + 2 * half + 1], pa[u], bv);
+        }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_plain(&empty[s]);  // this warp is done with the slot
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_plain(&empty[s]);  // this warp is done with the slot
   }
 
   // ---- normalise and store: thread holds dims [32c, 32c+32) of rows g and g+8 ----
@@ -328,7 +350,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
     l8 += __shfl_xor_sync(0xffffffffu, l8, sh);
   }
-  const bool failed = *abort_v != 0;
+  failed = failed || *abort_v != 0;
   const float inv0 = (l0 > 0.f && !failed) ? P.v_scale / l0 : 0.f;
   const float inv8 = (l8 > 0.f && !failed) ? P.v_scale / l8 : 0.f;
   TO* obase = reinterpret_cast<TO*>(P.out);
