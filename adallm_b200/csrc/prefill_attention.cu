@@ -16,21 +16,14 @@
 // statistics in fp32, probabilities rounded to fp16 for P.V, fp32 accumulation.  A row with no
 // visible key is written as zeros.
 //
-// Work split.  One CTA per (64-row query block, KV head, sequence): the 64 rows are
-// (token, head) pairs of the GQA group, head fastest, so QT = 64 / group consecutive query
-// tokens share every K/V tile the CTA loads (each e4m3 byte is read once per query block, not
-// once per head).  Warp 4 is the producer: one lane walks the block table and issues TMA loads
-// of 16-token K and V tiles (4-D tensor map over [pages][page][Hkv][128] bytes, 128-byte
-// swizzle) into a ring of stages; warps 0-3 each own 16 rows and run the flash-attention
-// recurrence with mma.sync m16n8k16 (f16 in, f32 accumulate): S = Q . K^T (rows x 16 keys),
-// online softmax on the S fragments, O += P . V with P taken straight from the S fragments.
+// Work split and roles: see the tcgen05 section below.  One CTA per (128-row query block, KV
+// head, sequence); the 128 rows are (token, head) pairs of the GQA group, head fastest, so
+// 128 / group consecutive query tokens share every K/V block the CTA loads (each e4m3 byte is
+// read once per query block, not once per head).  S = Q . K^T and O += P . V run on the
+// 5th-generation tensor cores (tcgen05.mma kind::f16, f16 operands staged in shared memory,
+// fp32 accumulators in TMEM); the e4m3 pages arrive by TMA (4-D tensor map over
+// [pages][page][Hkv][128] bytes) and are widened to f16 operand tiles in shared memory.
 // Query blocks are dealt last-first so the longest causal rows start first.
-//
-// Fragment layouts.  For Q . K^T the head dimension is permuted (identically for Q and K, so
-// the dot product is unchanged) so that thread (g, c) reads bytes [32c, 32c+32) of keys g and
-// g+8; for P . V the output dimension is permuted so that thread (g, c) reads bytes
-// [16g, 16g+16) of keys 2c, 2c+1, 2c+8, 2c+9 and ends up holding dims [32c, 32c+32) of its
-// rows: 16-byte shared-memory reads, conflict-free through the swizzle, and 64-byte row stores.
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -40,13 +33,6 @@ namespace pf {
 constexpr int D = 128;
 constexpr int TILE = 16;
 constexpr int TILE_BYTES = TILE * D;       // 16 keys x 128 e4m3 bytes
-constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K tile, V tile
-constexpr int STAGES = 8;
-constexpr int KB = 4;                      // tiles per online-softmax step (64 keys)
-constexpr int ROWS = 64;                   // (token, head) rows per CTA
-constexpr int MMA_WARPS = 4;
-constexpr int THREADS = (MMA_WARPS + 1) * 32;
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 2 * STAGES * 8 + STAGES * 4 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr unsigned int ERR_TILE_WAIT = 0x70;
 
@@ -67,115 +53,262 @@ struct Params {
   unsigned int* err;  // optional error word (bounded waits that ran out)
 };
 
-__device__ __forceinline__ uint4 tile_ld16(const uint8_t* tile, int row, int chunk) {
-  return *reinterpret_cast<const uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
 // Key range [lo, hi) visible to query token t (0-based among the new tokens).
 __device__ __forceinline__ void key_range(const Params& P, int t, int off, int len_k, int& lo, int& hi) {
   hi = min(len_k, t + off + 1);
   lo = P.window > 0 ? max(0, t + off - P.window) : 0;
 }
 
-// Q rows g and g+8 of this warp, dims [32c, 32c+32), as the A operand of the score MMA:
-// qa[4s + 0/1] = row g / g+8, dims 32c+4s+{0,1}; qa[4s + 2/3] = row g / g+8, dims 32c+4s+{2,3}.
-template <typename TQ>
-__device__ __forceinline__ void load_q(const Params& P, const TQ* q0, bool ok0, const TQ* q8, bool ok8,
-                                       uint32_t* qa) {
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const TQ* qp = half ? q8 : q0;
-    const bool ok = half ? ok8 : ok0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float f[8];
-      if (ok) {
-        unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * i), f);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = 0.f;
-      }
-      // dims 32c + 8i + e: k-steps s = 2i (e 0..3) and 2i+1 (e 4..7)
-      qa[4 * (2 * i) + half] = pack_half2(f[0], f[1]);
-      qa[4 * (2 * i) + 2 + half] = pack_half2(f[2], f[3]);
-      qa[4 * (2 * i + 1) + half] = pack_half2(f[4], f[5]);
-      qa[4 * (2 * i + 1) + 2 + half] = pack_half2(f[6], f[7]);
+// ======================= tensor-core (tcgen05) form =======================
+// One CTA per (128-row query block, KV head, sequence); the 128 rows are the TMEM lanes.
+// Roles (10 warps):
+//   warp 0      producer: lane 0 walks the block table, TMA-loads the e4m3 K and V rows of each
+//               64-key block (four 16-key page tiles each) into a staging ring;
+//   warp 1      MMA issuer (lane 0) and TMEM owner: S_j = Q . K_j^T (M 128, N 64, kind::f16) into
+//               one of two TMEM S buffers, then O += P_j . V_j (M 128, N 128) into the TMEM O;
+//   warps 2-5   converters: the query rows bf16/fp16 -> f16 once, then per block the staged e4m3
+//               K and V -> f16 operand tiles (128-byte swizzled; K read K-major, V MN-major, so
+//               neither needs a transpose);
+//   warps 6-9   softmax: thread = row; reads its 64 scores with tcgen05.ld, masks, one online-
+//               softmax step, rescales its O row in TMEM when the running max moved (after the
+//               previous P.V completed), writes its f16 probabilities as the A tile of the next
+//               P.V; finally normalises and stores its O row.
+// S_{j+1} is computed while the softmax works on S_j; P_j . V_j runs while the softmax works on
+// S_{j+1}.  Every wait is bounded (2 s) and ends the CTA's loops through a shared abort flag.
+namespace tc {
+constexpr int BM = 128;
+constexpr int BN = 64;
+constexpr int NSTG = 3;
+constexpr int NKV = 3;  // f16 K/V operand slots: the converters run up to NKV - 1 blocks ahead of P.V
+constexpr int NCONV = 4;
+constexpr int NSOFT = 4;
+constexpr int THREADS = (2 + NCONV + NSOFT) * 32;
+constexpr int Q_OFF = 0;                    // f16 Q [2 d-halves][128 rows][128 B]
+constexpr int KF_OFF = Q_OFF + 32768;         // f16 K, NKV slots x [2 d-halves][64 keys][128 B]
+constexpr int VF_OFF = KF_OFF + NKV * 16384;  // f16 V, NKV slots x [2 d-halves][64 keys][128 B]
+constexpr int P_OFF = VF_OFF + NKV * 16384;   // f16 P, 2 slots x [128 rows][64 keys = 128 B]
+constexpr int E_OFF = P_OFF + 2 * 16384;    // e4m3 staging, NSTG x (4 K page tiles + 4 V page tiles)
+constexpr int E_BYTES = 2 * 4 * TILE_BYTES;
+constexpr int BAR_OFF = E_OFF + NSTG * E_BYTES;
+constexpr int NBAR = 2 * NSTG + 2 * NKV + 4 + 3;
+constexpr int FLAG_OFF = BAR_OFF + NBAR * 8;  // page-tile flags: e_ok[NSTG], kv_ok[NKV] (bit i: tile i loaded)
+constexpr int SMEM = 1024 + FLAG_OFF + (NSTG + NKV) * 4 + 16;
+constexpr uint32_t TMEM_COLS = 256;  // O [0, 128), S buffers [128, 192) and [192, 256)
+constexpr float RESCALE_LOG2 = 8.f;  // move a row's reference max only when it grew by more than this
+constexpr uint32_t S_COL = 128;
+// instruction descriptors, kind::f16: D f32 (bit 4), A/B f16, M 128; P.V reads B (V) MN-major (bit 16)
+constexpr uint32_t IDESC_S = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 16) | ((uint32_t)(D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 16 consecutive fp32 columns of this thread's TMEM lane; the values are valid after tmem_wait_ld.
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// Wait for this thread's tcgen05.ld, then pin the 16 registers after the wait (an empty volatile
+// asm that redefines them), so no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+__device__ __forceinline__ void tmem_pin16(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes (or the hint
+// runs out) instead of spinning, so waiting roles leave the issue slots to the working ones.
+__device__ __forceinline__ bool try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(sm100::smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (2 s): gives up when another role aborted, or sets the abort flag and the error
+// code when the phase never completes.
+__device__ __forceinline__ bool wait_b(uint64_t* bar, uint32_t parity, volatile int* abort_v, unsigned int* err) {
+  if (try_wait_sleep(bar, parity)) return true;
+  const uint64_t t0 = sm100::globaltimer();
+  for (;;) {
+    if (try_wait_sleep(bar, parity)) return true;
+    if (*abort_v) return false;
+    if (sm100::globaltimer() - t0 > 2000000000ull) {
+      *abort_v = 1;
+      if (err) atomicOr(err, ERR_TILE_WAIT);
+      return false;
     }
   }
 }
 
+// Block-table entry of the 16-key tile starting at key0 of sequence b (-1 past the keys any
+// row of the block can see); tile_page turns it into the page id, or -1 for a hole.
+__device__ __forceinline__ int tile_entry(const Params& P, int b, int key0, int k_end) {
+  if (key0 >= k_end) return -1;
+  return __ldg(P.bt + (int64_t)b * P.bt_stride + key0 / P.page);
+}
+__device__ __forceinline__ int tile_page(const Params& P, int entry) {
+  return (entry < 0 || entry >= P.num_pages) ? -1 : entry;
+}
+
+// 16 e4m3 -> 16 f16 (two 16-byte chunks, element order kept).
+__device__ __forceinline__ void cvt16(const uint4& e, uint4& lo, uint4& hi) {
+  lo.x = e4m3x2_to_f16x2((uint16_t)(e.x & 0xFFFFu));
+  lo.y = e4m3x2_to_f16x2((uint16_t)(e.x >> 16));
+  lo.z = e4m3x2_to_f16x2((uint16_t)(e.y & 0xFFFFu));
+  lo.w = e4m3x2_to_f16x2((uint16_t)(e.y >> 16));
+  hi.x = e4m3x2_to_f16x2((uint16_t)(e.z & 0xFFFFu));
+  hi.y = e4m3x2_to_f16x2((uint16_t)(e.z >> 16));
+  hi.z = e4m3x2_to_f16x2((uint16_t)(e.w & 0xFFFFu));
+  hi.w = e4m3x2_to_f16x2((uint16_t)(e.w >> 16));
+}
+
 template <typename TQ, typename TO>
-__global__ void __launch_bounds__(THREADS, 2)
-    prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Params P) {
+__global__ void __launch_bounds__(THREADS, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Params P) {
   using namespace sm100;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, kvh = blockIdx.y;
   const int qblk = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  int* slot_ok = reinterpret_cast<int*>(empty + STAGES);
-  int* abort_flag = slot_ok + STAGES;
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = base + Q_OFF;
+  uint8_t* kf = base + KF_OFF;
+  uint8_t* vf = base + VF_OFF;
+  uint8_t* ps = base + P_OFF;
+  uint8_t* es = base + E_OFF;
+  uint64_t* e_full = reinterpret_cast<uint64_t*>(base + BAR_OFF);
+  uint64_t* e_empty = e_full + NSTG;
+  uint64_t* kv_full = e_empty + NSTG;
+  uint64_t* kv_empty = kv_full + NKV;
+  uint64_t* s_full = kv_empty + NKV;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* q_ready = o_done + 1;
+  uint64_t* fin = q_ready + 1;
+  int* e_ok = reinterpret_cast<int*>(base + FLAG_OFF);
+  int* kv_ok = e_ok + NSTG;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_ok + NKV);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_v = abort_flag;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], MMA_WARPS);
+    for (int s = 0; s < NSTG; ++s) {
+      mbar_init(&e_full[s], 1);
+      mbar_init(&e_empty[s], NCONV);
     }
+    for (int i = 0; i < NKV; ++i) {
+      mbar_init(&kv_full[i], NCONV);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], NSOFT);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(q_ready, NCONV);
+    mbar_init(fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
   pdl_wait();  // q, the cache pages and the metadata come from earlier kernels
   pdl_trigger();
 
   const int q_begin = __ldg(P.cu_q + b);
   const int len_q = __ldg(P.cu_q + b + 1) - q_begin;
   const int len_k = __ldg(P.cu_k + b + 1) - __ldg(P.cu_k + b);
-  const int t0 = qblk * P.qt;  // first query token of the block
-  if (t0 >= len_q) return;     // CTA-uniform, before any wait or load
-  const int t_last = min(t0 + P.qt, len_q) - 1;
+  const int t0 = qblk * P.qt;
+  const bool active = t0 < len_q;
   const int off = len_k - len_q;
-  // keys any row of the block can see; the table reaches max_pages * page keys at most
-  int k_lo, k_hi, dummy_lo, dummy_hi;
-  key_range(P, t0, off, len_k, k_lo, dummy_hi);
-  key_range(P, t_last, off, len_k, dummy_lo, k_hi);
-  k_hi = min(k_hi, P.max_pages * P.page);
-  const int kt0 = k_lo / TILE;
-  const int ntiles = k_hi > k_lo ? (k_hi + TILE - 1) / TILE - kt0 : 0;
+  int nblk = 0, kb0 = 0, k_end = 0;
+  if (active) {
+    const int t_last = min(t0 + P.qt, len_q) - 1;
+    int k_lo, k_hi, dlo, dhi;
+    key_range(P, t0, off, len_k, k_lo, dhi);
+    key_range(P, t_last, off, len_k, dlo, k_hi);
+    k_end = min(k_hi, P.max_pages * P.page);
+    kb0 = (k_lo / BN) * BN;
+    nblk = k_end > k_lo ? (k_end - kb0 + BN - 1) / BN : 0;
+  }
 
-  if (warp == MMA_WARPS) {  // ---------------- producer ----------------
+  if (warp == 0) {  // ---------------- producer ----------------
     if (lane == 0) {
       int issued = 0;
-      for (int i = 0; i < ntiles && !*abort_v; ++i) {
-        const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait_bounded(&empty[s], ((i / STAGES) - 1) & 1, abort_v, P.err, ERR_TILE_WAIT))
-          break;
+      int raw[4];  // block-table entries of block j, loaded one block ahead
+#pragma unroll
+      for (int i = 0; i < 4; ++i) raw[i] = nblk > 0 ? tile_entry(P, b, kb0 + TILE * i, k_end) : -1;
+      for (int j = 0; j < nblk && !*abort_v; ++j) {
+        const int s = j % NSTG;
+        if (j >= NSTG && !wait_b(&e_empty[s], ((j / NSTG) - 1) & 1, abort_v, P.err)) break;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const int key0 = (kt0 + i) * TILE;
-        const int page_idx = key0 / P.page;
-        int blk = __ldg(P.bt + (int64_t)b * P.bt_stride + page_idx);
-        if (blk < 0 || blk >= P.num_pages) blk = -1;
-        slot_ok[s] = blk >= 0;
-        if (blk >= 0) {
-          uint8_t* st = ring + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_4d(st, &tmk, &full[s], 0, kvh, key0 - page_idx * P.page, blk);
-          tma_load_4d(st + TILE_BYTES, &tmv, &full[s], 0, kvh, key0 - page_idx * P.page, blk);
-        } else {
-          mbar_arrive_plain(&full[s]);  // a hole in the block table: nothing to load
+        int blk[4];
+        uint32_t bytes = 0;
+        int mask = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          blk[i] = tile_page(P, raw[i]);
+          bytes += blk[i] >= 0 ? 2 * TILE_BYTES : 0;
+          mask |= (blk[i] >= 0 ? 1 : 0) << i;
         }
-        issued = i + 1;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) raw[i] = j + 1 < nblk ? tile_entry(P, b, kb0 + (j + 1) * BN + TILE * i, k_end) : -1;
+        e_ok[s] = mask;  // published by the arrive below (release), read after the phase completes
+        mbar_arrive_expect_tx(&e_full[s], bytes);
+        uint8_t* st = es + s * E_BYTES;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (blk[i] < 0) continue;
+          const int key0 = kb0 + j * BN + TILE * i;
+          const int row0 = key0 - (key0 / P.page) * P.page;
+          tma_load_4d(st + i * TILE_BYTES, &tmk, &e_full[s], 0, kvh, row0, blk[i]);
+          tma_load_4d(st + (4 + i) * TILE_BYTES, &tmv, &e_full[s], 0, kvh, row0, blk[i]);
+        }
+        issued = j + 1;
       }
       // leave no copy in flight when the CTA ends: wait (bounded) for the last use of each slot
-      for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) {
-        const int s = i % STAGES;
+      for (int j = issued > NSTG ? issued - NSTG : 0; j < issued; ++j) {
+        const int s = j % NSTG;
         uint32_t spins = 0;
         const uint64_t t_start = globaltimer();
-        while (!mbar_try_wait(&full[s], (i / STAGES) & 1)) {
+        while (!mbar_try_wait(&e_full[s], (j / NSTG) & 1)) {
           if ((++spins & 63u) == 0 && globaltimer() - t_start > 2000000000ull) {
             if (P.err) atomicOr(P.err, ERR_TILE_WAIT);
             break;
@@ -183,208 +316,281 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
       }
     }
-    return;
-  }
-
-  // ---------------- consumers: warps 0..3, rows 16 * warp + {g, g + 8} ----------------
-  const int g = lane >> 2, c = lane & 3;
-  const int r0 = 16 * warp + g, r8 = r0 + 8;
-  const int used = P.qt * P.group;  // rows past this are padding
-  const int tok0 = t0 + r0 / P.group, tok8 = t0 + r8 / P.group;
-  const bool ok0 = r0 < used && tok0 < len_q, ok8 = r8 < used && tok8 < len_q;
-  const int h0 = kvh * P.group + r0 % P.group, h8 = kvh * P.group + r8 % P.group;
-  int lo0, hi0, lo8, hi8;
-  key_range(P, tok0, off, len_k, lo0, hi0);
-  key_range(P, tok8, off, len_k, lo8, hi8);
-  if (!ok0) hi0 = lo0;  // padding rows see nothing
-  if (!ok8) hi8 = lo8;
-
-  const TQ* qbase = reinterpret_cast<const TQ*>(P.q);
-  uint32_t qa[32];
-  load_q<TQ>(P, qbase + (int64_t)(q_begin + tok0) * P.q_st + (int64_t)h0 * P.q_sh + 32 * c, ok0,
-             qbase + (int64_t)(q_begin + tok8) * P.q_st + (int64_t)h8 * P.q_sh + 32 * c, ok8, qa);
-
-  float o[16][4];
+  } else if (warp == 1) {  // ---------------- MMA issuer ----------------
+    if (lane == 0 && nblk > 0) {
+      const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(kf), v_addr = smem_u32(vf), p_addr = smem_u32(ps);
+      auto issue_s = [&](int j) {  // S_j = Q . K_j^T (K slot j % NKV) into S buffer j % 2
+        const uint32_t kb = (uint32_t)(j % NKV);
+        const uint32_t d = tmem + S_COL + BN * (uint32_t)(j & 1);
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m8 = -INFINITY, l0 = 0.f, l8 = 0.f;
-  const uint4 z = make_uint4(0, 0, 0, 0);
-
-  bool failed = false;
-  for (int i0 = 0; i0 < ntiles && !failed; i0 += KB) {
-    // ---- S = Q . K^T over KB tiles (64 keys): tile u, n-block j covers keys key0(u) + 8j .. +8
-    float sc[KB][2][4];
-    bool blk_ok[KB];
-#pragma unroll
-    for (int u = 0; u < KB; ++u) {
-      sc[u][0][0] = sc[u][0][1] = sc[u][0][2] = sc[u][0][3] = 0.f;
-      sc[u][1][0] = sc[u][1][1] = sc[u][1][2] = sc[u][1][3] = 0.f;
-      blk_ok[u] = false;
-      const int i = i0 + u;
-      if (i >= ntiles) continue;  // warp-uniform
-      const int s = i % STAGES;
-      // a wait that ran out marks the step failed; its (stale) tile is computed and discarded
-      if (!failed && !mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_v, P.err, ERR_TILE_WAIT)) failed = true;
-      blk_ok[u] = slot_ok[s] != 0;
-      const uint8_t* kt = ring + s * STAGE_BYTES;
-      uint4 kg[2], kg8[2];
-      kg[0] = tile_ld16(kt, g, 2 * c);
-      kg[1] = tile_ld16(kt, g, 2 * c + 1);
-      kg8[0] = tile_ld16(kt, g + 8, 2 * c);
-      kg8[1] = tile_ld16(kt, g + 8, 2 * c + 1);
-      const uint32_t* kw = reinterpret_cast<const uint32_t*>(kg);
-      const uint32_t* kw8 = reinterpret_cast<const uint32_t*>(kg8);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t b0[2], b1[2];
-        b0[0] = e4m3x2_to_f16x2((uint16_t)(kw[ks] & 0xFFFFu));
-        b0[1] = e4m3x2_to_f16x2((uint16_t)(kw[ks] >> 16));
-        b1[0] = e4m3x2_to_f16x2((uint16_t)(kw8[ks] & 0xFFFFu));
-        b1[1] = e4m3x2_to_f16x2((uint16_t)(kw8[ks] >> 16));
-        mma_16816_f16(sc[u][0], &qa[4 * ks], b0);
-        mma_16816_f16(sc[u][1], &qa[4 * ks], b1);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t hoff = (uint32_t)(kk / 4) * 16384u + (uint32_t)(kk % 4) * 32u;  // Q: 128 rows per half
+          const uint32_t koff = kb * 16384u + (uint32_t)(kk / 4) * 8192u + (uint32_t)(kk % 4) * 32u;
+          mma_f16(d, desc_kmajor_sw128(q_addr + hoff), desc_kmajor_sw128(k_addr + koff), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[j & 1]);
+      };
+      bool ok = wait_b(q_ready, 0, abort_v, P.err) && wait_b(&kv_full[0], 0, abort_v, P.err);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
       }
-    }
-    if (failed) break;
-
-    // ---- masks, one online-softmax step for the 64 keys (rows g: [..][0..1], rows g+8: [..][2..3])
-    float mx0 = -INFINITY, mx8 = -INFINITY;
+      for (int j = 0; ok && j < nblk; ++j) {
+        if (j + 1 < nblk) {
+          if (!wait_b(&kv_full[(j + 1) % NKV], ((j + 1) / NKV) & 1, abort_v, P.err)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!wait_b(&p_full[j & 1], (j >> 1) & 1, abort_v, P.err)) break;
+        tc_fence_after();
+        const uint32_t kb = (uint32_t)(j % NKV), pb = (uint32_t)(j & 1);
 #pragma unroll
-    for (int u = 0; u < KB; ++u) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = (kt0 + i0 + u) * TILE + 8 * j + 2 * c + e;
-          sc[u][j][e] = (blk_ok[u] && key >= lo0 && key < hi0) ? sc[u][j][e] * P.scale_log2 : -INFINITY;
-          sc[u][j][2 + e] = (blk_ok[u] && key >= lo8 && key < hi8) ? sc[u][j][2 + e] * P.scale_log2 : -INFINITY;
-          mx0 = fmaxf(mx0, sc[u][j][e]);
-          mx8 = fmaxf(mx8, sc[u][j][2 + e]);
+        for (int kk = 0; kk < BN / 16; ++kk) {  // O += P_j . V_j, 16 keys per MMA
+          const uint64_t pd = desc_kmajor_sw128(p_addr + pb * 16384u + (uint32_t)kk * 32u);
+          // V MN-major: d-halves 8 KB apart (leading), 8-key groups 1 KB apart (stride)
+          const uint64_t vd = smem_desc(v_addr + kb * 16384u + (uint32_t)kk * 16u * 128u, 8192, 1024, SWZ_128B);
+          mma_f16(tmem, pd, vd, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&kv_empty[kb]);
+        tc_commit(o_done);
+      }
+      // every MMA issued above has completed before the teardown
+      tc_commit(fin);
+      uint32_t spins = 0;
+      const uint64_t t_start = globaltimer();
+      while (!mbar_try_wait(fin, 0)) {
+        if ((++spins & 63u) == 0 && globaltimer() - t_start > 2000000000ull) {
+          if (P.err) atomicOr(P.err, ERR_TILE_WAIT);
+          break;
         }
       }
     }
-#pragma unroll
-    for (int sh = 1; sh < 4; sh <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
-      mx8 = fmaxf(mx8, __shfl_xor_sync(0xffffffffu, mx8, sh));
-    }
-    const float mn0 = fmaxf(m0, mx0), mn8 = fmaxf(m8, mx8);
-    const float al0 = mn0 != -INFINITY ? fast_exp2(m0 - mn0) : 1.f;
-    const float al8 = mn8 != -INFINITY ? fast_exp2(m8 - mn8) : 1.f;
-    const float sub0 = mn0 != -INFINITY ? mn0 : 0.f;  // exp2(-inf - 0) = 0 for a row with nothing yet
-    const float sub8 = mn8 != -INFINITY ? mn8 : 0.f;
-    m0 = mn0;
-    m8 = mn8;
-    float ps0 = 0.f, ps8 = 0.f;
-    uint32_t pa[KB][4];
-#pragma unroll
-    for (int u = 0; u < KB; ++u) {
-      float p[2][4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        p[j][0] = fast_exp2(sc[u][j][0] - sub0);
-        p[j][1] = fast_exp2(sc[u][j][1] - sub0);
-        p[j][2] = fast_exp2(sc[u][j][2] - sub8);
-        p[j][3] = fast_exp2(sc[u][j][3] - sub8);
-      }
-      // fp32 probabilities feed the row sums, fp16 ones feed P.V; the S accumulator layout is
-      // the A-operand layout of P . V (keys 2c.. in a0/a1, 2c+8.. in a2/a3)
-      ps0 += (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
-      ps8 += (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
-      pa[u][0] = pack_half2(p[0][0], p[0][1]);
-      pa[u][1] = pack_half2(p[0][2], p[0][3]);
-      pa[u][2] = pack_half2(p[1][0], p[1][1]);
-      pa[u][3] = pack_half2(p[1][2], p[1][3]);
-    }
-    l0 = l0 * al0 + ps0;
-    l8 = l8 * al8 + ps8;
-#pragma unroll
-    for (int nb = 0; nb < 16; ++nb) {
-      o[nb][0] *= al0;
-      o[nb][1] *= al0;
-      o[nb][2] *= al8;
-      o[nb][3] *= al8;
-    }
-
-    // ---- O += P . V, tile by tile; keys past len_k and holes may hold stale bytes (NaN in
-    // e4m3): their V rows are zeroed
-#pragma unroll
-    for (int u = 0; u < KB; ++u) {
-      const int i = i0 + u;
-      if (i >= ntiles) continue;  // warp-uniform
-      const int s = i % STAGES;
-      const uint8_t* vt = ring + s * STAGE_BYTES + TILE_BYTES;
-      const int key0 = (kt0 + i) * TILE;
-      uint4 vv[4];
-      const int vk[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vv[e] = (blk_ok[u] && key0 + vk[e] < len_k) ? tile_ld16(vt, vk[e], g) : z;
-      const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0]);
-      const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1]);
-      const uint32_t* v8 = reinterpret_cast<const uint32_t*>(&vv[2]);
-      const uint32_t* v9 = reinterpret_cast<const uint32_t*>(&vv[3]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t sel = half ? 0x7362u : 0x5140u;
-          const uint32_t w01 = prmt(v0[j], v1[j], sel);  // dims 16g + 4j + 2half + {0, 1}, keys 2c, 2c+1
-          const uint32_t w89 = prmt(v8[j], v9[j], sel);  // same dims, keys 2c+8, 2c+9
-          uint32_t bv[2];
-          bv[0] = e4m3x2_to_f16x2((uint16_t)(w01 & 0xFFFFu));
-          bv[1] = e4m3x2_to_f16x2((uint16_t)(w89 & 0xFFFFu));
-          mma_16816_f16(o[4 * j + 2 * half], pa[u], bv);
-          bv[0] = e4m3x2_to_f16x2((uint16_t)(w01 >> 16));
-          bv[1] = e4m3x2_to_f16x2((uint16_t)(w89 >> 16));
-          mma_16816_f16(o[4 * j + 2 * half + 1], pa[u], bv);
+  } else if (warp < 2 + NCONV) {  // ---------------- converters ----------------
+    const int ct = threadIdx.x - 64;  // 0..127
+    if (active) {
+      // query rows -> f16 Q tile: row r = (token t0 + r / group, head r % group of KV head kvh)
+      const int r = ct;
+      const int tok = t0 + r / P.group;
+      const bool ok = r < P.qt * P.group && tok < len_q;
+      const TQ* qp = reinterpret_cast<const TQ*>(P.q) + (int64_t)(q_begin + tok) * P.q_st +
+                     (int64_t)(kvh * P.group + r % P.group) * P.q_sh;
+#pragma unroll 4
+      for (int c = 0; c < 16; ++c) {  // 8 elements per chunk
+        uint4 h = make_uint4(0, 0, 0, 0);
+        if (ok) {
+          float f[8];
+          unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * c), f);
+          h.x = pack_half2(f[0], f[1]);
+          h.y = pack_half2(f[2], f[3]);
+          h.z = pack_half2(f[4], f[5]);
+          h.w = pack_half2(f[6], f[7]);
         }
+        const int half = c >> 3, ch = c & 7;
+        *reinterpret_cast<uint4*>(qs + half * 16384 + r * 128 + ((ch ^ (r & 7)) << 4)) = h;
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive_plain(&empty[s]);  // this warp is done with the slot
+      if (lane == 0) mbar_arrive_plain(q_ready);
+    }
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j % NSTG, kb = j % NKV;
+      if (!wait_b(&e_full[s], (j / NSTG) & 1, abort_v, P.err)) break;
+      if (j >= NKV && !wait_b(&kv_empty[kb], ((j / NKV) - 1) & 1, abort_v, P.err)) break;
+      const uint8_t* st = es + s * E_BYTES;
+      const int mask = e_ok[s];
+      int blk_ok[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) blk_ok[i] = (mask >> i) & 1;
+      // 64 keys x 8 chunks of 16 e4m3 per operand: 4 units per thread for K, 4 for V
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int unit = ct + 128 * u;
+        const int key = unit >> 3, ch = unit & 7;
+        const int sub = key >> 4, row = key & 15;
+        const int half = ch >> 2;
+        const int c0 = ((ch & 3) * 2) ^ (key & 7), c1 = ((ch & 3) * 2 + 1) ^ (key & 7);
+        const bool kok = blk_ok[sub] != 0;
+        const bool vok = kok & (kb0 + j * BN + key < len_k);
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        // the staging slot is always in bounds: load, then select (no branch per unit)
+        uint4 ke = *reinterpret_cast<const uint4*>(st + sub * TILE_BYTES + row * 128 + ((ch ^ (row & 7)) << 4));
+        uint4 ve = *reinterpret_cast<const uint4*>(st + (4 + sub) * TILE_BYTES + row * 128 + ((ch ^ (row & 7)) << 4));
+        if (!kok) ke = z;
+        if (!vok) ve = z;
+        uint4 lo, hi;
+        cvt16(ke, lo, hi);
+        uint8_t* kd = kf + kb * 16384 + half * 8192 + key * 128;  // slot kb of NKV
+        *reinterpret_cast<uint4*>(kd + (c0 << 4)) = lo;
+        *reinterpret_cast<uint4*>(kd + (c1 << 4)) = hi;
+        cvt16(ve, lo, hi);
+        uint8_t* vd = vf + kb * 16384 + half * 8192 + key * 128;
+        *reinterpret_cast<uint4*>(vd + (c0 << 4)) = lo;
+        *reinterpret_cast<uint4*>(vd + (c1 << 4)) = hi;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        if (warp == 2) kv_ok[kb] = mask;  // for the softmax, published by this lane's arrive
+        mbar_arrive_plain(&kv_full[kb]);
+        mbar_arrive_plain(&e_empty[s]);
+      }
+    }
+  } else {  // ---------------- softmax + epilogue: thread = row ----------------
+    const int q4 = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = 32 * q4 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * q4) << 16);
+    const int tok = t0 + r / P.group;
+    const bool valid = active && r < P.qt * P.group && tok < len_q;
+    int lo = 0, hi = 0;
+    if (valid) key_range(P, tok, off, len_k, lo, hi);
+    float m = -INFINITY, l = 0.f;
+    bool failed = false;
+    for (int j = 0; j < nblk; ++j) {
+      const int sb = j & 1;
+      // warp-uniform outcome: the tcgen05.ld / st below are warp-collective
+      if (!__all_sync(0xffffffffu, wait_b(&s_full[sb], (j >> 1) & 1, abort_v, P.err))) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[64];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tmem_ld16_async(trow + S_COL + BN * sb + 16 * i, sr + 16 * i);
+      tmem_wait_ld16(sr);
+      tmem_pin16(sr + 16);
+      tmem_pin16(sr + 32);
+      tmem_pin16(sr + 48);
+      const int key_base = kb0 + j * BN;
+      // the page flags the converters stored with K/V slot j % NKV: S_j was computed from that
+      // slot, so its kv_full phase is complete (this wait returns at once and orders the read)
+      if (!__all_sync(0xffffffffu, wait_b(&kv_full[j % NKV], (j / NKV) & 1, abort_v, P.err))) {
+        failed = true;
+        break;
+      }
+      const int blk_ok = kv_ok[j % NKV];
+      // visible columns i of this block: [a, e) and a loaded page tile; a warp-uniform branch
+      // takes the unmasked form for blocks every row sees whole, and the mask is built with
+      // non-short-circuit operators (selects, no per-element branches)
+      const int a = lo - key_base, e = hi - key_base;
+      float x[64];
+      if (__all_sync(0xffffffffu, blk_ok == 15 && a <= 0 && e >= BN)) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i]) * P.scale_log2;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const bool vis = (i >= a) & (i < e) & (((blk_ok >> (i >> 4)) & 1) != 0);
+          x[i] = vis ? __uint_as_float(sr[i]) * P.scale_log2 : -INFINITY;
+        }
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; i += 4) {
+        mx0 = fmaxf(mx0, x[i]);
+        mx1 = fmaxf(mx1, x[i + 1]);
+        mx2 = fmaxf(mx2, x[i + 2]);
+        mx3 = fmaxf(mx3, x[i + 3]);
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      // The running max is the reference point of this row's O and l.  It is moved (and O, l
+      // rescaled by alpha) only when the block's max exceeds it by more than 2^RESCALE_LOG2, so
+      // the probabilities stay <= 2^8 (exact in fp16's range) and O / l is unchanged: the same
+      // reference point scales numerator and denominator.
+      float alpha = 1.f;
+      if (mx > m + RESCALE_LOG2 || (m == -INFINITY && mx != -INFINITY)) {
+        alpha = fast_exp2(m - mx);  // 0 when the row had no visible key yet
+        m = mx;
+      }
+      const float sub = m != -INFINITY ? m : 0.f;
+      float ps0 = 0.f, ps1 = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = fast_exp2(x[2 * i] - sub), p1 = fast_exp2(x[2 * i + 1] - sub);
+        ps0 += p0;  // fp32 probabilities feed the row sum, fp16 ones feed P.V
+        ps1 += p1;
+        pk[i] = pack_half2(p0, p1);
+      }
+      l = l * alpha + (ps0 + ps1);
+      if (j > 0) {  // P.V of the previous block has completed: O is stable, P slot sb is free
+        if (!__all_sync(0xffffffffu, wait_b(o_done, (j - 1) & 1, abort_v, P.err))) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        // warp-uniform rescale decision (tcgen05.ld / st are warp-collective)
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld16_async(trow + 16 * c, o);
+            tmem_wait_ld16(o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(trow + 16 * c, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      // probabilities as the A tile of P.V: row r, 64 keys = 128 B, 128-byte swizzle
+      uint8_t* prow = ps + sb * 16384 + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_plain(&p_full[sb]);
+    }
+    // ---- epilogue: O row / l -> out (dims 0..127 of head kvh * group + r % group)
+    if (!failed && nblk > 0) {
+      failed = !__all_sync(0xffffffffu, wait_b(o_done, (nblk - 1) & 1, abort_v, P.err));
+      tc_fence_after();
+    }
+    failed = __any_sync(0xffffffffu, failed || *abort_v != 0);
+    const float inv = (valid && l > 0.f && !failed) ? P.v_scale / l : 0.f;
+    TO* op = reinterpret_cast<TO*>(P.out) + (int64_t)(q_begin + tok) * P.o_st +
+             (int64_t)(kvh * P.group + r % P.group) * P.o_sh;
+#pragma unroll 1
+    for (int c = 0; c < D / 16; ++c) {
+      uint32_t o[16];
+      if (nblk > 0 && !failed) {
+        tmem_ld16_async(trow + 16 * c, o);
+        tmem_wait_ld16(o);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = 0u;
+      }
+      if (valid) {
+        float f[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(o[i]) * inv;
+        *reinterpret_cast<uint4*>(op + 16 * c) = pack8<TO>(f);
+        *reinterpret_cast<uint4*>(op + 16 * c + 8) = pack8<TO>(f + 8);
+      }
     }
   }
 
-  // ---- normalise and store: thread holds dims [32c, 32c+32) of rows g and g+8 ----
-#pragma unroll
-  for (int sh = 1; sh < 4; sh <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
-    l8 += __shfl_xor_sync(0xffffffffu, l8, sh);
-  }
-  failed = failed || *abort_v != 0;
-  const float inv0 = (l0 > 0.f && !failed) ? P.v_scale / l0 : 0.f;
-  const float inv8 = (l8 > 0.f && !failed) ? P.v_scale / l8 : 0.f;
-  TO* obase = reinterpret_cast<TO*>(P.out);
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const bool ok = half ? ok8 : ok0;
-    if (!ok) continue;
-    const float inv = half ? inv8 : inv0;
-    TO* op = obase + (int64_t)(q_begin + (half ? tok8 : tok0)) * P.o_st + (int64_t)(half ? h8 : h0) * P.o_sh + 32 * c;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {  // dims 32c + 8i .. +8: i < 2 from o[.][0/2] (nb = 8i..), else o[.][1/3]
-      float f[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int dd = 8 * i + e;  // 0..31
-        const int nb = dd & 15;
-        f[e] = o[nb][(dd >> 4) + 2 * half] * inv;
-      }
-      *reinterpret_cast<uint4*>(op + 8 * i) = pack8<TO>(f);
-    }
-  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 template <typename TQ, typename TO>
-inline bool smem_ready() {
+inline bool tc_smem_ready() {
   static bool done[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
   if (done[dev]) return true;
-  if (cudaFuncSetAttribute(prefill_kernel<TQ, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+  if (cudaFuncSetAttribute(prefill_tc_kernel<TQ, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) !=
+      cudaSuccess)
     return false;
   done[dev] = true;
   return true;
 }
+}  // namespace tc
 
 }  // namespace pf
 }  // namespace ada
@@ -410,7 +616,7 @@ extern "C" int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_strid
   if (head_dim != pf::D) return ADA_ERR_UNSUPPORTED;
   if (num_heads % num_kv_heads != 0) return ADA_ERR_INVALID_ARG;
   const int group = num_heads / num_kv_heads;
-  if (group > pf::ROWS) return ADA_ERR_UNSUPPORTED;
+  if (group > pf::tc::BM) return ADA_ERR_UNSUPPORTED;
   if (page_size % pf::TILE != 0) return ADA_ERR_UNSUPPORTED;
   if (window < 0 || bt_stride < max_pages || num_pages <= 0) return ADA_ERR_INVALID_ARG;
   if ((int64_t)max_pages * page_size > (1LL << 30)) return ADA_ERR_UNSUPPORTED;
@@ -434,7 +640,7 @@ extern "C" int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_strid
   P.cu_q = cu_seqlens_q;
   P.cu_k = cu_seqlens_k;
   P.group = group;
-  P.qt = pf::ROWS / group;
+  P.qt = pf::tc::BM / group;
   P.page = page_size;
   P.window = window;
   P.scale_log2 = scale * k_scale * pf::LOG2E;
@@ -454,10 +660,11 @@ extern "C" int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_strid
   if (qblocks > 0x7fffffff || num_kv_heads > 65535 || batch > 65535) return ADA_ERR_UNSUPPORTED;
   const dim3 grid((unsigned)qblocks, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define ADA_PF(TQ, TO)                                                                                  \
-  do {                                                                                                  \
-    if (!pf::smem_ready<TQ, TO>()) return ADA_ERR_CUDA;                                                 \
-    (void)ada::launch_k(pf::prefill_kernel<TQ, TO>, grid, dim3(pf::THREADS), pf::SMEM, st, tmk, tmv, P); \
+#define ADA_PF(TQ, TO)                                                                                        \
+  do {                                                                                                        \
+    if (!pf::tc::tc_smem_ready<TQ, TO>()) return ADA_ERR_CUDA;                                                \
+    (void)ada::launch_k(pf::tc::prefill_tc_kernel<TQ, TO>, grid, dim3(pf::tc::THREADS), pf::tc::SMEM, st, tmk, tmv, \
+                        P);                                                                                   \
   } while (0)
   if (q_dtype == ADA_DT_BF16) {
     if (out_dtype == ADA_DT_BF16) ADA_PF(__nv_bfloat16, __nv_bfloat16); else ADA_PF(__nv_bfloat16, __half);
