@@ -270,26 +270,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   if (warp == 0) {  // ---------------- producer ----------------
-    if (lane == 0) {
-      int issued = 0;
-      int raw[4];  // block-table entries of block j, loaded one block ahead
+    // The warp holds the block-table entries of 8 blocks (32 page tiles, one per lane) and the
+    // next 8 in flight, so no table load is waited for in the per-block path; lane 0 issues.
+    auto entry = [&](int t) { return tile_entry(P, b, kb0 + TILE * t, k_end); };
+    int cur = nblk > 0 ? entry(lane) : -1;
+    int nxt = nblk > 8 ? entry(32 + lane) : -1;
+    int issued = 0;
+    for (int j = 0; j < nblk; ++j) {
+      if (j > 0 && (j & 7) == 0) {
+        cur = nxt;
+        nxt = j + 8 < nblk ? entry(32 * (j / 8 + 1) + lane) : -1;
+      }
+      int blk[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) raw[i] = nblk > 0 ? tile_entry(P, b, kb0 + TILE * i, k_end) : -1;
-      for (int j = 0; j < nblk && !*abort_v; ++j) {
-        const int s = j % NSTG;
-        if (j >= NSTG && !wait_b(&e_empty[s], ((j / NSTG) - 1) & 1, abort_v, P.err)) break;
+      for (int i = 0; i < 4; ++i) blk[i] = tile_page(P, __shfl_sync(0xffffffffu, cur, 4 * (j & 7) + i));
+      const int s = j % NSTG;
+      int go = 1;
+      if (lane == 0) go = !*abort_v && (j < NSTG || wait_b(&e_empty[s], ((j / NSTG) - 1) & 1, abort_v, P.err));
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      if (lane == 0) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        int blk[4];
         uint32_t bytes = 0;
         int mask = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          blk[i] = tile_page(P, raw[i]);
           bytes += blk[i] >= 0 ? 2 * TILE_BYTES : 0;
           mask |= (blk[i] >= 0 ? 1 : 0) << i;
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) raw[i] = j + 1 < nblk ? tile_entry(P, b, kb0 + (j + 1) * BN + TILE * i, k_end) : -1;
         e_ok[s] = mask;  // published by the arrive below (release), read after the phase completes
         mbar_arrive_expect_tx(&e_full[s], bytes);
         uint8_t* st = es + s * E_BYTES;
@@ -301,8 +308,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_4d(st + i * TILE_BYTES, &tmk, &e_full[s], 0, kvh, row0, blk[i]);
           tma_load_4d(st + (4 + i) * TILE_BYTES, &tmv, &e_full[s], 0, kvh, row0, blk[i]);
         }
-        issued = j + 1;
       }
+      issued = j + 1;
+    }
+    if (lane == 0) {
       // leave no copy in flight when the CTA ends: wait (bounded) for the last use of each slot
       for (int j = issued > NSTG ? issued - NSTG : 0; j < issued; ++j) {
         const int s = j % NSTG;
