@@ -16,9 +16,9 @@
 // statistics in fp32, probabilities rounded to fp16 for P.V, fp32 accumulation.  A row with no
 // visible key is written as zeros.
 //
-// Work split and roles: see the tcgen05 section below.  One CTA per (128-row query block, KV
-// head, sequence); the 128 rows are (token, head) pairs of the GQA group, head fastest, so
-// 128 / group consecutive query tokens share every K/V block the CTA loads (each e4m3 byte is
+// Work split and roles: see the tcgen05 section below.  One CTA per (256-row query block, KV
+// head, sequence); the 256 rows are (token, head) pairs of the GQA group, head fastest, so
+// 256 / group consecutive query tokens share every K/V block the CTA loads (each e4m3 byte is
 // read once per query block, not once per head).  S = Q . K^T and O += P . V run on the
 // 5th-generation tensor cores (tcgen05.mma kind::f16, f16 operands staged in shared memory,
 // fp32 accumulators in TMEM); the e4m3 pages arrive by TMA (4-D tensor map over
@@ -60,42 +60,50 @@ __device__ __forceinline__ void key_range(const Params& P, int t, int off, int l
 }
 
 // ======================= tensor-core (tcgen05) form =======================
-// One CTA per (128-row query block, KV head, sequence); the 128 rows are the TMEM lanes.
-// Roles (10 warps):
-//   warp 0      producer: lane 0 walks the block table, TMA-loads the e4m3 K and V rows of each
-//               64-key block (four 16-key page tiles each) into a staging ring;
-//   warp 1      MMA issuer (lane 0) and TMEM owner: S_j = Q . K_j^T (M 128, N 64, kind::f16) into
-//               one of two TMEM S buffers, then O += P_j . V_j (M 128, N 128) into the TMEM O;
-//   warps 2-5   converters: the query rows bf16/fp16 -> f16 once, then per block the staged e4m3
-//               K and V -> f16 operand tiles (128-byte swizzled; K read K-major, V MN-major, so
-//               neither needs a transpose);
-//   warps 6-9   softmax: thread = row; reads its 64 scores with tcgen05.ld, masks, one online-
-//               softmax step, rescales its O row in TMEM when the running max moved (after the
-//               previous P.V completed), writes its f16 probabilities as the A tile of the next
-//               P.V; finally normalises and stores its O row.
-// S_{j+1} is computed while the softmax works on S_j; P_j . V_j runs while the softmax works on
-// S_{j+1}.  Every wait is bounded (2 s) and ends the CTA's loops through a shared abort flag.
+// One CTA per (256-row query block, KV head, sequence): two 128-row query tiles (the 128 rows
+// of a tile are the TMEM lanes) share every K/V block the CTA loads and widens.
+// Roles (14 warps):
+//   warp 0       producer: walks the block table (entries held in the warp's lanes 8 blocks
+//                ahead), lane 0 TMA-loads the e4m3 K and V rows of each 64-key block (four
+//                16-key page tiles) into a staging ring;
+//   warp 1       MMA issuer (lane 0) and TMEM owner: per block and tile t, S_t = Q_t . K^T
+//                (M 128, N 64, kind::f16) into one of tile t's two TMEM S buffers, then
+//                O_t += P_t . V (M 128, N 128) into tile t's TMEM O;
+//   warps 2-5    converters: the query rows bf16/fp16 -> f16 once, then per block the staged
+//                e4m3 K and V -> f16 operand tiles (128-byte swizzled; K read K-major, V
+//                MN-major, so neither needs a transpose);
+//   warps 6-9    softmax of tile 0, warps 10-13 softmax of tile 1: thread = row; reads its 64
+//                scores with tcgen05.ld, masks, one online-softmax step, rescales its O row in
+//                TMEM when its reference max moved (after the previous P.V completed), writes
+//                its f16 probabilities as the A tile of the next P.V; finally normalises and
+//                stores its O row.
+// S of block j + 1 is computed while the softmax warpgroups work on block j, and each tile's
+// P.V runs while its warpgroup works on the next block; the two warpgroups (two warps per
+// scheduler) hide each other's latency.  Every wait is bounded (2 s) and ends the CTA's loops
+// through a shared abort flag.
 namespace tc {
-constexpr int BM = 128;
+constexpr int NT = 2;    // 128-row query tiles per CTA, one softmax warpgroup each, sharing every K/V block
+constexpr int BM = 128;  // rows per tile = TMEM lanes
 constexpr int BN = 64;
-constexpr int NSTG = 3;
+constexpr int NSTG = 2;
 constexpr int NKV = 3;  // f16 K/V operand slots: the converters run up to NKV - 1 blocks ahead of P.V
 constexpr int NCONV = 4;
-constexpr int NSOFT = 4;
-constexpr int THREADS = (2 + NCONV + NSOFT) * 32;
-constexpr int Q_OFF = 0;                    // f16 Q [2 d-halves][128 rows][128 B]
-constexpr int KF_OFF = Q_OFF + 32768;         // f16 K, NKV slots x [2 d-halves][64 keys][128 B]
-constexpr int VF_OFF = KF_OFF + NKV * 16384;  // f16 V, NKV slots x [2 d-halves][64 keys][128 B]
-constexpr int P_OFF = VF_OFF + NKV * 16384;   // f16 P, 2 slots x [128 rows][64 keys = 128 B]
-constexpr int E_OFF = P_OFF + 2 * 16384;    // e4m3 staging, NSTG x (4 K page tiles + 4 V page tiles)
+constexpr int NSOFT = 4;  // warps per softmax warpgroup
+constexpr int THREADS = (2 + NCONV + NT * NSOFT) * 32;
+constexpr int Q_OFF = 0;                        // f16 Q, NT x [2 d-halves][128 rows][128 B]
+constexpr int KF_OFF = Q_OFF + NT * 32768;      // f16 K, NKV slots x [2 d-halves][64 keys][128 B]
+constexpr int VF_OFF = KF_OFF + NKV * 16384;    // f16 V, NKV slots x [2 d-halves][64 keys][128 B]
+constexpr int P_OFF = VF_OFF + NKV * 16384;     // f16 P, NT x [128 rows][64 keys = 128 B]
+constexpr int E_OFF = P_OFF + NT * 16384;       // e4m3 staging, NSTG x (4 K page tiles + 4 V page tiles)
 constexpr int E_BYTES = 2 * 4 * TILE_BYTES;
 constexpr int BAR_OFF = E_OFF + NSTG * E_BYTES;
-constexpr int NBAR = 2 * NSTG + 2 * NKV + 4 + 3;
+constexpr int NBAR = 2 * NSTG + 2 * NKV + 4 * NT + 2;
 constexpr int FLAG_OFF = BAR_OFF + NBAR * 8;  // page-tile flags: e_ok[NSTG], kv_ok[NKV] (bit i: tile i loaded)
 constexpr int SMEM = 1024 + FLAG_OFF + (NSTG + NKV) * 4 + 16;
-constexpr uint32_t TMEM_COLS = 256;  // O [0, 128), S buffers [128, 192) and [192, 256)
+constexpr uint32_t TMEM_COLS = 512;  // O of tile t at [128 t, +128); S buffer b of tile t at 256 + 128 t + 64 b
 constexpr float RESCALE_LOG2 = 8.f;  // move a row's reference max only when it grew by more than this
-constexpr uint32_t S_COL = 128;
+constexpr uint32_t S_COL = 256;
+static_assert(SMEM <= 232448, "shared memory per CTA");
 // instruction descriptors, kind::f16: D f32 (bit 4), A/B f16, M 128; P.V reads B (V) MN-major (bit 16)
 constexpr uint32_t IDESC_S = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 16) | ((uint32_t)(D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -214,10 +222,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* e_empty = e_full + NSTG;
   uint64_t* kv_full = e_empty + NSTG;
   uint64_t* kv_empty = kv_full + NKV;
-  uint64_t* s_full = kv_empty + NKV;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 2;
-  uint64_t* q_ready = o_done + 1;
+  uint64_t* s_full = kv_empty + NKV;  // [NT][2]
+  uint64_t* p_full = s_full + 2 * NT;  // [NT]
+  uint64_t* o_done = p_full + NT;      // [NT]
+  uint64_t* q_ready = o_done + NT;
   uint64_t* fin = q_ready + 1;
   int* e_ok = reinterpret_cast<int*>(base + FLAG_OFF);
   int* kv_ok = e_ok + NSTG;
@@ -234,11 +242,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&kv_full[i], NCONV);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], NSOFT);
+    for (int i = 0; i < 2 * NT; ++i) mbar_init(&s_full[i], 1);
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&p_full[t], NSOFT);
+      mbar_init(&o_done[t], 1);
     }
-    mbar_init(o_done, 1);
     mbar_init(q_ready, NCONV);
     mbar_init(fin, 1);
     *abort_flag = 0;
@@ -328,16 +336,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {  // ---------------- MMA issuer ----------------
     if (lane == 0 && nblk > 0) {
       const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(kf), v_addr = smem_u32(vf), p_addr = smem_u32(ps);
-      auto issue_s = [&](int j) {  // S_j = Q . K_j^T (K slot j % NKV) into S buffer j % 2
+      auto issue_s = [&](int j) {  // S_{t,j} = Q_t . K_j^T (K slot j % NKV) into S buffer j % 2 of tile t
         const uint32_t kb = (uint32_t)(j % NKV);
-        const uint32_t d = tmem + S_COL + BN * (uint32_t)(j & 1);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t hoff = (uint32_t)(kk / 4) * 16384u + (uint32_t)(kk % 4) * 32u;  // Q: 128 rows per half
-          const uint32_t koff = kb * 16384u + (uint32_t)(kk / 4) * 8192u + (uint32_t)(kk % 4) * 32u;
-          mma_f16(d, desc_kmajor_sw128(q_addr + hoff), desc_kmajor_sw128(k_addr + koff), IDESC_S, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < NT; ++t) {
+          const uint32_t d = tmem + S_COL + 128u * (uint32_t)t + BN * (uint32_t)(j & 1);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t hoff = (uint32_t)t * 32768u + (uint32_t)(kk / 4) * 16384u + (uint32_t)(kk % 4) * 32u;
+            const uint32_t koff = kb * 16384u + (uint32_t)(kk / 4) * 8192u + (uint32_t)(kk % 4) * 32u;
+            mma_f16(d, desc_kmajor_sw128(q_addr + hoff), desc_kmajor_sw128(k_addr + koff), IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[2 * t + (j & 1)]);
         }
-        tc_commit(&s_full[j & 1]);
       };
       bool ok = wait_b(q_ready, 0, abort_v, P.err) && wait_b(&kv_full[0], 0, abort_v, P.err);
       if (ok) {
@@ -350,18 +361,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           issue_s(j + 1);
         }
-        if (!wait_b(&p_full[j & 1], (j >> 1) & 1, abort_v, P.err)) break;
-        tc_fence_after();
-        const uint32_t kb = (uint32_t)(j % NKV), pb = (uint32_t)(j & 1);
+        const uint32_t kb = (uint32_t)(j % NKV);
+        bool pv_ok = true;
+        for (int t = 0; t < NT && pv_ok; ++t) {  // O_t += P_{t,j} . V_j, 16 keys per MMA
+          if (!wait_b(&p_full[t], j & 1, abort_v, P.err)) {
+            pv_ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {  // O += P_j . V_j, 16 keys per MMA
-          const uint64_t pd = desc_kmajor_sw128(p_addr + pb * 16384u + (uint32_t)kk * 32u);
-          // V MN-major: d-halves 8 KB apart (leading), 8-key groups 1 KB apart (stride)
-          const uint64_t vd = smem_desc(v_addr + kb * 16384u + (uint32_t)kk * 16u * 128u, 8192, 1024, SWZ_128B);
-          mma_f16(tmem, pd, vd, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t pd = desc_kmajor_sw128(p_addr + (uint32_t)t * 16384u + (uint32_t)kk * 32u);
+            // V MN-major: d-halves 8 KB apart (leading), 8-key groups 1 KB apart (stride)
+            const uint64_t vd = smem_desc(v_addr + kb * 16384u + (uint32_t)kk * 16u * 128u, 8192, 1024, SWZ_128B);
+            mma_f16(tmem + 128u * (uint32_t)t, pd, vd, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&o_done[t]);
         }
+        if (!pv_ok) break;
         tc_commit(&kv_empty[kb]);
-        tc_commit(o_done);
       }
       // every MMA issued above has completed before the teardown
       tc_commit(fin);
@@ -377,25 +395,29 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp < 2 + NCONV) {  // ---------------- converters ----------------
     const int ct = threadIdx.x - 64;  // 0..127
     if (active) {
-      // query rows -> f16 Q tile: row r = (token t0 + r / group, head r % group of KV head kvh)
-      const int r = ct;
-      const int tok = t0 + r / P.group;
-      const bool ok = r < P.qt * P.group && tok < len_q;
-      const TQ* qp = reinterpret_cast<const TQ*>(P.q) + (int64_t)(q_begin + tok) * P.q_st +
-                     (int64_t)(kvh * P.group + r % P.group) * P.q_sh;
+      // query rows -> f16 Q tiles: CTA row R = (token t0 + R / group, head R % group of KV head
+      // kvh) is row R % 128 of tile R / 128
+      for (int R = ct; R < NT * BM; R += NCONV * 32) {
+        const int r = R % BM;
+        const int tok = t0 + R / P.group;
+        const bool ok = R < P.qt * P.group && tok < len_q;
+        const TQ* qp = reinterpret_cast<const TQ*>(P.q) + (int64_t)(q_begin + tok) * P.q_st +
+                       (int64_t)(kvh * P.group + R % P.group) * P.q_sh;
+        uint8_t* qt = qs + (R / BM) * 32768;
 #pragma unroll 4
-      for (int c = 0; c < 16; ++c) {  // 8 elements per chunk
-        uint4 h = make_uint4(0, 0, 0, 0);
-        if (ok) {
-          float f[8];
-          unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * c), f);
-          h.x = pack_half2(f[0], f[1]);
-          h.y = pack_half2(f[2], f[3]);
-          h.z = pack_half2(f[4], f[5]);
-          h.w = pack_half2(f[6], f[7]);
+        for (int c = 0; c < 16; ++c) {  // 8 elements per chunk
+          uint4 h = make_uint4(0, 0, 0, 0);
+          if (ok) {
+            float f[8];
+            unpack8<TQ>(*reinterpret_cast<const uint4*>(qp + 8 * c), f);
+            h.x = pack_half2(f[0], f[1]);
+            h.y = pack_half2(f[2], f[3]);
+            h.z = pack_half2(f[4], f[5]);
+            h.w = pack_half2(f[6], f[7]);
+          }
+          const int half = c >> 3, ch = c & 7;
+          *reinterpret_cast<uint4*>(qt + half * 16384 + r * 128 + ((ch ^ (r & 7)) << 4)) = h;
         }
-        const int half = c >> 3, ch = c & 7;
-        *reinterpret_cast<uint4*>(qs + half * 16384 + r * 128 + ((ch ^ (r & 7)) << 4)) = h;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -444,12 +466,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_arrive_plain(&e_empty[s]);
       }
     }
-  } else {  // ---------------- softmax + epilogue: thread = row ----------------
+  } else {  // ---------------- softmax + epilogue: warpgroup t, thread = row r of tile t ----------------
+    const int t = (warp - 2 - NCONV) / NSOFT;
     const int q4 = warp & 3;  // TMEM lane quarter this warp may access
     const int r = 32 * q4 + lane;
+    const int R = t * BM + r;  // row of the CTA
     const uint32_t trow = tmem + ((uint32_t)(32 * q4) << 16);
-    const int tok = t0 + r / P.group;
-    const bool valid = active && r < P.qt * P.group && tok < len_q;
+    const uint32_t o_col = 128u * (uint32_t)t, s_col = S_COL + 128u * (uint32_t)t;
+    const int tok = t0 + R / P.group;
+    const bool valid = active && R < P.qt * P.group && tok < len_q;
     int lo = 0, hi = 0;
     if (valid) key_range(P, tok, off, len_k, lo, hi);
     float m = -INFINITY, l = 0.f;
@@ -457,14 +482,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < nblk; ++j) {
       const int sb = j & 1;
       // warp-uniform outcome: the tcgen05.ld / st below are warp-collective
-      if (!__all_sync(0xffffffffu, wait_b(&s_full[sb], (j >> 1) & 1, abort_v, P.err))) {
+      if (!__all_sync(0xffffffffu, wait_b(&s_full[2 * t + sb], (j >> 1) & 1, abort_v, P.err))) {
         failed = true;
         break;
       }
       tc_fence_after();
       uint32_t sr[64];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tmem_ld16_async(trow + S_COL + BN * sb + 16 * i, sr + 16 * i);
+      for (int i = 0; i < 4; ++i) tmem_ld16_async(trow + s_col + BN * sb + 16 * i, sr + 16 * i);
       tmem_wait_ld16(sr);
       tmem_pin16(sr + 16);
       tmem_pin16(sr + 32);
@@ -521,8 +546,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         pk[i] = pack_half2(p0, p1);
       }
       l = l * alpha + (ps0 + ps1);
-      if (j > 0) {  // P.V of the previous block has completed: O is stable, P slot sb is free
-        if (!__all_sync(0xffffffffu, wait_b(o_done, (j - 1) & 1, abort_v, P.err))) {
+      if (j > 0) {  // P.V of the previous block has completed: O is stable, the P tile is free
+        if (!__all_sync(0xffffffffu, wait_b(&o_done[t], (j - 1) & 1, abort_v, P.err))) {
           failed = true;
           break;
         }
@@ -532,17 +557,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < D / 16; ++c) {
             uint32_t o[16];
-            tmem_ld16_async(trow + 16 * c, o);
+            tmem_ld16_async(trow + o_col + 16 * c, o);
             tmem_wait_ld16(o);
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(trow + 16 * c, o);
+            tmem_st16(trow + o_col + 16 * c, o);
           }
           tmem_wait_st();
         }
       }
       // probabilities as the A tile of P.V: row r, 64 keys = 128 B, 128-byte swizzle
-      uint8_t* prow = ps + sb * 16384 + r * 128;
+      uint8_t* prow = ps + t * 16384 + r * 128;  // one P tile per query tile: P.V of block j - 1 has completed
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
@@ -550,22 +575,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_plain(&p_full[sb]);
+      if (lane == 0) mbar_arrive_plain(&p_full[t]);
     }
     // ---- epilogue: O row / l -> out (dims 0..127 of head kvh * group + r % group)
     if (!failed && nblk > 0) {
-      failed = !__all_sync(0xffffffffu, wait_b(o_done, (nblk - 1) & 1, abort_v, P.err));
+      failed = !__all_sync(0xffffffffu, wait_b(&o_done[t], (nblk - 1) & 1, abort_v, P.err));
       tc_fence_after();
     }
     failed = __any_sync(0xffffffffu, failed || *abort_v != 0);
     const float inv = (valid && l > 0.f && !failed) ? P.v_scale / l : 0.f;
     TO* op = reinterpret_cast<TO*>(P.out) + (int64_t)(q_begin + tok) * P.o_st +
-             (int64_t)(kvh * P.group + r % P.group) * P.o_sh;
+             (int64_t)(kvh * P.group + R % P.group) * P.o_sh;
 #pragma unroll 1
     for (int c = 0; c < D / 16; ++c) {
       uint32_t o[16];
       if (nblk > 0 && !failed) {
-        tmem_ld16_async(trow + 16 * c, o);
+        tmem_ld16_async(trow + o_col + 16 * c, o);
         tmem_wait_ld16(o);
       } else {
 #pragma unroll
@@ -625,7 +650,7 @@ extern "C" int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_strid
   if (head_dim != pf::D) return ADA_ERR_UNSUPPORTED;
   if (num_heads % num_kv_heads != 0) return ADA_ERR_INVALID_ARG;
   const int group = num_heads / num_kv_heads;
-  if (group > pf::tc::BM) return ADA_ERR_UNSUPPORTED;
+  if (group > pf::tc::NT * pf::tc::BM) return ADA_ERR_UNSUPPORTED;
   if (page_size % pf::TILE != 0) return ADA_ERR_UNSUPPORTED;
   if (window < 0 || bt_stride < max_pages || num_pages <= 0) return ADA_ERR_INVALID_ARG;
   if ((int64_t)max_pages * page_size > (1LL << 30)) return ADA_ERR_UNSUPPORTED;
@@ -649,7 +674,7 @@ extern "C" int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_strid
   P.cu_q = cu_seqlens_q;
   P.cu_k = cu_seqlens_k;
   P.group = group;
-  P.qt = pf::tc::BM / group;
+  P.qt = pf::tc::NT * pf::tc::BM / group;
   P.page = page_size;
   P.window = window;
   P.scale_log2 = scale * k_scale * pf::LOG2E;
