@@ -506,15 +506,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       // takes the unmasked form for blocks every row sees whole, and the mask is built with
       // non-short-circuit operators (selects, no per-element branches)
       const int a = lo - key_base, e = hi - key_base;
+      // raw scores (masked: -inf); the softmax scale (> 0) is applied inside the exponent's FFMA
       float x[64];
       if (__all_sync(0xffffffffu, blk_ok == 15 && a <= 0 && e >= BN)) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i]) * P.scale_log2;
+        for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           const bool vis = (i >= a) & (i < e) & (((blk_ok >> (i >> 4)) & 1) != 0);
-          x[i] = vis ? __uint_as_float(sr[i]) * P.scale_log2 : -INFINITY;
+          x[i] = vis ? __uint_as_float(sr[i]) : -INFINITY;
         }
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
@@ -525,7 +526,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         mx2 = fmaxf(mx2, x[i + 2]);
         mx3 = fmaxf(mx3, x[i + 3]);
       }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      const float c = P.scale_log2;
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
       // The running max is the reference point of this row's O and l.  It is moved (and O, l
       // rescaled by alpha) only when the block's max exceeds it by more than 2^RESCALE_LOG2, so
       // the probabilities stay <= 2^8 (exact in fp16's range) and O / l is unchanged: the same
@@ -540,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = fast_exp2(x[2 * i] - sub), p1 = fast_exp2(x[2 * i + 1] - sub);
+        const float p0 = fast_exp2(fmaf(x[2 * i], c, -sub)), p1 = fast_exp2(fmaf(x[2 * i + 1], c, -sub));
         ps0 += p0;  // fp32 probabilities feed the row sum, fp16 ones feed P.V
         ps1 += p1;
         pk[i] = pack_half2(p0, p1);
@@ -653,6 +655,7 @@ extern "C" int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_strid
   if (group > pf::tc::NT * pf::tc::BM) return ADA_ERR_UNSUPPORTED;
   if (page_size % pf::TILE != 0) return ADA_ERR_UNSUPPORTED;
   if (window < 0 || bt_stride < max_pages || num_pages <= 0) return ADA_ERR_INVALID_ARG;
+  if (!(scale * k_scale > 0.f)) return ADA_ERR_INVALID_ARG;  // the row max is taken on unscaled scores
   if ((int64_t)max_pages * page_size > (1LL << 30)) return ADA_ERR_UNSUPPORTED;
   if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) return ADA_ERR_ALIGNMENT;
   if ((kv_stride_page | kv_stride_tok | kv_stride_head) & 15) return ADA_ERR_ALIGNMENT;
