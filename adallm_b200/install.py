@@ -15,6 +15,9 @@ Replaces, by the same names and signatures:
   adallm.ops.activation.SiluAndMul.forward / GeluAndMul.forward                   (activation.py:11-26)
   adallm.runtime.model_runner.ModelRunner.fp8_decode_selftest (model_runner.py:171-232 imports the
       Triton kernel by name; the replacement runs the same zero-input smoke on this kernel)
+  adallm.infra.loader's post-load step (loader.py:129-162, called at the end of load_model): runs
+      the reference's step, then prepack_model() derives every NVFP4 weight's tensor-core
+      scale layout once at load
 and points this package's forward context at adallm.infra.context.get_context.
 
 Weight layout, loader and engine are untouched: NVFP4 parameters keep their
@@ -115,6 +118,19 @@ def install(terms: int | None = None) -> None:
             torch.cuda.synchronize()
 
         ref_runner.ModelRunner.fp8_decode_selftest = selftest
+    except Exception:
+        pass
+
+    try:  # load-time scale prepack, after the reference's own post-load step (loader.py:129-162)
+        import adallm.infra.loader as ref_loader
+        orig_post = getattr(ref_loader, "_adallm_ref_post_load", ref_loader._init_nvfp4_bcol_scales)
+        ref_loader._adallm_ref_post_load = orig_post
+
+        def post_load(model):
+            orig_post(model)
+            nvfp4_gemm.prepack_model(model)
+
+        ref_loader._init_nvfp4_bcol_scales = post_load
     except Exception:
         pass
 

@@ -69,6 +69,29 @@ def _cached_sf(w_scale: torch.Tensor, n: int, k: int, owner: torch.Tensor | None
     return sf
 
 
+def prepack_model(model) -> int:
+    """Load-time scale prepack for a loaded model (the reference's post-load step,
+    adallm/infra/loader.py:129-162, where weight_scale_col is derived): for every module whose
+    `weight` is NVFP4 (uint8 [N, K/2] on a GPU) with `weight_scale` [N, K/16], derive the MMA
+    scale-factor layout once and cache it on `weight_scale`, where nvfp4_linear looks it up, so
+    no forward pays for it.  Modules on the CPU or in another layout are skipped.  Returns the
+    number of weights prepacked."""
+    done = 0
+    for mod in model.modules():
+        w = getattr(mod, "weight", None)
+        s = getattr(mod, "weight_scale", None)
+        if not isinstance(w, torch.Tensor) or not isinstance(s, torch.Tensor):
+            continue
+        if w.dtype != torch.uint8 or w.dim() != 2 or s.dim() != 2 or not w.is_cuda or not s.is_cuda:
+            continue
+        n, k = int(w.shape[0]), int(w.shape[1]) * 2
+        if tuple(s.shape) != (n, k // 16) or k % 64:
+            continue
+        _cached_sf(s, n, k)
+        done += 1
+    return done
+
+
 def workspace_bytes(m: int, n: int, k: int, terms: int) -> int:
     return int(N.lib().ada_nvfp4_linear_workspace_size(m, n, k, terms))
 

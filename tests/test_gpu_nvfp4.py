@@ -174,6 +174,28 @@ def test_bias_fp16_and_leading_dims():
     assert rel_l2(y.reshape(m, n).float().cpu(), y_ref) < 1e-2
 
 
+def test_prepack_model_at_load_time():
+    """prepack_model derives the tensor-core scale layout of every NVFP4 module once; the
+    forward then reuses it (same result, no new prepack) and skips non-NVFP4 modules."""
+    from adallm_b200.nvfp4_gemm import prepack_model
+    d = dev()
+    n, k = 256, 512
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=13)
+    lin = torch.nn.Module()
+    lin.weight = torch.nn.Parameter(torch.from_numpy(packed).to(d), requires_grad=False)
+    lin.weight_scale = torch.nn.Parameter(torch.from_numpy(scale16).to(d), requires_grad=False)
+    lin.weight_scale_2 = torch.nn.Parameter(torch.tensor(s2, device=d), requires_grad=False)
+    model = torch.nn.Sequential(lin, torch.nn.Linear(4, 4).to(d))
+    assert prepack_model(model) == 1
+    cached = lin.weight_scale._ada_sf[1]
+    assert torch.equal(cached, prepack_scales(lin.weight_scale, n, k))
+    x = torch.randn((8, k), device=d, dtype=torch.bfloat16)
+    y = nvfp4_linear(x, lin.weight, lin.weight_scale, lin.weight_scale_2, None, None, 16)
+    assert lin.weight_scale._ada_sf[1] is cached  # the load-time layout was used, not rebuilt
+    y_ref = nv.linear_ref(x.float().cpu().numpy(), packed, scale16.astype(np.float32), s2)
+    assert rel_l2(y.float().cpu(), y_ref) < 1e-2
+
+
 def test_prepack_from_e4m3_bytes_matches_fp16():
     d = dev()
     n, k = 256, 512

@@ -111,3 +111,19 @@ def test_prefill_routing(ref, monkeypatch):
     finally:
         rc.reset_context()
         context.use_context_provider(None)
+
+
+def test_load_time_prepack_hook(ref, monkeypatch):
+    """After install(): the loader's post-load step runs the reference's step, then
+    prepack_model on the loaded model (recorded here; no CUDA)."""
+    import adallm.infra.loader as rl
+    import adallm_b200
+    from adallm_b200 import nvfp4_gemm, context
+    adallm_b200.install()
+    calls = []
+    monkeypatch.setattr(nvfp4_gemm, "prepack_model", lambda m: calls.append(m) or 0)
+    try:
+        rl._init_nvfp4_bcol_scales(type("M", (), {"modules": lambda self: iter(())})())
+        assert len(calls) == 1
+    finally:
+        context.use_context_provider(None)
