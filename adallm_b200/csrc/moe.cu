@@ -83,15 +83,22 @@ __global__ void __launch_bounds__(128) route_kernel(const T* __restrict__ logits
 }
 
 // One CTA per token, 8 hidden elements per thread and step.
+// With ids (expert parallelism): slots whose expert is outside [expert_base, expert_base +
+// num_local) belong to another rank and are skipped (their expert rows were not computed here).
 template <typename T>
 __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, int64_t ldy, const T* __restrict__ w,
-                                                      int topk, int hidden, T* __restrict__ out, int64_t ldo) {
+                                                      int topk, int hidden, T* __restrict__ out, int64_t ldo,
+                                                      const int32_t* __restrict__ ids, int expert_base, int num_local) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < topk; ++j) {
+      if (ids) {
+        const int e = __ldg(ids + (int64_t)t * topk + j) - expert_base;
+        if (e < 0 || e >= num_local) continue;
+      }
       const float wj = to_f32(w[(int64_t)t * topk + j]);
       float v[8];
       unpack8<T>(*reinterpret_cast<const uint4*>(y + ((int64_t)t * topk + j) * ldy + c), v);
@@ -128,8 +135,9 @@ extern "C" int ada_moe_route_topk(const void* logits, int dtype, int64_t ld, int
   return ADA_OK;
 }
 
-extern "C" int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void* weights, int64_t tokens,
-                               int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream) {
+static int combine_impl(const void* y, int dtype, int64_t ldy, const void* weights, const int32_t* ids,
+                        int32_t expert_base, int32_t num_local, int64_t tokens, int32_t topk, int32_t hidden,
+                        void* out, int64_t ldo, void* stream) {
   if (tokens < 0 || topk <= 0 || hidden <= 0 || ldy < hidden || ldo < hidden) return ADA_ERR_INVALID_ARG;
   if (tokens == 0) return ADA_OK;
   if (!y || !weights || !out) return ADA_ERR_INVALID_ARG;
@@ -139,12 +147,26 @@ extern "C" int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void
   if (dtype == ADA_DT_BF16)
     (void)launch_k(moe::combine_kernel<__nv_bfloat16>, dim3((unsigned)tokens), dim3(256), 0, st,
                    (const __nv_bfloat16*)y, ldy, (const __nv_bfloat16*)weights, (int)topk, (int)hidden,
-                   (__nv_bfloat16*)out, ldo);
+                   (__nv_bfloat16*)out, ldo, ids, (int)expert_base, (int)num_local);
   else if (dtype == ADA_DT_F16)
     (void)launch_k(moe::combine_kernel<__half>, dim3((unsigned)tokens), dim3(256), 0, st, (const __half*)y, ldy,
-                   (const __half*)weights, (int)topk, (int)hidden, (__half*)out, ldo);
+                   (const __half*)weights, (int)topk, (int)hidden, (__half*)out, ldo, ids, (int)expert_base,
+                   (int)num_local);
   else
     return ADA_ERR_INVALID_ARG;
   ADA_CHECK_LAUNCH();
   return ADA_OK;
+}
+
+extern "C" int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void* weights, int64_t tokens,
+                               int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream) {
+  return combine_impl(y, dtype, ldy, weights, nullptr, 0, 0, tokens, topk, hidden, out, ldo, stream);
+}
+
+extern "C" int ada_moe_combine_ep(const void* y, int dtype, int64_t ldy, const void* weights,
+                                  const int32_t* expert_ids, int32_t expert_base, int32_t num_local, int64_t tokens,
+                                  int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream) {
+  if (!expert_ids || expert_base < 0 || num_local <= 0) return ADA_ERR_INVALID_ARG;
+  return combine_impl(y, dtype, ldy, weights, expert_ids, expert_base, num_local, tokens, topk, hidden, out, ldo,
+                      stream);
 }

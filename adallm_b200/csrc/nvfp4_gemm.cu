@@ -920,8 +920,12 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
 constexpr int GROUP_BN = 16;
 constexpr unsigned int ERR_EXPERT_ID = 0x60;
 
+// Expert parallelism: ids in [expert_base, expert_base + experts) are this rank's experts (local
+// index id - expert_base); with strict == 0 every other id is another rank's and its row is
+// skipped (output row untouched), with strict == 1 it is an error.
 __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__ ids, int m, int experts, int t_max,
-                                                     int* tile_expert, int* row_map, unsigned int* err) {
+                                                     int* tile_expert, int* row_map, unsigned int* err,
+                                                     int expert_base, int strict) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ int route_smem[];
@@ -933,10 +937,10 @@ __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__
   for (int r = threadIdx.x; r < t_max * GROUP_BN; r += blockDim.x) row_map[r] = -1;
   __syncthreads();
   for (int r = threadIdx.x; r < m; r += blockDim.x) {
-    const int e = __ldg(ids + r);
+    const int e = __ldg(ids + r) - expert_base;
     if (e >= 0 && e < experts)
       atomicAdd(&cnt[e], 1);
-    else
+    else if (strict)
       atomicExch(err, ERR_EXPERT_ID);
   }
   __syncthreads();
@@ -951,7 +955,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__
   for (int e = threadIdx.x; e < experts; e += blockDim.x)
     for (int t = 0; t < (cnt[e] + GROUP_BN - 1) / GROUP_BN; ++t) tile_expert[base[e] + t] = e;
   for (int r = threadIdx.x; r < m; r += blockDim.x) {
-    const int e = __ldg(ids + r);
+    const int e = __ldg(ids + r) - expert_base;
     if (e < 0 || e >= experts) continue;
     row_map[base[e] * GROUP_BN + atomicAdd(&fill[e], 1)] = r;
   }
@@ -1039,11 +1043,11 @@ extern "C" size_t ada_nvfp4_linear_grouped_workspace_size(int64_t m, int64_t n, 
   return grouped_plan(m, n, k, terms, num_experts, P, off, total) == ADA_OK ? total : 0;
 }
 
-extern "C" int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
-                                        const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
-                                        const float* w_scale_2, int32_t num_experts, int64_t n,
-                                        const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy, int terms,
-                                        void* workspace, size_t workspace_bytes, void* stream) {
+static int linear_grouped_impl(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                               const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w, const float* w_scale_2,
+                               int32_t num_experts, int64_t n, const int32_t* expert_ids, void* y, int y_dtype,
+                               int64_t ldy, int terms, void* workspace, size_t workspace_bytes, void* stream,
+                               int32_t expert_base, int strict) {
   if (m == 0) return ADA_OK;
   if (!x || !w_packed || !sf_w || !w_scale_2 || !expert_ids || !y || !workspace) return ADA_ERR_INVALID_ARG;
   if ((x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16) || (y_dtype != ADA_DT_BF16 && y_dtype != ADA_DT_F16))
@@ -1069,7 +1073,7 @@ extern "C" int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx,
       cudaFuncSetAttribute(fp4::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem) != cudaSuccess)
     return ADA_ERR_CUDA;
   (void)launch_k(fp4::route_kernel, dim3(1), dim3(1024), rsmem, st, expert_ids, (int)m, (int)num_experts, t_max,
-                 tile_expert, row_map, err);
+                 tile_expert, row_map, err, (int)expert_base, strict);
   ADA_CHECK_LAUNCH();
   const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
   rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, row_map);
@@ -1078,6 +1082,25 @@ extern "C" int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx,
   return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, y,
                        y_dtype, ldy, err, st, nullptr, 0, 0, 1, 0, nullptr, nullptr, 0, 0, tile_expert, row_map,
                        (int64_t)num_experts * n);
+}
+
+extern "C" int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                        const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                        const float* w_scale_2, int32_t num_experts, int64_t n,
+                                        const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy, int terms,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  return linear_grouped_impl(x, x_dtype, ldx, m, k, w_packed, ldw, sf_w, w_scale_2, num_experts, n, expert_ids, y,
+                             y_dtype, ldy, terms, workspace, workspace_bytes, stream, 0, 1);
+}
+
+extern "C" int ada_nvfp4_linear_grouped_ep(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                           const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                           const float* w_scale_2, int32_t num_experts, int32_t expert_base,
+                                           int64_t n, const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy,
+                                           int terms, void* workspace, size_t workspace_bytes, void* stream) {
+  if (expert_base < 0) return ADA_ERR_INVALID_ARG;
+  return linear_grouped_impl(x, x_dtype, ldx, m, k, w_packed, ldw, sf_w, w_scale_2, num_experts, n, expert_ids, y,
+                             y_dtype, ldy, terms, workspace, workspace_bytes, stream, expert_base, 0);
 }
 
 extern "C" int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,

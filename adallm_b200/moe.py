@@ -4,6 +4,10 @@
     ids, w = route_topk(router_logits, top_k, norm_topk_prob)   # softmax fp32, top-k, renormalise
     h = nvfp4_linear_gather(x.repeat_interleave(top_k, 0), ...)  # grouped NVFP4 GEMM per routed row
     out = combine(h, w, top_k)                                   # sum of the k expert rows, weighted
+
+Expert parallelism (beyond the reference, which runs MoE at TP = 1 only, qwen3.py:1383): each
+rank holds a contiguous block of experts (expert_shard), moe_block_ep computes that block's
+share and sums the ranks' shares with one all-reduce.
 """
 from __future__ import annotations
 
@@ -27,15 +31,61 @@ def route_topk(router_logits: torch.Tensor, top_k: int, norm_topk_prob: bool = T
     return ids, w
 
 
-def combine(expert_out: torch.Tensor, weights: torch.Tensor, top_k: int) -> torch.Tensor:
-    """[T * top_k, H] expert rows (row t*top_k + j = token t's j-th expert) -> [T, H]."""
+def combine(expert_out: torch.Tensor, weights: torch.Tensor, top_k: int, expert_ids: torch.Tensor | None = None,
+            expert_base: int = 0, num_local: int | None = None) -> torch.Tensor:
+    """[T * top_k, H] expert rows (row t*top_k + j = token t's j-th expert) -> [T, H].
+
+    With expert_ids (expert parallelism) only the slots whose expert is in
+    [expert_base, expert_base + num_local) are summed: this rank's share of the block output."""
     N.require_cuda(expert_out, weights, what="moe combine")
     y = expert_out if expert_out.stride(-1) == 1 else expert_out.contiguous()
     rows, h = y.shape
     t = rows // top_k
     w = weights.to(y.dtype).reshape(-1).contiguous()
     out = torch.empty((t, h), dtype=y.dtype, device=y.device)
-    st = N.lib().ada_moe_combine(y.data_ptr(), N.DT[y.dtype], y.stride(0), w.data_ptr(), t, top_k, h, out.data_ptr(),
-                                 out.stride(0), N.stream_ptr(y.device))
+    if expert_ids is None:
+        st = N.lib().ada_moe_combine(y.data_ptr(), N.DT[y.dtype], y.stride(0), w.data_ptr(), t, top_k, h,
+                                     out.data_ptr(), out.stride(0), N.stream_ptr(y.device))
+    else:
+        ids = expert_ids.to(device=y.device, dtype=torch.int32).reshape(-1).contiguous()
+        if ids.numel() != t * top_k or num_local is None:
+            raise ValueError("expert_ids must have top_k entries per token, and num_local must be given")
+        st = N.lib().ada_moe_combine_ep(y.data_ptr(), N.DT[y.dtype], y.stride(0), w.data_ptr(), ids.data_ptr(),
+                                        int(expert_base), int(num_local), t, top_k, h, out.data_ptr(), out.stride(0),
+                                        N.stream_ptr(y.device))
     N.check(st, "moe combine")
+    return out
+
+
+def expert_shard(num_experts: int, world: int, rank: int) -> tuple[int, int]:
+    """(first expert, expert count) of `rank` when num_experts are split over `world` ranks in
+    contiguous, equal blocks (num_experts must divide evenly)."""
+    if world <= 0 or not 0 <= rank < world or num_experts % world:
+        raise ValueError("experts must split evenly over the ranks")
+    per = num_experts // world
+    return rank * per, per
+
+
+def moe_block_ep(x: torch.Tensor, router_logits: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                 gate_up: tuple, down: tuple, expert_base: int, group=None) -> torch.Tensor:
+    """One MoE block with this rank's experts: route (the same on every rank), the grouped gate+up
+    GEMM over the rows routed here, SiLU(gate) * up, the grouped down GEMM, the weighted sum of the
+    local slots, then (with a process group) the sum over the ranks.
+
+    x [T, H]; router_logits [T, E_total]; gate_up = (packed [E, 2I, H/2], scale [E, 2I, H/16],
+    scale_2 [E]) with gate rows first; down = (packed [E, H, I/2], scale [E, H, I/16], scale_2 [E]);
+    E = this rank's experts, starting at expert_base."""
+    from .activation import gated_act
+    from .nvfp4_gemm import nvfp4_linear_gather
+    ids, w = route_topk(router_logits, top_k, norm_topk_prob)
+    flat = ids.reshape(-1)
+    xr = x.repeat_interleave(top_k, 0)
+    h = nvfp4_linear_gather(xr, gate_up[0], gate_up[1], gate_up[2], flat, 16, expert_base=expert_base)
+    # rows routed to other ranks hold stale values; the down GEMM and the combine never read them
+    a = gated_act(h, 0)
+    y = nvfp4_linear_gather(a, down[0], down[1], down[2], flat, 16, expert_base=expert_base)
+    out = combine(y, w, top_k, expert_ids=ids, expert_base=expert_base, num_local=gate_up[0].shape[0])
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(out, group=group)
     return out

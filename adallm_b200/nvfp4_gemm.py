@@ -171,11 +171,16 @@ def nvfp4_linear_dual(x, w1_packed, w1_scale, w1_scale_2, w2_packed, w2_scale, w
     return y1, y2
 
 
-def nvfp4_linear_gather(x, w_packed, w_scale, w_scale_2, expert_ids, group_size, terms: int | None = None):
+def nvfp4_linear_gather(x, w_packed, w_scale, w_scale_2, expert_ids, group_size, terms: int | None = None,
+                        expert_base: int | None = None):
     """Row m uses expert expert_ids[m] (adallm/ops/nvfp4_gemm.py:657-714).  One grouped
     tensor-core GEMM on the device (ada_nvfp4_linear_grouped): a routing kernel gives every
     expert whole 16-row operand tiles, the quantiser gathers the rows into them and the GEMM
-    streams only the weights of the experts in use.  No host synchronisation: graph-capturable."""
+    streams only the weights of the experts in use.  No host synchronisation: graph-capturable.
+
+    expert_base (expert parallelism): w_packed / w_scale / w_scale_2 hold this rank's experts
+    [expert_base, expert_base + E); rows routed elsewhere are skipped and their output rows are
+    left unwritten (ada_nvfp4_linear_grouped_ep)."""
     if not x.is_cuda:
         raise RuntimeError("nvfp4_linear_gather requires CUDA tensors")
     if group_size != 16:
@@ -205,8 +210,15 @@ def nvfp4_linear_gather(x, w_packed, w_scale, w_scale_2, expert_ids, group_size,
     if need == 0:
         raise ValueError(f"nvfp4_linear_gather: unsupported shape M={m} N={n} K={k} E={e}")
     ws = _workspace(x.device, need)
-    st = N.lib().ada_nvfp4_linear_grouped(x2.data_ptr(), N.DT[dt], x2.stride(0), m, k, wp.data_ptr(), wp.stride(1),
-                                          sf.data_ptr(), g2.data_ptr(), e, n, ids.data_ptr(), y.data_ptr(), N.DT[dt],
-                                          y.stride(0), t, ws.data_ptr(), ws.numel(), N.stream_ptr(x.device))
+    if expert_base is None:
+        st = N.lib().ada_nvfp4_linear_grouped(x2.data_ptr(), N.DT[dt], x2.stride(0), m, k, wp.data_ptr(),
+                                              wp.stride(1), sf.data_ptr(), g2.data_ptr(), e, n, ids.data_ptr(),
+                                              y.data_ptr(), N.DT[dt], y.stride(0), t, ws.data_ptr(), ws.numel(),
+                                              N.stream_ptr(x.device))
+    else:
+        st = N.lib().ada_nvfp4_linear_grouped_ep(x2.data_ptr(), N.DT[dt], x2.stride(0), m, k, wp.data_ptr(),
+                                                 wp.stride(1), sf.data_ptr(), g2.data_ptr(), e, int(expert_base), n,
+                                                 ids.data_ptr(), y.data_ptr(), N.DT[dt], y.stride(0), t,
+                                                 ws.data_ptr(), ws.numel(), N.stream_ptr(x.device))
     N.check(st, "NVFP4 grouped kernel")
     return y.to(x.dtype).view(*x.shape[:-1], n)

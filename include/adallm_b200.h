@@ -306,6 +306,21 @@ ADA_API int ada_moe_route_topk(const void* logits, int dtype, int64_t ld, int64_
                                int32_t topk, int32_t norm_topk_prob, int32_t* ids, void* weights, void* stream);
 ADA_API int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void* weights, int64_t tokens,
                             int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream);
+/* Expert parallelism (no reference counterpart: the reference runs MoE at TP = 1 only,
+ * qwen3.py:1383).  Each rank holds experts [expert_base, expert_base + num_local) of the model.
+ * ada_nvfp4_linear_grouped_ep is ada_nvfp4_linear_grouped over the rank's stacked local experts
+ * ([num_experts = num_local][n][k/2]): rows routed to another rank's expert are skipped (their
+ * output rows are left untouched), not an error.  ada_moe_combine_ep sums only the slots whose
+ * expert (expert_ids [tokens][topk]) is local; summing the ranks' outputs (all-reduce) gives
+ * the block's output. */
+ADA_API int ada_nvfp4_linear_grouped_ep(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                        const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                        const float* w_scale_2, int32_t num_experts, int32_t expert_base,
+                                        int64_t n, const int32_t* expert_ids, void* y, int y_dtype, int64_t ldy,
+                                        int terms, void* workspace, size_t workspace_bytes, void* stream);
+ADA_API int ada_moe_combine_ep(const void* y, int dtype, int64_t ldy, const void* weights,
+                               const int32_t* expert_ids, int32_t expert_base, int32_t num_local, int64_t tokens,
+                               int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream);
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by

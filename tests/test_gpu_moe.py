@@ -69,3 +69,51 @@ def test_moe_projection_end_to_end():
             wt = ws[idn[i, j]]
             ref[i] += wn[i, j] * nv.linear_ref(xr[i:i + 1], wt[0], wt[2].astype(np.float32), wt[3])[0]
     assert rel_l2(out.float().cpu(), torch.from_numpy(ref)) < 1e-2
+
+
+def _experts(e, n, k, seed):
+    ws = [random_weight(n, k, seed=seed + i, realistic=False) for i in range(e)]
+    d = dev()
+    return (torch.stack([torch.from_numpy(w[0]) for w in ws]).to(d),
+            torch.stack([torch.from_numpy(w[2]) for w in ws]).to(d),
+            torch.tensor([w[3] for w in ws], dtype=torch.float32, device=d)), ws
+
+
+def test_expert_parallel_block_sums_to_the_full_block():
+    """Experts split over two emulated ranks on one GPU (the all-reduce replaced by a sum of the
+    ranks' outputs): the sum equals the single-rank block, and both match the oracle (dequantised
+    weights, bf16 activations, SiLU(gate) * up, routing weights)."""
+    from adallm_b200.moe import expert_shard, moe_block_ep
+    d = dev()
+    t, e, k, hid, inter, world = 16, 16, 4, 512, 256, 2
+    gu, gu_np = _experts(e, 2 * inter, hid, 700)
+    dn, dn_np = _experts(e, hid, inter, 800)
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn((t, hid), generator=g).to(torch.bfloat16).to(d)
+    logits = torch.randn((t, e), generator=g).to(torch.bfloat16).to(d)
+    full = moe_block_ep(x, logits, k, True, gu, dn, 0)
+    parts = []
+    for r in range(world):
+        base, cnt = expert_shard(e, world, r)
+        sl = lambda p: tuple(a[base:base + cnt] for a in p)
+        parts.append(moe_block_ep(x, logits, k, True, sl(gu), sl(dn), base).float())
+    torch.cuda.synchronize()
+    summed = parts[0] + parts[1]
+    assert torch.isfinite(summed).all()
+    assert rel_l2(summed.cpu(), full.float().cpu()) < 1e-2
+    ids, w = route_topk(logits, k, True)
+    ids, w = ids.cpu().numpy(), w.float().cpu().numpy()
+    xr = x.float().cpu().numpy()
+    ref = np.zeros((t, hid), np.float32)
+    for i in range(t):
+        for j in range(k):
+            ex = int(ids[i, j])
+            a = gu_np[ex]
+            h = nv.linear_ref(xr[i:i + 1], a[0], a[2].astype(np.float32), a[3])
+            gate, up = h[:, :inter], h[:, inter:]
+            act = (gate / (1 + np.exp(-gate)) * up).astype(np.float32)
+            act = torch.from_numpy(act).to(torch.bfloat16).float().numpy()
+            b = dn_np[ex]
+            ref[i] += w[i, j] * nv.linear_ref(act, b[0], b[2].astype(np.float32), b[3])[0]
+    assert rel_l2(summed.cpu(), torch.from_numpy(ref)) < 2e-2
+    assert rel_l2(full.float().cpu(), torch.from_numpy(ref)) < 2e-2

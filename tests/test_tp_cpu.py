@@ -13,6 +13,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -109,3 +110,60 @@ def test_tensor_parallel_sharding_gloo_world2():
         assert "exception" not in errs, (rank, errs)
         assert errs["column"] < 1e-9 and errs["row"] < 1e-9, (rank, errs)
         assert errs["scale_2_shared"] == 0 and errs["embed"] == 0 and errs["pick"] == 0, (rank, errs)
+
+
+def _ep_rank(rank, world, port, q):
+    """Expert parallelism host logic on gloo: each rank owns a contiguous expert block and
+    contributes only the routed slots of its experts; the all-reduce of the shares equals the
+    full weighted sum."""
+    import os
+    import torch
+    import torch.distributed as dist
+    from adallm_b200.moe import expert_shard
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        e, t, k, h = 8, 5, 3, 4
+        g = torch.Generator().manual_seed(0)
+        ids = torch.stack([torch.randperm(e, generator=g)[:k] for _ in range(t)])
+        w = torch.rand((t, k), generator=g)
+        expert_out = torch.randn((e, t, h), generator=g)  # what expert x would give token t
+        base, cnt = expert_shard(e, world, rank)
+        mine = (ids >= base) & (ids < base + cnt)
+        share = torch.zeros((t, h))
+        for i in range(t):
+            for j in range(k):
+                if mine[i, j]:
+                    share[i] += w[i, j] * expert_out[ids[i, j], i]
+        dist.all_reduce(share)
+        full = torch.zeros((t, h))
+        for i in range(t):
+            for j in range(k):
+                full[i] += w[i, j] * expert_out[ids[i, j], i]
+        q.put((rank, float((share - full).abs().max())))
+        dist.destroy_process_group()
+    except Exception as exc:
+        q.put((rank, repr(exc)))
+
+
+def test_expert_parallel_shares_all_reduce_to_full_gloo():
+    import socket
+    import torch.multiprocessing as mp
+    from adallm_b200.moe import expert_shard
+    assert expert_shard(128, 8, 3) == (48, 16)
+    with pytest.raises(ValueError):
+        expert_shard(10, 4, 0)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert isinstance(res[r], float) and res[r] < 1e-5, res[r]
