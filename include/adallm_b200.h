@@ -135,8 +135,10 @@ ADA_API int ada_fp8_paged_decode_quant_ex(const void* q, int q_dtype, int64_t q_
  *          [i + len_k - len_q - W, i + len_k - len_q] (flash-attn's window_size = (W, 0))
  * out      [total_q, num_heads, head_dim] (out_dtype), strides out_stride_t / out_stride_h
  * err      optional uint32 word: 0x70 is OR-ed in if a tile load wait ran out (~2 s)
- * Implemented: head_dim 128, num_heads / num_kv_heads <= 64, page_size % 16 == 0.  Rows that
- * see no key are written as zeros.
+ * scale * k_scale must be > 0.
+ * Implemented: head_dim 128, num_heads / num_kv_heads <= 256, page_size % 16 == 0.  Rows that
+ * see no key are written as zeros.  One CTA per 256 (token, head) rows of a KV head uses
+ * 230 KB of shared memory and all 512 TMEM columns of its SM.
  * ---------------------------------------------------------------------- */
 ADA_API int ada_fp8_paged_prefill(const void* q, int q_dtype, int64_t q_stride_t, int64_t q_stride_h,
                                   const uint8_t* k_cache, const uint8_t* v_cache, int64_t kv_stride_page,
