@@ -3,6 +3,7 @@ Python code (tests/golden/make_golden.py)."""
 import os
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import nvfp4 as nv
@@ -117,6 +118,33 @@ def test_paged_decode_oracle_matches_gather_softmax():
             p = np.exp(s - s.max())
             p /= p.sum()
             np.testing.assert_allclose(out[b, h], p @ vs[:, h // 4], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("window", [0, 9])
+def test_paged_prefill_oracle_matches_gather_causal_softmax(window):
+    """The prefill oracle is the reference's gather (pinned above by golden_kv.npz) followed by
+    flash-attn's varlen causal attention as published: bottom-right aligned mask, window (W, 0).
+    Restated here with explicit loops over sequences, heads and query rows."""
+    case = oa.make_prefill_case(4, [0, 13, 40], [21, 1, 18], 8, 2, 32, 16)
+    out = oa.paged_prefill(case["q"], case["k"], case["v"], case["block_tables"], case["cu_q"], case["cu_k"],
+                           case["scale"], window)
+    kf = nv.e4m3_decode(case["k"]).astype(np.float16)
+    vf = nv.e4m3_decode(case["v"]).astype(np.float16)
+    len_k = np.diff(case["cu_k"])
+    k_out, v_out, cu = oa.gather_kv_from_blocks(kf, vf, case["block_tables"], len_k)
+    q16 = case["q"].astype(np.float16).astype(np.float64)
+    for b in range(3):
+        q0, lq = int(case["cu_q"][b]), int(case["cu_q"][b + 1] - case["cu_q"][b])
+        ks = k_out[cu[b]:cu[b + 1]].astype(np.float64)
+        vs = v_out[cu[b]:cu[b + 1]].astype(np.float64)
+        off = ks.shape[0] - lq
+        for h in range(8):
+            for i in range(lq):
+                lo = max(0, i + off - window) if window else 0
+                s = ks[lo:i + off + 1, h // 4] @ q16[q0 + i, h] * case["scale"]
+                p = np.exp(s - s.max())
+                p /= p.sum()
+                np.testing.assert_allclose(out[q0 + i, h], p @ vs[lo:i + off + 1, h // 4], rtol=1e-5, atol=1e-5)
 
 
 def test_act_terms_reconstruct():
