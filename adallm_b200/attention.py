@@ -93,6 +93,7 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     k_cache/v_cache [num_pages, page, Hkv, D] e4m3 holding every sequence's cached prefix and
     new tokens (store_kvcache runs first); block_tables int32 [B, max_pages] (-1 padded);
     cu_seqlens_q / cu_seqlens_k int32 [B + 1] (the reference's forward-context fields);
+    max_seqlen_q must be at least every sequence's new-token count (the grid is sized by it).
     window W > 0: query i sees keys [i + off - W, i + off], off = len_k - len_q.
     Returns [total_q, Hq, D] in q.dtype (the reference returns fp16 cast back to q.dtype).
     err: optional int32 [1] device word; 0x70 is OR-ed in if a tile wait ran out."""

@@ -129,7 +129,9 @@ ADA_API int ada_fp8_paged_decode_quant_ex(const void* q, int q_dtype, int64_t q_
  * cu_seqlens_q, cu_seqlens_k  int32 [batch + 1] (the reference's forward-context fields):
  *          len_k(b) = cu_seqlens_k[b+1] - cu_seqlens_k[b] keys, cached prefix + the new tokens,
  *          all already stored in the pages (store_kvcache runs first)
- * max_seqlen_q  max over b of len_q(b) (sizes the grid; larger is allowed)
+ * max_seqlen_q  max over b of len_q(b) (sizes the grid; larger is allowed; smaller leaves the
+ *          rows past it unwritten, which the kernel cannot detect without reading cu_seqlens_q
+ *          on the host)
  * k_cache, v_cache, block_tables, num_pages, page_size, k_scale, v_scale: as the decode entry
  * window   0 = causal only; W > 0: query i (0-based among the new tokens) sees keys
  *          [i + len_k - len_q - W, i + len_k - len_q] (flash-attn's window_size = (W, 0))
