@@ -199,21 +199,27 @@ __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restric
   quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch));
 }
 
-// grid (ctas, m_pad), cluster (ctas, 1, 1).  row_map (grouped operands): operand row m holds
-// input row row_map[m] (< 0: padding).
+// grid (ctas, m_pad), cluster (ctas, 1, 1): operand row m from input row m; rows past `rows`
+// are zero padding.  Grouped operands (dest != null): grid (ctas, rows), input row r goes to
+// operand row dest[r] (< 0: not routed here, nothing written); the operand rows no input row
+// maps to are left as they are, since the grouped GEMM discards their output columns.
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) act_quant_kernel(const T* __restrict__ x, int64_t ldx, int rows, int k,
-                                                        q::QuantDst dst, const int* row_map) {
+                                                        q::QuantDst dst, const int* dest) {
   __shared__ float red[cl::MAX_WARPS];
   __shared__ cl::Exchange xch;
   cl::cluster_start(&xch, 1);
   pdl_wait();
   pdl_trigger();
-  const int m = blockIdx.y;
-  const int src = row_map ? row_map[m] : m;
+  const int src = blockIdx.y;
+  const int m = dest ? dest[src] : src;
   int o0, o1;
   slice_of(k, o0, o1);
-  if (src < 0 || src >= rows) {
+  if (m < 0) {  // cluster-uniform: every CTA of the cluster has this row
+    cl::cluster_wait();
+    return;
+  }
+  if (src >= rows) {
     zero_slice(dst, m, o0, o1);
     cl::cluster_wait();
     return;
@@ -289,17 +295,17 @@ int launch_rmsnorm16(const void* x, int64_t ldx, const void* res, int64_t ldr, v
 
 // Quantise x [m, k] into the GEMM operand (prologue of ada_nvfp4_linear).
 int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
-                     cudaStream_t st, const int* row_map = nullptr) {
+                     cudaStream_t st, const int* dest = nullptr) {
   const cl::RowSplit sp = cl::row_split(dst.k / 16);
   if (!sp.maxu || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
-  const dim3 grid_((unsigned)sp.ctas, (unsigned)m_pad);
+  const dim3 grid_((unsigned)sp.ctas, (unsigned)(dest ? m : m_pad));
   cudaError_t err_;
   if (x_dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
-    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, row_map);
+    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, dest);
   } else {
     using TT = __half;
-    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, row_map);
+    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, dest);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }

@@ -923,8 +923,9 @@ constexpr unsigned int ERR_EXPERT_ID = 0x60;
 // Expert parallelism: ids in [expert_base, expert_base + experts) are this rank's experts (local
 // index id - expert_base); with strict == 0 every other id is another rank's and its row is
 // skipped (output row untouched), with strict == 1 it is an error.
+// dest[r]: the operand row of input row r (-1: another rank's expert), for the gathering quantiser.
 __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__ ids, int m, int experts, int t_max,
-                                                     int* tile_expert, int* row_map, unsigned int* err,
+                                                     int* tile_expert, int* row_map, int* dest, unsigned int* err,
                                                      int expert_base, int strict) {
   pdl_wait();
   pdl_trigger();
@@ -944,9 +945,34 @@ __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__
       atomicExch(err, ERR_EXPERT_ID);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {  // tiles per expert, prefix sum (experts is at most a few thousand)
-    int run = 0;
-    for (int e = 0; e < experts; ++e) {
+  {  // tiles per expert, exclusive prefix sum: each thread sums a run of up to 4 experts, then a
+     // scan over the warps' totals (experts <= 4096 = 4 x 1024 threads)
+    __shared__ int warp_tot[32];
+    const int per = (experts + 1023) / 1024;
+    const int e0 = threadIdx.x * per;
+    int local = 0;
+    for (int e = e0; e < e0 + per && e < experts; ++e) local += (cnt[e] + GROUP_BN - 1) / GROUP_BN;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int inc = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    if (lane == 31) warp_tot[wid] = inc;
+    __syncthreads();
+    if (wid == 0) {
+      int t = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += v;
+      }
+      warp_tot[lane] = t;  // inclusive totals of warps 0..lane
+    }
+    __syncthreads();
+    int run = inc - local + (wid > 0 ? warp_tot[wid - 1] : 0);
+    for (int e = e0; e < e0 + per && e < experts; ++e) {
       base[e] = run;
       run += (cnt[e] + GROUP_BN - 1) / GROUP_BN;
     }
@@ -956,8 +982,13 @@ __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__
     for (int t = 0; t < (cnt[e] + GROUP_BN - 1) / GROUP_BN; ++t) tile_expert[base[e] + t] = e;
   for (int r = threadIdx.x; r < m; r += blockDim.x) {
     const int e = __ldg(ids + r) - expert_base;
-    if (e < 0 || e >= experts) continue;
-    row_map[base[e] * GROUP_BN + atomicAdd(&fill[e], 1)] = r;
+    if (e < 0 || e >= experts) {
+      dest[r] = -1;
+      continue;
+    }
+    const int pos = base[e] * GROUP_BN + atomicAdd(&fill[e], 1);
+    row_map[pos] = r;
+    dest[r] = pos;
   }
 }
 
@@ -968,7 +999,7 @@ inline int64_t group_tiles(int64_t m, int64_t experts) { return cdiv(m, GROUP_BN
 
 namespace fused {
 int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
-                     cudaStream_t st, const int* row_map);
+                     cudaStream_t st, const int* dest);
 }
 }  // namespace ada
 
@@ -1032,7 +1063,7 @@ static int grouped_plan(int64_t m, int64_t n, int64_t k, int terms, int64_t expe
   const int rc = fp4::make_plan(t_max * fp4::GROUP_BN, n, k, terms, 1, P, false, fp4::GROUP_BN);
   if (rc != ADA_OK) return rc;
   off_route = (P.total + 255) & ~(size_t)255;
-  total = off_route + (size_t)(1 + t_max + t_max * fp4::GROUP_BN) * sizeof(int);
+  total = off_route + (size_t)(1 + t_max + t_max * fp4::GROUP_BN + m) * sizeof(int);
   return ADA_OK;
 }
 
@@ -1067,16 +1098,17 @@ static int linear_grouped_impl(const void* x, int x_dtype, int64_t ldx, int64_t 
   const int t_max = P.m_tiles;
   int* tile_expert = reinterpret_cast<int*>(ws + off_route) + 1;
   int* row_map = tile_expert + t_max;
+  int* dest = row_map + t_max * fp4::GROUP_BN;
   unsigned int* err = reinterpret_cast<unsigned int*>(ws);
   const size_t rsmem = (size_t)3 * num_experts * sizeof(int);
   if (rsmem > 48 * 1024 &&
       cudaFuncSetAttribute(fp4::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem) != cudaSuccess)
     return ADA_ERR_CUDA;
   (void)launch_k(fp4::route_kernel, dim3(1), dim3(1024), rsmem, st, expert_ids, (int)m, (int)num_experts, t_max,
-                 tile_expert, row_map, err, (int)expert_base, strict);
+                 tile_expert, row_map, dest, err, (int)expert_base, strict);
   ADA_CHECK_LAUNCH();
   const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
-  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, row_map);
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, dest);
   if (rc != ADA_OK) return rc;
   // the stacked weight matrix [num_experts * n, k / 2]: expert e's tile j is 128-row block e * (n / 128) + j
   return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, y,
