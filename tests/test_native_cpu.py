@@ -53,3 +53,37 @@ def test_argument_errors_are_reported_before_any_launch(built):
         N.check(N.ADA_ERR_ALIGNMENT, "x")
     with pytest.raises(RuntimeError, match="no fallback"):
         N.check(N.ADA_ERR_LAUNCH, "x")
+
+
+def test_prefill_and_expert_parallel_argument_errors(built):
+    """The entries added for the prefill attention and expert parallelism validate their
+    arguments before any CUDA call (pointers are placeholders, never dereferenced)."""
+    lib = N.lib()
+    P = 1 << 20  # 16-byte aligned placeholder address
+
+    def prefill(**kw):
+        a = dict(q=P, q_dtype=0, q_st=32 * 128, q_sh=128, k=P, v=P, s_page=16 * 8 * 128, s_tok=8 * 128, s_head=128,
+                 num_pages=64, bt=P, bt_stride=8, max_pages=8, cu_q=P, cu_k=P, batch=2, max_q=40, hq=32, hkv=8,
+                 d=128, page=16, scale=0.088, k_scale=1.0, v_scale=1.0, window=0, out=P, out_dtype=0,
+                 o_st=32 * 128, o_sh=128, err=None, stream=None)
+        a.update(kw)
+        return lib.ada_fp8_paged_prefill(*a.values())
+
+    assert prefill(d=64) == N.ADA_ERR_UNSUPPORTED            # head_dim 128 only
+    assert prefill(page=24) == N.ADA_ERR_UNSUPPORTED          # pages of whole 16-key tiles
+    assert prefill(hq=30) == N.ADA_ERR_INVALID_ARG            # GQA groups must divide
+    assert prefill(hq=512, hkv=1) == N.ADA_ERR_UNSUPPORTED    # at most 256 rows of a KV head per CTA
+    assert prefill(scale=0.0) == N.ADA_ERR_INVALID_ARG        # the row max is taken on unscaled scores
+    assert prefill(window=-1) == N.ADA_ERR_INVALID_ARG
+    assert prefill(q=P + 8) == N.ADA_ERR_ALIGNMENT
+    assert prefill(o_sh=100) == N.ADA_ERR_ALIGNMENT
+    assert prefill(batch=0) == 0 and prefill(max_q=0) == 0    # nothing to do
+    assert prefill(cu_q=None) == N.ADA_ERR_INVALID_ARG
+    # expert parallelism
+    st = lib.ada_moe_combine_ep(P, 0, 64, P, None, 0, 4, 2, 2, 64, P, 64, None)
+    assert st == N.ADA_ERR_INVALID_ARG                        # expert ids are required
+    st = lib.ada_moe_combine_ep(P, 0, 64, P, P, -1, 4, 2, 2, 64, P, 64, None)
+    assert st == N.ADA_ERR_INVALID_ARG
+    st = lib.ada_nvfp4_linear_grouped_ep(P, 0, 256, 8, 256, P, 128, P, P, 4, -1, 128, P, P, 0, 128, 4, P, 1 << 20,
+                                         None)
+    assert st == N.ADA_ERR_INVALID_ARG                        # negative expert base
