@@ -87,3 +87,16 @@ def test_prefill_and_expert_parallel_argument_errors(built):
     st = lib.ada_nvfp4_linear_grouped_ep(P, 0, 256, 8, 256, P, 128, P, P, 4, -1, 128, P, P, 0, 128, 4, P, 1 << 20,
                                          None)
     assert st == N.ADA_ERR_INVALID_ARG                        # negative expert base
+
+
+def test_prepack_model_skips_modules_off_the_gpu():
+    """prepack_model only touches NVFP4 weights on a GPU; CPU modules and other layouts are
+    skipped without any CUDA call."""
+    import torch
+    from adallm_b200.nvfp4_gemm import prepack_model
+    lin = torch.nn.Module()
+    lin.weight = torch.nn.Parameter(torch.zeros((128, 256), dtype=torch.uint8), requires_grad=False)
+    lin.weight_scale = torch.nn.Parameter(torch.zeros((128, 32), dtype=torch.float16), requires_grad=False)
+    model = torch.nn.Sequential(lin, torch.nn.Linear(4, 4))
+    assert prepack_model(model) == 0
+    assert not hasattr(lin.weight_scale, "_ada_sf")
