@@ -81,6 +81,20 @@ __device__ __forceinline__ void key_range(const Params& P, int t, int off, int l
 // P.V runs while its warpgroup works on the next block; the two warpgroups (two warps per
 // scheduler) hide each other's latency.  Every wait is bounded (2 s) and ends the CTA's loops
 // through a shared abort flag.
+//
+// Barriers (phase k of a barrier = its k-th completion; block j, tile t):
+//   e_full[j % NSTG]   producer arrive.expect_tx + TMA bytes -> converters   (phase j / NSTG)
+//   e_empty[j % NSTG]  4 converter warps -> producer, slot reusable           (phase j / NSTG)
+//   kv_full[j % NKV]   4 converter warps -> MMA (and softmax, page flags)     (phase j / NKV)
+//   kv_empty[j % NKV]  commit after both tiles' P.V of block j -> converters (phase j / NKV)
+//   s_full[t][j % 2]   commit after S_{t,j} -> softmax warpgroup t            (phase j / 2)
+//   p_full[t]          4 softmax warps of tile t -> MMA, P tile written       (phase j)
+//   o_done[t]          commit after P.V of tile t, block j -> softmax t       (phase j)
+//   q_ready            4 converter warps -> MMA, Q tiles written              (phase 0)
+//   fin                commit after the last MMA -> teardown                  (phase 0)
+// A barrier can run at most one phase ahead of any waiter: each refill of a slot waits for the
+// consumer's release of the previous use (e_empty, kv_empty; S buffers by p_full, the single P
+// tile by o_done of the previous block).
 namespace tc {
 constexpr int NT = 2;    // 128-row query tiles per CTA, one softmax warpgroup each, sharing every K/V block
 constexpr int BM = 128;  // rows per tile = TMEM lanes
