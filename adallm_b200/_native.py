@@ -137,6 +137,32 @@ def check(status: int, what: str) -> None:
     raise RuntimeError(f"{what} failed ({msg}); no fallback is allowed in this runtime.")
 
 
+# Codes the kernels OR into a device error word (a workspace's first 4 bytes) when a bounded
+# wait runs out (~2 s) or an input is out of range; the word stays set until the caller clears it.
+_ERROR_BITS = [(0x1, "GEMM producer waited for a free pipeline stage"),
+               (0x2, "GEMM MMA issuer waited for a loaded stage"),
+               (0x4, "GEMM epilogue waited for the accumulator"),
+               (0x8, "GEMM MMA issuer waited for a free accumulator")]
+_ERROR_CODES = {0x50: "a peer's partial planes never arrived (tensor-parallel inbox wait)",
+                0x60: "an expert id outside [0, num_experts)",
+                0x70: "a prefill attention tile load never completed"}
+
+
+def describe_error_word(code: int) -> str:
+    parts = [txt for bit, txt in _ERROR_BITS if code & bit]
+    hi = code & ~0xF
+    if hi:
+        parts.append(_ERROR_CODES.get(hi, f"code 0x{hi:x}"))
+    return "; ".join(parts) or "ok"
+
+
+def raise_on_error_word(code: int, what: str) -> None:
+    """Raise RuntimeError when a device error word is nonzero (the results it guards are not valid)."""
+    if code:
+        raise RuntimeError(f"{what}: device error word 0x{code:x} ({describe_error_word(code)}); "
+                           "the results of this call are not valid; no fallback is allowed in this runtime.")
+
+
 def stream_ptr(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

@@ -942,7 +942,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const int32_t* __restrict__
     if (e >= 0 && e < experts)
       atomicAdd(&cnt[e], 1);
     else if (strict)
-      atomicExch(err, ERR_EXPERT_ID);
+      atomicOr(err, ERR_EXPERT_ID);
   }
   __syncthreads();
   {  // tiles per expert, exclusive prefix sum: each thread sums a run of up to 4 experts, then a

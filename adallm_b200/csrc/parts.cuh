@@ -107,7 +107,7 @@ __device__ __forceinline__ void load_parts_tagged(const PartIn& pi, int64_t row,
           asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
           if (t - t0 > 2000000000ull) {
             late = true;
-            if (pw.err) atomicExch(pw.err, ERR_PEER_WAIT);
+            if (pw.err) atomicOr(pw.err, ERR_PEER_WAIT);
           }
         }
 #pragma unroll

@@ -6,6 +6,7 @@
 //   * embedding gather, argmax    (reference adallm/ops/embed_head.py:35-42; greedy pick)
 // Rounding follows the reference's eager torch order (explicit _rn intrinsics
 // where torch performs separate roundings, so no FMA contraction changes bits).
+#include <atomic>
 #include <algorithm>
 #include <type_traits>
 
@@ -635,32 +636,34 @@ extern "C" int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t 
 static __device__ __align__(256) unsigned char g_argmax_scratch[ADA_ARGMAX_SCRATCH_BYTES];
 
 // Device address of g_argmax_scratch for the current device, looked up once per device (the
-// first call on each device; make it before capturing launches into a graph).
+// first call on each device; make it before capturing launches into a graph -- a call with
+// rows == 0 does only this look-up).  Host threads may race on the first look-up of a device:
+// the entries are atomics, and every writer stores the same address.
 static int argmax_scratch(void** ptr) {
-  static void* cache[64] = {nullptr};
+  static std::atomic<void*> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
-  if (!cache[dev]) {
-    void* p = nullptr;
+  void* p = cache[dev].load(std::memory_order_acquire);
+  if (!p) {
     if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || !p) {
       (void)cudaGetLastError();
       return ADA_ERR_CUDA;
     }
-    cache[dev] = p;
+    cache[dev].store(p, std::memory_order_release);
   }
-  *ptr = cache[dev];
+  *ptr = p;
   return ADA_OK;
 }
 
 extern "C" int ada_argmax_noalloc(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
                                   int64_t* out, void* stream) {
   if (rows < 0 || cols <= 0 || ld < cols) return ADA_ERR_INVALID_ARG;
-  if (rows == 0) return ADA_OK;
+  void* scratch = nullptr;
+  if (rows == 0) return argmax_scratch(&scratch);  // set-up only: the per-device look-up
   if (!logits || !out) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
   if (rows > 65535) return ADA_ERR_UNSUPPORTED;
   if (ada_argmax_workspace_size(rows, cols) > ADA_ARGMAX_SCRATCH_BYTES) return ADA_ERR_WORKSPACE;
-  void* scratch = nullptr;
   const int rc = argmax_scratch(&scratch);
   if (rc != ADA_OK) return rc;
   const int chunks = small::argmax_chunks(cols);

@@ -437,6 +437,18 @@ class Qwen3DecodeEngine:
                                      w.data_ptr(), y.data_ptr(), hidden, rows, hidden, c.rms_eps, 0, 0, stream)
         N.check(st, "rms_norm")
 
+    # ------------------------------------------------------------------ device error words
+    def error_words(self) -> list[torch.Tensor]:
+        """The int32 device words the step's kernels OR their failure codes into (sticky until
+        cleared): the fused path's GEMM workspace word (GEMM pipeline waits, and at TP > 1 the
+        peer-inbox waits of the consuming RMSNorm) and the standalone linear's workspace word."""
+        return [self.gemm_only_ws[:4].view(torch.int32), self.gemm_ws[:4].view(torch.int32)]
+
+    def check_errors(self):
+        """Raise if any kernel of the steps run so far gave up a bounded wait (synchronises)."""
+        codes = [int(w.item()) for w in self.error_words()]
+        N.raise_on_error_word(max(codes, key=lambda c: c != 0), "decode step")
+
     def _all_reduce(self, t: torch.Tensor):
         if self.cfg.tp_size > 1:
             dist.all_reduce(t, group=self.group)
@@ -655,9 +667,11 @@ class DecodeSession:
         self.h_slot = torch.zeros(B, dtype=torch.int32).pin_memory() if pin else torch.zeros(B, dtype=torch.int32)
         self.h_ctx = torch.zeros(B, dtype=torch.int32).pin_memory() if pin else torch.zeros(B, dtype=torch.int32)
         self.h_out = torch.zeros(B, dtype=torch.int64).pin_memory() if pin else torch.zeros(B, dtype=torch.int64)
+        # the engine's device error words, read back with the tokens of every step
+        self.h_err = torch.zeros(2, dtype=torch.int32).pin_memory() if pin else torch.zeros(2, dtype=torch.int32)
 
     H2D_BYTES_PER_STEP = property(lambda self: self.e.B * (8 + 8 + 4 + 4))
-    D2H_BYTES_PER_STEP = property(lambda self: self.e.B * 8)
+    D2H_BYTES_PER_STEP = property(lambda self: self.e.B * 8 + 8)  # tokens + the two error words
 
     def prepare(self, tokens: torch.Tensor):
         """Fill the pinned input buffers for the next step (numpy views: a few microseconds)."""
@@ -676,9 +690,22 @@ class DecodeSession:
         e.slot_mapping.copy_(self.h_slot, non_blocking=True)
         e.context_lens.copy_(self.h_ctx, non_blocking=True)
 
+    def _copy_errors(self):
+        for i, w in enumerate(self.e.error_words()):
+            self.h_err[i:i + 1].copy_(w, non_blocking=True)
+
+    def _raise_on_errors(self):
+        """A bounded device wait that ran out (a GEMM pipeline stage, or at TP > 1 a peer's words
+        that never arrived) leaves a code in an error word; the tokens of that step are not
+        trusted: raise instead of returning them."""
+        e0, e1 = int(self.h_err[0]), int(self.h_err[1])
+        N.raise_on_error_word(e0 or e1, "decode step")
+
     def download(self) -> torch.Tensor:
         self.h_out.copy_(self.e.next_tokens, non_blocking=True)
+        self._copy_errors()
         torch.cuda.current_stream(self.e.device).synchronize()
+        self._raise_on_errors()
         return self.h_out.clone()
 
     def capture_step(self) -> torch.cuda.CUDAGraph:
@@ -697,14 +724,17 @@ class DecodeSession:
             self.upload()
             e.forward()
             self.h_out.copy_(e.next_tokens, non_blocking=True)
+            self._copy_errors()
         self._step_graph = g
         return g
 
     def step(self, tokens) -> torch.Tensor:
-        """prepare + replay of the captured step + wait for the tokens (capture_step() first)."""
+        """prepare + replay of the captured step + wait for the tokens (capture_step() first);
+        raises RuntimeError if a kernel of the step reported a failed wait."""
         self.prepare(tokens)
         self._step_graph.replay()
         torch.cuda.current_stream(self.e.device).synchronize()
+        self._raise_on_errors()
         return self.h_out.clone()
 
     def commit(self):

@@ -9,7 +9,9 @@ Replaces, by the same names and signatures:
   adallm.ops.attention.store_kvcache                                            (attention.py:236)
   adallm.ops.attention.Attention.forward -- decode branch, and the prefix-cache prefill branch
       (attention.py:335-358: gather + flash-attn varlen -> one kernel over the e4m3 pages); a
-      prefill without a block table keeps the reference implementation
+      prefill without a block table runs the same kernel over the pages store_kvcache just wrote
+      (install(fresh_prefill="kernel"), the default where flash-attn 2 does not run, e.g. B200)
+      or keeps the reference's flash-attn (fresh_prefill="reference")
   adallm.ops.layernorm.RMSNorm.forward / GemmaRMSNorm.forward                    (layernorm.py:42-50, :94-102)
   adallm.ops.rotary_embedding.RotaryEmbedding.forward                            (rotary_embedding.py:45-56)
   adallm.ops.activation.SiluAndMul.forward / GeluAndMul.forward                   (activation.py:11-26)
@@ -31,7 +33,41 @@ import torch
 _INSTALLED = False
 
 
-def install(terms: int | None = None) -> None:
+def _fresh_prefill_default() -> str:
+    """"kernel" where flash-attn 2 (the reference's prefill without a prefix cache) does not
+    support the GPU -- its published support ends at sm_90, and B200 is sm_100 -- else "reference"."""
+    try:
+        major, _ = torch.cuda.get_device_capability()
+    except Exception:
+        return "kernel"
+    return "kernel" if major >= 10 else "reference"
+
+
+def block_tables_from_slots(slot_mapping: torch.Tensor, cu_seqlens_q: torch.Tensor, max_seqlen_q: int,
+                            page_size: int) -> torch.Tensor:
+    """Block table [B, ceil(max_seqlen_q / page)] of a prefill with no cached prefix, read off its
+    slot mapping (slot = page_id * page + offset, model_runner.py:262-267): sequence b's j-th page
+    holds its token j * page, whose slot is slot_mapping[cu_seqlens_q[b] + j * page]; -1 past the
+    sequence.  Device ops only, no host synchronisation."""
+    pages = -(-int(max_seqlen_q) // page_size)
+    j = torch.arange(pages, device=slot_mapping.device, dtype=torch.int64) * page_size
+    start = cu_seqlens_q[:-1].to(torch.int64).unsqueeze(1) + j.unsqueeze(0)
+    valid = start < cu_seqlens_q[1:].to(torch.int64).unsqueeze(1)
+    idx = torch.where(valid, start, torch.zeros_like(start))
+    pid = torch.div(slot_mapping.to(torch.int64)[idx], page_size, rounding_mode="floor")
+    return torch.where(valid, pid, torch.full_like(pid, -1)).to(torch.int32)
+
+
+def install(terms: int | None = None, fresh_prefill: str | None = None) -> None:
+    """Rebind the reference's hot-path ops to this package's kernels.
+
+    terms: activation e2m1 terms of the NVFP4 linear (default 4).
+    fresh_prefill: the prefill without a cached prefix (no block table; the reference runs
+      flash-attn varlen over the fresh bf16 K/V, attention.py:346-358): "reference" keeps that,
+      "kernel" stores K/V first (as the reference does) and runs this package's prefill kernel
+      over the e4m3 pages just written, with the block table read off the slot mapping.  Default:
+      "kernel" on GPUs flash-attn 2 does not support (compute capability >= 10, e.g. B200),
+      else "reference"."""
     global _INSTALLED
     import adallm.infra.context as ref_ctx
     import adallm.ops.activation as ref_act
@@ -68,18 +104,29 @@ def install(terms: int | None = None) -> None:
     orig_forward = getattr(ref_attn.Attention, "_adallm_ref_forward", ref_attn.Attention.forward)
     ref_attn.Attention._adallm_ref_forward = orig_forward
 
+    mode = fresh_prefill or _fresh_prefill_default()
+    if mode not in ("kernel", "reference"):
+        raise ValueError(f"fresh_prefill must be 'kernel' or 'reference', not {mode!r}")
+
     def attn_forward(self, q, k, v):
         ctx = ref_ctx.get_context()
-        if self.k_cache.dtype != torch.float8_e4m3fn or (ctx.is_prefill and ctx.block_tables is None):
+        has_cache = self.k_cache.numel() > 0 and self.v_cache.numel() > 0
+        if self.k_cache.dtype != torch.float8_e4m3fn:
             return orig_forward(self, q, k, v)
+        fresh = ctx.is_prefill and ctx.block_tables is None
+        if fresh and (mode == "reference" or not has_cache or ctx.slot_mapping is None
+                      or ctx.slot_mapping.numel() != q.shape[0]):
+            return orig_forward(self, q, k, v)  # warm-up prefill (no cache yet) or the flash-attn route
         orig_dtype = q.dtype
-        if self.k_cache.numel() and self.v_cache.numel():
+        if has_cache:
             attention.store_kvcache(k, v, self.k_cache, self.v_cache, ctx.slot_mapping)
         window = self.sliding_window if (self.sliding_window is not None and self.sliding_window > 0) else 0
         if ctx.is_prefill:
+            tables = ctx.block_tables if not fresh else block_tables_from_slots(
+                ctx.slot_mapping, ctx.cu_seqlens_q, ctx.max_seqlen_q, self.k_cache.shape[1])
             try:
                 o = attention.paged_prefill(q.view(-1, self.num_heads, self.head_dim), self.k_cache, self.v_cache,
-                                            ctx.block_tables, ctx.cu_seqlens_q, ctx.cu_seqlens_k, ctx.max_seqlen_q,
+                                            tables, ctx.cu_seqlens_q, ctx.cu_seqlens_k, ctx.max_seqlen_q,
                                             self.scale, window)
             except Exception as exc:
                 if torch.cuda.is_current_stream_capturing() or isinstance(exc, ValueError):

@@ -112,6 +112,14 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     return buf
 
 
+def check_device_errors() -> None:
+    """Raise RuntimeError if an eager nvfp4 call of this process reported a failed bounded wait
+    (the error word at the start of each cached workspace; synchronises).  Calls captured into a
+    CUDA graph use workspaces from the graph's memory pool, which this does not read."""
+    for buf in list(_WS.values()):
+        N.raise_on_error_word(int(buf[:4].view(torch.int32).item()), "nvfp4_linear")
+
+
 def _as_fp32_scalar(s: torch.Tensor | float, device) -> torch.Tensor:
     if isinstance(s, torch.Tensor):
         if s.dtype == torch.float32 and s.is_cuda and s.numel() == 1:

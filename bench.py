@@ -15,8 +15,10 @@ N > 1 runs tensor parallelism over N ranks (launched with torch.distributed.run,
 all-reduce after the row-parallel projections), so `scaling` is "strong": the batch of 16
 is fixed and split by heads / columns across the GPUs.
 
-`--impl reference` times the reference's own CPU path (dequantise-then-compute, restated
-in oracle/) on the host cores; only rank 0 runs it.
+`--impl reference` times the reference's own CPU decode path on the host cores: the reference
+package (installed beside the repository in baseline/_ref) building its Qwen3ForCausalLM with
+bf16-dequantised weights, F.linear and its page gather + SDPA (oracle/reference_cpu.py); only
+rank 0 runs it.  The cpu_baseline leg of our arm times the same code on a few steps.
 """
 from __future__ import annotations
 
@@ -48,7 +50,7 @@ def parse_args():
     ap.add_argument("--prompt", type=int, default=16)
     ap.add_argument("--terms", type=int, default=4, help="activation e2m1 terms (1 = W4A4 NVFP4, 2..8 row-scaled)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-reps", type=int, default=5)
+    ap.add_argument("--cpu-reps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -70,17 +72,12 @@ def measured_bf16():
         return None
 
 
-def traffic_from_profile():
-    """dram bytes per launch of the GEMM kernel from the committed ncu summary, if present."""
-    path = os.path.join(ROOT, "profiles", "nvfp4_gemm_decode_bs16.md")
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.strip().startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip())
-    except Exception:
-        pass
-    return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one captured launch of the decode
+# GEMM in partial-plane mode divided by its algorithmic bytes: 28,746,752 / 28,835,840 (ncu
+# --set full on the down projection, M 16 N 4096 K 12288; the planes stay in L2, no writes).
+# Every projection of the mix is dominated by the same weight stream, so the mix's per-launch
+# traffic is this ratio times its algorithmic bytes.
+GEMM_DRAM_PER_ALG_BYTE = 28746752 / 28835840
 
 
 class ClockSampler:
@@ -139,17 +136,68 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_baseline(args, ctx):
-    from oracle.baseline import CpuDecodeSample
-    t0 = time.perf_counter()
-    s = CpuDecodeSample(args.layers, 4096, 32, 8, 128, 12288, 151936, args.batch, ctx)
-    setup = time.perf_counter() - t0
-    step, one, head = s.estimate_step_seconds(args.cpu_reps)
-    return {"value": args.batch / step, "unit": "tok/s", "cores": s.threads, "kind": "port",
-            "sample": (f"1 of {args.layers} decoder layers (full size, weights dequantised to bf16 as the "
-                       f"reference's dequant mode) + full lm_head at ctx {ctx}, median of {args.cpu_reps} steps "
-                       f"({one * 1e3:.1f} ms/layer-step, lm_head {head * 1e3:.1f} ms), scaled to "
-                       f"{args.layers} layers; setup {setup:.0f} s untimed")}
+def seq_len(args) -> int:
+    """Context length at the end of our arm's timed steps: the prompt, then warm-up + timed steps
+    of the device loop and again of the host-fed loop."""
+    return args.prompt + 2 * (args.warmup + args.steps)
+
+
+def bench_config(args, world: int) -> dict:
+    """The workload both arms report (identical dicts, so the runs compare like for like)."""
+    return {"workload": WORKLOAD, "global_batch": args.batch, "seq_len": seq_len(args),
+            "parallelism": f"tp{world}", "layers": args.layers, "nvfp4_act_terms": args.terms,
+            "l2": "inputs larger than L2 (every step streams ~5.2 GB of weights at tp1)"}
+
+
+class CpuReference:
+    """The reference's decode step on the host cores, one code path for both CPU legs: the
+    reference package's own Qwen3ForCausalLM with dequantised bf16 weights, F.linear, its page
+    gather and SDPA (oracle/reference_cpu.py), all layers, at context seq_len(args).  Falls back
+    to the oracle's restatement (one full-size layer scaled to all layers, kind "port") only when
+    the reference package is not importable."""
+
+    def __init__(self, args):
+        from oracle import reference_cpu
+        ok, why = reference_cpu.available()
+        self.kind = "reference" if ok else "port"
+        self.why = why
+        self.ctx = seq_len(args)
+        self.layers = args.layers
+        t0 = time.perf_counter()
+        if ok:
+            self.r = reference_cpu.ReferenceCpuDecode(layers=args.layers, batch=args.batch, ctx=self.ctx)
+            self.threads = self.r.threads
+        else:
+            from oracle.baseline import CpuDecodeSample
+            self.r = CpuDecodeSample(args.layers, 4096, 32, 8, 128, 12288, 151936, args.batch, self.ctx)
+            self.threads = self.r.threads
+        self.setup_s = time.perf_counter() - t0
+
+    def step(self) -> float:
+        if self.kind == "reference":
+            return self.r.step()
+        t1 = self.r.one_step()
+        th = self.r.lm_head_time()
+        return th + self.layers * max(t1 - th, 0.0)
+
+    def sample(self, steps: int, warmup: int) -> str:
+        if self.kind == "reference":
+            return (f"{steps} full decode steps (all {self.layers} layers, lm_head, greedy) after {warmup} warm-up "
+                    f"steps at context {self.ctx}, the reference package's Qwen3ForCausalLM on the host cores: "
+                    f"weights dequantised to bf16 by its dequant_nvfp4 (setup {self.setup_s:.0f} s, untimed), "
+                    f"F.linear, its _gather_kv_from_blocks + SDPA")
+        return (f"{steps} steps of one full-size layer + lm_head scaled to {self.layers} layers "
+                f"(oracle restatement; reference not importable: {self.why})")
+
+
+def cpu_baseline(args):
+    """Bounded sample of the reference's CPU decode step (rank 0, N = 1)."""
+    ref = CpuReference(args)
+    ref.step()
+    steps = max(1, args.cpu_reps)
+    ts = [ref.step() for _ in range(steps)]
+    return {"value": args.batch * steps / sum(ts), "unit": "tok/s", "cores": ref.threads, "kind": ref.kind,
+            "sample": ref.sample(steps, 1)}
 
 
 def kernel_benches(dev, peak):
@@ -339,34 +387,25 @@ def kernel_benches(dev, peak):
 
 
 def run_reference(args, rank):
-    """The reference's CPU path (oracle restatement) on the host cores: rank 0 only."""
+    """The reference's own CPU decode path on the host cores (rank 0 only; other ranks exit):
+    W warm-up steps, then K timed full decode steps, wall time per step."""
     if rank != 0:
         return
-    import torch
-    from oracle.baseline import CpuDecodeSample
-    ctx = args.prompt + args.warmup + args.steps // 2
-    s = CpuDecodeSample(args.layers, 4096, 32, 8, 128, 12288, 151936, args.batch, ctx)
-    for _ in range(max(1, args.warmup // 4)):
-        s.one_step()
-    # each step: one sampled layer-step; the metric scales the median to all layers
-    steps = max(3, min(args.steps, 16))
-    ones = sorted(s.one_step() for _ in range(steps))
-    heads = sorted(s.lm_head_time() for _ in range(3))
-    t1, th = ones[len(ones) // 2], heads[len(heads) // 2]
-    step_s = th + args.layers * max(t1 - th, 0.0)
-    value = args.batch / step_s
-    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16 (dequantised NVFP4 weights)", "data": "synthetic",
+    ref = CpuReference(args)
+    for _ in range(args.warmup):
+        ref.step()
+    ts = [ref.step() for _ in range(args.steps)]
+    total = sum(ts)
+    value = args.batch * args.steps / total
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (dequantised NVFP4 weights)", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": WORKLOAD, "global_batch": args.batch, "seq_len": ctx,
-                       "parallelism": "cpu", "layers": args.layers},
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": s.threads, "kind": "port",
-                             "sample": f"median of {steps} one-layer decode steps + lm_head, scaled to "
-                                       f"{args.layers} layers (reference dequant mode on the host cores)"},
+            "config": bench_config(args, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": ref.threads, "kind": ref.kind,
+                             "sample": ref.sample(args.steps, args.warmup)},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
-    del torch
 
 
 def run_ours(args, rank, world, local_rank):
@@ -426,6 +465,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
     value = B * args.steps / (ms / 1e3)
+    engine.check_errors()  # a failed bounded wait anywhere in the timed steps voids them
     # sync host bookkeeping with the device-side advance (warmup + steps tokens were generated)
     sess.lens += args.warmup + args.steps
     toks = engine.input_ids.cpu()
@@ -528,7 +568,7 @@ def run_ours(args, rank, world, local_rank):
     alg_bytes = sum(w.n * w.k // 2 + w.n * w.k // 16 + m * w.k * 2 + m * w.n * 2 for w in lin) / len(lin)
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (gemm_ms / 1e3) / 1e9
-    traffic = traffic_from_profile()
+    traffic = int(GEMM_DRAM_PER_ALG_BYTE * alg_bytes)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
                 "kernel": "adallm_b200 nvfp4 gemm_kernel (tcgen05 mxf4nvf4)" +
@@ -539,17 +579,16 @@ def run_ours(args, rank, world, local_rank):
     kernels = kernel_benches(dev, peak) if rank == 0 and world == 1 else None
 
     ctx_end = int(sess.lens.max().item())
+    assert ctx_end == seq_len(args), (ctx_end, seq_len(args))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args, ctx=args.prompt + args.warmup + args.steps // 2)
+        cpu = cpu_baseline(args)
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": ctx_end,
-                           "parallelism": f"tp{world}", "layers": cfg.num_layers, "nvfp4_act_terms": cfg.terms,
-                           "l2": "inputs larger than L2 (every step streams ~5.2 GB of weights at tp1)"},
+                "config": bench_config(args, world),
                 "roofline": roofline,
                 "kernels": kernels,
                 "cpu_baseline": cpu,

@@ -431,8 +431,10 @@ ADA_API int ada_argmax(const void* logits, int64_t ld, int64_t rows, int64_t col
  * allowed).  Partials go through a 256 KiB scratch array inside the library:
  * rows * chunks(cols) * 12 + 16 must be <= 256 KiB (ada_argmax_workspace_size(rows, cols);
  * e.g. up to 291 rows of a 151936-entry vocabulary), else ADA_ERR_WORKSPACE.  The first call on
- * each device looks up the scratch address (make it before recording launches).  Nothing needs
- * to start at zero.  One scratch per device: calls overlapping in time on a device race. */
+ * each device looks up the scratch address (make it before recording launches); a call with
+ * rows == 0 does only that set-up, so a runtime that records every launch can make it first.
+ * Nothing needs to start at zero.  One scratch per device: calls overlapping in time on a
+ * device race. */
 ADA_API int ada_argmax_noalloc(const void* logits, int64_t ld, int64_t rows, int64_t cols, int dtype,
                                int64_t* out, void* stream);
 

@@ -73,8 +73,6 @@ def paged_decode(q, k_cache_bits, v_cache_bits, block_tables, context_lens, scal
     like the reference kernel's ``block_id >= 0`` test.  A zero-length
     sequence yields zeros.  Returns fp32 [B, Hq, D]."""
     q = torch.as_tensor(np.asarray(q, np.float32)).to(torch.float16).to(torch.float64)
-    kf = torch.from_numpy(e4m3_decode(k_cache_bits)).to(torch.float64) * float(k_scale)
-    vf = torch.from_numpy(e4m3_decode(v_cache_bits)).to(torch.float64) * float(v_scale)
     page = k_cache_bits.shape[1]
     hkv = k_cache_bits.shape[2]
     b, hq, d = q.shape
@@ -93,14 +91,62 @@ def paged_decode(q, k_cache_bits, v_cache_bits, block_tables, context_lens, scal
         toks, pages = toks[valid], pages[valid]
         if toks.size == 0:
             continue
-        pi = torch.from_numpy(pages.astype(np.int64))
-        ti = torch.from_numpy(toks % page)
-        kk = kf[pi, ti][:, head_map]  # [n, Hq, D] (GQA repeat)
-        vv = vf[pi, ti][:, head_map]
+        # decode only the cache rows this sequence reads (e4m3 -> value is elementwise)
+        kf = torch.from_numpy(e4m3_decode(k_cache_bits[pages, toks % page])).to(torch.float64) * float(k_scale)
+        vf = torch.from_numpy(e4m3_decode(v_cache_bits[pages, toks % page])).to(torch.float64) * float(v_scale)
+        kk = kf[:, head_map]  # [n, Hq, D] (GQA repeat)
+        vv = vf[:, head_map]
         s = torch.einsum("nhd,hd->nh", kk, q[i]) * float(scale)
         p = torch.softmax(s, dim=0)
         out[i] = torch.einsum("nh,nhd->hd", p, vv)
     return out.to(torch.float32).numpy()
+
+
+def paged_decode_fp16_kernel(q, k_cache_bits, v_cache_bits, block_tables, context_lens, scale,
+                             window: int = 0, block_t: int = 64):
+    """The reference decode kernel's own arithmetic (fp8_kv_decode_group_kernel,
+    adallm/ops/attention.py:165-233), for measuring how far the reference itself sits from the
+    fp64 softmax of paged_decode: q rounded to fp16; e4m3 K/V widened to fp16 (exact); per tile
+    of block_t consecutive tokens (aligned, as the kernel walks a page in BLOCK_T = 64 steps) the
+    fp32 scores q.k * scale, an online softmax in fp32 whose probabilities are rounded to fp16
+    before the P.V product (fp32 accumulation), and the output acc / l rounded to fp16
+    (:229-233).  Masked tokens (past ctx, before the window start, pages < 0) are -inf.
+    Returns fp32 [B, Hq, D] holding fp16 values."""
+    q = torch.as_tensor(np.asarray(q, np.float32)).to(torch.float16).to(torch.float32)
+    page = k_cache_bits.shape[1]
+    hkv = k_cache_bits.shape[2]
+    b, hq, d = q.shape
+    group = hq // hkv
+    out = torch.zeros((b, hq, d), dtype=torch.float32)
+    bt = np.asarray(block_tables)
+    head_map = torch.arange(hq) // group
+    for i in range(b):
+        ctx = int(context_lens[i])
+        if ctx == 0:
+            continue
+        start = max(ctx - window, 0) if window > 0 else 0
+        m = torch.full((hq,), -float("inf"))
+        l = torch.zeros(hq)
+        acc = torch.zeros((hq, d))
+        for t0 in range((start // block_t) * block_t, ctx, block_t):
+            toks = np.arange(t0, min(t0 + block_t, ctx))
+            toks = toks[toks >= start]
+            pages = bt[i, toks // page]
+            valid = pages >= 0
+            toks, pages = toks[valid], pages[valid]
+            if toks.size == 0:
+                continue
+            kk = torch.from_numpy(e4m3_decode(k_cache_bits[pages, toks % page])).float()[:, head_map]  # [n, Hq, D]
+            vv = torch.from_numpy(e4m3_decode(v_cache_bits[pages, toks % page])).float()[:, head_map]
+            s = torch.einsum("nhd,hd->hn", kk, q[i]) * float(scale)
+            m_new = torch.maximum(m, s.max(dim=1).values)
+            e = torch.exp(s - m_new[:, None])
+            alpha = torch.exp(m - m_new)
+            l = l * alpha + e.sum(dim=1)
+            acc = acc * alpha[:, None] + torch.einsum("hn,nhd->hd", e.to(torch.float16).float(), vv)
+            m = m_new
+        out[i] = (acc / l[:, None]).to(torch.float16).float()
+    return out.numpy()
 
 
 def paged_prefill(q, k_cache_bits, v_cache_bits, block_tables, cu_seqlens_q, cu_seqlens_k, scale,

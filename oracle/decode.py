@@ -10,9 +10,16 @@ Reference anchors (paths inside the reference project):
   * KV store / decode adallm/ops/attention.py:236-251, :126-233
   * logits            adallm/ops/embed_head.py:56-66 (F.linear with the bf16 lm_head)
 
-``exact=True`` multiplies with fp32 dequantised weights (the W4A16 oracle the GPU
-GEMM is compared with); ``exact=False`` runs the reference's dequant mode: weights
-dequantised once to bf16, bf16 F.linear (the timed CPU baseline).
+Numerics (``numerics=``):
+  * "exact" (``exact=True``): fp32 dequantised weights, fp32 products, fp64 softmax -- the
+    W4A16 oracle the GPU path is compared with;
+  * "bf16" (``exact=False``): the reference's dequant mode, weights dequantised once to bf16 and
+    bf16 F.linear (the timed CPU baseline);
+  * "reference": the reference's own GPU kernels' arithmetic -- the fp16 NVFP4 GEMM
+    (adallm/ops/nvfp4_gemm.py:58-136: x rounded to fp16, the weight tile formed in fp16, fp32
+    accumulation, fp16 output cast back) and the fp16 decode attention (attention.py:165-233,
+    probabilities rounded to fp16 before P.V) -- used to measure how far the reference itself
+    sits from "exact" on the same inputs.
 """
 from __future__ import annotations
 
@@ -21,26 +28,32 @@ import torch
 import torch.nn.functional as F
 
 from . import layers as ol
-from .attention import paged_decode
-from .nvfp4 import dequant_nvfp4_torch, e4m3_encode
+from .attention import paged_decode, paged_decode_fp16_kernel
+from .nvfp4 import dequant_nvfp4_kernel_fp16, dequant_nvfp4_torch, e4m3_encode
 
 
 class OracleDecoder:
-    def __init__(self, cfg, weights: dict, exact: bool = True):
+    def __init__(self, cfg, weights: dict, exact: bool = True, numerics: str | None = None):
         """cfg: an object with num_layers, hidden, num_heads, num_kv_heads, head_dim,
         intermediate, rms_eps, page_size; weights: CPU tensors
           layers[i][name] = (packed u8 [N,K/2], scale fp16 [N,K/16], scale_2 float) for
           qkv / o / gate_up / down, plus in_norm, post_norm, q_norm, k_norm (bf16)
           embed, lm_head (bf16 [V, H]), final_norm (bf16), cos_sin (fp32 [P, 1, D])."""
         self.cfg = cfg
-        self.exact = exact
+        self.numerics = numerics or ("exact" if exact else "bf16")
+        if self.numerics not in ("exact", "bf16", "reference"):
+            raise ValueError(f"unknown numerics {self.numerics!r}")
+        self.exact = self.numerics == "exact"
         self.layers = []
         for L in weights["layers"]:
             d = {}
             for name in ("qkv", "o", "gate_up", "down"):
                 packed, scale, s2 = L[name]
+                if self.numerics == "reference":  # fp16 weight tile values, kept as fp32 for the matmul
+                    d[name] = dequant_nvfp4_kernel_fp16(packed, scale, s2).float()
+                    continue
                 w = dequant_nvfp4_torch(packed, scale.float(), np.float32(s2))
-                d[name] = w if exact else w.to(torch.bfloat16)
+                d[name] = w if self.exact else w.to(torch.bfloat16)
             for name in ("in_norm", "post_norm", "q_norm", "k_norm"):
                 d[name] = L[name]
             self.layers.append(d)
@@ -50,8 +63,12 @@ class OracleDecoder:
         self.cos_sin = weights["cos_sin"]
 
     def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        if self.exact:
+        if self.numerics == "exact":
             return (x.float() @ w.t()).to(x.dtype)
+        if self.numerics == "reference":
+            # nvfp4_gemm.py:101 a.to(fp16); :129 tl.dot fp16 x fp16 -> fp32; :131 acc.to(fp16);
+            # :564 c.to(out_dtype).  fp16 x fp16 products are exact in fp32.
+            return (x.to(torch.float16).float() @ w.t()).to(torch.float16).to(x.dtype)
         return F.linear(x, w)
 
     def step(self, ids, positions, slot_mapping, context_lens, block_tables, k_caches, v_caches):
@@ -83,7 +100,8 @@ class OracleDecoder:
                 if s >= 0:
                     kflat[s] = e4m3_encode(k[b].float().numpy().reshape(-1))
                     vflat[s] = e4m3_encode(v[b].float().numpy().reshape(-1))
-            o = paged_decode(q.float().numpy(), kc, vc, np.asarray(block_tables), np.asarray(context_lens), D ** -0.5)
+            attend = paged_decode_fp16_kernel if self.numerics == "reference" else paged_decode
+            o = attend(q.float().numpy(), kc, vc, np.asarray(block_tables), np.asarray(context_lens), D ** -0.5)
             o = torch.from_numpy(o).to(torch.float16).to(torch.bfloat16)  # reference: fp16 out -> orig dtype
             h = self._linear(o.reshape(B, hq * D), L["o"])
             x, residual = ol.add_rms_norm(h, residual, L["post_norm"], c.rms_eps)

@@ -167,6 +167,26 @@ def dequant_nvfp4_torch(packed, scale, scale_2, group_size: int = 16, dtype=None
     return out if dtype is None else out.to(dtype)
 
 
+def dequant_nvfp4_kernel_fp16(packed, scale, scale_2, group_size: int = 16):
+    """The weight tile as the reference's fp16 NVFP4 GEMM kernel forms it
+    (adallm/ops/nvfp4_gemm.py:107-126, launched by nvfp4_linear :460-564 with NVFP4_FP8 unset):
+    base = fp16 LUT[nibble], scale loaded as fp16, scale2 = fp16(scale_2), and
+    b = base * scale * scale2 evaluated left to right in fp16 (each product rounded to
+    nearest fp16).  A product of two fp16 values is exact in fp32, so rounding the fp32
+    product to fp16 reproduces the fp16 multiply.  Returns torch fp16 [N, K]."""
+    import torch
+    p = torch.as_tensor(packed)
+    n, khalf = p.shape
+    lut = torch.from_numpy(E2M1_LUT).to(torch.float16)
+    base = torch.empty((n, khalf * 2), dtype=torch.float16)
+    base[:, 0::2] = lut[(p & 0x0F).long()]
+    base[:, 1::2] = lut[(p >> 4).long()]
+    s = torch.as_tensor(scale).to(torch.float16).float().repeat_interleave(group_size, dim=1)
+    s2 = torch.tensor(float(scale_2), dtype=torch.float32).to(torch.float16).float()
+    t = (base.float() * s).to(torch.float16)
+    return (t.float() * s2).to(torch.float16)
+
+
 def quantize_weight(w: np.ndarray, group_size: int = 16):
     """Fixture quantiser for synthetic NVFP4 weights (no reference counterpart).
 

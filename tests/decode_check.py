@@ -1,15 +1,26 @@
-"""Greedy-token agreement between the B200 decode engine and the CPU oracle decoder
-(teacher-forced: both consume the oracle's token each step, so one disagreement does
-not cascade).  Used by tests/test_gpu_decode.py and __graft_entry__.smoke().
+"""Greedy-token agreement between the B200 decode engine and the CPU oracle decoder.
+Used by tests/test_gpu_decode.py and __graft_entry__.smoke().
 
-Two figures are returned: raw agreement, and agreement over *decisive* steps where the
-oracle's top-1 / top-2 logit gap exceeds 10% of the logit RMS.  Random-init models have
-near-tied logits, and the e4m3 KV cache turns last-bit bf16 differences into ~6% jumps
-of single K/V elements, so any implementation whose k/v are not bit-identical to the
-oracle's flips some near-ties (an emulation of the reference's own fp16 numerics agrees
-on ~95-96% of raw tokens in the same setting)."""
+Teacher-forced: every decoder consumes the exact oracle's token each step, so one disagreement
+does not cascade.  Three decoders run on the same weights and inputs:
+  * ours       -- the engine (all hot-path kernels, one CUDA graph per step);
+  * exact      -- the oracle with fp32 dequantised weights and an fp64 softmax (W4A16);
+  * reference  -- the oracle with the reference's own kernel arithmetic (fp16 NVFP4 GEMM,
+                  fp16 probabilities in the decode attention; oracle.decode "reference").
+Raw greedy agreement of ours and of the reference emulation with the exact oracle, and the
+relative L2 of each one's logits against the exact oracle's, are returned.
+
+Why the reference emulation is measured beside the engine: random-init models have near-tied
+logits (the top-2 gap of 151,936 Gaussian logits is ~0.2 standard deviations, and bf16 logits
+near 6 have a 1/32 spacing), and the e4m3 KV cache turns last-bit bf16 differences of k/v into
+one-e4m3-step (6-12%) jumps of single cache elements.  Any implementation whose arithmetic is
+not bit-identical to the exact oracle therefore flips some near-ties -- the reference itself
+included.  The pass criterion compares the engine with what the reference's own numerics reach
+on the same inputs."""
 from __future__ import annotations
 
+import math
+from dataclasses import dataclass
 from types import SimpleNamespace
 
 import numpy as np
@@ -24,23 +35,51 @@ def small_config(layers: int) -> DecodeConfig:
                         intermediate=3072, vocab=4096, max_position=4096, page_size=16)
 
 
-def run_agreement(layers=2, steps=8, batch=4, prompt=4, graph=True, return_logits=False):
+def qwen3_8b_config(layers: int) -> DecodeConfig:
+    """BASELINE config 3 widths (hidden 4096, 32/8 heads of 128, SwiGLU 12288, vocab 151936,
+    theta 1e6, page 16) with `layers` decoder layers."""
+    return DecodeConfig(num_layers=layers, max_position=4096)
+
+
+@dataclass
+class Agreement:
+    raw: float                 # ours vs exact, greedy tokens
+    raw_reference: float       # reference emulation vs exact (nan when not run)
+    logits_rel_l2_max: float   # ours vs exact, worst step
+    logits_rel_l2_mean: float
+    ref_logits_rel_l2_mean: float
+    tokens: int
+
+    def margin(self, z: float = 2.5) -> float:
+        """z standard errors of the difference of two agreement rates measured on `tokens` tokens."""
+        p = min(max(self.raw_reference, 0.5), 1.0)
+        return z * math.sqrt(2.0 * max(p * (1.0 - p), 1.0 / self.tokens) / self.tokens)
+
+
+def run_agreement(cfg: DecodeConfig | None = None, layers=2, steps=8, batch=4, prompt=4, graph=True,
+                  emulate=False, seed=1) -> Agreement:
     d = torch.device("cuda:0")
-    cfg = small_config(layers)
-    eng = Qwen3DecodeEngine(cfg, d, batch, max_ctx=prompt + steps + 8, seed=1)
-    sess = DecodeSession(eng, seed=1)
+    cfg = cfg or small_config(layers)
+    layers = cfg.num_layers
+    eng = Qwen3DecodeEngine(cfg, d, batch, max_ctx=prompt + steps + 8, seed=seed)
+    sess = DecodeSession(eng, seed=seed)
     w = eng.export_cpu_weights()
     ocfg = SimpleNamespace(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
                            num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, intermediate=cfg.intermediate,
                            rms_eps=cfg.rms_eps, page_size=cfg.page_size)
-    oracle = OracleDecoder(ocfg, w, exact=True)
-    kc = [np.zeros((eng.num_pages, cfg.page_size, cfg.num_kv_heads, cfg.head_dim), np.uint8) for _ in range(layers)]
-    vc = [np.zeros_like(kc[0]) for _ in range(layers)]
+    exact = OracleDecoder(ocfg, w, numerics="exact")
+    emul = OracleDecoder(ocfg, w, numerics="reference") if emulate else None
+
+    def caches():
+        kc = [np.zeros((eng.num_pages, cfg.page_size, cfg.num_kv_heads, cfg.head_dim), np.uint8) for _ in range(layers)]
+        return kc, [np.zeros_like(kc[0]) for _ in range(layers)]
+    kc, vc = caches()
+    kr, vr = caches() if emulate else (None, None)
     g = eng.capture() if graph else None
-    gen = torch.Generator().manual_seed(3)
+    gen = torch.Generator().manual_seed(seed + 2)
     tokens = torch.randint(0, cfg.vocab, (batch, prompt), generator=gen)
-    agree, total, dec_agree, dec_total = 0, 0, 0, 0
-    logit_err = []
+    agree = agree_ref = total = 0
+    errs, ref_errs = [], []
     cur = tokens[:, 0]
     for i in range(prompt + steps):
         sess.prepare(cur)
@@ -50,23 +89,20 @@ def run_agreement(layers=2, steps=8, batch=4, prompt=4, graph=True, return_logit
         else:
             eng.forward()
         ours = sess.download()
-        logits = oracle.step(sess.h_ids.clone(), sess.h_pos.clone(), sess.h_slot.numpy().copy(),
-                             sess.h_ctx.numpy().copy(), sess.block_tables.numpy(), kc, vc)
+        meta = (sess.h_ids.clone(), sess.h_pos.clone(), sess.h_slot.numpy().copy(), sess.h_ctx.numpy().copy(),
+                sess.block_tables.numpy())
+        logits = exact.step(*meta, kc, vc)
         theirs = logits.argmax(dim=1)
+        ref_logits = emul.step(*meta, kr, vr) if emulate else None
         sess.commit()
-        if i >= prompt - 1:
+        if i >= prompt - 1:  # the tokens generated after the prompt
             agree += int((ours == theirs).sum())
             total += batch
-            # decisive steps: the oracle's top-1 / top-2 gap exceeds 10% of the logit RMS (about three
-            # standard deviations of the top-2 difference under the ~2% logit deviation measured here)
-            top2 = logits.topk(2, dim=1).values
-            decisive = (top2[:, 0] - top2[:, 1]) > 0.1 * logits.pow(2).mean(dim=1).sqrt()
-            dec_agree += int(((ours == theirs) & decisive).sum())
-            dec_total += int(decisive.sum())
+            errs.append(float((eng.logits.float().cpu() - logits).norm() / logits.norm()))
+            if emulate:
+                agree_ref += int((ref_logits.argmax(dim=1) == theirs).sum())
+                ref_errs.append(float((ref_logits - logits).norm() / logits.norm()))
         cur = tokens[:, i + 1] if i + 1 < prompt else theirs
-        logit_err.append(float((eng.logits.float().cpu() - logits).norm() / logits.norm()))
-    frac = agree / max(total, 1)
-    decisive_frac = dec_agree / max(dec_total, 1)
-    if return_logits:
-        return frac, decisive_frac, logit_err
-    return frac, decisive_frac
+    return Agreement(raw=agree / max(total, 1), raw_reference=agree_ref / max(total, 1) if emulate else float("nan"),
+                     logits_rel_l2_max=max(errs), logits_rel_l2_mean=float(np.mean(errs)),
+                     ref_logits_rel_l2_mean=float(np.mean(ref_errs)) if emulate else float("nan"), tokens=total)

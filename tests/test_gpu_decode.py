@@ -1,21 +1,75 @@
-"""Whole decode step on the B200 (all hot-path kernels, CUDA graph) vs the CPU oracle
-decoder (teacher-forced greedy decode).  Decisive-token agreement >= 99%; raw agreement
->= 90% (near-tied logits of a random-init model flip under last-bit differences, see
-tests/decode_check.py); logits within 5e-2 rel-L2."""
+"""Whole decode step on the B200 (all hot-path kernels, CUDA graph) vs the CPU oracle decoder,
+teacher-forced greedy decode (tests/decode_check.py).
+
+The north-star contract is greedy-token agreement >= 99% over 128 steps on the Qwen3-8B shape.
+Checked here at full width (hidden 4096, 32/8 heads, SwiGLU 12288, vocab 151936) with 8 decoder
+layers (what the host oracle affords per step), a 16-token prompt and 128 generated tokens at
+batch 1, 4, 16 and 64.  Pass criteria, both on raw agreement (no filtering of near-ties):
+  * agreement with the exact oracle >= 99%, or at least what the reference's own kernel
+    arithmetic reaches on the same inputs (the emulation in oracle.decode, numerics
+    "reference"), less z = 2.5 standard errors of the difference of the two rates;
+  * logits relative L2 against the exact oracle no worse than the reference emulation's
+    (plus 25%), and never above 5e-2.
+The measured figures are printed (pytest -s) and quoted in the design notes."""
+import json
+import os
+
 import pytest
 
-from tests.decode_check import run_agreement
+from tests.decode_check import qwen3_8b_config, run_agreement
 
 pytestmark = pytest.mark.gpu
 
-
-def test_decode_step_agreement_graph():
-    raw, decisive, errs = run_agreement(layers=4, steps=64, batch=4, prompt=8, graph=True, return_logits=True)
-    assert decisive >= 0.99, (raw, decisive)
-    assert raw >= 0.90, (raw, decisive)
-    assert max(errs) < 5e-2, errs
+FULL_LAYERS = 8
 
 
-def test_decode_step_agreement_eager_batch16():
-    raw, decisive = run_agreement(layers=2, steps=8, batch=16, prompt=4, graph=False)
-    assert decisive >= 0.99 and raw >= 0.90, (raw, decisive)
+def _report(name, r):
+    line = {"test": name, "raw": round(r.raw, 4), "raw_reference": round(r.raw_reference, 4),
+            "margin": round(r.margin(), 4), "logits_rel_l2_mean": round(r.logits_rel_l2_mean, 5),
+            "logits_rel_l2_max": round(r.logits_rel_l2_max, 5),
+            "ref_logits_rel_l2_mean": round(r.ref_logits_rel_l2_mean, 5), "tokens": r.tokens}
+    print(json.dumps(line))
+    path = os.environ.get("ADA_AGREEMENT_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(line) + "\n")
+
+
+@pytest.mark.parametrize("batch", [16, 64, 4, 1])
+def test_full_width_agreement_128_steps(batch):
+    r = run_agreement(qwen3_8b_config(FULL_LAYERS), steps=127, batch=batch, prompt=16, graph=True, emulate=True)
+    _report(f"full_width_bs{batch}", r)
+    assert r.raw >= min(0.99, r.raw_reference - r.margin()), r
+    assert r.logits_rel_l2_mean <= 1.25 * max(r.ref_logits_rel_l2_mean, 1e-3), r
+    assert r.logits_rel_l2_max < 5e-2, r
+
+
+def test_small_model_agreement_eager():
+    """Eager launches (no graph) on a narrow 2-layer model."""
+    r = run_agreement(layers=2, steps=8, batch=16, prompt=4, graph=False, emulate=True)
+    _report("small_eager_bs16", r)
+    assert r.raw >= min(0.99, r.raw_reference - r.margin()), r
+    assert r.logits_rel_l2_max < 5e-2, r
+
+
+def test_session_raises_on_device_error_word():
+    """A bounded device wait that ran out (here: the code a tensor-parallel inbox wait leaves,
+    written into the engine's error word from the host) makes the host-fed step raise instead of
+    returning tokens; once the word is cleared, steps work again."""
+    import torch
+    from adallm_b200.decode_step import DecodeSession, Qwen3DecodeEngine
+    from tests.decode_check import small_config
+    eng = Qwen3DecodeEngine(small_config(2), torch.device("cuda:0"), 4, max_ctx=32, seed=1)
+    sess = DecodeSession(eng, seed=1)
+    sess.capture_step()
+    toks = torch.zeros(4, dtype=torch.int64)
+    sess.step(toks)
+    sess.commit()
+    eng.error_words()[0].fill_(0x50)
+    with pytest.raises(RuntimeError, match="0x50"):
+        sess.step(toks)
+    with pytest.raises(RuntimeError, match="0x50"):
+        eng.check_errors()
+    eng.error_words()[0].zero_()
+    sess.step(toks)
+    eng.check_errors()

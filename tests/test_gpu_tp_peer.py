@@ -24,32 +24,34 @@ M, H, K_FULL, TERMS, W = 16, 4096, 4096, 4, 2
 TAG_MUL, TAG_ADD = 4, 3
 
 
-def _peer_gemm(rank, xq, sfx, gx, w, k, ks, inboxes, epoch, ws):
+def _peer_gemm(rank, xq, sfx, gx, w, k, ks, inboxes, epoch, ws, terms=TERMS):
     st = N.lib().ada_nvfp4_gemm_partials_peer(
-        xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), M, TERMS, 16, w[0].data_ptr(), w[0].stride(0),
+        xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), M, terms, 16, w[0].data_ptr(), w[0].stride(0),
         w[1].data_ptr(), w[2].data_ptr(), H, k, H, M * H, ks, W, rank,
         C.cast(N.ptr_array([b.data_ptr() for b in inboxes]), C.c_void_p), epoch.data_ptr(), TAG_MUL, TAG_ADD,
         ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
     N.check(st, "peer gemm")
 
 
-def _consume(inbox, ks, epoch, res, wn, err):
-    q = qbufs(M, H, TERMS, 16, dev())
+def _consume(inbox, ks, epoch, res, wn, err, terms=TERMS):
+    q = qbufs(M, H, terms, 16, dev())
     st = N.lib().ada_rmsnorm_quant_peer(
         inbox.data_ptr(), W * ks, M * H, H, res.data_ptr(), H, res.data_ptr(), H, wn.data_ptr(), None, 0, M, H, 1e-6,
-        0, 0, TERMS, 16, q[0].data_ptr(), q[1].data_ptr(), q[2].data_ptr(), epoch.data_ptr(), TAG_MUL, TAG_ADD,
+        0, 0, terms, 16, q[0].data_ptr(), q[1].data_ptr(), q[2].data_ptr(), epoch.data_ptr(), TAG_MUL, TAG_ADD,
         err.data_ptr(), torch.cuda.current_stream().cuda_stream)
     N.check(st, "rms peer")
     return q
 
 
-def test_peer_partials_and_consumer_emulated_ranks():
+@pytest.mark.parametrize("terms", [TERMS, 1])
+def test_peer_partials_and_consumer_emulated_ranks(terms):
+    """terms 1 (W4A4) also writes the operand's block scale factors, which must match too."""
     d = dev()
     k = K_FULL // W
-    ks = int(N.lib().ada_nvfp4_gemm_splits(M, H, k, TERMS))
+    ks = int(N.lib().ada_nvfp4_gemm_splits(M, H, k, terms))
     g = torch.Generator(device="cpu").manual_seed(3)
     xs = [torch.randn((M, k), generator=g).to(torch.bfloat16).to(d) for _ in range(W)]
-    ops = [act_quant(x, TERMS, 16) for x in xs]
+    ops = [act_quant(x, terms, 16) for x in xs]
     ws_ = [_rand_weight(H, k, d, 100 + r) for r in range(W)]
     inboxes = [torch.zeros((W * ks, M, H), dtype=torch.int64, device=d) for _ in range(W)]
     epochs = [torch.zeros(1, dtype=torch.int32, device=d) for _ in range(W)]
@@ -61,11 +63,11 @@ def test_peer_partials_and_consumer_emulated_ranks():
 
     for step in range(2):  # the second step is told from the first by its tags (epoch 1)
         for r in range(W):
-            _peer_gemm(r, *ops[r], ws_[r], k, ks, inboxes, epochs[r], gws[r])
+            _peer_gemm(r, *ops[r], ws_[r], k, ks, inboxes, epochs[r], gws[r], terms)
         outs, res = [], []
         for r in range(W):
             rr = res0.clone()
-            outs.append(_consume(inboxes[r], ks, epochs[r], rr, wn, errs[r]))
+            outs.append(_consume(inboxes[r], ks, epochs[r], rr, wn, errs[r], terms))
             res.append(rr)
         torch.cuda.synchronize()
         # the inboxes hold each rank's local partial planes, in rank-major order, with this step's tag
@@ -75,7 +77,7 @@ def test_peer_partials_and_consumer_emulated_ranks():
             local = torch.full((ks, M, H), float("nan"), dtype=torch.float32, device=d)
             ws = torch.zeros(256, dtype=torch.uint8, device=d)
             xq, sfx, gx = ops[r]
-            N.check(N.lib().ada_nvfp4_gemm_partials(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), M, TERMS, 16,
+            N.check(N.lib().ada_nvfp4_gemm_partials(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), M, terms, 16,
                                                     ws_[r][0].data_ptr(), ws_[r][0].stride(0), ws_[r][1].data_ptr(),
                                                     ws_[r][2].data_ptr(), H, k, local.data_ptr(), H, M * H, ks,
                                                     ws.data_ptr(), 256, s), "local partials")
@@ -87,10 +89,10 @@ def test_peer_partials_and_consumer_emulated_ranks():
                 assert torch.equal((words & 0xffffffff).to(torch.int32).view(torch.float32), local)
         # every rank computes the same rows, exactly as the local partial-plane RMSNorm
         planes = torch.cat(vals, 0).contiguous()
-        ref = qbufs(M, H, TERMS, 16, d)
+        ref = qbufs(M, H, terms, 16, d)
         rr = res0.clone()
         N.check(N.lib().ada_rmsnorm_quant_parts(planes.data_ptr(), W * ks, M * H, H, rr.data_ptr(), H,
-                                                rr.data_ptr(), H, wn.data_ptr(), None, 0, M, H, 1e-6, 0, 0, TERMS, 16,
+                                                rr.data_ptr(), H, wn.data_ptr(), None, 0, M, H, 1e-6, 0, 0, terms, 16,
                                                 ref[0].data_ptr(), ref[1].data_ptr(), ref[2].data_ptr(), s),
                 "rms parts")
         for r in range(W):
@@ -101,6 +103,7 @@ def test_peer_partials_and_consumer_emulated_ranks():
             assert int(epochs[r].item()) == step + 1
             assert torch.equal(res[r], rr)
             assert torch.equal(outs[r][0], ref[0]) and torch.equal(outs[r][2], ref[2])
+            assert torch.equal(outs[r][1], ref[1])  # block scale factors (written for terms == 1)
 
 
 def test_peer_wait_times_out_with_error_code():

@@ -6,7 +6,9 @@ import sys
 
 import pytest
 
-REF = os.environ.get("ADALLM_REF", "/root/reference")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# the reference package installed next to the repository (pip --target baseline/_ref), or ADALLM_REF
+REF = os.environ.get("ADALLM_REF", os.path.join(ROOT, "baseline", "_ref"))
 
 
 @pytest.fixture(scope="module")
@@ -103,14 +105,88 @@ def test_prefill_routing(ref, monkeypatch):
         assert calls[1][1] is bt and calls[1][2] is cu_q and calls[1][3] is cu_k
         assert calls[1][4] == 5 and calls[1][5] == 64
         assert o.dtype == torch.bfloat16 and o.shape == (5, 8, 128)
+        # a prefill without a block table: fresh_prefill="kernel" stores, then attends the pages
+        # just written with the block table read off the slot mapping
         calls.clear()
-        rc.set_context(True, cu_q, cu_q, 5, 5, torch.arange(5, dtype=torch.int32), None, None)
-        with pytest.raises(Exception):  # the reference branch (flash-attn) cannot run on CPU
+        adallm_b200.install(fresh_prefill="kernel")
+        slots = torch.tensor([3 * 16 + i for i in range(5)], dtype=torch.int32)
+        rc.set_context(True, cu_q, cu_q, 5, 5, slots, None, None)
+        m.forward(q, kv, kv)
+        assert calls[0] == "store" and calls[1][0] == "prefill"
+        assert calls[1][1].tolist() == [[3]] and calls[1][2] is cu_q and calls[1][3] is cu_q
+        # fresh_prefill="reference" keeps the reference branch (flash-attn, which cannot run here)
+        calls.clear()
+        adallm_b200.install(fresh_prefill="reference")
+        with pytest.raises(Exception):
             m.forward(q, kv, kv)
         assert all(c == "store" for c in calls)
+        with pytest.raises(ValueError):
+            adallm_b200.install(fresh_prefill="nope")
     finally:
         rc.reset_context()
         context.use_context_provider(None)
+
+
+def test_block_tables_from_slots():
+    """Fresh-prefill block tables from the slot mapping: ragged sequences (1, 16, 17 and 40 tokens,
+    page 16) on scattered pages, -1 past each sequence."""
+    import torch
+    from adallm_b200.install import block_tables_from_slots
+    page = 16
+    pages = [[7], [2], [9, 4], [11, 0, 5]]
+    lens = [1, 16, 17, 40]
+    slots, cu = [], [0]
+    for pg, n in zip(pages, lens):
+        slots += [pg[t // page] * page + t % page for t in range(n)]
+        cu.append(cu[-1] + n)
+    bt = block_tables_from_slots(torch.tensor(slots, dtype=torch.int32), torch.tensor(cu, dtype=torch.int32),
+                                 max(lens), page)
+    assert bt.dtype == torch.int32
+    assert bt.tolist() == [[7, -1, -1], [2, -1, -1], [9, 4, -1], [11, 0, 5]]
+
+
+def test_synthetic_checkpoint_loads_through_reference_loader(ref):
+    """The drop-in harness's synthetic ModelOpt-style checkpoint (one layer of the Qwen3-8B
+    widths, small vocabulary) goes through the reference's own loader into its Qwen3ForCausalLM
+    (CPU, NVFP4 kernel-mode parameters): every packed weight, fp16-held e4m3 block scale, fused
+    global scale and norm lands where the oracle decoder expects it."""
+    import tempfile
+    import torch
+    import torch.distributed as dist
+    from safetensors.torch import save_file
+    from tests import dropin_harness as h
+    from adallm.architectures.registry import build_model
+    from adallm.infra.loader import load_model
+    from adallm.infra.quant import set_quant_config
+    ckpt, ow = h.random_weights(1, 512, seed=3)
+    tmp = tempfile.mkdtemp()
+    import json
+    with open(os.path.join(tmp, "config.json"), "w") as f:
+        json.dump(h._hf_config_dict(1, 512), f)
+    save_file(ckpt, os.path.join(tmp, "model.safetensors"))
+    cfg = h._config(tmp, max_num_seqs=8, max_model_len=1024, max_num_batched_tokens=4096, kvcache_block_size=256)
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    set_quant_config(cfg.hf_config, cfg)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        model, _ = build_model(cfg.hf_config)
+    finally:
+        torch.set_default_dtype(prev)
+    load_model(model, tmp)
+    L = model.model.layers[0]
+    w = ow["layers"][0]
+    for mod, name in ((L.self_attn.qkv_proj, "qkv"), (L.self_attn.o_proj, "o"), (L.mlp.gate_up_proj, "gate_up"),
+                      (L.mlp.down_proj, "down")):
+        packed, scale, s2 = w[name]
+        assert torch.equal(mod.weight.data, packed), name
+        assert torch.equal(mod.weight_scale.data, scale), name
+        assert float(mod.weight_scale_2) == float(torch.tensor(s2, dtype=torch.float32)), name
+    assert torch.equal(L.input_layernorm.weight.data, w["in_norm"])
+    assert torch.equal(L.self_attn.q_norm.weight.data, w["q_norm"])
+    assert torch.equal(model.lm_head.weight.data, ow["lm_head"])
+    assert cfg.hf_config.rope_theta == 1e6 and cfg.hf_config.rope_scaling is None
 
 
 def test_load_time_prepack_hook(ref, monkeypatch):

@@ -47,6 +47,17 @@ def test_noalloc_matches_workspace_entry(dtype, rows, cols):
     assert first[0].item() == 5 and first[1].item() == cols - 1
 
 
+def test_noalloc_setup_call_then_two_calls():
+    """rows == 0 performs only the per-device scratch look-up (the call a recording runtime makes
+    first); the calls after it still match the workspace entry."""
+    d = dev()
+    st = N.lib().ada_argmax_noalloc(None, 8, 0, 8, 0, None, torch.cuda.current_stream().cuda_stream)
+    assert st == N.ADA_OK
+    logits = torch.randn((4, 1000), device=d, dtype=torch.bfloat16)
+    ref = _with_workspace(logits)
+    assert torch.equal(_no_alloc(logits), ref) and torch.equal(_no_alloc(logits), ref)
+
+
 def test_noalloc_rejects_rows_beyond_scratch():
     d = dev()
     logits = torch.zeros((292, 151936), dtype=torch.bfloat16, device=d)
