@@ -56,6 +56,12 @@ _SIGS = {
     "ada_qk_norm_rope_store": (INT, [P, I64, I64, I32, I32, I32, P, P, F32, P, P, I64, P, P, P, F32, F32, P, P,
                                      INT, P]),
     "ada_embedding": (INT, [P, I64, P, I64, I64, I32, P, INT, P]),
+    "ada_gemma_norm2_quant_parts": (INT, [P, I32, I64, I64, P, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT,
+                                         INT, P, P, P, P]),
+    "ada_qk_norm_rope_store_parts_ex": (INT, [P, I32, I64, I64, I64, I32, I32, I32, P, P, F32, INT, P, P, I64, P, P,
+                                             P, F32, F32, P, P, INT, P]),
+    "ada_qk_norm_rope_store_ex": (INT, [P, I64, I64, I32, I32, I32, P, P, F32, INT, P, P, I64, P, P, P, F32, F32, P, P,
+                                       INT, P]),
     "ada_argmax_workspace_size": (SZ, [I64, I64]),
     "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P, SZ, P]),
     "ada_argmax_noalloc": (INT, [P, I64, I64, I64, INT, P, P]),

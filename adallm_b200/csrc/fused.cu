@@ -66,24 +66,31 @@ __device__ __forceinline__ void store8(T* p, const float* f) {
 }
 
 // grid (ctas, m_pad), cluster (ctas, 1, 1).  dst.xq == null: plain RMSNorm (ada_rmsnorm).
+// wpre != null: the loaded row first goes through a GemmaRMSNorm of its own (weight wpre; the
+// post-attention / post-feedforward norm of a Gemma3 layer, applied to the projection output
+// before it joins the residual stream), then the residual add and the main norm as usual.
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict__ x, int64_t ldx, const T* res,
                                                             int64_t ldr, T* res_out, int64_t ldro,
-                                                            const T* __restrict__ w, T* y, int64_t ldy, int rows,
-                                                            int hidden, float eps, int gemma, q::QuantDst dst,
-                                                            PartIn pin, PeerWait pw) {
+                                                            const T* __restrict__ w, const T* __restrict__ wpre, T* y,
+                                                            int64_t ldy, int rows, int hidden, float eps, int gemma,
+                                                            q::QuantDst dst, PartIn pin, PeerWait pw) {
   __shared__ float red[cl::MAX_WARPS];
-  __shared__ cl::Exchange xch[2];
-  cl::cluster_start(xch, 2);
+  __shared__ cl::Exchange xch[3];
+  cl::cluster_start(xch, wpre ? 3 : 2);
   const int m = blockIdx.y;
   int o0, o1;
   slice_of(hidden, o0, o1);
   const bool quant = dst.xq != nullptr;
-  float wf[MAXU][8];  // the norm weight never depends on the previous kernel: load it first
+  float wf[MAXU][8];  // the norm weights never depend on the previous kernel: load them first
+  float wp[MAXU][8];
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
     const int o = my_oct(u, o0, o1);
-    if (o >= 0 && m < rows) load8<T>(w + o * 8, wf[u]);
+    if (o >= 0 && m < rows) {
+      load8<T>(w + o * 8, wf[u]);
+      if (wpre) load8<T>(wpre + o * 8, wp[u]);
+    }
   }
   pdl_wait();
   pdl_trigger();
@@ -105,6 +112,30 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
         load_parts<T, 8>(pin, m, o * 8, v[u]);  // the producing GEMM's split-K planes
       else
         load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+    }
+  }
+  if (wpre) {  // GemmaRMSNorm of the loaded row (layernorm.py:64-74): x * rs * (1 + w), then cast
+    float ss0 = 0.f;
+#pragma unroll
+    for (int u = 0; u < MAXU; ++u)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss0 = fmaf(v[u][i], v[u][i], ss0);
+    cl::cluster_wait();
+    const float rs0 = rsqrtf(cl::cluster_allreduce_x<cl::OpSum>(ss0, red, &xch[2]) / (float)hidden + eps);
+#pragma unroll
+    for (int u = 0; u < MAXU; ++u)
+      if (my_oct(u, o0, o1) >= 0)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          v[u][i] = round_to<T>(__fmul_rn(__fmul_rn(v[u][i], rs0), __fadd_rn(1.f, wp[u][i])));
+  }
+#pragma unroll
+  for (int u = 0; u < MAXU; ++u) {
+    const int o = my_oct(u, o0, o1);
+    if (o >= 0) {
       if (res) {
         float r[8];
         load8<T>(res + (int64_t)m * ldr + o * 8, r);
@@ -117,12 +148,9 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = fmaf(v[u][i], v[u][i], ss);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     }
   }
-  cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
+  if (!wpre) cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
   const float rs = rsqrtf(cl::cluster_allreduce_x<cl::OpSum>(ss, red, &xch[0]) / (float)hidden + eps);
   float amax = 0.f;
 #pragma unroll
@@ -266,7 +294,7 @@ bool quant_args_ok(const q::QuantDst& d) {
 int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro, const void* w,
                    void* y, int64_t ldy, int64_t rows, int64_t launch_rows, int hidden, float eps, int gemma,
                    int dtype, const q::QuantDst& dst, cudaStream_t st, const PartIn& pin = PartIn{nullptr, 0, 0, 0},
-                   const PeerWait& pw = PeerWait{nullptr, 0, 0, nullptr}) {
+                   const PeerWait& pw = PeerWait{nullptr, 0, 0, nullptr}, const void* wpre = nullptr) {
   if (hidden % 16) return ADA_ERR_UNSUPPORTED;
   const cl::RowSplit sp = cl::row_split(hidden / 16);
   if (!sp.maxu || launch_rows > 65535) return ADA_ERR_UNSUPPORTED;
@@ -275,11 +303,11 @@ int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, voi
   if (dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
+                     (const TT*)w, (const TT*)wpre, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
   } else {
     using TT = __half;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
+                     (const TT*)w, (const TT*)wpre, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
@@ -384,7 +412,7 @@ static int rmsnorm_quant_parts_impl(const float* parts, int32_t nparts, int64_t 
                                     const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
                                     const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden, float eps,
                                     int gemma, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
-                                    void* stream, const PeerWait& pw) {
+                                    void* stream, const PeerWait& pw, const void* pre_weight = nullptr) {
   if (rows <= 0 || hidden <= 0 || !weight || (residual && !residual_out) || nparts < 1) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
   const PartIn pin{parts, nparts, plane, ldp};
@@ -393,12 +421,24 @@ static int rmsnorm_quant_parts_impl(const float* parts, int32_t nparts, int64_t 
   const q::QuantDst dst{xq, sfx, gx, quant ? terms : 1, quant ? block_n : 16, hidden};
   if (quant ? !fused::quant_args_ok(dst) : !y) return ADA_ERR_INVALID_ARG;
   if (!fused::a16(weight) || (y && (!fused::a16(y) || (ldy & 7)))) return ADA_ERR_ALIGNMENT;
+  if (pre_weight && !fused::a16(pre_weight)) return ADA_ERR_ALIGNMENT;
   if (residual && (!fused::a16(residual) || !fused::a16(residual_out) || (ld_res & 7) || (ld_res_out & 7)))
     return ADA_ERR_ALIGNMENT;
   const int64_t launch_rows = quant ? cdiv(rows, block_n) * block_n : rows;
   return fused::launch_rmsnorm(nullptr, 0, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
                                launch_rows, hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream), pin,
-                               pw);
+                               pw, pre_weight);
+}
+
+extern "C" int ada_gemma_norm2_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                           const void* post_weight, const void* residual, int64_t ld_res,
+                                           void* residual_out, int64_t ld_res_out, const void* weight, void* y,
+                                           int64_t ldy, int64_t rows, int32_t hidden, float eps, int dtype, int terms,
+                                           int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream) {
+  if (!post_weight || !residual) return ADA_ERR_INVALID_ARG;
+  return rmsnorm_quant_parts_impl(parts, nparts, plane, ldp, residual, ld_res, residual_out, ld_res_out, weight, y,
+                                  ldy, rows, hidden, eps, 1, dtype, terms, block_n, xq, sfx, gx, stream,
+                                  PeerWait{nullptr, 0, 0, nullptr}, post_weight);
 }
 
 extern "C" int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,

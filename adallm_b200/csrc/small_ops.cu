@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_store_kernel(
     const T* __restrict__ qkv, int64_t ld, int hq, int hkv, const T* __restrict__ qw, const T* __restrict__ kw,
     float eps, const int64_t* __restrict__ pos, const float* __restrict__ cs, int64_t max_pos,
     const int32_t* __restrict__ slots, uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, float k_scale,
-    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out, int64_t num_tokens, PartIn pin) {
+    float v_scale, T* __restrict__ q_out, T* __restrict__ k_out, int64_t num_tokens, PartIn pin, int gemma) {
   pdl_wait();
   pdl_trigger();
 
@@ -232,9 +232,15 @@ __global__ void __launch_bounds__(128) qk_norm_rope_store_kernel(
         const float rs = rsqrtf(ss / (float)D + eps);
         const uint2 wu = *reinterpret_cast<const uint2*>(w + lane * 4);
         const T* we = reinterpret_cast<const T*>(&wu);
+        if (gemma) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)  // layernorm.py:24-25: cast, then weight multiply, cast again
-          x[j] = to_f32(from_f32<T>(__fmul_rn(to_f32(from_f32<T>(__fmul_rn(x[j], rs))), to_f32(we[j]))));
+          for (int j = 0; j < 4; ++j)  // layernorm.py:70-73: x * rs * (1 + w) in fp32, then cast
+            x[j] = to_f32(from_f32<T>(__fmul_rn(__fmul_rn(x[j], rs), __fadd_rn(1.f, to_f32(we[j])))));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)  // layernorm.py:24-25: cast, then weight multiply, cast again
+            x[j] = to_f32(from_f32<T>(__fmul_rn(to_f32(from_f32<T>(__fmul_rn(x[j], rs))), to_f32(we[j]))));
+        }
       }
       float y[4];
 #pragma unroll
@@ -501,8 +507,9 @@ static int qk_norm_rope_store_impl(const void* qkv, int64_t ld, const PartIn& pi
                                    const void* k_norm_w, float eps, const int64_t* positions, const float* cos_sin,
                                    int64_t max_position, const int32_t* slot_mapping, uint8_t* k_cache,
                                    uint8_t* v_cache, float k_scale, float v_scale, void* q_out, void* k_out, int dtype,
-                                   void* stream) {
+                                   void* stream, int gemma = 0) {
   if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return ADA_ERR_INVALID_ARG;
+  if (gemma != 0 && gemma != 1) return ADA_ERR_INVALID_ARG;
   if (num_tokens == 0) return ADA_OK;
   if (!positions || !cos_sin || !slot_mapping || !k_cache || !v_cache || !q_out || max_position <= 0)
     return ADA_ERR_INVALID_ARG;
@@ -526,7 +533,7 @@ static int qk_norm_rope_store_impl(const void* qkv, int64_t ld, const PartIn& pi
   (void)ada::launch_k(small::qk_norm_rope_store_kernel<T>, dim3(blocks), dim3(128), 0, st, (const T*)qkv, ld,      \
                       num_q_heads, num_kv_heads, (const T*)q_norm_w, (const T*)k_norm_w, eps, positions, cos_sin, \
                       max_position, slot_mapping, k_cache, v_cache, k_scale, v_scale, (T*)q_out, (T*)k_out,       \
-                      num_tokens, pin)
+                      num_tokens, pin, gemma)
   if (dtype == ADA_DT_BF16) ADA_QK(__nv_bfloat16);
   else ADA_QK(__half);
 #undef ADA_QK
@@ -556,6 +563,30 @@ extern "C" int ada_qk_norm_rope_store_parts(const float* parts, int32_t nparts, 
   return qk_norm_rope_store_impl(nullptr, 0, PartIn{parts, nparts, plane, ldp}, num_tokens, num_q_heads,
                                  num_kv_heads, head_dim, q_norm_w, k_norm_w, eps, positions, cos_sin, max_position,
                                  slot_mapping, k_cache, v_cache, k_scale, v_scale, q_out, k_out, dtype, stream);
+}
+
+extern "C" int ada_qk_norm_rope_store_parts_ex(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                               int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                               int32_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                                               int gemma, const int64_t* positions, const float* cos_sin,
+                                               int64_t max_position, const int32_t* slot_mapping, uint8_t* k_cache,
+                                               uint8_t* v_cache, float k_scale, float v_scale, void* q_out, void* k_out,
+                                               int dtype, void* stream) {
+  if (nparts < 1) return ADA_ERR_INVALID_ARG;
+  return qk_norm_rope_store_impl(nullptr, 0, PartIn{parts, nparts, plane, ldp}, num_tokens, num_q_heads,
+                                 num_kv_heads, head_dim, q_norm_w, k_norm_w, eps, positions, cos_sin, max_position,
+                                 slot_mapping, k_cache, v_cache, k_scale, v_scale, q_out, k_out, dtype, stream, gemma);
+}
+
+extern "C" int ada_qk_norm_rope_store_ex(const void* qkv, int64_t ld, int64_t num_tokens, int32_t num_q_heads,
+                                         int32_t num_kv_heads, int32_t head_dim, const void* q_norm_w,
+                                         const void* k_norm_w, float eps, int gemma, const int64_t* positions,
+                                         const float* cos_sin, int64_t max_position, const int32_t* slot_mapping,
+                                         uint8_t* k_cache, uint8_t* v_cache, float k_scale, float v_scale, void* q_out,
+                                         void* k_out, int dtype, void* stream) {
+  return qk_norm_rope_store_impl(qkv, ld, PartIn{nullptr, 0, 0, 0}, num_tokens, num_q_heads, num_kv_heads, head_dim,
+                                 q_norm_w, k_norm_w, eps, positions, cos_sin, max_position, slot_mapping, k_cache,
+                                 v_cache, k_scale, v_scale, q_out, k_out, dtype, stream, gemma);
 }
 
 extern "C" int ada_gated_act(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter, int act,

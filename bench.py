@@ -386,6 +386,117 @@ def kernel_benches(dev, peak):
     return out
 
 
+def _graph_steps(eng, sess, steps, warmup, prompt, toks):
+    """Device-resident graph steps (forward + on-device advance) after `prompt` + `warmup`
+    untimed ones; (ms per timed step, context lengths when timing starts)."""
+    import torch
+    gr = eng.capture(with_advance=True)
+    sess.prepare(toks)
+    sess.upload()
+    for _ in range(prompt + warmup):
+        gr.replay()
+    torch.cuda.synchronize()
+    ctx_start = sess.lens + prompt + warmup + 1
+    st = torch.cuda.current_stream(eng.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        gr.replay()
+    e1.record(st)
+    e1.synchronize()
+    eng.check_errors()
+    del gr
+    return e0.elapsed_time(e1) / steps, ctx_start
+
+
+def gemma3_bench(dev, peak, steps=32, warmup=3):
+    """the Gemma3-27B-shape decode step (62 layers, hidden 5376, 32/16 heads,
+    GeGLU 21504, vocab 262208 tied lm_head, 5:1 local/global with window 1024) at batch 4 on
+    sequences whose FP8 paged caches already hold U[4096, 16384] tokens (random e4m3), after a
+    16-token prompt; device-resident graph steps, CUDA events.  Algorithmic bytes per step: NVFP4
+    weights + e4m3 scales of every layer, the bf16 lm_head, and the K/V bytes the attention reads
+    (all cached tokens on global layers, the last 1024 on local ones)."""
+    import torch
+    from adallm_b200.decode_step import DecodeSession
+    from adallm_b200.gemma3_step import Gemma3Config, Gemma3DecodeEngine
+    cfg = Gemma3Config()
+    B, prompt = 4, 16
+    g = torch.Generator().manual_seed(0)
+    ctx0 = torch.randint(4096, 16385, (B,), generator=g)
+    eng = Gemma3DecodeEngine(cfg, dev, B, max_ctx=int(ctx0.max()) + prompt + warmup + steps + 8, seed=0)
+    kv = eng.kv_cache.view(torch.uint8)
+    for li in range(cfg.num_layers):  # finite random e4m3 bytes (magnitude codes < 0x7e, random sign)
+        blk = kv[:, li]
+        blk.copy_(torch.randint(0, 0x7e, blk.shape, device=dev, dtype=torch.int16).to(torch.uint8)
+                  | (torch.randint(0, 2, blk.shape, device=dev, dtype=torch.int16).to(torch.uint8) << 7))
+    sess = DecodeSession(eng, seed=0)
+    sess.lens[:] = ctx0
+    ms, ctx_start = _graph_steps(eng, sess, steps, warmup, prompt, torch.randint(0, cfg.vocab, (B,), generator=g))
+    w_bytes = sum(w.n * w.k // 2 + w.n * w.k // 16 for L in eng.layers for w in (L["qkv"], L["o"], L["gate_up"],
+                                                                                 L["down"]))
+    head = cfg.vocab * cfg.hidden * 2
+    per_tok = 2 * cfg.num_kv_heads * cfg.head_dim
+    ctx_mid = (ctx_start + steps // 2).double()
+    kv_bytes = sum(float((ctx_mid if not cfg.is_sliding(li) else ctx_mid.clamp(max=cfg.sliding_window)).sum())
+                   * per_tok for li in range(cfg.num_layers))
+    nb = w_bytes + head + kv_bytes
+    out = {"tok_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4), "layers": cfg.num_layers, "batch": B,
+           "ctx_start": [int(c) for c in ctx_start], "window": cfg.sliding_window, "alg_bytes_per_step": int(nb),
+           "gbs": round(nb / ms / 1e6, 1), "frac": round(nb / ms / 1e6 / peak, 4),
+           "launches_per_step": eng.kernels_per_step(), "mode": "device-resident graph steps"}
+    del eng, sess, kv
+    torch.cuda.empty_cache()
+    return out
+
+
+def moe_bench(dev, peak, steps=32, warmup=3):
+    """the Qwen3-30B-A3B-shape MoE decode step (48 layers, hidden 2048, 32/4
+    heads, 128 experts top-8 of intermediate 768, vocab 151936) at batch 16 after a 16-token
+    prompt, TP = 1; device-resident graph steps, CUDA events.  Algorithmic bytes per step: the
+    attention NVFP4 weights + scales, every expert touched in the step (counted from the routing
+    of one timed step, the same in every layer's estimate) x its gate, up and down weights +
+    scales, the bf16 router and lm_head, the K/V read."""
+    import torch
+    from adallm_b200.decode_step import DecodeSession
+    from adallm_b200.moe_step import MoEConfig, Qwen3MoeDecodeEngine
+    cfg = MoEConfig()
+    B, prompt = 16, 16
+    g = torch.Generator().manual_seed(0)
+    eng = Qwen3MoeDecodeEngine(cfg, dev, B, max_ctx=prompt + warmup + steps + 8, seed=0)
+    sess = DecodeSession(eng, seed=0)
+    ms, ctx_start = _graph_steps(eng, sess, steps, warmup, prompt, torch.randint(0, cfg.vocab, (B,), generator=g))
+    touched = int(eng.route_ids.unique().numel())  # the last layer's routing of the last step
+    ex = eng.layers[0]["experts_gate_up"], eng.layers[0]["experts_down"]
+    per_expert = sum(w.n * w.k // 2 + w.n * w.k // 16 for w in ex)
+    attn = sum(w.n * w.k // 2 + w.n * w.k // 16 for w in (eng.layers[0]["qkv"], eng.layers[0]["o"]))
+    kv = 2 * cfg.num_kv_heads * cfg.head_dim * float((ctx_start + steps // 2).sum())
+    nb = cfg.num_layers * (attn + touched * per_expert + cfg.num_experts * cfg.hidden * 2 + kv) \
+        + cfg.vocab * cfg.hidden * 2
+    out = {"tok_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4), "layers": cfg.num_layers, "batch": B,
+           "experts_touched_per_layer": touched, "alg_bytes_per_step": int(nb), "gbs": round(nb / ms / 1e6, 1),
+           "frac": round(nb / ms / 1e6 / peak, 4), "launches_per_step": eng.kernels_per_step(),
+           "mode": "device-resident graph steps, TP 1"}
+    del eng, sess
+    torch.cuda.empty_cache()
+    return out
+
+
+def dropin_bench(layers=36, batch=16, ctx=64):
+    """The reference runtime's own decode graph (its Qwen3ForCausalLM, KV allocation and graph
+    capture) with this package installed, in a child process (tests/dropin_harness.py)."""
+    import subprocess
+    r = subprocess.run([sys.executable, "-m", "tests.dropin_harness", "bench", "--layers", str(layers), "--batch",
+                        str(batch), "--ctx", str(ctx), "--reps", "20"], cwd=ROOT, capture_output=True, text=True,
+                       timeout=900)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("DROPIN ")]
+    if r.returncode != 0 or not lines:
+        return {"error": (r.stderr or r.stdout)[-400:]}
+    out = json.loads(lines[-1][len("DROPIN "):])
+    out["what"] = ("reference Qwen3ForCausalLM + ModelRunner.capture_cudagraph/run_model with adallm_b200.install() "
+                   "(per-op kernels, page 256); run_model_ms includes the eager lm_head and static-buffer copies")
+    return out
+
+
 def run_reference(args, rank):
     """The reference's own CPU decode path on the host cores (rank 0 only; other ranks exit):
     W warm-up steps, then K timed full decode steps, wall time per step."""
@@ -577,6 +688,13 @@ def run_ours(args, rank, world, local_rank):
                 "launch_mix": "qkv/o/gate_up/down of all layers, batch 16", "per_shape": per_shape}
 
     kernels = kernel_benches(dev, peak) if rank == 0 and world == 1 else None
+    if kernels is not None and args.layers == 36 and B == 16:
+        for name, fn in (("gemma3_config2", gemma3_bench), ("moe_config4", moe_bench)):
+            try:
+                kernels[name] = fn(dev, peak)
+            except Exception as exc:  # recorded; the headline line still prints
+                kernels[name] = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+        kernels["dropin_decode_step"] = dropin_bench(batch=B, ctx=seq_len(args))
 
     ctx_end = int(sess.lens.max().item())
     assert ctx_end == seq_len(args), (ctx_end, seq_len(args))

@@ -420,6 +420,36 @@ ADA_API int ada_qk_norm_rope_store_parts(const float* parts, int32_t nparts, int
                                          float k_scale, float v_scale, void* q_out, void* k_out, int dtype,
                                          void* stream);
 
+/* Gemma3 forms of the producers (adallm/architectures/gemma3.py:156-181; norms layernorm.py:64-92).
+ * ada_gemma_norm2_quant_parts: the projection output (sum of the partial planes, rounded to
+ * dtype) goes through GemmaRMSNorm(post_weight) -- the layer's post-attention or post-feedforward
+ * norm -- then joins the residual stream (bf16: native add, rounded; the new residual is written
+ * to residual_out) and the sum goes through GemmaRMSNorm(weight) -- the next pre-attention /
+ * pre-feedforward / final norm -- quantised into (xq, sfx, gx) as ada_rmsnorm_quant does
+ * (xq == NULL: plain norm into y).  Bit for bit the reference's
+ *   h = post_norm(o); x, residual = pre_norm(h, residual).
+ * ada_qk_norm_rope_store[_parts]_ex: ada_qk_norm_rope_store[_parts] with the per-head norm
+ * chosen by `gemma` (0: RMSNorm, cast then weight multiply; 1: GemmaRMSNorm, x * rs * (1 + w)
+ * then cast, gemma3.py:88-89). */
+ADA_API int ada_gemma_norm2_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                        const void* post_weight, const void* residual, int64_t ld_res,
+                                        void* residual_out, int64_t ld_res_out, const void* weight, void* y,
+                                        int64_t ldy, int64_t rows, int32_t hidden, float eps, int dtype, int terms,
+                                        int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
+ADA_API int ada_qk_norm_rope_store_parts_ex(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,
+                                            int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                            int32_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                                            int gemma, const int64_t* positions, const float* cos_sin,
+                                            int64_t max_position, const int32_t* slot_mapping, uint8_t* k_cache,
+                                            uint8_t* v_cache, float k_scale, float v_scale, void* q_out, void* k_out,
+                                            int dtype, void* stream);
+ADA_API int ada_qk_norm_rope_store_ex(const void* qkv, int64_t ld, int64_t num_tokens, int32_t num_q_heads,
+                                      int32_t num_kv_heads, int32_t head_dim, const void* q_norm_w,
+                                      const void* k_norm_w, float eps, int gemma, const int64_t* positions,
+                                      const float* cos_sin, int64_t max_position, const int32_t* slot_mapping,
+                                      uint8_t* k_cache, uint8_t* v_cache, float k_scale, float v_scale, void* q_out,
+                                      void* k_out, int dtype, void* stream);
+
 /* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum, like torch.argmax),
  * logits bf16/f16.  workspace: ada_argmax_workspace_size(rows, cols) bytes, 8-byte aligned. */
 ADA_API size_t ada_argmax_workspace_size(int64_t rows, int64_t cols);

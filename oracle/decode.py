@@ -48,6 +48,8 @@ class OracleDecoder:
         for L in weights["layers"]:
             d = {}
             for name in ("qkv", "o", "gate_up", "down"):
+                if name not in L:
+                    continue
                 packed, scale, s2 = L[name]
                 if self.numerics == "reference":  # fp16 weight tile values, kept as fp32 for the matmul
                     d[name] = dequant_nvfp4_kernel_fp16(packed, scale, s2).float()
@@ -55,7 +57,8 @@ class OracleDecoder:
                 w = dequant_nvfp4_torch(packed, scale.float(), np.float32(s2))
                 d[name] = w if self.exact else w.to(torch.bfloat16)
             for name in ("in_norm", "post_norm", "q_norm", "k_norm"):
-                d[name] = L[name]
+                if name in L:
+                    d[name] = L[name]
             self.layers.append(d)
         self.embed = weights["embed"]
         self.lm_head = weights["lm_head"]
@@ -107,5 +110,154 @@ class OracleDecoder:
             x, residual = ol.add_rms_norm(h, residual, L["post_norm"], c.rms_eps)
             gu = self._linear(x, L["gate_up"])
             h = self._linear(ol.silu_and_mul(gu), L["down"])
+        x, _ = ol.add_rms_norm(h, residual, self.final_norm, c.rms_eps)
+        return F.linear(x, self.lm_head).float()
+
+
+class Gemma3OracleDecoder(OracleDecoder):
+    """One Gemma3 decode step (adallm/architectures/gemma3.py) with the same numerics modes.
+
+    Reference anchors (paths inside the reference project):
+      * embedding x bf16(sqrt(hidden))        gemma3.py:198-205
+      * decoder layer (4 GemmaRMSNorms)       gemma3.py:156-181
+      * attention (q/k GemmaRMSNorm, local / global RoPE, scale, window)   gemma3.py:32-93, :136-139
+      * MLP GELU(tanh) * up                   gemma3.py:97-125, adallm/ops/activation.py:17-26
+      * final norm, tied lm_head              gemma3.py:205-206, :223-225
+    cfg additionally carries query_pre_attn_scalar, sliding_window and is_sliding(layer);
+    weights carry per layer in_norm / post_attn_norm / pre_ff_norm / post_ff_norm / q_norm /
+    k_norm and the two rope caches cos_sin_local / cos_sin_global."""
+
+    def __init__(self, cfg, weights: dict, numerics: str = "exact"):
+        w = dict(weights)
+        w["cos_sin"] = weights["cos_sin_global"]
+        super().__init__(cfg, w, numerics=numerics)
+        for L, src in zip(self.layers, weights["layers"]):
+            for name in ("post_attn_norm", "pre_ff_norm", "post_ff_norm"):
+                L[name] = src[name]
+        self.cos_sin_local = weights["cos_sin_local"]
+        self.normalizer = torch.tensor(cfg.hidden ** 0.5, dtype=torch.bfloat16)
+
+    def step(self, ids, positions, slot_mapping, context_lens, block_tables, k_caches, v_caches):
+        c = self.cfg
+        B, D = ids.shape[0], c.head_dim
+        hq, hkv = c.num_heads, c.num_kv_heads
+        h = self.embed[torch.as_tensor(ids)] * self.normalizer
+        residual = None
+        pos = torch.as_tensor(positions)
+        attend = paged_decode_fp16_kernel if self.numerics == "reference" else paged_decode
+        for li, L in enumerate(self.layers):
+            if residual is None:
+                residual = h
+                x = ol.gemma_rms_norm(h, L["in_norm"], c.rms_eps)
+            else:
+                x, residual = ol.gemma_add_rms_norm(h, residual, L["in_norm"], c.rms_eps)
+            qkv = self._linear(x, L["qkv"])
+            q, k, v = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+            q = ol.gemma_rms_norm(q.reshape(B, hq, D), L["q_norm"], c.rms_eps)
+            k = ol.gemma_rms_norm(k.reshape(B, hkv, D), L["k_norm"], c.rms_eps)
+            sliding = c.is_sliding(li)
+            q, k = ol.apply_rope(pos, q, k, self.cos_sin_local if sliding else self.cos_sin)
+            _store(k_caches[li], v_caches[li], k, v, slot_mapping, hkv * D)
+            o = attend(q.float().numpy(), k_caches[li], v_caches[li], np.asarray(block_tables),
+                       np.asarray(context_lens), c.query_pre_attn_scalar ** -0.5,
+                       window=c.sliding_window if sliding else 0)
+            o = torch.from_numpy(o).to(torch.float16).to(torch.bfloat16)
+            h = ol.gemma_rms_norm(self._linear(o.reshape(B, hq * D), L["o"]), L["post_attn_norm"], c.rms_eps)
+            x, residual = ol.gemma_add_rms_norm(h, residual, L["pre_ff_norm"], c.rms_eps)
+            gu = self._linear(x, L["gate_up"])
+            h = ol.gemma_rms_norm(self._linear(ol.gelu_and_mul(gu), L["down"]), L["post_ff_norm"], c.rms_eps)
+        x, _ = ol.gemma_add_rms_norm(h, residual, self.final_norm, c.rms_eps)
+        return F.linear(x, self.lm_head).float()
+
+
+def _store(kc, vc, k, v, slot_mapping, width):
+    """The e4m3 KV store of one step (attention.py:245-251): rows with slot -1 are skipped."""
+    kflat = kc.reshape(-1, width)
+    vflat = vc.reshape(-1, width)
+    for b in range(k.shape[0]):
+        s = int(slot_mapping[b])
+        if s >= 0:
+            kflat[s] = e4m3_encode(k[b].float().numpy().reshape(-1))
+            vflat[s] = e4m3_encode(v[b].float().numpy().reshape(-1))
+
+
+class MoEOracleDecoder(OracleDecoder):
+    """One Qwen3-MoE decode step (adallm/architectures/qwen3.py, Qwen3MoeDecoderLayer) with the
+    same numerics modes.  The attention half is OracleDecoder's; the MLP restates
+    Qwen3MoeSparseMoeBlock.forward's TP = 1 path (qwen3.py:1010-1032, :1263-1290):
+      router_logits = F.linear(x, gate)  (bf16);  softmax fp32, top-k, renormalise, to bf16;
+      for each slot k: gate / up / down of expert ids[:, k] (nvfp4_linear_gather, bf16 out),
+      act = SiLU(gate) * up, final += out * w[:, k]  (bf16 arithmetic, slot order).
+    numerics "reference" forms the expert weights as the gather kernel does (fp16 tile,
+    nvfp4_gemm.py:403-449) with fp32 accumulation; the kernel also rounds each product a * b to
+    fp16 before its sum (:452), which is not restated.
+    weights: per layer qkv / o as OracleDecoder, experts_gate_up = (packed [E, 2I, H/2],
+    scale [E, 2I, H/16], scale_2 [E]) with gate rows first, experts_down likewise, router bf16
+    [E, H]; cfg adds num_experts, top_k, moe_intermediate, norm_topk_prob."""
+
+    def __init__(self, cfg, weights: dict, numerics: str = "exact"):
+        super().__init__(cfg, weights, numerics=numerics)
+        for L, src in zip(self.layers, weights["layers"]):
+            L["router"] = src["router"]
+            for name in ("experts_gate_up", "experts_down"):
+                packed, scale, s2 = src[name]
+                mats = []
+                for e in range(packed.shape[0]):
+                    if self.numerics == "reference":
+                        mats.append(dequant_nvfp4_kernel_fp16(packed[e], scale[e], float(s2[e])).float())
+                    else:
+                        mats.append(dequant_nvfp4_torch(packed[e], scale[e].float(), np.float32(s2[e])))
+                L[name] = torch.stack(mats)
+
+    def _moe(self, x: torch.Tensor, L) -> torch.Tensor:
+        c = self.cfg
+        logits = F.linear(x, L["router"])
+        w = torch.softmax(logits.float(), dim=1, dtype=torch.float32)
+        w, ids = torch.topk(w, c.top_k, dim=-1)
+        if c.norm_topk_prob:
+            w = w / w.sum(dim=-1, keepdim=True)
+        w = w.to(x.dtype)
+        final = torch.zeros_like(x)
+        inter = c.moe_intermediate
+        for k in range(c.top_k):
+            gu = torch.empty((x.shape[0], 2 * inter), dtype=x.dtype)
+            out = torch.empty_like(x)
+            experts = ids[:, k].unique().tolist()
+            for e in experts:
+                rows = (ids[:, k] == e).nonzero().view(-1)
+                gu[rows] = self._linear(x[rows], L["experts_gate_up"][e])
+            act = ol.silu_and_mul(gu)
+            for e in experts:
+                rows = (ids[:, k] == e).nonzero().view(-1)
+                out[rows] = self._linear(act[rows], L["experts_down"][e])
+            final = final + out * w[:, k:k + 1]
+        return final
+
+    def step(self, ids, positions, slot_mapping, context_lens, block_tables, k_caches, v_caches):
+        c = self.cfg
+        B, D = ids.shape[0], c.head_dim
+        hq, hkv = c.num_heads, c.num_kv_heads
+        h = self.embed[torch.as_tensor(ids)]
+        residual = None
+        pos = torch.as_tensor(positions)
+        attend = paged_decode_fp16_kernel if self.numerics == "reference" else paged_decode
+        for li, L in enumerate(self.layers):
+            if residual is None:
+                residual = h
+                x = ol.rms_norm(h, L["in_norm"], c.rms_eps)
+            else:
+                x, residual = ol.add_rms_norm(h, residual, L["in_norm"], c.rms_eps)
+            qkv = self._linear(x, L["qkv"])
+            q, k, v = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+            q = ol.rms_norm(q.reshape(B, hq, D), L["q_norm"], c.rms_eps)
+            k = ol.rms_norm(k.reshape(B, hkv, D), L["k_norm"], c.rms_eps)
+            q, k = ol.apply_rope(pos, q, k, self.cos_sin)
+            _store(k_caches[li], v_caches[li], k, v, slot_mapping, hkv * D)
+            o = attend(q.float().numpy(), k_caches[li], v_caches[li], np.asarray(block_tables),
+                       np.asarray(context_lens), D ** -0.5)
+            o = torch.from_numpy(o).to(torch.float16).to(torch.bfloat16)
+            h = self._linear(o.reshape(B, hq * D), L["o"])
+            x, residual = ol.add_rms_norm(h, residual, L["post_norm"], c.rms_eps)
+            h = self._moe(x, L)
         x, _ = ol.add_rms_norm(h, residual, self.final_norm, c.rms_eps)
         return F.linear(x, self.lm_head).float()

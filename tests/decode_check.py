@@ -60,15 +60,60 @@ def run_agreement(cfg: DecodeConfig | None = None, layers=2, steps=8, batch=4, p
                   emulate=False, seed=1) -> Agreement:
     d = torch.device("cuda:0")
     cfg = cfg or small_config(layers)
-    layers = cfg.num_layers
     eng = Qwen3DecodeEngine(cfg, d, batch, max_ctx=prompt + steps + 8, seed=seed)
-    sess = DecodeSession(eng, seed=seed)
-    w = eng.export_cpu_weights()
-    ocfg = SimpleNamespace(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
+    ocfg = SimpleNamespace(num_layers=cfg.num_layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
                            num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, intermediate=cfg.intermediate,
                            rms_eps=cfg.rms_eps, page_size=cfg.page_size)
+    w = eng.export_cpu_weights()
     exact = OracleDecoder(ocfg, w, numerics="exact")
     emul = OracleDecoder(ocfg, w, numerics="reference") if emulate else None
+    return agreement_loop(eng, exact, emul, steps, batch, prompt, graph, seed)
+
+
+def gemma3_test_config(layers: int, window: int = 64):
+    """BASELINE config 2 widths (hidden 5376, 32/16 heads of 128, GeGLU 21504, vocab 262208,
+    5:1 local/global) with `layers` layers and a window short enough for the test's contexts
+    to cross it (the kernels take any window; the bench runs the 1024 of config 2)."""
+    from adallm_b200.gemma3_step import Gemma3Config
+    return Gemma3Config(num_layers=layers, sliding_window=window, max_position=4096)
+
+
+def run_agreement_gemma3(cfg, steps=8, batch=4, prompt=4, graph=True, emulate=False, seed=1) -> Agreement:
+    from adallm_b200.gemma3_step import Gemma3DecodeEngine
+    from oracle.decode import Gemma3OracleDecoder
+    d = torch.device("cuda:0")
+    eng = Gemma3DecodeEngine(cfg, d, batch, max_ctx=prompt + steps + 8, seed=seed)
+    w = eng.export_cpu_weights()
+    exact = Gemma3OracleDecoder(cfg, w, numerics="exact")
+    emul = Gemma3OracleDecoder(cfg, w, numerics="reference") if emulate else None
+    return agreement_loop(eng, exact, emul, steps, batch, prompt, graph, seed)
+
+
+def moe_test_config(layers: int):
+    """BASELINE config 4 widths (hidden 2048, 32/4 heads of 128, 128 experts top-8 of
+    intermediate 768, vocab 151936) with `layers` layers."""
+    from adallm_b200.moe_step import MoEConfig
+    return MoEConfig(num_layers=layers, max_position=4096)
+
+
+def run_agreement_moe(cfg, steps=8, batch=16, prompt=4, graph=True, emulate=False, seed=1) -> Agreement:
+    from adallm_b200.moe_step import Qwen3MoeDecodeEngine
+    from oracle.decode import MoEOracleDecoder
+    d = torch.device("cuda:0")
+    eng = Qwen3MoeDecodeEngine(cfg, d, batch, max_ctx=prompt + steps + 8, seed=seed)
+    w = eng.export_cpu_weights()
+    exact = MoEOracleDecoder(cfg, w, numerics="exact")
+    emul = MoEOracleDecoder(cfg, w, numerics="reference") if emulate else None
+    return agreement_loop(eng, exact, emul, steps, batch, prompt, graph, seed)
+
+
+def agreement_loop(eng, exact, emul, steps, batch, prompt, graph, seed) -> Agreement:
+    """Teacher-forced greedy decode of `prompt` random tokens then `steps` more through the engine
+    (one captured graph per step, or eager launches) and the oracle decoders."""
+    cfg = eng.cfg
+    layers = cfg.num_layers
+    emulate = emul is not None
+    sess = DecodeSession(eng, seed=seed)
 
     def caches():
         kc = [np.zeros((eng.num_pages, cfg.page_size, cfg.num_kv_heads, cfg.head_dim), np.uint8) for _ in range(layers)]
@@ -103,6 +148,7 @@ def run_agreement(cfg: DecodeConfig | None = None, layers=2, steps=8, batch=4, p
                 agree_ref += int((ref_logits.argmax(dim=1) == theirs).sum())
                 ref_errs.append(float((ref_logits - logits).norm() / logits.norm()))
         cur = tokens[:, i + 1] if i + 1 < prompt else theirs
+    eng.check_errors()
     return Agreement(raw=agree / max(total, 1), raw_reference=agree_ref / max(total, 1) if emulate else float("nan"),
                      logits_rel_l2_max=max(errs), logits_rel_l2_mean=float(np.mean(errs)),
                      ref_logits_rel_l2_mean=float(np.mean(ref_errs)) if emulate else float("nan"), tokens=total)
