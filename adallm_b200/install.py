@@ -28,6 +28,8 @@ scale layout is derived from weight_scale on first use and cached on the tensor.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 _INSTALLED = False
@@ -83,6 +85,12 @@ def install(terms: int | None = None, fresh_prefill: str | None = None) -> None:
     N.lib()  # fail loudly now if the CUDA library is missing: there is no fallback
     if terms is not None:
         nvfp4_gemm.DEFAULT_TERMS = int(terms)
+    # NVFP4_FP8=1 selects the reference's W4A8 kernel (e4m3 activations per 64-wide K chunk and
+    # e4m3 weights, nvfp4_gemm.py:23-40, :496-535).  The replacement has one arithmetic for both
+    # settings: the multi-term activation (DEFAULT_TERMS), which sits closer to the exact W4A16
+    # product than the W4A8 kernel does (measured by tests/test_gpu_reference_triton.py).  The
+    # setting is recorded, not acted on.
+    nvfp4_gemm.REFERENCE_FP8_REQUESTED = os.getenv("NVFP4_FP8", "0").strip().lower() not in ("0", "false", "off")
 
     ref_gemm.nvfp4_linear = nvfp4_gemm.nvfp4_linear
     ref_gemm.nvfp4_linear_dual = nvfp4_gemm.nvfp4_linear_dual

@@ -187,6 +187,28 @@ def dequant_nvfp4_kernel_fp16(packed, scale, scale_2, group_size: int = 16):
     return (t.float() * s2).to(torch.float16)
 
 
+def linear_w4a8_ref(x, packed, scale, scale_2, block_k: int = 64):
+    """The reference's W4A8 linear (nvfp4_gemm_kernel_fp8, adallm/ops/nvfp4_gemm.py:252-360, taken
+    when NVFP4_FP8=1 with its defaults NVFP4_FP8_A_SCALE=1, NVFP4_FP8_B_SCALE=0,
+    NVFP4_FP8_BCOL=0, NVFP4_FP8_FORMAT=e4nv; BLOCK_K = 64 for M <= 16 or K < 8192, :480-490).
+    Per BLOCK_K chunk: a = fp16(x); amax = row max |a| over the chunk (0 -> 1);
+    a8 = e4m3(a / amax); b8 = e4m3(b) of the fp16 weight tile b = LUT * scale * scale2 (unscaled);
+    acc += (a8 . b8) * amax in fp32; output fp16.  Returns torch fp16 [M, N]."""
+    import torch
+    a = torch.as_tensor(x).to(torch.float16).float()
+    w16 = dequant_nvfp4_kernel_fp16(packed, scale, scale_2).float()
+    b8 = torch.from_numpy(e4m3_decode(e4m3_encode(w16.numpy())))
+    m, k = a.shape
+    acc = torch.zeros((m, w16.shape[0]), dtype=torch.float32)
+    for k0 in range(0, k, block_k):
+        ac = a[:, k0:k0 + block_k]
+        amax = ac.abs().amax(dim=1, keepdim=True)
+        amax = torch.where(amax == 0, torch.ones_like(amax), amax)
+        a8 = torch.from_numpy(e4m3_decode(e4m3_encode((ac / amax).numpy())))
+        acc += (a8.double() @ b8[:, k0:k0 + block_k].double().t()).float() * amax
+    return acc.to(torch.float16)
+
+
 def quantize_weight(w: np.ndarray, group_size: int = 16):
     """Fixture quantiser for synthetic NVFP4 weights (no reference counterpart).
 

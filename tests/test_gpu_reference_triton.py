@@ -1,0 +1,57 @@
+"""The reference's own Triton kernels run on the B200 (tests/ref_triton_check.py, one process per
+case) pin the oracle's restatements of their arithmetic:
+  * fp16 NVFP4 GEMM (NVFP4_FP8=0) == oracle.decode "reference" linear, within fp32 summation-order
+    noise (rel-L2 < 2e-3; both round to fp16);
+  * W4A8 GEMM (NVFP4_FP8=1, the mode of the reference's published numbers) == oracle.nvfp4
+    .linear_w4a8_ref (rel-L2 < 1e-2: a few e4m3 roundings of a / amax may land differently);
+  * fp8 decode attention (page 256) == oracle.attention.paged_decode_fp16_kernel (< 2e-3).
+And the measurement behind the drop-in's NVFP4_FP8 contract: this package's NVFP4 linear (4
+activation terms) is closer to the exact W4A16 product than the reference's W4A8 path is."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_DIR = os.environ.get("ADALLM_REF", os.path.join(ROOT, "baseline", "_ref"))
+
+
+def _run(mode, fp8="0"):
+    if not os.path.isdir(os.path.join(REF_DIR, "adallm")):
+        pytest.skip("reference package not installed beside the repository")
+    env = dict(os.environ, NVFP4_FP8=fp8)
+    r = subprocess.run([sys.executable, "-m", "tests.ref_triton_check", mode], cwd=ROOT, capture_output=True,
+                       text=True, timeout=900, env=env)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("REFTRITON ")]
+    assert r.returncode == 0 and lines, (r.stdout[-2000:], r.stderr[-4000:])
+    out = json.loads(lines[-1][len("REFTRITON "):])
+    print(json.dumps(out))
+    path = os.environ.get("ADA_AGREEMENT_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"test": f"reference_triton_{mode}_{fp8}", **out}) + "\n")
+    return out
+
+
+def test_reference_fp16_gemm_matches_emulation():
+    r = _run("gemm", "0")
+    assert r["mode"] == "w4a16"
+    assert r["triton_vs_oracle"] < 2e-3, r
+    assert r["ours_vs_exact"] < 1e-2, r
+
+
+def test_reference_w4a8_gemm_matches_restatement_and_is_less_accurate_than_ours():
+    r = _run("gemm", "1")
+    assert r["mode"] == "w4a8"
+    assert r["triton_vs_oracle"] < 1e-2, r
+    assert r["ours_vs_exact"] < r["triton_vs_exact"], r
+
+
+def test_reference_decode_attention_matches_emulation():
+    r = _run("attn")
+    assert r["triton_vs_emulation"] < 2e-3, r
+    assert r["triton_vs_exact"] < 1e-2, r

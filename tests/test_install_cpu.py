@@ -203,3 +203,20 @@ def test_load_time_prepack_hook(ref, monkeypatch):
         assert len(calls) == 1
     finally:
         context.use_context_provider(None)
+
+
+def test_nvfp4_fp8_setting_is_recorded_and_keeps_the_terms(ref, monkeypatch):
+    """NVFP4_FP8=1 (the reference's W4A8 mode) under install(): recorded, and the linear keeps its
+    multi-term activation arithmetic (more accurate than W4A8; measured on the GPU)."""
+    import adallm_b200
+    from adallm_b200 import nvfp4_gemm, context
+    terms = nvfp4_gemm.DEFAULT_TERMS
+    try:
+        monkeypatch.setenv("NVFP4_FP8", "1")
+        adallm_b200.install()
+        assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is True and nvfp4_gemm.DEFAULT_TERMS == terms
+        monkeypatch.setenv("NVFP4_FP8", "0")
+        adallm_b200.install()
+        assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is False and nvfp4_gemm.DEFAULT_TERMS == terms
+    finally:
+        context.use_context_provider(None)
