@@ -62,6 +62,8 @@ _SIGS = {
                                              P, F32, F32, P, P, INT, P]),
     "ada_qk_norm_rope_store_ex": (INT, [P, I64, I64, I32, I32, I32, P, P, F32, INT, P, P, I64, P, P, P, F32, F32, P, P,
                                        INT, P]),
+    "ada_lm_head_workspace_size": (SZ, [I64, I64]),
+    "ada_lm_head_argmax": (INT, [P, I64, I64, I64, P, I64, I64, I64, P, I64, P, P, P, SZ, P]),
     "ada_argmax_workspace_size": (SZ, [I64, I64]),
     "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P, SZ, P]),
     "ada_argmax_noalloc": (INT, [P, I64, I64, I64, INT, P, P]),

@@ -261,8 +261,11 @@ class Qwen3DecodeEngine:
         self.gate_up = torch.zeros((B, 2 * c.inter), dtype=bf, device=d)
         self.act = torch.zeros((B, c.inter), dtype=bf, device=d)
         self.logits = torch.zeros((B, c.vocab_shard), dtype=bf, device=d)
-        self.argmax_ws = torch.zeros(int(N.lib().ada_argmax_workspace_size(B, c.vocab_shard)), dtype=torch.uint8,
-                                     device=d)
+        # lm_head + greedy pick (ada_lm_head_argmax), in groups of at most 64 tokens
+        self.lm_group = min(B, 64)
+        self.lmh_ws = torch.zeros(int(N.lib().ada_lm_head_workspace_size(self.lm_group, c.vocab_shard)),
+                                  dtype=torch.uint8, device=d)
+        self.local_max = torch.zeros(B, dtype=torch.float32, device=d)
         # workspaces (zeroed once; the kernels leave them ready for reuse)
         shapes = [(B, w.n, w.k) for w in self.layers[0].values() if isinstance(w, NVFP4Weight)]
         self.gemm_ws = torch.zeros(max(workspace_bytes(*s, c.terms) for s in shapes), dtype=torch.uint8, device=d)
@@ -442,12 +445,15 @@ class Qwen3DecodeEngine:
         """The int32 device words the step's kernels OR their failure codes into (sticky until
         cleared): the fused path's GEMM workspace word (GEMM pipeline waits, and at TP > 1 the
         peer-inbox waits of the consuming RMSNorm) and the standalone linear's workspace word."""
-        return [self.gemm_only_ws[:4].view(torch.int32), self.gemm_ws[:4].view(torch.int32)]
+        return [self.gemm_only_ws[:4].view(torch.int32), self.gemm_ws[:4].view(torch.int32),
+                self.lmh_ws[:4].view(torch.int32)]
 
     def check_errors(self):
         """Raise if any kernel of the steps run so far gave up a bounded wait (synchronises)."""
-        codes = [int(w.item()) for w in self.error_words()]
-        N.raise_on_error_word(max(codes, key=lambda c: c != 0), "decode step")
+        code = 0
+        for w in self.error_words():
+            code |= int(w.item())
+        N.raise_on_error_word(code, "decode step")
 
     def _all_reduce(self, t: torch.Tensor):
         if self.cfg.tp_size > 1:
@@ -469,8 +475,7 @@ class Qwen3DecodeEngine:
             self._layers_unfused(lib, stream)
         elif self.use_parts:
             self._layers_parts(lib, stream)
-            torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
-            self._argmax(stream)
+            self._lm_head(stream)
             return
         else:
             for li, L in enumerate(self.layers):
@@ -505,8 +510,7 @@ class Qwen3DecodeEngine:
                 self._gemm(self.q_inter, L["down"], self.hidden, stream)
                 self._all_reduce(self.hidden)
         self._rms(self.hidden, self.final_norm, self.xnorm, stream, residual=self.residual)
-        torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
-        self._argmax(stream)
+        self._lm_head(stream)
 
     def _layers_parts(self, lib, stream):
         """Fused step where every projection leaves split-K partial planes and the next kernel
@@ -584,15 +588,22 @@ class Qwen3DecodeEngine:
             self._linear(self.act, L["down"], self.hidden, stream, "down")
             self._all_reduce(self.hidden)
 
-    def _argmax(self, stream):
+    def _lm_head(self, stream):
+        """logits = xnorm . lm_head^T (bf16) and this rank's greedy pick in one tensor-core pass
+        (ada_lm_head_argmax); at TP > 1 the ranks' (max, index) pairs are gathered
+        (vocab_parallel_pick).  The logits are kept for inspection (4.8 MB at bs16)."""
         c = self.cfg
-        N.check(N.lib().ada_argmax(self.logits.data_ptr(), c.vocab_shard, self.B, c.vocab_shard, 0,
-                                   self.next_tokens.data_ptr(), self.argmax_ws.data_ptr(), self.argmax_ws.numel(),
-                                   stream), "argmax")
+        H, V = self.xnorm.shape[1], c.vocab_shard
+        for g0 in range(0, self.B, self.lm_group):
+            g1 = min(self.B, g0 + self.lm_group)
+            st = N.lib().ada_lm_head_argmax(self.xnorm[g0].data_ptr(), H, g1 - g0, H, self.lm_head.data_ptr(),
+                                            self.lm_head.stride(0), V, 0, self.logits[g0].data_ptr(), V,
+                                            self.next_tokens[g0].data_ptr(), self.local_max[g0].data_ptr(),
+                                            self.lmh_ws.data_ptr(), self.lmh_ws.numel(), stream)
+            N.check(st, "lm_head")
         if c.tp_size > 1:
-            loc = self.logits.float().gather(1, self.next_tokens.view(-1, 1)).view(-1)
-            self.next_tokens.copy_(vocab_parallel_pick(loc, self.next_tokens, c.tp_rank, c.vocab_shard, c.tp_size,
-                                                       self.group))
+            self.next_tokens.copy_(vocab_parallel_pick(self.local_max, self.next_tokens, c.tp_rank, c.vocab_shard,
+                                                       c.tp_size, self.group))
 
     # ------------------------------------------------------------------ graphs
     def advance(self):
@@ -668,10 +679,11 @@ class DecodeSession:
         self.h_ctx = torch.zeros(B, dtype=torch.int32).pin_memory() if pin else torch.zeros(B, dtype=torch.int32)
         self.h_out = torch.zeros(B, dtype=torch.int64).pin_memory() if pin else torch.zeros(B, dtype=torch.int64)
         # the engine's device error words, read back with the tokens of every step
-        self.h_err = torch.zeros(2, dtype=torch.int32).pin_memory() if pin else torch.zeros(2, dtype=torch.int32)
+        nerr = len(engine.error_words())
+        self.h_err = torch.zeros(nerr, dtype=torch.int32).pin_memory() if pin else torch.zeros(nerr, dtype=torch.int32)
 
     H2D_BYTES_PER_STEP = property(lambda self: self.e.B * (8 + 8 + 4 + 4))
-    D2H_BYTES_PER_STEP = property(lambda self: self.e.B * 8 + 8)  # tokens + the two error words
+    D2H_BYTES_PER_STEP = property(lambda self: self.e.B * 8 + 4 * self.h_err.numel())  # tokens + error words
 
     def prepare(self, tokens: torch.Tensor):
         """Fill the pinned input buffers for the next step (numpy views: a few microseconds)."""
@@ -698,8 +710,10 @@ class DecodeSession:
         """A bounded device wait that ran out (a GEMM pipeline stage, or at TP > 1 a peer's words
         that never arrived) leaves a code in an error word; the tokens of that step are not
         trusted: raise instead of returning them."""
-        e0, e1 = int(self.h_err[0]), int(self.h_err[1])
-        N.raise_on_error_word(e0 or e1, "decode step")
+        code = 0
+        for v in self.h_err.tolist():
+            code |= int(v)
+        N.raise_on_error_word(code, "decode step")
 
     def download(self) -> torch.Tensor:
         self.h_out.copy_(self.e.next_tokens, non_blocking=True)

@@ -178,8 +178,7 @@ class Gemma3DecodeEngine(Qwen3DecodeEngine):
                                                   stream), "gelu_and_mul+quant")
             planes = ("local",) + self._gemm_parts(self.q_inter, L["down"], "down", stream)
         self._norm2(planes, self.layers[-1]["post_ff_norm"], self.final_norm, None, stream, y=self.xnorm)
-        torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
-        self._argmax(stream)
+        self._lm_head(stream)
 
     def kernels_per_step(self) -> int:
         """Embedding; per layer: norm(+quant), qkv GEMM, q/k-norm+RoPE+store, attention (split +

@@ -234,8 +234,7 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
         N.check(lib.ada_rmsnorm(self.hidden.data_ptr(), H, self.residual.data_ptr(), H, self.residual.data_ptr(), H,
                                 self.final_norm.data_ptr(), self.xnorm.data_ptr(), H, B, H, c.rms_eps, 0, 0, stream),
                 "rms_norm")
-        torch.matmul(self.xnorm, self.lm_head.t(), out=self.logits)
-        self._argmax(stream)
+        self._lm_head(stream)
 
     def kernels_per_step(self) -> int:
         """Embedding; per layer: RMSNorm+quant, qkv GEMM, q/k-norm+RoPE+store, attention (one kernel

@@ -450,6 +450,21 @@ ADA_API int ada_qk_norm_rope_store_ex(const void* qkv, int64_t ld, int64_t num_t
                                       uint8_t* k_cache, uint8_t* v_cache, float k_scale, float v_scale, void* q_out,
                                       void* k_out, int dtype, void* stream);
 
+/* Vocabulary projection with the greedy pick fused in.  Replaces ParallelLMHead.forward's
+ * F.linear (adallm/ops/embed_head.py:56-66) followed by the greedy argmax over its bf16 logits.
+ * x bf16 [m, k] (row stride ldx), w bf16 [vocab, k] (row stride ldw): logits = x . w^T with fp32
+ * accumulation rounded to bf16 (written to `logits` [m][ldl] when it is not NULL); out_idx[r] =
+ * idx_base + the first row of the maximum bf16 logit of token r (torch.argmax), out_val[r] = that
+ * logit as fp32 (either may be NULL).  idx_base: the first vocabulary row of this shard.
+ * Implemented: m <= 64, k % 64 == 0, x / w 16-byte aligned with ldx, ldw % 8 == 0.
+ * workspace: ada_lm_head_workspace_size(m, vocab) bytes, 256-byte aligned (first 4 bytes: the
+ * error word, a bounded pipeline wait that ran out ORs 1/2/4/8 into it).  Two kernels: the
+ * persistent tcgen05 projection (one CTA per SM) and the cross-tile pick. */
+ADA_API size_t ada_lm_head_workspace_size(int64_t m, int64_t vocab);
+ADA_API int ada_lm_head_argmax(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw,
+                               int64_t vocab, int64_t idx_base, void* logits, int64_t ldl, int64_t* out_idx,
+                               float* out_val, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Greedy sampling helper: out[r] = argmax_j logits[r, j] (first maximum, like torch.argmax),
  * logits bf16/f16.  workspace: ada_argmax_workspace_size(rows, cols) bytes, 8-byte aligned. */
 ADA_API size_t ada_argmax_workspace_size(int64_t rows, int64_t cols);
