@@ -64,6 +64,8 @@ _SIGS = {
                                        INT, P]),
     "ada_lm_head_workspace_size": (SZ, [I64, I64]),
     "ada_lm_head_argmax": (INT, [P, I64, I64, I64, P, I64, I64, I64, P, I64, P, P, P, SZ, P]),
+    "ada_nvfp4_gemm_partials_pf": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, I64, I64, INT, P, SZ, P,
+                                        SZ, P, SZ, P]),
     "ada_argmax_workspace_size": (SZ, [I64, I64]),
     "ada_argmax": (INT, [P, I64, I64, I64, INT, P, P, SZ, P]),
     "ada_argmax_noalloc": (INT, [P, I64, I64, I64, INT, P, P]),

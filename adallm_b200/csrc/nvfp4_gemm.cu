@@ -68,7 +68,24 @@ struct GemmParams {
   unsigned long long* inbox[MAX_PEERS];
   const unsigned int* epoch;
   unsigned int tag_mul, tag_add;
+  // optional: byte ranges (the next projection's packed weights and scale factors) that this
+  // launch's CTAs pull into L2 once their own loads are issued, so the next GEMM of a decode
+  // layer finds its weights in L2 while the latency-bound kernels in between leave HBM idle
+  const uint8_t* pf[2];
+  int64_t pf_bytes[2];
 };
+
+// This CTA's share (CTA `id` of `n`) of `bytes` starting at `base`, requested into L2 in pieces
+// of at most 32 KiB (16-byte aligned addresses and sizes; `bytes` a multiple of 16).
+__device__ __forceinline__ void prefetch_share(const uint8_t* base, int64_t bytes, int64_t id, int64_t n) {
+  if (!base || bytes <= 0) return;
+  const int64_t chunk = ((bytes + n - 1) / n + 15) & ~int64_t(15);
+  const int64_t b0 = id * chunk, b1 = b0 + chunk < bytes ? b0 + chunk : bytes;
+  for (int64_t off = b0; off < b1; off += 32768) {
+    const int64_t sz = b1 - off < 32768 ? b1 - off : 32768;
+    sm100::bulk_prefetch_l2(base + off, (uint32_t)sz);
+  }
+}
 
 template <int BN, int T>
 struct Cfg {
@@ -218,6 +235,9 @@ __global__ void __launch_bounds__(192, (BN * T <= 96) ? 3 : 2)
           bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
                     p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES, &full[s]);
       }
+      // every load of this CTA is issued: its share of the next projection's weights goes to L2
+      const int64_t cta = (int64_t)blockIdx.y * gridDim.x + blockIdx.x, ctas = (int64_t)gridDim.x * gridDim.y;
+      for (int r = 0; r < 2; ++r) prefetch_share(p.pf[r], p.pf_bytes[r], cta, ctas);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -870,7 +890,8 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
                     float* part = nullptr, int64_t part_plane = 0, int64_t part_ld = 0, int world = 1, int tp_rank = 0,
                     unsigned long long* const* inboxes = nullptr, const unsigned int* epoch = nullptr,
                     unsigned int tag_mul = 0, unsigned int tag_add = 0, const int* tile_expert = nullptr,
-                    const int* row_map = nullptr, int64_t w_rows = 0) {
+                    const int* row_map = nullptr, int64_t w_rows = 0, const uint8_t* const* pf = nullptr,
+                    const int64_t* pf_bytes = nullptr) {
   CUtensorMap tmw, tmx;
   if (!make_map(&tmw, w_packed, (uint64_t)(k / 2), (uint64_t)(w_rows ? w_rows : n), (uint64_t)ldw, BM))
     return ADA_ERR_CUDA;
@@ -908,6 +929,10 @@ static int run_gemm(const Plan& P, const uint8_t* xq, const uint8_t* sfx, const 
   gp.tile_expert = tile_expert;
   gp.row_map = row_map;
   gp.m_tiles_max = P.m_tiles;
+  for (int r = 0; r < 2; ++r) {
+    gp.pf[r] = pf ? pf[r] : nullptr;
+    gp.pf_bytes[r] = pf && pf[r] ? pf_bytes[r] : 0;
+  }
   return dispatch_gemm(tmw, tmx, gp, P, st);
 }
 
@@ -1205,6 +1230,36 @@ extern "C" int ada_nvfp4_gemm_splits(int64_t m, int64_t n, int64_t k, int terms)
   fp4::Plan P;
   if (fp4::make_plan(m, n, k, terms, 0, P, true) != ADA_OK) return 0;
   return P.ks;
+}
+
+static bool pf_ok(const void* p, size_t bytes) { return !p || (((uintptr_t)p & 15) == 0 && (bytes & 15) == 0); }
+
+extern "C" int ada_nvfp4_gemm_partials_pf(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m,
+                                          int terms, int block_n, const uint8_t* w_packed, int64_t ldw,
+                                          const uint8_t* sf_w, const float* w_scale_2, int64_t n, int64_t k,
+                                          float* parts, int64_t part_ld, int64_t part_plane, int nplanes,
+                                          const void* next_w, size_t next_w_bytes, const void* next_sf,
+                                          size_t next_sf_bytes, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  if (m == 0) return ADA_OK;
+  if (!xq || !gx || !w_packed || !sf_w || !w_scale_2 || !parts || !workspace) return ADA_ERR_INVALID_ARG;
+  if (terms == 1 && !sfx) return ADA_ERR_INVALID_ARG;
+  if (ldw < k / 2 || part_ld < n || part_plane < m * part_ld || nplanes < 1) return ADA_ERR_INVALID_ARG;
+  if (part_ld > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
+  if (!pf_ok(next_w, next_w_bytes) || !pf_ok(next_sf, next_sf_bytes)) return ADA_ERR_ALIGNMENT;
+  fp4::Plan P;
+  int rc = fp4::make_plan(m, n, k, terms, nplanes, P, true);
+  if (rc != ADA_OK) return rc;
+  if (block_n != P.bn || P.ks != nplanes) return ADA_ERR_INVALID_ARG;
+  if (workspace_bytes < fp4::ERR_BYTES) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)xq & 15) || (sfx && ((uintptr_t)sfx & 15)) || ((uintptr_t)w_packed & 15) || (ldw & 15) ||
+      ((uintptr_t)sf_w & 15) || ((uintptr_t)workspace & 255) || ((uintptr_t)parts & 3))
+    return ADA_ERR_ALIGNMENT;
+  const uint8_t* pf[2] = {reinterpret_cast<const uint8_t*>(next_w), reinterpret_cast<const uint8_t*>(next_sf)};
+  const int64_t pfb[2] = {(int64_t)next_w_bytes, (int64_t)next_sf_bytes};
+  return fp4::run_gemm(P, xq, sfx, gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, nullptr,
+                       ADA_DT_BF16, n, reinterpret_cast<unsigned int*>(workspace), reinterpret_cast<cudaStream_t>(stream),
+                       parts, part_plane, part_ld, 1, 0, nullptr, nullptr, 0, 0, nullptr, nullptr, 0, pf, pfb);
 }
 
 extern "C" int ada_nvfp4_gemm_partials(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,

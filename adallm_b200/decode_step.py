@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 import zlib
 from dataclasses import dataclass, field
 
@@ -181,6 +182,8 @@ class Qwen3DecodeEngine:
                  group=None, fused: bool = True):
         self.cfg = cfg
         self.fused = fused
+        # each GEMM of the step pulls the next one's weights into L2 (ADALLM_B200_L2_PREFETCH=0: off)
+        self.l2_prefetch = os.environ.get("ADALLM_B200_L2_PREFETCH", "1") != "0"
         self.device = torch.device(device)
         self.B = max_batch
         self.max_pages_per_seq = -(-max_ctx // cfg.page_size)
@@ -346,11 +349,11 @@ class Qwen3DecodeEngine:
         lib.ada_peer_free(self._peer_own)
         self._peer_own = None
 
-    def _gemm_rowpar(self, qb, w: NVFP4Weight, name: str, li: int, stream: int):
+    def _gemm_rowpar(self, qb, w: NVFP4Weight, name: str, li: int, stream: int, next_w: NVFP4Weight | None = None):
         """Row-parallel projection (o / down): TP1 -> local partial planes; TP > 1 -> this rank's
         partials, tagged for (step, layer, kind), into every rank's inbox of that kind."""
         if not self.tp_peer:
-            return ("local",) + self._gemm_parts(qb, w, name, stream)
+            return ("local",) + self._gemm_parts(qb, w, name, stream, next_w=next_w)
         c, B, W = self.cfg, self.B, self.cfg.tp_size
         xq, sfx, gx = qb
         ks, kind = self.peer_ks[name], (0 if name == "o" else 1)
@@ -385,15 +388,20 @@ class Qwen3DecodeEngine:
                                     self.gemm_only_ws.numel(), stream)
         N.check(st, "NVFP4 kernel")
 
-    def _gemm_parts(self, qb, w: NVFP4Weight, name: str, stream: int):
+    def _gemm_parts(self, qb, w: NVFP4Weight, name: str, stream: int, next_w: NVFP4Weight | None = None):
+        """Partial-plane GEMM; with next_w (and L2 prefetch on) its CTAs also pull the next
+        projection's packed weights and scale factors into L2 once their own loads are issued."""
         c = self.cfg
         xq, sfx, gx = qb
         ns = self.splits[name]
-        st = N.lib().ada_nvfp4_gemm_partials(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), self.B, c.terms, self.bn,
-                                             w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
-                                             w.scale_2.data_ptr(), w.n, w.k, self.parts.data_ptr(), w.n,
-                                             self.B * w.n, ns, self.gemm_only_ws.data_ptr(),
-                                             self.gemm_only_ws.numel(), stream)
+        nw = next_w if self.l2_prefetch else None
+        st = N.lib().ada_nvfp4_gemm_partials_pf(xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(), self.B, c.terms,
+                                                self.bn, w.packed.data_ptr(), w.packed.stride(0), w.sf.data_ptr(),
+                                                w.scale_2.data_ptr(), w.n, w.k, self.parts.data_ptr(), w.n,
+                                                self.B * w.n, ns, N.ptr(nw.packed if nw else None),
+                                                nw.packed.numel() if nw else 0, N.ptr(nw.sf if nw else None),
+                                                nw.sf.numel() if nw else 0, self.gemm_only_ws.data_ptr(),
+                                                self.gemm_only_ws.numel(), stream)
         N.check(st, "NVFP4 kernel")
         return ns, w.n  # planes, row stride
 
@@ -521,12 +529,13 @@ class Qwen3DecodeEngine:
         qn = c.hq * D
         planes = None
         for li, L in enumerate(self.layers):
+            nxt = self.layers[li + 1] if li + 1 < len(self.layers) else None
             if li == 0:
                 self.residual.copy_(self.hidden)
                 self._rms_quant(self.hidden, L["in_norm"], self.q_hidden, stream)
             else:
                 self._rms_quant_parts(planes, L["in_norm"], self.q_hidden, stream)
-            ns, ld = self._gemm_parts(self.q_hidden, L["qkv"], "qkv", stream)
+            ns, ld = self._gemm_parts(self.q_hidden, L["qkv"], "qkv", stream, next_w=L["o"])
             kc, vc = self.kv_cache[0, li], self.kv_cache[1, li]
             N.check(lib.ada_qk_norm_rope_store_parts(self.parts.data_ptr(), ns, B * ld, ld, B, c.hq, c.hkv, D,
                                                      L["q_norm"].data_ptr(), L["k_norm"].data_ptr(), c.rms_eps,
@@ -541,14 +550,15 @@ class Qwen3DecodeEngine:
                 self.max_pages_per_seq, self.context_lens.data_ptr(), B, c.hq, c.hkv, D, c.page_size,
                 D ** -0.5, 1.0, 1.0, 0, None, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
                 gx.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws_bytes, ATTN_META_EARLY, stream), "attention")
-            planes = self._gemm_rowpar(self.q_attn, L["o"], "o", li, stream)
+            planes = self._gemm_rowpar(self.q_attn, L["o"], "o", li, stream, next_w=L["gate_up"])
             self._rms_quant_parts(planes, L["post_norm"], self.q_hidden, stream)
-            ns, ld = self._gemm_parts(self.q_hidden, L["gate_up"], "gate_up", stream)
+            ns, ld = self._gemm_parts(self.q_hidden, L["gate_up"], "gate_up", stream, next_w=L["down"])
             xq, sfx, gx = self.q_inter
             N.check(lib.ada_gated_act_quant_parts(self.parts.data_ptr(), ns, B * ld, ld, None, 0, B, c.inter, 0, 0,
                                                   c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(),
                                                   stream), "silu_and_mul+quant")
-            planes = self._gemm_rowpar(self.q_inter, L["down"], "down", li, stream)
+            planes = self._gemm_rowpar(self.q_inter, L["down"], "down", li, stream,
+                                       next_w=nxt["qkv"] if nxt is not None else None)
         self._rms_quant_parts(planes, self.final_norm, None, stream, y=self.xnorm)
         if self.tp_peer:  # every counter of this step has been consumed
             N.check(lib.ada_tp_epoch_advance(self.epoch_ptr, stream), "tp epoch")

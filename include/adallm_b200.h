@@ -359,6 +359,18 @@ ADA_API int ada_nvfp4_gemm_partials(const uint8_t* xq, const uint8_t* sfx, const
                                     int64_t part_plane, int nplanes, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/* ada_nvfp4_gemm_partials with the next projection's weights pulled into L2: once each CTA has
+ * issued its own loads it requests its share of [next_w, next_w + next_w_bytes) and
+ * [next_sf, + next_sf_bytes) into L2 (fire-and-forget prefetches, no result, no wait), so the
+ * GEMM after the latency-bound kernels between the two finds its weights in L2.  Either range may
+ * be NULL / 0; addresses and sizes 16-byte aligned.  No reference counterpart. */
+ADA_API int ada_nvfp4_gemm_partials_pf(const uint8_t* xq, const uint8_t* sfx, const float* gx, int64_t m, int terms,
+                                       int block_n, const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                       const float* w_scale_2, int64_t n, int64_t k, float* parts, int64_t part_ld,
+                                       int64_t part_plane, int nplanes, const void* next_w, size_t next_w_bytes,
+                                       const void* next_sf, size_t next_sf_bytes, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Tensor parallelism over NVLink peer memory (no counterpart in the reference, whose row-parallel
  * linears all-reduce their outputs with NCCL, adallm/ops/linear.py:193-215).  One process per GPU;
