@@ -50,6 +50,7 @@ def parse_args():
     ap.add_argument("--prompt", type=int, default=16)
     ap.add_argument("--terms", type=int, default=4, help="activation e2m1 terms (1 = W4A4 NVFP4, 2..8 row-scaled)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel and other-config lines")
     ap.add_argument("--cpu-reps", type=int, default=3)
     return ap.parse_args()
 
@@ -687,7 +688,7 @@ def run_ours(args, rank, world, local_rank):
                 "alg_bytes_per_launch": int(alg_bytes), "us_per_launch": round(gemm_ms * 1e3, 3),
                 "launch_mix": "qkv/o/gate_up/down of all layers, batch 16", "per_shape": per_shape}
 
-    kernels = kernel_benches(dev, peak) if rank == 0 and world == 1 else None
+    kernels = kernel_benches(dev, peak) if rank == 0 and world == 1 and not args.no_kernels else None
     if kernels is not None and args.layers == 36 and B == 16:
         for name, fn in (("gemma3_config2", gemma3_bench), ("moe_config4", moe_bench)):
             try:

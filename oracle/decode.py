@@ -29,6 +29,7 @@ import torch.nn.functional as F
 
 from . import layers as ol
 from .attention import paged_decode, paged_decode_fp16_kernel
+from .moe import route_topk
 from .nvfp4 import dequant_nvfp4_kernel_fp16, dequant_nvfp4_torch, e4m3_encode
 
 
@@ -211,12 +212,7 @@ class MoEOracleDecoder(OracleDecoder):
 
     def _moe(self, x: torch.Tensor, L) -> torch.Tensor:
         c = self.cfg
-        logits = F.linear(x, L["router"])
-        w = torch.softmax(logits.float(), dim=1, dtype=torch.float32)
-        w, ids = torch.topk(w, c.top_k, dim=-1)
-        if c.norm_topk_prob:
-            w = w / w.sum(dim=-1, keepdim=True)
-        w = w.to(x.dtype)
+        ids, w = route_topk(F.linear(x, L["router"]), c.top_k, c.norm_topk_prob, x.dtype)
         final = torch.zeros_like(x)
         inter = c.moe_intermediate
         for k in range(c.top_k):

@@ -1,7 +1,7 @@
 """The tensor-core lm_head with the fused greedy pick (ada_lm_head_argmax) through the C ABI.
 
-* logits: within 2 bf16 ulps of x . W^T computed in fp32 and rounded to bf16 (the reference's
-  F.linear, adallm/ops/embed_head.py:56-66, accumulates in fp32 and rounds once);
+* logits: within one bf16 ulp (plus 2^-11 for the fp32 accumulation over k) of x . W^T in fp64
+  (the reference's F.linear, adallm/ops/embed_head.py:56-66, accumulates in fp32 and rounds once);
 * the pick: exactly torch.argmax over the kernel's own bf16 logits (first maximum), and the
   returned value is that logit; planted ties (duplicated weight rows, in one tile and across
   tiles) go to the lower row; idx_base offsets the index (a vocabulary shard);
@@ -40,9 +40,11 @@ def test_lm_head_logits_and_pick(m, v, k):
     w = (torch.randn((v, k), generator=g) * 0.02).to(torch.bfloat16).to(d)
     lg, idx, val, ws = _call(x, w)
     torch.cuda.synchronize()
-    ref = (x.float() @ w.float().t())
+    # fp64 product on the host; the kernel's fp32 accumulation over k terms of mean magnitude
+    # ~0.013 adds up to ~1e-4 absolute, the bf16 rounding half an ulp
+    ref = (x.double().cpu() @ w.double().cpu().t())
     ulp = torch.clamp(ref.abs(), min=2.0 ** -100).log2().floor().exp2() * 2.0 ** -7
-    assert bool(((lg.float() - ref).abs() <= 2 * ulp + 1e-6).all())
+    assert bool(((lg.double().cpu() - ref).abs() <= ulp + 2.0 ** -11).all())
     assert torch.equal(idx, lg.float().argmax(dim=1))
     assert torch.equal(val, lg.float().max(dim=1).values)
     assert int(ws[:4].view(torch.int32).item()) == 0

@@ -36,6 +36,21 @@ def test_route_topk_matches_torch(t, e, k, norm):
     assert torch.allclose(w.float(), rw.float(), rtol=2 ** -7, atol=1e-6)
 
 
+@pytest.mark.parametrize("t,e,k,norm", [(16, 128, 8, True), (7, 64, 4, False)])
+def test_route_topk_matches_cpu_oracle(t, e, k, norm):
+    """Against the CPU restatement of qwen3.py:1026-1032 (oracle.moe) on N(0, 1) bf16 logits (the
+    config-4 router): identical experts in identical order, weights within one bf16 ulp."""
+    from oracle.moe import route_topk as oracle_route
+    d = dev()
+    g = torch.Generator().manual_seed(100 + t)
+    logits = torch.randn((t, e), generator=g).to(torch.bfloat16)
+    ids, w = route_topk(logits.to(d), k, norm)
+    rid, rw = oracle_route(logits, k, norm)
+    torch.cuda.synchronize()
+    assert torch.equal(ids.long().cpu(), rid)
+    assert torch.allclose(w.float().cpu(), rw.float(), rtol=2 ** -8, atol=0)
+
+
 def test_combine_weighted_sum():
     d = dev()
     t, k, h = 7, 8, 2048

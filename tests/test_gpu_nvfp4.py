@@ -138,10 +138,13 @@ def test_prefill_size(terms, tol):
     assert rel_l2(y.float(), ref) < tol
 
 
-def test_config0_full_size():
-    # x bf16 [16, 4096] ~N(0,1), W [12288, 4096] NVFP4, output bf16 [16, 12288]
+@pytest.mark.parametrize("realistic", [True, False])
+def test_config0_full_size(realistic):
+    # x bf16 [16, 4096] ~N(0,1), W [12288, 4096] NVFP4, output bf16 [16, 12288];
+    # realistic: the whole matrix N(0, 0.02) through the fixture quantiser (block amax / 6 e4m3
+    # scales, amax / 2688 global scale), else random codes and scales
     m, n, k = 16, 12288, 4096
-    packed, sbits, scale16, s2 = random_weight(n, k, seed=0, realistic=False)
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=0, realistic=realistic)
     xb = torch.randn((m, k), generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
     y = run_linear(xb, packed, scale16, s2, 4)
     y_ref = nv.linear_ref(xb.float().numpy(), packed, scale16.astype(np.float32), s2)
