@@ -24,6 +24,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 
 from . import _native as N
 from .decode_step import ATTN_META_EARLY, Qwen3DecodeEngine, random_nvfp4, stable_seed
@@ -51,6 +52,8 @@ class MoEConfig:
     terms: int = 4
     tp_size: int = 1
     tp_rank: int = 0
+    ep_size: int = 1   # expert parallelism: rank ep_rank holds experts [ep_rank * E / ep_size, +E / ep_size)
+    ep_rank: int = 0
 
     hq = property(lambda self: self.num_heads)
     hkv = property(lambda self: self.num_kv_heads)
@@ -83,12 +86,23 @@ class Experts:
 
 
 class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
-    """Static-shape MoE decode engine for batch ``max_batch`` (graph-capturable, TP = 1)."""
+    """Static-shape MoE decode engine for batch ``max_batch`` (graph-capturable).
 
-    def __init__(self, cfg: MoEConfig, device, max_batch: int, max_ctx: int, seed: int = 0):
+    Attention runs at tensor-parallel size 1 (as the reference's MoE).  With cfg.ep_size > 1
+    (expert parallelism, beyond the reference; one process per GPU, `group` the NCCL group of the
+    ep_size ranks) every rank runs the same attention and routing, holds a contiguous block of
+    experts, runs the grouped GEMMs over the rows routed to its experts only
+    (ada_nvfp4_linear_grouped_ep), sums its slots (ada_moe_combine_ep) and all-reduces the block
+    output: one NCCL all-reduce of [batch, hidden] bf16 per layer."""
+
+    def __init__(self, cfg: MoEConfig, device, max_batch: int, max_ctx: int, seed: int = 0, group=None):
         if cfg.tp_size != 1:
-            raise ValueError("the MoE decode engine runs at tensor-parallel size 1 (as the reference's MoE)")
-        super().__init__(cfg, device, max_batch, max_ctx, seed=seed, group=None, fused=True)
+            raise ValueError("the MoE decode engine runs attention at tensor-parallel size 1 (as the reference)")
+        if cfg.num_experts % cfg.ep_size or not 0 <= cfg.ep_rank < cfg.ep_size:
+            raise ValueError("experts must split evenly over the expert-parallel ranks")
+        self.local_experts = cfg.num_experts // cfg.ep_size
+        self.expert_base = cfg.ep_rank * self.local_experts
+        super().__init__(cfg, device, max_batch, max_ctx, seed=seed, group=group, fused=True)
         if not self.use_parts:
             raise ValueError("MoE engine: an attention projection has no partial-plane split at this batch")
         self._alloc_moe()
@@ -96,14 +110,15 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
     def _experts(self, name: str, layer: int, n: int, k: int) -> Experts:
         c = self.cfg
         packs, scales, s2 = [], [], []
-        for e in range(c.num_experts):
+        for e in range(self.expert_base, self.expert_base + self.local_experts):  # seeded by the global id
             p, s, g2 = random_nvfp4(n, k, stable_seed(self.seed, "expert", name, layer, e), self.device)
             packs.append(p)
             scales.append(s)
             s2.append(g2)
         packed = torch.stack(packs).contiguous()
         scale = torch.stack(scales).contiguous()
-        sf = prepack_scales(scale.view(c.num_experts * n, k // 16), c.num_experts * n, k)
+        ne = self.local_experts
+        sf = prepack_scales(scale.view(ne * n, k // 16), ne * n, k)
         return Experts(packed, scale, torch.tensor(s2, dtype=torch.float32, device=self.device), sf)
 
     def _init_weights(self):
@@ -165,10 +180,17 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
         return words
 
     def _grouped(self, x: torch.Tensor, w: Experts, y: torch.Tensor, ws: torch.Tensor, stream: int):
-        st = N.lib().ada_nvfp4_linear_grouped(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
+        lib = N.lib()
+        if self.cfg.ep_size == 1:
+            st = lib.ada_nvfp4_linear_grouped(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
                                               w.packed.stride(1), w.sf.data_ptr(), w.scale_2.data_ptr(), w.e, w.n,
                                               self.route_ids.data_ptr(), y.data_ptr(), 0, y.stride(0), self.cfg.terms,
                                               ws.data_ptr(), ws.numel(), stream)
+        else:  # rows routed to other ranks' experts are skipped
+            st = lib.ada_nvfp4_linear_grouped_ep(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
+                                                 w.packed.stride(1), w.sf.data_ptr(), w.scale_2.data_ptr(), w.e,
+                                                 self.expert_base, w.n, self.route_ids.data_ptr(), y.data_ptr(), 0,
+                                                 y.stride(0), self.cfg.terms, ws.data_ptr(), ws.numel(), stream)
         N.check(st, "grouped NVFP4 kernel")
 
     def _moe_block(self, L, stream: int):
@@ -186,9 +208,16 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
                                   self.a_rows.stride(0), self.a_rows.shape[0], c.moe_intermediate, 0, 0, stream),
                 "silu_and_mul")
         self._grouped(self.a_rows, L["experts_down"], self.y_rows, self.ws_down, stream)
-        N.check(lib.ada_moe_combine(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(), B,
-                                    c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
-                "moe combine")
+        if c.ep_size == 1:
+            N.check(lib.ada_moe_combine(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(), B,
+                                        c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
+                    "moe combine")
+        else:  # this rank's slots, then the sum over the ranks
+            N.check(lib.ada_moe_combine_ep(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(),
+                                           self.route_ids.data_ptr(), self.expert_base, self.local_experts, B,
+                                           c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
+                    "moe combine (expert-parallel)")
+            dist.all_reduce(self.hidden, group=self.group)
 
     def forward(self):
         c = self.cfg
@@ -240,11 +269,13 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
         """Embedding; per layer: RMSNorm+quant, qkv GEMM, q/k-norm+RoPE+store, attention (one kernel
         for short caches, else split + merge+quant), o GEMM, RMSNorm from planes, route top-k,
         grouped gate_up (route + gathering quantiser + GEMM), SiLU*up, grouped down (3), combine;
-        final RMSNorm; argmax x2."""
+        final RMSNorm; lm_head + pick (the expert-parallel all-reduce is NCCL's)."""
         attn = 1 if self.max_pages_per_seq * self.cfg.page_size <= 1024 and self.cfg.hkv <= 8 else 2
         return 1 + self.cfg.num_layers * (14 + attn) + 3
 
     def export_cpu_weights(self) -> dict:
+        if self.cfg.ep_size != 1:
+            raise ValueError("CPU weights are exported from an engine holding every expert (ep_size 1)")
         layers = []
         for L in self.layers:
             d = {}
