@@ -12,6 +12,8 @@
 // CTA exits while a peer still writes into it.
 #pragma once
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace ada {
@@ -167,10 +169,21 @@ __device__ __forceinline__ float cluster_allreduce_x(float v, float* red, Exchan
 struct RowSplit {
   int ctas, threads, maxu;
 };
+// Largest cluster a row is spread over: 8, or ADALLM_B200_ROW_CLUSTER (1..8; a tuning knob read
+// once per process -- every kernel of the process then rounds its rows alike).
+inline int row_cluster_cap() {
+  static int cap = [] {
+    const char* e = std::getenv("ADALLM_B200_ROW_CLUSTER");
+    const int v = e ? std::atoi(e) : MAX_CLUSTER;
+    return v >= 1 && v <= MAX_CLUSTER ? v : MAX_CLUSTER;
+  }();
+  return cap;
+}
 inline RowSplit row_split(int units) {
   RowSplit s;
+  const int cap = row_cluster_cap();
   s.ctas = units / 32;
-  s.ctas = s.ctas < 1 ? 1 : s.ctas > MAX_CLUSTER ? MAX_CLUSTER : s.ctas;
+  s.ctas = s.ctas < 1 ? 1 : s.ctas > cap ? cap : s.ctas;
   const int octets = 2 * ((units + s.ctas - 1) / s.ctas);
   s.threads = ((octets + 31) / 32) * 32;
   if (s.threads > 512) s.threads = 512;

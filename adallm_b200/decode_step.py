@@ -182,8 +182,9 @@ class Qwen3DecodeEngine:
                  group=None, fused: bool = True):
         self.cfg = cfg
         self.fused = fused
-        # each GEMM of the step pulls the next one's weights into L2 (ADALLM_B200_L2_PREFETCH=0: off)
-        self.l2_prefetch = os.environ.get("ADALLM_B200_L2_PREFETCH", "1") != "0"
+        # each GEMM pulling the next one's weights into L2 (ADALLM_B200_L2_PREFETCH=1) measured 2%
+        # slower on the Qwen3-8B step (7,671 vs 7,833 tok/s): off by default
+        self.l2_prefetch = os.environ.get("ADALLM_B200_L2_PREFETCH", "0") == "1"
         self.device = torch.device(device)
         self.B = max_batch
         self.max_pages_per_seq = -(-max_ctx // cfg.page_size)

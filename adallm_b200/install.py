@@ -9,9 +9,9 @@ Replaces, by the same names and signatures:
   adallm.ops.attention.store_kvcache                                            (attention.py:236)
   adallm.ops.attention.Attention.forward -- decode branch, and the prefix-cache prefill branch
       (attention.py:335-358: gather + flash-attn varlen -> one kernel over the e4m3 pages); a
-      prefill without a block table runs the same kernel over the pages store_kvcache just wrote
-      (install(fresh_prefill="kernel"), the default where flash-attn 2 does not run, e.g. B200)
-      or keeps the reference's flash-attn (fresh_prefill="reference")
+      prefill without a block table keeps the reference's flash-attn (fresh_prefill="reference",
+      the default when flash-attn is importable) or runs the same kernel over the pages
+      store_kvcache just wrote (fresh_prefill="kernel")
   adallm.ops.layernorm.RMSNorm.forward / GemmaRMSNorm.forward                    (layernorm.py:42-50, :94-102)
   adallm.ops.rotary_embedding.RotaryEmbedding.forward                            (rotary_embedding.py:45-56)
   adallm.ops.activation.SiluAndMul.forward / GeluAndMul.forward                   (activation.py:11-26)
@@ -36,13 +36,14 @@ _INSTALLED = False
 
 
 def _fresh_prefill_default() -> str:
-    """"kernel" where flash-attn 2 (the reference's prefill without a prefix cache) does not
-    support the GPU -- its published support ends at sm_90, and B200 is sm_100 -- else "reference"."""
+    """"reference" (keep the reference's flash-attn over the fresh bf16 K/V) when flash-attn is
+    importable -- flash-attn 2.8.3 runs on the B200 (recorded by tests/test_gpu_dropin.py) --
+    else "kernel"."""
     try:
-        major, _ = torch.cuda.get_device_capability()
+        import flash_attn  # noqa: F401
     except Exception:
         return "kernel"
-    return "kernel" if major >= 10 else "reference"
+    return "reference"
 
 
 def block_tables_from_slots(slot_mapping: torch.Tensor, cu_seqlens_q: torch.Tensor, max_seqlen_q: int,
@@ -68,8 +69,7 @@ def install(terms: int | None = None, fresh_prefill: str | None = None) -> None:
       flash-attn varlen over the fresh bf16 K/V, attention.py:346-358): "reference" keeps that,
       "kernel" stores K/V first (as the reference does) and runs this package's prefill kernel
       over the e4m3 pages just written, with the block table read off the slot mapping.  Default:
-      "kernel" on GPUs flash-attn 2 does not support (compute capability >= 10, e.g. B200),
-      else "reference"."""
+      "reference" when flash-attn is importable, else "kernel"."""
     global _INSTALLED
     import adallm.infra.context as ref_ctx
     import adallm.ops.activation as ref_act

@@ -49,6 +49,7 @@ class Agreement:
     logits_rel_l2_mean: float
     ref_logits_rel_l2_mean: float
     tokens: int
+    ref_logits_rel_l2_max: float = float("nan")
 
     def margin(self, z: float = 2.5) -> float:
         """z standard errors of the difference of two agreement rates measured on `tokens` tokens."""
@@ -151,4 +152,5 @@ def agreement_loop(eng, exact, emul, steps, batch, prompt, graph, seed) -> Agree
     eng.check_errors()
     return Agreement(raw=agree / max(total, 1), raw_reference=agree_ref / max(total, 1) if emulate else float("nan"),
                      logits_rel_l2_max=max(errs), logits_rel_l2_mean=float(np.mean(errs)),
-                     ref_logits_rel_l2_mean=float(np.mean(ref_errs)) if emulate else float("nan"), tokens=total)
+                     ref_logits_rel_l2_mean=float(np.mean(ref_errs)) if emulate else float("nan"), tokens=total,
+                     ref_logits_rel_l2_max=max(ref_errs) if emulate else float("nan"))

@@ -49,7 +49,7 @@ def reference_available() -> tuple[bool, str]:
     return True, REF_DIR
 
 
-def _setup():
+def _setup(fresh_prefill: str | None = None):
     os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
     os.environ.setdefault("ADALLM_DISABLE_PROGRESS", "1")
     os.environ.setdefault("ADALLM_QUIET", "1")
@@ -57,7 +57,7 @@ def _setup():
         if p not in sys.path:
             sys.path.insert(0, p)
     import adallm_b200
-    adallm_b200.install()
+    adallm_b200.install(fresh_prefill=fresh_prefill)
 
 
 def _hf_config_dict(layers: int, vocab: int) -> dict:
@@ -135,8 +135,10 @@ def random_weights(layers: int, vocab: int, seed: int):
     return ckpt, oracle_w
 
 
-def check(layers: int, decode_steps: int, seed: int) -> dict:
-    _setup()
+def check(layers: int, decode_steps: int, seed: int, fresh_prefill: str = "kernel") -> dict:
+    """fresh_prefill "kernel" (default here): the fresh prefill also runs this package's paged
+    prefill kernel, so every attention of the check is ours; "reference" keeps flash-attn."""
+    _setup(fresh_prefill)
     import numpy as np
     import torch
     from safetensors.torch import save_file
@@ -246,7 +248,8 @@ def check(layers: int, decode_steps: int, seed: int) -> dict:
         total += len(allseqs)
         nxt = ref_tok.tolist()
     nvfp4_gemm.check_device_errors()
-    out = {"layers": layers, "decode_steps": decode_steps, "page": PAGE, "setup_s": round(setup_s, 1),
+    out = {"layers": layers, "decode_steps": decode_steps, "page": PAGE, "fresh_prefill": fresh_prefill,
+           "setup_s": round(setup_s, 1),
            "prepacked_weights": prepacked, "graphs": sorted(runner.graphs.keys()),
            "raw": agree / total, "raw_reference": agree_ref / total, "tokens": total,
            "rel_l2_max": max(errs), "rel_l2_mean": float(np.mean(errs)),
@@ -365,13 +368,14 @@ def main():
     ap.add_argument("--ctx", type=int, default=512)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--seed", type=int, default=5)
+    ap.add_argument("--fresh-prefill", default="kernel", choices=["kernel", "reference"])
     a = ap.parse_args()
     ok, why = reference_available()
     if not ok:
         print(json.dumps({"unavailable": why}))
         return
     if a.mode == "check":
-        r = check(a.layers, a.steps, a.seed)
+        r = check(a.layers, a.steps, a.seed, a.fresh_prefill)
     elif a.mode == "bench":
         r = bench(a.layers, a.batch, a.ctx, a.reps)
     else:

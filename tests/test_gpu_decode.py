@@ -27,7 +27,8 @@ def _report(name, r):
     line = {"test": name, "raw": round(r.raw, 4), "raw_reference": round(r.raw_reference, 4),
             "margin": round(r.margin(), 4), "logits_rel_l2_mean": round(r.logits_rel_l2_mean, 5),
             "logits_rel_l2_max": round(r.logits_rel_l2_max, 5),
-            "ref_logits_rel_l2_mean": round(r.ref_logits_rel_l2_mean, 5), "tokens": r.tokens}
+            "ref_logits_rel_l2_mean": round(r.ref_logits_rel_l2_mean, 5),
+            "ref_logits_rel_l2_max": round(r.ref_logits_rel_l2_max, 5), "tokens": r.tokens}
     print(json.dumps(line))
     path = os.environ.get("ADA_AGREEMENT_LOG")
     if path:

@@ -3,7 +3,10 @@ top-8 of intermediate 768, vocab 151936) on the B200 against the CPU oracle deco
 forced: 3 layers, batch 16, a 16-token prompt and 128 generated tokens, with the same criteria
 as the dense agreement test (tests/test_gpu_decode.py): raw agreement with the exact oracle at
 least what the reference's own kernel arithmetic reaches on the same inputs (less 2.5 standard
-errors) or 99%, logits within 1.25x of the emulation's deviation and under 5e-2."""
+errors) or 99%, logits within 1.25x of the emulation's deviation (mean and worst step).  No
+absolute bound: near-tied router logits pick different experts under last-bit differences, so
+the reference's own arithmetic already sits ~7% (relative L2 of the logits) from the exact
+oracle on this random-init model."""
 import pytest
 
 from tests.decode_check import moe_test_config, run_agreement_moe
@@ -17,4 +20,4 @@ def test_moe_decode_agreement_128_steps():
     _report("moe_full_width_bs16", r)
     assert r.raw >= min(0.99, r.raw_reference - r.margin()), r
     assert r.logits_rel_l2_mean <= 1.25 * max(r.ref_logits_rel_l2_mean, 1e-3), r
-    assert r.logits_rel_l2_max < 5e-2, r
+    assert r.logits_rel_l2_max <= 1.25 * max(r.ref_logits_rel_l2_max, 1e-3), r
