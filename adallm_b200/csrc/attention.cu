@@ -248,16 +248,38 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   pdl_trigger();
 
   uint32_t uses = 0;  // tiles this warp has put through its ring (slot = uses % RING, parity = (uses / RING) & 1)
-  const int items = batch * num_kv_heads * P.max_splits;
+  // Work items are the splits that hold tokens -- (sequence b, split s < nsplit(b), KV head) in
+  // sequence-major order, KV head fastest so neighbouring warps (and CTAs) read the rows of the
+  // same pages together -- dealt round-robin to the grid's warps, so every warp gets the same
+  // number of live items whatever the spread of context lengths.
+  int live = 0;
+  for (int bb = lane; bb < batch; bb += 32) {
+    int st_, st16_, ns_;
+    seq_range(P, clamp_ctx(P, __ldg(P.ctx + bb)), st_, st16_, ns_);
+    live += ns_;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) live += __shfl_xor_sync(0xffffffffu, live, o);
+  const int items = live * num_kv_heads;
+  int cur_b = 0, cur_first = 0, cur_n = 0;  // sequence cur_b owns flat splits [cur_first, cur_first + cur_n)
+  {
+    int st_, st16_;
+    if (batch > 0) seq_range(P, clamp_ctx(P, __ldg(P.ctx)), st_, st16_, cur_n);
+  }
   for (int item = blockIdx.x * SPLIT_WARPS + warp; item < items; item += gridDim.x * SPLIT_WARPS) {
-    // KV head fastest: neighbouring warps (and CTAs) read the rows of the same pages together
     const int kvh = item % num_kv_heads;
-    const int s = (item / num_kv_heads) % P.max_splits;
-    const int b = item / (P.max_splits * num_kv_heads);
+    const int flat = item / num_kv_heads;
+    while (flat >= cur_first + cur_n && cur_b + 1 < batch) {  // items only move forward: a running cursor
+      cur_first += cur_n;
+      ++cur_b;
+      int st_, st16_;
+      seq_range(P, clamp_ctx(P, __ldg(P.ctx + cur_b)), st_, st16_, cur_n);
+    }
+    const int b = cur_b, s = flat - cur_first;
     const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
     int start, start16, nsplit;
     seq_range(P, ctx, start, start16, nsplit);
-    if (s >= nsplit) continue;  // warp-uniform
+    if (s < 0 || s >= nsplit) continue;  // warp-uniform; cannot happen with a consistent cursor
     const int t0 = start16 + s * CHUNK;
     const int t1 = min(ctx, t0 + CHUNK);
     const int ntiles = (t1 - t0 + 15) >> 4;
