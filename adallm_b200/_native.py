@@ -83,6 +83,7 @@ _SIGS = {
     "ada_moe_route_topk": (INT, [P, INT, I64, I64, I32, I32, I32, P, P, P]),
     "ada_moe_combine": (INT, [P, INT, I64, P, I64, I32, I32, P, I64, P]),
     "ada_moe_combine_ep": (INT, [P, INT, I64, P, P, I32, I32, I64, I32, I32, P, I64, P]),
+    "ada_moe_combine_ep_f32": (INT, [P, INT, I64, P, P, I32, I32, I64, I32, I32, P, I64, P]),
     "ada_nvfp4_linear_grouped_ep": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I32, I32, I64, P, P, INT, I64, INT,
                                           P, SZ, P]),
     "ada_nvfp4_linear_grouped_workspace_size": (SZ, [I64, I64, I64, INT, I32]),

@@ -7,6 +7,7 @@
 //   combine: out[t] = sum_j w[t, j] * y[t * k + j] over the token's k expert rows, fp32 in
 //            expert-slot order, rounded once to the activation dtype.
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -85,9 +86,11 @@ __global__ void __launch_bounds__(128) route_kernel(const T* __restrict__ logits
 // One CTA per token, 8 hidden elements per thread and step.
 // With ids (expert parallelism): slots whose expert is outside [expert_base, expert_base +
 // num_local) belong to another rank and are skipped (their expert rows were not computed here).
-template <typename T>
+// OutT float keeps the rank's fp32 sum unrounded, so that an fp32 sum over the ranks rounds once,
+// as the single-GPU combine does.
+template <typename T, typename OutT>
 __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, int64_t ldy, const T* __restrict__ w,
-                                                      int topk, int hidden, T* __restrict__ out, int64_t ldo,
+                                                      int topk, int hidden, OutT* __restrict__ out, int64_t ldo,
                                                       const int32_t* __restrict__ ids, int expert_base, int num_local) {
   pdl_wait();
   pdl_trigger();
@@ -105,7 +108,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, i
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = fmaf(wj, v[i], acc[i]);
     }
-    *reinterpret_cast<uint4*>(out + (int64_t)t * ldo + c) = pack8<T>(acc);
+    if constexpr (std::is_same<OutT, float>::value) {
+      float4* o = reinterpret_cast<float4*>(out + (int64_t)t * ldo + c);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      *reinterpret_cast<uint4*>(out + (int64_t)t * ldo + c) = pack8<T>(acc);
+    }
   }
 }
 
@@ -137,19 +146,29 @@ extern "C" int ada_moe_route_topk(const void* logits, int dtype, int64_t ld, int
 
 static int combine_impl(const void* y, int dtype, int64_t ldy, const void* weights, const int32_t* ids,
                         int32_t expert_base, int32_t num_local, int64_t tokens, int32_t topk, int32_t hidden,
-                        void* out, int64_t ldo, void* stream) {
+                        void* out, int64_t ldo, void* stream, bool out_f32 = false) {
   if (tokens < 0 || topk <= 0 || hidden <= 0 || ldy < hidden || ldo < hidden) return ADA_ERR_INVALID_ARG;
   if (tokens == 0) return ADA_OK;
   if (!y || !weights || !out) return ADA_ERR_INVALID_ARG;
   if (hidden % 8 || tokens > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
   if (((uintptr_t)y & 15) || ((uintptr_t)out & 15) || (ldy & 7) || (ldo & 7)) return ADA_ERR_ALIGNMENT;
+  if (out_f32 && (ldo & 3)) return ADA_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == ADA_DT_BF16)
-    (void)launch_k(moe::combine_kernel<__nv_bfloat16>, dim3((unsigned)tokens), dim3(256), 0, st,
+  const dim3 grid((unsigned)tokens);
+  if (dtype == ADA_DT_BF16 && out_f32)
+    (void)launch_k(moe::combine_kernel<__nv_bfloat16, float>, grid, dim3(256), 0, st, (const __nv_bfloat16*)y, ldy,
+                   (const __nv_bfloat16*)weights, (int)topk, (int)hidden, (float*)out, ldo, ids, (int)expert_base,
+                   (int)num_local);
+  else if (dtype == ADA_DT_BF16)
+    (void)launch_k(moe::combine_kernel<__nv_bfloat16, __nv_bfloat16>, grid, dim3(256), 0, st,
                    (const __nv_bfloat16*)y, ldy, (const __nv_bfloat16*)weights, (int)topk, (int)hidden,
                    (__nv_bfloat16*)out, ldo, ids, (int)expert_base, (int)num_local);
+  else if (dtype == ADA_DT_F16 && out_f32)
+    (void)launch_k(moe::combine_kernel<__half, float>, grid, dim3(256), 0, st, (const __half*)y, ldy,
+                   (const __half*)weights, (int)topk, (int)hidden, (float*)out, ldo, ids, (int)expert_base,
+                   (int)num_local);
   else if (dtype == ADA_DT_F16)
-    (void)launch_k(moe::combine_kernel<__half>, dim3((unsigned)tokens), dim3(256), 0, st, (const __half*)y, ldy,
+    (void)launch_k(moe::combine_kernel<__half, __half>, grid, dim3(256), 0, st, (const __half*)y, ldy,
                    (const __half*)weights, (int)topk, (int)hidden, (__half*)out, ldo, ids, (int)expert_base,
                    (int)num_local);
   else
@@ -169,4 +188,13 @@ extern "C" int ada_moe_combine_ep(const void* y, int dtype, int64_t ldy, const v
   if (!expert_ids || expert_base < 0 || num_local <= 0) return ADA_ERR_INVALID_ARG;
   return combine_impl(y, dtype, ldy, weights, expert_ids, expert_base, num_local, tokens, topk, hidden, out, ldo,
                       stream);
+}
+
+extern "C" int ada_moe_combine_ep_f32(const void* y, int dtype, int64_t ldy, const void* weights,
+                                      const int32_t* expert_ids, int32_t expert_base, int32_t num_local,
+                                      int64_t tokens, int32_t topk, int32_t hidden, float* out, int64_t ldo,
+                                      void* stream) {
+  if (!expert_ids || expert_base < 0 || num_local <= 0) return ADA_ERR_INVALID_ARG;
+  return combine_impl(y, dtype, ldy, weights, expert_ids, expert_base, num_local, tokens, topk, hidden, out, ldo,
+                      stream, true);
 }

@@ -32,17 +32,20 @@ def route_topk(router_logits: torch.Tensor, top_k: int, norm_topk_prob: bool = T
 
 
 def combine(expert_out: torch.Tensor, weights: torch.Tensor, top_k: int, expert_ids: torch.Tensor | None = None,
-            expert_base: int = 0, num_local: int | None = None) -> torch.Tensor:
+            expert_base: int = 0, num_local: int | None = None, fp32: bool = False) -> torch.Tensor:
     """[T * top_k, H] expert rows (row t*top_k + j = token t's j-th expert) -> [T, H].
 
     With expert_ids (expert parallelism) only the slots whose expert is in
-    [expert_base, expert_base + num_local) are summed: this rank's share of the block output."""
+    [expert_base, expert_base + num_local) are summed: this rank's share of the block output,
+    returned unrounded in fp32 when fp32 is set (sum the ranks' shares in fp32, then round once)."""
     N.require_cuda(expert_out, weights, what="moe combine")
     y = expert_out if expert_out.stride(-1) == 1 else expert_out.contiguous()
     rows, h = y.shape
     t = rows // top_k
     w = weights.to(y.dtype).reshape(-1).contiguous()
-    out = torch.empty((t, h), dtype=y.dtype, device=y.device)
+    if fp32 and expert_ids is None:
+        raise ValueError("fp32 output is the expert-parallel share; pass expert_ids")
+    out = torch.empty((t, h), dtype=torch.float32 if fp32 else y.dtype, device=y.device)
     if expert_ids is None:
         st = N.lib().ada_moe_combine(y.data_ptr(), N.DT[y.dtype], y.stride(0), w.data_ptr(), t, top_k, h,
                                      out.data_ptr(), out.stride(0), N.stream_ptr(y.device))
@@ -50,9 +53,9 @@ def combine(expert_out: torch.Tensor, weights: torch.Tensor, top_k: int, expert_
         ids = expert_ids.to(device=y.device, dtype=torch.int32).reshape(-1).contiguous()
         if ids.numel() != t * top_k or num_local is None:
             raise ValueError("expert_ids must have top_k entries per token, and num_local must be given")
-        st = N.lib().ada_moe_combine_ep(y.data_ptr(), N.DT[y.dtype], y.stride(0), w.data_ptr(), ids.data_ptr(),
-                                        int(expert_base), int(num_local), t, top_k, h, out.data_ptr(), out.stride(0),
-                                        N.stream_ptr(y.device))
+        fn = N.lib().ada_moe_combine_ep_f32 if fp32 else N.lib().ada_moe_combine_ep
+        st = fn(y.data_ptr(), N.DT[y.dtype], y.stride(0), w.data_ptr(), ids.data_ptr(), int(expert_base),
+                int(num_local), t, top_k, h, out.data_ptr(), out.stride(0), N.stream_ptr(y.device))
     N.check(st, "moe combine")
     return out
 
@@ -70,7 +73,8 @@ def moe_block_ep(x: torch.Tensor, router_logits: torch.Tensor, top_k: int, norm_
                  gate_up: tuple, down: tuple, expert_base: int, group=None) -> torch.Tensor:
     """One MoE block with this rank's experts: route (the same on every rank), the grouped gate+up
     GEMM over the rows routed here, SiLU(gate) * up, the grouped down GEMM, the weighted sum of the
-    local slots, then (with a process group) the sum over the ranks.
+    local slots, then (with a process group) the sum over the ranks: fp32 shares, one fp32
+    all-reduce, one rounding to x's dtype.
 
     x [T, H]; router_logits [T, E_total]; gate_up = (packed [E, 2I, H/2], scale [E, 2I, H/16],
     scale_2 [E]) with gate rows first; down = (packed [E, H, I/2], scale [E, H, I/16], scale_2 [E]);
@@ -84,8 +88,10 @@ def moe_block_ep(x: torch.Tensor, router_logits: torch.Tensor, top_k: int, norm_
     # rows routed to other ranks hold stale values; the down GEMM and the combine never read them
     a = gated_act(h, 0)
     y = nvfp4_linear_gather(a, down[0], down[1], down[2], flat, 16, expert_base=expert_base)
-    out = combine(y, w, top_k, expert_ids=ids, expert_base=expert_base, num_local=gate_up[0].shape[0])
+    share = combine(y, w, top_k, expert_ids=ids, expert_base=expert_base, num_local=gate_up[0].shape[0],
+                    fp32=group is not None)
     if group is not None:
         import torch.distributed as dist
-        dist.all_reduce(out, group=group)
-    return out
+        dist.all_reduce(share, group=group)
+        share = share.to(x.dtype)
+    return share

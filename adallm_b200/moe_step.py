@@ -92,8 +92,9 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
     (expert parallelism, beyond the reference; one process per GPU, `group` the NCCL group of the
     ep_size ranks) every rank runs the same attention and routing, holds a contiguous block of
     experts, runs the grouped GEMMs over the rows routed to its experts only
-    (ada_nvfp4_linear_grouped_ep), sums its slots (ada_moe_combine_ep) and all-reduces the block
-    output: one NCCL all-reduce of [batch, hidden] bf16 per layer."""
+    (ada_nvfp4_linear_grouped_ep), sums its slots in fp32 (ada_moe_combine_ep_f32) and all-reduces
+    them: one NCCL all-reduce of [batch, hidden] fp32 per layer, rounded once to bf16 afterwards, so
+    the block output is the single-GPU combine's up to the order of the fp32 additions."""
 
     def __init__(self, cfg: MoEConfig, device, max_batch: int, max_ctx: int, seed: int = 0, group=None):
         if cfg.tp_size != 1:
@@ -166,6 +167,7 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
         self.h_rows = torch.zeros((rows, 2 * c.moe_intermediate), dtype=bf, device=d)
         self.a_rows = torch.zeros((rows, c.moe_intermediate), dtype=bf, device=d)
         self.y_rows = torch.zeros((rows, c.hidden), dtype=bf, device=d)
+        self.moe_sum = torch.zeros((B, c.hidden), dtype=torch.float32, device=d) if c.ep_size > 1 else None
         lib = N.lib()
         gu, dn = self.layers[0]["experts_gate_up"], self.layers[0]["experts_down"]
         self.ws_gate_up = torch.zeros(int(lib.ada_nvfp4_linear_grouped_workspace_size(rows, gu.n, gu.k, c.terms, gu.e)),
@@ -212,12 +214,13 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
             N.check(lib.ada_moe_combine(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(), B,
                                         c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
                     "moe combine")
-        else:  # this rank's slots, then the sum over the ranks
-            N.check(lib.ada_moe_combine_ep(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(),
-                                           self.route_ids.data_ptr(), self.expert_base, self.local_experts, B,
-                                           c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
-                    "moe combine (expert-parallel)")
-            dist.all_reduce(self.hidden, group=self.group)
+        else:  # this rank's slots in fp32, the fp32 sum over the ranks, one rounding
+            N.check(lib.ada_moe_combine_ep_f32(self.y_rows.data_ptr(), 0, self.y_rows.stride(0),
+                                               self.route_w.data_ptr(), self.route_ids.data_ptr(), self.expert_base,
+                                               self.local_experts, B, c.top_k, c.hidden, self.moe_sum.data_ptr(),
+                                               self.moe_sum.stride(0), stream), "moe combine (expert-parallel)")
+            dist.all_reduce(self.moe_sum, group=self.group)
+            self.hidden.copy_(self.moe_sum)
 
     def forward(self):
         c = self.cfg

@@ -325,6 +325,13 @@ ADA_API int ada_nvfp4_linear_grouped_ep(const void* x, int x_dtype, int64_t ldx,
 ADA_API int ada_moe_combine_ep(const void* y, int dtype, int64_t ldy, const void* weights,
                                const int32_t* expert_ids, int32_t expert_base, int32_t num_local, int64_t tokens,
                                int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream);
+/* ada_moe_combine_ep with the rank's fp32 sums left unrounded (out fp32, ldo % 4 == 0): an fp32
+ * all-reduce of them, rounded once to the model dtype, is the single-GPU combine up to the order
+ * of the fp32 additions. */
+ADA_API int ada_moe_combine_ep_f32(const void* y, int dtype, int64_t ldy, const void* weights,
+                                   const int32_t* expert_ids, int32_t expert_base, int32_t num_local,
+                                   int64_t tokens, int32_t topk, int32_t hidden, float* out, int64_t ldo,
+                                   void* stream);
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by

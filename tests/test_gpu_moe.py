@@ -62,6 +62,28 @@ def test_combine_weighted_sum():
     assert rel_l2(out.float(), ref) < 4e-3
 
 
+def test_combine_expert_parallel_fp32_shares():
+    """Two ranks' fp32 shares (ada_moe_combine_ep_f32), summed in fp32 and rounded once, give the
+    single-GPU combine up to the order of the fp32 additions: within one bf16 ulp everywhere, and
+    the same bf16 value almost everywhere; the bf16 share entry agrees with the fp32 one rounded."""
+    d = dev()
+    t, k, h, e = 16, 8, 2048, 128
+    g = torch.Generator().manual_seed(21)
+    y = torch.randn((t * k, h), generator=g).to(torch.bfloat16).to(d)
+    w = torch.rand((t, k), generator=g).to(torch.bfloat16).to(d)
+    ids = torch.stack([torch.randperm(e, generator=g)[:k] for _ in range(t)]).to(torch.int32).to(d)
+    full = combine(y, w, k)
+    s0 = combine(y, w, k, expert_ids=ids, expert_base=0, num_local=e // 2, fp32=True)
+    s1 = combine(y, w, k, expert_ids=ids, expert_base=e // 2, num_local=e // 2, fp32=True)
+    b0 = combine(y, w, k, expert_ids=ids, expert_base=0, num_local=e // 2)
+    torch.cuda.synchronize()
+    assert s0.dtype == torch.float32 and torch.equal(b0, s0.to(torch.bfloat16))
+    summed = (s0 + s1).to(torch.bfloat16).float()
+    ulp = full.float().abs().clamp(min=2.0 ** -100).log2().floor().exp2() * 2.0 ** -7
+    assert bool(((summed - full.float()).abs() <= ulp).all())
+    assert float((summed == full.float()).float().mean()) > 0.99
+
+
 def test_moe_projection_end_to_end():
     d = dev()
     t, e, k, hid, n = 16, 32, 4, 512, 256

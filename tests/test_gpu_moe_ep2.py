@@ -2,10 +2,10 @@
 
 Two processes, one per GPU: each holds half of the 128 experts of every layer (ep_size 2), runs
 the same attention and routing, the grouped GEMMs over the rows routed to its own experts, sums
-its slots and all-reduces the block output (NCCL).  With the same tokens fed to every step, both
-ranks hold identical logits, which match the single-GPU engine holding every expert within 2e-2
-relative L2 (the slot sum is split over the ranks, so it rounds differently), and no bounded wait
-ran out."""
+its slots in fp32 and all-reduces them in fp32 (NCCL) before the one rounding to bf16.  With the
+same tokens fed to every step, both ranks hold identical logits, which match the single-GPU engine
+holding every expert within 1e-2 relative L2 (only the order of the fp32 additions differs; a bf16
+all-reduce of per-rank rounded sums measured 2.2e-2 here), and no bounded wait ran out."""
 import os
 import socket
 
@@ -89,4 +89,4 @@ def test_moe_ep2_engine_matches_single_gpu():
     assert (res[0]["logits"] == res[1]["logits"]).all()
     got, ref = torch.from_numpy(res[0]["logits"]), torch.from_numpy(res[0]["ref"])
     rel = float((got - ref).norm() / ref.norm())
-    assert rel < 2e-2, rel
+    assert rel < 1e-2, rel
