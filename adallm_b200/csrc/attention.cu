@@ -5,18 +5,19 @@
 // attend to tokens [start, ctx) of the paged e4m3 cache, with q rounded to
 // fp16, K/V widened to fp16, fp32 scores and softmax statistics, fp16
 // probabilities for P.V and fp32 accumulation.  Differences by design:
-//   * split-K over the context (flash-decoding): each CTA owns one CHUNK of
-//     tokens of one (sequence, kv head) and writes an unnormalised partial
-//     (max, sum, O) to the workspace; a reduction kernel merges the splits;
+//   * split-K over the context (flash-decoding): each warp takes splits of 64-512 tokens of
+//     one (sequence, kv head) -- the length chosen per launch so the work fits one wave of
+//     the grid -- and writes an unnormalised partial (max, sum, O) to the workspace; a
+//     reduction kernel merges the splits;
 //   * the page walk is exact for any page size that is a multiple of 16
 //     (the reference reads past a page for pages < 64);
 //   * optional per-tensor k_scale / v_scale (1.0 reproduces the reference).
 //
-// Tile = 16 tokens of one page.  At start one thread issues a TMA load (4-D tensor map
-// over [pages][page][Hkv][D] bytes, 128-byte swizzle, one mbarrier per tile) of the K and
-// V rows of every tile of the CTA's 256-token chunk: the whole 64 KB chunk is in flight
-// at once, gathered page by page through the block table.  Warps take tiles round-robin
-// as they land.  One warp computes S^T = K_tile . Q^T with mma.m16n8k16 (tokens on M,
+// Tile = 16 tokens of one page.  Each warp streams its split's tiles through its own ring of
+// RING slots: lane 0 issues a TMA load (4-D tensor map over [pages][page][Hkv][D] bytes,
+// 128-byte swizzle, one mbarrier per slot) of a tile's K and V rows, gathered page by page
+// through the block table, and refills a slot as soon as the tile in it has been consumed.
+// The warp computes S^T = K_tile . Q^T with mma.m16n8k16 (tokens on M,
 // heads on N), an online softmax per head, and O^T += V_tile^T . P^T.  For the K operand
 // the head dimension is permuted so that thread (g, c) needs bytes [32c, 32c+32) of tokens
 // g and g+8 (the permutation is applied to Q identically); for the V operand the output
@@ -30,8 +31,11 @@ namespace ada {
 namespace attn {
 
 constexpr int D = 128;
-constexpr int CHUNK = 256;  // tokens per split (CTA)
 constexpr int TILE = 16;
+// Split length of the long-cache kernel, in tiles of 16 tokens: chosen per launch on the device
+// (split_tiles_for) between CT_MIN and CT_MAX (one lane per tile holds the split's page ids).
+constexpr int CT_MIN = 4;
+constexpr int CT_MAX = 32;
 constexpr int TILE_BYTES = TILE * D;  // one K (or V) tile: 16 rows x 128 bytes
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -55,6 +59,7 @@ struct Params {
   // short-cache kernel may read them (and start the TMA loads of those tiles) before its
   // programmatic-launch wait; q and the newest row are read after it.
   int early;
+  int* split_tiles;  // workspace word: the split length the split kernel chose, for the merges
 };
 
 // Tokens beyond the block table's reach (ctx > max_pages * page) cannot be addressed and are
@@ -63,10 +68,67 @@ __device__ __forceinline__ int clamp_ctx(const Params& P, int ctx) {
   return min(ctx, P.max_pages * P.page);
 }
 
-__device__ __forceinline__ void seq_range(const Params& P, int ctx, int& start, int& start16, int& nsplit) {
+// Tokens [start, ctx) of a sequence are attended (start > 0 with a sliding window); its splits of
+// ct tiles begin at the tile-aligned start16.
+__device__ __forceinline__ void seq_range(const Params& P, int ctx, int ct, int& start, int& start16, int& nsplit) {
   start = P.window > 0 ? max(ctx - P.window, 0) : 0;
   start16 = start & ~15;
-  nsplit = ctx > 0 ? min((ctx - start16 + CHUNK - 1) / CHUNK, P.max_splits) : 0;
+  const int chunk = ct * TILE;
+  nsplit = ctx > 0 ? min((ctx - start16 + chunk - 1) / chunk, P.max_splits) : 0;
+}
+
+// Warp-wide: work items (sequence, split of ct tiles, KV head) of the launch.
+__device__ __forceinline__ int split_items(const Params& P, int batch, int num_kv_heads, int ct) {
+  int n = 0;
+  for (int b = (int)(threadIdx.x & 31); b < batch; b += 32) {
+    int st, st16, ns;
+    seq_range(P, clamp_ctx(P, __ldg(P.ctx + b)), ct, st, st16, ns);
+    n += ns;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  return n * num_kv_heads;
+}
+// Warp-wide: the split length of this launch -- the shortest split (most parallel work) whose
+// items all fit in one wave of the grid's `warps`, found by bisection (items only fall as splits
+// grow); CT_MAX when even that needs several waves.  A first wave of whole splits saturates HBM
+// (a KV page's heads are read by neighbouring warps together), while the warps of a second,
+// partial wave run alone, each latency-bound on its own ring.  Integer arithmetic on the
+// context lengths only, so every warp gets the same answer.
+__device__ __forceinline__ int split_tiles_for(const Params& P, int batch, int num_kv_heads, int warps) {
+  const int lane = threadIdx.x & 31;
+  if (batch <= 32) {  // one lane per candidate length; the sequences' tile counts read once
+    int tiles = 0;
+    if (lane < batch) {
+      int st, st16, ns;
+      const int ctx = clamp_ctx(P, __ldg(P.ctx + lane));
+      seq_range(P, ctx, CT_MAX, st, st16, ns);
+      tiles = ctx > 0 ? (ctx - st16 + TILE - 1) / TILE : 0;
+    }
+    // items(ct) >= total tiles x heads / ct: start at that bound and lengthen until one wave holds
+    int total = tiles;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    const int64_t need = (int64_t)total * num_kv_heads;
+    int ct = (int)max((int64_t)CT_MIN, (need + warps - 1) / warps);
+    for (; ct < CT_MAX; ++ct) {
+      int n = min((tiles + ct - 1) / ct, P.max_splits);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+      if ((int64_t)n * num_kv_heads <= warps) break;
+    }
+    return min(ct, CT_MAX);
+  }
+  if (split_items(P, batch, num_kv_heads, CT_MAX) > warps) return CT_MAX;
+  int lo = CT_MIN, hi = CT_MAX;  // items(hi) <= warps
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (split_items(P, batch, num_kv_heads, mid) <= warps)
+      hi = mid;
+    else
+      lo = mid + 1;
+  }
+  return lo;
 }
 
 // 16 bytes at (row, 16-byte chunk) of a 128-byte-swizzled tile (chunk index XOR row % 8).
@@ -214,8 +276,8 @@ __device__ __forceinline__ void attn_tile(const Params& P, const uint8_t* kt, bo
   }
 }
 
-// One warp = one work item (sequence b, KV head, 256-token split) at a time: items are dealt
-// to the grid's warps round-robin.  Each warp streams its item's tiles through its own ring of
+// One warp = one work item (sequence b, KV head, split) at a time: items are dealt to the
+// grid's warps round-robin.  Each warp streams its item's tiles through its own ring of
 // RING tile slots (K and V, 4 KB per tile): lane i looks up tile i's page, lane 0 issues the
 // TMA loads RING tiles ahead of the tile being computed, and the warp writes the item's
 // unnormalised partial (per head: O, max, sum) straight from its registers.
@@ -244,9 +306,14 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   if (lane < RING) mbar_init(&bar[lane], 1);
   fence_mbar_init();
   __syncthreads();
+  // the split length depends on the context lengths only: with settled metadata (P.early) it is
+  // worked out while the previous kernel finishes
+  int ct = P.early ? split_tiles_for(P, batch, num_kv_heads, (int)gridDim.x * SPLIT_WARPS) : 0;
   pdl_wait();
   pdl_trigger();
-
+  if (!P.early) ct = split_tiles_for(P, batch, num_kv_heads, (int)gridDim.x * SPLIT_WARPS);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *P.split_tiles = ct;  // after the wait: the last merge read it
+  const int chunk = ct * TILE;
   uint32_t uses = 0;  // tiles this warp has put through its ring (slot = uses % RING, parity = (uses / RING) & 1)
   // Work items are the splits that hold tokens -- (sequence b, split s < nsplit(b), KV head) in
   // sequence-major order, KV head fastest so neighbouring warps (and CTAs) read the rows of the
@@ -255,7 +322,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   int live = 0;
   for (int bb = lane; bb < batch; bb += 32) {
     int st_, st16_, ns_;
-    seq_range(P, clamp_ctx(P, __ldg(P.ctx + bb)), st_, st16_, ns_);
+    seq_range(P, clamp_ctx(P, __ldg(P.ctx + bb)), ct, st_, st16_, ns_);
     live += ns_;
   }
 #pragma unroll
@@ -264,7 +331,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   int cur_b = 0, cur_first = 0, cur_n = 0;  // sequence cur_b owns flat splits [cur_first, cur_first + cur_n)
   {
     int st_, st16_;
-    if (batch > 0) seq_range(P, clamp_ctx(P, __ldg(P.ctx)), st_, st16_, cur_n);
+    if (batch > 0) seq_range(P, clamp_ctx(P, __ldg(P.ctx)), ct, st_, st16_, cur_n);
   }
   for (int item = blockIdx.x * SPLIT_WARPS + warp; item < items; item += gridDim.x * SPLIT_WARPS) {
     const int kvh = item % num_kv_heads;
@@ -273,15 +340,15 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
       cur_first += cur_n;
       ++cur_b;
       int st_, st16_;
-      seq_range(P, clamp_ctx(P, __ldg(P.ctx + cur_b)), st_, st16_, cur_n);
+      seq_range(P, clamp_ctx(P, __ldg(P.ctx + cur_b)), ct, st_, st16_, cur_n);
     }
     const int b = cur_b, s = flat - cur_first;
     const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
     int start, start16, nsplit;
-    seq_range(P, ctx, start, start16, nsplit);
+    seq_range(P, ctx, ct, start, start16, nsplit);
     if (s < 0 || s >= nsplit) continue;  // warp-uniform; cannot happen with a consistent cursor
-    const int t0 = start16 + s * CHUNK;
-    const int t1 = min(ctx, t0 + CHUNK);
+    const int t0 = start16 + s * chunk;
+    const int t1 = min(ctx, t0 + chunk);
     const int ntiles = (t1 - t0 + 15) >> 4;
     const int lo = max(start, t0);
 
@@ -425,7 +492,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
   }
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
-  seq_range(P, ctx, start, start16, nsplit);
+  seq_range(P, ctx, CT_MAX, start, start16, nsplit);  // the tile range only
   const int t0 = start16, t1 = ctx;
   const int ntiles = ctx > t0 ? (t1 - t0 + 15) >> 4 : 0;
   const int nk = ntiles > warp ? (ntiles - warp + SPLIT_WARPS - 1) / SPLIT_WARPS : 0;  // this warp's tiles
@@ -640,7 +707,7 @@ __global__ void __launch_bounds__(128) decode_reduce_kernel(Params P, TO* __rest
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
-  seq_range(P, ctx, start, start16, nsplit);
+  seq_range(P, ctx, *P.split_tiles, start, start16, nsplit);  // the split kernel's split length
   merge_weights(P, b, h, 1, nsplit, merge_smem, sl);
   float A[4];
   merge_partial<4>(P, b, h, 4 * lane, nsplit, merge_smem, warp, A);
@@ -676,7 +743,7 @@ __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* 
   }
   const int ctx = clamp_ctx(P, __ldg(P.ctx + b));
   int start, start16, nsplit;
-  seq_range(P, ctx, start, start16, nsplit);
+  seq_range(P, ctx, *P.split_tiles, start, start16, nsplit);
   extern __shared__ float merge_smem[];  // [heads of this slice][nsplit] weights, then [heads] sums
   const int h0 = (o0 * 8) / D, nh = ((o1 * 8 - 1) / D) - h0 + 1;
   float* sl = merge_smem + nh * nsplit;
@@ -728,8 +795,9 @@ inline bool split_smem_ready() {
 
 inline int max_splits_for(int32_t max_pages, int32_t page) {
   const int64_t toks = (int64_t)max_pages * page;
-  return (int)cdiv(toks + 15, CHUNK);  // +15: the tile-aligned window start can add one tile
+  return (int)cdiv(toks + 15, CT_MIN * TILE);  // +15: the tile-aligned window start can add one tile
 }
+constexpr size_t SPLIT_WORD_BYTES = 256;  // the chosen split length, after the partials
 
 }  // namespace attn
 }  // namespace ada
@@ -740,7 +808,7 @@ extern "C" size_t ada_fp8_paged_decode_workspace_size(int32_t batch, int32_t num
                                                       int32_t page_size, int32_t head_dim) {
   if (batch <= 0 || num_heads <= 0 || max_pages <= 0 || page_size <= 0 || head_dim <= 0) return 0;
   const int64_t S = attn::max_splits_for(max_pages, page_size);
-  return (size_t)batch * num_heads * S * (head_dim + 2) * sizeof(float);
+  return (size_t)batch * num_heads * S * (head_dim + 2) * sizeof(float) + attn::SPLIT_WORD_BYTES;
 }
 
 static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
@@ -853,6 +921,7 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
   P.v_scale = v_scale;
   P.o_part = reinterpret_cast<float*>(workspace);
   P.ml_part = P.o_part + (size_t)batch * num_heads * P.max_splits * attn::D;
+  P.split_tiles = reinterpret_cast<int*>(P.ml_part + (size_t)batch * num_heads * P.max_splits * 2);
   P.early = (flags & ADA_ATTN_META_EARLY) ? 1 : 0;
 
   // K / V caches as 4-D byte tensors [num_pages][page][Hkv][D] -> TMA box of 16 rows x 128 B

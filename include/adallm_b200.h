@@ -105,7 +105,8 @@ ADA_API int ada_fp8_paged_decode_quant(const void* q, int q_dtype, int64_t q_str
  * ADA_ATTN_META_EARLY: context_lens, block_tables and every cached K/V row except each sequence's
  * newest position (context_lens[b] - 1) were written at least two kernels earlier on `stream`
  * (e.g. the kernel just before is the one appending the new token's K/V): the short-cache kernel
- * then reads the metadata and starts its cache loads before waiting for that kernel. */
+ * then reads the metadata and starts its cache loads before waiting for that kernel, and the
+ * long-cache kernel works out its split length (from context_lens) before that wait. */
 #define ADA_ATTN_META_EARLY 1
 ADA_API int ada_fp8_paged_decode_quant_ex(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                                           const uint8_t* k_cache, const uint8_t* v_cache,

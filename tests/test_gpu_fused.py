@@ -116,10 +116,13 @@ def test_gated_act_quant_matches_unfused(inter, act, terms):
 
 
 @pytest.mark.parametrize("flags", [0, 1])
-@pytest.mark.parametrize("batch,hq,hkv,terms", [(16, 32, 8, 4), (7, 16, 2, 1), (16, 64, 8, 5)])
-def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms, flags):
+@pytest.mark.parametrize("batch,hq,hkv,terms,ctx_hi", [(16, 32, 8, 4, 900), (7, 16, 2, 1, 900), (16, 64, 8, 5, 900),
+                                                       (16, 32, 8, 4, 5000), (3, 16, 2, 4, 3000)])
+def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms, ctx_hi, flags):
+    """Short caches (one fused kernel) and long ones (split kernel, whose split length is worked
+    out before the launch wait under ADA_ATTN_META_EARLY, then merge + quantise)."""
     d = dev()
-    case = oa.make_paged_case(5, batch=batch, hq=hq, hkv=hkv, d=128, page=16, ctx_lo=1, ctx_hi=900)
+    case = oa.make_paged_case(5, batch=batch, hq=hq, hkv=hkv, d=128, page=16, ctx_lo=1, ctx_hi=ctx_hi)
     q = torch.from_numpy(case["q"]).to(torch.bfloat16).to(d)
     k = torch.from_numpy(case["k"]).to(d).view(torch.float8_e4m3fn)
     v = torch.from_numpy(case["v"]).to(d).view(torch.float8_e4m3fn)
