@@ -83,6 +83,10 @@ _SIGS = {
     "ada_moe_route_topk": (INT, [P, INT, I64, I64, I32, I32, I32, P, P, P]),
     "ada_moe_combine": (INT, [P, INT, I64, P, I64, I32, I32, P, I64, P]),
     "ada_moe_combine_ep": (INT, [P, INT, I64, P, P, I32, I32, I64, I32, I32, P, I64, P]),
+    "ada_moe_experts_workspace_size": (SZ, [I64, I32, I64, I64, INT, I32]),
+    "ada_moe_experts": (INT, [P, INT, I64, I64, I32, P, I32, I32, I32, P, I64, P, P, P, I64, P, P, I64, I64, INT, P,
+                              I64, INT, P, SZ, P]),
+    "ada_moe_router_topk": (INT, [P, INT, I64, I64, P, I64, I32, I32, I32, I32, P, P, P, P]),
     "ada_moe_combine_ep_f32": (INT, [P, INT, I64, P, P, I32, I32, I64, I32, I32, P, I64, P]),
     "ada_nvfp4_linear_grouped_ep": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I32, I32, I64, P, P, INT, I64, INT,
                                           P, SZ, P]),
@@ -156,7 +160,8 @@ _ERROR_BITS = [(0x1, "GEMM producer waited for a free pipeline stage"),
                (0x8, "GEMM MMA issuer waited for a free accumulator")]
 _ERROR_CODES = {0x50: "a peer's partial planes never arrived (tensor-parallel inbox wait)",
                 0x60: "an expert id outside [0, num_experts)",
-                0x70: "a prefill attention tile load never completed"}
+                0x70: "a prefill attention tile load never completed",
+                0x80: "a router logit never arrived (fused MoE router wait)"}
 
 
 def describe_error_word(code: int) -> str:

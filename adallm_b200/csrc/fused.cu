@@ -179,20 +179,26 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   return 0.5f * x * (1.f + tanhf(inner));
 }
 
-// grid (ctas, m_pad), cluster (ctas, 1, 1).
+// grid (ctas, m_pad), cluster (ctas, 1, 1).  Grouped operands (dest != null): grid (ctas, rows),
+// input row r goes to operand row dest[r] (< 0: not routed here, nothing written).
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restrict__ x, int64_t ldx, T* y, int64_t ldy,
                                                               int rows, int inter, int act, q::QuantDst dst,
-                                                              PartIn pin) {
+                                                              PartIn pin, const int* dest) {
   __shared__ float red[cl::MAX_WARPS];
   __shared__ cl::Exchange xch;
   cl::cluster_start(&xch, 1);
   pdl_wait();
   pdl_trigger();
-  const int m = blockIdx.y;
+  const int src = blockIdx.y;
+  const int m = dest ? dest[src] : src;
   int o0, o1;
   slice_of(inter, o0, o1);
-  if (m >= rows) {
+  if (m < 0) {  // cluster-uniform: every CTA of the cluster has this row
+    cl::cluster_wait();
+    return;
+  }
+  if (src >= rows) {
     zero_slice(dst, m, o0, o1);
     cl::cluster_wait();
     return;
@@ -205,11 +211,11 @@ __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restric
     if (o >= 0) {
       float gt[8], up[8];
       if (pin.n) {
-        load_parts<T, 8>(pin, m, o * 8, gt);
-        load_parts<T, 8>(pin, m, inter + o * 8, up);
+        load_parts<T, 8>(pin, src, o * 8, gt);
+        load_parts<T, 8>(pin, src, inter + o * 8, up);
       } else {
-        load8<T>(x + (int64_t)m * ldx + o * 8, gt);
-        load8<T>(x + (int64_t)m * ldx + inter + o * 8, up);
+        load8<T>(x + (int64_t)src * ldx + o * 8, gt);
+        load8<T>(x + (int64_t)src * ldx + inter + o * 8, up);
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -217,7 +223,7 @@ __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restric
         v[u][i] = round_to<T>(__fmul_rn(round_to<T>(a), up[i]));
         amax = fmaxf(amax, fabsf(v[u][i]));
       }
-      if (y) store8<T>(y + (int64_t)m * ldy + o * 8, v[u]);
+      if (y) store8<T>(y + (int64_t)src * ldy + o * 8, v[u]);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
@@ -231,9 +237,11 @@ __global__ void __launch_bounds__(512) gated_act_quant_kernel(const T* __restric
 // are zero padding.  Grouped operands (dest != null): grid (ctas, rows), input row r goes to
 // operand row dest[r] (< 0: not routed here, nothing written); the operand rows no input row
 // maps to are left as they are, since the grouped GEMM discards their output columns.
+// row_div > 1: input row r reads row r / row_div of x (the rows of a token's expert slots all
+// read that token's row: the gather of the grouped MoE operand).
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(512) act_quant_kernel(const T* __restrict__ x, int64_t ldx, int rows, int k,
-                                                        q::QuantDst dst, const int* dest) {
+                                                        q::QuantDst dst, const int* dest, int row_div) {
   __shared__ float red[cl::MAX_WARPS];
   __shared__ cl::Exchange xch;
   cl::cluster_start(&xch, 1);
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(512) act_quant_kernel(const T* __restrict__ x,
   for (int u = 0; u < MAXU; ++u) {
     const int o = my_oct(u, o0, o1);
     if (o >= 0) {
-      load8<T>(x + (int64_t)src * ldx + o * 8, v[u]);
+      load8<T>(x + (int64_t)(src / row_div) * ldx + o * 8, v[u]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
     } else {
@@ -323,17 +331,17 @@ int launch_rmsnorm16(const void* x, int64_t ldx, const void* res, int64_t ldr, v
 
 // Quantise x [m, k] into the GEMM operand (prologue of ada_nvfp4_linear).
 int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
-                     cudaStream_t st, const int* dest = nullptr) {
+                     cudaStream_t st, const int* dest = nullptr, int row_div = 1) {
   const cl::RowSplit sp = cl::row_split(dst.k / 16);
   if (!sp.maxu || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
   const dim3 grid_((unsigned)sp.ctas, (unsigned)(dest ? m : m_pad));
   cudaError_t err_;
   if (x_dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
-    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, dest);
+    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, dest, row_div);
   } else {
     using TT = __half;
-    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, dest);
+    ADA_ROW_DISPATCH(act_quant_kernel, TT, sp, (const TT*)x, ldx, (int)m, dst.k, dst, dest, row_div);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
@@ -360,9 +368,11 @@ extern "C" int ada_rmsnorm_quant(const void* x, int64_t ldx, const void* residua
                                hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream));
 }
 
-static int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter, int act,
-                                int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream,
-                                const PartIn& pin) {
+namespace ada {
+namespace fused {
+int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter, int act,
+                         int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream,
+                         const PartIn& pin, const int* dest) {
   if (rows <= 0 || inter <= 0 || (act != 0 && act != 1)) return ADA_ERR_INVALID_ARG;
   if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
   const q::QuantDst dst{xq, sfx, gx, terms, block_n, inter};
@@ -376,36 +386,38 @@ static int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy
   }
   if (y && (!fused::a16(y) || (ldy & 7))) return ADA_ERR_ALIGNMENT;
   const cl::RowSplit sp = cl::row_split(inter / 16);
-  const int64_t m_pad = cdiv(rows, block_n) * block_n;
+  const int64_t m_pad = dest ? rows : cdiv(rows, block_n) * block_n;  // grouped rows: no padding rows
   if (!sp.maxu || m_pad > 65535) return ADA_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const dim3 grid_((unsigned)sp.ctas, (unsigned)m_pad);
   cudaError_t err_;
   if (dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
-    ADA_ROW_DISPATCH(fused::gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows,
-                     (int)inter, act, dst, pin);
+    ADA_ROW_DISPATCH(gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows, (int)inter, act, dst,
+                     pin, dest);
   } else {
     using TT = __half;
-    ADA_ROW_DISPATCH(fused::gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows,
-                     (int)inter, act, dst, pin);
+    ADA_ROW_DISPATCH(gated_act_quant_kernel, TT, sp, (const TT*)x, ldx, (TT*)y, ldy, (int)rows, (int)inter, act, dst,
+                     pin, dest);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
+}  // namespace fused
+}  // namespace ada
 
 extern "C" int ada_gated_act_quant(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter,
                                    int act, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx,
                                    void* stream) {
-  return gated_act_quant_impl(x, ldx, y, ldy, rows, inter, act, dtype, terms, block_n, xq, sfx, gx, stream,
-                              PartIn{nullptr, 0, 0, 0});
+  return fused::gated_act_quant_impl(x, ldx, y, ldy, rows, inter, act, dtype, terms, block_n, xq, sfx, gx, stream,
+                                     PartIn{nullptr, 0, 0, 0}, nullptr);
 }
 
 extern "C" int ada_gated_act_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp, void* y,
                                          int64_t ldy, int64_t rows, int32_t inter, int act, int dtype, int terms,
                                          int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream) {
   if (nparts < 1) return ADA_ERR_INVALID_ARG;
-  return gated_act_quant_impl(nullptr, 0, y, ldy, rows, inter, act, dtype, terms, block_n, xq, sfx, gx, stream,
-                              PartIn{parts, nparts, plane, ldp});
+  return fused::gated_act_quant_impl(nullptr, 0, y, ldy, rows, inter, act, dtype, terms, block_n, xq, sfx, gx,
+                                     stream, PartIn{parts, nparts, plane, ldp}, nullptr);
 }
 
 static int rmsnorm_quant_parts_impl(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,

@@ -26,6 +26,7 @@
 // epilogue (warp w reads TMEM lanes 32*(w%4)..+31).  Every mbarrier wait is bounded (2 s);
 // a timeout sets an error bit in the workspace and the CTA drains and exits.
 #include "cluster.cuh"
+#include "parts.cuh"
 #include "quant.cuh"
 #include "sm100.cuh"
 
@@ -422,10 +423,13 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {  // ---------------- producer ----------------
       pdl_wait();
       uint32_t it = 0;
+      // the routing of the next tile is read one tile ahead, off the issue path
+      int expert = p.tile_expert && (int)blockIdx.x < tiles ? p.tile_expert[blockIdx.x / p.n_tiles] : 0;
       for (int t = blockIdx.x; t < tiles && !*abort_v; t += gridDim.x) {
         const int n_tile = t % p.n_tiles, m_tile = t / p.n_tiles;
-        const int expert = p.tile_expert ? p.tile_expert[m_tile] : 0;
         if (expert < 0) break;
+        const int tn = t + (int)gridDim.x;
+        const int expert_next = p.tile_expert && tn < tiles ? p.tile_expert[tn / p.n_tiles] : 0;
         const int w_tile = expert * p.n_tiles + n_tile;
         for (int kt = 0; kt < nkt; ++kt, ++it) {
           const int s = (int)(it % (uint32_t)stages);
@@ -442,6 +446,7 @@ __global__ void __launch_bounds__(192, 1)
             bulk_load(st + C::A_BYTES + C::B_BYTES + C::SFA_BYTES,
                       p.sfx + ((size_t)m_tile * kb64 + (size_t)kt * 4) * SF_BLOCK, C::SFB_BYTES, &full[s]);
         }
+        expert = expert_next;
       }
     }
     __syncwarp();
@@ -453,8 +458,11 @@ __global__ void __launch_bounds__(192, 1)
       if (!C::BLOCK_SF) tmem_cp_32x128b_x4(sfb_unit, desc_sf(smem_u32(const_sf)));
       if (p.tile_expert) pdl_wait();  // the routing is read below
       uint32_t it = 0, lt = 0;
+      int expert = p.tile_expert && (int)blockIdx.x < tiles ? p.tile_expert[blockIdx.x / p.n_tiles] : 0;
       for (int t = blockIdx.x; t < tiles && !*abort_v; t += gridDim.x, ++lt) {
-        if (p.tile_expert && p.tile_expert[t / p.n_tiles] < 0) break;
+        if (expert < 0) break;
+        const int tn = t + (int)gridDim.x;
+        const int expert_next = p.tile_expert && tn < tiles ? p.tile_expert[tn / p.n_tiles] : 0;  // one tile ahead
         const uint32_t b = lt & 1, use = lt >> 1;
         if (use > 0 && !mbar_wait_bounded(&acce[b], (use - 1) & 1, abort_v, p.err, 8u)) break;
         tc_fence_after();
@@ -485,6 +493,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_commit(&accf[b]);  // also after a failure: drains the issued MMAs
         if (failed) break;
+        expert = expert_next;
       }
     }
     __syncwarp();
@@ -495,14 +504,36 @@ __global__ void __launch_bounds__(192, 1)
     const int et = threadIdx.x - 64;
     const int r = q * 32 + lane;
     uint32_t lt = 0;
+    // the next tile's expert, row scale and (grouped, 16-token tiles) output rows are read one
+    // tile ahead, while this tile's accumulator is still being computed
+    constexpr bool RM_REGS = BN <= 16;
+    int ex_n = 0, rm_n[RM_REGS ? BN : 1];
+    float g_n = 1.f, gw_n = 1.f;
+    auto read_ahead = [&](int t) {
+      if (t >= tiles) return;
+      const int mt = t / p.n_tiles;
+      ex_n = p.tile_expert ? p.tile_expert[mt] : 0;
+      if (et < BN) {
+        g_n = p.gx[mt * BN + et];
+        if (ex_n >= 0) gw_n = __ldg(p.gw + ex_n);
+      }
+      if (RM_REGS && p.row_map)
+#pragma unroll
+        for (int k = 0; k < (RM_REGS ? BN : 1); ++k) rm_n[k] = p.row_map[mt * BN + k];
+    };
+    read_ahead(blockIdx.x);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
       const int n_tile = t % p.n_tiles, m_tile = t / p.n_tiles;
-      const int expert = p.tile_expert ? p.tile_expert[m_tile] : 0;
+      const int expert = ex_n;
       if (expert < 0) break;
-      const float gw = __ldg(p.gw + expert);
+      const float g_t = g_n, gw = gw_n;
+      int rm[RM_REGS ? BN : 1];
+#pragma unroll
+      for (int k = 0; k < (RM_REGS ? BN : 1); ++k) rm[k] = rm_n[k];
+      read_ahead(t + (int)gridDim.x);
       const uint32_t b = lt & 1, use = lt >> 1;
       if (et < BN) {
-        float g = p.gx[m_tile * BN + et];
+        float g = g_t;
 #pragma unroll
         for (int tt = 0; tt < T; ++tt) {
           gsc[tt * BN + et] = __fmul_rn(gw, g);
@@ -521,17 +552,19 @@ __global__ void __launch_bounds__(192, 1)
         float o[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) o[k] = 0.f;
+        uint32_t v[T][16];  // every term's 16 columns in flight together, one wait
 #pragma unroll
-        for (int tt = 0; tt < T; ++tt) {
-          float v[16];
-          tmem_ld16(lane_addr + tt * BN + c, v);
+        for (int tt = 0; tt < T; ++tt) tmem_ld16_nowait(lane_addr + tt * BN + c, v[tt]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int k = 0; k < 16; ++k) o[k] = fmaf(v[k], gsc[tt * BN + c + k], o[k]);
-        }
+        for (int tt = 0; tt < T; ++tt)
+#pragma unroll
+          for (int k = 0; k < 16; ++k) o[k] = fmaf(__uint_as_float(v[tt][k]), gsc[tt * BN + c + k], o[k]);
         if (ok) {
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const int m = p.row_map ? p.row_map[m_tile * BN + c + k] : m_tile * BN + c + k;
+            const int m = !p.row_map ? m_tile * BN + c + k : RM_REGS ? rm[(c + k) % (RM_REGS ? BN : 1)]
+                                                                       : p.row_map[m_tile * BN + c + k];
             if (m >= 0 && m < p.M) store_out(p.y, p.out_dtype, (int64_t)m * p.ldy + n, o[k] + bias);
           }
         }
@@ -1024,7 +1057,10 @@ inline int64_t group_tiles(int64_t m, int64_t experts) { return cdiv(m, GROUP_BN
 
 namespace fused {
 int launch_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t m_pad, const q::QuantDst& dst,
-                     cudaStream_t st, const int* dest);
+                     cudaStream_t st, const int* dest, int row_div);
+int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int32_t inter, int act,
+                         int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream,
+                         const PartIn& pin, const int* dest);
 }
 }  // namespace ada
 
@@ -1073,7 +1109,7 @@ extern "C" int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int6
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
-  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, nullptr);
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, nullptr, 1);
   if (rc != ADA_OK) return rc;
   return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, bias, y,
                        y_dtype, ldy, reinterpret_cast<unsigned int*>(ws), st);
@@ -1133,7 +1169,7 @@ static int linear_grouped_impl(const void* x, int x_dtype, int64_t ldx, int64_t 
                  tile_expert, row_map, dest, err, (int)expert_base, strict);
   ADA_CHECK_LAUNCH();
   const q::QuantDst dst{ws + P.off_xq, ws + P.off_sfx, reinterpret_cast<float*>(ws + P.off_gx), terms, P.bn, (int)k};
-  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, dest);
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, P.m_pad, dst, st, dest, 1);
   if (rc != ADA_OK) return rc;
   // the stacked weight matrix [num_experts * n, k / 2]: expert e's tile j is 128-row block e * (n / 128) + j
   return fp4::run_gemm(P, dst.xq, dst.sfx, dst.gx, (int)m, (int)n, (int)k, w_packed, ldw, sf_w, w_scale_2, nullptr, y,
@@ -1160,6 +1196,112 @@ extern "C" int ada_nvfp4_linear_grouped_ep(const void* x, int x_dtype, int64_t l
                              y_dtype, ldy, terms, workspace, workspace_bytes, stream, expert_base, 0);
 }
 
+// ---- the expert MLP of a MoE block in one call ----------------------------------------
+// Layout of its workspace (every region 256-byte aligned): [error word][routing: one int, tile
+// experts, operand row map, destination of each input row][gate_up operand: codes, scales, row
+// scales][gate_up output h, the model dtype][down operand: codes, scales, row scales].
+struct ExpertsLayout {
+  fp4::Plan gu, dn;
+  size_t off_route, off_xq1, off_sfx1, off_gx1, off_h, off_xq2, off_sfx2, off_gx2, total;
+};
+static size_t al256z(size_t v) { return (v + 255) & ~(size_t)255; }
+static int experts_layout(int64_t m, int64_t hidden, int64_t inter, int terms, int64_t experts, ExpertsLayout& L) {
+  size_t o1 = 0, t1 = 0, o2 = 0, t2 = 0;
+  int rc = grouped_plan(m, 2 * inter, hidden, terms, experts, L.gu, o1, t1);
+  if (rc != ADA_OK) return rc;
+  rc = grouped_plan(m, hidden, inter, terms, experts, L.dn, o2, t2);
+  if (rc != ADA_OK) return rc;
+  const int64_t t_max = L.gu.m_tiles, m_pad = L.gu.m_pad;
+  size_t off = fp4::ERR_BYTES;
+  L.off_route = off;
+  off = al256z(off + (size_t)(1 + t_max + t_max * fp4::GROUP_BN + m) * sizeof(int));
+  L.off_xq1 = off;
+  off = al256z(off + (size_t)terms * m_pad * (size_t)(hidden / 2));
+  L.off_sfx1 = off;
+  if (terms == 1) off = al256z(off + (size_t)t_max * (size_t)(hidden / 64) * 512);
+  L.off_gx1 = off;
+  off = al256z(off + (size_t)m_pad * 4);
+  L.off_h = off;
+  off = al256z(off + (size_t)m * (size_t)(2 * inter) * 2);
+  L.off_xq2 = off;
+  off = al256z(off + (size_t)terms * m_pad * (size_t)(inter / 2));
+  L.off_sfx2 = off;
+  if (terms == 1) off = al256z(off + (size_t)t_max * (size_t)(inter / 64) * 512);
+  L.off_gx2 = off;
+  off = al256z(off + (size_t)m_pad * 4);
+  L.total = off;
+  return ADA_OK;
+}
+
+extern "C" size_t ada_moe_experts_workspace_size(int64_t tokens, int32_t topk, int64_t hidden, int64_t inter,
+                                                 int terms, int32_t num_experts) {
+  if (tokens <= 0 || topk <= 0) return 0;
+  ExpertsLayout L;
+  return experts_layout(tokens * topk, hidden, inter, terms, num_experts, L) == ADA_OK ? L.total : 0;
+}
+
+extern "C" int ada_moe_experts(const void* x, int x_dtype, int64_t ldx, int64_t tokens, int32_t topk,
+                               const int32_t* expert_ids, int32_t num_experts, int32_t expert_base, int32_t all_local,
+                               const uint8_t* w_gate_up, int64_t ld_gate_up, const uint8_t* sf_gate_up,
+                               const float* scale2_gate_up, const uint8_t* w_down, int64_t ld_down,
+                               const uint8_t* sf_down, const float* scale2_down, int64_t inter, int64_t hidden,
+                               int act, void* y, int64_t ldy, int terms, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  if (tokens == 0) return ADA_OK;
+  if (tokens < 0 || topk <= 0 || num_experts <= 0 || expert_base < 0 || (act != 0 && act != 1))
+    return ADA_ERR_INVALID_ARG;
+  if (!x || !expert_ids || !w_gate_up || !sf_gate_up || !scale2_gate_up || !w_down || !sf_down || !scale2_down || !y ||
+      !workspace)
+    return ADA_ERR_INVALID_ARG;
+  if (x_dtype != ADA_DT_BF16 && x_dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  if (ldx < hidden || ldy < hidden || ld_gate_up < hidden / 2 || ld_down < inter / 2) return ADA_ERR_INVALID_ARG;
+  if ((int64_t)num_experts * 2 * inter > (1 << 24) || tokens * topk > (1 << 24)) return ADA_ERR_UNSUPPORTED;
+  const int64_t m = tokens * topk;
+  ExpertsLayout L;
+  int rc = experts_layout(m, hidden, inter, terms, num_experts, L);
+  if (rc != ADA_OK) return rc;
+  if (workspace_bytes < L.total) return ADA_ERR_WORKSPACE;
+  if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)y & 15) || (ldy & 7) || ((uintptr_t)w_gate_up & 15) ||
+      (ld_gate_up & 15) || ((uintptr_t)w_down & 15) || (ld_down & 15) || ((uintptr_t)sf_gate_up & 15) ||
+      ((uintptr_t)sf_down & 15) || ((uintptr_t)workspace & 255) || ((uintptr_t)expert_ids & 3))
+    return ADA_ERR_ALIGNMENT;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned int* err = reinterpret_cast<unsigned int*>(ws);
+  const int t_max = L.gu.m_tiles;
+  int* tile_expert = reinterpret_cast<int*>(ws + L.off_route) + 1;
+  int* row_map = tile_expert + t_max;
+  int* dest = row_map + t_max * fp4::GROUP_BN;
+  // one routing for both projections: 16-row tiles of each local expert's rows
+  const size_t rsmem = (size_t)3 * num_experts * sizeof(int);
+  if (rsmem > 48 * 1024 &&
+      cudaFuncSetAttribute(fp4::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem) != cudaSuccess)
+    return ADA_ERR_CUDA;
+  (void)launch_k(fp4::route_kernel, dim3(1), dim3(1024), rsmem, st, expert_ids, (int)m, (int)num_experts, t_max,
+                 tile_expert, row_map, dest, err, (int)expert_base, all_local ? 1 : 0);
+  ADA_CHECK_LAUNCH();
+  // gate_up operand: routed row r reads token r / topk's row of x (the gather) and lands in its
+  // expert's tile
+  const q::QuantDst d1{ws + L.off_xq1, ws + L.off_sfx1, reinterpret_cast<float*>(ws + L.off_gx1), terms,
+                       fp4::GROUP_BN, (int)hidden};
+  rc = fused::launch_act_quant(x, x_dtype, ldx, m, L.gu.m_pad, d1, st, dest, topk);
+  if (rc != ADA_OK) return rc;
+  void* h = ws + L.off_h;
+  rc = fp4::run_gemm(L.gu, d1.xq, d1.sfx, d1.gx, (int)m, (int)(2 * inter), (int)hidden, w_gate_up, ld_gate_up,
+                     sf_gate_up, scale2_gate_up, nullptr, h, x_dtype, 2 * inter, err, st, nullptr, 0, 0, 1, 0, nullptr,
+                     nullptr, 0, 0, tile_expert, row_map, (int64_t)num_experts * 2 * inter);
+  if (rc != ADA_OK) return rc;
+  // act(gate) * up of each routed row, quantised straight into the down projection's operand
+  const q::QuantDst d2{ws + L.off_xq2, ws + L.off_sfx2, reinterpret_cast<float*>(ws + L.off_gx2), terms,
+                       fp4::GROUP_BN, (int)inter};
+  rc = fused::gated_act_quant_impl(h, 2 * inter, nullptr, 0, m, (int32_t)inter, act, x_dtype, terms, fp4::GROUP_BN,
+                                   d2.xq, d2.sfx, d2.gx, stream, PartIn{nullptr, 0, 0, 0}, dest);
+  if (rc != ADA_OK) return rc;
+  return fp4::run_gemm(L.dn, d2.xq, d2.sfx, d2.gx, (int)m, (int)hidden, (int)inter, w_down, ld_down, sf_down,
+                       scale2_down, nullptr, y, x_dtype, ldy, err, st, nullptr, 0, 0, 1, 0, nullptr, nullptr, 0, 0,
+                       tile_expert, row_map, (int64_t)num_experts * hidden);
+}
+
 extern "C" int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
                                 const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w, const float* w_scale_2,
                                 int64_t n, const void* bias, void* y, int y_dtype, int64_t ldy, int terms,
@@ -1178,7 +1320,7 @@ extern "C" int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int6
   if (((uintptr_t)x & 15) || (ldx & 7) || ((uintptr_t)xq & 15) || ((uintptr_t)gx & 3)) return ADA_ERR_ALIGNMENT;
   const int64_t m_pad = cdiv(m, block_n) * block_n;
   const q::QuantDst dst{xq, sfx, gx, terms, block_n, (int)k};
-  return fused::launch_act_quant(x, x_dtype, ldx, m, m_pad, dst, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  return fused::launch_act_quant(x, x_dtype, ldx, m, m_pad, dst, reinterpret_cast<cudaStream_t>(stream), nullptr, 1);
 }
 
 extern "C" int ada_nvfp4_workspace_status(const void* workspace, int64_t m, int64_t n, int64_t k, int terms,

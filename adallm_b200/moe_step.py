@@ -10,13 +10,15 @@ loop :1263-1290):
 
     x, residual = post_attention_layernorm(o, residual)   one kernel summing the o planes
     router_logits = gate(x)                              bf16 [T, E] (FP16Linear, qwen3.py:696)
-    ids, w = softmax fp32 -> top-k -> renormalise         ada_moe_route_topk
+    ids, w = softmax fp32 -> top-k -> renormalise         one kernel with the router GEMM
+                                                          (ada_moe_router_topk)
     h = grouped NVFP4 gate+up over the T * top_k routed rows (only the touched experts streamed)
-    a = SiLU(gate) * up;  y = grouped NVFP4 down;  out = sum_k w_k * y_k     ada_moe_combine
+    a = SiLU(gate) * up;  y = grouped NVFP4 down         ada_moe_experts (5 launches)
+    out = sum_k w_k * y_k                                 ada_moe_combine
 
 The reference runs the experts as top_k separate gather GEMMs per projection (gate, up and down
-each, qwen3.py:1263-1290); here gate and up are one stacked [E, 2I, H] weight and each projection
-is one grouped launch over all routed rows.  Weights are random-init NVFP4 (decode_step.py's
+each, qwen3.py:1263-1290); here gate and up are one stacked [E, 2I, H] weight, each projection is
+one grouped launch over all routed rows, and one routing plan serves both.  Weights are random-init NVFP4 (decode_step.py's
 generator); router weights N(0, 1/H), so router logits are ~N(0, 1) as the config states.
 """
 from __future__ import annotations
@@ -91,8 +93,8 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
     Attention runs at tensor-parallel size 1 (as the reference's MoE).  With cfg.ep_size > 1
     (expert parallelism, beyond the reference; one process per GPU, `group` the NCCL group of the
     ep_size ranks) every rank runs the same attention and routing, holds a contiguous block of
-    experts, runs the grouped GEMMs over the rows routed to its experts only
-    (ada_nvfp4_linear_grouped_ep), sums its slots in fp32 (ada_moe_combine_ep_f32) and all-reduces
+    experts, runs the expert MLP over the rows routed to its experts only (ada_moe_experts with
+    all_local = 0), sums its slots in fp32 (ada_moe_combine_ep_f32) and all-reduces
     them: one NCCL all-reduce of [batch, hidden] fp32 per layer, rounded once to bf16 afterwards, so
     the block output is the single-GPU combine's up to the order of the fp32 additions."""
 
@@ -159,57 +161,46 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
         B, k = self.B, c.top_k
         bf = torch.bfloat16
         rows = B * k
-        self.router_logits = torch.zeros((B, c.num_experts), dtype=bf, device=d)
         self.route_ids = torch.zeros(rows, dtype=torch.int32, device=d)
         self.route_w = torch.zeros(rows, dtype=bf, device=d)
-        self.token_of_row = torch.arange(B, device=d).repeat_interleave(k)
-        self.x_rows = torch.zeros((rows, c.hidden), dtype=bf, device=d)
-        self.h_rows = torch.zeros((rows, 2 * c.moe_intermediate), dtype=bf, device=d)
-        self.a_rows = torch.zeros((rows, c.moe_intermediate), dtype=bf, device=d)
         self.y_rows = torch.zeros((rows, c.hidden), dtype=bf, device=d)
         self.moe_sum = torch.zeros((B, c.hidden), dtype=torch.float32, device=d) if c.ep_size > 1 else None
         lib = N.lib()
-        gu, dn = self.layers[0]["experts_gate_up"], self.layers[0]["experts_down"]
-        self.ws_gate_up = torch.zeros(int(lib.ada_nvfp4_linear_grouped_workspace_size(rows, gu.n, gu.k, c.terms, gu.e)),
+        gu = self.layers[0]["experts_gate_up"]
+        self.ws_experts = torch.zeros(int(lib.ada_moe_experts_workspace_size(B, k, c.hidden, c.moe_intermediate,
+                                                                             c.terms, gu.e)),
                                       dtype=torch.uint8, device=d)
-        self.ws_down = torch.zeros(int(lib.ada_nvfp4_linear_grouped_workspace_size(rows, dn.n, dn.k, c.terms, dn.e)),
-                                   dtype=torch.uint8, device=d)
 
     def error_words(self) -> list[torch.Tensor]:
         words = super().error_words()
-        if hasattr(self, "ws_down"):
-            words += [self.ws_gate_up[:4].view(torch.int32), self.ws_down[:4].view(torch.int32)]
+        if hasattr(self, "ws_experts"):
+            words.append(self.ws_experts[:4].view(torch.int32))
         return words
 
-    def _grouped(self, x: torch.Tensor, w: Experts, y: torch.Tensor, ws: torch.Tensor, stream: int):
-        lib = N.lib()
-        if self.cfg.ep_size == 1:
-            st = lib.ada_nvfp4_linear_grouped(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
-                                              w.packed.stride(1), w.sf.data_ptr(), w.scale_2.data_ptr(), w.e, w.n,
-                                              self.route_ids.data_ptr(), y.data_ptr(), 0, y.stride(0), self.cfg.terms,
-                                              ws.data_ptr(), ws.numel(), stream)
-        else:  # rows routed to other ranks' experts are skipped
-            st = lib.ada_nvfp4_linear_grouped_ep(x.data_ptr(), 0, x.stride(0), x.shape[0], w.k, w.packed.data_ptr(),
-                                                 w.packed.stride(1), w.sf.data_ptr(), w.scale_2.data_ptr(), w.e,
-                                                 self.expert_base, w.n, self.route_ids.data_ptr(), y.data_ptr(), 0,
-                                                 y.stride(0), self.cfg.terms, ws.data_ptr(), ws.numel(), stream)
-        N.check(st, "grouped NVFP4 kernel")
+    def _experts_mlp(self, L, stream: int):
+        """self.xnorm -> self.y_rows: every routed row through its (local) expert's gate_up, SiLU*up
+        and down (ada_moe_experts: one routing, the gather folded into the quantiser); rows routed
+        to another rank's expert are skipped."""
+        c = self.cfg
+        gu, dn = L["experts_gate_up"], L["experts_down"]
+        st = N.lib().ada_moe_experts(self.xnorm.data_ptr(), 0, self.xnorm.stride(0), self.B, c.top_k,
+                                     self.route_ids.data_ptr(), gu.e, self.expert_base, int(c.ep_size == 1),
+                                     gu.packed.data_ptr(), gu.packed.stride(1), gu.sf.data_ptr(), gu.scale_2.data_ptr(),
+                                     dn.packed.data_ptr(), dn.packed.stride(1), dn.sf.data_ptr(), dn.scale_2.data_ptr(),
+                                     c.moe_intermediate, c.hidden, 0, self.y_rows.data_ptr(), self.y_rows.stride(0),
+                                     c.terms, self.ws_experts.data_ptr(), self.ws_experts.numel(), stream)
+        N.check(st, "MoE expert MLP")
 
     def _moe_block(self, L, stream: int):
         """self.xnorm -> self.hidden: router, top-k, grouped experts, weighted combine."""
         c = self.cfg
         lib = N.lib()
         B = self.B
-        torch.matmul(self.xnorm, L["router"].t(), out=self.router_logits)
-        N.check(lib.ada_moe_route_topk(self.router_logits.data_ptr(), 0, c.num_experts, B, c.num_experts, c.top_k,
-                                       int(c.norm_topk_prob), self.route_ids.data_ptr(), self.route_w.data_ptr(),
-                                       stream), "moe route")
-        torch.index_select(self.xnorm, 0, self.token_of_row, out=self.x_rows)
-        self._grouped(self.x_rows, L["experts_gate_up"], self.h_rows, self.ws_gate_up, stream)
-        N.check(lib.ada_gated_act(self.h_rows.data_ptr(), self.h_rows.stride(0), self.a_rows.data_ptr(),
-                                  self.a_rows.stride(0), self.a_rows.shape[0], c.moe_intermediate, 0, 0, stream),
-                "silu_and_mul")
-        self._grouped(self.a_rows, L["experts_down"], self.y_rows, self.ws_down, stream)
+        N.check(lib.ada_moe_router_topk(self.xnorm.data_ptr(), 0, self.xnorm.stride(0), B, L["router"].data_ptr(),
+                                        L["router"].stride(0), c.hidden, c.num_experts, c.top_k,
+                                        int(c.norm_topk_prob), self.route_ids.data_ptr(), self.route_w.data_ptr(),
+                                        self.ws_experts.data_ptr(), stream), "moe router + route")
+        self._experts_mlp(L, stream)
         if c.ep_size == 1:
             N.check(lib.ada_moe_combine(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(), B,
                                         c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
@@ -270,11 +261,12 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
 
     def kernels_per_step(self) -> int:
         """Embedding; per layer: RMSNorm+quant, qkv GEMM, q/k-norm+RoPE+store, attention (one kernel
-        for short caches, else split + merge+quant), o GEMM, RMSNorm from planes, route top-k,
-        grouped gate_up (route + gathering quantiser + GEMM), SiLU*up, grouped down (3), combine;
+        for short caches, else split + merge+quant), o GEMM, RMSNorm from planes, router GEMM +
+        top-k, the
+        expert MLP (routing, gathering quantiser, gate_up GEMM, SiLU*up+quant, down GEMM), combine;
         final RMSNorm; lm_head + pick (the expert-parallel all-reduce is NCCL's)."""
         attn = 1 if self.max_pages_per_seq * self.cfg.page_size <= 1024 and self.cfg.hkv <= 8 else 2
-        return 1 + self.cfg.num_layers * (14 + attn) + 3
+        return 1 + self.cfg.num_layers * (12 + attn) + 3
 
     def export_cpu_weights(self) -> dict:
         if self.cfg.ep_size != 1:

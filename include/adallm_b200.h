@@ -309,6 +309,13 @@ ADA_API int ada_nvfp4_linear_grouped(const void* x, int x_dtype, int64_t ldx, in
  * (fp32, slot order; hidden % 8 == 0). */
 ADA_API int ada_moe_route_topk(const void* logits, int dtype, int64_t ld, int64_t tokens, int32_t experts,
                                int32_t topk, int32_t norm_topk_prob, int32_t* ids, void* weights, void* stream);
+/* The router GEMM (router_logits = x . router_w^T, rounded to dtype as the reference's F.linear
+ * output, qwen3.py:1026) fused with ada_moe_route_topk: x [tokens, hidden], router_w [experts,
+ * hidden] (row strides ldx, ldw; hidden % 8 == 0, experts <= 1024); ids / weights as
+ * ada_moe_route_topk.  err: a device word ORed with 0x80 if a bounded wait ran out. */
+ADA_API int ada_moe_router_topk(const void* x, int dtype, int64_t ldx, int64_t tokens, const void* router_w,
+                                int64_t ldw, int32_t hidden, int32_t experts, int32_t topk, int32_t norm_topk_prob,
+                                int32_t* ids, void* weights, unsigned int* err, void* stream);
 ADA_API int ada_moe_combine(const void* y, int dtype, int64_t ldy, const void* weights, int64_t tokens,
                             int32_t topk, int32_t hidden, void* out, int64_t ldo, void* stream);
 /* Expert parallelism (no reference counterpart: the reference runs MoE at TP = 1 only,
@@ -333,6 +340,25 @@ ADA_API int ada_moe_combine_ep_f32(const void* y, int dtype, int64_t ldy, const 
                                    const int32_t* expert_ids, int32_t expert_base, int32_t num_local,
                                    int64_t tokens, int32_t topk, int32_t hidden, float* out, int64_t ldo,
                                    void* stream);
+/* The expert MLP of a MoE block in one call (Qwen3MoeSparseMoeBlock's expert loop,
+ * adallm/architectures/qwen3.py:1263-1290, for the rows routed to this rank's experts): for every
+ * routed row r = t * topk + j with expert e = expert_ids[r] in [expert_base, expert_base +
+ * num_experts): y[r] = down_e(act(gate_e(x[t])) * up_e(x[t])), act SiLU (0) or GELU-tanh (1).
+ * w_gate_up is the stack [num_experts][2 * inter][hidden / 2] (gate rows first, row stride
+ * ld_gate_up), w_down [num_experts][hidden][inter / 2]; sf_* their prepacked scales, scale2_*
+ * [num_experts].  One routing (16-row expert tiles) serves both projections; x's rows are gathered
+ * by the quantiser, act(gate) * up is quantised straight into the down operand.  Rows routed to
+ * another rank's expert are left untouched when all_local == 0, an error (workspace error word)
+ * when all_local == 1.  workspace: ada_moe_experts_workspace_size bytes, 256-byte aligned, its
+ * first 4 bytes the error word (zero before the first use). */
+ADA_API size_t ada_moe_experts_workspace_size(int64_t tokens, int32_t topk, int64_t hidden, int64_t inter, int terms,
+                                              int32_t num_experts);
+ADA_API int ada_moe_experts(const void* x, int x_dtype, int64_t ldx, int64_t tokens, int32_t topk,
+                            const int32_t* expert_ids, int32_t num_experts, int32_t expert_base, int32_t all_local,
+                            const uint8_t* w_gate_up, int64_t ld_gate_up, const uint8_t* sf_gate_up,
+                            const float* scale2_gate_up, const uint8_t* w_down, int64_t ld_down,
+                            const uint8_t* sf_down, const float* scale2_down, int64_t inter, int64_t hidden, int act,
+                            void* y, int64_t ldy, int terms, void* workspace, size_t workspace_bytes, void* stream);
 ADA_API int ada_nvfp4_act_quant(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int terms,
                                 int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);
 /* The tensor-core GEMM on its own, for activations already quantised by

@@ -6,6 +6,7 @@ import pytest
 import torch
 
 from oracle import nvfp4 as nv
+from adallm_b200 import _native as N
 from adallm_b200.moe import route_topk, combine
 from adallm_b200.nvfp4_gemm import nvfp4_linear_gather
 from tests.gpu_util import dev, rel_l2
@@ -154,3 +155,96 @@ def test_expert_parallel_block_sums_to_the_full_block():
             ref[i] += w[i, j] * nv.linear_ref(act, b[0], b[2].astype(np.float32), b[3])[0]
     assert rel_l2(summed.cpu(), torch.from_numpy(ref)) < 2e-2
     assert rel_l2(full.float().cpu(), torch.from_numpy(ref)) < 2e-2
+
+
+@pytest.mark.parametrize("t,e,k,hid,inter,base,cnt,terms", [(16, 32, 8, 2048, 768, 0, 32, 4),
+                                                            (16, 32, 8, 2048, 768, 16, 16, 4),
+                                                            (5, 8, 2, 512, 256, 0, 8, 1)])
+def test_moe_experts_matches_the_grouped_pipeline(t, e, k, hid, inter, base, cnt, terms):
+    """ada_moe_experts (one routing, the gather folded into the quantiser, SiLU*up quantised
+    straight into the down operand) against the unfused pipeline -- row gather, grouped gate_up,
+    SiLU*up, grouped down, each through its own entry point: bit-identical rows for the experts
+    held ([base, base + cnt)), other rows untouched, no error."""
+    from adallm_b200.activation import gated_act
+    d = dev()
+    gu, _ = _experts(cnt, 2 * inter, hid, 900 + base)
+    dn, _ = _experts(cnt, hid, inter, 950 + base)
+    g = torch.Generator().manual_seed(t + e)
+    x = torch.randn((t, hid), generator=g).to(torch.bfloat16).to(d)
+    ids = torch.stack([torch.randperm(e, generator=g)[:k] for _ in range(t)]).to(torch.int32).to(d)
+    flat = ids.reshape(-1)
+    h = nvfp4_linear_gather(x.repeat_interleave(k, 0), gu[0], gu[1], gu[2], flat, 16, expert_base=base, terms=terms)
+    a = gated_act(h, 0)
+    y_ref = nvfp4_linear_gather(a, dn[0], dn[1], dn[2], flat, 16, expert_base=base, terms=terms)
+    from adallm_b200.nvfp4_gemm import prepack_scales
+    sf_gu = prepack_scales(gu[1].reshape(cnt * 2 * inter, hid // 16), cnt * 2 * inter, hid)
+    sf_dn = prepack_scales(dn[1].reshape(cnt * hid, inter // 16), cnt * hid, inter)
+    lib = N.lib()
+    ws = torch.zeros(int(lib.ada_moe_experts_workspace_size(t, k, hid, inter, terms, cnt)), dtype=torch.uint8, device=d)
+    y = torch.full((t * k, hid), 7.0, dtype=torch.bfloat16, device=d)
+    st = lib.ada_moe_experts(x.data_ptr(), 0, x.stride(0), t, k, flat.data_ptr(), cnt, base, int(cnt == e),
+                             gu[0].data_ptr(), gu[0].stride(1), sf_gu.data_ptr(), gu[2].data_ptr(), dn[0].data_ptr(),
+                             dn[0].stride(1), sf_dn.data_ptr(), dn[2].data_ptr(), inter, hid, 0, y.data_ptr(),
+                             y.stride(0), terms, ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    N.check(st, "moe experts")
+    torch.cuda.synchronize()
+    local = ((flat >= base) & (flat < base + cnt)).cpu()
+    assert int(ws[:4].view(torch.int32).item()) == 0
+    assert torch.equal(y.cpu()[local], y_ref.cpu()[local])
+    assert bool((y.cpu()[~local] == 7.0).all())
+
+
+def _router_case(t, e, h, seed, exact):
+    g = torch.Generator().manual_seed(seed)
+    if exact:  # small integers times powers of two: every product and sum is exact in fp32 and bf16
+        x = torch.randint(-2, 3, (t, h), generator=g).float() * 0.25
+        w = torch.randint(-2, 3, (e, h), generator=g).float() * 0.125
+    else:  # the config-4 router: N(0, 1/H) weights, so logits ~ N(0, 1)
+        x = torch.randn((t, h), generator=g)
+        w = torch.randn((e, h), generator=g) * h ** -0.5
+    return x.to(torch.bfloat16), w.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("t,e,h,k,norm", [(16, 128, 2048, 8, True), (5, 64, 512, 4, False), (3, 256, 1024, 8, True),
+                                          (2, 24, 256, 2, True)])
+def test_router_topk_fused_exact(t, e, h, k, norm):
+    """The fused router GEMM + routing on exactly representable inputs: identical experts, order
+    and weights to ada_moe_route_topk over the exact logits (rounded to bf16, as F.linear)."""
+    d = dev()
+    x, w = _router_case(t, e, h, 31 + t, exact=True)
+    logits = (x.double() @ w.double().t()).to(torch.bfloat16)
+    rid, rw = route_topk(logits.to(d), k, norm)
+    ids = torch.empty((t, k), dtype=torch.int32, device=d)
+    wts = torch.empty((t, k), dtype=torch.bfloat16, device=d)
+    err = torch.zeros(1, dtype=torch.int32, device=d)
+    xd, wd = x.to(d), w.to(d)
+    N.check(N.lib().ada_moe_router_topk(xd.data_ptr(), 0, h, t, wd.data_ptr(), h, h, e, k, int(norm), ids.data_ptr(),
+                                        wts.data_ptr(), err.data_ptr(), torch.cuda.current_stream().cuda_stream),
+            "router")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(ids.long(), rid.long().view(t, k))
+    assert torch.equal(wts, rw.view(t, k))
+
+
+def test_router_topk_fused_config4():
+    """N(0, 1) router logits (config 4): the fused kernel's fp32 sums differ from an fp64 product
+    only in order, so its routing equals the routing of the fp64 logits rounded to bf16 except
+    where two logits sit within one bf16 rounding of each other."""
+    d = dev()
+    t, e, h, k = 16, 128, 2048, 8
+    x, w = _router_case(t, e, h, 5, exact=False)
+    logits = (x.double() @ w.double().t()).to(torch.bfloat16)
+    rid, rw = route_topk(logits.to(d), k, True)
+    ids = torch.empty((t, k), dtype=torch.int32, device=d)
+    wts = torch.empty((t, k), dtype=torch.bfloat16, device=d)
+    err = torch.zeros(1, dtype=torch.int32, device=d)
+    xd, wd = x.to(d), w.to(d)
+    N.check(N.lib().ada_moe_router_topk(xd.data_ptr(), 0, h, t, wd.data_ptr(), h, h, e, k, 1, ids.data_ptr(),
+                                        wts.data_ptr(), err.data_ptr(), torch.cuda.current_stream().cuda_stream),
+            "router")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    same = (ids.long() == rid.long().view(t, k)).float().mean().item()
+    assert same >= 0.97, same
+    assert torch.allclose(wts.float(), rw.view(t, k).float(), atol=2e-2)
