@@ -138,6 +138,19 @@ __device__ __forceinline__ bool exchange_wait(unsigned long long* bar) {
   }
 }
 
+// Two reductions in one exchange: each CTA sends (a, b) as one 8-byte transaction.
+struct Exchange2 {
+  float2 slots[MAX_CLUSTER];
+  unsigned long long bar;
+};
+__device__ __forceinline__ void exchange2_init(Exchange2* x) { exchange_init_bytes(&x->bar, nctarank() * 8u); }
+__device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, float a, float b, uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   cluster_addr),
+               "f"(a), "f"(b), "r"(cluster_bar)
+               : "memory");
+}
+
 // Start of a cluster row kernel: initialise its `count` exchanges, then arrive on the
 // cluster's start barrier (the matching cluster_wait() makes the initialisation visible).
 __device__ __forceinline__ void cluster_start(Exchange* xs, int count) {
@@ -159,6 +172,39 @@ __device__ __forceinline__ float cluster_allreduce_x(float v, float* red, Exchan
   exchange_wait(&x->bar);
   float r = x->slots[0];
   for (uint32_t i = 1; i < n; ++i) r = Op::apply(r, x->slots[i]);
+  return r;
+}
+
+// Cluster-wide reduction of two values at once (OpA on a, OpB on b; `red` holds 2 * MAX_WARPS
+// floats): one exchange, CTA partials combined in rank order for each.
+template <typename OpA, typename OpB>
+__device__ __forceinline__ float2 cluster_allreduce2_x(float a, float b, float* red, Exchange2* x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a = OpA::apply(a, __shfl_xor_sync(0xffffffffu, a, o));
+    b = OpB::apply(b, __shfl_xor_sync(0xffffffffu, b, o));
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) {
+    red[w] = a;
+    red[MAX_WARPS + w] = b;
+  }
+  __syncthreads();
+  float ra = red[0], rb = red[MAX_WARPS];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) {
+    ra = OpA::apply(ra, red[i]);
+    rb = OpB::apply(rb, red[MAX_WARPS + i]);
+  }
+  const uint32_t n = nctarank();
+  if (n == 1) return make_float2(ra, rb);
+  if (threadIdx.x < n) st_async_v2(mapa(&x->slots[ctarank()], threadIdx.x), ra, rb, mapa(&x->bar, threadIdx.x));
+  exchange_wait(&x->bar);
+  float2 r = x->slots[0];
+  for (uint32_t i = 1; i < n; ++i) {
+    r.x = OpA::apply(r.x, x->slots[i].x);
+    r.y = OpB::apply(r.y, x->slots[i].y);
+  }
   return r;
 }
 

@@ -6,8 +6,10 @@
 //   * SiLU(gate) * up / GELU(tanh)(gate) * up -> quantised operand of down_proj
 //     (reference adallm/ops/activation.py:6-26)
 //   * plain quantisation of a bf16/fp16 matrix (the prologue of ada_nvfp4_linear)
-// The bf16 value each kernel quantises is exactly the value the unfused op would
-// have returned (same rounding order), so fused and unfused paths agree bit for bit.
+// The bf16 value each kernel quantises is exactly the value the unfused op would have returned
+// (same rounding order).  The gated-activation and plain producers quantise it exactly as
+// ada_nvfp4_act_quant does; the RMSNorm producers scale by a bound on the row amax carried with
+// the sum of squares (one cluster exchange instead of two), with the same codes for that scale.
 //
 // Decode rows are short (16 tokens x 4096..21504 values), so each row is spread over
 // a thread-block cluster of up to 8 CTAs (cluster.cuh): grid (ctas, rows), every CTA
@@ -26,6 +28,9 @@ template <typename T>
 __device__ __forceinline__ float round_to(float v) {
   return to_f32(from_f32<T>(v));
 }
+
+// 1 + 2^-6: the margin of the RMSNorm producers' bound on the normalised row's amax.
+constexpr float AMAX_BOUND_MARGIN = 1.015625f;
 
 // Octet `u` of this thread (u < MAXU) in the CTA's slice [o0, o1), or -1.
 __device__ __forceinline__ int my_oct(int u, int o0, int o1) {
@@ -75,9 +80,15 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
                                                             const T* __restrict__ w, const T* __restrict__ wpre, T* y,
                                                             int64_t ldy, int rows, int hidden, float eps, int gemma,
                                                             q::QuantDst dst, PartIn pin, PeerWait pw) {
-  __shared__ float red[cl::MAX_WARPS];
-  __shared__ cl::Exchange xch[3];
-  cl::cluster_start(xch, wpre ? 3 : 2);
+  __shared__ float red[2 * cl::MAX_WARPS];
+  __shared__ cl::Exchange xpre;    // the Gemma post-norm's sum of squares
+  __shared__ cl::Exchange2 xmain;  // the sum of squares and max |x * w| together
+  if (threadIdx.x == 0) {
+    cl::exchange2_init(&xmain);
+    if (wpre) cl::exchange_init(&xpre);
+    cl::fence_exchange_init();
+  }
+  cl::cluster_arrive_relaxed();
   const int m = blockIdx.y;
   int o0, o1;
   slice_of(hidden, o0, o1);
@@ -101,7 +112,7 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
   }
   const unsigned int tag = pw.epoch ? peer_tag(pw) : 0u;
   float v[MAXU][8];
-  float ss = 0.f;
+  float ss = 0.f, aw = 0.f;
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
     const int o = my_oct(u, o0, o1);
@@ -124,7 +135,7 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss0 = fmaf(v[u][i], v[u][i], ss0);
     cl::cluster_wait();
-    const float rs0 = rsqrtf(cl::cluster_allreduce_x<cl::OpSum>(ss0, red, &xch[2]) / (float)hidden + eps);
+    const float rs0 = rsqrtf(cl::cluster_allreduce_x<cl::OpSum>(ss0, red, &xpre) / (float)hidden + eps);
 #pragma unroll
     for (int u = 0; u < MAXU; ++u)
       if (my_oct(u, o0, o1) >= 0)
@@ -147,12 +158,19 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
         store8<T>(res_out + (int64_t)m * ldro + o * 8, v[u]);
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss = fmaf(v[u][i], v[u][i], ss);
+      for (int i = 0; i < 8; ++i) {
+        ss = fmaf(v[u][i], v[u][i], ss);
+        aw = fmaxf(aw, fabsf(__fmul_rn(v[u][i], gemma ? __fadd_rn(1.f, wf[u][i]) : wf[u][i])));
+      }
     }
   }
   if (!wpre) cl::cluster_wait();  // all CTAs of the cluster run: their shared memory may be written
-  const float rs = rsqrtf(cl::cluster_allreduce_x<cl::OpSum>(ss, red, &xch[0]) / (float)hidden + eps);
-  float amax = 0.f;
+  // One exchange for both row reductions.  The quantiser's row scale comes from the bound
+  // rs * max|x * w| * (1 + 2^-6) on the normalised row's amax instead of its exact value: the
+  // normalised element is x * rs * w rounded to bf16 at most twice (a factor <= (1 + 2^-8)^2 over
+  // the exact product), so the bound is never below it, and the terms never saturate.
+  const float2 red2 = cl::cluster_allreduce2_x<cl::OpSum, cl::OpMax>(ss, aw, red, &xmain);
+  const float rs = rsqrtf(red2.x / (float)hidden + eps);
 #pragma unroll
   for (int u = 0; u < MAXU; ++u) {
     const int o = my_oct(u, o0, o1);
@@ -162,13 +180,12 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
         const float xn = __fmul_rn(v[u][i], rs);
         v[u][i] = gemma ? round_to<T>(__fmul_rn(xn, __fadd_rn(1.f, wf[u][i])))
                         : round_to<T>(__fmul_rn(round_to<T>(xn), wf[u][i]));
-        amax = fmaxf(amax, fabsf(v[u][i]));
       }
       if (y) store8<T>(y + (int64_t)m * ldy + o * 8, v[u]);
     }
   }
   if (!quant) return;
-  quant_slice<MAXU>(dst, m, v, o0, o1, cl::cluster_allreduce_x<cl::OpMax>(amax, red, &xch[1]));
+  quant_slice<MAXU>(dst, m, v, o0, o1, __fmul_rn(__fmul_rn(rs, red2.y), AMAX_BOUND_MARGIN));
 }
 
 // SiLU with the hardware exponential (within 2 ulp of fp32 before the bf16 rounding).

@@ -183,7 +183,11 @@ ADA_API int ada_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_
 /* RMSNorm fused with the NVFP4 activation quantiser: the normalised row (exactly what
  * ada_rmsnorm returns) is written as the GEMM operand in the ada_nvfp4_act_quant layout
  * (xq / sfx / gx for `terms` and block_n; rows up to ceil(rows/block_n)*block_n, padding
- * rows zero).  y may be NULL (no bf16 copy).  hidden must be a multiple of 256. */
+ * rows zero).  y may be NULL (no bf16 copy).  hidden must be a multiple of 256.  The row scale
+ * comes from a bound on the normalised row's amax taken with its sum of squares (one cluster
+ * exchange): amax_bound = rsqrt(mean(x^2) + eps) * max|x * w'| * (1 + 2^-6) (w' = w, or 1 + w
+ * for gemma), never below the exact amax and at most ~2.4% above it; given that scale the codes
+ * are exactly ada_nvfp4_act_quant's.  The same holds for every RMSNorm+quant producer below. */
 ADA_API int ada_rmsnorm_quant(const void* x, int64_t ldx, const void* residual, int64_t ld_res,
                               void* residual_out, int64_t ld_res_out, const void* weight, void* y,
                               int64_t ldy, int64_t rows, int32_t hidden, float eps, int gemma, int dtype,

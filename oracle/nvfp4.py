@@ -236,9 +236,12 @@ MIN_AMAX = np.float32(2.0 ** -64)
 MAX_TERMS = 8
 
 
-def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16):
+def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16, row_scale: np.ndarray | None = None):
     """Bit-exact specification of adallm_b200's activation quantiser (csrc/quant.cuh).
 
+    row_scale: the rows' g (terms == 1) or g_0 (terms >= 2) as a producer chose them, used as
+    given instead of being derived from the exact amax (the RMSNorm producers derive it from a
+    bound on the amax, which is never below it).
     x: [M, K] (bf16 values given as fp32).  Per row, with amax = max|x| (a row whose amax
     is below 2^-64 quantises to zero with scale 1.0):
       terms == 1 (NVFP4, block scales): g = amax / 2688; per 16-block
@@ -258,6 +261,8 @@ def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16):
     live = amax >= MIN_AMAX
     if terms == 1:
         g = np.where(live, (amax / np.float32(GLOBAL_DIV)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+        if row_scale is not None:
+            g = np.asarray(row_scale, np.float32).reshape(m).copy()
         g6 = (g * np.float32(6.0)).astype(np.float32)
         r = x.reshape(m, groups, group_size)
         bamax = np.max(np.abs(r), axis=-1).astype(np.float32)
@@ -270,6 +275,8 @@ def quantize_act_terms(x: np.ndarray, terms: int, group_size: int = 16):
         c = np.where((sv > 0)[..., None], c, np.uint8(0))
         return c.reshape(1, m, k), sb, g
     g0 = np.where(live, (amax / np.float32(6.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+    if row_scale is not None:
+        g0 = np.asarray(row_scale, np.float32).reshape(m).copy()
     g = g0.copy()
     r = x.copy()
     codes = np.zeros((terms, m, k), np.uint8)

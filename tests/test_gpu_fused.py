@@ -36,6 +36,33 @@ def same(a, b):
         assert torch.equal(u, v)
 
 
+def same_with_bound(got, y_ref, terms, bn):
+    """The RMSNorm producers' quantised operand: the row scale comes from a bound on the
+    normalised row's amax (rs * max|x w| * (1 + 2^-6)), never below amax / 6 (amax / 2688 for
+    one term) and at most ~2.4% above it (the margin over the two bf16 roundings); given that scale, the codes (and block scales) are
+    exactly the quantiser's (oracle.nvfp4.quantize_act_terms with the scale as given)."""
+    from oracle import nvfp4 as nv
+    from tests.test_gpu_nvfp4 import unpack_sf, unpack_xq
+    rows, k = y_ref.shape
+    m_tiles = -(-rows // bn)
+    yf = y_ref.float().cpu().numpy()
+    amax = np.abs(yf).max(axis=1)
+    div = 2688.0 if terms == 1 else 6.0
+    gx = got[2].cpu().numpy()[:rows]
+    min_amax = np.float32(2.0 ** -64)  # rows whose (bound on the) amax is below it quantise to zero, scale 1
+    live = amax >= min_amax
+    dead = amax * 1.025 < min_amax
+    assert np.all(gx[live] >= amax[live] / div * (1 - 2.0 ** -20))
+    assert np.all(gx[live] <= amax[live] / div * 1.025)
+    assert np.all(gx[dead] == 1.0)
+    codes, sbits, _ = nv.quantize_act_terms(yf, terms, row_scale=gx)
+    got_codes = unpack_xq(got[0].cpu().numpy(), terms, m_tiles, bn, k)
+    norm = lambda c: np.where((c & 7) == 0, 0, c)  # +0 / -0 codes decode identically
+    np.testing.assert_array_equal(norm(got_codes[:, :rows]), norm(codes))
+    if terms == 1:
+        np.testing.assert_array_equal(unpack_sf(got[1].cpu().numpy(), m_tiles, bn, k)[:rows], sbits)
+
+
 @pytest.mark.parametrize("hidden,gemma,with_res", [(4096, False, True), (4096, False, False), (5376, True, True),
                                                    (512, False, True)])
 @pytest.mark.parametrize("rows,terms,bn", [(16, 4, 16), (5, 1, 16), (40, 2, 64), (16, 8, 16)])
@@ -50,7 +77,6 @@ def test_rmsnorm_quant_matches_unfused(hidden, gemma, with_res, rows, terms, bn)
         y_ref, r_ref = rms_norm(x, w, 1e-6, r.clone(), gemma=gemma)
     else:
         y_ref = rms_norm(x, w, 1e-6, gemma=gemma)
-    ref = act_quant(y_ref, terms, bn)
     got = qbufs(rows, hidden, terms, bn, d)
     y = torch.empty_like(x)
     r2 = r.clone()
@@ -62,15 +88,15 @@ def test_rmsnorm_quant_matches_unfused(hidden, gemma, with_res, rows, terms, bn)
     assert torch.equal(y, y_ref)
     if with_res:
         assert torch.equal(r2, r_ref)
-    same(got, ref)
+    same_with_bound(got, y_ref, terms, bn)
 
 
 @pytest.mark.parametrize("gemma", [False, True])
 def test_rmsnorm_quant_amax_edge_rows(gemma):
-    """The normalised row amax travels with the sum of squares as candidates; rows where that
-    cannot work take the second exchange.  Both give exactly the unfused amax: a constant row
-    (every element a candidate), ties of the maximum across CTAs, an all-zero row, rows near the
-    bottom and the top of the range, one huge outlier, and ordinary rows."""
+    """The bound on the normalised row amax travels with the sum of squares (one exchange): a
+    constant row, ties of the maximum across CTAs, an all-zero row, rows near the bottom and the
+    top of the range, one huge outlier, zero norm weights, and ordinary rows all get a row scale
+    within the bound's margin and exactly the quantiser's codes for it."""
     d = dev()
     H, rows, terms, bn = 4096, 16, 4, 16
     g = torch.Generator(device="cpu").manual_seed(21)
@@ -88,7 +114,6 @@ def test_rmsnorm_quant_amax_edge_rows(gemma):
     w = w.to(d)
     s = torch.cuda.current_stream().cuda_stream
     y_ref = rms_norm(x, w, 1e-6, gemma=gemma)
-    ref = act_quant(y_ref, terms, bn)
     got = qbufs(rows, H, terms, bn, d)
     y = torch.empty_like(x)
     N.check(N.lib().ada_rmsnorm_quant(x.data_ptr(), H, None, H, None, H, w.data_ptr(), y.data_ptr(), H, rows, H,
@@ -96,7 +121,7 @@ def test_rmsnorm_quant_amax_edge_rows(gemma):
                                       got[2].data_ptr(), s), "rmsnorm_quant")
     torch.cuda.synchronize()
     assert torch.equal(y, y_ref)
-    same(got, ref)
+    same_with_bound(got, y_ref, terms, bn)
 
 
 @pytest.mark.parametrize("inter,act,terms", [(12288, 0, 4), (1536, 0, 1), (3072, 1, 4), (21504, 1, 6)])
@@ -146,6 +171,8 @@ def test_paged_decode_quant_matches_unfused(batch, hq, hkv, terms, ctx_hi, flags
 
 
 def test_fused_engine_matches_unfused():
+    """The fused engine (quantisers inside the producers) against the unfused one (plain op, then
+    ada_nvfp4_act_quant) on the same weights and tokens."""
     from tests.decode_check import small_config
     from adallm_b200.decode_step import Qwen3DecodeEngine, DecodeSession
     d = dev()
@@ -153,17 +180,23 @@ def test_fused_engine_matches_unfused():
     for fused in (True, False):
         eng = Qwen3DecodeEngine(small_config(3), d, 4, max_ctx=32, seed=7, fused=fused)
         sess = DecodeSession(eng, seed=7)
-        toks = torch.tensor([1, 2, 3, 4])
         outs = []
-        for _ in range(5):
-            sess.prepare(toks)
+        for step in range(5):  # teacher-forced: both engines see the same tokens every step
+            sess.prepare(torch.tensor([(7 * step + 3 * i + 1) % 1000 for i in range(4)]))
             sess.upload()
             eng.forward()
-            toks = sess.download()
+            sess.download()
             sess.commit()
             outs.append(eng.logits.clone())
         logits.append(torch.stack(outs))
-    assert torch.equal(logits[0], logits[1])
+    # the fused RMSNorm producers take their row scale from a bound on the amax (<= 2.4% above
+    # it), the unfused path from the exact amax: the operands differ at the quantiser's noise,
+    # which the e4m3 KV cache amplifies to the level the engine shows against the exact oracle
+    # (~0.03 logits rel-L2 in the agreement tests)
+    a, b = logits[0].float(), logits[1].float()
+    rel = [float((a[i] - b[i]).norm() / b[i].norm()) for i in range(a.shape[0])]
+    print("fused vs unfused logits rel-L2 per step", rel)
+    assert max(rel) < 5e-2 and sum(rel) / len(rel) < 3e-2, rel
 
 
 def test_pdl_toggle_gives_identical_results():

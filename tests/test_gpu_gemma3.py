@@ -17,7 +17,7 @@ import torch
 from adallm_b200 import _native as N
 from adallm_b200.layernorm import rms_norm
 from tests.gpu_util import dev
-from tests.test_gpu_fused import act_quant, qbufs, same
+from tests.test_gpu_fused import qbufs, same_with_bound
 
 pytestmark = pytest.mark.gpu
 
@@ -52,7 +52,7 @@ def test_gemma_norm2_matches_composition(rows, hidden, terms, quant):
     assert torch.equal(r2, r_ref)
     assert torch.equal(y, y_ref)
     if quant:
-        same(got, act_quant(y_ref, terms, 16))
+        same_with_bound(got, y_ref, terms, 16)
 
 
 def test_qk_norm_gemma_planes_and_oracle():
