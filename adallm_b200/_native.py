@@ -38,6 +38,7 @@ _SIGS = {
     "ada_status_string": (C.c_char_p, [INT]),
     "ada_abi_version": (INT, []),
     "ada_set_pdl": (INT, [INT]),
+    "ada_set_pair_gemm": (INT, [INT]),
     "ada_fp8_paged_decode_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "ada_fp8_paged_decode": (INT, [P, INT, I64, I64, P, P, I64, I64, I64, I64, P, I64, I32, P, I32, I32, I32, I32, I32,
                                    F32, F32, F32, I32, P, INT, P, SZ, P]),
@@ -132,6 +133,8 @@ def lib():
             fn.argtypes = args
         if os.environ.get("ADALLM_B200_PDL", "1") == "0":
             h.ada_set_pdl(0)
+        if os.environ.get("ADALLM_B200_PAIR_GEMM", "1") == "0":
+            h.ada_set_pair_gemm(0)
         _lib = h
     return _lib
 

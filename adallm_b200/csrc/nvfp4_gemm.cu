@@ -580,6 +580,220 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc(tmem, p.tmem_cols);
 }
 
+// ---- CTA-pair persistent GEMM (W4A4 at prefill sizes) ------------------------------------
+// Operand reuse per staged byte decides the prefill-size GEMM: with 128 x 128 tiles every K
+// step moves 256 operand rows from L2 into shared memory per 128 x 128 outputs, which bounds the
+// one-CTA kernel above by the L2 -> SM copy rate long before the tensor pipe.  Here two CTAs of a
+// cluster (one per SM) share one tcgen05.mma.cta_group::2 of M 256 x N 256 x K 64: the
+// activations are the A operand (256 token rows, 128 in each CTA), the weights the B operand
+// (256 weight rows, 128 in each CTA), and each CTA's TMEM holds its 128 token rows x 256 weight
+// rows in fp32.  Per CTA and K step that is 256 staged rows for 128 x 256 outputs: half the
+// traffic per FLOP.  Not swapped (tokens are the MMA M): a TMEM lane is a token row, so the
+// epilogue writes each row's 256 outputs as contiguous 16-byte vectors.
+//
+// Scale factors: the A scales (each CTA's 128 tokens) sit in its own TMEM, 4 columns per 64-wide K
+// block; the B scales cover all 256 weight rows in both CTAs (8 columns per K block: rows 0-127,
+// then 128-255), copied from each CTA's own shared memory by one cta_group::2 tcgen05.cp.
+//
+// Protocol (CTA rank 0 of the pair leads; no multicast anywhere):
+//   full[s]  (rank 0): both CTAs' TMA loads of stage s complete_tx here (cta_group::2 loads);
+//                      rank 0's producer arms it with both CTAs' bytes.
+//   empty[s] (each):   the leader's MMA thread commits to both CTAs' copies after stage s is read.
+//   accf     (each):   accumulator complete, committed to both CTAs after a tile's last MMA.
+//   acce     (rank 0): the 8 epilogue warps of both CTAs arrive once their TMEM loads are done
+//                      (16 arrivals): one accumulator, drained into registers before the stores.
+// Every wait is bounded (2 s); a timeout sets an error bit and the CTA drains and exits.
+namespace pair {
+constexpr int BT = 256;                     // tokens per tile (MMA M, 128 per CTA)
+constexpr int BW = 256;                     // weight rows per tile (MMA N, 128 per CTA)
+constexpr uint32_t A_BYTES = 128 * KT_BYTES;   // this CTA's 128 token rows x 256 K (16 KiB)
+constexpr uint32_t B_BYTES = 128 * KT_BYTES;   // this CTA's 128 weight rows (16 KiB)
+constexpr uint32_t SFA_BYTES = 4 * SF_BLOCK;   // this CTA's tokens, 4 K blocks (2 KiB)
+constexpr uint32_t SFB_BYTES = 8 * SF_BLOCK;   // all 256 weight rows, 4 K blocks (4 KiB)
+constexpr uint32_t STAGE = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // 38 KiB, multiple of 1024
+constexpr int STAGES = 5;
+constexpr uint32_t SF_COLS = 16 + 32;       // TMEM scale columns per stage (A 4 x 4, B 4 x 8)
+constexpr uint32_t ACC_COLS = BW;
+constexpr uint32_t TMEM_COLS = 512;         // 256 accumulator + 5 x 48 scale columns, power of 2
+constexpr int EPI_WARPS = 8;                // two per TMEM lane quarter, 128 columns each
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + 1024;
+static_assert(ACC_COLS + STAGES * SF_COLS <= TMEM_COLS, "TMEM budget");
+static_assert(STAGE % 1024 == 0, "stage alignment");
+}  // namespace pair
+
+__global__ void __launch_bounds__(pair::THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                     const __grid_constant__ CUtensorMap tsw, const __grid_constant__ CUtensorMap tsx,
+                     const GemmParams p) {
+  using namespace pair;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ctrl = smem + (size_t)STAGES * STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_v = abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cl::ctarank() & 1u, peer = rank ^ 1u;
+  const int w_pairs = p.N / BW;
+  const int t_tiles = (p.M + BT - 1) / BT;
+  const int tiles = w_pairs * t_tiles;
+  const int pair_id = (int)(blockIdx.x >> 1), pairs = (int)(gridDim.x >> 1);
+  const int kb64 = p.K / 64;
+  const int nkt = p.nkt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    mbar_init(acce, 2 * EPI_WARPS);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmw);
+    prefetch_tmap(&tmx);
+    prefetch_tmap(&tsw);
+    prefetch_tmap(&tsx);
+  }
+  tc_fence_before();
+  cl::cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any pair traffic
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- producer (both CTAs) ----------------
+      pdl_wait();
+      const uint32_t full0 = cl::mapa(&full[0], 0);  // the leader's stage barriers
+      uint32_t it = 0;
+      for (int t = pair_id; t < tiles && !*abort_v; t += pairs) {
+        const int wp = t % w_pairs, tt = t / w_pairs;
+        const int x_row = tt * BT + (int)rank * 128;       // this CTA's token rows (A)
+        const int w_row = wp * BW + (int)rank * 128;       // this CTA's weight rows (B)
+        const int x_blk = tt * 2 + (int)rank;              // 128-token scale block
+        for (int kt = 0; kt < nkt; ++kt, ++it) {
+          const int s = (int)(it % (uint32_t)STAGES);
+          if (it >= (uint32_t)STAGES &&
+              !mbar_wait_bounded(&empty[s], ((it / STAGES) & 1) ^ 1, abort_v, p.err, 1u))
+            break;
+          uint8_t* st = smem + (size_t)s * STAGE;
+          const uint32_t bar = full0 + (uint32_t)s * 8u;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE);
+          tma_load_2d_pair(st, &tmx, bar, kt * KT_BYTES, x_row);
+          tma_load_2d_pair(st + A_BYTES, &tmw, bar, kt * KT_BYTES, w_row);
+          // scale maps: rows of 128 bytes; a (block, stage) chunk is 2 KiB = 16 rows
+          tma_load_2d_pair(st + A_BYTES + B_BYTES, &tsx, bar, 0, (x_blk * kb64 + kt * 4) * 4);
+          tma_load_2d_pair(st + A_BYTES + B_BYTES + SFA_BYTES, &tsw, bar, 0, ((wp * 2) * kb64 + kt * 4) * 4);
+          tma_load_2d_pair(st + A_BYTES + B_BYTES + SFA_BYTES + 4 * SF_BLOCK, &tsw, bar, 0,
+                           ((wp * 2 + 1) * kb64 + kt * 4) * 4);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {  // ---------------- MMA issuer (leader CTA only) ----------------
+      constexpr uint32_t idesc = idesc_mxf4nvf4_m256(BW);
+      const uint32_t empty0_own = cl::mapa(&empty[0], 0), empty0_peer = cl::mapa(&empty[0], peer);
+      const uint32_t accf_own = cl::mapa(accf, 0), accf_peer = cl::mapa(accf, peer);
+      uint32_t it = 0, lt = 0;
+      for (int t = pair_id; t < tiles && !*abort_v; t += pairs, ++lt) {
+        if (lt > 0 && !mbar_wait_bounded_cluster(acce, (lt - 1) & 1, abort_v, p.err, 8u)) break;
+        tc_fence_after();
+        bool failed = false;
+        for (int kt = 0; kt < nkt; ++kt, ++it) {
+          const int s = (int)(it % (uint32_t)STAGES);
+          if (!mbar_wait_bounded(&full[s], (it / STAGES) & 1, abort_v, p.err, 2u)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + (size_t)s * STAGE);
+          const uint32_t b_addr = a_addr + A_BYTES;
+          const uint32_t sfa_addr = b_addr + B_BYTES;
+          const uint32_t sfb_addr = sfa_addr + SFA_BYTES;
+          const uint32_t sf_col = tmem + ACC_COLS + (uint32_t)s * SF_COLS;
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            tmem_cp_32x128b_x4_pair(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
+            tmem_cp_32x128b_x4_pair(sf_col + 16 + 8 * kb, desc_sf(sfb_addr + kb * SF_BLOCK));
+            tmem_cp_32x128b_x4_pair(sf_col + 16 + 8 * kb + 4, desc_sf(sfb_addr + 4 * SF_BLOCK + kb * SF_BLOCK));
+          }
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb)
+            mma_mxf4nvf4_pair(tmem, desc_kmajor_sw128(a_addr + kb * 32), desc_kmajor_sw128(b_addr + kb * 32), idesc,
+                              (kt | kb) != 0, sf_col + 4 * kb, sf_col + 16 + 8 * kb);
+          tc_commit_pair(empty0_own + (uint32_t)s * 8u);
+          tc_commit_pair(empty0_peer + (uint32_t)s * 8u);
+        }
+        tc_commit_pair(accf_own);  // also after a failure: drains the issued MMAs
+        tc_commit_pair(accf_peer);
+        if (failed) break;
+      }
+    }
+    __syncwarp();
+  } else {  // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    pdl_wait();
+    pdl_trigger();
+    const int q = warp & 3;                 // TMEM lane quarter this warp may read
+    const int h = (warp - 2) >> 2;          // column half: weight rows h*128 .. +127 of the tile
+    const uint32_t acce_lead = cl::mapa(acce, 0);
+    const float gw = __ldg(p.gw);
+    const bool bf16 = p.out_dtype == ADA_DT_BF16;
+    uint32_t lt = 0;
+    for (int t = pair_id; t < tiles; t += pairs, ++lt) {
+      const int wp = t % w_pairs, tt = t / w_pairs;
+      const int m = tt * BT + (int)rank * 128 + q * 32 + lane;
+      const float g = m < p.M ? p.gx[m] : 0.f;  // read before the wait, off the drain path
+      const bool ok = mbar_wait_bounded(accf, lt & 1, abort_v, p.err, 4u) && !*abort_v;
+      tc_fence_after();
+      __syncwarp();
+      uint32_t v[128];
+      const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)h * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) tmem_ld16_nowait(lane_addr + 16 * c, v + 16 * c);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_lead);  // the accumulator is free for the next tile
+      if (!ok) break;
+      if (m < p.M) {
+        const float gsc = __fmul_rn(gw, g);
+        const int n0 = wp * BW + h * 128;
+        const uint4* bias8 = p.bias ? reinterpret_cast<const uint4*>(p.bias) + n0 / 8 : nullptr;
+        uint4* yrow = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.y) + (int64_t)m * p.ldy + n0);
+#pragma unroll
+        for (int gi = 0; gi < 16; ++gi) {
+          float b[8];
+          if (bias8) {
+            const uint4 u = __ldg(bias8 + gi);
+            if (bf16) unpack8<__nv_bfloat16>(u, b); else unpack8<__half>(u, b);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) b[k] = 0.f;
+          }
+          float o[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = fmaf(__uint_as_float(v[gi * 8 + k]), gsc, 0.f) + b[k];
+          yrow[gi] = bf16 ? pack8<__nv_bfloat16>(o) : pack8<__half>(o);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cl::cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals may still reach it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
+}
+
 // Scale prepack: [N, K/16] (fp16 holding e4m3 values, or raw e4m3 bytes) ->
 // [N/128][K/64][512] bytes in the MMA scale-factor layout.
 __global__ void __launch_bounds__(128) prepack_kernel(const void* __restrict__ scale, int is_fp16, int64_t ld, int N,
@@ -876,9 +1090,81 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
   return ADA_OK;
 }
 
+// ---- CTA-pair launch ------------------------------------------------------------------
+static bool g_pair_gemm = true;  // ada_set_pair_gemm
+
+static inline bool a16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Scale-factor bytes as rows of 128 bytes (a 2 KiB chunk = one box of 16 rows), no swizzle.
+static bool make_sf_map(CUtensorMap* map, const void* base, uint64_t bytes) {
+  if (!a16(base) || bytes % 2048) return false;
+  const cuuint64_t dims[2] = {128, bytes / 128};
+  const cuuint64_t strides[1] = {128};
+  const cuuint32_t box[2] = {128, 16};
+  return encode_bytes(map, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Pairs of CTAs that are resident at once (one CTA per SM; 0 if the query fails).
+static int pair_capacity() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cache[dev]) return cache[dev] > 0 ? cache[dev] : 0;
+  int n = 0;
+  if (cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pair::SMEM) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(pair::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = pair::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  (void)cudaGetLastError();
+  cache[dev] = n > 0 ? n : -1;
+  return n;
+}
+
+// The pair kernel covers the dense W4A4 GEMM with 256-row weight tiles and 16-byte output rows;
+// everything else (row-scaled terms, grouped, tensor-parallel, partial planes) stays on the
+// one-CTA kernels.
+static bool pair_eligible(const GemmParams& gp) {
+  return g_pair_gemm && !gp.part && !gp.tile_expert && !gp.row_map && gp.world <= 1 && gp.sfx && gp.N % pair::BW == 0 &&
+         gp.ldy % 8 == 0 && a16(gp.y) && (!gp.bias || a16(gp.bias)) && gp.nkt >= 1;
+}
+
+// Launches the pair kernel; returns ADA_ERR_UNSUPPORTED (nothing launched) when its maps or
+// residency cannot be had, so the caller falls back to the one-CTA persistent kernel.
+static int launch_pair(const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmParams& gp, const Plan& P,
+                       cudaStream_t st) {
+  CUtensorMap tsw, tsx;
+  if (!make_sf_map(&tsw, gp.sfw, (uint64_t)gp.N * (uint64_t)gp.K / 16)) return ADA_ERR_UNSUPPORTED;
+  if (!make_sf_map(&tsx, gp.sfx, (uint64_t)P.m_tiles * (uint64_t)(gp.K / 64) * 512)) return ADA_ERR_UNSUPPORTED;
+  const int cap = pair_capacity();
+  if (cap < 1) return ADA_ERR_UNSUPPORTED;
+  const int64_t tiles = (int64_t)(gp.N / pair::BW) * cdiv(gp.M, pair::BT);
+  const int64_t pairs = tiles < cap ? tiles : cap;
+  (void)ada::launch_kc(gemm_pair_kernel, dim3((unsigned)(2 * pairs)), dim3(pair::THREADS), pair::SMEM, st, 2, tmw,
+                       tmx, tsw, tsx, gp);
+  ADA_CHECK_LAUNCH();
+  return ADA_OK;
+}
+
 template <int BN, int T>
 static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmParams& gp, const Plan& P,
                        cudaStream_t st) {
+  if constexpr (BN == 128 && T == 1) {
+    if (P.persistent && pair_eligible(gp)) {
+      const int rc = launch_pair(tmw, tmx, gp, P, st);
+      if (rc != ADA_ERR_UNSUPPORTED) return rc;
+    }
+  }
   if (P.persistent && !gp.part) {  // prefill-size dense GEMM, or the grouped MoE GEMM
     static size_t configured[64] = {0};
     int dev = 0;
@@ -1065,6 +1351,12 @@ int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy, int64
 }  // namespace ada
 
 using namespace ada;
+
+extern "C" int ada_set_pair_gemm(int enable) {
+  const int prev = fp4::g_pair_gemm ? 1 : 0;
+  fp4::g_pair_gemm = enable != 0;
+  return prev;
+}
 
 extern "C" size_t ada_nvfp4_sf_bytes(int64_t n, int64_t k) {
   if (n <= 0 || k <= 0 || k % 64) return 0;

@@ -56,6 +56,13 @@ ADA_API int ada_abi_version(void);
  * anything that kernel wrote.  ada_set_pdl(0) launches kernels with plain stream ordering.
  * Returns the previous setting.  Process-wide; set it before capturing graphs. */
 ADA_API int ada_set_pdl(int enable);
+/* CTA-pair GEMM (on by default): dense W4A4 (terms == 1) NVFP4 GEMMs large enough for the
+ * persistent kernel, with N a multiple of 256, a 16-byte aligned output (ldy a multiple of 8)
+ * and bias, run on pairs of SMs sharing one tcgen05 MMA of 256 tokens x 256 weight rows (the
+ * prefill-size path of nvfp4_linear, adallm/ops/nvfp4_gemm.py:460-564).  ada_set_pair_gemm(0)
+ * keeps them on the one-CTA 128 x 128 persistent kernel; results are the same either way.
+ * Returns the previous setting.  Process-wide. */
+ADA_API int ada_set_pair_gemm(int enable);
 
 /* ------------------------------------------------------------------------
  * FP8 paged split-K decode attention

@@ -138,6 +138,36 @@ def test_prefill_size(terms, tol):
     assert rel_l2(y.float(), ref) < tol
 
 
+@pytest.mark.parametrize("m,n,with_bias,dtype", [(2048, 6144, False, torch.bfloat16), (1100, 6144, True, torch.float16),
+                                                  (4096, 4096, True, torch.bfloat16)])
+def test_pair_gemm_matches_one_cta_kernel(m, n, with_bias, dtype):
+    """W4A4 prefill-size GEMM on SM pairs (tcgen05.mma.cta_group::2, 256 tokens x 256 weight rows
+    a tile) against the one-CTA 128 x 128 persistent kernel (ada_set_pair_gemm(0)): the same
+    block-scaled products accumulated over the same K order, so the outputs are identical.  M 1100
+    leaves the second half of the last 256-token tile beyond the operand (zero-filled by the
+    loads, never stored).  Both against dequantise-then-matmul as in test_prefill_size."""
+    d = dev()
+    k = 4096
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=21, realistic=False)
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn((m, k), generator=g).to(dtype).to(d)
+    bias = (torch.randn((n,), generator=g) * 0.1).to(dtype).to(d) if with_bias else None
+    args = (torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d), torch.tensor(s2, device=d), None, bias, 16)
+    lib = N.lib()
+    y_pair = nvfp4_linear(x, *args, terms=1)
+    prev = lib.ada_set_pair_gemm(0)
+    try:
+        y_one = nvfp4_linear(x, *args, terms=1)
+    finally:
+        lib.ada_set_pair_gemm(prev)
+    torch.cuda.synchronize()
+    mismatch = (y_pair != y_one).float().mean().item()
+    assert mismatch == 0.0, f"pair vs one-CTA: {mismatch:.2e} of outputs differ, rel-L2 {rel_l2(y_pair, y_one):.2e}"
+    w = nv.dequant_nvfp4_torch(packed, scale16.astype(np.float32), s2).to(d)
+    ref = x.float() @ w.float().t() + (bias.float() if bias is not None else 0.0)
+    assert rel_l2(y_pair.float(), ref) < 0.15
+
+
 @pytest.mark.parametrize("realistic", [True, False])
 def test_config0_full_size(realistic):
     # BASELINE config 0: x bf16 [16, 4096] ~N(0,1), W [12288, 4096] NVFP4, output bf16 [16, 12288];
