@@ -13,6 +13,12 @@ since the reference reads NVFP4_FP8 when its module is imported (nvfp4_gemm.py:2
            its kernel walks pages in 64-token steps, so smaller pages are outside its contract)
            against oracle.attention.paged_decode_fp16_kernel and the fp64 paged_decode.
 
+  prefill  the prefix-cache prefill branch of Attention.forward (attention.py:335-358: its
+           _gather_kv_from_blocks of the e4m3 pages to fp16, then flash_attn_varlen_func with
+           causal=True and window (W, 0)) against oracle.attention.paged_prefill -- the
+           restatement of flash-attn's bottom-right causal mask and window -- and against this
+           package's paged prefill kernel, on ragged cached/new lengths with and without a window.
+
 One JSON line ("REFTRITON {...}").  Test infrastructure only (tests/test_gpu_reference_triton.py)."""
 from __future__ import annotations
 
@@ -96,11 +102,59 @@ def attn() -> dict:
             "emulation_vs_exact": rel_l2(emul, exact), "page": 256}
 
 
+def prefill() -> dict:
+    _path()
+    os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
+    import numpy as np
+    import torch
+    import adallm.infra.context as rc
+    import adallm.ops.attention as ra
+    from oracle import attention as oa
+    from oracle.nvfp4 import rel_l2
+    from adallm_b200.attention import paged_prefill
+    d = torch.device("cuda", 0)
+    cases = [  # cached, new, hq, hkv, page, window
+        ([0, 37, 300, 5], [50, 1, 129, 3], 32, 8, 16, 0),
+        ([0, 37, 300, 5], [50, 1, 129, 3], 32, 8, 16, 40),
+        ([100, 0], [77, 200], 32, 4, 64, 0),
+        ([3, 250], [130, 60], 4, 4, 16, 17),
+    ]
+    res = []
+    for i, (cached, new, hq, hkv, page, window) in enumerate(cases):
+        c = oa.make_prefill_case(100 + i, cached, new, hq, hkv, 128, page, extra_pages=3)
+        m = ra.Attention(hq, 128, float(c["scale"]), hkv, sliding_window=window or None)
+        m.k_cache = torch.from_numpy(c["k"]).to(d).view(torch.float8_e4m3fn)
+        m.v_cache = torch.from_numpy(c["v"]).to(d).view(torch.float8_e4m3fn)
+        q = torch.from_numpy(c["q"]).to(torch.bfloat16).to(d)
+        tq = q.shape[0]
+        len_k = np.diff(c["cu_k"])
+        rc.set_context(True, cu_seqlens_q=torch.from_numpy(c["cu_q"]).to(d),
+                       cu_seqlens_k=torch.from_numpy(c["cu_k"]).to(d), max_seqlen_q=int(c["max_seqlen_q"]),
+                       max_seqlen_k=int(len_k.max()), slot_mapping=torch.full((tq,), -1, dtype=torch.int32, device=d),
+                       block_tables=torch.from_numpy(c["block_tables"]).to(d))
+        kv = torch.zeros((tq, hkv, 128), dtype=torch.bfloat16, device=d)
+        ref_out = m.forward(q, kv, kv)  # slot -1: nothing stored, the cache is read as built
+        torch.cuda.synchronize()
+        rc.reset_context()
+        ref_out = ref_out.float().cpu().numpy().reshape(tq, hq, 128)
+        oracle = oa.paged_prefill(c["q"], c["k"], c["v"], c["block_tables"], c["cu_q"], c["cu_k"], c["scale"],
+                                  window)
+        ours = paged_prefill(q, m.k_cache, m.v_cache, torch.from_numpy(c["block_tables"]).to(d),
+                             torch.from_numpy(c["cu_q"]).to(d), torch.from_numpy(c["cu_k"]).to(d),
+                             int(c["max_seqlen_q"]), float(c["scale"]), window)
+        torch.cuda.synchronize()
+        ours = ours.float().cpu().numpy().reshape(tq, hq, 128)
+        res.append({"case": i, "window": window, "reference_vs_oracle": rel_l2(ref_out, oracle),
+                    "ours_vs_reference": rel_l2(ours, ref_out), "ours_vs_oracle": rel_l2(ours, oracle)})
+    return {"cases": res, "reference_vs_oracle_max": max(r["reference_vs_oracle"] for r in res),
+            "ours_vs_reference_max": max(r["ours_vs_reference"] for r in res)}
+
+
 def main():
     if not os.path.isdir(os.path.join(REF_DIR, "adallm")):
         print("REFTRITON " + json.dumps({"unavailable": f"reference package not found in {REF_DIR}"}))
         return
-    r = gemm() if sys.argv[1] == "gemm" else attn()
+    r = {"gemm": gemm, "attn": attn, "prefill": prefill}[sys.argv[1]]()
     print("REFTRITON " + json.dumps(r), flush=True)
 
 
