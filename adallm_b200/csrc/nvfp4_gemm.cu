@@ -612,6 +612,7 @@ constexpr uint32_t SFA_BYTES = 4 * SF_BLOCK;   // this CTA's tokens, 4 K blocks 
 constexpr uint32_t SFB_BYTES = 8 * SF_BLOCK;   // all 256 weight rows, 4 K blocks (4 KiB)
 constexpr uint32_t STAGE = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // 38 KiB, multiple of 1024
 constexpr int STAGES = 5;
+constexpr int PRE_COPY = 3;                 // stages whose scale copies precede the accumulator wait
 constexpr uint32_t SF_COLS = 16 + 32;       // TMEM scale columns per stage (A 4 x 4, B 4 x 8)
 constexpr uint32_t ACC_COLS = BW;
 constexpr uint32_t TMEM_COLS = 512;         // 256 accumulator + 5 x 48 scale columns, power of 2
@@ -703,29 +704,48 @@ __global__ void __launch_bounds__(pair::THREADS, 1)
       constexpr uint32_t idesc = idesc_mxf4nvf4_m256(BW);
       const uint32_t empty0_own = cl::mapa(&empty[0], 0), empty0_peer = cl::mapa(&empty[0], peer);
       const uint32_t accf_own = cl::mapa(accf, 0), accf_peer = cl::mapa(accf, peer);
+      // the scale-factor copies of one stage (they touch only that stage's TMEM scale columns)
+      auto copy_scales = [&](int s) {
+        const uint32_t sfa_addr = smem_u32(smem + (size_t)s * STAGE) + A_BYTES + B_BYTES;
+        const uint32_t sfb_addr = sfa_addr + SFA_BYTES;
+        const uint32_t sf_col = tmem + ACC_COLS + (uint32_t)s * SF_COLS;
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          tmem_cp_32x128b_x4_pair(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
+          tmem_cp_32x128b_x4_pair(sf_col + 16 + 8 * kb, desc_sf(sfb_addr + kb * SF_BLOCK));
+          tmem_cp_32x128b_x4_pair(sf_col + 16 + 8 * kb + 4, desc_sf(sfb_addr + 4 * SF_BLOCK + kb * SF_BLOCK));
+        }
+      };
       uint32_t it = 0, lt = 0;
       for (int t = pair_id; t < tiles && !*abort_v; t += pairs, ++lt) {
-        if (lt > 0 && !mbar_wait_bounded_cluster(acce, (lt - 1) & 1, abort_v, p.err, 8u)) break;
-        tc_fence_after();
+        // The first stages' scale copies go in before the accumulator-empty wait: they overlap
+        // the epilogue's drain of the previous tile instead of following it.
+        const int pre = nkt < PRE_COPY ? nkt : PRE_COPY;
         bool failed = false;
-        for (int kt = 0; kt < nkt; ++kt, ++it) {
-          const int s = (int)(it % (uint32_t)STAGES);
-          if (!mbar_wait_bounded(&full[s], (it / STAGES) & 1, abort_v, p.err, 2u)) {
+        for (int j = 0; j < pre; ++j) {
+          const uint32_t ij = it + (uint32_t)j;
+          if (!mbar_wait_bounded(&full[ij % STAGES], (ij / STAGES) & 1, abort_v, p.err, 2u)) {
             failed = true;
             break;
           }
           tc_fence_after();
+          copy_scales((int)(ij % STAGES));
+        }
+        if (!failed && lt > 0 && !mbar_wait_bounded_cluster(acce, (lt - 1) & 1, abort_v, p.err, 8u)) failed = true;
+        tc_fence_after();
+        for (int kt = 0; kt < nkt && !failed; ++kt, ++it) {
+          const int s = (int)(it % (uint32_t)STAGES);
+          if (kt >= pre) {
+            if (!mbar_wait_bounded(&full[s], (it / STAGES) & 1, abort_v, p.err, 2u)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            copy_scales(s);
+          }
           const uint32_t a_addr = smem_u32(smem + (size_t)s * STAGE);
           const uint32_t b_addr = a_addr + A_BYTES;
-          const uint32_t sfa_addr = b_addr + B_BYTES;
-          const uint32_t sfb_addr = sfa_addr + SFA_BYTES;
           const uint32_t sf_col = tmem + ACC_COLS + (uint32_t)s * SF_COLS;
-#pragma unroll
-          for (int kb = 0; kb < 4; ++kb) {
-            tmem_cp_32x128b_x4_pair(sf_col + 4 * kb, desc_sf(sfa_addr + kb * SF_BLOCK));
-            tmem_cp_32x128b_x4_pair(sf_col + 16 + 8 * kb, desc_sf(sfb_addr + kb * SF_BLOCK));
-            tmem_cp_32x128b_x4_pair(sf_col + 16 + 8 * kb + 4, desc_sf(sfb_addr + 4 * SF_BLOCK + kb * SF_BLOCK));
-          }
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb)
             mma_mxf4nvf4_pair(tmem, desc_kmajor_sw128(a_addr + kb * 32), desc_kmajor_sw128(b_addr + kb * 32), idesc,
