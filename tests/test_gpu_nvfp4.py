@@ -168,6 +168,34 @@ def test_pair_gemm_matches_one_cta_kernel(m, n, with_bias, dtype):
     assert rel_l2(y_pair.float(), ref) < 0.15
 
 
+def test_pair_gemm_in_cuda_graph_and_unaligned_output_fallback():
+    """The pair GEMM replays from a CUDA graph (its kernel attributes are set by the first, eager
+    call) with the eager result; an output whose rows are not 16-byte aligned (ldy 6145) cannot take
+    the pair kernel's vector stores and runs on the one-CTA kernel, with the same values."""
+    d = dev()
+    m, n, k = 2048, 6144, 1024
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=22, realistic=False)
+    x = torch.randn((m, k), generator=torch.Generator().manual_seed(22)).to(torch.bfloat16).to(d)
+    pk, sc, s2t = torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d), torch.tensor(s2, device=d)
+    sf = prepack_scales(sc, n, k)
+    ws = torch.zeros(workspace_bytes(m, n, k, 1), dtype=torch.uint8, device=d)
+    y_eager = nvfp4_linear(x, pk, sc, s2t, None, None, 16, terms=1, sf=sf, workspace=ws)
+    y_graph = torch.empty_like(y_eager)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        nvfp4_linear(x, pk, sc, s2t, None, None, 16, terms=1, sf=sf, out=y_graph, workspace=ws)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y_graph, y_eager)
+    wide = torch.zeros((m, n + 1), dtype=torch.bfloat16, device=d)
+    y_odd = nvfp4_linear(x, pk, sc, s2t, None, None, 16, terms=1, sf=sf, out=wide[:, :n], workspace=ws)
+    torch.cuda.synchronize()
+    assert y_odd.stride(0) == n + 1
+    assert torch.equal(y_odd, y_eager)
+    assert (wide[:, n] == 0).all()
+
+
 @pytest.mark.parametrize("realistic", [True, False])
 def test_config0_full_size(realistic):
     # BASELINE config 0: x bf16 [16, 4096] ~N(0,1), W [12288, 4096] NVFP4, output bf16 [16, 12288];
