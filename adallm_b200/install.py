@@ -17,6 +17,8 @@ Replaces, by the same names and signatures:
   adallm.ops.activation.SiluAndMul.forward / GeluAndMul.forward                   (activation.py:11-26)
   adallm.runtime.model_runner.ModelRunner.fp8_decode_selftest (model_runner.py:171-232 imports the
       Triton kernel by name; the replacement runs the same zero-input smoke on this kernel)
+  adallm.architectures.qwen3.Qwen3DecoderLayer.forward at decode time (qwen3.py:1358-1371): the
+      layer as nine fused kernels (adallm_b200.fused_layer), the reference's forward otherwise
   adallm.infra.loader's post-load step (loader.py:129-162, called at the end of load_model): runs
       the reference's step, then prepack_model() derives every NVFP4 weight's tensor-core
       scale layout once at load
@@ -61,10 +63,15 @@ def block_tables_from_slots(slot_mapping: torch.Tensor, cu_seqlens_q: torch.Tens
     return torch.where(valid, pid, torch.full_like(pid, -1)).to(torch.int32)
 
 
-def install(terms: int | None = None, fresh_prefill: str | None = None) -> None:
+def install(terms: int | None = None, fresh_prefill: str | None = None, fused_layers: bool = True) -> None:
     """Rebind the reference's hot-path ops to this package's kernels.
 
     terms: activation e2m1 terms of the NVFP4 linear (default 4).
+    fused_layers: decode steps of the reference's Qwen3DecoderLayer (qwen3.py:1358-1371) run as
+      nine fused kernels (adallm_b200.fused_layer: RMSNorm+quantiser producers, split-K partial
+      planes summed by the next kernel, attention with the o_proj quantiser) on the layer's own
+      parameters, KV cache and forward context; every call the fused path does not cover
+      (prefill, TP > 1, ...) runs the reference's forward over the replaced ops.
     fresh_prefill: the prefill without a cached prefix (no block table; the reference runs
       flash-attn varlen over the fresh bf16 K/V, attention.py:346-358): "reference" keeps that,
       "kernel" stores K/V first (as the reference does) and runs this package's prefill kernel
@@ -186,6 +193,24 @@ def install(terms: int | None = None, fresh_prefill: str | None = None) -> None:
             nvfp4_gemm.prepack_model(model)
 
         ref_loader._init_nvfp4_bcol_scales = post_load
+    except Exception:
+        pass
+
+    try:  # the decode step of the Qwen3 decoder layer on the fused kernels
+        import adallm.architectures.qwen3 as ref_qwen3
+        from . import fused_layer
+
+        layer_cls = ref_qwen3.Qwen3DecoderLayer
+        orig_layer = getattr(layer_cls, "_adallm_ref_forward", layer_cls.forward)
+        layer_cls._adallm_ref_forward = orig_layer
+        if fused_layers:
+            def layer_forward(self, positions, hidden_states, residual):
+                out = fused_layer.decode_forward(self, positions, hidden_states, residual, ref_ctx.get_context())
+                return out if out is not None else orig_layer(self, positions, hidden_states, residual)
+
+            layer_cls.forward = layer_forward
+        else:
+            layer_cls.forward = orig_layer
     except Exception:
         pass
 

@@ -494,7 +494,8 @@ def dropin_bench(layers=36, batch=16, ctx=64):
         return {"error": (r.stderr or r.stdout)[-400:]}
     out = json.loads(lines[-1][len("DROPIN "):])
     out["what"] = ("reference Qwen3ForCausalLM + ModelRunner.capture_cudagraph/run_model with adallm_b200.install() "
-                   "(per-op kernels, page 256); run_model_ms includes the eager lm_head and static-buffer copies")
+                   "(decode layers as nine fused kernels on the reference's parameters, KV cache and context; "
+                   "page 256); run_model_ms includes the eager lm_head and static-buffer copies")
     return out
 
 

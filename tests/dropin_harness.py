@@ -49,7 +49,7 @@ def reference_available() -> tuple[bool, str]:
     return True, REF_DIR
 
 
-def _setup(fresh_prefill: str | None = None):
+def _setup(fresh_prefill: str | None = None, fused_layers: bool = True):
     os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
     os.environ.setdefault("ADALLM_DISABLE_PROGRESS", "1")
     os.environ.setdefault("ADALLM_QUIET", "1")
@@ -57,7 +57,7 @@ def _setup(fresh_prefill: str | None = None):
         if p not in sys.path:
             sys.path.insert(0, p)
     import adallm_b200
-    adallm_b200.install(fresh_prefill=fresh_prefill)
+    adallm_b200.install(fresh_prefill=fresh_prefill, fused_layers=fused_layers)
 
 
 def _hf_config_dict(layers: int, vocab: int) -> dict:
@@ -135,10 +135,11 @@ def random_weights(layers: int, vocab: int, seed: int):
     return ckpt, oracle_w
 
 
-def check(layers: int, decode_steps: int, seed: int, fresh_prefill: str = "kernel") -> dict:
+def check(layers: int, decode_steps: int, seed: int, fresh_prefill: str = "kernel", fused_layers: bool = True) -> dict:
     """fresh_prefill "kernel" (default here): the fresh prefill also runs this package's paged
-    prefill kernel, so every attention of the check is ours; "reference" keeps flash-attn."""
-    _setup(fresh_prefill)
+    prefill kernel, so every attention of the check is ours; "reference" keeps flash-attn.
+    fused_layers: install()'s fused decode layers (default) or the per-op path."""
+    _setup(fresh_prefill, fused_layers)
     import numpy as np
     import torch
     from safetensors.torch import save_file
@@ -253,14 +254,20 @@ def check(layers: int, decode_steps: int, seed: int, fresh_prefill: str = "kerne
            "prepacked_weights": prepacked, "graphs": sorted(runner.graphs.keys()),
            "raw": agree / total, "raw_reference": agree_ref / total, "tokens": total,
            "rel_l2_max": max(errs), "rel_l2_mean": float(np.mean(errs)),
-           "ref_rel_l2_mean": float(np.mean(ref_errs)), "phases": phases[:2]}
+           "ref_rel_l2_mean": float(np.mean(ref_errs)), "phases": phases[:2],
+           "fused_layers": fused_layers, "fused_layer_calls": _fused_calls()}
     runner.exit()
     return out
 
 
-def bench(layers: int, batch: int, ctx: int, reps: int) -> dict:
+def _fused_calls() -> int:
+    from adallm_b200 import fused_layer
+    return int(fused_layer.CALLS)
+
+
+def bench(layers: int, batch: int, ctx: int, reps: int, fused_layers: bool = True) -> dict:
     """Decode-step time of the reference runtime's captured graph with this package installed."""
-    _setup()
+    _setup(None, fused_layers)
     import torch
     import torch.distributed as dist
     from adallm.architectures.registry import build_model
@@ -337,7 +344,8 @@ def bench(layers: int, batch: int, ctx: int, reps: int) -> dict:
     nvfp4_gemm.check_device_errors()
     return {"layers": layers, "batch": batch, "ctx": ctx, "page": PAGE, "graph_ms": round(step_ms, 4),
             "run_model_ms": round(run_ms, 4), "tok_s": round(batch / (run_ms / 1e3), 1),
-            "graph_tok_s": round(batch / (step_ms / 1e3), 1)}
+            "graph_tok_s": round(batch / (step_ms / 1e3), 1), "fused_layers": fused_layers,
+            "fused_layer_calls": _fused_calls()}
 
 
 def flash_attn_probe() -> dict:
@@ -369,15 +377,16 @@ def main():
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--fresh-prefill", default="kernel", choices=["kernel", "reference"])
+    ap.add_argument("--per-op", action="store_true", help="install(fused_layers=False): the per-op decode path")
     a = ap.parse_args()
     ok, why = reference_available()
     if not ok:
         print(json.dumps({"unavailable": why}))
         return
     if a.mode == "check":
-        r = check(a.layers, a.steps, a.seed, a.fresh_prefill)
+        r = check(a.layers, a.steps, a.seed, a.fresh_prefill, not a.per_op)
     elif a.mode == "bench":
-        r = bench(a.layers, a.batch, a.ctx, a.reps)
+        r = bench(a.layers, a.batch, a.ctx, a.reps, not a.per_op)
     else:
         r = flash_attn_probe()
     print("DROPIN " + json.dumps(r), flush=True)

@@ -39,14 +39,21 @@ def _run(*args, timeout=1500):
     path = os.environ.get("ADA_AGREEMENT_LOG")
     if path:
         with open(path, "a") as f:
-            f.write(json.dumps({"test": "dropin_" + args[0], **out}) + "\n")
+            f.write(json.dumps({"test": "dropin_" + "_".join(args[:1] + [a.strip("-") for a in args if a == "--per-op"]), **out}) + "\n")
     return out
 
 
-def test_dropin_inside_reference_model_runner():
-    r = _run("check", "--layers", str(LAYERS), "--steps", "24")
+@pytest.mark.parametrize("path", ["fused_layers", "per_op"])
+def test_dropin_inside_reference_model_runner(path):
+    """Both install() decode paths: the reference's Qwen3DecoderLayer as nine fused kernels
+    (the default) and the per-op replacements under the reference's own layer forward."""
+    r = _run("check", "--layers", str(LAYERS), "--steps", "24", *(["--per-op"] if path == "per_op" else []))
     assert r["prepacked_weights"] == 4 * LAYERS, r
     assert r["graphs"] == [1, 2, 4, 8], r
+    if path == "fused_layers":
+        assert r["fused_layer_calls"] >= LAYERS * len(r["graphs"]), r  # every captured decode layer
+    else:
+        assert r["fused_layer_calls"] == 0, r
     assert r["rel_l2_max"] < 5e-2, r
     assert r["rel_l2_mean"] <= 1.25 * max(r["ref_rel_l2_mean"], 1e-3), r
     p = min(max(r["raw_reference"], 0.5), 1.0)
