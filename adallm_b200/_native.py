@@ -97,6 +97,8 @@ _SIGS = {
     "ada_nvfp4_gemm_partials": (INT, [P, P, P, I64, INT, INT, P, I64, P, P, I64, I64, P, I64, I64, INT, P, SZ, P]),
     "ada_rmsnorm_quant_parts": (INT, [P, I32, I64, I64, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT,
                                       P, P, P, P]),
+    "ada_rmsnorm_quant_combine": (INT, [P, I64, P, I32, P, I64, P, I64, P, P, I64, I64, I32, F32, INT, INT, INT, INT,
+                                        P, P, P, P]),
     "ada_peer_alloc": (INT, [SZ, PP, P]),
     "ada_peer_open": (INT, [P, PP]),
     "ada_peer_close": (INT, [P]),

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
                                                             int64_t ldr, T* res_out, int64_t ldro,
                                                             const T* __restrict__ w, const T* __restrict__ wpre, T* y,
                                                             int64_t ldy, int rows, int hidden, float eps, int gemma,
-                                                            q::QuantDst dst, PartIn pin, PeerWait pw) {
+                                                            q::QuantDst dst, PartIn pin, PeerWait pw, SlotIn sin) {
   __shared__ float red[2 * cl::MAX_WARPS];
   __shared__ cl::Exchange xpre;    // the Gemma post-norm's sum of squares
   __shared__ cl::Exchange2 xmain;  // the sum of squares and max |x * w| together
@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(512) rmsnorm_quant_kernel(const T* __restrict_
         load_parts_tagged<T, 8>(pin, m, o * 8, pw, tag, v[u]);
       else if (pin.n)
         load_parts<T, 8>(pin, m, o * 8, v[u]);  // the producing GEMM's split-K planes
+      else if (sin.y)
+        load_slots<T, 8>(sin, m, o * 8, v[u]);  // the MoE block's weighted combine of the expert rows
       else
         load8<T>(x + (int64_t)m * ldx + o * 8, v[u]);
     } else {
@@ -319,7 +321,8 @@ bool quant_args_ok(const q::QuantDst& d) {
 int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, void* ro, int64_t ldro, const void* w,
                    void* y, int64_t ldy, int64_t rows, int64_t launch_rows, int hidden, float eps, int gemma,
                    int dtype, const q::QuantDst& dst, cudaStream_t st, const PartIn& pin = PartIn{nullptr, 0, 0, 0},
-                   const PeerWait& pw = PeerWait{nullptr, 0, 0, nullptr}, const void* wpre = nullptr) {
+                   const PeerWait& pw = PeerWait{nullptr, 0, 0, nullptr}, const void* wpre = nullptr,
+                   const SlotIn& sin = SlotIn{nullptr, 0, nullptr, 0}) {
   if (hidden % 16) return ADA_ERR_UNSUPPORTED;
   const cl::RowSplit sp = cl::row_split(hidden / 16);
   if (!sp.maxu || launch_rows > 65535) return ADA_ERR_UNSUPPORTED;
@@ -328,11 +331,11 @@ int launch_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldr, voi
   if (dtype == ADA_DT_BF16) {
     using TT = __nv_bfloat16;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (const TT*)wpre, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
+                     (const TT*)w, (const TT*)wpre, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw, sin);
   } else {
     using TT = __half;
     ADA_ROW_DISPATCH(rmsnorm_quant_kernel, TT, sp, (const TT*)x, ldx, (const TT*)res, ldr, (TT*)ro, ldro,
-                     (const TT*)w, (const TT*)wpre, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw);
+                     (const TT*)w, (const TT*)wpre, (TT*)y, ldy, (int)rows, hidden, eps, gemma, dst, pin, pw, sin);
   }
   return err_ == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
@@ -457,6 +460,29 @@ static int rmsnorm_quant_parts_impl(const float* parts, int32_t nparts, int64_t 
   return fused::launch_rmsnorm(nullptr, 0, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
                                launch_rows, hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream), pin,
                                pw, pre_weight);
+}
+
+extern "C" int ada_rmsnorm_quant_combine(const void* y_rows, int64_t ld_rows, const void* route_w, int32_t topk,
+                                         const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                         const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
+                                         float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
+                                         uint8_t* sfx, float* gx, void* stream) {
+  if (rows <= 0 || hidden <= 0 || !weight || !y_rows || !route_w || topk < 1 || ld_rows < hidden ||
+      (residual && !residual_out))
+    return ADA_ERR_INVALID_ARG;
+  if (dtype != ADA_DT_BF16 && dtype != ADA_DT_F16) return ADA_ERR_INVALID_ARG;
+  const bool quant = xq != nullptr;  // without a quantised output this is a plain RMSNorm into y
+  const q::QuantDst dst{xq, sfx, gx, quant ? terms : 1, quant ? block_n : 16, hidden};
+  if (quant ? !fused::quant_args_ok(dst) : !y) return ADA_ERR_INVALID_ARG;
+  if (!fused::a16(weight) || !fused::a16(y_rows) || (ld_rows & 7) || (y && (!fused::a16(y) || (ldy & 7))))
+    return ADA_ERR_ALIGNMENT;
+  if (residual && (!fused::a16(residual) || !fused::a16(residual_out) || (ld_res & 7) || (ld_res_out & 7)))
+    return ADA_ERR_ALIGNMENT;
+  const int64_t launch_rows = quant ? cdiv(rows, block_n) * block_n : rows;
+  return fused::launch_rmsnorm(nullptr, 0, residual, ld_res, residual_out, ld_res_out, weight, y, ldy, rows,
+                               launch_rows, hidden, eps, gemma, dtype, dst, reinterpret_cast<cudaStream_t>(stream),
+                               PartIn{nullptr, 0, 0, 0}, PeerWait{nullptr, 0, 0, nullptr}, nullptr,
+                               SlotIn{y_rows, ld_rows, route_w, topk});
 }
 
 extern "C" int ada_gemma_norm2_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp,

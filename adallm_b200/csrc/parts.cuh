@@ -15,6 +15,34 @@ struct PartIn {
   int64_t ld;      // floats between rows
 };
 
+// The MoE block's weighted combine as an input: element (t, c) is sum_j w[t][j] * y[t * topk + j][c]
+// (fp32 fma in slot order from 0, as the combine kernel accumulates), rounded to T.
+struct SlotIn {
+  const void* y;  // [tokens * topk, ldy] expert rows (T); null: not this input mode
+  int64_t ldy;
+  const void* w;  // [tokens, topk] routing weights (T)
+  int topk;
+};
+
+template <typename T, int N>
+__device__ __forceinline__ void load_slots(const SlotIn& si, int64_t row, int64_t col, float* f) {
+  static_assert(N == 8, "one 16-byte vector of T");
+  const T* y = reinterpret_cast<const T*>(si.y);
+  const T* w = reinterpret_cast<const T*>(si.w);
+  float acc[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) acc[i] = 0.f;
+  for (int j = 0; j < si.topk; ++j) {
+    const float wj = to_f32(w[row * si.topk + j]);
+    float v[N];
+    unpack8<T>(*reinterpret_cast<const uint4*>(y + (row * si.topk + j) * si.ldy + col), v);
+#pragma unroll
+    for (int i = 0; i < N; ++i) acc[i] = fmaf(wj, v[i], acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) f[i] = to_f32(from_f32<T>(acc[i]));
+}
+
 // Elements [col, col + N) of row `row`: sum of the planes (plane order), rounded to T.
 template <typename T, int N>
 __device__ __forceinline__ void load_parts(const PartIn& pi, int64_t row, int64_t col, float* f) {

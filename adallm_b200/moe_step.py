@@ -23,6 +23,8 @@ generator); router weights N(0, 1/H), so router logits are ~N(0, 1) as the confi
 """
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass
 
 import torch
@@ -105,6 +107,9 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
             raise ValueError("experts must split evenly over the expert-parallel ranks")
         self.local_experts = cfg.num_experts // cfg.ep_size
         self.expert_base = cfg.ep_rank * self.local_experts
+        # at EP 1 the weighted combine is the input stage of the next RMSNorm (one launch fewer per
+        # layer, the same values); ADALLM_B200_MOE_FOLD_COMBINE=0 keeps the separate combine kernel
+        self.fold_combine = os.environ.get("ADALLM_B200_MOE_FOLD_COMBINE", "1") != "0"
         super().__init__(cfg, device, max_batch, max_ctx, seed=seed, group=group, fused=True)
         if not self.use_parts:
             raise ValueError("MoE engine: an attention projection has no partial-plane split at this batch")
@@ -201,6 +206,8 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
                                         int(c.norm_topk_prob), self.route_ids.data_ptr(), self.route_w.data_ptr(),
                                         self.ws_experts.data_ptr(), stream), "moe router + route")
         self._experts_mlp(L, stream)
+        if c.ep_size == 1 and self.fold_combine:
+            return  # the weighted combine is the input stage of the next RMSNorm (ada_rmsnorm_quant_combine)
         if c.ep_size == 1:
             N.check(lib.ada_moe_combine(self.y_rows.data_ptr(), 0, self.y_rows.stride(0), self.route_w.data_ptr(), B,
                                         c.top_k, c.hidden, self.hidden.data_ptr(), self.hidden.stride(0), stream),
@@ -222,6 +229,7 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
                                   self.hidden.data_ptr(), 0, stream), "embedding")
         qn = c.hq * D
         H = c.hidden
+        fold = c.ep_size == 1 and self.fold_combine
         for li, L in enumerate(self.layers):
             xq, sfx, gx = self.q_hidden
             if li == 0:
@@ -229,9 +237,16 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
                 res = None
             else:
                 res = self.residual.data_ptr()
-            N.check(lib.ada_rmsnorm_quant(self.hidden.data_ptr(), H, res, H, res, H, L["in_norm"].data_ptr(), None, 0,
-                                          B, H, c.rms_eps, 0, 0, c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(),
-                                          gx.data_ptr(), stream), "rms_norm+quant")
+            if li > 0 and fold:  # the previous layer's combine + residual add + RMSNorm + quantiser
+                N.check(lib.ada_rmsnorm_quant_combine(self.y_rows.data_ptr(), self.y_rows.stride(0),
+                                                      self.route_w.data_ptr(), c.top_k, res, H, res, H,
+                                                      L["in_norm"].data_ptr(), None, 0, B, H, c.rms_eps, 0, 0,
+                                                      c.terms, self.bn, xq.data_ptr(), sfx.data_ptr(), gx.data_ptr(),
+                                                      stream), "moe combine + rms_norm + quant")
+            else:
+                N.check(lib.ada_rmsnorm_quant(self.hidden.data_ptr(), H, res, H, res, H, L["in_norm"].data_ptr(),
+                                              None, 0, B, H, c.rms_eps, 0, 0, c.terms, self.bn, xq.data_ptr(),
+                                              sfx.data_ptr(), gx.data_ptr(), stream), "rms_norm+quant")
             ns, ld = self._gemm_parts(self.q_hidden, L["qkv"], "qkv", stream)
             kc, vc = self.kv_cache[0, li], self.kv_cache[1, li]
             N.check(lib.ada_qk_norm_rope_store_parts(self.parts.data_ptr(), ns, B * ld, ld, B, c.hq, c.hkv, D,
@@ -254,9 +269,17 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
                                                 L["post_norm"].data_ptr(), self.xnorm.data_ptr(), H, B, H, c.rms_eps,
                                                 0, 0, c.terms, self.bn, None, None, None, stream), "rms_norm")
             self._moe_block(L, stream)
-        N.check(lib.ada_rmsnorm(self.hidden.data_ptr(), H, self.residual.data_ptr(), H, self.residual.data_ptr(), H,
-                                self.final_norm.data_ptr(), self.xnorm.data_ptr(), H, B, H, c.rms_eps, 0, 0, stream),
-                "rms_norm")
+        if fold:
+            rp = self.residual.data_ptr()
+            N.check(lib.ada_rmsnorm_quant_combine(self.y_rows.data_ptr(), self.y_rows.stride(0),
+                                                  self.route_w.data_ptr(), c.top_k, rp, H, rp, H,
+                                                  self.final_norm.data_ptr(), self.xnorm.data_ptr(), H, B, H,
+                                                  c.rms_eps, 0, 0, c.terms, self.bn, None, None, None, stream),
+                    "moe combine + rms_norm")
+        else:
+            N.check(lib.ada_rmsnorm(self.hidden.data_ptr(), H, self.residual.data_ptr(), H, self.residual.data_ptr(),
+                                    H, self.final_norm.data_ptr(), self.xnorm.data_ptr(), H, B, H, c.rms_eps, 0, 0,
+                                    stream), "rms_norm")
         self._lm_head(stream)
 
     def kernels_per_step(self) -> int:
@@ -266,7 +289,8 @@ class Qwen3MoeDecodeEngine(Qwen3DecodeEngine):
         expert MLP (routing, gathering quantiser, gate_up GEMM, SiLU*up+quant, down GEMM), combine;
         final RMSNorm; lm_head + pick (the expert-parallel all-reduce is NCCL's)."""
         attn = 1 if self.max_pages_per_seq * self.cfg.page_size <= 1024 and self.cfg.hkv <= 8 else 2
-        return 1 + self.cfg.num_layers * (12 + attn) + 3
+        fold = self.cfg.ep_size == 1 and self.fold_combine  # the combine folded into the next RMSNorm
+        return 1 + self.cfg.num_layers * (12 + attn - (1 if fold else 0)) + 3
 
     def export_cpu_weights(self) -> dict:
         if self.cfg.ep_size != 1:

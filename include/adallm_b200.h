@@ -466,6 +466,16 @@ ADA_API int ada_rmsnorm_quant_parts(const float* parts, int32_t nparts, int64_t 
                                     const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden, float eps,
                                     int gemma, int dtype, int terms, int block_n, uint8_t* xq, uint8_t* sfx,
                                     float* gx, void* stream);
+/* RMSNorm whose input row is the MoE block's weighted combine (the reference's
+ * sum_k w_k * expert_k(x) of Qwen3MoeSparseMoeBlock, qwen3.py:1263-1290): element (t, c) =
+ * sum_j route_w[t][j] * y_rows[t * topk + j][c] (fp32, slot order, rounded to dtype), i.e.
+ * exactly ada_moe_combine's output, then exactly ada_rmsnorm_quant (xq == NULL: plain RMSNorm
+ * into y).  Replaces the combine kernel and the next layer's input norm by one launch. */
+ADA_API int ada_rmsnorm_quant_combine(const void* y_rows, int64_t ld_rows, const void* route_w, int32_t topk,
+                                      const void* residual, int64_t ld_res, void* residual_out, int64_t ld_res_out,
+                                      const void* weight, void* y, int64_t ldy, int64_t rows, int32_t hidden,
+                                      float eps, int gemma, int dtype, int terms, int block_n, uint8_t* xq,
+                                      uint8_t* sfx, float* gx, void* stream);
 ADA_API int ada_gated_act_quant_parts(const float* parts, int32_t nparts, int64_t plane, int64_t ldp, void* y,
                                       int64_t ldy, int64_t rows, int32_t inter, int act, int dtype, int terms,
                                       int block_n, uint8_t* xq, uint8_t* sfx, float* gx, void* stream);

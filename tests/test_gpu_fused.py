@@ -344,3 +344,40 @@ def test_qk_norm_rope_store_from_planes():
     torch.cuda.synchronize()
     for a, b in zip(out[0], out[1]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("m,with_res", [(16, True), (5, True), (16, False)])
+def test_rmsnorm_quant_combine_matches_combine_then_rmsnorm(m, with_res):
+    """The MoE block's weighted combine folded into the next RMSNorm (ada_rmsnorm_quant_combine)
+    equals ada_moe_combine followed by ada_rmsnorm_quant bit for bit (quantised operand, new
+    residual) and, without a quantised output, ada_moe_combine + ada_rmsnorm (config-4 widths)."""
+    d = dev()
+    s = torch.cuda.current_stream().cuda_stream
+    H, k, terms, bn = 2048, 8, 4, 16
+    g = torch.Generator(device="cpu").manual_seed(12)
+    y_rows = torch.randn((m * k, H), generator=g).to(torch.bfloat16).to(d)
+    rw = torch.rand((m, k), generator=g).to(torch.bfloat16).to(d)
+    res = torch.randn((m, H), generator=g).to(torch.bfloat16).to(d)
+    w = (torch.randn(H, generator=g) * 0.1 + 1).to(torch.bfloat16).to(d)
+    hidden = torch.empty((m, H), dtype=torch.bfloat16, device=d)
+    N.check(N.lib().ada_moe_combine(y_rows.data_ptr(), 0, H, rw.data_ptr(), m, k, H, hidden.data_ptr(), H, s),
+            "combine")
+    r1, r2 = res.clone(), res.clone()
+    rp1 = r1.data_ptr() if with_res else None
+    rp2 = r2.data_ptr() if with_res else None
+    ref, got = qbufs(m, H, terms, bn, d), qbufs(m, H, terms, bn, d)
+    N.check(N.lib().ada_rmsnorm_quant(hidden.data_ptr(), H, rp1, H, rp1, H, w.data_ptr(), None, 0, m, H, 1e-6, 0, 0,
+                                      terms, bn, ref[0].data_ptr(), ref[1].data_ptr(), ref[2].data_ptr(), s), "rmsq")
+    N.check(N.lib().ada_rmsnorm_quant_combine(y_rows.data_ptr(), H, rw.data_ptr(), k, rp2, H, rp2, H, w.data_ptr(),
+                                              None, 0, m, H, 1e-6, 0, 0, terms, bn, got[0].data_ptr(),
+                                              got[1].data_ptr(), got[2].data_ptr(), s), "rmsq_combine")
+    y1, y2 = torch.empty_like(hidden), torch.empty_like(hidden)
+    r3, r4 = res.clone(), res.clone()
+    N.check(N.lib().ada_rmsnorm(hidden.data_ptr(), H, r3.data_ptr(), H, r3.data_ptr(), H, w.data_ptr(), y1.data_ptr(),
+                                H, m, H, 1e-6, 0, 0, s), "rms")
+    N.check(N.lib().ada_rmsnorm_quant_combine(y_rows.data_ptr(), H, rw.data_ptr(), k, r4.data_ptr(), H, r4.data_ptr(),
+                                              H, w.data_ptr(), y2.data_ptr(), H, m, H, 1e-6, 0, 0, terms, bn, None,
+                                              None, None, s), "rms_combine_plain")
+    torch.cuda.synchronize()
+    same(got, ref)
+    assert torch.equal(r1, r2) and torch.equal(y1, y2) and torch.equal(r3, r4)
