@@ -220,3 +220,33 @@ def test_nvfp4_fp8_setting_is_recorded_and_keeps_the_terms(ref, monkeypatch):
         assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is False and nvfp4_gemm.DEFAULT_TERMS == terms
     finally:
         context.use_context_provider(None)
+
+
+def test_install_routes_the_qwen3_decoder_layer(ref):
+    """install() routes Qwen3DecoderLayer.forward through the fused decode layer (fused_layers,
+    the default) and keeps the reference's forward for every call it does not cover: a prefill
+    context, no context, tensors off the GPU.  fused_layers=False restores the reference's."""
+    import torch
+    import adallm.architectures.qwen3 as rq
+    import adallm_b200
+    from adallm_b200 import fused_layer
+    from types import SimpleNamespace
+    layer_cls = rq.Qwen3DecoderLayer
+    adallm_b200.install()
+    orig = layer_cls._adallm_ref_forward
+    assert layer_cls.forward.__name__ == "layer_forward"
+    x = torch.zeros(4, 4096, dtype=torch.bfloat16)
+    pos = torch.zeros(4, dtype=torch.int64)
+    prefill = SimpleNamespace(is_prefill=True, block_tables=None, context_lens=None, slot_mapping=None)
+    decode = SimpleNamespace(is_prefill=False, block_tables=torch.zeros((4, 1), dtype=torch.int32),
+                             context_lens=torch.ones(4, dtype=torch.int32), slot_mapping=torch.zeros(4, dtype=torch.int32))
+    fake_layer = SimpleNamespace()
+    assert fused_layer.decode_forward(fake_layer, pos, x, None, prefill) is None
+    assert fused_layer.decode_forward(fake_layer, pos, x, None, None) is None
+    assert fused_layer.decode_forward(fake_layer, pos, x, None, decode) is None  # CPU tensors
+    adallm_b200.install(fused_layers=False)
+    assert layer_cls.forward is orig
+    adallm_b200.install()
+    assert layer_cls.forward.__name__ == "layer_forward" and layer_cls._adallm_ref_forward is orig
+    from adallm_b200 import context
+    context.use_context_provider(None)
