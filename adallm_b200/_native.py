@@ -74,6 +74,8 @@ _SIGS = {
     "ada_nvfp4_prepack_scales": (INT, [P, INT, I64, I64, I64, P, P]),
     "ada_nvfp4_linear_workspace_size": (SZ, [I64, I64, I64, INT]),
     "ada_nvfp4_linear": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I64, P, P, INT, I64, INT, P, SZ, P]),
+    "ada_nvfp4_linear_w4a16_workspace_size": (SZ, [I64, I64]),
+    "ada_nvfp4_linear_w4a16": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I64, P, P, INT, I64, P, SZ, P]),
     "ada_nvfp4_linear_ex": (INT, [P, INT, I64, I64, I64, P, I64, P, P, I64, P, P, INT, I64, INT, INT, P, SZ, P]),
     "ada_nvfp4_workspace_status": (INT, [P, I64, I64, I64, INT, P, P]),
     "ada_nvfp4_act_quant": (INT, [P, INT, I64, I64, I64, INT, INT, P, P, P, P]),

@@ -169,6 +169,40 @@ def nvfp4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor,
     return y.to(out_dtype).view(*x.shape[:-1], n)
 
 
+def nvfp4_linear_w4a16(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, w_scale_2: torch.Tensor,
+                       bias: torch.Tensor | None = None, sf: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ dequant(W)^T (+ bias) in the reference's W4A16 arithmetic (fp16 activations,
+    fp16-exact dequantised weights, fp32 accumulation; adallm/ops/nvfp4_gemm.py:460-564) on
+    SM-pair tensor-core tiles, for prefill-size M.  Needs N % 256 == 0 and K % 64 == 0."""
+    if not x.is_cuda:
+        raise RuntimeError("nvfp4_linear_w4a16 requires CUDA tensors")
+    out_dtype = x.dtype
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        x = x.to(torch.float16)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1 or (x2.stride(0) % 8) or (x2.data_ptr() % 16):
+        x2 = x2.contiguous()
+    m, k = x2.shape
+    n = w_packed.shape[0]
+    if w_packed.shape[1] * 2 != k:
+        raise ValueError("Packed weight shape does not match input features")
+    if sf is None:
+        sf = _cached_sf(w_scale, n, k)
+    g2 = _as_fp32_scalar(w_scale_2, x.device)
+    ydt = x2.dtype
+    y = out if out is not None else torch.empty((m, n), dtype=ydt, device=x.device)
+    b = None if bias is None else bias.to(ydt).contiguous()
+    if m == 0:
+        return y.to(out_dtype).view(*x.shape[:-1], n)
+    ws = _workspace(x.device, int(N.lib().ada_nvfp4_linear_w4a16_workspace_size(m, k)))
+    st = N.lib().ada_nvfp4_linear_w4a16(x2.data_ptr(), N.DT[ydt], x2.stride(0), m, k, w_packed.data_ptr(),
+                                        w_packed.stride(0), sf.data_ptr(), g2.data_ptr(), n, N.ptr(b), y.data_ptr(),
+                                        N.DT[ydt], y.stride(0), ws.data_ptr(), ws.numel(), N.stream_ptr(x.device))
+    N.check(st, "NVFP4 W4A16 kernel")
+    return y.to(out_dtype).view(*x.shape[:-1], n)
+
+
 def nvfp4_linear_dual(x, w1_packed, w1_scale, w1_scale_2, w2_packed, w2_scale, w2_scale_2, bias1, bias2,
                       group_size, terms: int | None = None):
     """gate and up projections sharing one activation (adallm/ops/nvfp4_gemm.py:567-654)."""

@@ -278,6 +278,19 @@ ADA_API int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m,
                              const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
                              const float* w_scale_2, int64_t n, const void* bias, void* y, int y_dtype,
                              int64_t ldy, int terms, void* workspace, size_t workspace_bytes, void* stream);
+/* The reference's W4A16 arithmetic for prefill-size M (adallm/ops/nvfp4_gemm.py:460-564):
+ * x [M, K] bf16/f16 is cast to fp16 (bf16 input: into the workspace), the e2m1 weights are
+ * widened to fp16 on chip (code value x e4m3 block scale, exact), and
+ * tcgen05.mma.cta_group::2.kind::f16 tiles of 256 tokens x 256 weight rows accumulate in fp32;
+ * the fp32 global scale and the bias are applied in the epilogue.  sf_w is the prepacked scale
+ * layout of ada_nvfp4_prepack_scales.  Implemented: N % 256 == 0, K % 64 == 0; x, y, bias,
+ * w_packed and sf_w 16-byte aligned, ldx and ldy multiples of 8, ldw a multiple of 16.
+ * workspace: ada_nvfp4_linear_w4a16_workspace_size(M, K) bytes, 256-byte aligned. */
+ADA_API size_t ada_nvfp4_linear_w4a16_workspace_size(int64_t m, int64_t k);
+ADA_API int ada_nvfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
+                                   const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
+                                   const float* w_scale_2, int64_t n, const void* bias, void* y, int y_dtype,
+                                   int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 /* Same as ada_nvfp4_linear with an explicit split-K factor (0 = library choice, else 1..8
  * CTAs per output tile; tests and tuning). */
 ADA_API int ada_nvfp4_linear_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,

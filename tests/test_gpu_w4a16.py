@@ -1,0 +1,90 @@
+"""NVFP4 linear in the reference's W4A16 arithmetic on SM-pair tensor-core tiles
+(ada_nvfp4_linear_w4a16, tcgen05.mma.cta_group::2.kind::f16) vs dequantise-then-matmul.
+
+The weights are widened to fp16 exactly (e2m1 value x e4m3 block scale), the activations are
+cast to fp16 as the reference casts them (adallm/ops/nvfp4_gemm.py:475), and the products
+accumulate in fp32, so against an fp64 matmul of the same fp16 operands the only error is fp32
+summation order and the output rounding: rel-L2 <= 2e-3 for bf16 outputs, <= 5e-4 for fp16."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nvfp4 as nv
+from adallm_b200.nvfp4_gemm import nvfp4_linear_w4a16, prepack_scales
+from tests.gpu_util import dev, rel_l2
+from tests.test_gpu_nvfp4 import random_weight
+
+pytestmark = pytest.mark.gpu
+
+
+def ref_w4a16(x, packed, scale16, s2, bias):
+    """fp64 x.half() @ (lut x block scale)^T x scale_2 (+ bias)."""
+    w = nv.dequant_nvfp4_torch(packed, scale16.astype(np.float32), None).double()
+    y = (x.half().double().cpu() @ w.t()) * float(s2)
+    if bias is not None:
+        y = y + bias.double().cpu()
+    return y
+
+
+@pytest.mark.parametrize("m,n,k,with_bias,dtype", [
+    (2048, 6144, 4096, False, torch.bfloat16),
+    (300, 512, 256, True, torch.float16),      # ragged last tile (rows 300..511 never stored)
+    (17, 256, 64, False, torch.bfloat16),      # one K stage, one tile
+    (1100, 4096, 1024, True, torch.bfloat16),
+])
+def test_w4a16_matches_dequant_matmul(m, n, k, with_bias, dtype):
+    d = dev()
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=31, realistic=False)
+    g = torch.Generator().manual_seed(31)
+    x = torch.randn((m, k), generator=g).to(dtype)
+    bias = (torch.randn((n,), generator=g) * 0.1).to(dtype) if with_bias else None
+    y = nvfp4_linear_w4a16(x.to(d), torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d),
+                           torch.tensor(s2, device=d), None if bias is None else bias.to(d))
+    torch.cuda.synchronize()
+    assert y.dtype == dtype and y.shape == (m, n)
+    ref = ref_w4a16(x, packed, scale16, s2, bias)
+    tol = 2e-3 if dtype == torch.bfloat16 else 5e-4
+    err = rel_l2(y.double().cpu(), ref)
+    assert err < tol, f"rel-L2 {err:.2e}"
+    # against the reference's own formula (fp32 dequantised weights incl. scale_2): same bar
+    w = nv.dequant_nvfp4_torch(packed, scale16.astype(np.float32), s2)
+    ref2 = x.half().float() @ w.t() + (bias.float() if bias is not None else 0.0)
+    assert rel_l2(y.float().cpu(), ref2) < tol
+
+
+def test_w4a16_in_cuda_graph_and_strided_io():
+    """Replays from a CUDA graph with the eager result; a strided input view (ldx > K) and an
+    output slice of a wider buffer (ldy > N) give the same values as contiguous ones."""
+    d = dev()
+    m, n, k = 1024, 2048, 1024
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=32, realistic=False)
+    pk, sc, s2t = torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d), torch.tensor(s2, device=d)
+    sf = prepack_scales(sc, n, k)
+    xw = torch.randn((m, k + 64), generator=torch.Generator().manual_seed(32)).to(torch.bfloat16).to(d)
+    x = xw[:, :k]
+    y_eager = nvfp4_linear_w4a16(x.contiguous(), pk, sc, s2t, sf=sf)
+    wide = torch.zeros((m, n + 256), dtype=torch.bfloat16, device=d)
+    y_strided = nvfp4_linear_w4a16(x, pk, sc, s2t, sf=sf, out=wide[:, :n])
+    torch.cuda.synchronize()
+    assert torch.equal(y_strided, y_eager)
+    assert torch.count_nonzero(wide[:, n:]) == 0
+    y_graph = torch.empty_like(y_eager)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            nvfp4_linear_w4a16(x, pk, sc, s2t, sf=sf, out=y_graph)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y_graph, y_eager)
+    del graph
+
+
+def test_w4a16_rejects_unsupported_shapes():
+    d = dev()
+    packed, sbits, scale16, s2 = random_weight(128, 256, seed=33, realistic=False)
+    x = torch.randn((64, 256), dtype=torch.bfloat16, device=d)
+    with pytest.raises(Exception):  # N % 256 != 0
+        nvfp4_linear_w4a16(x, torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d),
+                           torch.tensor(s2, device=d))
