@@ -10,7 +10,7 @@
 //     are the MMA's A operand: 256 token rows per CTA pair, 128 staged by each CTA (TMA, 128-byte
 //     swizzle);
 //   * each CTA stages the packed e2m1 bytes and e4m3 block scales of its 128 of the tile's 256
-//     weight rows (TMA + bulk copy), and eight converter warps widen them in shared memory to fp16
+//     weight rows (TMA + bulk copy), and converter warps widen them in shared memory to fp16
 //     (lut[code] * block scale is exact in fp16) in the swizzled K-major layout the MMA reads;
 //   * one tcgen05.mma.cta_group::2.kind::f16 of M 256 x N 256 x K 16 per 16-wide K step, fp32
 //     accumulators in TMEM, two of them (2 x 256 columns) so the epilogue of tile i overlaps the
@@ -19,7 +19,7 @@
 //
 // Protocol (CTA rank 0 of the pair leads; no multicast anywhere):
 //   full[s]  (each):   this CTA's activation, packed-weight and scale loads of stage s landed.
-//   ready[s] (rank 0): the converter warps of both CTAs wrote stage s's fp16 weights (16 arrivals).
+//   ready[s] (rank 0): one converter group of each CTA wrote stage s's fp16 weights (8 arrivals).
 //   empty[s] (each):   the leader's MMA thread commits to both CTAs once stage s is read.
 //   accf[b]  (each):   accumulator b complete (committed to both CTAs).
 //   acce[b]  (rank 0): accumulator b drained by the 8 epilogue warps of both CTAs (16 arrivals).
@@ -44,7 +44,11 @@ constexpr uint32_t LOAD_BYTES = A_BYTES + W_BYTES + S_BYTES;
 constexpr uint32_t STAGE = 38 * 1024;          // A | B | W | S, padded to keep A and B 1 KiB aligned
 constexpr int STAGES = 5;
 constexpr uint32_t TMEM_COLS = 512;            // two 256-column accumulators
-constexpr int CONV_WARPS = 8;               // two threads per weight row
+#ifndef ADA_W16_CONV_GROUPS
+#define ADA_W16_CONV_GROUPS 2
+#endif
+constexpr int CONV_GROUPS = ADA_W16_CONV_GROUPS;  // converter groups taking the stages in turn
+constexpr int CONV_WARPS = 4 * CONV_GROUPS;       // four warps (one thread per weight row) a group
 constexpr int EPI_WARPS = 8;                   // two per TMEM lane quarter, 128 columns each
 constexpr int EPI_WARP0 = 2 + CONV_WARPS;
 constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 2 * CONV_WARPS);
+      mbar_init(&ready[s], 2 * 4);  // one group's four warps in each CTA
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -188,33 +192,38 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else if (warp < EPI_WARP0) {  // ---------------- converters (both CTAs) ----------------
-    // converter thread i widens half hk = i / 128 of weight row r = i % 128 of this CTA's 128:
-    // 32 e2m1 codes x their 2 block scales -> 32 fp16 values, chunks 4hk .. 4hk+3 of the row's
-    // eight 16-byte chunks in the swizzled K-major tile (chunk c of row r at 16 * (c ^ (r % 8))
-    // within the row's 128 bytes; 8-row atoms 1 KiB apart)
+    // CONV_GROUPS groups of four warps take the stages in turn (group g the stages it with
+    // it % CONV_GROUPS == g), so one group's wait, fence and arrive overlap the next group's work.
+    // Thread r of a group widens weight row r of this CTA's 128: 64 e2m1 codes x their 4 block
+    // scales -> 64 fp16 values, the row's eight 16-byte chunks in the swizzled K-major tile
+    // (chunk c of row r at 16 * (c ^ (r % 8)) within the row's 128 bytes; 8-row atoms 1 KiB apart)
     const int i = threadIdx.x - 64;
-    const int r = i & 127, hk = i >> 7;
+    const int r = i & 127, grp = i >> 7;
     const uint32_t ready0_lead = cl::mapa(&ready[0], 0);
     uint32_t it = 0;
     bool ok = true;
     for (int t = pair_id; t < tiles && ok; t += pairs) {
       for (int kt = 0; kt < nks; ++kt, ++it) {
+        if ((int)(it % (uint32_t)CONV_GROUPS) != grp) continue;
         const int s = (int)(it % (uint32_t)STAGES);
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / STAGES) & 1, abort_v, p.err, ERR_FULL))) {
           ok = false;
           break;
         }
         uint8_t* st = smem + (size_t)s * STAGE;
-        const uint4 w = *reinterpret_cast<const uint4*>(st + A_BYTES + B_BYTES + r * (KS / 2) + hk * 16);
-        const uint16_t sc = *reinterpret_cast<const uint16_t*>(st + A_BYTES + B_BYTES + W_BYTES + (r & 31) * 16 +
-                                                               (r >> 5) * 4 + hk * 2);
-        const uint32_t s01 = e4m3x2_to_f16x2(sc);
-        const __half2 sh[2] = {__half2half2(__low2half(*reinterpret_cast<const __half2*>(&s01))),
-                               __half2half2(__high2half(*reinterpret_cast<const __half2*>(&s01)))};
-        const uint32_t codes[4] = {w.x, w.y, w.z, w.w};
+        const uint4* wrow = reinterpret_cast<const uint4*>(st + A_BYTES + B_BYTES + r * (KS / 2));
+        const uint4 w0 = wrow[0], w1 = wrow[1];
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + A_BYTES + B_BYTES + W_BYTES + (r & 31) * 16 +
+                                                               (r >> 5) * 4);
+        const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc & 0xFFFFu)), s23 = e4m3x2_to_f16x2((uint16_t)(sc >> 16));
+        const __half2 sh[4] = {__half2half2(__low2half(*reinterpret_cast<const __half2*>(&s01))),
+                               __half2half2(__high2half(*reinterpret_cast<const __half2*>(&s01))),
+                               __half2half2(__low2half(*reinterpret_cast<const __half2*>(&s23))),
+                               __half2half2(__high2half(*reinterpret_cast<const __half2*>(&s23)))};
+        const uint32_t codes[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         uint8_t* brow = st + A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 8; ++c) {
           uint32_t h[4];
           e2m1x8_to_f16x8_cvt(codes[c], h);
 #pragma unroll
@@ -222,11 +231,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             const __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&h[j]), sh[c >> 1]);
             h[j] = *reinterpret_cast<const uint32_t*>(&v);
           }
-          *reinterpret_cast<uint4*>(brow + (((4 * hk + c) ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by tcgen05.mma
+        // the tile stays in this CTA's shared memory, where this CTA's half of the pair MMA reads
+        // it: the async-proxy fence and a CTA-scope release order the writes before the arrival
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(ready0_lead + (uint32_t)s * 8u);
+        if (lane == 0) mbar_arrive_remote_cta(ready0_lead + (uint32_t)s * 8u);
       }
     }
     __syncwarp();

@@ -305,6 +305,13 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
+// Arrive on an mbarrier of another CTA of the cluster, release at CTA scope: orders this thread's
+// earlier writes to its OWN CTA's shared memory before the arrival (with fence.proxy.async first,
+// for operand tiles that this CTA's half of a pair MMA reads from there).  The cluster-scope
+// release above also waits for cluster-wide visibility, which costs about a microsecond.
+__device__ __forceinline__ void mbar_arrive_remote_cta(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 // Instruction descriptor, kind::mxf4nvf4 with M = 256 (the CTA-pair shape), N = n.
 __host__ __device__ constexpr uint32_t idesc_mxf4nvf4_m256(int n) {
   return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);

@@ -66,7 +66,8 @@ def block_tables_from_slots(slot_mapping: torch.Tensor, cu_seqlens_q: torch.Tens
 def install(terms: int | None = None, fresh_prefill: str | None = None, fused_layers: bool = True) -> None:
     """Rebind the reference's hot-path ops to this package's kernels.
 
-    terms: activation e2m1 terms of the NVFP4 linear (default 4).
+    terms: activation e2m1 terms of the NVFP4 linear below prefill size (default 4); calls of
+      256 tokens or more run the reference's own W4A16 arithmetic (nvfp4_gemm.nvfp4_linear_w4a16).
     fused_layers: decode steps of the reference's Qwen3DecoderLayer (qwen3.py:1358-1371) run as
       nine fused kernels (adallm_b200.fused_layer: RMSNorm+quantiser producers, split-K partial
       planes summed by the next kernel, attention with the o_proj quantiser) on the layer's own
@@ -94,9 +95,9 @@ def install(terms: int | None = None, fresh_prefill: str | None = None, fused_la
         nvfp4_gemm.DEFAULT_TERMS = int(terms)
     # NVFP4_FP8=1 selects the reference's W4A8 kernel (e4m3 activations per 64-wide K chunk and
     # e4m3 weights, nvfp4_gemm.py:23-40, :496-535).  The replacement has one arithmetic for both
-    # settings: the multi-term activation (DEFAULT_TERMS), which sits closer to the exact W4A16
-    # product than the W4A8 kernel does (measured by tests/test_gpu_reference_triton.py).  The
-    # setting is recorded, not acted on.
+    # settings: the multi-term activation (DEFAULT_TERMS) below prefill size and the W4A16 product
+    # above it, both closer to the exact W4A16 product than the W4A8 kernel is (measured by
+    # tests/test_gpu_reference_triton.py).  The setting is recorded, not acted on.
     nvfp4_gemm.REFERENCE_FP8_REQUESTED = os.getenv("NVFP4_FP8", "0").strip().lower() not in ("0", "false", "off")
 
     ref_gemm.nvfp4_linear = nvfp4_gemm.nvfp4_linear

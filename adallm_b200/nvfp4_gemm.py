@@ -14,6 +14,12 @@ with per-16 block scales (W4A4, ~0.1 relative deviation from the reference); 2..
 row-scaled terms whose sum approximates the bf16 activation (4 terms, the default:
 ~5e-4 relative L2 for Gaussian rows; 6 terms: ~1e-5).  Set with the environment
 variable ADALLM_B200_NVFP4_TERMS or per call.
+
+Prefill-size calls (M >= W4A16_MIN_M = 256 tokens, N % 256 == 0, K % 64 == 0) that leave
+``terms`` at its default run the reference's own W4A16 arithmetic instead
+(``nvfp4_linear_w4a16``: fp16 activations, e2m1 weights widened exactly to fp16 on chip, fp32
+accumulation on SM-pair tensor-core tiles), which at these sizes is also the faster form.
+ADALLM_B200_W4A16_MIN_M=0 turns this off.
 """
 from __future__ import annotations
 
@@ -24,6 +30,7 @@ import torch
 from . import _native as N
 
 DEFAULT_TERMS = int(os.environ.get("ADALLM_B200_NVFP4_TERMS", "4"))
+W4A16_MIN_M = int(os.environ.get("ADALLM_B200_W4A16_MIN_M", "256"))
 
 
 def sf_bytes(n: int, k: int) -> int:
@@ -148,6 +155,8 @@ def nvfp4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor,
     n = w_packed.shape[0]
     if w_packed.shape[1] * 2 != k:
         raise ValueError("Packed weight shape does not match input features")
+    if terms is None and _w4a16_eligible(m, n, k, w_packed, out, ksplit):
+        return nvfp4_linear_w4a16(x, w_packed, w_scale, w_scale_2, bias, sf, out).to(out_dtype)
     t = DEFAULT_TERMS if terms is None else int(terms)
     if sf is None:
         sf = _cached_sf(w_scale, n, k)
@@ -167,6 +176,14 @@ def nvfp4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor,
                                      N.stream_ptr(x.device))
     N.check(st, "NVFP4 kernel")
     return y.to(out_dtype).view(*x.shape[:-1], n)
+
+
+def _w4a16_eligible(m: int, n: int, k: int, w_packed: torch.Tensor, out: torch.Tensor | None, ksplit: int) -> bool:
+    if W4A16_MIN_M <= 0 or m < W4A16_MIN_M or ksplit or n % 256 or k % 64:
+        return False
+    if w_packed.stride(-1) != 1 or w_packed.stride(0) % 16 or w_packed.data_ptr() % 16:
+        return False
+    return out is None or (out.stride(-1) == 1 and out.stride(0) % 8 == 0 and out.data_ptr() % 16 == 0)
 
 
 def nvfp4_linear_w4a16(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, w_scale_2: torch.Tensor,

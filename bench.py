@@ -217,7 +217,7 @@ def kernel_benches(dev, peak):
     import torch
     from adallm_b200.attention import paged_decode, paged_decode_workspace_bytes
     from adallm_b200.decode_step import random_nvfp4
-    from adallm_b200.nvfp4_gemm import nvfp4_linear, prepack_scales, workspace_bytes
+    from adallm_b200.nvfp4_gemm import nvfp4_linear, nvfp4_linear_w4a16, prepack_scales, workspace_bytes
 
     st = torch.cuda.current_stream(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -355,7 +355,16 @@ def kernel_benches(dev, peak):
                                 "frac_fp4_spec": round(tf / 9000.0, 4),
                                 "frac_4x_bf16_measured": round(tf / (4 * bf16_burst), 4) if bf16_burst else None,
                                 "mode": "steady", "launches": 2}
-    del xp, yp, wsp, packed, scale, flush
+    # the same GEMM in the reference's W4A16 arithmetic (fp16 activations, weights widened to
+    # fp16 on chip, tcgen05 kind::f16 on SM pairs): what nvfp4_linear runs from 256 tokens
+    yp16 = torch.empty((mp, npf), device=dev, dtype=torch.bfloat16)
+    pf16 = lambda: nvfp4_linear_w4a16(xp, packed, scale, s2t, sf=sfp, out=yp16)
+    us = steady([pf16] * 4, reps=3)
+    tf = 2 * mp * npf * kpf / us / 1e6
+    out["gemm_prefill_w4a16"] = {"us": round(us, 1), "tflops": round(tf, 1), "m": mp, "n": npf, "k": kpf,
+                                 "frac_bf16_measured": round(tf / bf16_burst, 4) if bf16_burst else None,
+                                 "mode": "steady", "launches": 2}
+    del xp, yp, yp16, wsp, packed, scale, flush
     torch.cuda.empty_cache()
 
     # prefix-cache prefill attention on the e4m3 pages (Qwen3-8B heads): 4 sequences with 2048

@@ -67,6 +67,35 @@ def gemm() -> dict:
             "oracle_vs_exact": nv.rel_l2(oracle, exact), "ours_vs_exact": nv.rel_l2(ours.float().cpu().numpy(), exact)}
 
 
+def gemm_prefill() -> dict:
+    """The reference's fp16 NVFP4 GEMM (NVFP4_FP8=0) at prefill size (1024 tokens) against this
+    package's W4A16 kernel, called directly and through nvfp4_linear's route from 256 tokens:
+    the same fp16 operands and fp32 accumulation; the reference folds scale_2 into its fp16
+    weights (one more rounding), this package applies it in fp32 after the sum."""
+    _path()
+    import numpy as np
+    import torch
+    import adallm.ops.nvfp4_gemm as rg
+    from oracle import nvfp4 as nv
+    from adallm_b200.nvfp4_gemm import nvfp4_linear, nvfp4_linear_w4a16
+    d = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(1)
+    w = (torch.randn((4096, 4096), generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    packed, sbits, s2 = nv.quantize_weight(w)
+    scale16 = nv.e4m3_decode(sbits).astype(np.float16)
+    x = torch.randn((1024, 4096), generator=g).to(torch.bfloat16)
+    pk, sc, s2t = torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d), torch.tensor(s2, device=d)
+    exact = nv.linear_ref(x.float().numpy(), packed, scale16.astype(np.float32), s2)
+    tri = rg.nvfp4_linear(x.to(d), pk, sc, s2t, None, None, 16)
+    ours = nvfp4_linear(x.to(d), pk, sc, s2t, None, None, 16)
+    direct = nvfp4_linear_w4a16(x.to(d), pk, sc, s2t)
+    torch.cuda.synchronize()
+    tri_np, ours_np = tri.float().cpu().numpy(), ours.float().cpu().numpy()
+    return {"mode": "w4a8" if rg._FP8_ENABLED else "w4a16", "routed_equals_direct": bool(torch.equal(ours, direct)),
+            "ours_vs_triton": nv.rel_l2(ours_np, tri_np), "triton_vs_exact": nv.rel_l2(tri_np, exact),
+            "ours_vs_exact": nv.rel_l2(ours_np, exact)}
+
+
 def attn() -> dict:
     _path()
     os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
@@ -154,7 +183,7 @@ def main():
     if not os.path.isdir(os.path.join(REF_DIR, "adallm")):
         print("REFTRITON " + json.dumps({"unavailable": f"reference package not found in {REF_DIR}"}))
         return
-    r = {"gemm": gemm, "attn": attn, "prefill": prefill}[sys.argv[1]]()
+    r = {"gemm": gemm, "gemm_prefill": gemm_prefill, "attn": attn, "prefill": prefill}[sys.argv[1]]()
     print("REFTRITON " + json.dumps(r), flush=True)
 
 

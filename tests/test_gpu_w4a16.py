@@ -88,3 +88,46 @@ def test_w4a16_rejects_unsupported_shapes():
     with pytest.raises(Exception):  # N % 256 != 0
         nvfp4_linear_w4a16(x, torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d),
                            torch.tensor(s2, device=d))
+
+
+def test_w4a16_full_code_and_scale_range():
+    """Every e2m1 code pair and block scales over the whole finite e4m3 range (subnormal 2^-9 to
+    448): code value x block scale is exact in fp16 across it (2^-10 .. 2688), so the bar is the
+    same as for moderate scales."""
+    d = dev()
+    m, n, k = 256, 256, 512
+    g = torch.Generator().manual_seed(34)
+    packed = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.int32).to(torch.uint8).numpy()
+    packed[0, :] = np.arange(256, dtype=np.uint8)  # row 0 holds every byte once
+    sbits = torch.randint(0x01, 0x7F, (n, k // 16), generator=g, dtype=torch.int32).to(torch.uint8).numpy()
+    scale16 = nv.e4m3_decode(sbits).astype(np.float16)
+    s2 = np.float32(0.01)
+    x = torch.randn((m, k), generator=g).to(torch.float16)
+    y = nvfp4_linear_w4a16(x.to(d), torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d),
+                           torch.tensor(s2, device=d))
+    torch.cuda.synchronize()
+    ref = ref_w4a16(x, packed, scale16, s2, None)
+    assert rel_l2(y.double().cpu(), ref) < 5e-4
+    assert rel_l2(y[:, 0].double().cpu(), ref[:, 0]) < 5e-4
+
+
+def test_nvfp4_linear_routes_prefill_size_to_w4a16(monkeypatch):
+    """nvfp4_linear with the default terms runs the W4A16 kernel from W4A16_MIN_M (256) tokens
+    (identical to nvfp4_linear_w4a16) and the multi-term operand below it (identical to terms=4);
+    an explicit terms or W4A16_MIN_M = 0 keeps the multi-term operand at any size."""
+    from adallm_b200 import nvfp4_gemm
+    from adallm_b200.nvfp4_gemm import nvfp4_linear
+    d = dev()
+    n, k = 1024, 1024
+    packed, sbits, scale16, s2 = random_weight(n, k, seed=35, realistic=False)
+    args = (torch.from_numpy(packed).to(d), torch.from_numpy(scale16).to(d), torch.tensor(s2, device=d))
+    g = torch.Generator().manual_seed(35)
+    x_big = torch.randn((3, 200, k), generator=g).to(torch.bfloat16).to(d)   # 600 tokens, leading dims
+    x_small = torch.randn((100, k), generator=g).to(torch.bfloat16).to(d)
+    y = nvfp4_linear(x_big, *args, None, None, 16)
+    assert y.shape == (3, 200, n)
+    assert torch.equal(y, nvfp4_linear_w4a16(x_big, *args))
+    assert not torch.equal(y, nvfp4_linear(x_big, *args, None, None, 16, terms=4))
+    assert torch.equal(nvfp4_linear(x_small, *args, None, None, 16), nvfp4_linear(x_small, *args, None, None, 16, terms=4))
+    monkeypatch.setattr(nvfp4_gemm, "W4A16_MIN_M", 0)
+    assert torch.equal(nvfp4_linear(x_big, *args, None, None, 16), nvfp4_linear(x_big, *args, None, None, 16, terms=4))
