@@ -100,3 +100,52 @@ def test_prepack_model_skips_modules_off_the_gpu():
     model = torch.nn.Sequential(lin, torch.nn.Linear(4, 4))
     assert prepack_model(model) == 0
     assert not hasattr(lin.weight_scale, "_ada_sf")
+
+
+def test_w4a16_linear_argument_errors(built):
+    """ada_nvfp4_linear_w4a16 (the reference's W4A16 arithmetic at prefill size) validates shapes,
+    dtypes, workspace size and alignment before any CUDA call (placeholder pointers)."""
+    lib = N.lib()
+    P = 1 << 20
+    m, n, k = 512, 1024, 2048
+    ws = int(lib.ada_nvfp4_linear_w4a16_workspace_size(m, k))
+    assert ws == 256 + m * k * 2 and lib.ada_nvfp4_linear_w4a16_workspace_size(0, k) == 0
+
+    def call(**kw):
+        a = dict(x=P, x_dt=0, ldx=k, m=m, k=k, w=P, ldw=k // 2, sf=P, s2=P, n=n, bias=None, y=P, y_dt=0, ldy=n,
+                 ws=P, ws_bytes=ws, stream=None)
+        a.update(kw)
+        return lib.ada_nvfp4_linear_w4a16(*a.values())
+
+    assert call(m=0) == 0                                     # nothing to do
+    assert call(x=None) == N.ADA_ERR_INVALID_ARG
+    assert call(m=-1) == N.ADA_ERR_INVALID_ARG
+    assert call(x_dt=7) == N.ADA_ERR_INVALID_ARG
+    assert call(ldx=k - 8) == N.ADA_ERR_INVALID_ARG
+    assert call(n=n - 128, ldy=n) == N.ADA_ERR_UNSUPPORTED    # 256 weight rows per pair tile
+    assert call(k=k - 32, ldx=k) == N.ADA_ERR_UNSUPPORTED     # 64-wide K stages
+    assert call(ws_bytes=ws - 1) == N.ADA_ERR_WORKSPACE
+    assert call(x=P + 8) == N.ADA_ERR_ALIGNMENT
+    assert call(ldy=n + 4) == N.ADA_ERR_ALIGNMENT
+    assert call(bias=P + 2) == N.ADA_ERR_ALIGNMENT
+    assert call(ldw=k // 2 + 8) == N.ADA_ERR_ALIGNMENT        # weight rows 16-byte aligned
+    assert call(ws=P + 16) == N.ADA_ERR_ALIGNMENT             # workspace 256-byte aligned
+
+
+def test_w4a16_route_eligibility(monkeypatch):
+    """nvfp4_linear sends a default-terms call to the W4A16 kernel only from W4A16_MIN_M tokens,
+    for shapes and output views that kernel takes, and never with an explicit split-K."""
+    import torch
+    from adallm_b200 import nvfp4_gemm as G
+    w = torch.zeros((512, 1024), dtype=torch.uint8)
+    assert G._w4a16_eligible(256, 512, 2048, w, None, 0)
+    assert not G._w4a16_eligible(255, 512, 2048, w, None, 0)
+    assert not G._w4a16_eligible(4096, 512, 2048, w, None, 2)          # explicit split-K
+    assert not G._w4a16_eligible(4096, 384, 2048, w[:384], None, 0)     # N % 256
+    assert not G._w4a16_eligible(4096, 512, 2016, w[:, :1008], None, 0)  # K % 64
+    wide = torch.zeros((4096, 520), dtype=torch.bfloat16)
+    assert G._w4a16_eligible(4096, 512, 2048, w, wide[:, :512], 0)
+    odd = torch.zeros((4096, 516), dtype=torch.bfloat16)
+    assert not G._w4a16_eligible(4096, 512, 2048, w, odd[:, :512], 0)   # row stride not 16 bytes
+    monkeypatch.setattr(G, "W4A16_MIN_M", 0)
+    assert not G._w4a16_eligible(4096, 512, 2048, w, None, 0)
