@@ -297,7 +297,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
 
-// bf16 activations -> fp16 rows (the reference casts x to fp16, nvfp4_gemm.py:475), 8 a thread.
+// bf16 activations -> fp16 rows (the reference's kernel casts its x tile to fp16,
+// adallm/ops/nvfp4_gemm.py:100-105), 8 a thread.
 __global__ void __launch_bounds__(256) to_f16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t m,
                                                      int64_t k, __half* __restrict__ out) {
   pdl_wait();

@@ -6,6 +6,7 @@ Reference anchors (paths inside the reference project):
                                adallm/ops/nvfp4_gemm.py:7-18)
   * dequant_nvfp4              adallm/infra/nvfp4.py:36-77
   * nvfp4_linear semantics     adallm/ops/nvfp4_gemm.py:460-564 (kernel :58-136)
+  * its fp16 (W4A16) product  adallm/ops/nvfp4_gemm.py:100-128 (linear_w4a16_ref)
   * weight / scale layout      adallm/ops/linear.py:31-43 (uint8 [N, K/2],
                                fp16 [N, K/16] holding e4m3 values, fp32 [])
 
@@ -320,6 +321,21 @@ def linear_ref(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, scale_2, bi
     if bias is not None:
         y = y + np.asarray(bias, dtype=np.float32)
     return y.astype(np.float32)
+
+
+def linear_w4a16_ref(x, packed, scale, scale_2, bias=None):
+    """The W4A16 product of the reference's fp16 NVFP4 GEMM (adallm/ops/nvfp4_gemm.py:58-136,
+    launched by nvfp4_linear :460-564 with NVFP4_FP8 unset): the activation tile cast to fp16
+    (:100-105), the weight element LUT[code] * e4m3 block scale (:118-126; exact in fp16), fp32
+    accumulation (:128).  Here the sum is taken in float64 over those fp16 operands and scale_2
+    is applied after it (the arithmetic of adallm_b200's W4A16 kernel, which does not fold scale_2
+    into fp16 weights as :126 does), bias last.  float64 torch [M, N]."""
+    import torch
+    w = dequant_nvfp4_torch(packed, np.asarray(scale, dtype=np.float32), None).double()
+    y = (torch.as_tensor(x).cpu().to(torch.float16).double() @ w.t()) * float(scale_2)
+    if bias is not None:
+        y = y + torch.as_tensor(bias).cpu().double()
+    return y
 
 
 def linear_terms_ref(codes, sbits, g, packed, scale, scale_2) -> np.ndarray:

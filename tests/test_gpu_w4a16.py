@@ -2,7 +2,7 @@
 (ada_nvfp4_linear_w4a16, tcgen05.mma.cta_group::2.kind::f16) vs dequantise-then-matmul.
 
 The weights are widened to fp16 exactly (e2m1 value x e4m3 block scale), the activations are
-cast to fp16 as the reference casts them (adallm/ops/nvfp4_gemm.py:475), and the products
+cast to fp16 as the reference's kernel casts them (adallm/ops/nvfp4_gemm.py:100-105), and the products
 accumulate in fp32, so against an fp64 matmul of the same fp16 operands the only error is fp32
 summation order and the output rounding: rel-L2 <= 2e-3 for bf16 outputs, <= 5e-4 for fp16."""
 import numpy as np
@@ -18,12 +18,8 @@ pytestmark = pytest.mark.gpu
 
 
 def ref_w4a16(x, packed, scale16, s2, bias):
-    """fp64 x.half() @ (lut x block scale)^T x scale_2 (+ bias)."""
-    w = nv.dequant_nvfp4_torch(packed, scale16.astype(np.float32), None).double()
-    y = (x.half().double().cpu() @ w.t()) * float(s2)
-    if bias is not None:
-        y = y + bias.double().cpu()
-    return y
+    """fp64 x.half() @ (lut x block scale)^T x scale_2 (+ bias): oracle.nvfp4.linear_w4a16_ref."""
+    return nv.linear_w4a16_ref(x, packed, scale16.astype(np.float32), s2, bias)
 
 
 @pytest.mark.parametrize("m,n,k,with_bias,dtype", [

@@ -190,3 +190,26 @@ def test_torch_dequant_matches_numpy(golden_dir):
     b = nv.dequant_nvfp4_torch(torch.from_numpy(g["packed"]), torch.from_numpy(g["scale_fp16"]).float(),
                                float(g["scale_2"]))
     np.testing.assert_array_equal(a, b.numpy())
+
+
+def test_w4a16_oracle_matches_reference_golden_and_fp16_kernel_emulation(golden_dir):
+    """oracle.nvfp4.linear_w4a16_ref (the W4A16 product: fp16 x, exact fp16 code x block scale,
+    scale_2 after the sum) against the reference's golden linear output (bf16 weights in its
+    dequant mode: within 1e-2 as linear_ref) and against the emulation of the reference's fp16
+    Triton kernel, which folds scale_2 into fp16 weights and rounds its output to fp16 (within
+    those roundings, < 2e-3); on exactly representable inputs the oracle is exact."""
+    g = _load(golden_dir, "golden_nvfp4.npz")
+    x = bf16_from_bits(g["x_bf16"]).float()
+    y = nv.linear_w4a16_ref(x, g["packed"], g["scale_fp16"].astype(np.float32), g["scale_2"])
+    y_ref = bf16_from_bits(g["y_bf16"]).float().numpy()
+    assert nv.rel_l2(y.numpy(), y_ref) < 1e-2
+    w16 = nv.dequant_nvfp4_kernel_fp16(g["packed"], g["scale_fp16"], g["scale_2"]).float()
+    emu = (x.half().float() @ w16.t()).half().double()
+    assert nv.rel_l2(y.numpy(), emu.numpy()) < 2e-3
+    # one code per row, a unit scale, scale_2 = 1: the product is exact
+    packed = np.zeros((4, 8), np.uint8)
+    packed[:, 0] = [0x01, 0x07, 0x0F, 0x19]        # (K 0, K 1): (0.5, 0) | (6, 0) | (-6, 0) | (-0.5, 0.5)
+    xk = torch.zeros((1, 16), dtype=torch.float16)
+    xk[0, 0], xk[0, 1] = 2.0, 3.0
+    out = nv.linear_w4a16_ref(xk, packed, np.ones((4, 1), np.float32), np.float32(1.0))
+    np.testing.assert_array_equal(out.numpy(), [[1.0, 12.0, -12.0, -1.0 + 1.5]])
