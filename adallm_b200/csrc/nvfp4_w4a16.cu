@@ -369,6 +369,9 @@ extern "C" int ada_nvfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, i
     return ADA_ERR_INVALID_ARG;
   if (ldx < k || ldy < n || ldw < k / 2) return ADA_ERR_INVALID_ARG;
   if (n % w16::BW || k % w16::KS || m > (1 << 24) || n > (1 << 24) || k > (1 << 24)) return ADA_ERR_UNSUPPORTED;
+  // one pair may walk every tile: its K-step counter (uint32, stage parities modulo 5 stages)
+  // and the tile index (int) must not wrap
+  if ((n / w16::BW) * cdiv(m, (int64_t)w16::BT) * (k / w16::KS) >= (int64_t(1) << 31)) return ADA_ERR_UNSUPPORTED;
   if (workspace_bytes < ada_nvfp4_linear_w4a16_workspace_size(m, k)) return ADA_ERR_WORKSPACE;
   if (!a16p(x) || (ldx & 7) || !a16p(y) || (ldy & 7) || (bias && !a16p(bias)) || !a16p(w_packed) || (ldw & 15) ||
       !a16p(sf_w) || ((uintptr_t)workspace & 255))

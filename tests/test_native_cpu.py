@@ -124,6 +124,10 @@ def test_w4a16_linear_argument_errors(built):
     assert call(ldx=k - 8) == N.ADA_ERR_INVALID_ARG
     assert call(n=n - 128, ldy=n) == N.ADA_ERR_UNSUPPORTED    # 256 weight rows per pair tile
     assert call(k=k - 32, ldx=k) == N.ADA_ERR_UNSUPPORTED     # 64-wide K stages
+    # a pair may walk every tile: more than 2^31 K steps in all is refused (counters would wrap)
+    big = dict(m=1 << 24, k=1 << 16, ldx=1 << 16, ldw=1 << 15, n=1 << 14, ldy=1 << 14, ws_bytes=1 << 62)
+    assert call(**big) == N.ADA_ERR_UNSUPPORTED                   # 2^32 K steps
+    assert call(**dict(big, m=1 << 22, x=P + 8)) == N.ADA_ERR_ALIGNMENT  # 2^30: past the bound
     assert call(ws_bytes=ws - 1) == N.ADA_ERR_WORKSPACE
     assert call(x=P + 8) == N.ADA_ERR_ALIGNMENT
     assert call(ldy=n + 4) == N.ADA_ERR_ALIGNMENT
