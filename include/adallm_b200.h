@@ -284,8 +284,11 @@ ADA_API int ada_nvfp4_linear(const void* x, int x_dtype, int64_t ldx, int64_t m,
  * tcgen05.mma.cta_group::2.kind::f16 tiles of 256 tokens x 256 weight rows accumulate in fp32;
  * the fp32 global scale and the bias are applied in the epilogue.  sf_w is the prepacked scale
  * layout of ada_nvfp4_prepack_scales.  Implemented: N % 256 == 0, K % 64 == 0; x, y, bias,
- * w_packed and sf_w 16-byte aligned, ldx and ldy multiples of 8, ldw a multiple of 16.
- * workspace: ada_nvfp4_linear_w4a16_workspace_size(M, K) bytes, 256-byte aligned. */
+ * w_packed and sf_w 16-byte aligned, ldx and ldy multiples of 8, ldw a multiple of 16;
+ * (N/256) x ceil(M/256) x (K/64) below 2^31 (else ADA_ERR_UNSUPPORTED).
+ * workspace: ada_nvfp4_linear_w4a16_workspace_size(M, K) bytes, 256-byte aligned; its first 4
+ * bytes are an error word (bounded waits that gave up OR a code into it).  Calls that share a
+ * workspace must be ordered (same stream). */
 ADA_API size_t ada_nvfp4_linear_w4a16_workspace_size(int64_t m, int64_t k);
 ADA_API int ada_nvfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k,
                                    const uint8_t* w_packed, int64_t ldw, const uint8_t* sf_w,
