@@ -94,9 +94,9 @@ def install(terms: int | None = None, fresh_prefill: str | None = None, fused_la
     if terms is not None:
         nvfp4_gemm.DEFAULT_TERMS = int(terms)
     # NVFP4_FP8=1 selects the reference's W4A8 kernel (e4m3 activations per 64-wide K chunk and
-    # e4m3 weights, nvfp4_gemm.py:23-40, :496-535).  The replacement has one arithmetic for both
+    # e4m3 weights, nvfp4_gemm.py:23-40, :496-535).  The replacement computes the same under both
     # settings: the multi-term activation (DEFAULT_TERMS) below prefill size and the W4A16 product
-    # above it, both closer to the exact W4A16 product than the W4A8 kernel is (measured by
+    # from 256 tokens, both closer to the exact W4A16 product than the W4A8 kernel is (measured by
     # tests/test_gpu_reference_triton.py).  The setting is recorded, not acted on.
     nvfp4_gemm.REFERENCE_FP8_REQUESTED = os.getenv("NVFP4_FP8", "0").strip().lower() not in ("0", "false", "off")
 

@@ -207,14 +207,16 @@ def test_load_time_prepack_hook(ref, monkeypatch):
 
 def test_nvfp4_fp8_setting_is_recorded_and_keeps_the_terms(ref, monkeypatch):
     """NVFP4_FP8=1 (the reference's W4A8 mode) under install(): recorded, and the linear keeps its
-    multi-term activation arithmetic (more accurate than W4A8; measured on the GPU)."""
+    multi-term activation arithmetic below 256 tokens and the W4A16 route from there (both more
+    accurate than W4A8; measured on the GPU)."""
     import adallm_b200
     from adallm_b200 import nvfp4_gemm, context
-    terms = nvfp4_gemm.DEFAULT_TERMS
+    terms, min_m = nvfp4_gemm.DEFAULT_TERMS, nvfp4_gemm.W4A16_MIN_M
     try:
         monkeypatch.setenv("NVFP4_FP8", "1")
         adallm_b200.install()
         assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is True and nvfp4_gemm.DEFAULT_TERMS == terms
+        assert nvfp4_gemm.W4A16_MIN_M == min_m == 256
         monkeypatch.setenv("NVFP4_FP8", "0")
         adallm_b200.install()
         assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is False and nvfp4_gemm.DEFAULT_TERMS == terms
