@@ -216,7 +216,7 @@ def test_nvfp4_fp8_setting_is_recorded_and_keeps_the_terms(ref, monkeypatch):
         monkeypatch.setenv("NVFP4_FP8", "1")
         adallm_b200.install()
         assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is True and nvfp4_gemm.DEFAULT_TERMS == terms
-        assert nvfp4_gemm.W4A16_MIN_M == min_m == 256
+        assert nvfp4_gemm.W4A16_MIN_M == min_m
         monkeypatch.setenv("NVFP4_FP8", "0")
         adallm_b200.install()
         assert nvfp4_gemm.REFERENCE_FP8_REQUESTED is False and nvfp4_gemm.DEFAULT_TERMS == terms
