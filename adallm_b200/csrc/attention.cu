@@ -617,7 +617,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32, 3)
 
 template <typename TQ, typename TO>
 inline bool fused_smem_ready() {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
   if (done[dev]) return true;
@@ -780,7 +780,7 @@ __global__ void __launch_bounds__(512) decode_reduce_quant_kernel(Params P, TO* 
 // set once per device.
 template <typename TQ>
 inline bool split_smem_ready() {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
   if (done[dev]) return true;
@@ -958,15 +958,19 @@ static int paged_decode_impl(const void* q, int q_dtype, int64_t q_stride_b, int
     return ADA_OK;
   }
   // persistent-style grid: every warp takes work items (sequence, KV head, split) round-robin
-  static int sms[64] = {0};
+  static std::atomic<int> sms[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
-  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return ADA_ERR_CUDA;
+  int n_sm = sms[dev].load(std::memory_order_relaxed);
+  if (!n_sm) {
+    if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm <= 0)
+      return ADA_ERR_CUDA;
+    sms[dev].store(n_sm, std::memory_order_relaxed);
+  }
   const int64_t items = (int64_t)batch * num_kv_heads * P.max_splits;
   if (items > 0x7fffffff) return ADA_ERR_UNSUPPORTED;
   const int64_t want = (items + attn::SPLIT_WARPS - 1) / attn::SPLIT_WARPS;
-  const unsigned grid = (unsigned)(want < 3 * (int64_t)sms[dev] ? want : 3 * (int64_t)sms[dev]);
+  const unsigned grid = (unsigned)(want < 3 * (int64_t)n_sm ? want : 3 * (int64_t)n_sm);
   if (q_dtype == ADA_DT_BF16) {
     if (!attn::split_smem_ready<__nv_bfloat16>()) return ADA_ERR_CUDA;
     (void)ada::launch_k(attn::decode_split_kernel<__nv_bfloat16>, dim3(grid), dim3(attn::SPLIT_WARPS * 32),

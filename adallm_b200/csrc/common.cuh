@@ -5,6 +5,8 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <atomic>
+#include <mutex>
 #include <utility>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>

@@ -263,11 +263,15 @@ static int nb_for(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 48 ? 48
 
 template <int NB>
 static bool smem_ready() {
-  static bool done = false;
-  if (!done)
-    done = cudaFuncSetAttribute(lm_head_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)Cfg<NB>::SMEM) == cudaSuccess;
-  return done;
+  static std::atomic<bool> done[64];  // function attributes are per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return true;
+  if (cudaFuncSetAttribute(lm_head_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<NB>::SMEM) !=
+      cudaSuccess)
+    return false;
+  done[dev] = true;
+  return true;
 }
 
 }  // namespace lmh
@@ -316,12 +320,16 @@ extern "C" int ada_lm_head_argmax(const void* x, int64_t ldx, int64_t m, int64_t
       !sm100::encode_bytes(&tmx, x, 2, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_128B))
     return ADA_ERR_CUDA;
 
-  static int sms[64] = {0};
+  static std::atomic<int> sms[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
-  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return ADA_ERR_CUDA;
-  const unsigned grid = (unsigned)(P.n_tiles < sms[dev] ? P.n_tiles : sms[dev]);
+  int n_sm = sms[dev].load(std::memory_order_relaxed);
+  if (!n_sm) {
+    if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm <= 0)
+      return ADA_ERR_CUDA;
+    sms[dev].store(n_sm, std::memory_order_relaxed);
+  }
+  const unsigned grid = (unsigned)(P.n_tiles < n_sm ? P.n_tiles : n_sm);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define ADA_LMH(NB_)                                                                                         \
   do {                                                                                                       \

@@ -943,10 +943,13 @@ static void stages_dispatch(int bn, int t, int ks, int rows_max, int max_units, 
 // maximum shared-memory carveout.
 template <int BN, int T>
 static bool ensure_smem(size_t smem) {
-  static size_t configured[64] = {0};  // per device
+  static std::atomic<size_t> configured[64];  // per device
+  static std::mutex raise;                    // raises only: concurrent callers must not lower it
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  if (smem <= configured[dev]) return true;
+  if (smem <= configured[dev].load(std::memory_order_acquire)) return true;
+  std::lock_guard<std::mutex> hold(raise);
+  if (smem <= configured[dev].load(std::memory_order_acquire)) return true;
   if (cudaFuncSetAttribute(gemm_kernel<BN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return false;
   // The whole unified L1/shared array as shared memory, so two ~100 KB CTAs fit on one SM
@@ -954,7 +957,7 @@ static bool ensure_smem(size_t smem) {
   if (cudaFuncSetAttribute(gemm_kernel<BN, T>, cudaFuncAttributePreferredSharedMemoryCarveout,
                            (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return false;
-  configured[dev] = smem;
+  configured[dev].store(smem, std::memory_order_release);
   return true;
 }
 
@@ -968,11 +971,12 @@ __global__ void __launch_bounds__(192, 2) occupancy_twin() {}
 // once; 0 if unknown.  A split whose clusters do not all fit runs in two waves.
 template <int BN, int T>
 static int active_clusters(int ks, int per_sm = 2) {
-  static int cache[64][2][MAX_KS + 1] = {};
+  static std::atomic<int> cache[64][2][MAX_KS + 1];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || ks < 1 || ks > MAX_KS) return 0;
-  int& slot = cache[dev][per_sm == 3 ? 1 : 0][ks];
-  if (slot) return slot > 0 ? slot : 0;
+  std::atomic<int>& slot = cache[dev][per_sm == 3 ? 1 : 0][ks];
+  const int known = slot.load(std::memory_order_relaxed);
+  if (known) return known > 0 ? known : 0;
   int stages = 0;
   uint32_t cols = 0;
   size_t smem = 0;
@@ -997,7 +1001,7 @@ static int active_clusters(int ks, int per_sm = 2) {
     if (cudaOccupancyMaxActiveClusters(&n, occupancy_twin, &cfg) != cudaSuccess) n = 0;
   }
   (void)cudaGetLastError();
-  slot = n > 0 ? n : -1;
+  slot.store(n > 0 ? n : -1, std::memory_order_relaxed);
   return n;
 }
 
@@ -1009,14 +1013,16 @@ static int active_clusters_dispatch(int bn, int t, int ks, int per_sm = 2) {
 }
 
 static int num_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!cache[dev]) {
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (!n) {
     int v = 0;
-    cache[dev] = (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) ? v : 148;
+    n = (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) ? v : 148;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 // A plan of ks splits whose pipeline (with the cluster reduction buffer when `cluster`) fits
@@ -1111,7 +1117,7 @@ static int make_plan(int64_t m, int64_t n, int64_t k, int terms, int force_ks, P
 }
 
 // ---- CTA-pair launch ------------------------------------------------------------------
-static bool g_pair_gemm = true;  // ada_set_pair_gemm
+static std::atomic<bool> g_pair_gemm{true};  // ada_set_pair_gemm
 
 static inline bool a16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
@@ -1126,10 +1132,11 @@ static bool make_sf_map(CUtensorMap* map, const void* base, uint64_t bytes) {
 
 // Pairs of CTAs that are resident at once (one CTA per SM; 0 if the query fails).
 static int pair_capacity() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (cache[dev]) return cache[dev] > 0 ? cache[dev] : 0;
+  const int known = cache[dev].load(std::memory_order_relaxed);
+  if (known) return known > 0 ? known : 0;
   int n = 0;
   if (cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pair::SMEM) ==
       cudaSuccess) {
@@ -1186,14 +1193,18 @@ static int launch_gemm(const CUtensorMap& tmw, const CUtensorMap& tmx, const Gem
     }
   }
   if (P.persistent && !gp.part) {  // prefill-size dense GEMM, or the grouped MoE GEMM
-    static size_t configured[64] = {0};
+    static std::atomic<size_t> configured[64];
+    static std::mutex raise;  // raises only: concurrent callers must not lower the limit
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ADA_ERR_CUDA;
-    if (P.p_smem > configured[dev]) {
-      if (cudaFuncSetAttribute(gemm_persistent_kernel<BN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)P.p_smem) != cudaSuccess)
-        return ADA_ERR_CUDA;
-      configured[dev] = P.p_smem;
+    if (P.p_smem > configured[dev].load(std::memory_order_acquire)) {
+      std::lock_guard<std::mutex> hold(raise);
+      if (P.p_smem > configured[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(gemm_persistent_kernel<BN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)P.p_smem) != cudaSuccess)
+          return ADA_ERR_CUDA;
+        configured[dev].store(P.p_smem, std::memory_order_release);
+      }
     }
     GemmParams pp = gp;
     pp.stages = P.p_stages;
@@ -1373,8 +1384,7 @@ int gated_act_quant_impl(const void* x, int64_t ldx, void* y, int64_t ldy, int64
 using namespace ada;
 
 extern "C" int ada_set_pair_gemm(int enable) {
-  const int prev = fp4::g_pair_gemm ? 1 : 0;
-  fp4::g_pair_gemm = enable != 0;
+  const int prev = fp4::g_pair_gemm.exchange(enable != 0) ? 1 : 0;
   return prev;
 }
 

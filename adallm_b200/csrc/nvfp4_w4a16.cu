@@ -322,10 +322,11 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, u
 }
 
 static int pair_capacity() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (cache[dev]) return cache[dev] > 0 ? cache[dev] : 0;
+  const int known = cache[dev].load(std::memory_order_relaxed);
+  if (known) return known > 0 ? known : 0;
   int n = 0;
   if (cudaFuncSetAttribute(gemm_w4a16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM) ==
       cudaSuccess) {

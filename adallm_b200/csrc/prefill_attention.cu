@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 template <typename TQ, typename TO>
 inline bool tc_smem_ready() {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
   if (done[dev]) return true;
